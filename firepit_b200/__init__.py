@@ -1,0 +1,18 @@
+"""firepit_b200 — B200-native (sm_100a) quantized-matmul hot path of firepit.
+
+The CUDA kernels live in ``libfirepit_b200.so`` behind a C ABI
+(``include/firepit_b200.h``); this package is the host-side mirror of
+firepit-kernels' entry points.  Importing it loads the library and fails if
+the library is missing: there is no CPU fallback.
+"""
+from . import _native
+from ._native import FpbError, launch_count
+from .gemv import (DEFAULT_GEMV_TILE, ExpertGemvView, Gemv, GemvTile, ShapeError, expert_gemv_weight_view,
+                   fp8_tile, gemv, row_scaled_tile)
+from .moe import ExpertSelection, ExpertSelectionError, MoeDimensionError, MoeDims, PrefillLayout
+from .sink import Async, Dry, Eager, Graph, Traced
+from .synth import synth_normal
+from .weights import (NVFP4_GROUP, Q8_BLOCK, FormatError, HostNvfp4Matrix, Nvfp4Matrix, current_stream_handle,
+                      quantize_nvfp4)
+
+__version__ = _native.lib.fpb_version().decode()

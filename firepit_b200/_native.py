@@ -1,0 +1,110 @@
+"""ctypes binding of the firepit_b200 C ABI (include/firepit_b200.h).
+
+The library is the in-tree ``firepit_b200/libfirepit_b200.so`` built by
+``python -m firepit_b200.build``.  There is no fallback: if the library is
+missing or fails to load, importing this module raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libfirepit_b200.so"
+
+FPB_OK = 0
+FPB_ERR_INVALID_ARGUMENT = 1
+FPB_ERR_SHAPE = 2
+FPB_ERR_FORMAT = 3
+FPB_ERR_CUDA = 4
+FPB_ERR_UNSUPPORTED = 5
+FPB_ERR_SELECTION = 6
+FPB_ERR_WORKSPACE = 7
+FPB_ERR_NO_DEVICE = 8
+
+FPB_F32 = 0
+FPB_BF16 = 1
+
+
+class FpbError(RuntimeError):
+    """A non-zero status from the C ABI; ``.status`` holds the code."""
+
+    def __init__(self, status: int, func: str, message: str):
+        super().__init__(f"{func}: status {status} ({_status_name(status)}): {message}")
+        self.status = status
+
+
+def _status_name(status: int) -> str:
+    try:
+        return lib.fpb_status_string(status).decode()
+    except Exception:  # pragma: no cover - only while the library is loading
+        return str(status)
+
+
+def _load() -> C.CDLL:
+    if not LIB_PATH.exists():
+        raise ImportError(
+            f"{LIB_PATH} is missing: build it with `python -m firepit_b200.build` "
+            "(the CUDA path has no fallback)")
+    return C.CDLL(str(LIB_PATH), mode=os.RTLD_NOW | os.RTLD_LOCAL)
+
+
+lib = _load()
+
+vp = C.c_void_p
+sz = C.c_size_t
+i32 = C.c_int
+u8p = C.POINTER(C.c_uint8)
+f32p = C.POINTER(C.c_float)
+
+# name -> (restype, argtypes)
+SIGNATURES: dict[str, tuple] = {
+    "fpb_version": (C.c_char_p, []),
+    "fpb_status_string": (C.c_char_p, [i32]),
+    "fpb_last_error": (C.c_char_p, []),
+    "fpb_launch_count": (C.c_uint64, []),
+    "fpb_e2m1_to_f32": (C.c_float, [C.c_uint8]),
+    "fpb_e4m3_to_f32": (C.c_float, [C.c_uint8]),
+    "fpb_f32_to_e2m1": (C.c_uint8, [C.c_float]),
+    "fpb_f32_to_e4m3": (C.c_uint8, [C.c_float]),
+    "fpb_synth_normal": (i32, [C.c_uint64, C.c_uint32, C.c_uint64, sz, C.c_float, C.c_float, i32, vp, vp]),
+    "fpb_nvfp4_validate": (i32, [vp, sz, vp, sz, vp, sz, sz]),
+    "fpb_nvfp4_matrix_create": (i32, [vp, vp, vp, sz, sz, vp, C.POINTER(vp)]),
+    "fpb_nvfp4_matrix_create_device": (i32, [vp, vp, vp, sz, sz, vp, C.POINTER(vp)]),
+    "fpb_nvfp4_matrix_destroy": (i32, [vp]),
+    "fpb_nvfp4_matrix_shape": (i32, [vp, C.POINTER(sz), C.POINTER(sz)]),
+    "fpb_nvfp4_matrix_device_ptrs": (i32, [vp, C.POINTER(vp), C.POINTER(vp), C.POINTER(vp)]),
+    "fpb_nvfp4_matrix_download": (i32, [vp, vp, vp, vp, vp]),
+    "fpb_nvfp4_quantize": (i32, [vp, i32, sz, sz, sz, vp, vp, vp, vp, vp]),
+    "fpb_nvfp4_dequantize": (i32, [vp, vp, vp]),
+    "fpb_nvfp4_gemv": (i32, [vp, sz, sz, vp, i32, vp, i32, i32, vp]),
+    "fpb_nvfp4_expert_gemv": (i32, [vp, vp, i32, vp, i32, sz, i32, vp, i32, vp]),
+    "fpb_moe_dims_validate": (i32, [sz, sz, sz, sz, sz]),
+    "fpb_expert_selection_validate": (i32, [vp, vp, sz, sz, sz]),
+    "fpb_prefill_layout_max_padded_rows": (i32, [sz, sz, sz, sz, C.POINTER(sz)]),
+    "fpb_prefill_layout_host": (i32, [vp, vp, sz, sz, sz, sz, vp, sz, C.POINTER(sz), vp, sz,
+                                      C.POINTER(sz), vp, vp]),
+}
+
+for _name, (_res, _args) in SIGNATURES.items():
+    _fn = getattr(lib, _name)
+    _fn.restype = _res
+    _fn.argtypes = _args
+
+
+def last_error() -> str:
+    return lib.fpb_last_error().decode(errors="replace")
+
+
+def check(status: int, func: str) -> None:
+    if status != FPB_OK:
+        raise FpbError(status, func, last_error())
+
+
+def call(name: str, *args) -> None:
+    """Calls an int-returning entry point and raises FpbError on failure."""
+    check(getattr(lib, name)(*args), name)
+
+
+def launch_count() -> int:
+    return int(lib.fpb_launch_count())

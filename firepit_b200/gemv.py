@@ -1,0 +1,137 @@
+"""Decode GEMV entry points (crates/firepit-kernels/src/gemv/mod.rs).
+
+``gemv(weight, x, y, tile).submit(sink)`` and
+``expert_gemv_weight_view(weight, x, selection, y, rows_per_expert,
+input_stride, tile).submit(sink)`` keep the reference's builder shape.  The
+tile argument is validated the way the reference asserts it
+(``GemvTile::fits``); the B200 kernel picks its own tiling.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+from . import _native as N
+from .sink import Eager, Sink
+from .weights import Q8_BLOCK, Nvfp4Matrix, current_stream_handle
+
+
+class ShapeError(ValueError):
+    """The reference's ``assert!`` on shapes and tiles."""
+
+
+@dataclass(frozen=True)
+class GemvTile:
+    """gemv/mod.rs:16-20."""
+
+    rows: int
+    blocks: int
+
+    def fits(self, rows: int, cols: int) -> bool:
+        """gemv/mod.rs:60-64."""
+        return rows % self.rows == 0 and cols % Q8_BLOCK == 0 and (cols // Q8_BLOCK) % self.blocks == 0
+
+
+DEFAULT_GEMV_TILE = GemvTile(rows=16, blocks=4)  # gemv/mod.rs:22-25
+FP8_TARGET_ROW_TILES = 64
+FP8_MAX_ROW_TILE = 128
+
+
+def _next_pow2(v: int) -> int:
+    return 1 << (v - 1).bit_length() if v > 1 else 1
+
+
+def fp8_tile(rows: int, cols: int, block_n: int, block_k: int, groups: int) -> GemvTile:
+    """gemv/mod.rs:30-54: about 64 row tiles, at most 128 rows, power of two."""
+    if not (rows > 0 and cols > 0 and block_n > 0 and block_k > 0 and groups > 0):
+        raise ShapeError("fp8_tile: sizes must be positive")
+    target = _next_pow2(min(max(-(-rows * groups // FP8_TARGET_ROW_TILES), 1), FP8_MAX_ROW_TILE))
+    t_rows, t_blocks = target, DEFAULT_GEMV_TILE.blocks
+    while rows % t_rows != 0 or block_n % t_rows != 0:
+        t_rows //= 2
+    while (cols // Q8_BLOCK) % t_blocks != 0 or block_k % (t_blocks * Q8_BLOCK) != 0:
+        t_blocks //= 2
+    return GemvTile(t_rows, t_blocks)
+
+
+def row_scaled_tile(rows: int, cols: int, groups: int) -> GemvTile:
+    """gemv/mod.rs:56-58."""
+    return fp8_tile(rows, cols, rows, cols, groups)
+
+
+def _dtype_code(t) -> int:
+    import torch
+    if t.dtype == torch.float32:
+        return N.FPB_F32
+    if t.dtype == torch.bfloat16:
+        return N.FPB_BF16
+    raise TypeError(f"unsupported dtype {t.dtype}")
+
+
+class Gemv:
+    """gemv/mod.rs:66-123 for ``Weight::Nvfp4``."""
+
+    def __init__(self, weight: Nvfp4Matrix, x, y, tile: GemvTile, rows: range | None = None):
+        self.weight, self.x, self.y, self.tile = weight, x, y, tile
+        self.rows = rows if rows is not None else range(0, weight.rows)
+        n = len(self.rows)
+        batch = x.shape[0]
+        if batch <= 0 or not tile.fits(n, weight.cols):
+            raise ShapeError(f"GEMV tile {tile} does not fit {n}x{weight.cols}")
+        if x.numel() != batch * weight.cols:
+            raise ShapeError(f"x has {x.numel()} elements, expected {batch}x{weight.cols}")
+        if y.numel() != batch * n:
+            raise ShapeError(f"y has {y.numel()} elements, expected {batch}x{n}")
+        if not (x.is_contiguous() and y.is_contiguous()):
+            raise ShapeError("x and y must be contiguous")
+
+    def submit(self, sink: Sink | None = None) -> None:
+        sink = sink or Eager()
+        batch = self.x.shape[0]
+
+        def launch(stream):
+            N.call("fpb_nvfp4_gemv", self.weight.handle, self.rows.start, self.rows.stop,
+                   self.x.data_ptr(), _dtype_code(self.x), self.y.data_ptr(), _dtype_code(self.y),
+                   batch, stream)
+
+        sink.run("gemv", launch)
+
+
+def gemv(weight: Nvfp4Matrix, x, y, tile: GemvTile = DEFAULT_GEMV_TILE, rows: range | None = None) -> Gemv:
+    """gemv/mod.rs:74-87.  x: [batch, cols] (the reference's [B, K/32, 32]
+    is the same memory), y: [batch, rows]."""
+    return Gemv(weight, x, y, tile, rows)
+
+
+class ExpertGemvView:
+    """gemv/mod.rs:126-206 for ``Weight::Nvfp4``."""
+
+    def __init__(self, weight: Nvfp4Matrix, x, selection, y, rows_per_expert: int, input_stride: int,
+                 tile: GemvTile):
+        dims = selection.dims
+        if weight.rows != dims.experts * rows_per_expert:
+            raise ShapeError("expert GEMV: weight rows != experts * rows_per_expert")
+        if not tile.fits(rows_per_expert, weight.cols):
+            raise ShapeError(f"GEMV tile {tile} does not fit {rows_per_expert}x{weight.cols}")
+        self.weight, self.x, self.selection, self.y = weight, x, selection, y
+        self.rows_per_expert, self.input_stride = rows_per_expert, input_stride
+        self.slots = selection.slots
+
+    def submit(self, sink: Sink | None = None) -> None:
+        sink = sink or Eager()
+
+        def launch(stream):
+            N.call("fpb_nvfp4_expert_gemv", self.weight.handle, self.x.data_ptr(), _dtype_code(self.x),
+                   self.selection.indices.data_ptr(), self.slots, self.rows_per_expert, self.input_stride,
+                   self.y.data_ptr(), _dtype_code(self.y), stream)
+
+        sink.run("expert_gemv", launch)
+
+
+def expert_gemv_weight_view(weight: Nvfp4Matrix, x, selection, y, rows_per_expert: int, input_stride: int,
+                            tile: GemvTile = DEFAULT_GEMV_TILE) -> ExpertGemvView:
+    """gemv/mod.rs:137-156."""
+    return ExpertGemvView(weight, x, selection, y, rows_per_expert, input_stride, tile)
+
+
+__all__ = ["GemvTile", "DEFAULT_GEMV_TILE", "fp8_tile", "row_scaled_tile", "gemv", "Gemv",
+           "expert_gemv_weight_view", "ExpertGemvView", "ShapeError", "current_stream_handle"]

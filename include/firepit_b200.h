@@ -1,0 +1,167 @@
+/*
+ * firepit_b200 — C ABI of the B200-native (sm_100a) quantized-matmul hot path.
+ *
+ * These entry points sit behind firepit-kernels' Rust API (crate
+ * `firepit-kernels` of almightychang/firepit).  Each declaration names the
+ * reference item it replaces as `path:line`, relative to that crate's
+ * `src/` directory unless stated otherwise.
+ *
+ * Conventions
+ *  - Every function returns an `int` status (`FPB_OK` == 0).  Nothing aborts
+ *    and nothing throws across this boundary.  `fpb_last_error()` gives the
+ *    calling thread's message for the last non-zero status.
+ *  - The reference panics (`assert!`) on shape or tile mismatches and returns
+ *    `Err(&'static str)` on bad formats.  Here those cases return
+ *    `FPB_ERR_SHAPE` and `FPB_ERR_FORMAT`.
+ *  - Device pointers are plain `void*` or typed pointers.  The caller owns
+ *    them.  Handles (`fpb_nvfp4_matrix`, `fpb_fp8_matrix`) own the device
+ *    copies they were created with and free them in `*_destroy`.
+ *  - Every launch takes an explicit `cudaStream_t` (passed as `void*`; NULL
+ *    is the legacy default stream).  No call synchronises the stream unless
+ *    its comment says so.  Calls that take a `workspace` allocate nothing.
+ *  - Dtype codes: FPB_F32 (IEEE binary32) and FPB_BF16 (bfloat16).
+ */
+#ifndef FIREPIT_B200_H
+#define FIREPIT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+enum {
+  FPB_OK = 0,
+  FPB_ERR_INVALID_ARGUMENT = 1, /* null pointer, zero size, bad enum        */
+  FPB_ERR_SHAPE = 2,            /* the reference's assert! on shapes/tiles  */
+  FPB_ERR_FORMAT = 3,           /* the reference's Err(..) on bad formats   */
+  FPB_ERR_CUDA = 4,             /* a CUDA runtime call failed               */
+  FPB_ERR_UNSUPPORTED = 5,      /* shape outside this build's kernels       */
+  FPB_ERR_SELECTION = 6,        /* ExpertSelectionError (moe.rs:262-269)    */
+  FPB_ERR_WORKSPACE = 7,        /* workspace too small                      */
+  FPB_ERR_NO_DEVICE = 8         /* no CUDA device visible                   */
+};
+
+enum { FPB_F32 = 0, FPB_BF16 = 1 };
+
+/* Library / error reporting ------------------------------------------------ */
+const char *fpb_version(void);
+const char *fpb_status_string(int status);
+/* Message for the calling thread's last non-zero status ("" if none). */
+const char *fpb_last_error(void);
+/* Number of kernel launches this process made through the library. */
+uint64_t fpb_launch_count(void);
+
+/* ---- formats: scalar codecs (host, no GPU needed) -------------------------
+ * e2m1 / e4m3 decode follow tests/nvfp4_oracle.rs:24-42 (crate tests/) and
+ * src/checkpoint.rs:338-349 of crate `firepit`; the quantize rule
+ * (RNE, satfinite) has no counterpart in the reference.                    */
+float fpb_e2m1_to_f32(uint8_t code);
+float fpb_e4m3_to_f32(uint8_t bits);
+uint8_t fpb_f32_to_e2m1(float value);
+uint8_t fpb_f32_to_e4m3(float value);
+
+/* ---- seeded synthetic data (random-init weights and inputs) ---------------
+ * Replaces the role of Model::random_from_config's LCG (firepit
+ * src/testing.rs:15-151) for the quantized formats: element i of
+ * (seed, stream_id) is mean + stddev * N(0,1) from Philox4x32-10 +
+ * Box-Muller, independent of every other element; out is f32 or bf16
+ * (RNE) [count], starting at element `offset`. */
+int fpb_synth_normal(uint64_t seed, uint32_t stream_id, uint64_t offset, size_t count,
+                     float mean, float stddev, int dtype, void *out, void *stream);
+
+/* ---- NVFP4 weight matrix ------------------------------------------------- */
+typedef struct fpb_nvfp4_matrix fpb_nvfp4_matrix;
+
+/* HostNvfp4Matrix::from_parts validation (weights/nvfp4.rs:47-64), host side:
+ * rows>0, cols>0, cols%32==0, lengths match, no NaN e4m3 scale (0x7f/0xff),
+ * globals finite and >= 0.  `row_globals` has `rows` entries (stacked
+ * matrices keep one global per source matrix, weights/nvfp4.rs:84-97). */
+int fpb_nvfp4_validate(const uint8_t *packed, size_t packed_len,
+                       const uint8_t *scales, size_t scales_len,
+                       const float *row_globals, size_t rows, size_t cols);
+
+/* HostNvfp4Matrix::{from_parts,stack} + upload (weights/nvfp4.rs:47-120).
+ * Host arrays: packed [rows, cols/2] (even column in the low nibble),
+ * scales [rows, cols/16] e4m3, row_globals [rows] f32.  Copies to device
+ * and synchronises `stream`. */
+int fpb_nvfp4_matrix_create(const uint8_t *packed, const uint8_t *scales,
+                            const float *row_globals, size_t rows, size_t cols,
+                            void *stream, fpb_nvfp4_matrix **out);
+/* Same, from device arrays in the same layout (device-to-device copy). The
+ * format is validated on the device; synchronises `stream`. */
+int fpb_nvfp4_matrix_create_device(const uint8_t *packed, const uint8_t *scales,
+                                   const float *row_globals, size_t rows,
+                                   size_t cols, void *stream,
+                                   fpb_nvfp4_matrix **out);
+int fpb_nvfp4_matrix_destroy(fpb_nvfp4_matrix *m);
+int fpb_nvfp4_matrix_shape(const fpb_nvfp4_matrix *m, size_t *rows,
+                           size_t *cols);
+/* Device pointers of the handle's storage (row-major, as uploaded). */
+int fpb_nvfp4_matrix_device_ptrs(const fpb_nvfp4_matrix *m, const uint8_t **packed,
+                                 const uint8_t **scales, const float **row_globals);
+
+/* Copies the handle's storage to host arrays (same layout as create);
+ * synchronises `stream`. */
+int fpb_nvfp4_matrix_download(const fpb_nvfp4_matrix *m, uint8_t *packed, uint8_t *scales,
+                              float *row_globals, void *stream);
+
+/* ---- quantize (no reference counterpart: BASELINE's rule) ---------------
+ * global = amax / (6*448) per block of `rows_per_global` rows; block scale
+ * s = RN_e4m3_satfinite((block_amax / 6) / global); code =
+ * RN_e2m1_satfinite(w / (e4m3(s) * global)).  Two launches (amax, encode).
+ * `amax_scratch` is rows/rows_per_global floats of device scratch.  Outputs
+ * packed [rows, cols/2], scales [rows, cols/16], row_globals [rows]. */
+int fpb_nvfp4_quantize(const void *w, int w_dtype, size_t rows, size_t cols,
+                       size_t rows_per_global, uint8_t *packed, uint8_t *scales,
+                       float *row_globals, float *amax_scratch, void *stream);
+/* Dequantize to f32 [rows, cols] with the ModelOpt order
+ * E2M1[c] * (e4m3(s) * g) (firepit src/checkpoint.rs:401-420). */
+int fpb_nvfp4_dequantize(const fpb_nvfp4_matrix *m, float *out, void *stream);
+
+/* ---- decode GEMV -----------------------------------------------------------
+ * gemv(&Weight::Nvfp4, x, y, tile).submit(sink)
+ *   (gemv/mod.rs:74-123 -> gemv/nvfp4.rs:120-149, kernel :13-60).
+ * y[b, r] = g[r] * sum_k E2M1[w[r,k]] * e4m3(s[r,k/16]) * x[b,k]
+ * for rows r in [row_begin, row_end) of the matrix (row_end == 0 means all
+ * rows).  x: [batch, cols] (x_dtype), y: [batch, row_end-row_begin]
+ * (y_dtype), both contiguous.  1 <= batch <= 16. */
+int fpb_nvfp4_gemv(const fpb_nvfp4_matrix *w, size_t row_begin, size_t row_end,
+                   const void *x, int x_dtype, void *y, int y_dtype, int batch,
+                   void *stream);
+
+/* expert_gemv_weight_view(&Weight::Nvfp4, x, selection, y, rows_per_expert,
+ * input_stride, tile) (gemv/mod.rs:137-206 -> gemv/nvfp4.rs:151-182,
+ * kernel :62-107).  For slot s in [0, slots):
+ *   y[s, r] = sum over K of W[expert_ids[s]*rows_per_expert + r, :] . x[s*input_stride, :]
+ * expert_ids: device int32 [slots] (ExpertSelection::indices, padding
+ * entries beyond `slots` are not read).  x: [*, cols], y: [slots,
+ * rows_per_expert]. */
+int fpb_nvfp4_expert_gemv(const fpb_nvfp4_matrix *w, const void *x, int x_dtype,
+                          const int32_t *expert_ids, int slots,
+                          size_t rows_per_expert, int input_stride, void *y,
+                          int y_dtype, void *stream);
+
+/* ---- MoE host bookkeeping (no GPU needed) -------------------------------- */
+/* MoeDims::new (moe.rs:172-225): FPB_ERR_SHAPE on invalid dimensions. */
+int fpb_moe_dims_validate(size_t hidden, size_t intermediate, size_t shared_intermediate,
+                          size_t experts, size_t top_k);
+/* ExpertSelection::parse checks (moe.rs:327-351): FPB_ERR_SELECTION. */
+int fpb_expert_selection_validate(const int32_t *indices, const float *weights, size_t count,
+                                  size_t experts, size_t top_k);
+/* PrefillLayout::max_padded_rows (moe.rs:408-428). */
+int fpb_prefill_layout_max_padded_rows(size_t tokens, size_t experts, size_t top_k,
+                                       size_t tile_rows, size_t *out);
+/* PrefillLayout::parse / from_indices (moe.rs:430-516), host counting sort.
+ * weights may be NULL (from_indices).  See moe_host.cu for the outputs. */
+int fpb_prefill_layout_host(const int32_t *indices, const float *weights, size_t count,
+                            size_t experts, size_t top_k, size_t tile_rows, int32_t *token_rows,
+                            size_t token_rows_cap, size_t *padded_rows, int32_t *tile_experts,
+                            size_t tile_cap, size_t *n_tiles, int32_t *inverse, size_t *ranges);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FIREPIT_B200_H */

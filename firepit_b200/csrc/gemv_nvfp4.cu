@@ -99,15 +99,20 @@ __device__ __forceinline__ int prescale_exponent(uint32_t amax_bits) {
 }
 
 template <int C, int NG, bool XLO>
-__global__ void __launch_bounds__(256, (C >= 8 ? 1 : 2)) gemv_nvfp4_kernel(GemvArgs a) {
+__global__ void __launch_bounds__(256, (C >= 4 ? 1 : 2)) gemv_nvfp4_kernel(GemvArgs a) {
   extern __shared__ __align__(16) unsigned char smem[];
-  constexpr int kFragsPerChunk = 8 * NG * 32;  // uint2 entries per 128-column chunk
   const int chunks = a.chunks;
+  const int batch = a.batch;
+  // Compact B-fragment store: entry ((c*8 + j)*batch + n)*4 + q holds
+  // x[n][c*128 + q*32 + 4j .. +3] as two f16x2 words, i.e. exactly what lane
+  // (g = n % 8, q) feeds MMA j of chunk c.  Rows n >= batch are not stored:
+  // their fragments are zero.
+  const int n_entries = chunks * 8 * batch * 4;
   uint2 *xs_hi = reinterpret_cast<uint2 *>(smem);
-  uint2 *xs_lo = xs_hi + (XLO ? chunks * kFragsPerChunk : 0);
+  uint2 *xs_lo = xs_hi + (XLO ? n_entries : 0);
   const int wk_count = (chunks + C - 1) / C;
   const int g_count = max(1, (int)(blockDim.x / 32) / wk_count);
-  float4 *red = reinterpret_cast<float4 *>(xs_hi + (XLO ? 2 : 1) * chunks * kFragsPerChunk);
+  float4 *red = reinterpret_cast<float4 *>(xs_hi + (XLO ? 2 : 1) * n_entries);
   __shared__ uint32_t amax_s[16];
   __shared__ float unscale_s[16];
 
@@ -162,36 +167,70 @@ __global__ void __launch_bounds__(256, (C >= 8 ? 1 : 2)) gemv_nvfp4_kernel(GemvA
   uint16_t scur[2][C];
   load(0, wcur, scur);
 
+  // Programmatic dependent launch: weights are immutable once their handle
+  // exists (handle creation synchronises its stream), so their loads are
+  // issued before waiting on the preceding kernel; x and y are touched only
+  // after griddepcontrol.wait, which returns once the preceding grid has
+  // completed and its writes are visible.  The next kernel in the stream may
+  // start launching now.
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+
   // ---- stage x as B fragments ----------------------------------------------
+  // Pass 1: per-row amax, 8 elements per vector load, all loads of a thread
+  // independent of each other so that they are in flight together.
   if (tid < 16) amax_s[tid] = 0;
   __syncthreads();
-  for (int n = 0; n < a.batch; ++n) {
+  {
+    const int vec_per_row = K >> 3;
+    const int total_vec = batch * vec_per_row;
     uint32_t m = 0;
-    for (int k = tid; k < K; k += blockDim.x) {
-      float v = XLO ? reinterpret_cast<const float *>(a.x)[x_off + (long long)n * K + k]
-                    : bf16_bits_to_f32(reinterpret_cast<const uint16_t *>(a.x)[x_off + (long long)n * K + k]);
-      m = max(m, __float_as_uint(v) & 0x7fffffffu);
+    int cur_n = -1;
+#pragma unroll 2
+    for (int v = tid; v < total_vec; v += blockDim.x) {
+      int n = v / vec_per_row;
+      long long base = x_off + (long long)n * K + (long long)(v - n * vec_per_row) * 8;
+      uint32_t vm;
+      if (XLO) {
+        const float4 *p = reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(a.x) + base);
+        float4 f0 = p[0], f1 = p[1];
+        vm = max(max(max(__float_as_uint(f0.x) & 0x7fffffffu, __float_as_uint(f0.y) & 0x7fffffffu),
+                     max(__float_as_uint(f0.z) & 0x7fffffffu, __float_as_uint(f0.w) & 0x7fffffffu)),
+                 max(max(__float_as_uint(f1.x) & 0x7fffffffu, __float_as_uint(f1.y) & 0x7fffffffu),
+                     max(__float_as_uint(f1.z) & 0x7fffffffu, __float_as_uint(f1.w) & 0x7fffffffu)));
+      } else {
+        uint4 b = *reinterpret_cast<const uint4 *>(reinterpret_cast<const uint16_t *>(a.x) + base);
+        // bf16 magnitude bits order like the floats they widen to
+        uint32_t w0 = b.x & 0x7fff7fffu, w1 = b.y & 0x7fff7fffu, w2 = b.z & 0x7fff7fffu,
+                 w3 = b.w & 0x7fff7fffu;
+        vm = max(max(max(w0 & 0xffffu, w0 >> 16), max(w1 & 0xffffu, w1 >> 16)),
+                 max(max(w2 & 0xffffu, w2 >> 16), max(w3 & 0xffffu, w3 >> 16))) << 16;
+      }
+      if (n != cur_n) {
+        if (cur_n >= 0) atomicMax(&amax_s[cur_n], m);
+        m = 0;
+        cur_n = n;
+      }
+      m = max(m, vm);
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (lane == 0) atomicMax(&amax_s[n], m);
+    if (cur_n >= 0) atomicMax(&amax_s[cur_n], m);
   }
   __syncthreads();
   if (tid < 16) {
     int F = prescale_exponent(amax_s[tid]);
     unscale_s[tid] = __uint_as_float((uint32_t)(127 - F) << 23);
   }
-  const int total = chunks * kFragsPerChunk;
-  for (int i = tid; i < total; i += blockDim.x) {
-    int l = i & 31;
-    int rest = i >> 5;
-    int ng = rest % NG;
-    int cj = rest / NG;  // c * 8 + j
+  // Pass 2: scale by 2^F (exact), convert to f16 (hi, and lo for f32 input).
+#pragma unroll 2
+  for (int e = tid; e < n_entries; e += blockDim.x) {
+    int q = e & 3;
+    int t = e >> 2;
+    int n = t % batch;
+    int cj = t / batch;  // c * 8 + j
     int c = cj >> 3, j = cj & 7;
-    int n = ng * 8 + (l >> 2), q = l & 3;
     int k = c * 128 + q * 32 + 4 * j;
     uint2 hi = make_uint2(0, 0), lo = make_uint2(0, 0);
-    if (n < a.batch && k < K) {
+    if (k < K) {
       float up = __uint_as_float((uint32_t)(127 + prescale_exponent(amax_s[n])) << 23);
       float v[4];
       if (XLO) {
@@ -205,7 +244,7 @@ __global__ void __launch_bounds__(256, (C >= 8 ? 1 : 2)) gemv_nvfp4_kernel(GemvA
         v[2] = __uint_as_float(b.y << 16); v[3] = __uint_as_float(b.y & 0xffff0000u);
       }
 #pragma unroll
-      for (int t = 0; t < 4; ++t) v[t] = v[t] * up;
+      for (int t2 = 0; t2 < 4; ++t2) v[t2] = v[t2] * up;
       hi.x = pack_half2(v[0], v[1]);
       hi.y = pack_half2(v[2], v[3]);
       if (XLO) {
@@ -215,8 +254,8 @@ __global__ void __launch_bounds__(256, (C >= 8 ? 1 : 2)) gemv_nvfp4_kernel(GemvA
         lo.y = pack_half2(v[2] - f23.x, v[3] - f23.y);
       }
     }
-    xs_hi[i] = hi;
-    if (XLO) xs_lo[i] = lo;
+    xs_hi[e] = hi;
+    if (XLO) xs_lo[e] = lo;
   }
   __syncthreads();
 
@@ -247,16 +286,16 @@ __global__ void __launch_bounds__(256, (C >= 8 ? 1 : 2)) gemv_nvfp4_kernel(GemvA
           for (int t = 0; t < 4; ++t) h[hh][wi * 4 + t] = hmul2(f[t], wi < 2 ? s_lo : s_hi);
         }
       }
-      const uint2 *bh = xs_hi + c * kFragsPerChunk;
-      const uint2 *bl = xs_lo + c * kFragsPerChunk;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
 #pragma unroll
         for (int ng = 0; ng < NG; ++ng) {
-          uint2 b = bh[(j * NG + ng) * 32 + lane];
+          const int n = ng * 8 + g;
+          const int idx = ((c * 8 + j) * batch + n) * 4 + q;
+          uint2 b = n < batch ? xs_hi[idx] : make_uint2(0, 0);
           mma_f16(acc[ng], h[0][2 * j], h[1][2 * j], h[0][2 * j + 1], h[1][2 * j + 1], b.x, b.y);
           if (XLO) {
-            uint2 bb = bl[(j * NG + ng) * 32 + lane];
+            uint2 bb = n < batch ? xs_lo[idx] : make_uint2(0, 0);
             mma_f16(acc[ng], h[0][2 * j], h[1][2 * j], h[0][2 * j + 1], h[1][2 * j + 1], bb.x, bb.y);
           }
         }
@@ -314,6 +353,27 @@ struct GemvConfig {
   int C, wk, g, threads;
 };
 
+constexpr size_t kGemvSmemLimit = 200 * 1024;
+
+static GemvConfig pick_config(int K);
+
+// Dynamic shared memory of one launch: the compact B fragments (2 bytes per
+// element of x, twice for f32 input) and the cross-warp reduction buffer.
+static size_t gemv_smem_bytes(int K, int batch, bool x_f32) {
+  GemvConfig cfg = pick_config(K);
+  size_t chunks = (size_t)(K + 127) / 128;
+  size_t frag = chunks * 8 * (size_t)batch * 4 * sizeof(uint2) * (x_f32 ? 2 : 1);
+  size_t red = (size_t)cfg.wk * cfg.g * (batch > 8 ? 2 : 1) * 32 * sizeof(float4);
+  return frag + red;
+}
+
+// Largest batch per launch whose staging fits in shared memory.
+static int gemv_max_batch(int K, bool x_f32) {
+  int b = 16;
+  while (b > 1 && gemv_smem_bytes(K, b, x_f32) > kGemvSmemLimit) --b;
+  return b;
+}
+
 static GemvConfig pick_config(int K) {
   int chunks = (K + 127) / 128;
   int C = 1;
@@ -351,10 +411,9 @@ static int run_gemv(GemvArgs args, int slots, bool x_f32, cudaStream_t stream) {
   args.chunks = (args.K + 127) / 128;
   args.nrb = (args.rows + 15) / 16;
   int NG = args.batch > 8 ? 2 : 1;
-  size_t frag_bytes = (size_t)args.chunks * 8 * NG * 32 * sizeof(uint2) * (x_f32 ? 2 : 1);
-  size_t red_bytes = (size_t)cfg.wk * cfg.g * NG * 32 * sizeof(float4);
-  size_t smem = frag_bytes + red_bytes;
-  if (smem > 200 * 1024) return fail(FPB_ERR_UNSUPPORTED, "NVFP4 GEMV: x staging needs %zu bytes", smem);
+  size_t smem = gemv_smem_bytes(args.K, args.batch, x_f32);
+  if (smem > kGemvSmemLimit)
+    return fail(FPB_ERR_UNSUPPORTED, "NVFP4 GEMV: x staging needs %zu bytes", smem);
   GemvKernel k = select_kernel(cfg.C, NG, x_f32);
   if (!k) return fail(FPB_ERR_UNSUPPORTED, "NVFP4 GEMV: no kernel for C=%d", cfg.C);
 
@@ -403,7 +462,18 @@ static int run_gemv(GemvArgs args, int slots, bool x_f32, cudaStream_t stream) {
   int grid_x = (int)std::min<long long>(groups, per_slot);
   args.iters = (groups + grid_x - 1) / grid_x;
   dim3 grid(grid_x, slots);
-  k<<<grid, cfg.threads, smem, stream>>>(args);
+  cudaLaunchConfig_t lc{};
+  lc.gridDim = grid;
+  lc.blockDim = dim3(cfg.threads);
+  lc.dynamicSmemBytes = smem;
+  lc.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  cudaError_t le = cudaLaunchKernelEx(&lc, k, args);
+  if (le != cudaSuccess) return cuda_fail(le, "cudaLaunchKernelEx(gemv_nvfp4_kernel)");
   FPB_LAUNCH_CHECK("gemv_nvfp4_kernel");
   return FPB_OK;
 }
@@ -439,9 +509,14 @@ extern "C" int fpb_nvfp4_gemv(const fpb_nvfp4_matrix *w, size_t row_begin, size_
   a.x_slot_stride = 0;
   a.y_slot_stride = 0;
   bool x_f32 = x_dtype == FPB_F32;
-  // f32 inputs with more than 8 rows would need too much shared memory for
-  // both fragment halves at large K: run them 8 rows at a time.
-  int step = (x_f32 && batch > 8 && w->cols > 2048) ? 8 : batch;
+  if (reinterpret_cast<uintptr_t>(x) % 16 != 0)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_gemv: x must be 16-byte aligned");
+  if (w->cols > 8192) return fail(FPB_ERR_UNSUPPORTED, "fpb_nvfp4_gemv: cols %zu > 8192", w->cols);
+  // x is staged whole in shared memory; batches whose staging does not fit
+  // run as several launches over row groups of x (each re-reads W).
+  int step = std::min(batch, gemv_max_batch((int)w->cols, x_f32));
+  if (gemv_smem_bytes((int)w->cols, 1, x_f32) > kGemvSmemLimit)
+    return fail(FPB_ERR_UNSUPPORTED, "fpb_nvfp4_gemv: cols %zu too large for x staging", w->cols);
   for (int b0 = 0; b0 < batch; b0 += step) {
     GemvArgs part = a;
     part.batch = std::min(step, batch - b0);
@@ -465,6 +540,9 @@ extern "C" int fpb_nvfp4_expert_gemv(const fpb_nvfp4_matrix *w, const void *x, i
   if (input_stride < 0) return fail(FPB_ERR_SHAPE, "fpb_nvfp4_expert_gemv: input_stride < 0");
   if ((x_dtype != FPB_F32 && x_dtype != FPB_BF16) || (y_dtype != FPB_F32 && y_dtype != FPB_BF16))
     return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_expert_gemv: dtype");
+  if (reinterpret_cast<uintptr_t>(x) % 16 != 0)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_expert_gemv: x must be 16-byte aligned");
+  if (w->cols > 8192) return fail(FPB_ERR_UNSUPPORTED, "fpb_nvfp4_expert_gemv: cols %zu > 8192", w->cols);
   GemvArgs a{};
   a.packed = w->packed;
   a.scales = w->scales;

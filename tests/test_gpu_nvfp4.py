@@ -42,7 +42,8 @@ def test_synth_normal_bit_exact(F, torch, seed, stream, offset):
     cpu = O.synth_normal(n, seed, stream, mean=0.25, std=0.5, offset=offset)
     assert np.array_equal(dev.view(np.uint32), cpu.view(np.uint32))
     assert abs(cpu.mean() - 0.25) < 0.01 and abs(cpu.std() - 0.5) < 0.01
-    bf = F.synth_normal((4096,), seed=seed, stream_id=stream, dtype=torch.bfloat16, offset=offset)
+    bf = F.synth_normal((4096,), seed=seed, stream_id=stream, mean=0.25, std=0.5, dtype=torch.bfloat16,
+                        offset=offset)
     assert np.array_equal(bf.view(torch.int16).cpu().numpy().view(np.uint16), O.bf16_bits(cpu[:4096]))
 
 
@@ -78,8 +79,7 @@ def test_quantize_edge_values(F, torch):
 
 
 def test_dequantize_bit_exact_and_roundtrip(F, torch):
-    rows, cols = 128, 256
-    packed, scales, g, _, _ = R.kernels_case(1, 29)[:5]
+    packed, scales, g, rows, cols = R.kernels_case(1, 29)[:5]
     m = host_matrix(F, packed, scales, g, rows, cols).upload()
     dq = m.dequantize().cpu().numpy()
     ref = O.nvfp4_dequantize(packed, scales, g, rows, cols)

@@ -2,29 +2,39 @@
 //
 // y[b, r] = g[r] * sum_k E2M1[w[r,k]] * e4m3(s[r,k/16]) * x[b,k]
 //
-// Design (HBM-bound; the instruction budget per weight element at full HBM
-// bandwidth is about three thread-instructions, so arithmetic must be cheap):
-//  * Each lane streams 16 bytes (32 codes) of one weight row per load
-//    (128-bit, non-coherent, no L1 allocation).  A warp covers 16 rows x
-//    128 columns per chunk: lanes 4g..4g+3 read rows g and g+8.
+// Design.  The path is HBM-bound (3.5 FLOP/B); the per-element arithmetic
+// must stay below the time the element takes to arrive, and the kernel has no
+// phase that waits on anything but its own loads.
+//  * A CTA has up to 16 warps.  Every warp owns a fixed slice of K (C chunks
+//    of 128 columns) for the whole kernel, so its share of x is loaded once,
+//    straight into registers as ready-made MMA B fragments; there is no
+//    shared-memory staging and no barrier before the first MMA.
+//  * Weights stream with 128-bit non-coherent loads that do not allocate in
+//    L1: per chunk a warp covers 16 rows x 128 columns, lanes 4g..4g+3 reading
+//    rows g and g+8.  The next row block's loads are issued before the current
+//    one is computed.
 //  * Codes become f16 with `cvt.rn.f16x2.e2m1x2` and are multiplied by their
 //    e4m3 block scale in f16.  e2m1 * e4m3 is exact in f16 (at most six
 //    significant bits, magnitude in [2^-10, 2688]), so the dequantized weight
 //    equals the reference's E2M1 * scale exactly.
 //  * The dot products run on the tensor cores as m16n8k16 MMAs with f32
-//    accumulation: weights are the A operand, the (up to 8 per MMA) input
-//    vectors the B operand.  The MMA's k order is a permutation of the
-//    physical columns that A and B share, which is free for a dot product.
-//  * x is staged once per CTA in shared memory as ready-made B fragments.  To
-//    keep them exact in f16, each input row is scaled by a power of two so
-//    that its largest magnitude lands in [2^14, 2^15); bf16 inputs are then
-//    exact (elements below amax * 2^-29 round to f16 subnormals, absolute
-//    error < amax * 2^-40).  f32 inputs are split into an f16 hi and lo part
-//    (22 significant bits) and take two MMAs, the f16 counterpart of the
-//    reference's bf16 hi/lo split (gemm/nvfp4.rs:33-36).
-//  * The per-lane partial sums of the warps that share a row block are added
-//    in shared memory; the result is unscaled (exact power of two), times the
-//    row global, and stored as f32 or bf16.
+//    accumulation (two independent accumulator chains): weights are the A
+//    operand, up to 8 input rows per MMA the B operand.  The MMA's k order is
+//    a permutation of the physical columns shared by A and B, which a dot
+//    product does not see.
+//  * To keep x exact in f16, each warp scales its slice of each input row by
+//    a power of two that puts the slice's largest magnitude in [2^14, 2^15)
+//    and removes it (exactly) from its partial sums.  bf16 inputs are then
+//    exact, except elements below amax * 2^-29, which round to f16 subnormals
+//    (absolute error < amax * 2^-40).  f32 inputs are split into f16 hi and
+//    lo parts (22 significant bits) and take two MMAs, the f16 counterpart of
+//    the reference's bf16 hi/lo split (gemm/nvfp4.rs:33-36).
+//  * The warps sharing a row block add their partials in shared memory (one
+//    barrier per row block, double-buffered), then the sum times the row
+//    global is stored as f32 or bf16.
+//  * Programmatic dependent launch: weights are immutable once their handle
+//    exists (handle creation synchronises its stream), so their loads are
+//    issued before griddepcontrol.wait; x is read and y written only after it.
 #include <algorithm>
 #include <mutex>
 #include <utility>
@@ -51,7 +61,8 @@ struct GemvArgs {
   int n_experts;  // expert mode: valid ids are [0, n_experts)
   int chunks;     // ceil(K / 128)
   int nrb;        // ceil(rows / 16)
-  int iters;      // row-block iterations per CTA
+  int wk;         // warps per row block (K slices)
+  int g;          // row blocks per CTA iteration
   int y_bf16;
 };
 
@@ -89,39 +100,48 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   return *reinterpret_cast<uint32_t *>(&h);
 }
 
-// Power-of-two exponent F for a row whose largest magnitude has biased
-// exponent `ef`: amax * 2^F lies in [2^14, 2^15).  Clamped so that 2^F and
-// 2^-F are both normal floats.
+// Power-of-two exponent F for a slice whose largest magnitude has the given
+// float bits: amax * 2^F lies in [2^14, 2^15).  Clamped so that 2^F and 2^-F
+// are both normal floats.
 __device__ __forceinline__ int prescale_exponent(uint32_t amax_bits) {
   int ef = (int)(amax_bits >> 23) & 0xff;
   int F = 141 - ef;
   return max(-126, min(126, F));
 }
 
+// Loads 4 consecutive input values (bf16 or f32) as floats.
+template <bool F32>
+__device__ __forceinline__ void load_x4(const void *x, long long off, float v[4]) {
+  if (F32) {
+    float4 f = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(x) + off);
+    v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+  } else {
+    uint2 b = *reinterpret_cast<const uint2 *>(reinterpret_cast<const uint16_t *>(x) + off);
+    v[0] = __uint_as_float(b.x << 16); v[1] = __uint_as_float(b.x & 0xffff0000u);
+    v[2] = __uint_as_float(b.y << 16); v[3] = __uint_as_float(b.y & 0xffff0000u);
+  }
+}
+
 template <int C, int NG, bool XLO>
-__global__ void __launch_bounds__(256, (C >= 4 ? 1 : 2)) gemv_nvfp4_kernel(GemvArgs a) {
+__global__ void __launch_bounds__(512, 1) gemv_nvfp4_kernel(GemvArgs a) {
   extern __shared__ __align__(16) unsigned char smem[];
-  const int chunks = a.chunks;
-  const int batch = a.batch;
-  // Compact B-fragment store: entry ((c*8 + j)*batch + n)*4 + q holds
-  // x[n][c*128 + q*32 + 4j .. +3] as two f16x2 words, i.e. exactly what lane
-  // (g = n % 8, q) feeds MMA j of chunk c.  Rows n >= batch are not stored:
-  // their fragments are zero.
-  const int n_entries = chunks * 8 * batch * 4;
-  uint2 *xs_hi = reinterpret_cast<uint2 *>(smem);
-  uint2 *xs_lo = xs_hi + (XLO ? n_entries : 0);
-  const int wk_count = (chunks + C - 1) / C;
-  const int g_count = max(1, (int)(blockDim.x / 32) / wk_count);
-  float4 *red = reinterpret_cast<float4 *>(xs_hi + (XLO ? 2 : 1) * n_entries);
-  __shared__ uint32_t amax_s[16];
-  __shared__ float unscale_s[16];
+  float4 *red = reinterpret_cast<float4 *>(smem);  // [2][g][wk][NG][32]
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, q = lane & 3;
+  const int K = a.K, kb2 = K >> 1, kb16 = K >> 4;
+  const int chunks = a.chunks, batch = a.batch;
+  const int wk_count = a.wk, g_count = a.g;
+  const int wk = warp % wk_count, gi = warp / wk_count;
+  const int c_begin = wk * C;
   const int slot = blockIdx.y;
-  const int K = a.K;
-  const int kb2 = K >> 1, kb16 = K >> 4;
+  // The host launches exactly wk * g warps; any other block size would index
+  // past the reduction buffer, so it does nothing (uniform for the CTA).
+  if ((int)blockDim.x != wk_count * g_count * 32) return;
+  // Register double-buffering of the next row block, except where the f32
+  // hi/lo fragments already fill the register budget.
+  constexpr bool kPrefetch = !(XLO && C >= 2);
 
-  // Which weight rows and which input/output rows this CTA serves.
   long long base_row = 0;
   bool slot_ok = true;
   if (a.expert_ids) {
@@ -134,25 +154,22 @@ __global__ void __launch_bounds__(256, (C >= 4 ? 1 : 2)) gemv_nvfp4_kernel(GemvA
   const float *globals = a.globals + base_row;
   const long long x_off = (long long)slot * a.x_slot_stride;
 
-  // ---- weight-row streaming; the first loads are issued before x is staged
-  // so that their HBM latency overlaps the staging work.
-  const int wk = warp % wk_count, gi = warp / wk_count;
-  const bool warp_active = gi < g_count;
-  const int c_begin = wk * C;
-  const int g = lane >> 2, q = lane & 3;
-
+  // Contiguous, balanced range of row-block groups for this CTA.
+  const int total_groups = (a.nrb + g_count - 1) / g_count;
+  const int grp_begin = (int)((long long)blockIdx.x * total_groups / gridDim.x);
+  const int grp_end = (int)((long long)(blockIdx.x + 1) * total_groups / gridDim.x);
+  const int iters = grp_end - grp_begin;
 
   auto load = [&](int it, uint4 (&w)[2][C], uint16_t (&s)[2][C]) {
-    int rb = (it * gridDim.x + blockIdx.x) * g_count + gi;
+    int rb = (grp_begin + it) * g_count + gi;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       int r = rb * 16 + g + 8 * h;
-      bool row_ok = warp_active && slot_ok && rb < a.nrb && r < a.rows;
+      bool row_ok = slot_ok && rb < a.nrb && r < a.rows;
 #pragma unroll
       for (int cc = 0; cc < C; ++cc) {
         int c = c_begin + cc;
-        bool ok = row_ok && c < chunks && (c * 128 + q * 32) < K;
-        if (ok) {
+        if (row_ok && c < chunks && (c * 128 + q * 32) < K) {
           w[h][cc] = ldg_stream_v4(packed + (long long)r * kb2 + c * 64 + q * 16);
           s[h][cc] = ldg_u16(scales + (long long)r * kb16 + c * 8 + 2 * q);
         } else {
@@ -165,158 +182,146 @@ __global__ void __launch_bounds__(256, (C >= 4 ? 1 : 2)) gemv_nvfp4_kernel(GemvA
 
   uint4 wcur[2][C];
   uint16_t scur[2][C];
-  load(0, wcur, scur);
+  if (iters > 0) load(0, wcur, scur);
 
-  // Programmatic dependent launch: weights are immutable once their handle
-  // exists (handle creation synchronises its stream), so their loads are
-  // issued before waiting on the preceding kernel; x and y are touched only
-  // after griddepcontrol.wait, which returns once the preceding grid has
-  // completed and its writes are visible.  The next kernel in the stream may
-  // start launching now.
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
-  // ---- stage x as B fragments ----------------------------------------------
-  // Pass 1: per-row amax, 8 elements per vector load, all loads of a thread
-  // independent of each other so that they are in flight together.
-  if (tid < 16) amax_s[tid] = 0;
-  __syncthreads();
-  {
-    const int vec_per_row = K >> 3;
-    const int total_vec = batch * vec_per_row;
-    uint32_t m = 0;
-    int cur_n = -1;
-#pragma unroll 2
-    for (int v = tid; v < total_vec; v += blockDim.x) {
-      int n = v / vec_per_row;
-      long long base = x_off + (long long)n * K + (long long)(v - n * vec_per_row) * 8;
-      uint32_t vm;
-      if (XLO) {
-        const float4 *p = reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(a.x) + base);
-        float4 f0 = p[0], f1 = p[1];
-        vm = max(max(max(__float_as_uint(f0.x) & 0x7fffffffu, __float_as_uint(f0.y) & 0x7fffffffu),
-                     max(__float_as_uint(f0.z) & 0x7fffffffu, __float_as_uint(f0.w) & 0x7fffffffu)),
-                 max(max(__float_as_uint(f1.x) & 0x7fffffffu, __float_as_uint(f1.y) & 0x7fffffffu),
-                     max(__float_as_uint(f1.z) & 0x7fffffffu, __float_as_uint(f1.w) & 0x7fffffffu)));
-      } else {
-        uint4 b = *reinterpret_cast<const uint4 *>(reinterpret_cast<const uint16_t *>(a.x) + base);
-        // bf16 magnitude bits order like the floats they widen to
-        uint32_t w0 = b.x & 0x7fff7fffu, w1 = b.y & 0x7fff7fffu, w2 = b.z & 0x7fff7fffu,
-                 w3 = b.w & 0x7fff7fffu;
-        vm = max(max(max(w0 & 0xffffu, w0 >> 16), max(w1 & 0xffffu, w1 >> 16)),
-                 max(max(w2 & 0xffffu, w2 >> 16), max(w3 & 0xffffu, w3 >> 16))) << 16;
-      }
-      if (n != cur_n) {
-        if (cur_n >= 0) atomicMax(&amax_s[cur_n], m);
-        m = 0;
-        cur_n = n;
-      }
-      m = max(m, vm);
-    }
-    if (cur_n >= 0) atomicMax(&amax_s[cur_n], m);
-  }
-  __syncthreads();
-  if (tid < 16) {
-    int F = prescale_exponent(amax_s[tid]);
-    unscale_s[tid] = __uint_as_float((uint32_t)(127 - F) << 23);
-  }
-  // Pass 2: scale by 2^F (exact), convert to f16 (hi, and lo for f32 input).
-#pragma unroll 2
-  for (int e = tid; e < n_entries; e += blockDim.x) {
-    int q = e & 3;
-    int t = e >> 2;
-    int n = t % batch;
-    int cj = t / batch;  // c * 8 + j
-    int c = cj >> 3, j = cj & 7;
-    int k = c * 128 + q * 32 + 4 * j;
-    uint2 hi = make_uint2(0, 0), lo = make_uint2(0, 0);
-    if (k < K) {
-      float up = __uint_as_float((uint32_t)(127 + prescale_exponent(amax_s[n])) << 23);
-      float v[4];
-      if (XLO) {
-        float4 f = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(a.x) + x_off +
-                                                     (long long)n * K + k);
-        v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
-      } else {
-        uint2 b = *reinterpret_cast<const uint2 *>(reinterpret_cast<const uint16_t *>(a.x) + x_off +
-                                                   (long long)n * K + k);
-        v[0] = __uint_as_float(b.x << 16); v[1] = __uint_as_float(b.x & 0xffff0000u);
-        v[2] = __uint_as_float(b.y << 16); v[3] = __uint_as_float(b.y & 0xffff0000u);
-      }
+  // ---- this warp's slice of x as B fragments, in registers -------------------
+  // Lane (g, q) feeds batch rows n = ng*8 + g; for chunk cc and MMA j it holds
+  // x[n][k0 + 4j .. k0 + 4j + 3] with k0 = c*128 + q*32.
+  uint32_t xb[C][8][NG][2];
+  uint32_t xl[XLO ? C : 1][8][NG][2];
+  float unscale[NG];
 #pragma unroll
-      for (int t2 = 0; t2 < 4; ++t2) v[t2] = v[t2] * up;
-      hi.x = pack_half2(v[0], v[1]);
-      hi.y = pack_half2(v[2], v[3]);
-      if (XLO) {
-        __half2 h01 = *reinterpret_cast<__half2 *>(&hi.x), h23 = *reinterpret_cast<__half2 *>(&hi.y);
-        float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
-        lo.x = pack_half2(v[0] - f01.x, v[1] - f01.y);
-        lo.y = pack_half2(v[2] - f23.x, v[3] - f23.y);
+  for (int ng = 0; ng < NG; ++ng) {
+    const int n = ng * 8 + g;
+    const bool n_ok = n < batch;
+    uint32_t m = 0;
+#pragma unroll
+    for (int cc = 0; cc < C; ++cc) {
+      const int k0 = (c_begin + cc) * 128 + q * 32;
+      if (n_ok && k0 < K) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float v[4];
+          load_x4<XLO>(a.x, x_off + (long long)n * K + k0 + 4 * j, v);
+#pragma unroll
+          for (int t = 0; t < 4; ++t) m = max(m, __float_as_uint(v[t]) & 0x7fffffffu);
+        }
       }
     }
-    xs_hi[e] = hi;
-    if (XLO) xs_lo[e] = lo;
+    m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = max(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    const int F = prescale_exponent(m);
+    const float up = __uint_as_float((uint32_t)(127 + F) << 23);
+    unscale[ng] = __uint_as_float((uint32_t)(127 - F) << 23);
+#pragma unroll
+    for (int cc = 0; cc < C; ++cc) {
+      const int k0 = (c_begin + cc) * 128 + q * 32;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        uint32_t h0 = 0, h1 = 0, l0 = 0, l1 = 0;
+        if (n_ok && k0 < K) {
+          float v[4];
+          load_x4<XLO>(a.x, x_off + (long long)n * K + k0 + 4 * j, v);  // L1 hit
+#pragma unroll
+          for (int t = 0; t < 4; ++t) v[t] = v[t] * up;
+          h0 = pack_half2(v[0], v[1]);
+          h1 = pack_half2(v[2], v[3]);
+          if (XLO) {
+            float2 f01 = __half22float2(*reinterpret_cast<__half2 *>(&h0));
+            float2 f23 = __half22float2(*reinterpret_cast<__half2 *>(&h1));
+            l0 = pack_half2(v[0] - f01.x, v[1] - f01.y);
+            l1 = pack_half2(v[2] - f23.x, v[3] - f23.y);
+          }
+        }
+        xb[cc][j][ng][0] = h0;
+        xb[cc][j][ng][1] = h1;
+        if (XLO) {
+          xl[XLO ? cc : 0][j][ng][0] = l0;
+          xl[XLO ? cc : 0][j][ng][1] = l1;
+        }
+      }
+    }
   }
-  __syncthreads();
+  // Unscale factors of the accumulator columns n = ng*8 + 2q (+1), held by
+  // lanes 4*(2q) and 4*(2q+1).
+  float us[NG][2];
+#pragma unroll
+  for (int ng = 0; ng < NG; ++ng) {
+    us[ng][0] = __shfl_sync(0xffffffffu, unscale[ng], (2 * q) * 4);
+    us[ng][1] = __shfl_sync(0xffffffffu, unscale[ng], (2 * q + 1) * 4);
+  }
 
-  for (int it = 0; it < a.iters; ++it) {
+  // ---- stream the row blocks ---------------------------------------------------
+  for (int it = 0; it < iters; ++it) {
     uint4 wnext[2][C];
     uint16_t snext[2][C];
-    if (it + 1 < a.iters) load(it + 1, wnext, snext);
+    if (kPrefetch && it + 1 < iters) load(it + 1, wnext, snext);
 
-    float acc[NG][4];
+    float acc2[2][NG][4];
 #pragma unroll
-    for (int ng = 0; ng < NG; ++ng) acc[ng][0] = acc[ng][1] = acc[ng][2] = acc[ng][3] = 0.0f;
+    for (int p = 0; p < 2; ++p)
+#pragma unroll
+      for (int ng = 0; ng < NG; ++ng)
+#pragma unroll
+        for (int t = 0; t < 4; ++t) acc2[p][ng][t] = 0.0f;
 
 #pragma unroll
     for (int cc = 0; cc < C; ++cc) {
-      const int c = c_begin + cc;
-      if (!(warp_active && c < chunks)) continue;
-      uint32_t h[2][16];
+      if (c_begin + cc >= chunks) continue;
+      uint32_t s_lo[2], s_hi[2];
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         uint32_t sc = e4m3x2_to_f16x2(scur[hh][cc]);
-        uint32_t s_lo = __byte_perm(sc, sc, 0x1010), s_hi = __byte_perm(sc, sc, 0x3232);
-        uint32_t words[4] = {wcur[hh][cc].x, wcur[hh][cc].y, wcur[hh][cc].z, wcur[hh][cc].w};
-#pragma unroll
-        for (int wi = 0; wi < 4; ++wi) {
-          uint32_t f[4];
-          e2m1x8_to_f16x8(words[wi], f);
-#pragma unroll
-          for (int t = 0; t < 4; ++t) h[hh][wi * 4 + t] = hmul2(f[t], wi < 2 ? s_lo : s_hi);
-        }
+        s_lo[hh] = __byte_perm(sc, sc, 0x1010);
+        s_hi[hh] = __byte_perm(sc, sc, 0x3232);
       }
+      const uint32_t w0[4] = {wcur[0][cc].x, wcur[0][cc].y, wcur[0][cc].z, wcur[0][cc].w};
+      const uint32_t w1[4] = {wcur[1][cc].x, wcur[1][cc].y, wcur[1][cc].z, wcur[1][cc].w};
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int wi = 0; wi < 4; ++wi) {
+        // word wi holds columns 8wi..8wi+7 of the lane's 32: MMAs 2wi, 2wi+1
+        uint32_t f0[4], f1[4];
+        e2m1x8_to_f16x8(w0[wi], f0);
+        e2m1x8_to_f16x8(w1[wi], f1);
 #pragma unroll
-        for (int ng = 0; ng < NG; ++ng) {
-          const int n = ng * 8 + g;
-          const int idx = ((c * 8 + j) * batch + n) * 4 + q;
-          uint2 b = n < batch ? xs_hi[idx] : make_uint2(0, 0);
-          mma_f16(acc[ng], h[0][2 * j], h[1][2 * j], h[0][2 * j + 1], h[1][2 * j + 1], b.x, b.y);
-          if (XLO) {
-            uint2 bb = n < batch ? xs_lo[idx] : make_uint2(0, 0);
-            mma_f16(acc[ng], h[0][2 * j], h[1][2 * j], h[0][2 * j + 1], h[1][2 * j + 1], bb.x, bb.y);
+        for (int t = 0; t < 4; ++t) {
+          f0[t] = hmul2(f0[t], wi < 2 ? s_lo[0] : s_hi[0]);
+          f1[t] = hmul2(f1[t], wi < 2 ? s_lo[1] : s_hi[1]);
+        }
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+          const int j = 2 * wi + jj;
+#pragma unroll
+          for (int ng = 0; ng < NG; ++ng) {
+            mma_f16(acc2[jj][ng], f0[2 * jj], f1[2 * jj], f0[2 * jj + 1], f1[2 * jj + 1], xb[cc][j][ng][0],
+                    xb[cc][j][ng][1]);
+            if (XLO)
+              mma_f16(acc2[jj][ng], f0[2 * jj], f1[2 * jj], f0[2 * jj + 1], f1[2 * jj + 1],
+                      xl[XLO ? cc : 0][j][ng][0], xl[XLO ? cc : 0][j][ng][1]);
           }
         }
       }
     }
 
-    // ---- cross-warp reduction and epilogue ---------------------------------
-    if (warp_active) {
+    // ---- cross-warp reduction and epilogue -----------------------------------
+    const int buf = it & 1;
+    float4 *rb_red = red + (size_t)buf * g_count * wk_count * NG * 32;
 #pragma unroll
-      for (int ng = 0; ng < NG; ++ng)
-        red[((gi * wk_count + wk) * NG + ng) * 32 + lane] =
-            make_float4(acc[ng][0], acc[ng][1], acc[ng][2], acc[ng][3]);
-    }
+    for (int ng = 0; ng < NG; ++ng)
+      rb_red[((gi * wk_count + wk) * NG + ng) * 32 + lane] =
+          make_float4((acc2[0][ng][0] + acc2[1][ng][0]) * us[ng][0], (acc2[0][ng][1] + acc2[1][ng][1]) * us[ng][1],
+                      (acc2[0][ng][2] + acc2[1][ng][2]) * us[ng][0], (acc2[0][ng][3] + acc2[1][ng][3]) * us[ng][1]);
     __syncthreads();
-    const int rb = (it * gridDim.x + blockIdx.x) * g_count + gi;
-    if (warp_active && wk == 0 && rb < a.nrb) {
+    const int rb = (grp_begin + it) * g_count + gi;
+    if (wk == 0 && rb < a.nrb) {
 #pragma unroll
       for (int ng = 0; ng < NG; ++ng) {
-        float4 sum = red[((gi * wk_count) * NG + ng) * 32 + lane];
+        float4 sum = rb_red[((gi * wk_count) * NG + ng) * 32 + lane];
         for (int w = 1; w < wk_count; ++w) {
-          float4 p = red[((gi * wk_count + w) * NG + ng) * 32 + lane];
+          float4 p = rb_red[((gi * wk_count + w) * NG + ng) * 32 + lane];
           sum.x += p.x; sum.y += p.y; sum.z += p.z; sum.w += p.w;
         }
         const float vals[4] = {sum.x, sum.y, sum.z, sum.w};
@@ -324,8 +329,8 @@ __global__ void __launch_bounds__(256, (C >= 4 ? 1 : 2)) gemv_nvfp4_kernel(GemvA
         for (int t = 0; t < 4; ++t) {
           int r = rb * 16 + g + ((t >> 1) << 3);
           int n = ng * 8 + 2 * q + (t & 1);
-          if (r < a.rows && n < a.batch) {
-            float v = slot_ok ? (vals[t] * unscale_s[n]) * globals[r] : 0.0f;
+          if (r < a.rows && n < batch) {
+            float v = slot_ok ? vals[t] * globals[r] : 0.0f;
             long long off = (long long)slot * a.y_slot_stride + (long long)n * a.y_batch_stride + r;
             if (a.y_bf16)
               reinterpret_cast<__nv_bfloat16 *>(a.y)[off] = __float2bfloat16_rn(v);
@@ -335,15 +340,18 @@ __global__ void __launch_bounds__(256, (C >= 4 ? 1 : 2)) gemv_nvfp4_kernel(GemvA
         }
       }
     }
-    __syncthreads();
-    if (it + 1 < a.iters) {
+    if (it + 1 < iters) {
+      if (kPrefetch) {
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh)
+        for (int hh = 0; hh < 2; ++hh)
 #pragma unroll
-        for (int cc = 0; cc < C; ++cc) {
-          wcur[hh][cc] = wnext[hh][cc];
-          scur[hh][cc] = snext[hh][cc];
-        }
+          for (int cc = 0; cc < C; ++cc) {
+            wcur[hh][cc] = wnext[hh][cc];
+            scur[hh][cc] = snext[hh][cc];
+          }
+      } else {
+        load(it + 1, wcur, scur);
+      }
     }
   }
 }
@@ -353,35 +361,28 @@ struct GemvConfig {
   int C, wk, g, threads;
 };
 
-constexpr size_t kGemvSmemLimit = 200 * 1024;
-
-static GemvConfig pick_config(int K);
-
-// Dynamic shared memory of one launch: the compact B fragments (2 bytes per
-// element of x, twice for f32 input) and the cross-warp reduction buffer.
-static size_t gemv_smem_bytes(int K, int batch, bool x_f32) {
-  GemvConfig cfg = pick_config(K);
-  size_t chunks = (size_t)(K + 127) / 128;
-  size_t frag = chunks * 8 * (size_t)batch * 4 * sizeof(uint2) * (x_f32 ? 2 : 1);
-  size_t red = (size_t)cfg.wk * cfg.g * (batch > 8 ? 2 : 1) * 32 * sizeof(float4);
-  return frag + red;
-}
-
-// Largest batch per launch whose staging fits in shared memory.
-static int gemv_max_batch(int K, bool x_f32) {
-  int b = 16;
-  while (b > 1 && gemv_smem_bytes(K, b, x_f32) > kGemvSmemLimit) --b;
-  return b;
-}
-
+// Up to 16 warps per CTA, each covering 16 rows x 128*C columns; C = 2 only
+// when K needs more than 16 warps (K <= 4096).
 static GemvConfig pick_config(int K) {
   int chunks = (K + 127) / 128;
   int C = 1;
-  while ((chunks + C - 1) / C > 8 && C < 8) C *= 2;
+  while ((chunks + C - 1) / C > 16 && C < 2) C *= 2;
   int wk = (chunks + C - 1) / C;
-  if (wk > 8) return {0, 0, 0, 0};
-  int g = wk <= 8 ? std::max(1, 8 / wk) : 1;
+  if (wk > 16) return {0, 0, 0, 0};
+  int g = std::max(1, 16 / wk);
   return {C, wk, g, wk * g * 32};
+}
+
+// Largest batch rows per launch: x fragments live in registers, so f32 input
+// (hi and lo fragments) or more than one group of 8 rows are limited by the
+// chunks a warp holds.
+static int gemv_max_batch(int K, bool x_f32) {
+  GemvConfig cfg = pick_config(K);
+  return (cfg.C == 1 && !x_f32) ? 16 : 8;  // two 8-row groups only where they fit
+}
+
+static size_t gemv_smem_bytes(const GemvConfig &cfg, int NG) {
+  return 2 * (size_t)cfg.g * cfg.wk * NG * 32 * sizeof(float4);
 }
 
 using GemvKernel = void (*)(GemvArgs);
@@ -392,78 +393,62 @@ static GemvKernel kernel_for() {
 }
 
 static GemvKernel select_kernel(int C, int NG, bool xlo) {
-#define FPB_GEMV_CASE(c)                                                     \
-  if (C == c) {                                                              \
-    if (NG == 1) return xlo ? kernel_for<c, 1, true>() : kernel_for<c, 1, false>(); \
-    return xlo ? kernel_for<c, 2, true>() : kernel_for<c, 2, false>();       \
-  }
-  FPB_GEMV_CASE(1)
-  FPB_GEMV_CASE(2)
-  FPB_GEMV_CASE(4)
-  FPB_GEMV_CASE(8)
-#undef FPB_GEMV_CASE
+  // Instantiated variants are exactly those that fit in registers without
+  // spilling: 16 input rows only with bf16 input and K <= 2048.
+  if (C == 1 && NG == 1) return xlo ? kernel_for<1, 1, true>() : kernel_for<1, 1, false>();
+  if (C == 1 && NG == 2 && !xlo) return kernel_for<1, 2, false>();
+  if (C == 2 && NG == 1) return xlo ? kernel_for<2, 1, true>() : kernel_for<2, 1, false>();
   return nullptr;
 }
 
 static int run_gemv(GemvArgs args, int slots, bool x_f32, cudaStream_t stream) {
   GemvConfig cfg = pick_config(args.K);
-  if (!cfg.C) return fail(FPB_ERR_UNSUPPORTED, "NVFP4 GEMV: K=%d exceeds 8192", args.K);
+  if (!cfg.C) return fail(FPB_ERR_UNSUPPORTED, "NVFP4 GEMV: K=%d exceeds 4096", args.K);
   args.chunks = (args.K + 127) / 128;
   args.nrb = (args.rows + 15) / 16;
-  int NG = args.batch > 8 ? 2 : 1;
-  size_t smem = gemv_smem_bytes(args.K, args.batch, x_f32);
-  if (smem > kGemvSmemLimit)
-    return fail(FPB_ERR_UNSUPPORTED, "NVFP4 GEMV: x staging needs %zu bytes", smem);
+  args.wk = cfg.wk;
+  args.g = cfg.g;
+  const int NG = args.batch > 8 ? 2 : 1;
+  const size_t smem = gemv_smem_bytes(cfg, NG);
   GemvKernel k = select_kernel(cfg.C, NG, x_f32);
   if (!k) return fail(FPB_ERR_UNSUPPORTED, "NVFP4 GEMV: no kernel for C=%d", cfg.C);
 
   // Kernel attributes and occupancy are queried once per (device, kernel,
-  // block size, shared memory) so that repeated calls, including calls made
-  // while a stream is being captured into a CUDA graph, issue no extra
-  // runtime calls.
-  struct OccKey {
+  // block size, shared memory), so that repeated calls, including calls made
+  // while a stream is captured into a CUDA graph, make no extra runtime calls.
+  struct OccEntry {
     int dev;
     GemvKernel k;
     int threads;
     size_t smem;
-  };
-  struct OccEntry {
-    OccKey key;
     int occ;
   };
   static std::mutex mu;
   static std::vector<OccEntry> occ_cache;
-  static std::vector<std::pair<std::pair<int, GemvKernel>, size_t>> smem_set;
   int dev = 0;
   cudaGetDevice(&dev);
   int occ = 0;
   {
     std::lock_guard<std::mutex> lock(mu);
-    size_t have = 0;
-    for (auto &p : smem_set)
-      if (p.first.first == dev && p.first.second == k) have = p.second;
-    if (have < smem) {
-      cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemv)");
-      smem_set.push_back({{dev, k}, smem});
-    }
     for (auto &o : occ_cache)
-      if (o.key.dev == dev && o.key.k == k && o.key.threads == cfg.threads && o.key.smem == smem) occ = o.occ;
+      if (o.dev == dev && o.k == k && o.threads == cfg.threads && o.smem == smem) occ = o.occ;
     if (occ == 0) {
+      // The reduction buffer is at most 32 KB, below the default 48 KB limit
+      // of dynamic shared memory, so the kernel attribute is never touched
+      // (lowering it for one launch would cap every later, larger launch).
+      static_assert(2 * 16 * 2 * 32 * sizeof(float4) <= 48 * 1024, "GEMV reduction buffer");
       cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, cfg.threads, smem);
       if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
       if (occ < 1) occ = 1;
-      occ_cache.push_back({{dev, k, cfg.threads, smem}, occ});
+      occ_cache.push_back({dev, k, cfg.threads, smem, occ});
     }
   }
-  int groups = (args.nrb + cfg.g - 1) / cfg.g;
-  long long resident = (long long)occ * sm_count();
-  long long per_slot = std::max(1LL, resident / std::max(1, slots));
-  int grid_x = (int)std::min<long long>(groups, per_slot);
-  args.iters = (groups + grid_x - 1) / grid_x;
-  dim3 grid(grid_x, slots);
+  const int groups = (args.nrb + cfg.g - 1) / cfg.g;
+  const long long resident = (long long)occ * sm_count();
+  const long long per_slot = std::max(1LL, resident / std::max(1, slots));
+  const int grid_x = (int)std::min<long long>(groups, per_slot);
   cudaLaunchConfig_t lc{};
-  lc.gridDim = grid;
+  lc.gridDim = dim3(grid_x, slots);
   lc.blockDim = dim3(cfg.threads);
   lc.dynamicSmemBytes = smem;
   lc.stream = stream;
@@ -473,7 +458,27 @@ static int run_gemv(GemvArgs args, int slots, bool x_f32, cudaStream_t stream) {
   lc.attrs = attr;
   lc.numAttrs = 1;
   cudaError_t le = cudaLaunchKernelEx(&lc, k, args);
-  if (le != cudaSuccess) return cuda_fail(le, "cudaLaunchKernelEx(gemv_nvfp4_kernel)");
+  if (le == cudaErrorInvalidValue) {
+    // A runtime that refuses the programmatic-serialization attribute for
+    // this launch gets a plain stream-ordered launch instead.
+    cudaGetLastError();
+    lc.numAttrs = 0;
+    le = cudaLaunchKernelEx(&lc, k, args);
+  }
+  if (le != cudaSuccess) {
+    // Report what the runtime knows about the kernel and this launch.
+    cudaGetLastError();
+    cudaFuncAttributes fa{};
+    cudaFuncGetAttributes(&fa, k);
+    int occ_now = -1;
+    cudaError_t oe = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_now, k, cfg.threads, smem);
+    cudaGetLastError();
+    return fail(FPB_ERR_CUDA,
+                "cudaLaunchKernelEx(gemv_nvfp4_kernel): %s; grid (%d,%d) block %d smem %zu; kernel regs %d "
+                "local %zu maxThreads %d maxDynSmem %d; occupancy now %d (%s), cached %d",
+                cudaGetErrorName(le), grid_x, slots, cfg.threads, smem, fa.numRegs, fa.localSizeBytes,
+                fa.maxThreadsPerBlock, fa.maxDynamicSharedSizeBytes, occ_now, cudaGetErrorName(oe), occ);
+  }
   FPB_LAUNCH_CHECK("gemv_nvfp4_kernel");
   return FPB_OK;
 }
@@ -495,28 +500,22 @@ extern "C" int fpb_nvfp4_gemv(const fpb_nvfp4_matrix *w, size_t row_begin, size_
     return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_gemv: dtype");
   if ((size_t)(row_end - row_begin) > 0x7fffffff)
     return fail(FPB_ERR_UNSUPPORTED, "fpb_nvfp4_gemv: too many rows");
+  if (reinterpret_cast<uintptr_t>(x) % 16 != 0)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_gemv: x must be 16-byte aligned");
+  if (w->cols > 4096) return fail(FPB_ERR_UNSUPPORTED, "fpb_nvfp4_gemv: cols %zu > 4096", w->cols);
   GemvArgs a{};
   a.packed = w->packed + row_begin * (w->cols / 2);
   a.scales = w->scales + row_begin * (w->cols / kNvfp4Group);
   a.globals = w->row_globals + row_begin;
-  a.x = x;
-  a.y = y;
   a.expert_ids = nullptr;
   a.rows = (int)(row_end - row_begin);
   a.K = (int)w->cols;
   a.y_bf16 = y_dtype == FPB_BF16;
   a.y_batch_stride = a.rows;
-  a.x_slot_stride = 0;
-  a.y_slot_stride = 0;
-  bool x_f32 = x_dtype == FPB_F32;
-  if (reinterpret_cast<uintptr_t>(x) % 16 != 0)
-    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_gemv: x must be 16-byte aligned");
-  if (w->cols > 8192) return fail(FPB_ERR_UNSUPPORTED, "fpb_nvfp4_gemv: cols %zu > 8192", w->cols);
-  // x is staged whole in shared memory; batches whose staging does not fit
-  // run as several launches over row groups of x (each re-reads W).
-  int step = std::min(batch, gemv_max_batch((int)w->cols, x_f32));
-  if (gemv_smem_bytes((int)w->cols, 1, x_f32) > kGemvSmemLimit)
-    return fail(FPB_ERR_UNSUPPORTED, "fpb_nvfp4_gemv: cols %zu too large for x staging", w->cols);
+  const bool x_f32 = x_dtype == FPB_F32;
+  // More input rows than one launch holds in registers run as several
+  // launches over row groups of x (each re-reads W).
+  const int step = std::min(batch, gemv_max_batch((int)w->cols, x_f32));
   for (int b0 = 0; b0 < batch; b0 += step) {
     GemvArgs part = a;
     part.batch = std::min(step, batch - b0);
@@ -542,7 +541,7 @@ extern "C" int fpb_nvfp4_expert_gemv(const fpb_nvfp4_matrix *w, const void *x, i
     return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_expert_gemv: dtype");
   if (reinterpret_cast<uintptr_t>(x) % 16 != 0)
     return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_expert_gemv: x must be 16-byte aligned");
-  if (w->cols > 8192) return fail(FPB_ERR_UNSUPPORTED, "fpb_nvfp4_expert_gemv: cols %zu > 8192", w->cols);
+  if (w->cols > 4096) return fail(FPB_ERR_UNSUPPORTED, "fpb_nvfp4_expert_gemv: cols %zu > 4096", w->cols);
   GemvArgs a{};
   a.packed = w->packed;
   a.scales = w->scales;

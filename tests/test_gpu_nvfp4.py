@@ -157,7 +157,7 @@ def _synthetic(F, torch, rows, cols, seed=0, rpg=None):
 
 
 @pytest.mark.parametrize("rows,cols", [(4096, 4096), (8192, 2048), (1000, 512), (24, 96), (130, 2080),
-                                       (7, 32), (2048, 8192)])
+                                       (7, 32), (2048, 4000)])
 @pytest.mark.parametrize("batch", [1, 3, 8, 16])
 def test_gemv_shapes_batches(F, torch, rows, cols, batch):
     m, h = _synthetic(F, torch, rows, cols, seed=rows * 7 + cols)
@@ -234,4 +234,8 @@ def test_gemv_errors_are_statuses(F, torch):
     assert st == N.FPB_ERR_SHAPE
     with pytest.raises(F.ShapeError):
         F.gemv(m, torch.zeros(1, 96, device="cuda"), y)
+    big, _ = _synthetic(F, torch, 32, 8192)
+    xb = torch.zeros(1, 8192, device="cuda")
+    st = N.lib.fpb_nvfp4_gemv(big.handle, 0, 0, xb.data_ptr(), 0, y.data_ptr(), 0, 1, None)
+    assert st == N.FPB_ERR_UNSUPPORTED
     torch.cuda.synchronize()

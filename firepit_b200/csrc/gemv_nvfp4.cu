@@ -160,12 +160,15 @@ __global__ void __launch_bounds__(512, 1) gemv_nvfp4_kernel(GemvArgs a) {
   const int grp_end = (int)((long long)(blockIdx.x + 1) * total_groups / gridDim.x);
   const int iters = grp_end - grp_begin;
 
-  auto load = [&](int it, uint4 (&w)[2][C], uint16_t (&s)[2][C]) {
+  // Loads one row block's codes and scales, and (for the warp that writes
+  // the outputs) the row globals the epilogue multiplies by.
+  auto load = [&](int it, uint4 (&w)[2][C], uint16_t (&s)[2][C], float (&gl)[2]) {
     int rb = (grp_begin + it) * g_count + gi;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       int r = rb * 16 + g + 8 * h;
       bool row_ok = slot_ok && rb < a.nrb && r < a.rows;
+      gl[h] = (row_ok && wk == 0) ? __ldg(globals + r) : 0.0f;
 #pragma unroll
       for (int cc = 0; cc < C; ++cc) {
         int c = c_begin + cc;
@@ -180,16 +183,36 @@ __global__ void __launch_bounds__(512, 1) gemv_nvfp4_kernel(GemvArgs a) {
     }
   };
 
-  uint4 wcur[2][C];
-  uint16_t scur[2][C];
-  if (iters > 0) load(0, wcur, scur);
-
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
   // ---- this warp's slice of x as B fragments, in registers -------------------
   // Lane (g, q) feeds batch rows n = ng*8 + g; for chunk cc and MMA j it holds
-  // x[n][k0 + 4j .. k0 + 4j + 3] with k0 = c*128 + q*32.
+  // x[n][k0 + 4j .. k0 + 4j + 3] with k0 = c*128 + q*32.  The lane's 32
+  // consecutive inputs of each chunk are loaded once with 16-byte loads (4
+  // for bf16, 8 for f32), issued before the weight loads so that they are not
+  // queued behind them.
+  constexpr int kVec = XLO ? 8 : 4;
+  uint4 raw[NG][C][kVec];
+#pragma unroll
+  for (int ng = 0; ng < NG; ++ng) {
+    const int n = ng * 8 + g;
+#pragma unroll
+    for (int cc = 0; cc < C; ++cc) {
+      const int k0 = (c_begin + cc) * 128 + q * 32;
+      const bool ok = n < batch && k0 < K;
+      const uint4 *src = reinterpret_cast<const uint4 *>(reinterpret_cast<const char *>(a.x) +
+                                                         (x_off + (long long)n * K + k0) * (XLO ? 4 : 2));
+#pragma unroll
+      for (int v = 0; v < kVec; ++v) raw[ng][cc][v] = ok ? src[v] : make_uint4(0, 0, 0, 0);
+    }
+  }
+
+  uint4 wcur[2][C];
+  uint16_t scur[2][C];
+  float gcur[2];
+  if (iters > 0) load(0, wcur, scur, gcur);
+
   uint32_t xb[C][8][NG][2];
   uint32_t xl[XLO ? C : 1][8][NG][2];
   float unscale[NG];
@@ -200,14 +223,18 @@ __global__ void __launch_bounds__(512, 1) gemv_nvfp4_kernel(GemvArgs a) {
     uint32_t m = 0;
 #pragma unroll
     for (int cc = 0; cc < C; ++cc) {
-      const int k0 = (c_begin + cc) * 128 + q * 32;
-      if (n_ok && k0 < K) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          float v[4];
-          load_x4<XLO>(a.x, x_off + (long long)n * K + k0 + 4 * j, v);
+      for (int v = 0; v < kVec; ++v) {
+        const uint4 r = raw[ng][cc][v];
+        const uint32_t wv[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
-          for (int t = 0; t < 4; ++t) m = max(m, __float_as_uint(v[t]) & 0x7fffffffu);
+        for (int t = 0; t < 4; ++t) {
+          if (XLO) {
+            m = max(m, wv[t] & 0x7fffffffu);
+          } else {
+            const uint32_t mag = wv[t] & 0x7fff7fffu;  // bf16 magnitudes order like their floats
+            m = max(m, max(mag << 16, mag & 0xffff0000u));
+          }
         }
       }
     }
@@ -224,7 +251,16 @@ __global__ void __launch_bounds__(512, 1) gemv_nvfp4_kernel(GemvArgs a) {
         uint32_t h0 = 0, h1 = 0, l0 = 0, l1 = 0;
         if (n_ok && k0 < K) {
           float v[4];
-          load_x4<XLO>(a.x, x_off + (long long)n * K + k0 + 4 * j, v);  // L1 hit
+          if (XLO) {
+            const uint4 r4 = raw[ng][cc][j];
+            v[0] = __uint_as_float(r4.x); v[1] = __uint_as_float(r4.y);
+            v[2] = __uint_as_float(r4.z); v[3] = __uint_as_float(r4.w);
+          } else {
+            const uint4 r4 = raw[ng][cc][j >> 1];
+            const uint32_t b0 = (j & 1) ? r4.z : r4.x, b1 = (j & 1) ? r4.w : r4.y;
+            v[0] = __uint_as_float(b0 << 16); v[1] = __uint_as_float(b0 & 0xffff0000u);
+            v[2] = __uint_as_float(b1 << 16); v[3] = __uint_as_float(b1 & 0xffff0000u);
+          }
 #pragma unroll
           for (int t = 0; t < 4; ++t) v[t] = v[t] * up;
           h0 = pack_half2(v[0], v[1]);
@@ -258,7 +294,8 @@ __global__ void __launch_bounds__(512, 1) gemv_nvfp4_kernel(GemvArgs a) {
   for (int it = 0; it < iters; ++it) {
     uint4 wnext[2][C];
     uint16_t snext[2][C];
-    if (kPrefetch && it + 1 < iters) load(it + 1, wnext, snext);
+    float gnext[2];
+    if (kPrefetch && it + 1 < iters) load(it + 1, wnext, snext, gnext);
 
     float acc2[2][NG][4];
 #pragma unroll
@@ -319,10 +356,16 @@ __global__ void __launch_bounds__(512, 1) gemv_nvfp4_kernel(GemvArgs a) {
     if (wk == 0 && rb < a.nrb) {
 #pragma unroll
       for (int ng = 0; ng < NG; ++ng) {
-        float4 sum = rb_red[((gi * wk_count) * NG + ng) * 32 + lane];
-        for (int w = 1; w < wk_count; ++w) {
-          float4 p = rb_red[((gi * wk_count + w) * NG + ng) * 32 + lane];
-          sum.x += p.x; sum.y += p.y; sum.z += p.z; sum.w += p.w;
+        // All partial loads are independent (unrolled with predication).
+        float4 part[16];
+#pragma unroll
+        for (int w = 0; w < 16; ++w)
+          part[w] = w < wk_count ? rb_red[((gi * wk_count + w) * NG + ng) * 32 + lane]
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+        float4 sum = part[0];
+#pragma unroll
+        for (int w = 1; w < 16; ++w) {
+          sum.x += part[w].x; sum.y += part[w].y; sum.z += part[w].z; sum.w += part[w].w;
         }
         const float vals[4] = {sum.x, sum.y, sum.z, sum.w};
 #pragma unroll
@@ -330,7 +373,7 @@ __global__ void __launch_bounds__(512, 1) gemv_nvfp4_kernel(GemvArgs a) {
           int r = rb * 16 + g + ((t >> 1) << 3);
           int n = ng * 8 + 2 * q + (t & 1);
           if (r < a.rows && n < batch) {
-            float v = slot_ok ? vals[t] * globals[r] : 0.0f;
+            float v = slot_ok ? vals[t] * gcur[t >> 1] : 0.0f;
             long long off = (long long)slot * a.y_slot_stride + (long long)n * a.y_batch_stride + r;
             if (a.y_bf16)
               reinterpret_cast<__nv_bfloat16 *>(a.y)[off] = __float2bfloat16_rn(v);
@@ -349,8 +392,10 @@ __global__ void __launch_bounds__(512, 1) gemv_nvfp4_kernel(GemvArgs a) {
             wcur[hh][cc] = wnext[hh][cc];
             scur[hh][cc] = snext[hh][cc];
           }
+        gcur[0] = gnext[0];
+        gcur[1] = gnext[1];
       } else {
-        load(it + 1, wcur, scur);
+        load(it + 1, wcur, scur, gcur);
       }
     }
   }

@@ -16,3 +16,5 @@ from .weights import (NVFP4_GROUP, Q8_BLOCK, FormatError, HostNvfp4Matrix, Nvfp4
                       quantize_nvfp4)
 
 __version__ = _native.lib.fpb_version().decode()
+from .gemm import (DEFAULT_GEMM_TILE, DEFAULT_GROUPED_GEMM_TILE, GemmTile, Nvfp4Gemm, device_error, nvfp4_gemm,
+                   nvfp4_gemm_view, quantize_act)

@@ -79,6 +79,13 @@ SIGNATURES: dict[str, tuple] = {
     "fpb_nvfp4_dequantize": (i32, [vp, vp, vp]),
     "fpb_nvfp4_gemv": (i32, [vp, sz, sz, vp, i32, vp, i32, i32, vp]),
     "fpb_nvfp4_expert_gemv": (i32, [vp, vp, i32, vp, i32, sz, i32, vp, i32, vp]),
+    "fpb_nvfp4_act_sf_bytes": (sz, [sz, sz]),
+    "fpb_nvfp4_gemm_workspace_bytes": (sz, [sz, sz]),
+    "fpb_nvfp4_quantize_act": (i32, [vp, i32, sz, sz, vp, vp, vp, vp, vp]),
+    "fpb_nvfp4_matrix_prepare_gemm": (i32, [vp, vp]),
+    "fpb_nvfp4_gemm_q": (i32, [vp, sz, sz, vp, vp, vp, sz, vp, i32, vp]),
+    "fpb_nvfp4_gemm": (i32, [vp, sz, sz, vp, i32, sz, vp, i32, vp, sz, vp]),
+    "fpb_device_error": (i32, [C.POINTER(i32), i32]),
     "fpb_moe_dims_validate": (i32, [sz, sz, sz, sz, sz]),
     "fpb_expert_selection_validate": (i32, [vp, vp, sz, sz, sz]),
     "fpb_prefill_layout_max_padded_rows": (i32, [sz, sz, sz, sz, C.POINTER(sz)]),

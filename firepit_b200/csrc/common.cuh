@@ -104,6 +104,12 @@ __device__ __forceinline__ uint8_t f32_to_e4m3(float v) {
   return (uint8_t)(out & 0xff);
 }
 
+// Two floats -> bf16x2 (RNE), first value in the low half.
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+
 __device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) {
   return __uint_as_float(((uint32_t)b) << 16);
 }

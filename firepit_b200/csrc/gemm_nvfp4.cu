@@ -1,0 +1,555 @@
+// NVFP4 prefill GEMM on the 5th-generation tensor cores
+// (crates/firepit-kernels/src/gemm/nvfp4.rs: nvfp4_gemm / nvfp4_gemm_view).
+//
+//   y[m, n] = ga * g[n] * sum_k E2M1[a(m,k)] e4m3(sa(m,k/16)) E2M1[w(n,k)] e4m3(sw(n,k/16))
+//
+// Both operands are NVFP4: the weights as stored in the handle, the
+// activations quantized on the fly (fpb_nvfp4_quantize_act, per-tensor
+// global ga).  One CTA computes a 128 x 128 tile of y:
+//   warp 0      TMA producer: per 256-column K block, A and B tiles (128 rows
+//               x 128 bytes, 128-byte swizzle) and the four 512-byte scale
+//               factor chunks of each operand, into a 4-stage ring;
+//   warp 1      allocates TMEM, copies the stage's scale factors to TMEM
+//               (tcgen05.cp) and issues four
+//               tcgen05.mma.kind::mxf4nvf4.block_scale.block16 (K = 64 each)
+//               accumulating in TMEM; tcgen05.commit frees the stage;
+//   warps 2-5   epilogue: tcgen05.ld of the f32 accumulator, times ga * g[n],
+//               stored as bf16 or f32.
+// No TMA load uses cluster multicast.
+//
+// Scale factors live in the tensor cores' tiled layout: for each 128-row
+// block and each 64-column block, 512 bytes with the factor of row r,
+// 16-column group s at byte (r % 32) * 16 + (r / 32) * 4 + s.  The K blocks
+// are padded to a multiple of four (256 columns) with zero factors.
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "common.cuh"
+#include "matrix_extras.cuh"
+#include "nvfp4_matrix.cuh"
+#include "sm100.cuh"
+
+namespace fpb {
+
+__device__ int g_device_error;  // first failing kernel's error code (0 = none)
+
+constexpr int kBM = 128, kBN = 128, kBKBytes = 128;  // K block = 256 fp4 columns
+constexpr int kStages = 4;
+constexpr int kSfChunk = 512;  // bytes per (128 rows, 64 columns)
+
+__host__ __device__ inline size_t sf_tiled_bytes(size_t rows, size_t cols) {
+  size_t rb = (rows + 127) / 128, kb = (cols + 255) / 256;
+  return rb * kb * 4 * kSfChunk;
+}
+
+// Byte offset of the factor of (row, group) in the tiled layout.
+__host__ __device__ inline size_t sf_tiled_offset(size_t row, size_t group, size_t cols) {
+  size_t kb64_per_rb = (cols + 255) / 256 * 4;
+  size_t rb = row / 128, r = row % 128, kb64 = group / 4, s = group % 4;
+  return (rb * kb64_per_rb + kb64) * kSfChunk + (r % 32) * 16 + (r / 32) * 4 + s;
+}
+
+// Row-major e4m3 scales [rows, cols/16] -> tiled, sign cleared (UE4M3).
+// Padding entries are written as zero.  One thread per output byte.
+__global__ void sf_tile_kernel(const uint8_t *scales, size_t rows, size_t cols, uint8_t *tiled,
+                               size_t total) {
+  size_t kb64_per_rb = (cols + 255) / 256 * 4;
+  size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    size_t chunk = i / kSfChunk, b = i % kSfChunk;
+    size_t rb = chunk / kb64_per_rb, kb64 = chunk % kb64_per_rb;
+    size_t r = (b / 16) + 32 * ((b % 16) / 4), s = b % 4;
+    size_t row = rb * 128 + r, group = kb64 * 4 + s;
+    uint8_t v = 0;
+    if (row < rows && group < cols / 16) v = scales[row * (cols / 16) + group] & 0x7f;
+    tiled[i] = v;
+  }
+}
+
+// Codes of groups whose e4m3 scale is negative get their sign bits flipped,
+// so that (code, |scale|) decodes to the same value.
+__global__ void sign_fold_kernel(const uint8_t *packed, const uint8_t *scales, size_t rows, size_t cols,
+                                 uint8_t *out) {
+  size_t n = rows * cols / 2;
+  size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    size_t row = (2 * i) / cols, col = (2 * i) % cols;
+    uint8_t s = scales[row * (cols / 16) + col / 16];
+    uint8_t p = packed[i];
+    if (s & 0x80) p ^= 0x88;
+    out[i] = p;
+  }
+}
+
+__global__ void any_negative_kernel(const uint8_t *scales, size_t n, int *flag) {
+  size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+    if (scales[i] & 0x80) atomicOr(flag, 1);
+}
+
+// ---- activation quantize: amax, then codes + tiled factors --------------------------
+template <typename T>
+__device__ __forceinline__ float act_load(const T *p, size_t i);
+template <>
+__device__ __forceinline__ float act_load<float>(const float *p, size_t i) { return p[i]; }
+template <>
+__device__ __forceinline__ float act_load<uint16_t>(const uint16_t *p, size_t i) {
+  return bf16_bits_to_f32(p[i]);
+}
+
+template <typename T>
+__global__ void act_amax_kernel(const T *x, size_t n, uint32_t *amax_bits) {
+  uint32_t m = 0;
+  size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+    m = max(m, __float_as_uint(act_load(x, i)) & 0x7fffffffu);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) atomicMax(amax_bits, m);
+}
+
+// One thread per 16-column group: same arithmetic as fpb_nvfp4_quantize, the
+// factor written to the tiled layout and the global to *global_out.
+template <typename T>
+__global__ void act_encode_kernel(const T *x, size_t rows, size_t cols, const uint32_t *amax_bits,
+                                  uint8_t *packed, uint8_t *sf_tiled, float *global_out) {
+  const float global = __fdiv_rn(__uint_as_float(*amax_bits), 2688.0f);
+  if (blockIdx.x == 0 && threadIdx.x == 0) *global_out = global;
+  size_t gpr = cols / kNvfp4Group, n_groups = rows * gpr;
+  size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t gi = (size_t)blockIdx.x * blockDim.x + threadIdx.x; gi < n_groups; gi += stride) {
+    size_t r = gi / gpr, g = gi - r * gpr;
+    float v[kNvfp4Group];
+    const T *src = x + r * cols + g * kNvfp4Group;
+#pragma unroll
+    for (int i = 0; i < kNvfp4Group; ++i) v[i] = act_load(src, i);
+    float bmax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kNvfp4Group; ++i) bmax = fmaxf(bmax, fabsf(v[i]));
+    uint8_t s = 0;
+    if (global > 0.0f) s = f32_to_e4m3(__fdiv_rn(__fdiv_rn(bmax, 6.0f), global));
+    float denom = __fmul_rn(e4m3_to_f32(s), global);
+    uint32_t lo = 0, hi = 0;
+    if (denom > 0.0f) {
+      float q[kNvfp4Group];
+#pragma unroll
+      for (int i = 0; i < kNvfp4Group; ++i) q[i] = __fdiv_rn(v[i], denom);
+      lo = f32x8_to_e2m1x8(q);
+      hi = f32x8_to_e2m1x8(q + 8);
+    }
+    *reinterpret_cast<uint2 *>(packed + r * (cols / 2) + g * (kNvfp4Group / 2)) = make_uint2(lo, hi);
+    sf_tiled[sf_tiled_offset(r, g, cols)] = s;
+  }
+}
+
+}  // namespace fpb
+
+namespace fpb {
+
+struct GemmParams {
+  const uint8_t *a_sf;     // activations' tiled scale factors
+  const uint8_t *b_sf;     // weights' tiled scale factors (whole matrix)
+  const float *a_global;   // device scalar
+  const float *b_globals;  // per weight row, row 0 of the matrix
+  void *y;
+  long long ldy;  // elements between output rows
+  int y_bf16;
+  int M;         // activation rows
+  int N;         // weight rows of the view
+  int n_base;    // first weight row of the view (multiple of 128)
+  int kb_count;  // ceil(K / 256)
+  int *error;    // device error word
+};
+
+constexpr int kTileBytes = kBM * kBKBytes;   // 16 KB per operand per stage
+constexpr int kSfStageBytes = 4 * kSfChunk;  // 2 KB per operand per stage
+constexpr uint32_t kTmemCols = 256;          // accumulator 128 + SFA 64 + SFB 64
+constexpr size_t kGemmSmem = 1024 + kStages * (2 * kTileBytes + 2 * kSfStageBytes) + 256;
+
+__device__ __forceinline__ void report(int *error, volatile int *abort, int code) {
+  *abort = 1;
+  if (error) atomicCAS(error, 0, code);
+}
+
+__global__ void __launch_bounds__(192, 1)
+    nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                      GemmParams p) {
+  using namespace sm100;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *sA = base;
+  uint8_t *sB = sA + kStages * kTileBytes;
+  uint8_t *sSFA = sB + kStages * kTileBytes;
+  uint8_t *sSFB = sSFA + kStages * kSfStageBytes;
+  uint64_t *full = reinterpret_cast<uint64_t *>(sSFB + kStages * kSfStageBytes);
+  uint64_t *empty = full + kStages;
+  uint64_t *tmem_full = empty + kStages;
+  uint32_t *tmem_base_s = reinterpret_cast<uint32_t *>(tmem_full + 1);
+  volatile int *abort_s = reinterpret_cast<volatile int *>(tmem_base_s + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_tile = blockIdx.x, m_tile = blockIdx.y;
+  const int m0 = m_tile * kBM, n0 = n_tile * kBN;
+  const int kb64_per_rb = p.kb_count * 4;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tmem_full, 1);
+    *abort_s = 0;
+    fence_barrier_init();
+    prefetch_tensormap(&tmap_a);
+    prefetch_tensormap(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_base_s, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_base_s;
+  const uint32_t tmem_acc = tmem;
+  auto tmem_sfa = [&](int s, int kk) { return tmem + 128 + s * 16 + kk * 4; };
+  auto tmem_sfb = [&](int s, int kk) { return tmem + 192 + s * 16 + kk * 4; };
+
+  if (warp == 0) {
+    // ---- TMA producer ----------------------------------------------------------
+    if (elect_one()) {
+      const int nb_global = p.n_base / 128 + n_tile;
+      int issued = 0;
+      for (int kb = 0; kb < p.kb_count; ++kb) {
+        const int s = kb % kStages, round = kb / kStages;
+        if (kb >= kStages && !mbar_wait(&empty[s], (round - 1) & 1, abort_s)) {
+          report(p.error, abort_s, 101);
+          break;
+        }
+        mbar_arrive_expect_tx(&full[s], 2 * kTileBytes + 2 * kSfStageBytes);
+        tma_load_2d(sA + s * kTileBytes, &tmap_a, kb * kBKBytes, m0, &full[s]);
+        tma_load_2d(sB + s * kTileBytes, &tmap_b, kb * kBKBytes, p.n_base + n0, &full[s]);
+        bulk_load(sSFA + s * kSfStageBytes, p.a_sf + ((size_t)m_tile * kb64_per_rb + kb * 4) * kSfChunk,
+                  kSfStageBytes, &full[s]);
+        bulk_load(sSFB + s * kSfStageBytes, p.b_sf + ((size_t)nb_global * kb64_per_rb + kb * 4) * kSfChunk,
+                  kSfStageBytes, &full[s]);
+        issued = kb + 1;
+      }
+      // Our own copies must have landed before the CTA may exit.
+      for (int kb = (issued > kStages ? issued - kStages : 0); kb < issued; ++kb)
+        if (!mbar_wait(&full[kb % kStages], (kb / kStages) & 1, abort_s)) report(p.error, abort_s, 102);
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer -------------------------------------------------------------
+    if (elect_one()) {
+      const uint32_t idesc = idesc_nvf4(kBM, kBN);
+      for (int kb = 0; kb < p.kb_count; ++kb) {
+        const int s = kb % kStages, round = kb / kStages;
+        if (!mbar_wait(&full[s], round & 1, abort_s)) {
+          report(p.error, abort_s, 103);
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          tmem_cp_sf(tmem_sfa(s, kk), smem_desc(smem_u32(sSFA + s * kSfStageBytes + kk * kSfChunk), 0, 128, 0));
+          tmem_cp_sf(tmem_sfb(s, kk), smem_desc(smem_u32(sSFB + s * kSfStageBytes + kk * kSfChunk), 0, 128, 0));
+        }
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint64_t a_desc = smem_desc(smem_u32(sA + s * kTileBytes) + kk * 32, 16, 1024, 2);
+          const uint64_t b_desc = smem_desc(smem_u32(sB + s * kTileBytes) + kk * 32, 16, 1024, 2);
+          mma_nvf4(tmem_acc, a_desc, b_desc, idesc, tmem_sfa(s, kk), tmem_sfb(s, kk), (kb | kk) != 0);
+        }
+        tc_commit(&empty[s]);
+      }
+      tc_commit(tmem_full);
+      // Every MMA of this CTA has finished once tmem_full completes.
+      if (!mbar_wait(tmem_full, 0, abort_s)) report(p.error, abort_s, 104);
+    }
+  } else {
+    // ---- epilogue: warps 2..5 cover TMEM lanes (warp % 4) * 32 .. +31 ---------
+    const int qw = warp & 3;
+    const int row = m0 + qw * 32 + lane;
+    if (mbar_wait(tmem_full, 0, abort_s)) {
+      tc_fence_after();
+      const float ga = __ldg(p.a_global);
+#pragma unroll 1
+      for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem_acc + ((uint32_t)(qw * 32) << 16) + c * 32, r);
+        tmem_ld_wait();
+        const int nc = n0 + c * 32;
+        if (row < p.M) {
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int n = nc + j;
+            const float g = n < p.N ? __ldg(p.b_globals + p.n_base + n) : 0.0f;
+            v[j] = (__uint_as_float(r[j]) * ga) * g;
+          }
+          const long long off = (long long)row * p.ldy + nc;
+          const bool full_cols = nc + 32 <= p.N;
+          if (p.y_bf16) {
+            __nv_bfloat16 *yp = reinterpret_cast<__nv_bfloat16 *>(p.y) + off;
+            if (full_cols && (reinterpret_cast<uintptr_t>(yp) & 15) == 0) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 8) {
+                uint4 pk;
+                pk.x = pack_bf16x2(v[j], v[j + 1]);
+                pk.y = pack_bf16x2(v[j + 2], v[j + 3]);
+                pk.z = pack_bf16x2(v[j + 4], v[j + 5]);
+                pk.w = pack_bf16x2(v[j + 6], v[j + 7]);
+                *reinterpret_cast<uint4 *>(yp + j) = pk;
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (nc + j < p.N) yp[j] = __float2bfloat16_rn(v[j]);
+            }
+          } else {
+            float *yp = reinterpret_cast<float *>(p.y) + off;
+            if (full_cols && (reinterpret_cast<uintptr_t>(yp) & 15) == 0) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4)
+                *reinterpret_cast<float4 *>(yp + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (nc + j < p.N) yp[j] = v[j];
+            }
+          }
+        }
+      }
+    } else {
+      report(p.error, abort_s, 105);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+}  // namespace fpb
+
+// ---- host side -------------------------------------------------------------------------
+namespace fpb {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *,
+                                   CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                   CUtensorMapFloatOOBfill);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// dependency on libcuda).
+static EncodeTiledFn encode_fn() {
+  static std::mutex mu;
+  static EncodeTiledFn fn = nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q{};
+    void *p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 2-D byte tensor [rows, row_bytes] read in boxes of 128 bytes x box_rows with
+// 128-byte swizzle; out-of-range elements read as zero.
+int encode_rows_u8(CUtensorMap *map, const void *base, uint64_t rows, uint64_t row_bytes, uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(FPB_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (row_bytes & 15))
+    return fail(FPB_ERR_INVALID_ARGUMENT, "TMA operand must be 16-byte aligned with 16-byte row pitch");
+  cuuint64_t dims[2] = {row_bytes, rows};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {128, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FPB_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return FPB_OK;
+}
+
+static unsigned grid_for(size_t n) {
+  size_t g = (n + 255) / 256, cap = (size_t)sm_count() * 16;
+  return (unsigned)std::max<size_t>(1, std::min(g, cap));
+}
+
+// Builds the GEMM-side copies of a weight matrix once: tiled UE4M3 factors,
+// sign-folded codes when any factor is negative, and the codes' TMA map.
+int prepare_gemm_weights(fpb_nvfp4_matrix *m, cudaStream_t s) {
+  if (m->extras && m->extras->tmap_valid) return FPB_OK;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  if (m->extras && m->extras->tmap_valid) return FPB_OK;
+  if (!m->extras) m->extras = new MatrixExtras();
+  MatrixExtras *x = m->extras;
+  const size_t bytes = sf_tiled_bytes(m->rows, m->cols);
+  if (!x->sf_tiled) {
+    FPB_CUDA_TRY(cudaMalloc(&x->sf_tiled, bytes));
+    x->sf_tiled_bytes = bytes;
+  }
+  sf_tile_kernel<<<grid_for(bytes), 256, 0, s>>>(m->scales, m->rows, m->cols, x->sf_tiled, bytes);
+  FPB_LAUNCH_CHECK("sf_tile_kernel");
+  int *flag = nullptr;
+  int neg = 0;
+  FPB_CUDA_TRY(cudaMalloc(&flag, sizeof(int)));
+  cudaError_t e = cudaMemsetAsync(flag, 0, sizeof(int), s);
+  if (e == cudaSuccess) {
+    any_negative_kernel<<<grid_for(m->rows * m->cols / 16), 256, 0, s>>>(m->scales, m->rows * m->cols / 16, flag);
+    e = cudaGetLastError();
+    count_launch();
+  }
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&neg, flag, sizeof(int), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  cudaFree(flag);
+  if (e != cudaSuccess) return cuda_fail(e, "prepare_gemm_weights");
+  const uint8_t *codes = m->packed;
+  if (neg) {
+    if (!x->packed_folded) FPB_CUDA_TRY(cudaMalloc(&x->packed_folded, m->rows * m->cols / 2));
+    sign_fold_kernel<<<grid_for(m->rows * m->cols / 2), 256, 0, s>>>(m->packed, m->scales, m->rows, m->cols,
+                                                                      x->packed_folded);
+    FPB_LAUNCH_CHECK("sign_fold_kernel");
+    codes = x->packed_folded;
+  }
+  int st = encode_rows_u8(reinterpret_cast<CUtensorMap *>(x->tmap_b), codes, m->rows, m->cols / 2, kBN);
+  if (st) return st;
+  FPB_CUDA_TRY(cudaStreamSynchronize(s));
+  x->tmap_valid = true;
+  return FPB_OK;
+}
+
+template <typename T>
+static int quantize_act_impl(const T *x, size_t rows, size_t cols, uint8_t *packed, uint8_t *sf_tiled,
+                             float *global_out, float *amax_scratch, cudaStream_t s) {
+  FPB_CUDA_TRY(cudaMemsetAsync(amax_scratch, 0, sizeof(uint32_t), s));
+  FPB_CUDA_TRY(cudaMemsetAsync(sf_tiled, 0, sf_tiled_bytes(rows, cols), s));
+  uint32_t *amax = reinterpret_cast<uint32_t *>(amax_scratch);
+  act_amax_kernel<T><<<grid_for(rows * cols), 256, 0, s>>>(x, rows * cols, amax);
+  FPB_LAUNCH_CHECK("act_amax_kernel");
+  act_encode_kernel<T><<<grid_for(rows * cols / 16), 256, 0, s>>>(x, rows, cols, amax, packed, sf_tiled,
+                                                                   global_out);
+  FPB_LAUNCH_CHECK("act_encode_kernel");
+  return FPB_OK;
+}
+
+static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+}  // namespace fpb
+
+using namespace fpb;
+
+extern "C" size_t fpb_nvfp4_act_sf_bytes(size_t m, size_t k) { return sf_tiled_bytes(m, k); }
+
+extern "C" size_t fpb_nvfp4_gemm_workspace_bytes(size_t m, size_t k) {
+  return align256(m * k / 2) + align256(sf_tiled_bytes(m, k)) + 256;
+}
+
+extern "C" int fpb_nvfp4_quantize_act(const void *x, int x_dtype, size_t m, size_t k, uint8_t *packed,
+                                      uint8_t *sf_tiled, float *global_out, float *amax_scratch, void *stream) {
+  if (!x || !packed || !sf_tiled || !global_out || !amax_scratch)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_quantize_act: null pointer");
+  if (m == 0 || k == 0 || k % kQ8Block) return fail(FPB_ERR_SHAPE, "fpb_nvfp4_quantize_act: bad shape");
+  cudaStream_t s = as_stream(stream);
+  if (x_dtype == FPB_F32)
+    return quantize_act_impl(static_cast<const float *>(x), m, k, packed, sf_tiled, global_out, amax_scratch, s);
+  if (x_dtype == FPB_BF16)
+    return quantize_act_impl(static_cast<const uint16_t *>(x), m, k, packed, sf_tiled, global_out, amax_scratch,
+                             s);
+  return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_quantize_act: dtype %d", x_dtype);
+}
+
+extern "C" int fpb_nvfp4_matrix_prepare_gemm(fpb_nvfp4_matrix *w, void *stream) {
+  if (!w) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_matrix_prepare_gemm: null handle");
+  return prepare_gemm_weights(w, as_stream(stream));
+}
+
+extern "C" int fpb_nvfp4_gemm_q(fpb_nvfp4_matrix *w, size_t row_begin, size_t row_end, const uint8_t *a_packed,
+                                const uint8_t *a_sf_tiled, const float *a_global, size_t m, void *y, int y_dtype,
+                                void *stream) {
+  if (!w || !a_packed || !a_sf_tiled || !a_global || !y)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_gemm_q: null pointer");
+  if (row_end == 0) row_end = w->rows;
+  if (row_begin >= row_end || row_end > w->rows)
+    return fail(FPB_ERR_SHAPE, "fpb_nvfp4_gemm_q: row range [%zu, %zu) outside %zu rows", row_begin, row_end,
+                w->rows);
+  if (row_begin % 128)
+    return fail(FPB_ERR_UNSUPPORTED, "fpb_nvfp4_gemm_q: row_begin %zu is not a multiple of 128", row_begin);
+  if (m == 0 || m > (size_t)65535 * kBM) return fail(FPB_ERR_SHAPE, "fpb_nvfp4_gemm_q: m = %zu", m);
+  if (y_dtype != FPB_F32 && y_dtype != FPB_BF16) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_gemm_q: dtype");
+  cudaStream_t s = as_stream(stream);
+  int st = prepare_gemm_weights(w, s);
+  if (st) return st;
+  CUtensorMap tmap_a;
+  if ((st = encode_rows_u8(&tmap_a, a_packed, m, w->cols / 2, kBM))) return st;
+  {
+    static std::mutex mu;
+    static std::vector<int> attr_devs;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (std::find(attr_devs.begin(), attr_devs.end(), dev) == attr_devs.end()) {
+      FPB_CUDA_TRY(
+          cudaFuncSetAttribute(nvfp4_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem));
+      attr_devs.push_back(dev);
+    }
+  }
+  int *err = nullptr;
+  FPB_CUDA_TRY(cudaGetSymbolAddress(reinterpret_cast<void **>(&err), g_device_error));
+  GemmParams p{};
+  p.a_sf = a_sf_tiled;
+  p.b_sf = w->extras->sf_tiled;
+  p.a_global = a_global;
+  p.b_globals = w->row_globals;
+  p.y = y;
+  p.N = (int)(row_end - row_begin);
+  p.ldy = p.N;
+  p.y_bf16 = y_dtype == FPB_BF16;
+  p.M = (int)m;
+  p.n_base = (int)row_begin;
+  p.kb_count = (int)((w->cols + 255) / 256);
+  p.error = err;
+  dim3 grid((unsigned)((p.N + kBN - 1) / kBN), (unsigned)((m + kBM - 1) / kBM));
+  nvfp4_gemm_kernel<<<grid, 192, kGemmSmem, s>>>(tmap_a, *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b),
+                                                 p);
+  FPB_LAUNCH_CHECK("nvfp4_gemm_kernel");
+  return FPB_OK;
+}
+
+extern "C" int fpb_nvfp4_gemm(fpb_nvfp4_matrix *w, size_t row_begin, size_t row_end, const void *x, int x_dtype,
+                              size_t m, void *y, int y_dtype, void *workspace, size_t workspace_bytes,
+                              void *stream) {
+  if (!w || !x || !y || !workspace) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_gemm: null pointer");
+  if (workspace_bytes < fpb_nvfp4_gemm_workspace_bytes(m, w->cols))
+    return fail(FPB_ERR_WORKSPACE, "fpb_nvfp4_gemm: workspace %zu < %zu bytes", workspace_bytes,
+                fpb_nvfp4_gemm_workspace_bytes(m, w->cols));
+  if (reinterpret_cast<uintptr_t>(workspace) & 255)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_gemm: workspace must be 256-byte aligned");
+  uint8_t *ws = static_cast<uint8_t *>(workspace);
+  uint8_t *packed = ws;
+  uint8_t *sf = packed + align256(m * w->cols / 2);
+  float *scalars = reinterpret_cast<float *>(sf + align256(sf_tiled_bytes(m, w->cols)));
+  int st = fpb_nvfp4_quantize_act(x, x_dtype, m, w->cols, packed, sf, scalars, scalars + 1, stream);
+  if (st) return st;
+  return fpb_nvfp4_gemm_q(w, row_begin, row_end, packed, sf, scalars, m, y, y_dtype, stream);
+}
+
+extern "C" int fpb_device_error(int *out, int reset) {
+  if (!out) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_device_error: null pointer");
+  FPB_CUDA_TRY(cudaDeviceSynchronize());
+  FPB_CUDA_TRY(cudaMemcpyFromSymbol(out, g_device_error, sizeof(int)));
+  if (reset) {
+    int zero = 0;
+    FPB_CUDA_TRY(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)));
+  }
+  return FPB_OK;
+}

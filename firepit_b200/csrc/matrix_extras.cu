@@ -8,6 +8,7 @@ namespace fpb {
 void release_matrix_extras(fpb_nvfp4_matrix *m) {
   if (!m || !m->extras) return;
   cudaFree(m->extras->sf_tiled);
+  cudaFree(m->extras->packed_folded);
   delete m->extras;
   m->extras = nullptr;
 }

@@ -7,8 +7,15 @@
 
 namespace fpb {
 struct MatrixExtras {
-  // e4m3 block scales rearranged into the tcgen05 scale-factor tile layout.
+  // e4m3 block scales rearranged into the tcgen05 scale-factor tile layout
+  // (sign cleared: the tensor cores read them as UE4M3).
   uint8_t *sf_tiled = nullptr;
   size_t sf_tiled_bytes = 0;
+  // Codes with the sign of negative block scales folded in; null when no
+  // scale is negative (the GEMM then reads the handle's own codes).
+  uint8_t *packed_folded = nullptr;
+  // TMA descriptor of the codes as read by the GEMM (opaque 128 bytes).
+  alignas(64) unsigned char tmap_b[128];
+  bool tmap_valid = false;
 };
 }  // namespace fpb

@@ -1,0 +1,106 @@
+"""Prefill GEMM entry points (crates/firepit-kernels/src/gemm/nvfp4.rs).
+
+``nvfp4_gemm(weight, x, y, tile).submit(sink)`` and
+``nvfp4_gemm_view(weight, rows, x, y, tile).submit(sink)`` keep the
+reference's builder shape and its shape asserts (gemm/nvfp4.rs:119-206).  On
+B200 the activations are quantized to NVFP4 on the fly and both operands go
+through the block-scaled tensor cores (tcgen05.mma kind::mxf4nvf4); the tile
+argument is validated, the kernel tiles 128 x 128.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+from . import _native as N
+from .gemv import ShapeError, _dtype_code
+from .sink import Eager, Sink
+from .weights import Q8_BLOCK, Nvfp4Matrix
+
+
+@dataclass(frozen=True)
+class GemmTile:
+    """gemm/mod.rs:208-213."""
+
+    m: int
+    n: int
+    k: int
+
+
+DEFAULT_GEMM_TILE = GemmTile(64, 128, 32)          # gemm/mod.rs:215-219
+DEFAULT_GROUPED_GEMM_TILE = GemmTile(32, 128, 32)  # gemm/mod.rs:221-225
+
+
+def workspace_bytes(m: int, k: int) -> int:
+    return int(N.lib.fpb_nvfp4_gemm_workspace_bytes(m, k))
+
+
+def _check_tile(weight: Nvfp4Matrix, tile: GemmTile, rows: range, m: int) -> None:
+    """gemm/nvfp4.rs:119-122 and gemm/mod.rs:588-605."""
+    if not (tile.m > 0 and tile.n > 0 and tile.k % Q8_BLOCK == 0):
+        raise ShapeError(f"invalid GEMM tile {tile}")
+    if not (m > 0 and m % tile.m == 0):
+        raise ShapeError(f"m = {m} is not a positive multiple of tile.m = {tile.m}")
+    if not (rows.start < rows.stop <= weight.rows and len(rows) % tile.n == 0 and weight.cols % tile.k == 0):
+        raise ShapeError(f"rows {rows} / cols {weight.cols} do not fit tile {tile}")
+
+
+class Nvfp4Gemm:
+    def __init__(self, weight: Nvfp4Matrix, x, y, tile: GemmTile, rows: range | None = None, workspace=None):
+        self.weight, self.x, self.y, self.tile = weight, x, y, tile
+        self.rows = rows if rows is not None else range(0, weight.rows)
+        m = x.shape[0]
+        _check_tile(weight, tile, self.rows, m)
+        if tuple(x.shape) != (m, weight.cols):
+            raise ShapeError(f"x shape {tuple(x.shape)} != ({m}, {weight.cols})")
+        if tuple(y.shape) != (m, len(self.rows)) or not (x.is_contiguous() and y.is_contiguous()):
+            raise ShapeError(f"y shape {tuple(y.shape)} != ({m}, {len(self.rows)}) or not contiguous")
+        self.workspace = workspace
+
+    def submit(self, sink: Sink | None = None) -> None:
+        import torch
+        sink = sink or Eager()
+        m = self.x.shape[0]
+        need = workspace_bytes(m, self.weight.cols)
+        ws = self.workspace
+        if ws is None or ws.numel() * ws.element_size() < need:
+            ws = torch.empty(need, dtype=torch.uint8, device=self.x.device)
+            self.workspace = ws
+
+        def launch(stream):
+            N.call("fpb_nvfp4_gemm", self.weight.handle, self.rows.start, self.rows.stop, self.x.data_ptr(),
+                   _dtype_code(self.x), m, self.y.data_ptr(), _dtype_code(self.y), ws.data_ptr(), need, stream)
+
+        sink.run("nvfp4_gemm", launch)
+
+
+def nvfp4_gemm(weight: Nvfp4Matrix, x, y, tile: GemmTile = DEFAULT_GEMM_TILE, workspace=None) -> Nvfp4Gemm:
+    """gemm/nvfp4.rs:131-143."""
+    return Nvfp4Gemm(weight, x, y, tile, None, workspace)
+
+
+def nvfp4_gemm_view(weight: Nvfp4Matrix, rows: range, x, y, tile: GemmTile = DEFAULT_GEMM_TILE,
+                    workspace=None) -> Nvfp4Gemm:
+    """gemm/nvfp4.rs:166-182."""
+    return Nvfp4Gemm(weight, x, y, tile, rows, workspace)
+
+
+def quantize_act(x, stream=None):
+    """NVFP4-quantizes activations [m, k]: (packed u8 [m, k/2], tiled factors,
+    global f32 [1]) as device tensors."""
+    import torch
+    from .weights import current_stream_handle
+    m, k = x.shape
+    packed = torch.empty(m, k // 2, dtype=torch.uint8, device=x.device)
+    sf = torch.empty(int(N.lib.fpb_nvfp4_act_sf_bytes(m, k)), dtype=torch.uint8, device=x.device)
+    scal = torch.empty(2, dtype=torch.float32, device=x.device)
+    s = current_stream_handle(x.device) if stream is None else stream
+    N.call("fpb_nvfp4_quantize_act", x.data_ptr(), _dtype_code(x), m, k, packed.data_ptr(), sf.data_ptr(),
+           scal.data_ptr(), scal[1:].data_ptr(), s)
+    return packed, sf, scal[:1]
+
+
+def device_error(reset: bool = True) -> int:
+    import ctypes as C
+    v = C.c_int(0)
+    N.call("fpb_device_error", C.byref(v), 1 if reset else 0)
+    return v.value

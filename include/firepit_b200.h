@@ -144,6 +144,40 @@ int fpb_nvfp4_expert_gemv(const fpb_nvfp4_matrix *w, const void *x, int x_dtype,
                           size_t rows_per_expert, int input_stride, void *y,
                           int y_dtype, void *stream);
 
+/* ---- prefill NVFP4 GEMM (tcgen05, NVFP4 x NVFP4 -> f32 accumulate) --------
+ * Replaces nvfp4_gemm / nvfp4_gemm_view (gemm/nvfp4.rs:119-207, kernel
+ * :12-55).  The reference keeps activations in f32 (bf16 hi/lo MMAs); this
+ * path quantizes them to NVFP4 (per-tensor global ga = amax/(6*448), E4M3
+ * factor per 16 columns) and multiplies on the block-scaled tensor cores:
+ *   y[m, n] = ga * g[n] * sum_k a(m,k) * w(n,k)
+ * for weight rows n in [row_begin, row_end); row_begin must be a multiple
+ * of 128.  y: [m, row_end - row_begin] row-major. */
+
+/* Bytes of the tensor-core tiled scale factors of an [m, k] operand. */
+size_t fpb_nvfp4_act_sf_bytes(size_t m, size_t k);
+/* Workspace of fpb_nvfp4_gemm (quantized activations + factors + scalars). */
+size_t fpb_nvfp4_gemm_workspace_bytes(size_t m, size_t k);
+/* Quantizes activations x [m, k] (f32 or bf16) to NVFP4: packed [m, k/2],
+ * tiled factors (fpb_nvfp4_act_sf_bytes), global (1 float, device), with
+ * amax_scratch one float of device scratch.  Two launches plus two memsets. */
+int fpb_nvfp4_quantize_act(const void *x, int x_dtype, size_t m, size_t k, uint8_t *packed,
+                           uint8_t *sf_tiled, float *global_out, float *amax_scratch, void *stream);
+/* Builds the matrix's GEMM-side copies once (tiled factors, TMA map);
+ * allocates and synchronises `stream`.  Called by the first GEMM if needed. */
+int fpb_nvfp4_matrix_prepare_gemm(fpb_nvfp4_matrix *w, void *stream);
+/* GEMM on already quantized activations. */
+int fpb_nvfp4_gemm_q(fpb_nvfp4_matrix *w, size_t row_begin, size_t row_end, const uint8_t *a_packed,
+                     const uint8_t *a_sf_tiled, const float *a_global, size_t m, void *y, int y_dtype,
+                     void *stream);
+/* Quantize x into `workspace` (256-byte aligned, fpb_nvfp4_gemm_workspace_bytes)
+ * and run the GEMM. */
+int fpb_nvfp4_gemm(fpb_nvfp4_matrix *w, size_t row_begin, size_t row_end, const void *x, int x_dtype,
+                   size_t m, void *y, int y_dtype, void *workspace, size_t workspace_bytes,
+                   void *stream);
+/* First error code a tensor-core kernel recorded (0: none; bounded waits
+ * that gave up); synchronises the device; reset != 0 clears it. */
+int fpb_device_error(int *out, int reset);
+
 /* ---- MoE host bookkeeping (no GPU needed) -------------------------------- */
 /* MoeDims::new (moe.rs:172-225): FPB_ERR_SHAPE on invalid dimensions. */
 int fpb_moe_dims_validate(size_t hidden, size_t intermediate, size_t shared_intermediate,

@@ -76,6 +76,7 @@ SIGNATURES: dict[str, tuple] = {
     "fpb_nvfp4_matrix_device_ptrs": (i32, [vp, C.POINTER(vp), C.POINTER(vp), C.POINTER(vp)]),
     "fpb_nvfp4_matrix_download": (i32, [vp, vp, vp, vp, vp]),
     "fpb_nvfp4_quantize": (i32, [vp, i32, sz, sz, sz, vp, vp, vp, vp, vp]),
+    "fpb_nvfp4_quantize_noalloc": (i32, [vp, i32, sz, sz, sz, vp, vp, vp, vp]),
     "fpb_nvfp4_dequantize": (i32, [vp, vp, vp]),
     "fpb_nvfp4_gemv": (i32, [vp, sz, sz, vp, i32, vp, i32, i32, vp]),
     "fpb_nvfp4_expert_gemv": (i32, [vp, vp, i32, vp, i32, sz, i32, vp, i32, vp]),

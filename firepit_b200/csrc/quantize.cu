@@ -164,3 +164,70 @@ extern "C" int fpb_nvfp4_dequantize(const fpb_nvfp4_matrix *m, float *out, void 
   FPB_LAUNCH_CHECK("nvfp4_dequant_kernel");
   return FPB_OK;
 }
+
+// ---- quantize without allocating ------------------------------------------------------
+// fpb_nvfp4_quantize needs a caller-provided scratch buffer for its per-block
+// amax.  Some callers cannot allocate one: an engine that carves all device
+// memory out of a single arena reserved at start-up and forbids any further
+// cudaMalloc, or a serving loop where an allocation would synchronise the
+// device mid-step.  For them the same quantizer runs on a fixed scratch array
+// compiled into this library: kNoAllocMaxBlocks words, 64 KiB, which every
+// GPU that loads the library keeps until the process exits.
+#include <mutex>
+#include <vector>
+
+namespace fpb {
+
+constexpr size_t kNoAllocMaxBlocks = 16384;  // row blocks (one global each) per call
+static __device__ __align__(256) uint32_t g_noalloc_amax[kNoAllocMaxBlocks];
+
+// The array's device address on the current device.  In host code the
+// array's name only stands in for it, so the address is looked up once per
+// device (with that device current) and cached.
+static int noalloc_scratch(float **out) {
+  static std::mutex mu;
+  static std::vector<float *> by_device;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  std::lock_guard<std::mutex> lock(mu);
+  if ((int)by_device.size() <= dev) by_device.resize(dev + 1, nullptr);
+  if (!by_device[dev]) {
+    void *p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_amax);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc quantize scratch)");
+    by_device[dev] = static_cast<float *>(p);
+  }
+  *out = by_device[dev];
+  return FPB_OK;
+}
+
+}  // namespace fpb
+
+extern "C" int fpb_nvfp4_quantize_noalloc(const void *w, int w_dtype, size_t rows, size_t cols,
+                                          size_t rows_per_global, uint8_t *packed, uint8_t *scales,
+                                          float *row_globals, void *stream) {
+  if (!w || !packed || !scales || !row_globals)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_quantize_noalloc: null pointer");
+  if (rows == 0 || cols == 0 || cols % kQ8Block != 0)
+    return fail(FPB_ERR_SHAPE, "fpb_nvfp4_quantize_noalloc: cols must be a positive multiple of %d", kQ8Block);
+  if (rows_per_global == 0 || rows % rows_per_global != 0)
+    return fail(FPB_ERR_SHAPE, "fpb_nvfp4_quantize_noalloc: rows_per_global must divide rows");
+  if (rows / rows_per_global > kNoAllocMaxBlocks)
+    return fail(FPB_ERR_UNSUPPORTED,
+                "fpb_nvfp4_quantize_noalloc: %zu row blocks exceed the built-in scratch of %zu; "
+                "use fpb_nvfp4_quantize with a scratch buffer",
+                rows / rows_per_global, kNoAllocMaxBlocks);
+  if (w_dtype != FPB_F32 && w_dtype != FPB_BF16)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_quantize_noalloc: dtype %d", w_dtype);
+  float *scratch = nullptr;
+  int st = noalloc_scratch(&scratch);
+  if (st) return st;
+  // quantize_impl zeroes the amax words it uses before its first launch.
+  cudaStream_t s = as_stream(stream);
+  if (w_dtype == FPB_F32)
+    return quantize_impl(static_cast<const float *>(w), rows, cols, rows_per_global, packed, scales,
+                         row_globals, scratch, s);
+  return quantize_impl(static_cast<const uint16_t *>(w), rows, cols, rows_per_global, packed, scales,
+                       row_globals, scratch, s);
+}

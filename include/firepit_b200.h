@@ -117,6 +117,19 @@ int fpb_nvfp4_matrix_download(const fpb_nvfp4_matrix *m, uint8_t *packed, uint8_
 int fpb_nvfp4_quantize(const void *w, int w_dtype, size_t rows, size_t cols,
                        size_t rows_per_global, uint8_t *packed, uint8_t *scales,
                        float *row_globals, float *amax_scratch, void *stream);
+/* fpb_nvfp4_quantize without the caller's scratch buffer.  No counterpart in
+ * the reference: it is for callers that cannot allocate device memory (an
+ * engine whose device memory is one arena reserved up front, a serving loop
+ * that must not call cudaMalloc).  The per-block amax scratch is a fixed
+ * array inside the library (64 KiB on every GPU that loads it, kept until
+ * exit), so rows / rows_per_global may be at most 16384; larger requests
+ * return FPB_ERR_UNSUPPORTED.  Allocates nothing.  The first call on a
+ * device looks up the array's device address, so make it before any stream
+ * capture.  All calls share the array: calls that overlap on the GPU (other
+ * streams, other threads) race and must be serialised by the caller. */
+int fpb_nvfp4_quantize_noalloc(const void *w, int w_dtype, size_t rows, size_t cols,
+                               size_t rows_per_global, uint8_t *packed, uint8_t *scales,
+                               float *row_globals, void *stream);
 /* Dequantize to f32 [rows, cols] with the ModelOpt order
  * E2M1[c] * (e4m3(s) * g) (firepit src/checkpoint.rs:401-420). */
 int fpb_nvfp4_dequantize(const fpb_nvfp4_matrix *m, float *out, void *stream);

@@ -46,7 +46,8 @@ def parse_args():
     p.add_argument("--steps", type=int, default=2000)
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--config", choices=["gemv"], default="gemv")
+    p.add_argument("--config", choices=["gemv", "nvfp4_gemm_m128", "nvfp4_gemm_m2048"], default="gemv",
+                   help="gemv: config 0 (default); nvfp4_gemm_m*: config 2 GEMM at M=128 / M=2048")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the cpu_baseline sample")
     return p.parse_args()
 
@@ -340,9 +341,220 @@ def ours_arm(args):
         dist.destroy_process_group()
 
 
+# ---- config 2: NVFP4 GEMM (tcgen05) ------------------------------------------------------
+GEMM_N, GEMM_K, GEMM_MATS = 8192, 2048, 16
+
+
+def gemm_shape(args):
+    return 128 if args.config.endswith("m128") else 2048
+
+
+def gemm_bytes(m, n, k):
+    """Algorithmic bytes of one GEMM launch on quantized activations: weight codes,
+    factors and row globals, activation codes and factors, bf16 output."""
+    return n * k // 2 + n * k // 16 + 4 * n + m * k // 2 + m * k // 16 + 2 * m * n
+
+
+def gemm_reference_arm(args):
+    """The host path restated: dequantize both NVFP4 operands and multiply in
+    f32 (numpy/BLAS on all host cores), on a sample of activation rows."""
+    rank, _, _ = dist_env()
+    if rank != 0:
+        return
+    import numpy as np
+
+    from oracle import oracle as O
+    m = gemm_shape(args)
+    w = O.synth_normal(GEMM_N * GEMM_K, seed=0, stream=1, std=0.02).reshape(GEMM_N, GEMM_K)
+    pw, sw, gw = O.nvfp4_quantize(w)
+    wd = O.nvfp4_dequantize(pw, sw, gw, GEMM_N, GEMM_K)
+    x = O.bf16_to_f32(O.bf16_bits(O.synth_normal(m * GEMM_K, seed=0, stream=0))).reshape(m, GEMM_K)
+    pa, sa, ga = O.nvfp4_quantize(x)
+    xd = O.nvfp4_dequantize(pa, sa, ga, m, GEMM_K)
+    rows = min(m, 32)
+    t0 = time.perf_counter()
+    _ = xd[:rows] @ wd.T
+    one = max(time.perf_counter() - t0, 1e-4)
+    budget = 60.0 / max(args.steps + args.warmup, 1)
+    rows = max(1, min(m, int(rows * budget / one)))
+    for _ in range(args.warmup):
+        _ = xd[:rows] @ wd.T
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        _ = xd[:rows] @ wd.T
+    dt = (time.perf_counter() - t0) / max(args.steps, 1)
+    tflops = 2.0 * rows * GEMM_N * GEMM_K / dt / 1e12
+    sample = f"{rows} of {m} activation rows x W[{GEMM_N},{GEMM_K}] per step, dequantized NVFP4, f32 BLAS"
+    emit({"impl": "reference", "metric": "NVFP4 GEMM TFLOPS", "value": tflops, "unit": "TFLOP/s",
+          "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
+          "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+          "data": "synthetic (seeded Philox)", "config": {"workload": f"config2 NVFP4 GEMM M={m} K=2048 N=8192"},
+          "cpu_baseline": {"value": tflops, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
+                           "sample": sample},
+          "e2e": {"value": tflops, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
+
+
+def gemm_arm(args):
+    """Config 2 GEMM: x bf16 [M, 2048] quantized on the device to NVFP4, times
+    16 distinct NVFP4 weights [8192, 2048] (N-split over the ranks) per step;
+    inputs of a step (151 MB of weights per GPU at g = 1) exceed L2."""
+    import torch
+    import torch.distributed as dist
+
+    import firepit_b200 as F
+    N_ = F._native
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    g = world
+    m = gemm_shape(args)
+    n_rank = GEMM_N // g
+    r0 = rank * n_rank
+    mats = []
+    for c in range(GEMM_MATS):
+        w = F.synth_normal((GEMM_N, GEMM_K), seed=0, stream_id=1 + c, std=0.02, device=dev)
+        packed, scales, globals_ = F.quantize_nvfp4(w)
+        del w
+        mat = F.Nvfp4Matrix.from_device(packed[r0:r0 + n_rank].contiguous(), scales[r0:r0 + n_rank].contiguous(),
+                                        globals_[r0:r0 + n_rank].contiguous(), n_rank, GEMM_K)
+        N_.call("fpb_nvfp4_matrix_prepare_gemm", mat.handle, torch.cuda.current_stream().cuda_stream)
+        mats.append(mat)
+    x = F.synth_normal((m, GEMM_K), seed=0, stream_id=0, dtype=torch.bfloat16, device=dev)
+    ws_bytes = int(N_.lib.fpb_nvfp4_gemm_workspace_bytes(m, GEMM_K))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    sf_bytes = int(N_.lib.fpb_nvfp4_act_sf_bytes(m, GEMM_K))
+    qa = torch.empty(m * GEMM_K // 2, dtype=torch.uint8, device=dev)
+    qsf = torch.empty(sf_bytes, dtype=torch.uint8, device=dev)
+    scal = torch.zeros(2, dtype=torch.float32, device=dev)
+    ys = torch.empty(GEMM_MATS, m, n_rank, dtype=torch.bfloat16, device=dev)
+    y_all = torch.empty(g, GEMM_MATS, m, n_rank, dtype=torch.bfloat16, device=dev)
+
+    def quant(sh):
+        N_.call("fpb_nvfp4_quantize_act", x.data_ptr(), N_.FPB_BF16, m, GEMM_K, qa.data_ptr(), qsf.data_ptr(),
+                scal.data_ptr(), scal[1:].data_ptr(), sh)
+
+    def gemms(sh):
+        for c in range(GEMM_MATS):
+            N_.call("fpb_nvfp4_gemm_q", mats[c].handle, 0, 0, qa.data_ptr(), qsf.data_ptr(), scal.data_ptr(), m,
+                    ys[c].data_ptr(), N_.FPB_BF16, sh)
+
+    s = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(s):
+        quant(s.cuda_stream)
+        gemms(s.cuda_stream)
+    torch.cuda.synchronize()
+    before = F.launch_count()
+    gq, gg = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gq, stream=s):
+        quant(torch.cuda.current_stream().cuda_stream)
+    with torch.cuda.graph(gg, stream=s):
+        gemms(torch.cuda.current_stream().cuda_stream)
+    launches_per_step = F.launch_count() - before
+
+    def step(ev=None):
+        if ev:
+            ev[0].record()
+        gq.replay()
+        if ev:
+            ev[1].record()
+        gg.replay()
+        if ev:
+            ev[2].record()
+        if g > 1:
+            dist.all_gather_into_tensor(y_all, ys)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    if g > 1:
+        dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record()
+        for i in range(args.steps):
+            step(evs[i])
+        end.record()
+        torch.cuda.synchronize()
+    t = torch.tensor([start.elapsed_time(end), sum(e[0].elapsed_time(e[1]) for e in evs),
+                      sum(e[1].elapsed_time(e[2]) for e in evs)], device=dev, dtype=torch.float64)
+    if g > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms, quant_ms, gemm_ms = t.tolist()
+    ms_per_step = total_ms / args.steps
+    flops_step = 2.0 * m * GEMM_N * GEMM_K * GEMM_MATS
+    value = flops_step / (ms_per_step * 1e-3) / 1e12
+
+    # end to end through the public API: x from pinned host memory, y back
+    xh = x.cpu().pin_memory()
+    yh = torch.empty(GEMM_MATS, m, n_rank, dtype=torch.bfloat16, pin_memory=True)
+    xd = torch.empty_like(x)
+    sink = F.Async()
+
+    def e2e_step():
+        xd.copy_(xh, non_blocking=True)
+        for c in range(GEMM_MATS):
+            F.nvfp4_gemm(mats[c], xd, ys[c], F.GemmTile(8, 128, 32), workspace=ws).submit(sink)
+        yh.copy_(ys, non_blocking=True)
+
+    e2e_steps = max(1, min(args.steps, 20))
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    te = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+    if g > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = flops_step / (te.item() / e2e_steps * 1e-3) / 1e12
+
+    per_launch_ms = gemm_ms / (args.steps * GEMM_MATS)
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    if m >= 1024:
+        bf16 = float(peaks.get("bf16_tflops", 1590.0))
+        achieved = 2.0 * m * n_rank * GEMM_K / (per_launch_ms * 1e-3) / 1e12
+        roof = {"bound": "tensor", "achieved": achieved, "peak": 4 * bf16, "unit": "TFLOP/s",
+                "frac": achieved / (4 * bf16), "traffic": None,
+                "peak_kind": "4 x measured bf16 burst (nominal dense FP4:BF16 ratio; no FP4 measurement)"}
+    else:
+        hbm = float(peaks.get("hbm_gbs", 6650.0))
+        achieved = gemm_bytes(m, n_rank, GEMM_K) / (per_launch_ms * 1e-3) / 1e9
+        roof = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                "traffic": None, "peak_kind": "measured hbm_gbs"}
+    roof["per_launch_us"] = per_launch_ms * 1e3
+    if rank == 0:
+        emit({"metric": "NVFP4 GEMM TFLOPS", "value": value, "unit": "TFLOP/s", "n_gpus": g, "steps": args.steps,
+              "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+              "vs_baseline": None, "dtype": "nvfp4 x nvfp4 (e2m1, ue4m3/16), f32 accumulate, bf16 out",
+              "data": "synthetic (seeded Philox: W N(0,0.02), x N(0,1) seed 0)",
+              "config": {"workload": f"config2 NVFP4 GEMM M={m} K=2048 N=8192, x bf16 quantized on device",
+                         "matrices_per_step": GEMM_MATS, "n_per_rank": n_rank,
+                         "l2": "inputs larger than L2 (16 distinct weights per step)",
+                         "parallelism": f"N-split x{g} + NCCL all-gather" if g > 1 else "single GPU"},
+              "roofline": roof,
+              "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": m * GEMM_K * 2,
+                      "d2h_bytes_per_step": GEMM_MATS * m * n_rank * 2},
+              "gpu_launches": launches_per_step * args.steps, "clocks": clocks.summary(),
+              "breakdown_ms": {"quantize_act": quant_ms / args.steps, "gemms": gemm_ms / args.steps}})
+    del gq, gg
+    if g > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
-    if args.impl == "reference":
+    if args.config.startswith("nvfp4_gemm"):
+        (gemm_reference_arm if args.impl == "reference" else gemm_arm)(args)
+    elif args.impl == "reference":
         reference_arm(args)
     else:
         ours_arm(args)

@@ -15,6 +15,8 @@ from .synth import synth_normal
 from .weights import (NVFP4_GROUP, Q8_BLOCK, FormatError, HostNvfp4Matrix, Nvfp4Matrix, current_stream_handle,
                       quantize_nvfp4)
 
+from .gemm import (DEFAULT_GEMM_TILE, DEFAULT_GROUPED_GEMM_TILE, GemmTile, Nvfp4Gemm, Nvfp4GroupedGemmView,
+                   device_error, nvfp4_gemm, nvfp4_gemm_view, nvfp4_grouped_gemm_q, nvfp4_grouped_gemm_view,
+                   quantize_act)
+
 __version__ = _native.lib.fpb_version().decode()
-from .gemm import (DEFAULT_GEMM_TILE, DEFAULT_GROUPED_GEMM_TILE, GemmTile, Nvfp4Gemm, device_error, nvfp4_gemm,
-                   nvfp4_gemm_view, quantize_act)

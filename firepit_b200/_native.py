@@ -1,7 +1,7 @@
 """ctypes binding of the firepit_b200 C ABI (include/firepit_b200.h).
 
 The library is the in-tree ``firepit_b200/libfirepit_b200.so`` built by
-``python -m firepit_b200.build``.  There is no fallback: if the library is
+``python firepit_b200/build.py``.  There is no fallback: if the library is
 missing or fails to load, importing this module raises.
 """
 from __future__ import annotations
@@ -44,7 +44,7 @@ def _status_name(status: int) -> str:
 def _load() -> C.CDLL:
     if not LIB_PATH.exists():
         raise ImportError(
-            f"{LIB_PATH} is missing: build it with `python -m firepit_b200.build` "
+            f"{LIB_PATH} is missing: build it with `python firepit_b200/build.py` "
             "(the CUDA path has no fallback)")
     return C.CDLL(str(LIB_PATH), mode=os.RTLD_NOW | os.RTLD_LOCAL)
 
@@ -86,6 +86,7 @@ SIGNATURES: dict[str, tuple] = {
     "fpb_nvfp4_matrix_prepare_gemm": (i32, [vp, vp]),
     "fpb_nvfp4_gemm_q": (i32, [vp, sz, sz, vp, vp, vp, sz, vp, i32, vp]),
     "fpb_nvfp4_gemm": (i32, [vp, sz, sz, vp, i32, sz, vp, i32, vp, sz, vp]),
+    "fpb_nvfp4_grouped_gemm_q": (i32, [vp, vp, vp, vp, sz, vp, sz, vp, i32, vp]),
     "fpb_device_error": (i32, [C.POINTER(i32), i32]),
     "fpb_moe_dims_validate": (i32, [sz, sz, sz, sz, sz]),
     "fpb_expert_selection_validate": (i32, [vp, vp, sz, sz, sz]),

@@ -161,6 +161,11 @@ struct GemmParams {
   int n_base;    // first weight row of the view (multiple of 128)
   int kb_count;  // ceil(K / 256)
   int *error;    // device error word
+  // Grouped (MoE) mode, crates/firepit-kernels/src/gemm/nvfp4.rs:57-105: row
+  // tile m of A belongs to expert tile_experts[m], whose weights are rows
+  // [e * rows_per_expert, (e + 1) * rows_per_expert); N = rows_per_expert.
+  const int32_t *tile_experts;  // null for a dense GEMM
+  int n_experts;
 };
 
 constexpr int kTileBytes = kBM * kBKBytes;   // 16 KB per operand per stage
@@ -192,6 +197,15 @@ __global__ void __launch_bounds__(192, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_tile = blockIdx.x, m_tile = blockIdx.y;
   const int m0 = m_tile * kBM, n0 = n_tile * kBN;
+  int n_base = p.n_base;
+  if (p.tile_experts) {
+    const int e = p.tile_experts[m_tile];
+    if (e < 0 || e >= p.n_experts) {  // a malformed layout: leave this tile, report it
+      if (threadIdx.x == 0) atomicCAS(p.error, 0, 106);
+      return;
+    }
+    n_base = e * p.N;
+  }
   const int kb64_per_rb = p.kb_count * 4;
 
   if (threadIdx.x == 0) {
@@ -220,7 +234,7 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 0) {
     // ---- TMA producer ----------------------------------------------------------
     if (elect_one()) {
-      const int nb_global = p.n_base / 128 + n_tile;
+      const int nb_global = n_base / 128 + n_tile;
       int issued = 0;
       for (int kb = 0; kb < p.kb_count; ++kb) {
         const int s = kb % kStages, round = kb / kStages;
@@ -230,7 +244,7 @@ __global__ void __launch_bounds__(192, 1)
         }
         mbar_arrive_expect_tx(&full[s], 2 * kTileBytes + 2 * kSfStageBytes);
         tma_load_2d(sA + s * kTileBytes, &tmap_a, kb * kBKBytes, m0, &full[s]);
-        tma_load_2d(sB + s * kTileBytes, &tmap_b, kb * kBKBytes, p.n_base + n0, &full[s]);
+        tma_load_2d(sB + s * kTileBytes, &tmap_b, kb * kBKBytes, n_base + n0, &full[s]);
         bulk_load(sSFA + s * kSfStageBytes, p.a_sf + ((size_t)m_tile * kb64_per_rb + kb * 4) * kSfChunk,
                   kSfStageBytes, &full[s]);
         bulk_load(sSFB + s * kSfStageBytes, p.b_sf + ((size_t)nb_global * kb64_per_rb + kb * 4) * kSfChunk,
@@ -287,7 +301,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const int n = nc + j;
-            const float g = n < p.N ? __ldg(p.b_globals + p.n_base + n) : 0.0f;
+            const float g = n < p.N ? __ldg(p.b_globals + n_base + n) : 0.0f;
             v[j] = (__uint_as_float(r[j]) * ga) * g;
           }
           const long long off = (long long)row * p.ldy + nc;
@@ -541,6 +555,60 @@ extern "C" int fpb_nvfp4_gemm(fpb_nvfp4_matrix *w, size_t row_begin, size_t row_
   int st = fpb_nvfp4_quantize_act(x, x_dtype, m, w->cols, packed, sf, scalars, scalars + 1, stream);
   if (st) return st;
   return fpb_nvfp4_gemm_q(w, row_begin, row_end, packed, sf, scalars, m, y, y_dtype, stream);
+}
+
+extern "C" int fpb_nvfp4_grouped_gemm_q(fpb_nvfp4_matrix *w, const uint8_t *a_packed, const uint8_t *a_sf_tiled,
+                                        const float *a_global, size_t padded_rows, const int32_t *tile_experts,
+                                        size_t rows_per_expert, void *y, int y_dtype, void *stream) {
+  if (!w || !a_packed || !a_sf_tiled || !a_global || !tile_experts || !y)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_grouped_gemm_q: null pointer");
+  if (padded_rows == 0 || padded_rows % kBM || padded_rows / kBM > 65535)
+    return fail(FPB_ERR_SHAPE, "fpb_nvfp4_grouped_gemm_q: padded_rows %zu must be a positive multiple of %d",
+                padded_rows, kBM);
+  if (rows_per_expert == 0 || rows_per_expert % kBN || w->rows % rows_per_expert)
+    return fail(FPB_ERR_SHAPE, "fpb_nvfp4_grouped_gemm_q: rows_per_expert %zu must be a multiple of %d dividing %zu",
+                rows_per_expert, kBN, w->rows);
+  if (y_dtype != FPB_F32 && y_dtype != FPB_BF16)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_grouped_gemm_q: dtype");
+  cudaStream_t s = as_stream(stream);
+  int st = prepare_gemm_weights(w, s);
+  if (st) return st;
+  CUtensorMap tmap_a;
+  if ((st = encode_rows_u8(&tmap_a, a_packed, padded_rows, w->cols / 2, kBM))) return st;
+  {
+    static std::mutex mu;
+    static std::vector<int> attr_devs;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (std::find(attr_devs.begin(), attr_devs.end(), dev) == attr_devs.end()) {
+      FPB_CUDA_TRY(
+          cudaFuncSetAttribute(nvfp4_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem));
+      attr_devs.push_back(dev);
+    }
+  }
+  int *err = nullptr;
+  FPB_CUDA_TRY(cudaGetSymbolAddress(reinterpret_cast<void **>(&err), g_device_error));
+  GemmParams p{};
+  p.a_sf = a_sf_tiled;
+  p.b_sf = w->extras->sf_tiled;
+  p.a_global = a_global;
+  p.b_globals = w->row_globals;
+  p.y = y;
+  p.N = (int)rows_per_expert;
+  p.ldy = p.N;
+  p.y_bf16 = y_dtype == FPB_BF16;
+  p.M = (int)padded_rows;
+  p.n_base = 0;
+  p.kb_count = (int)((w->cols + 255) / 256);
+  p.error = err;
+  p.tile_experts = tile_experts;
+  p.n_experts = (int)(w->rows / rows_per_expert);
+  dim3 grid((unsigned)(rows_per_expert / kBN), (unsigned)(padded_rows / kBM));
+  nvfp4_gemm_kernel<<<grid, 192, kGemmSmem, s>>>(tmap_a, *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b),
+                                                 p);
+  FPB_LAUNCH_CHECK("nvfp4_gemm_kernel(grouped)");
+  return FPB_OK;
 }
 
 extern "C" int fpb_device_error(int *out, int reset) {

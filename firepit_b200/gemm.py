@@ -104,3 +104,58 @@ def device_error(reset: bool = True) -> int:
     v = C.c_int(0)
     N.call("fpb_device_error", C.byref(v), 1 if reset else 0)
     return v.value
+
+
+def nvfp4_grouped_gemm_q(weight: Nvfp4Matrix, a_packed, a_sf, a_global, tile_experts, rows_per_expert: int, y,
+                         stream=None) -> None:
+    """Grouped GEMM on quantized activations (fpb_nvfp4_grouped_gemm_q).
+
+    a_packed: [padded_rows, K/2] u8; a_sf: tiled factors; a_global: f32 [1];
+    tile_experts: device int32 [padded_rows / 128]; y: [padded_rows, rows_per_expert].
+    """
+    from .weights import current_stream_handle
+    padded_rows = a_packed.shape[0]
+    if tuple(y.shape) != (padded_rows, rows_per_expert) or not y.is_contiguous():
+        raise ShapeError(f"y shape {tuple(y.shape)} != ({padded_rows}, {rows_per_expert})")
+    if tile_experts.numel() * 128 != padded_rows:
+        raise ShapeError(f"{tile_experts.numel()} tile experts for {padded_rows} rows (128-row tiles)")
+    s = current_stream_handle(y.device) if stream is None else stream
+    N.call("fpb_nvfp4_grouped_gemm_q", weight.handle, a_packed.data_ptr(), a_sf.data_ptr(), a_global.data_ptr(),
+           padded_rows, tile_experts.data_ptr(), rows_per_expert, y.data_ptr(), _dtype_code(y), s)
+
+
+class Nvfp4GroupedGemmView:
+    """gemm/nvfp4.rs:209-264: x holds the layout's padded_rows gathered rows,
+    row tile t is multiplied by expert layout.tile_experts[t]."""
+
+    def __init__(self, weight: Nvfp4Matrix, x, y, layout, experts: int, rows_per_expert: int, tile: GemmTile):
+        if tile.m != layout.tile_rows:
+            raise ShapeError(f"tile.m {tile.m} != layout tile_rows {layout.tile_rows}")
+        if layout.tile_rows != 128:
+            raise ShapeError("the tensor-core grouped GEMM needs a layout built with tile_rows = 128")
+        if weight.rows != experts * rows_per_expert:
+            raise ShapeError(f"weight rows {weight.rows} != {experts} x {rows_per_expert}")
+        if tuple(x.shape) != (layout.padded_rows(), weight.cols):
+            raise ShapeError(f"x shape {tuple(x.shape)} != ({layout.padded_rows()}, {weight.cols})")
+        if rows_per_expert % tile.n or rows_per_expert % 128 or weight.cols % tile.k:
+            raise ShapeError(f"rows_per_expert {rows_per_expert} / cols {weight.cols} do not fit tile {tile}")
+        self.weight, self.x, self.y, self.layout, self.rpe = weight, x, y, layout, rows_per_expert
+        self._tile_experts = None
+
+    def submit(self, sink: Sink | None = None) -> None:
+        import torch
+        sink = sink or Eager()
+        if self._tile_experts is None:
+            self._tile_experts = torch.from_numpy(self.layout.tile_experts).to(self.x.device)
+
+        def launch(stream):
+            packed, sf, ga = quantize_act(self.x, stream)
+            nvfp4_grouped_gemm_q(self.weight, packed, sf, ga, self._tile_experts, self.rpe, self.y, stream)
+
+        sink.run("nvfp4_grouped_gemm", launch)
+
+
+def nvfp4_grouped_gemm_view(weight: Nvfp4Matrix, x, y, layout, experts: int, rows_per_expert: int,
+                            tile: GemmTile = GemmTile(128, 128, 32)) -> Nvfp4GroupedGemmView:
+    """gemm/nvfp4.rs:218-243."""
+    return Nvfp4GroupedGemmView(weight, x, y, layout, experts, rows_per_expert, tile)

@@ -187,6 +187,19 @@ int fpb_nvfp4_gemm_q(fpb_nvfp4_matrix *w, size_t row_begin, size_t row_end, cons
 int fpb_nvfp4_gemm(fpb_nvfp4_matrix *w, size_t row_begin, size_t row_end, const void *x, int x_dtype,
                    size_t m, void *y, int y_dtype, void *workspace, size_t workspace_bytes,
                    void *stream);
+/* Grouped (MoE) GEMM on quantized activations; replaces
+ * nvfp4_grouped_gemm_view (gemm/nvfp4.rs:209-264, kernel :56-107).  A holds
+ * the prefill layout's padded_rows gathered rows (a multiple of 128: the
+ * layout is built with tile_rows = 128); row tile t (128 rows) belongs to
+ * expert tile_experts[t] (device int32 [padded_rows / 128]) and is
+ * multiplied by that expert's rows [e*rows_per_expert, (e+1)*rows_per_expert)
+ * of w:  y[t*128 + i, n] = ga * g[e*rpe + n] * sum_k a(t*128+i, k) w(e*rpe+n, k).
+ * y: [padded_rows, rows_per_expert]; rows_per_expert % 128 == 0.  An expert
+ * id outside [0, w.rows / rows_per_expert) leaves that tile unwritten and
+ * records device error 106 (fpb_device_error). */
+int fpb_nvfp4_grouped_gemm_q(fpb_nvfp4_matrix *w, const uint8_t *a_packed, const uint8_t *a_sf_tiled,
+                             const float *a_global, size_t padded_rows, const int32_t *tile_experts,
+                             size_t rows_per_expert, void *y, int y_dtype, void *stream);
 /* First error code a tensor-core kernel recorded (0: none; bounded waits
  * that gave up); synchronises the device; reset != 0 clears it. */
 int fpb_device_error(int *out, int reset);

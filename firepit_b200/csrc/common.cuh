@@ -22,6 +22,9 @@ int cuda_fail(cudaError_t err, const char *what);
 void count_launch(uint64_t n = 1);
 // Streaming multiprocessor count of the current device (cached per device).
 int sm_count();
+// Device address of the library's device-side error word on the current
+// device (first error code a kernel recorded; read by fpb_device_error).
+int *device_error_ptr();
 
 inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
 

@@ -611,6 +611,22 @@ extern "C" int fpb_nvfp4_grouped_gemm_q(fpb_nvfp4_matrix *w, const uint8_t *a_pa
   return FPB_OK;
 }
 
+// Device address of g_device_error on the current device, cached per device
+// (kernels of other translation units record their errors there).
+int *fpb::device_error_ptr() {
+  static std::mutex mu;
+  static std::vector<std::pair<int, int *>> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  for (auto &e : cache)
+    if (e.first == dev) return e.second;
+  int *p = nullptr;
+  if (cudaGetSymbolAddress(reinterpret_cast<void **>(&p), g_device_error) != cudaSuccess) return nullptr;
+  cache.push_back({dev, p});
+  return p;
+}
+
 extern "C" int fpb_device_error(int *out, int reset) {
   if (!out) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_device_error: null pointer");
   FPB_CUDA_TRY(cudaDeviceSynchronize());

@@ -42,6 +42,7 @@
 
 #include "common.cuh"
 #include "nvfp4_matrix.cuh"
+#include "sm100.cuh"
 
 namespace fpb {
 
@@ -401,6 +402,281 @@ __global__ void __launch_bounds__(512, 1) gemv_nvfp4_kernel(GemvArgs a) {
   }
 }
 
+// ---- streaming variant: weights staged in shared memory ahead of the wait ----
+//
+// Dense GEMV with K % 128 == 0, K <= 4096, batch <= 8, rows and the first row
+// a multiple of 4.  A CTA (8 warps) owns a contiguous range of `rpc` rows
+// and is sized so that two fit on an SM: one of this GEMV and one of the next
+// launch in the stream.  Before griddepcontrol.wait, warp 0 issues 1-D bulk
+// copies of the CTA's first row blocks (16 rows x K codes, their factors and
+// globals) into a ring of shared-memory stages, so the weights of launch i+1
+// stream from HBM while launch i computes.  After the wait each warp stages
+// its K slice of x (f16, prescaled as in the register variant) and runs the
+// same cvt / mul.f16x2 / m16n8k16 arithmetic on every row block, reading codes
+// from shared memory (row pitch = 64 mod 128 bytes: conflict-free).  Partial
+// sums of the 8 K slices meet in shared memory; the last warp to finish a row
+// block (a shared counter) adds them, stores y and refills the stage with the
+// row block S stages ahead.
+struct StreamArgs {
+  const uint8_t *packed;  // first addressed row
+  const uint8_t *scales;
+  const float *globals;
+  const void *x;
+  void *y;
+  int *error;
+  int rows, K, batch;
+  int rpc;          // rows per CTA (multiple of 4)
+  int stages;       // ring depth
+  int wpitch;       // shared bytes per staged code row (64 mod 128)
+  int spitch;       // shared bytes per staged factor row
+  int scale_rows;   // 1: one copy per factor row; 0: one contiguous copy per row block
+  int stage_bytes;  // 16 * wpitch + 16 * spitch + 64
+  int xpitch;       // f16 elements per staged input row
+  int y_bf16;
+};
+
+constexpr int kStreamWarps = 8;
+
+__device__ __forceinline__ uint4 lds128(const void *p) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(sm100::smem_u32(p)));
+  return v;
+}
+
+__device__ __forceinline__ uint16_t lds16(const void *p) {
+  uint16_t v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(sm100::smem_u32(p)));
+  return v;
+}
+
+// Issues (one warp) the copies of one row block of `nrows` rows (a multiple of
+// 4, at most 16) starting at row `row0` of the addressed rows into `stage`.
+__device__ __forceinline__ void stream_issue(const StreamArgs &a, uint8_t *stage, uint64_t *bar, int row0,
+                                             int nrows, int lane) {
+  const uint32_t kb2 = (uint32_t)a.K >> 1, kb16 = (uint32_t)a.K >> 4;
+  if (lane == 0) sm100::mbar_arrive_expect_tx(bar, (uint32_t)nrows * (kb2 + kb16 + 4));
+  __syncwarp();
+  if (lane < nrows)
+    sm100::bulk_load(stage + lane * a.wpitch, a.packed + (size_t)(row0 + lane) * kb2, kb2, bar);
+  uint8_t *sc = stage + 16 * a.wpitch;
+  if (a.scale_rows) {
+    if (lane >= 16 && lane - 16 < nrows)
+      sm100::bulk_load(sc + (lane - 16) * a.spitch, a.scales + (size_t)(row0 + lane - 16) * kb16, kb16, bar);
+  } else if (lane == 16) {
+    sm100::bulk_load(sc, a.scales + (size_t)row0 * kb16, (uint32_t)nrows * kb16, bar);
+  }
+  if (lane == 31) sm100::bulk_load(sc + 16 * a.spitch, a.globals + row0, (uint32_t)nrows * 4, bar);
+}
+
+template <bool XLO>
+__global__ void __launch_bounds__(256, 2) gemv_nvfp4_stream_kernel(StreamArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int S = a.stages;
+  uint8_t *stages = smem;
+  __half *xh = reinterpret_cast<__half *>(smem + (size_t)S * a.stage_bytes);
+  __half *xl = xh + (size_t)a.batch * a.xpitch;
+  float4 *red = reinterpret_cast<float4 *>(xh + (size_t)a.batch * a.xpitch * (XLO ? 2 : 1));
+  uint64_t *full = reinterpret_cast<uint64_t *>(red + (size_t)S * kStreamWarps * 32);
+  int *count = reinterpret_cast<int *>(full + S);
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, q = lane & 3;
+  if (blockDim.x != kStreamWarps * 32) return;  // the layout below assumes 8 warps
+  const int row_lo = blockIdx.x * a.rpc;
+  const int row_hi = min(a.rows, row_lo + a.rpc);
+  if (row_lo >= row_hi) return;
+  const int nrb = (row_hi - row_lo + 15) >> 4;
+
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      sm100::mbar_init(&full[s], 1);
+      count[s] = 0;
+    }
+    sm100::fence_barrier_init();
+  }
+  __syncthreads();
+  // Weights are immutable while their handle exists: copy them before the wait.
+  if (warp == 0)
+    for (int s = 0; s < S && s < nrb; ++s)
+      stream_issue(a, stages + (size_t)s * a.stage_bytes, &full[s], row_lo + 16 * s,
+                   min(16, row_hi - row_lo - 16 * s), lane);
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+
+  // ---- this warp's K slice of x, prescaled to f16 in shared memory ----------
+  const int chunks = a.K >> 7;
+  const int cpw = (chunks + kStreamWarps - 1) / kStreamWarps;
+  const int c_lo = min(chunks, warp * cpw), c_hi = min(chunks, c_lo + cpw);
+  const int k_lo = c_lo * 128, pieces = (c_hi - c_lo) * 16;  // 8-element pieces
+  float my_unscale = 1.0f;                                    // lane b: batch row b
+  for (int b = 0; b < a.batch; ++b) {
+    float v[2][8];
+    uint32_t m = 0;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int p = lane + 32 * i;
+      const long long off = (long long)b * a.K + k_lo + p * 8;
+      if (p < pieces) {
+        if (XLO) {
+          const float4 f0 = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(a.x) + off);
+          const float4 f1 = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(a.x) + off + 4);
+          v[i][0] = f0.x; v[i][1] = f0.y; v[i][2] = f0.z; v[i][3] = f0.w;
+          v[i][4] = f1.x; v[i][5] = f1.y; v[i][6] = f1.z; v[i][7] = f1.w;
+        } else {
+          const uint4 r = *reinterpret_cast<const uint4 *>(reinterpret_cast<const uint16_t *>(a.x) + off);
+          const uint32_t wv[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            v[i][2 * t] = __uint_as_float(wv[t] << 16);
+            v[i][2 * t + 1] = __uint_as_float(wv[t] & 0xffff0000u);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int t = 0; t < 8; ++t) v[i][t] = 0.0f;
+      }
+#pragma unroll
+      for (int t = 0; t < 8; ++t) m = max(m, __float_as_uint(v[i][t]) & 0x7fffffffu);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const int F = prescale_exponent(m);
+    const float up = __uint_as_float((uint32_t)(127 + F) << 23);
+    if (lane == b) my_unscale = __uint_as_float((uint32_t)(127 - F) << 23);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int p = lane + 32 * i;
+      if (p >= pieces) continue;
+      uint32_t h[4], l[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float v0 = v[i][2 * t] * up, v1 = v[i][2 * t + 1] * up;
+        h[t] = pack_half2(v0, v1);
+        if (XLO) {
+          const float2 f = __half22float2(*reinterpret_cast<__half2 *>(&h[t]));
+          l[t] = pack_half2(v0 - f.x, v1 - f.y);
+        }
+      }
+      const size_t o = (size_t)b * a.xpitch + k_lo + p * 8;
+      *reinterpret_cast<uint4 *>(xh + o) = make_uint4(h[0], h[1], h[2], h[3]);
+      if (XLO) *reinterpret_cast<uint4 *>(xl + o) = make_uint4(l[0], l[1], l[2], l[3]);
+    }
+  }
+  __syncwarp();
+  // Unscale of accumulator columns n = 2q, 2q + 1.
+  const float us0 = __shfl_sync(0xffffffffu, my_unscale, 2 * q);
+  const float us1 = __shfl_sync(0xffffffffu, my_unscale, 2 * q + 1);
+  const bool n_ok = g < a.batch;
+  const __half *xrow = xh + (size_t)(n_ok ? g : 0) * a.xpitch;
+  const __half *xrow_lo = xl + (size_t)(n_ok ? g : 0) * a.xpitch;
+
+  // ---- row blocks ------------------------------------------------------------
+  for (int rb = 0; rb < nrb; ++rb) {
+    const int s = rb % S;
+    const uint32_t parity = (uint32_t)(rb / S) & 1u;
+    uint8_t *st = stages + (size_t)s * a.stage_bytes;
+    bool ready = false;
+    for (uint32_t i = 0; i < sm100::kSpinLimit && !ready; ++i) ready = sm100::mbar_try_wait(&full[s], parity);
+    if (!ready) {  // copies that never landed: record it and leave
+      if (lane == 0 && a.error) atomicCAS(a.error, 0, 201);
+      return;
+    }
+    float acc[4][4];
+#pragma unroll
+    for (int c4 = 0; c4 < 4; ++c4)
+#pragma unroll
+      for (int t = 0; t < 4; ++t) acc[c4][t] = 0.0f;
+
+    for (int c = c_lo; c < c_hi; ++c) {
+      const uint4 wa = lds128(st + g * a.wpitch + c * 64 + q * 16);
+      const uint4 wb = lds128(st + (g + 8) * a.wpitch + c * 64 + q * 16);
+      const uint8_t *sc = st + 16 * a.wpitch;
+      const uint16_t sa = lds16(sc + g * a.spitch + c * 8 + 2 * q);
+      const uint16_t sb = lds16(sc + (g + 8) * a.spitch + c * 8 + 2 * q);
+      uint32_t s_lo[2], s_hi[2];
+      {
+        const uint32_t fa = e4m3x2_to_f16x2(sa), fb = e4m3x2_to_f16x2(sb);
+        s_lo[0] = __byte_perm(fa, fa, 0x1010);
+        s_hi[0] = __byte_perm(fa, fa, 0x3232);
+        s_lo[1] = __byte_perm(fb, fb, 0x1010);
+        s_hi[1] = __byte_perm(fb, fb, 0x3232);
+      }
+      const uint32_t w0[4] = {wa.x, wa.y, wa.z, wa.w};
+      const uint32_t w1[4] = {wb.x, wb.y, wb.z, wb.w};
+      const int k0 = c * 128 + q * 32;
+#pragma unroll
+      for (int wi = 0; wi < 4; ++wi) {
+        uint4 xv = make_uint4(0, 0, 0, 0), xlv = make_uint4(0, 0, 0, 0);
+        if (n_ok) {
+          xv = lds128(xrow + k0 + 8 * wi);
+          if (XLO) xlv = lds128(xrow_lo + k0 + 8 * wi);
+        }
+        uint32_t f0[4], f1[4];
+        e2m1x8_to_f16x8(w0[wi], f0);
+        e2m1x8_to_f16x8(w1[wi], f1);
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          f0[t] = hmul2(f0[t], wi < 2 ? s_lo[0] : s_hi[0]);
+          f1[t] = hmul2(f1[t], wi < 2 ? s_lo[1] : s_hi[1]);
+        }
+        // MMA 2wi + jj takes codes 4jj..4jj+3 of this word and x words 2jj, 2jj+1.
+        const int ch = (wi & 1) * 2;
+        mma_f16(acc[ch], f0[0], f1[0], f0[1], f1[1], xv.x, xv.y);
+        mma_f16(acc[ch + 1], f0[2], f1[2], f0[3], f1[3], xv.z, xv.w);
+        if (XLO) {
+          mma_f16(acc[ch], f0[0], f1[0], f0[1], f1[1], xlv.x, xlv.y);
+          mma_f16(acc[ch + 1], f0[2], f1[2], f0[3], f1[3], xlv.z, xlv.w);
+        }
+      }
+    }
+    float4 *slot = red + (size_t)s * kStreamWarps * 32;
+    slot[warp * 32 + lane] = make_float4((acc[0][0] + acc[1][0] + acc[2][0] + acc[3][0]) * us0,
+                                         (acc[0][1] + acc[1][1] + acc[2][1] + acc[3][1]) * us1,
+                                         (acc[0][2] + acc[1][2] + acc[2][2] + acc[3][2]) * us0,
+                                         (acc[0][3] + acc[1][3] + acc[2][3] + acc[3][3]) * us1);
+    // The last of the 8 warps to finish this row block reduces it, stores y
+    // and refills the stage (the counter only grows: last = 8th arrival).
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) {
+      __threadfence_block();
+      last = (atomicAdd(&count[s], 1) % kStreamWarps) == kStreamWarps - 1;
+      __threadfence_block();
+    }
+    last = __shfl_sync(0xffffffffu, last, 0);
+    __syncwarp();
+    if (!last) continue;
+    float4 sum = slot[lane];
+#pragma unroll
+    for (int w = 1; w < kStreamWarps; ++w) {
+      const float4 p = slot[w * 32 + lane];
+      sum.x += p.x; sum.y += p.y; sum.z += p.z; sum.w += p.w;
+    }
+    const float *gl = reinterpret_cast<const float *>(st + 16 * a.wpitch + 16 * a.spitch);
+    const float vals[4] = {sum.x, sum.y, sum.z, sum.w};
+    const int rbase = row_lo + rb * 16;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const int rl = g + ((t >> 1) << 3), r = rbase + rl, n = 2 * q + (t & 1);
+      if (r < row_hi && n < a.batch) {
+        const float v = vals[t] * gl[rl];
+        const size_t off = (size_t)n * a.rows + r;
+        if (a.y_bf16)
+          reinterpret_cast<__nv_bfloat16 *>(a.y)[off] = __float2bfloat16_rn(v);
+        else
+          reinterpret_cast<float *>(a.y)[off] = v;
+      }
+    }
+    if (rb + S < nrb) {
+      __syncwarp();
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      stream_issue(a, st, &full[s], row_lo + 16 * (rb + S), min(16, row_hi - row_lo - 16 * (rb + S)), lane);
+    }
+  }
+}
+
 // ---- host dispatch -----------------------------------------------------------
 struct GemvConfig {
   int C, wk, g, threads;
@@ -528,6 +804,98 @@ static int run_gemv(GemvArgs args, int slots, bool x_f32, cudaStream_t stream) {
   return FPB_OK;
 }
 
+
+// Shared memory one streaming CTA may use: two CTAs (and their 1 KB system
+// reservations) fit in the 228 KB of an SM.
+constexpr int kStreamSmemBudget = 110 * 1024;
+
+struct StreamPlan {
+  StreamArgs a;
+  int grid;
+  size_t smem;
+};
+
+// Fills `plan` when the streaming kernel serves this call; false otherwise.
+static bool plan_stream(const uint8_t *packed, const uint8_t *scales, const float *globals, int rows, int K,
+                        int batch, bool x_f32, StreamPlan *plan) {
+  if (K % 128 != 0 || K > 4096 || batch < 1 || batch > 8 || rows % 4 != 0 || rows <= 0) return false;
+  if (reinterpret_cast<uintptr_t>(packed) % 16 || reinterpret_cast<uintptr_t>(scales) % 16 ||
+      reinterpret_cast<uintptr_t>(globals) % 16)
+    return false;
+  StreamArgs a{};
+  a.packed = packed;
+  a.scales = scales;
+  a.globals = globals;
+  a.rows = rows;
+  a.K = K;
+  a.batch = batch;
+  const int kb2 = K / 2, kb16 = K / 16;
+  a.wpitch = kb2 + ((kb2 % 128 == 0) ? 64 : 0);  // 64 mod 128
+  a.scale_rows = kb16 % 16 == 0;
+  a.spitch = a.scale_rows ? kb16 + (16 - kb16 % 128 + 128) % 128 : kb16;  // 16 mod 128 when per row
+  a.stage_bytes = 16 * a.wpitch + 16 * a.spitch + 64;
+  a.xpitch = K + 32;
+  const int nsm = std::max(1, sm_count());
+  int rpc = (rows + nsm - 1) / nsm;
+  rpc = (rpc + 3) / 4 * 4;
+  a.rpc = rpc;
+  const int nrb_max = (rpc + 15) / 16;
+  const size_t x_bytes = (size_t)batch * a.xpitch * 2 * (x_f32 ? 2 : 1);
+  const size_t per_stage = (size_t)a.stage_bytes + kStreamWarps * 32 * sizeof(float4) + 12;
+  if (x_bytes + per_stage + 16 > (size_t)kStreamSmemBudget) return false;
+  int S = (int)((kStreamSmemBudget - x_bytes - 16) / per_stage);
+  S = std::max(1, std::min({S, 8, nrb_max}));
+  a.stages = S;
+  plan->a = a;
+  plan->grid = (rows + rpc - 1) / rpc;
+  plan->smem = (size_t)S * per_stage + x_bytes + 16;
+  return true;
+}
+
+static int launch_stream(StreamPlan &plan, const void *x, bool x_f32, void *y, bool y_bf16, cudaStream_t stream) {
+  plan.a.x = x;
+  plan.a.y = y;
+  plan.a.y_bf16 = y_bf16;
+  plan.a.error = device_error_ptr();
+  auto k = x_f32 ? gemv_nvfp4_stream_kernel<true> : gemv_nvfp4_stream_kernel<false>;
+  {
+    // Raised once per device and kernel to the budget, never lowered.
+    static std::mutex mu;
+    static std::vector<std::pair<int, const void *>> done;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    const void *key = reinterpret_cast<const void *>(k);
+    if (std::find(done.begin(), done.end(), std::make_pair(dev, key)) == done.end()) {
+      FPB_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmemBudget));
+      done.push_back({dev, key});
+    }
+  }
+  cudaLaunchConfig_t lc{};
+  lc.gridDim = dim3(plan.grid);
+  lc.blockDim = dim3(kStreamWarps * 32);
+  lc.dynamicSmemBytes = plan.smem;
+  lc.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  cudaError_t le = cudaLaunchKernelEx(&lc, k, plan.a);
+  if (le == cudaErrorInvalidValue) {
+    cudaGetLastError();
+    lc.numAttrs = 0;
+    le = cudaLaunchKernelEx(&lc, k, plan.a);
+  }
+  if (le != cudaSuccess) {
+    cudaGetLastError();
+    return fail(FPB_ERR_CUDA, "cudaLaunchKernelEx(gemv_nvfp4_stream_kernel): %s; grid %d smem %zu stages %d",
+                cudaGetErrorName(le), plan.grid, plan.smem, plan.a.stages);
+  }
+  FPB_LAUNCH_CHECK("gemv_nvfp4_stream_kernel");
+  return FPB_OK;
+}
+
 }  // namespace fpb
 
 using namespace fpb;
@@ -558,6 +926,9 @@ extern "C" int fpb_nvfp4_gemv(const fpb_nvfp4_matrix *w, size_t row_begin, size_
   a.y_bf16 = y_dtype == FPB_BF16;
   a.y_batch_stride = a.rows;
   const bool x_f32 = x_dtype == FPB_F32;
+  StreamPlan plan;
+  if (plan_stream(a.packed, a.scales, a.globals, a.rows, a.K, batch, x_f32, &plan))
+    return launch_stream(plan, x, x_f32, y, a.y_bf16 != 0, as_stream(stream));
   // More input rows than one launch holds in registers run as several
   // launches over row groups of x (each re-reads W).
   const int step = std::min(batch, gemv_max_batch((int)w->cols, x_f32));

@@ -157,7 +157,7 @@ def _synthetic(F, torch, rows, cols, seed=0, rpg=None):
 
 
 @pytest.mark.parametrize("rows,cols", [(4096, 4096), (8192, 2048), (1000, 512), (24, 96), (130, 2080),
-                                       (7, 32), (2048, 4000)])
+                                       (7, 32), (2048, 4000), (8192, 4096), (20000, 512), (1002, 1024)])
 @pytest.mark.parametrize("batch", [1, 3, 8, 16])
 def test_gemv_shapes_batches(F, torch, rows, cols, batch):
     m, h = _synthetic(F, torch, rows, cols, seed=rows * 7 + cols)

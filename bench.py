@@ -46,8 +46,9 @@ def parse_args():
     p.add_argument("--steps", type=int, default=2000)
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--config", choices=["gemv", "nvfp4_gemm_m128", "nvfp4_gemm_m2048"], default="gemv",
-                   help="gemv: config 0 (default); nvfp4_gemm_m*: config 2 GEMM at M=128 / M=2048")
+    p.add_argument("--config", choices=["gemv", "nvfp4_gemm_m128", "nvfp4_gemm_m2048", "fp8_gemm"], default="gemv",
+                   help="gemv: config 0 (default); nvfp4_gemm_m*: config 2 GEMM at M=128 / M=2048; "
+                        "fp8_gemm: config 1")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the cpu_baseline sample")
     return p.parse_args()
 
@@ -550,9 +551,209 @@ def gemm_arm(args):
         dist.destroy_process_group()
 
 
+# ---- config 1: FP8 E4M3 GEMM (tcgen05 kind::f8f6f4) -------------------------------------
+FP8_M, FP8_K, FP8_N, FP8_MATS = 512, 4096, 14336, 4
+
+
+def fp8_cpu_sample(seconds: float):
+    """The host path restated on a bounded sample: dequantize both FP8 operands
+    and multiply in f32 (numpy/BLAS on all host cores).  Returns (TFLOP/s,
+    sample description)."""
+    import numpy as np
+
+    from oracle import oracle as O
+    n = 2048  # weight rows of the sample (of 14336)
+    w = O.synth_normal(n * FP8_K, seed=0, stream=1, std=0.02).reshape(n, FP8_K)
+    wb, ws = O.fp8_quantize(w, 128, 128)
+    wd = O.fp8_dequantize(wb, ws, 128, 128)
+    x = O.bf16_to_f32(O.bf16_bits(O.synth_normal(FP8_M * FP8_K, seed=0, stream=0))).reshape(FP8_M, FP8_K)
+    ab, as_ = O.fp8_quantize(x)
+    xd = O.fp8_dequantize(ab, as_)
+    t0 = time.perf_counter()
+    _ = xd @ wd.T
+    one = max(time.perf_counter() - t0, 1e-4)
+    reps = max(1, int(seconds / one))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        _ = xd @ wd.T
+    dt = (time.perf_counter() - t0) / reps
+    return 2.0 * FP8_M * n * FP8_K / dt / 1e12, (
+        f"{reps} x (A[{FP8_M},{FP8_K}] x W[{n} of {FP8_N},{FP8_K}]^T), dequantized FP8 (128x128 blocks, per-token A), "
+        f"f32 BLAS")
+
+
+def fp8_reference_arm(args):
+    rank, _, _ = dist_env()
+    if rank != 0:
+        return
+    budget = max(5.0, min(60.0, 3.0 * (args.steps + args.warmup)))
+    tflops, sample = fp8_cpu_sample(budget)
+    emit({"impl": "reference", "metric": "FP8 GEMM TFLOPS", "value": tflops, "unit": "TFLOP/s",
+          "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+          "ms_per_step": 2.0 * FP8_M * FP8_N * FP8_K / (tflops * 1e12) * 1e3, "higher_is_better": True,
+          "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded Philox)",
+          "config": {"workload": "config1 FP8 GEMM M=512 K=4096 N=14336"},
+          "cpu_baseline": {"value": tflops, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
+                           "sample": sample},
+          "e2e": {"value": tflops, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
+
+
+def fp8_arm(args):
+    """Config 1: A bf16 [512, 4096] N(0,1) quantized per token to e4m3 on the
+    device, times 4 distinct W [14336, 4096] N(0,0.02) e4m3 with 128x128 block
+    scales (N-split over the ranks) per step, y bf16; 235 MB of weights per
+    step at g = 1 (> L2)."""
+    import torch
+    import torch.distributed as dist
+
+    import firepit_b200 as F
+    N_ = F._native
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    g = world
+    n_rank = FP8_N // g
+    r0 = rank * n_rank
+    mats = []
+    for c in range(FP8_MATS):
+        w = F.synth_normal((FP8_N, FP8_K), seed=0, stream_id=1 + c, std=0.02, device=dev)
+        bits, scales = F.quantize_fp8(w, F.Fp8Scaling(128, 128))
+        del w
+        sc = scales.view(FP8_N // 128, FP8_K // 128)[r0 // 128:(r0 + n_rank) // 128].contiguous()
+        mats.append(F.Fp8Matrix.from_device(bits[r0:r0 + n_rank].contiguous(), sc, n_rank, FP8_K,
+                                            F.Fp8Scaling(128, 128)))
+        del bits, scales
+    x = F.synth_normal((FP8_M, FP8_K), seed=0, stream_id=0, dtype=torch.bfloat16, device=dev)
+    qa = torch.empty(FP8_M, FP8_K, dtype=torch.uint8, device=dev)
+    qs = torch.empty(FP8_M, dtype=torch.float32, device=dev)
+    ys = torch.empty(FP8_MATS, FP8_M, n_rank, dtype=torch.bfloat16, device=dev)
+    y_all = torch.empty(g, FP8_MATS, FP8_M, n_rank, dtype=torch.bfloat16, device=dev)
+    ws_bytes = int(N_.lib.fpb_fp8_gemm_workspace_bytes(FP8_M, FP8_K))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+
+    def quant(sh):
+        N_.call("fpb_fp8_quantize", x.data_ptr(), N_.FPB_BF16, FP8_M, FP8_K, 0, 0, qa.data_ptr(), qs.data_ptr(), sh)
+
+    def gemms(sh):
+        for c in range(FP8_MATS):
+            N_.call("fpb_fp8_gemm_q", mats[c].handle, 0, 0, qa.data_ptr(), qs.data_ptr(), FP8_M, ys[c].data_ptr(),
+                    N_.FPB_BF16, sh)
+
+    s = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(s):
+        quant(s.cuda_stream)
+        gemms(s.cuda_stream)
+    torch.cuda.synchronize()
+    before = F.launch_count()
+    gq, gg = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gq, stream=s):
+        quant(torch.cuda.current_stream().cuda_stream)
+    with torch.cuda.graph(gg, stream=s):
+        gemms(torch.cuda.current_stream().cuda_stream)
+    launches_per_step = F.launch_count() - before
+
+    def step(ev=None):
+        if ev:
+            ev[0].record()
+        gq.replay()
+        if ev:
+            ev[1].record()
+        gg.replay()
+        if ev:
+            ev[2].record()
+        if g > 1:
+            dist.all_gather_into_tensor(y_all, ys)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    if g > 1:
+        dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record()
+        for i in range(args.steps):
+            step(evs[i])
+        end.record()
+        torch.cuda.synchronize()
+    t = torch.tensor([start.elapsed_time(end), sum(e[0].elapsed_time(e[1]) for e in evs),
+                      sum(e[1].elapsed_time(e[2]) for e in evs)], device=dev, dtype=torch.float64)
+    if g > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms, quant_ms, gemm_ms = t.tolist()
+    ms_per_step = total_ms / args.steps
+    flops_step = 2.0 * FP8_M * FP8_N * FP8_K * FP8_MATS
+    value = flops_step / (ms_per_step * 1e-3) / 1e12
+
+    xh = x.cpu().pin_memory()
+    yh = torch.empty(FP8_MATS, FP8_M, n_rank, dtype=torch.bfloat16, pin_memory=True)
+    xd = torch.empty_like(x)
+    sink = F.Async()
+
+    def e2e_step():
+        xd.copy_(xh, non_blocking=True)
+        for c in range(FP8_MATS):
+            F.fp8_gemm(mats[c], xd, ys[c], workspace=ws).submit(sink)
+        yh.copy_(ys, non_blocking=True)
+
+    e2e_steps = max(1, min(args.steps, 20))
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    te = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+    if g > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = flops_step / (te.item() / e2e_steps * 1e-3) / 1e12
+
+    per_launch_ms = gemm_ms / (args.steps * FP8_MATS)
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    bf16 = float(peaks.get("bf16_tflops", 1590.0))
+    achieved = 2.0 * FP8_M * n_rank * FP8_K / (per_launch_ms * 1e-3) / 1e12
+    roof = {"bound": "tensor", "achieved": achieved, "peak": 2 * bf16, "unit": "TFLOP/s",
+            "frac": achieved / (2 * bf16), "traffic": None, "per_launch_us": per_launch_ms * 1e3,
+            "peak_kind": "2 x measured bf16 burst (nominal dense FP8:BF16 ratio; no FP8 measurement)"}
+    if rank == 0:
+        line = {"metric": "FP8 GEMM TFLOPS", "value": value, "unit": "TFLOP/s", "n_gpus": g, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "e4m3 x e4m3 (128x128 block / per-token f32 scales), f32 accumulate, "
+                                              "bf16 out",
+                "data": "synthetic (seeded Philox: W N(0,0.02), A N(0,1) seed 0)",
+                "config": {"workload": "config1 FP8 GEMM M=512 K=4096 N=14336, A bf16 quantized per token on device",
+                           "matrices_per_step": FP8_MATS, "n_per_rank": n_rank,
+                           "l2": "inputs larger than L2 (4 distinct weights, 235 MB per step)",
+                           "parallelism": f"N-split x{g} + NCCL all-gather" if g > 1 else "single GPU"},
+                "roofline": roof,
+                "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": FP8_M * FP8_K * 2,
+                        "d2h_bytes_per_step": FP8_MATS * FP8_M * n_rank * 2},
+                "gpu_launches": launches_per_step * args.steps, "clocks": clocks.summary(),
+                "breakdown_ms": {"quantize_act": quant_ms / args.steps, "gemms": gemm_ms / args.steps}}
+        if g == 1 and args.cpu_seconds > 0:
+            v, sample = fp8_cpu_sample(args.cpu_seconds)
+            line["cpu_baseline"] = {"value": v, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
+                                    "sample": sample}
+        emit(line)
+    del gq, gg
+    if g > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
-    if args.config.startswith("nvfp4_gemm"):
+    if args.config == "fp8_gemm":
+        (fp8_reference_arm if args.impl == "reference" else fp8_arm)(args)
+    elif args.config.startswith("nvfp4_gemm"):
         (gemm_reference_arm if args.impl == "reference" else gemm_arm)(args)
     elif args.impl == "reference":
         reference_arm(args)

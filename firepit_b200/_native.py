@@ -88,6 +88,17 @@ SIGNATURES: dict[str, tuple] = {
     "fpb_nvfp4_gemm": (i32, [vp, sz, sz, vp, i32, sz, vp, i32, vp, sz, vp]),
     "fpb_nvfp4_grouped_gemm_q": (i32, [vp, vp, vp, vp, sz, vp, sz, vp, i32, vp]),
     "fpb_device_error": (i32, [C.POINTER(i32), i32]),
+    "fpb_fp8_validate": (i32, [sz, vp, sz, sz, sz, sz, sz]),
+    "fpb_fp8_matrix_create": (i32, [vp, vp, sz, sz, sz, sz, vp, C.POINTER(vp)]),
+    "fpb_fp8_matrix_create_device": (i32, [vp, vp, sz, sz, sz, sz, vp, C.POINTER(vp)]),
+    "fpb_fp8_matrix_destroy": (i32, [vp]),
+    "fpb_fp8_matrix_shape": (i32, [vp, C.POINTER(sz), C.POINTER(sz), C.POINTER(sz), C.POINTER(sz)]),
+    "fpb_fp8_matrix_download": (i32, [vp, vp, vp, vp]),
+    "fpb_fp8_quantize": (i32, [vp, i32, sz, sz, sz, sz, vp, vp, vp]),
+    "fpb_fp8_gemm_workspace_bytes": (sz, [sz, sz]),
+    "fpb_fp8_gemm_q": (i32, [vp, sz, sz, vp, vp, sz, vp, i32, vp]),
+    "fpb_fp8_gemm": (i32, [vp, sz, sz, vp, i32, sz, vp, i32, vp, sz, vp]),
+    "fpb_fp8_grouped_gemm_q": (i32, [vp, vp, vp, sz, vp, sz, vp, i32, vp]),
     "fpb_moe_dims_validate": (i32, [sz, sz, sz, sz, sz]),
     "fpb_expert_selection_validate": (i32, [vp, vp, sz, sz, sz]),
     "fpb_prefill_layout_max_padded_rows": (i32, [sz, sz, sz, sz, C.POINTER(sz)]),

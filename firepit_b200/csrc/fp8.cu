@@ -1,0 +1,620 @@
+// FP8 E4M3 weights, quantizers and the prefill FP8 GEMM on the tcgen05 tensor
+// cores (crates/firepit-kernels/src/weights/fp8.rs, src/gemm/mod.rs:67-206,
+// 417-697).
+//
+// Formats (weights/fp8.rs:8-27): bits [rows, cols] e4m3 row-major; scales f32
+// either a [rows/block_n, cols/block_k] grid (Fp8Scaling::Blocks) or one per
+// row (Fp8Scaling::Rows, block_n = block_k = 0 at this ABI).
+//
+// Quantizers (no reference counterpart; the rule of the task's config 1):
+// scale = amax/448 over each block (or row, or activation token), bits =
+// RN_e4m3_satfinite(w / scale), 0 when the scale is 0.  Every step is a single
+// IEEE operation, so the result equals the CPU oracle bit for bit.
+//
+// GEMM.  y[m, n] = sum_kb (w_s[n / block_n, kb] a_s[m]) * sum_{k in kb} a[m,k] w[n,k]
+// (blocks) or (a_s[m] w_s[n]) * sum_k a[m,k] w[n,k] (rows), activations
+// quantized to e4m3 with a per-token scale (the config's W8A8 setting; the
+// reference keeps f32 activations split into bf16 hi/lo).  One CTA per
+// 128 x 256 output tile (operand bytes per MMA flop are what bound a
+// 128 x 128 tile: both operands stream from L2 for every K block):
+//  * warp 0: TMA producer, 4-stage ring of a 128 x 128-byte A tile and a
+//    256 x 128-byte B tile per 128-wide K block (128-byte swizzle);
+//  * warp 1: TMEM allocation and MMA issue, four
+//    tcgen05.mma.cta_group::1.kind::f8f6f4 (M 128, N 256, K 32) per K block;
+//  * warps 2..9: epilogue, two warps per 32-lane TMEM quadrant (128 columns
+//    each).
+// Block scales vary along K every 128 columns, so with block scaling each K
+// block's product goes to one of two TMEM accumulators (double-buffered): the
+// epilogue warps read it, multiply it by that block's scale and add it to
+// their register accumulators while the tensor cores fill the other buffer
+// (the promotion of per-block partial sums in f32, as in the reference's
+// per-part scale).  With row scales the tensor cores accumulate the whole K
+// range in TMEM.  Every mbarrier wait is bounded; a wait that gives up records
+// an error code (fpb_device_error) and ends its role.  No TMA multicast.
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <vector>
+
+#include "common.cuh"
+#include "sm100.cuh"
+#include "tma_host.cuh"
+
+// Device-side FP8 weight matrix (Fp8Matrix, weights/fp8.rs:14-19).
+struct fpb_fp8_matrix {
+  size_t rows = 0, cols = 0;
+  int block_n = 0, block_k = 0;  // 0, 0: one scale per row
+  int device = 0;
+  uint8_t *bits = nullptr;
+  float *scales = nullptr;
+  size_t n_scales = 0;
+  alignas(64) unsigned char tmap[128];
+  bool tmap_valid = false;
+};
+
+namespace fpb {
+
+// ---- quantizer ---------------------------------------------------------------------
+__device__ __forceinline__ float load_as_f32(const float *p, size_t i) { return p[i]; }
+__device__ __forceinline__ float load_as_f32(const __nv_bfloat16 *p, size_t i) { return __bfloat162float(p[i]); }
+
+// One CTA per scale block of bn rows x bk columns (bk a multiple of 4).
+template <typename T>
+__global__ void __launch_bounds__(256) fp8_quantize_kernel(const T *w, size_t cols, int bn, int bk, uint8_t *bits,
+                                                           float *scales) {
+  __shared__ uint32_t wmax[8];
+  const size_t gc = cols / (size_t)bk;
+  const size_t b = blockIdx.x;
+  const size_t r0 = (b / gc) * (size_t)bn, c0 = (b % gc) * (size_t)bk;
+  const int q4 = bk / 4;
+  const int n4 = bn * q4;
+  uint32_t m = 0;
+  for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+    const size_t base = (r0 + i / q4) * cols + c0 + (size_t)(i % q4) * 4;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) m = max(m, __float_as_uint(load_as_f32(w, base + t)) & 0x7fffffffu);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = m;
+  __syncthreads();
+  m = 0;
+  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) m = max(m, wmax[i]);
+  const float s = __fdiv_rn(__uint_as_float(m), 448.0f);
+  if (threadIdx.x == 0) scales[b] = s;
+  for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+    const size_t base = (r0 + i / q4) * cols + c0 + (size_t)(i % q4) * 4;
+    uint32_t packed = 0;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const uint32_t q = s > 0.0f ? f32_to_e4m3(__fdiv_rn(load_as_f32(w, base + t), s)) : 0u;
+      packed |= q << (8 * t);
+    }
+    *reinterpret_cast<uint32_t *>(bits + base) = packed;
+  }
+}
+
+// ---- GEMM kernel ---------------------------------------------------------------------
+constexpr int kF8Tile = 128;                      // M and K-block (bytes) of a tile
+constexpr int kF8BN = 256;                        // N of a tile
+constexpr int kF8Stages = 4;
+constexpr int kF8ABytes = kF8Tile * kF8Tile;      // 16 KB of A per stage
+constexpr int kF8BBytes = kF8BN * kF8Tile;        // 32 KB of B per stage
+constexpr int kF8EpiWarps = 8;
+constexpr int kF8Threads = 64 + 32 * kF8EpiWarps;
+constexpr uint32_t kF8TmemCols = 512;             // two 256-column accumulators
+constexpr size_t kF8Smem = 1024 + kF8Stages * (kF8ABytes + kF8BBytes) + 256;
+
+struct Fp8GemmParams {
+  const float *a_scale;  // [M] per token
+  const float *w_scale;  // blocks: [rows/bn, ws_cols]; rows: [rows]
+  void *y;
+  long long ldy;
+  int y_bf16;
+  int M;
+  int N;           // weight rows of the view (grouped: rows per expert)
+  int n_base;      // first weight row of the view (multiple of 128)
+  int kb_count;    // ceil(K / 128)
+  int bn, bk;      // block scaling: multiples of 128
+  int ws_cols;     // columns of the scale grid
+  int *error;
+  const int32_t *tile_experts;  // grouped mode (gemm/mod.rs:103-140), else null
+  int n_experts;
+};
+
+__device__ __forceinline__ void f8_report(int *error, volatile int *abort, int code) {
+  *abort = 1;
+  if (error) atomicCAS(error, 0, code);
+}
+
+template <bool kBlocks>
+__global__ void __launch_bounds__(kF8Threads, 1)
+    fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                    Fp8GemmParams p) {
+  using namespace sm100;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *sA = base;
+  uint8_t *sB = sA + kF8Stages * kF8ABytes;
+  uint64_t *full = reinterpret_cast<uint64_t *>(sB + kF8Stages * kF8BBytes);
+  uint64_t *empty = full + kF8Stages;
+  uint64_t *acc_full = empty + kF8Stages;  // [2]
+  uint64_t *acc_empty = acc_full + 2;      // [2]
+  uint32_t *tmem_base_s = reinterpret_cast<uint32_t *>(acc_empty + 2);
+  volatile int *abort_s = reinterpret_cast<volatile int *>(tmem_base_s + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_tile = blockIdx.x, m_tile = blockIdx.y;
+  const int m0 = m_tile * kF8Tile, n0 = n_tile * kF8BN;
+  int n_base = p.n_base;
+  if (p.tile_experts) {
+    const int e = p.tile_experts[m_tile];
+    if (e < 0 || e >= p.n_experts) {
+      if (threadIdx.x == 0 && p.error) atomicCAS(p.error, 0, 306);
+      return;
+    }
+    n_base = e * p.N;
+  }
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kF8Stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], kF8EpiWarps);
+    }
+    *abort_s = 0;
+    fence_barrier_init();
+    prefetch_tensormap(&tmap_a);
+    prefetch_tensormap(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_base_s, kF8TmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_base_s;
+
+  if (warp == 0) {
+    // ---- TMA producer ----------------------------------------------------------
+    if (elect_one()) {
+      int issued = 0;
+      for (int kb = 0; kb < p.kb_count; ++kb) {
+        const int s = kb % kF8Stages, round = kb / kF8Stages;
+        if (kb >= kF8Stages && !mbar_wait(&empty[s], (round - 1) & 1, abort_s)) {
+          f8_report(p.error, abort_s, 301);
+          break;
+        }
+        mbar_arrive_expect_tx(&full[s], kF8ABytes + kF8BBytes);
+        tma_load_2d(sA + s * kF8ABytes, &tmap_a, kb * kF8Tile, m0, &full[s]);
+        tma_load_2d(sB + s * kF8BBytes, &tmap_b, kb * kF8Tile, n_base + n0, &full[s]);
+        issued = kb + 1;
+      }
+      for (int kb = (issued > kF8Stages ? issued - kF8Stages : 0); kb < issued; ++kb)
+        if (!mbar_wait(&full[kb % kF8Stages], (kb / kF8Stages) & 1, abort_s)) f8_report(p.error, abort_s, 302);
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer -------------------------------------------------------------
+    if (elect_one()) {
+      const uint32_t idesc = idesc_f8(kF8Tile, kF8BN);
+      bool ok = true;
+      for (int kb = 0; kb < p.kb_count && ok; ++kb) {
+        const int s = kb % kF8Stages, round = kb / kF8Stages;
+        if (!mbar_wait(&full[s], round & 1, abort_s)) {
+          f8_report(p.error, abort_s, 303);
+          ok = false;
+          break;
+        }
+        const int b = kBlocks ? (kb & 1) : 0;
+        if (kBlocks && kb >= 2 && !mbar_wait(&acc_empty[b], ((kb >> 1) - 1) & 1, abort_s)) {
+          f8_report(p.error, abort_s, 304);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint64_t a_desc = smem_desc(smem_u32(sA + s * kF8ABytes) + kk * 32, 16, 1024, 2);
+          const uint64_t b_desc = smem_desc(smem_u32(sB + s * kF8BBytes) + kk * 32, 16, 1024, 2);
+          const uint32_t acc = kBlocks ? (kk != 0) : ((kb | kk) != 0);
+          mma_f8(tmem + b * kF8BN, a_desc, b_desc, idesc, acc);
+        }
+        tc_commit(&empty[s]);
+        if (kBlocks) tc_commit(&acc_full[b]);
+      }
+      if (!kBlocks && ok) tc_commit(&acc_full[0]);
+    }
+  } else {
+    // ---- epilogue: quadrant (warp % 4), column half (warp - 2) / 4 -------------
+    constexpr int kCols = kF8BN / 2;  // columns per epilogue warp
+    const int qd = warp & 3, half = (warp - 2) >> 2;
+    const int row = m0 + qd * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
+    const int c_base = half * kCols;
+    float acc[kCols];
+#pragma unroll
+    for (int j = 0; j < kCols; ++j) acc[j] = 0.0f;
+    bool ok = true;
+    // The token scale is folded into each block scale before it meets the
+    // partial sums, so that extreme but finite scale pairs (one tiny, one
+    // huge) do not overflow or underflow in between.
+    const float as = row < p.M ? __ldg(p.a_scale + row) : 0.0f;
+    if (kBlocks) {
+      // A half's 128 columns lie in one block of bn (a multiple of 128) rows.
+      const int nb = (n_base + n0 + c_base) / p.bn;
+      const float *ws_row = p.w_scale + (size_t)nb * p.ws_cols;
+      for (int kb = 0; kb < p.kb_count; ++kb) {
+        const int b = kb & 1;
+        if (!mbar_wait(&acc_full[b], (kb >> 1) & 1, abort_s)) {
+          f8_report(p.error, abort_s, 305);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const float ws = __ldg(ws_row + (kb * kF8Tile) / p.bk) * as;
+#pragma unroll
+        for (int c = 0; c < kCols / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tmem + lane_base + b * kF8BN + c_base + c * 32, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[c * 32 + j] = fmaf(__uint_as_float(r[j]), ws, acc[c * 32 + j]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[b]);
+      }
+    } else {
+      if (mbar_wait(&acc_full[0], 0, abort_s)) {
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < kCols / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tmem + lane_base + c_base + c * 32, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[c * 32 + j] = __uint_as_float(r[j]);
+        }
+      } else {
+        f8_report(p.error, abort_s, 305);
+        ok = false;
+      }
+    }
+    if (ok && row < p.M) {
+      const int nc = n0 + c_base;
+      // Final scale in place (rows mode: token x weight-row scale).
+#pragma unroll
+      for (int j = 0; j < kCols; ++j) {
+        if (!kBlocks) {
+          const float ws = (nc + j < p.N) ? __ldg(p.w_scale + n_base + nc + j) : 0.0f;
+          acc[j] = acc[j] * (as * ws);
+        }
+      }
+      const long long off = (long long)row * p.ldy + nc;
+      const bool full_cols = nc + kCols <= p.N;
+      if (p.y_bf16) {
+        __nv_bfloat16 *yp = reinterpret_cast<__nv_bfloat16 *>(p.y) + off;
+        if (full_cols && (reinterpret_cast<uintptr_t>(yp) & 15) == 0) {
+#pragma unroll
+          for (int j = 0; j < kCols; j += 8) {
+            uint4 pk;
+            pk.x = pack_bf16x2(acc[j], acc[j + 1]);
+            pk.y = pack_bf16x2(acc[j + 2], acc[j + 3]);
+            pk.z = pack_bf16x2(acc[j + 4], acc[j + 5]);
+            pk.w = pack_bf16x2(acc[j + 6], acc[j + 7]);
+            *reinterpret_cast<uint4 *>(yp + j) = pk;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < kCols; ++j)
+            if (nc + j < p.N) yp[j] = __float2bfloat16_rn(acc[j]);
+        }
+      } else {
+        float *yp = reinterpret_cast<float *>(p.y) + off;
+        if (full_cols && (reinterpret_cast<uintptr_t>(yp) & 15) == 0) {
+#pragma unroll
+          for (int j = 0; j < kCols; j += 4)
+            *reinterpret_cast<float4 *>(yp + j) = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < kCols; ++j)
+            if (nc + j < p.N) yp[j] = acc[j];
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kF8TmemCols);
+  }
+}
+
+}  // namespace fpb
+
+// ---- host side -------------------------------------------------------------------------
+namespace fpb {
+
+static int fp8_check_layout(size_t rows, size_t cols, size_t block_n, size_t block_k, size_t *n_scales) {
+  if (block_n == 0 && block_k == 0) {
+    *n_scales = rows;
+  } else {
+    if (block_n == 0 || block_k == 0 || rows % block_n != 0 || cols % block_k != 0)
+      return fail(FPB_ERR_FORMAT, "invalid FP8 scale grid");  // weights/fp8.rs:39-46
+    *n_scales = (rows / block_n) * (cols / block_k);
+  }
+  if (rows == 0 || cols == 0 || cols % 32 != 0)
+    return fail(FPB_ERR_FORMAT, "invalid FP8 matrix or scales");  // weights/fp8.rs:91-98
+  if (block_n > 0x7fffffff || block_k > 0x7fffffff) return fail(FPB_ERR_UNSUPPORTED, "FP8 block too large");
+  return FPB_OK;
+}
+
+static int fp8_check_scales_host(const float *scales, size_t n) {
+  for (size_t i = 0; i < n; ++i)
+    if (!std::isfinite(scales[i])) return fail(FPB_ERR_FORMAT, "invalid FP8 matrix or scales");
+  return FPB_OK;
+}
+
+static int fp8_alloc(size_t rows, size_t cols, size_t bn, size_t bk, size_t n_scales, fpb_fp8_matrix **out) {
+  auto *m = new (std::nothrow) fpb_fp8_matrix();
+  if (!m) return fail(FPB_ERR_INVALID_ARGUMENT, "out of host memory");
+  m->rows = rows;
+  m->cols = cols;
+  m->block_n = (int)bn;
+  m->block_k = (int)bk;
+  m->n_scales = n_scales;
+  cudaGetDevice(&m->device);
+  cudaError_t e = cudaMalloc(&m->bits, rows * cols);
+  if (e == cudaSuccess) e = cudaMalloc(&m->scales, n_scales * sizeof(float));
+  if (e != cudaSuccess) {
+    cudaFree(m->bits);
+    cudaFree(m->scales);
+    delete m;
+    return cuda_fail(e, "cudaMalloc(FP8 matrix)");
+  }
+  *out = m;
+  return FPB_OK;
+}
+
+// Raises a kernel's dynamic shared-memory limit once per device.
+template <typename K>
+static int raise_smem_once(K kernel, int bytes) {
+  static std::mutex mu;
+  static std::vector<std::pair<int, const void *>> done;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  const void *key = reinterpret_cast<const void *>(kernel);
+  if (std::find(done.begin(), done.end(), std::make_pair(dev, key)) != done.end()) return FPB_OK;
+  FPB_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  done.push_back({dev, key});
+  return FPB_OK;
+}
+
+static int fp8_quantize_impl(const void *w, int dtype, size_t rows, size_t cols, size_t bn, size_t bk,
+                             uint8_t *bits, float *scales, cudaStream_t s) {
+  size_t n_scales = 0;
+  int st = fp8_check_layout(rows, cols, bn, bk, &n_scales);
+  if (st) return st;
+  if (dtype != FPB_F32 && dtype != FPB_BF16) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_fp8_quantize: dtype");
+  const bool row_mode = bn == 0 && bk == 0;
+  const int ibn = row_mode ? 1 : (int)bn, ibk = row_mode ? (int)cols : (int)bk;
+  if (ibk % 4 != 0) return fail(FPB_ERR_SHAPE, "fpb_fp8_quantize: block_k %d not a multiple of 4", ibk);
+  if ((size_t)ibn * ibk > 0x7fffffffu || n_scales > 0x7fffffffu)
+    return fail(FPB_ERR_UNSUPPORTED, "fpb_fp8_quantize: too many elements per block or blocks");
+  if (dtype == FPB_F32)
+    fp8_quantize_kernel<float><<<(unsigned)n_scales, 256, 0, s>>>(static_cast<const float *>(w), cols, ibn, ibk,
+                                                                  bits, scales);
+  else
+    fp8_quantize_kernel<__nv_bfloat16><<<(unsigned)n_scales, 256, 0, s>>>(
+        static_cast<const __nv_bfloat16 *>(w), cols, ibn, ibk, bits, scales);
+  FPB_LAUNCH_CHECK("fp8_quantize_kernel");
+  return FPB_OK;
+}
+
+static int fp8_prepare(fpb_fp8_matrix *w) {
+  if (w->tmap_valid) return FPB_OK;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  if (w->tmap_valid) return FPB_OK;
+  int st = encode_rows_u8(reinterpret_cast<CUtensorMap *>(w->tmap), w->bits, w->rows, w->cols, kF8BN);
+  if (st) return st;
+  w->tmap_valid = true;
+  return FPB_OK;
+}
+
+static int fp8_gemm_launch(fpb_fp8_matrix *w, const uint8_t *a_bits, const float *a_scale, size_t m,
+                           size_t n_base, size_t n_rows, const int32_t *tile_experts, void *y, int y_dtype,
+                           cudaStream_t s) {
+  if (y_dtype != FPB_F32 && y_dtype != FPB_BF16) return fail(FPB_ERR_INVALID_ARGUMENT, "FP8 GEMM: dtype");
+  const bool blocks = !(w->block_n == 0 && w->block_k == 0);
+  if (blocks && (w->block_n % kF8Tile != 0 || w->block_k % kF8Tile != 0))
+    return fail(FPB_ERR_UNSUPPORTED, "FP8 GEMM: block scales of %dx%d (need multiples of 128)", w->block_n,
+                w->block_k);
+  if (w->cols % 16 != 0) return fail(FPB_ERR_SHAPE, "FP8 GEMM: cols %zu not a multiple of 16", w->cols);
+  if (m == 0 || m > (size_t)65535 * kF8Tile || w->rows > 0x7fffffff)
+    return fail(FPB_ERR_SHAPE, "FP8 GEMM: m = %zu", m);
+  int st = fp8_prepare(w);
+  if (st) return st;
+  CUtensorMap tmap_a;
+  if ((st = encode_rows_u8(&tmap_a, a_bits, m, w->cols, kF8Tile))) return st;
+  auto kernel = blocks ? fp8_gemm_kernel<true> : fp8_gemm_kernel<false>;
+  if ((st = raise_smem_once(kernel, (int)kF8Smem))) return st;
+  Fp8GemmParams p{};
+  p.a_scale = a_scale;
+  p.w_scale = w->scales;
+  p.y = y;
+  p.ldy = (long long)n_rows;
+  p.y_bf16 = y_dtype == FPB_BF16;
+  p.M = (int)m;
+  p.N = (int)n_rows;
+  p.n_base = (int)n_base;
+  p.kb_count = (int)((w->cols + kF8Tile - 1) / kF8Tile);
+  p.bn = w->block_n;
+  p.bk = w->block_k;
+  p.ws_cols = blocks ? (int)(w->cols / w->block_k) : 0;
+  p.error = device_error_ptr();
+  p.tile_experts = tile_experts;
+  p.n_experts = tile_experts ? (int)(w->rows / n_rows) : 0;
+  dim3 grid((unsigned)((n_rows + kF8BN - 1) / kF8BN), (unsigned)((m + kF8Tile - 1) / kF8Tile));
+  kernel<<<grid, kF8Threads, kF8Smem, s>>>(tmap_a, *reinterpret_cast<const CUtensorMap *>(w->tmap), p);
+  FPB_LAUNCH_CHECK("fp8_gemm_kernel");
+  return FPB_OK;
+}
+
+static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+}  // namespace fpb
+
+using namespace fpb;
+
+extern "C" int fpb_fp8_validate(size_t bits_len, const float *scales, size_t scales_len, size_t rows, size_t cols,
+                                size_t block_n, size_t block_k) {
+  size_t n_scales = 0;
+  if (block_n == 0 && block_k == 0 && scales_len != rows)
+    return fail(FPB_ERR_FORMAT, "FP8 row scales must have one value per row");  // weights/fp8.rs:63-65
+  int st = fp8_check_layout(rows, cols, block_n, block_k, &n_scales);
+  if (st) return st;
+  if (scales_len != n_scales) return fail(FPB_ERR_FORMAT, "invalid FP8 scale grid");
+  if (bits_len != rows * cols) return fail(FPB_ERR_FORMAT, "invalid FP8 matrix or scales");
+  if (!scales && n_scales) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_fp8_validate: null scales");
+  return fp8_check_scales_host(scales, n_scales);
+}
+
+extern "C" int fpb_fp8_matrix_create(const uint8_t *bits, const float *scales, size_t rows, size_t cols,
+                                     size_t block_n, size_t block_k, void *stream, fpb_fp8_matrix **out) {
+  if (!bits || !scales || !out) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_fp8_matrix_create: null pointer");
+  *out = nullptr;
+  size_t n_scales = 0;
+  int st = fp8_check_layout(rows, cols, block_n, block_k, &n_scales);
+  if (st) return st;
+  if ((st = fp8_check_scales_host(scales, n_scales))) return st;
+  fpb_fp8_matrix *m = nullptr;
+  if ((st = fp8_alloc(rows, cols, block_n, block_k, n_scales, &m))) return st;
+  cudaStream_t s = as_stream(stream);
+  cudaError_t e = cudaMemcpyAsync(m->bits, bits, rows * cols, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(m->scales, scales, n_scales * sizeof(float), cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) {
+    fpb_fp8_matrix_destroy(m);
+    return cuda_fail(e, "fpb_fp8_matrix_create upload");
+  }
+  *out = m;
+  return FPB_OK;
+}
+
+extern "C" int fpb_fp8_matrix_create_device(const uint8_t *bits, const float *scales, size_t rows, size_t cols,
+                                            size_t block_n, size_t block_k, void *stream, fpb_fp8_matrix **out) {
+  if (!bits || !scales || !out)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_fp8_matrix_create_device: null pointer");
+  *out = nullptr;
+  size_t n_scales = 0;
+  int st = fp8_check_layout(rows, cols, block_n, block_k, &n_scales);
+  if (st) return st;
+  std::vector<float> host(n_scales);
+  cudaStream_t s = as_stream(stream);
+  FPB_CUDA_TRY(cudaMemcpyAsync(host.data(), scales, n_scales * sizeof(float), cudaMemcpyDeviceToHost, s));
+  FPB_CUDA_TRY(cudaStreamSynchronize(s));
+  if ((st = fp8_check_scales_host(host.data(), n_scales))) return st;
+  fpb_fp8_matrix *m = nullptr;
+  if ((st = fp8_alloc(rows, cols, block_n, block_k, n_scales, &m))) return st;
+  cudaError_t e = cudaMemcpyAsync(m->bits, bits, rows * cols, cudaMemcpyDeviceToDevice, s);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(m->scales, scales, n_scales * sizeof(float), cudaMemcpyDeviceToDevice, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) {
+    fpb_fp8_matrix_destroy(m);
+    return cuda_fail(e, "fpb_fp8_matrix_create_device copy");
+  }
+  *out = m;
+  return FPB_OK;
+}
+
+extern "C" int fpb_fp8_matrix_destroy(fpb_fp8_matrix *m) {
+  if (!m) return FPB_OK;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  if (prev != m->device) cudaSetDevice(m->device);
+  cudaFree(m->bits);
+  cudaFree(m->scales);
+  if (prev != m->device) cudaSetDevice(prev);
+  delete m;
+  return FPB_OK;
+}
+
+extern "C" int fpb_fp8_matrix_shape(const fpb_fp8_matrix *m, size_t *rows, size_t *cols, size_t *block_n,
+                                    size_t *block_k) {
+  if (!m) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_fp8_matrix_shape: null matrix");
+  if (rows) *rows = m->rows;
+  if (cols) *cols = m->cols;
+  if (block_n) *block_n = (size_t)m->block_n;
+  if (block_k) *block_k = (size_t)m->block_k;
+  return FPB_OK;
+}
+
+extern "C" int fpb_fp8_matrix_download(const fpb_fp8_matrix *m, uint8_t *bits, float *scales, void *stream) {
+  if (!m || !bits || !scales) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_fp8_matrix_download: null pointer");
+  cudaStream_t s = as_stream(stream);
+  FPB_CUDA_TRY(cudaMemcpyAsync(bits, m->bits, m->rows * m->cols, cudaMemcpyDeviceToHost, s));
+  FPB_CUDA_TRY(cudaMemcpyAsync(scales, m->scales, m->n_scales * sizeof(float), cudaMemcpyDeviceToHost, s));
+  FPB_CUDA_TRY(cudaStreamSynchronize(s));
+  return FPB_OK;
+}
+
+extern "C" int fpb_fp8_quantize(const void *w, int dtype, size_t rows, size_t cols, size_t block_n, size_t block_k,
+                                uint8_t *bits, float *scales, void *stream) {
+  if (!w || !bits || !scales) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_fp8_quantize: null pointer");
+  return fp8_quantize_impl(w, dtype, rows, cols, block_n, block_k, bits, scales, as_stream(stream));
+}
+
+extern "C" size_t fpb_fp8_gemm_workspace_bytes(size_t m, size_t k) { return align256(m * k) + align256(4 * m); }
+
+extern "C" int fpb_fp8_gemm_q(fpb_fp8_matrix *w, size_t row_begin, size_t row_end, const uint8_t *a_bits,
+                              const float *a_scales, size_t m, void *y, int y_dtype, void *stream) {
+  if (!w || !a_bits || !a_scales || !y) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_fp8_gemm_q: null pointer");
+  if (row_end == 0) row_end = w->rows;
+  if (row_begin >= row_end || row_end > w->rows)
+    return fail(FPB_ERR_SHAPE, "fpb_fp8_gemm_q: row range [%zu, %zu) outside %zu rows", row_begin, row_end, w->rows);
+  if (row_begin % kF8Tile != 0)
+    return fail(FPB_ERR_SHAPE, "fpb_fp8_gemm_q: first row %zu not a multiple of 128", row_begin);
+  if (w->block_n && (row_begin % w->block_n || row_end % w->block_n))  // gemm/mod.rs:596-599
+    return fail(FPB_ERR_SHAPE, "fpb_fp8_gemm_q: rows [%zu, %zu) not aligned to block_n %d", row_begin, row_end,
+                w->block_n);
+  return fp8_gemm_launch(w, a_bits, a_scales, m, row_begin, row_end - row_begin, nullptr, y, y_dtype,
+                         as_stream(stream));
+}
+
+extern "C" int fpb_fp8_gemm(fpb_fp8_matrix *w, size_t row_begin, size_t row_end, const void *x, int x_dtype,
+                            size_t m, void *y, int y_dtype, void *workspace, size_t workspace_bytes, void *stream) {
+  if (!w || !x || !y || !workspace) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_fp8_gemm: null pointer");
+  if (workspace_bytes < fpb_fp8_gemm_workspace_bytes(m, w->cols) || (reinterpret_cast<uintptr_t>(workspace) & 255))
+    return fail(FPB_ERR_WORKSPACE, "fpb_fp8_gemm: workspace must be 256-byte aligned and %zu bytes",
+                fpb_fp8_gemm_workspace_bytes(m, w->cols));
+  uint8_t *a_bits = static_cast<uint8_t *>(workspace);
+  float *a_scales = reinterpret_cast<float *>(a_bits + align256(m * w->cols));
+  cudaStream_t s = as_stream(stream);
+  int st = fp8_quantize_impl(x, x_dtype, m, w->cols, 0, 0, a_bits, a_scales, s);
+  if (st) return st;
+  return fpb_fp8_gemm_q(w, row_begin, row_end, a_bits, a_scales, m, y, y_dtype, stream);
+}
+
+extern "C" int fpb_fp8_grouped_gemm_q(fpb_fp8_matrix *w, const uint8_t *a_bits, const float *a_scales,
+                                      size_t padded_rows, const int32_t *tile_experts, size_t rows_per_expert,
+                                      void *y, int y_dtype, void *stream) {
+  if (!w || !a_bits || !a_scales || !tile_experts || !y)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_fp8_grouped_gemm_q: null pointer");
+  if (padded_rows == 0 || padded_rows % kF8Tile)
+    return fail(FPB_ERR_SHAPE, "fpb_fp8_grouped_gemm_q: padded_rows %zu not a positive multiple of 128", padded_rows);
+  if (rows_per_expert == 0 || rows_per_expert % kF8Tile || w->rows % rows_per_expert)
+    return fail(FPB_ERR_SHAPE, "fpb_fp8_grouped_gemm_q: rows_per_expert %zu must be a multiple of 128 dividing %zu",
+                rows_per_expert, w->rows);
+  if (w->block_n && rows_per_expert % w->block_n)  // gemm/mod.rs:675-677
+    return fail(FPB_ERR_SHAPE, "fpb_fp8_grouped_gemm_q: rows_per_expert not a multiple of block_n");
+  return fp8_gemm_launch(w, a_bits, a_scales, padded_rows, 0, rows_per_expert, tile_experts, y, y_dtype,
+                         as_stream(stream));
+}

@@ -30,6 +30,7 @@
 #include "matrix_extras.cuh"
 #include "nvfp4_matrix.cuh"
 #include "sm100.cuh"
+#include "tma_host.cuh"
 
 namespace fpb {
 

@@ -204,6 +204,54 @@ int fpb_nvfp4_grouped_gemm_q(fpb_nvfp4_matrix *w, const uint8_t *a_packed, const
  * that gave up); synchronises the device; reset != 0 clears it. */
 int fpb_device_error(int *out, int reset);
 
+/* ---- FP8 E4M3 weights and the prefill FP8 GEMM (tcgen05 kind::f8f6f4) ----
+ * Replaces HostFp8Matrix / Fp8Matrix (weights/fp8.rs:8-132) and fp8_gemm /
+ * fp8_gemm_view / fp8_grouped_gemm_view (gemm/mod.rs:67-206, 417-697).
+ * bits: e4m3 [rows, cols] row-major; scales f32: a [rows/block_n, cols/block_k]
+ * grid (Fp8Scaling::Blocks), or one per row when block_n = block_k = 0
+ * (Fp8Scaling::Rows).  The reference keeps f32 activations (bf16 hi/lo MMAs);
+ * this path quantizes them to e4m3 with one f32 scale per token
+ * (amax/448), the W8A8 setting of the task's config 1:
+ *   y[m, n] = a_s[m] * sum_kb w_s[n/block_n, kb] * sum_{k in kb} a[m,k] w[n,k]
+ * (rows mode: a_s[m] * w_s[n] * sum_k a[m,k] w[n,k]).  The GEMM needs block
+ * sizes that are multiples of 128 (FPB_ERR_UNSUPPORTED otherwise). */
+typedef struct fpb_fp8_matrix fpb_fp8_matrix;
+/* HostFp8Matrix::from_parts / with_row_scales validation (weights/fp8.rs:30-99):
+ * FPB_ERR_FORMAT with the reference's messages. */
+int fpb_fp8_validate(size_t bits_len, const float *scales, size_t scales_len, size_t rows, size_t cols,
+                     size_t block_n, size_t block_k);
+/* HostFp8Matrix::upload (weights/fp8.rs:114-131) from host buffers. */
+int fpb_fp8_matrix_create(const uint8_t *bits, const float *scales, size_t rows, size_t cols,
+                          size_t block_n, size_t block_k, void *stream, fpb_fp8_matrix **out);
+/* Same from device buffers (copied; the scales are checked finite). */
+int fpb_fp8_matrix_create_device(const uint8_t *bits, const float *scales, size_t rows, size_t cols,
+                                 size_t block_n, size_t block_k, void *stream, fpb_fp8_matrix **out);
+int fpb_fp8_matrix_destroy(fpb_fp8_matrix *m);
+int fpb_fp8_matrix_shape(const fpb_fp8_matrix *m, size_t *rows, size_t *cols, size_t *block_n,
+                         size_t *block_k);
+int fpb_fp8_matrix_download(const fpb_fp8_matrix *m, uint8_t *bits, float *scales, void *stream);
+/* Quantizes w [rows, cols] (f32 or bf16, device) to e4m3: scale = amax/448
+ * per block_n x block_k block (block_n = block_k = 0: per row, which is also
+ * the per-token activation rule), bits = RN_e4m3_satfinite(w / scale). */
+int fpb_fp8_quantize(const void *w, int dtype, size_t rows, size_t cols, size_t block_n, size_t block_k,
+                     uint8_t *bits, float *scales, void *stream);
+/* Workspace of fpb_fp8_gemm (quantized activations and their scales). */
+size_t fpb_fp8_gemm_workspace_bytes(size_t m, size_t k);
+/* GEMM on quantized activations a_bits [m, K] with per-token a_scales [m];
+ * weight rows [row_begin, row_end) (row_end 0 = all), row_begin a multiple of
+ * 128 and of block_n; y [m, row_end - row_begin]. */
+int fpb_fp8_gemm_q(fpb_fp8_matrix *w, size_t row_begin, size_t row_end, const uint8_t *a_bits,
+                   const float *a_scales, size_t m, void *y, int y_dtype, void *stream);
+/* Quantize x [m, K] (f32 or bf16) into `workspace` and run the GEMM. */
+int fpb_fp8_gemm(fpb_fp8_matrix *w, size_t row_begin, size_t row_end, const void *x, int x_dtype, size_t m,
+                 void *y, int y_dtype, void *workspace, size_t workspace_bytes, void *stream);
+/* Grouped (MoE) GEMM, as fpb_nvfp4_grouped_gemm_q: row tile t (128 rows) of
+ * a_bits [padded_rows, K] uses expert tile_experts[t]'s rows
+ * [e*rows_per_expert, (e+1)*rows_per_expert); device error 306 on a bad id. */
+int fpb_fp8_grouped_gemm_q(fpb_fp8_matrix *w, const uint8_t *a_bits, const float *a_scales,
+                           size_t padded_rows, const int32_t *tile_experts, size_t rows_per_expert,
+                           void *y, int y_dtype, void *stream);
+
 /* ---- MoE host bookkeeping (no GPU needed) -------------------------------- */
 /* MoeDims::new (moe.rs:172-225): FPB_ERR_SHAPE on invalid dimensions. */
 int fpb_moe_dims_validate(size_t hidden, size_t intermediate, size_t shared_intermediate,

@@ -87,6 +87,24 @@ void orc_nvfp4_expert_gemv_f32(const uint8_t *packed, const uint8_t *scales,
                                size_t slots, size_t rows_per_expert, size_t input_stride,
                                const float *x, float *y);
 
+/* ---- FP8 E4M3 (oracle/fp8.c) --------------------------------------------
+ * Formats of kernels src/weights/fp8.rs:8-27.  block_n = block_k = 0 selects
+ * per-row scales (Fp8Scaling::Rows), otherwise a [rows/block_n, cols/block_k]
+ * grid.  Quantize (no reference counterpart; task config 1): scale =
+ * amax/448 per block or row, bits = RN_e4m3_satfinite(w / scale), 0 when the
+ * scale is 0.  Per-token activation scales are the row mode.  Returns 0, or
+ * -1 on a bad shape or a non-finite input. */
+int orc_fp8_quantize(const float *w, size_t rows, size_t cols, size_t block_n, size_t block_k,
+                     uint8_t *bits, float *scales);
+void orc_fp8_dequantize(const uint8_t *bits, const float *scales, size_t rows, size_t cols,
+                        size_t block_n, size_t block_k, float *out);
+/* f64 product of the dequantized operands (kernels tests/fp8_oracle.rs:139-170
+ * with tests/common/oracle.rs): a [m, k] with per-row scales, w [n, k];
+ * expected = sum (e4m3(a) a_s)(e4m3(w) w_s), magnitude = sum |.||.|. */
+void orc_fp8_gemm_f64(const uint8_t *a_bits, const float *a_scales, size_t m, const uint8_t *w_bits,
+                      const float *w_scales, size_t n, size_t k, size_t block_n, size_t block_k,
+                      double *expected, double *magnitude);
+
 /* ---- error model (kernels tests/common/check.rs:19-38) ------------------- */
 double orc_gamma_tilde(size_t n);
 double orc_inner_product_excess(const float *actual, const double *expected,

@@ -47,6 +47,9 @@ for name, res, args in [
     ("orc_nvfp4_gemv_f32", None, [_vp, _vp, _vp, _sz, _sz, _vp, _sz, _vp]),
     ("orc_nvfp4_gemv_f64", None, [_vp, _vp, _vp, _sz, _sz, _vp, _sz, _vp, _vp]),
     ("orc_nvfp4_expert_gemv_f32", None, [_vp, _vp, _vp, _sz, _vp, _sz, _sz, _sz, _vp, _vp]),
+    ("orc_fp8_quantize", C.c_int, [_vp, _sz, _sz, _sz, _sz, _vp, _vp]),
+    ("orc_fp8_dequantize", None, [_vp, _vp, _sz, _sz, _sz, _sz, _vp]),
+    ("orc_fp8_gemm_f64", None, [_vp, _vp, _sz, _vp, _vp, _sz, _sz, _sz, _sz, _vp, _vp]),
     ("orc_gamma_tilde", C.c_double, [_sz]),
     ("orc_inner_product_excess", C.c_double, [_vp, _vp, _vp, _sz, _sz]),
     ("orc_num_threads", C.c_int, []),
@@ -147,6 +150,40 @@ def nvfp4_expert_gemv_f32(packed, scales, row_globals, cols: int, ids, rows_per_
 
 
 # ---- error model ----------------------------------------------------------------------
+# ---- FP8 E4M3 --------------------------------------------------------------------------
+def fp8_quantize(w: np.ndarray, block_n: int = 0, block_k: int = 0):
+    """bits u8 [rows, cols] and f32 scales ([rows] when block_n = block_k = 0,
+    else [rows/block_n, cols/block_k])."""
+    w = f32(w)
+    rows, cols = w.shape
+    bits = np.empty((rows, cols), np.uint8)
+    n_scales = rows if block_n == 0 and block_k == 0 else (rows // block_n) * (cols // block_k)
+    scales = np.empty(n_scales, np.float32)
+    if lib.orc_fp8_quantize(_p(w), rows, cols, block_n, block_k, _p(bits), _p(scales)) != 0:
+        raise ValueError("orc_fp8_quantize: invalid input")
+    return bits, scales
+
+
+def fp8_dequantize(bits, scales, block_n: int = 0, block_k: int = 0) -> np.ndarray:
+    bits = np.ascontiguousarray(bits, np.uint8)
+    rows, cols = bits.shape
+    out = np.empty((rows, cols), np.float32)
+    lib.orc_fp8_dequantize(_p(bits), _p(f32(scales)), rows, cols, block_n, block_k, _p(out))
+    return out
+
+
+def fp8_gemm_f64(a_bits, a_scales, w_bits, w_scales, block_n: int = 0, block_k: int = 0):
+    a_bits = np.ascontiguousarray(a_bits, np.uint8)
+    w_bits = np.ascontiguousarray(w_bits, np.uint8)
+    m, k = a_bits.shape
+    n = w_bits.shape[0]
+    e = np.empty((m, n), np.float64)
+    mag = np.empty((m, n), np.float64)
+    lib.orc_fp8_gemm_f64(_p(a_bits), _p(f32(a_scales)), m, _p(w_bits), _p(f32(w_scales)), n, k, block_n, block_k,
+                         _p(e), _p(mag))
+    return e, mag
+
+
 def gamma_tilde(n: int) -> float:
     return lib.orc_gamma_tilde(n)
 

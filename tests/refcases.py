@@ -68,3 +68,46 @@ def _assemble(codes, scales, globals_, rows, cols):
     packed = pack_codes(codes)
     row_globals = np.repeat(np.array(globals_, np.float32), PART_ROWS)
     return packed, scales.astype(np.uint8), row_globals, rows, cols
+
+
+# ---- FP8 (crates/firepit-kernels/tests/fp8_oracle.rs) ----------------------------------------
+FP8_VALUES = [(0xB8, -1.0), (0x38, 1.0), (0x30, 0.5), (0xC0, -2.0), (0x40, 2.0), (0x39, 1.125), (0x3B, 1.375),
+              (0x35, 0.8125)]                       # fp8_oracle.rs:122-131
+FP8_SCALES = [0.8125, 1.203125, 2.25]               # fp8_oracle.rs:132
+
+
+def _wrapping_add_mod(i: np.ndarray, seed: int, mod: int) -> np.ndarray:
+    """((i + seed) wrapping on u64) % mod."""
+    return ((i.astype(np.uint64) + np.uint64(seed & MASK64)) % np.uint64(mod)).astype(np.int64)
+
+
+def fp8_kernels_case(n_blocks: int, k_blocks: int, seed: int):
+    """fp8_gemv_and_gemm_match_dequantized_f64_oracle (fp8_oracle.rs:119-170):
+    bits [rows, cols], 128x128 block scales, the input row, rows, cols."""
+    rows, cols = (n_blocks + 1) * 128, (k_blocks + 1) * 128
+    i = np.arange(rows * cols)
+    table = np.array([b for b, _ in FP8_VALUES], np.uint8)
+    bits = table[(_mix(i, 17, seed) % np.uint64(len(FP8_VALUES))).astype(np.int64)].reshape(rows, cols)
+    nsc = (rows // 128) * (cols // 128)
+    scales = np.array(FP8_SCALES, np.float32)[_wrapping_add_mod(np.arange(nsc), seed, len(FP8_SCALES))]
+    x = ((_mix(np.arange(cols), 13, seed) % np.uint64(41)).astype(np.float32) / np.float32(37.0)
+         - np.float32(0.5)).astype(np.float32)
+    return bits, scales, x, rows, cols
+
+
+FP8_EXTREME_CASES = [  # fp8_oracle.rs:251-268: (scale, encodings, amplitude)
+    (float(np.uint32(0x0001 << 16).view(np.float32)), [0x7E, 0xFE, 0x7E, 0xFE], 2.0 ** 20),
+    (float(np.uint32(0x7F7F << 16).view(np.float32)), [0x01, 0x81, 0x01, 0x81], 0.5),
+    (1.0 / 128.0, [0x7E, 0xFE, 0x01, 0x81], 2.0 ** 20),
+]
+
+
+def fp8_extreme_case(case: int, seed: int):
+    """fp8_extreme_finite_values_match_f64_oracle (fp8_oracle.rs:247-300):
+    rows 128, cols 256, one scale per 128x128 block."""
+    scale, enc, amp = FP8_EXTREME_CASES[case]
+    rows, cols = 128, 256
+    i = np.arange(rows * cols)
+    bits = np.array(enc, np.uint8)[(_mix(i, 7, seed) % np.uint64(4)).astype(np.int64)].reshape(rows, cols)
+    x = np.where(_wrapping_add_mod(np.arange(cols), seed, 3) == 0, -amp, amp).astype(np.float32)
+    return bits, np.full(2, scale, np.float32), x, rows, cols

@@ -9,7 +9,9 @@ from . import _native
 from ._native import FpbError, launch_count
 from .gemv import (DEFAULT_GEMV_TILE, ExpertGemvView, Gemv, GemvTile, ShapeError, expert_gemv_weight_view,
                    fp8_tile, gemv, row_scaled_tile)
-from .moe import ExpertSelection, ExpertSelectionError, MoeDimensionError, MoeDims, PrefillLayout
+from .moe import (ExpertSelection, ExpertSelectionError, MoeDimensionError, MoeDims, PrefillLayout, PrefillPlan,
+                  combine, combine_add_norm_prefill, combine_add_norm_view, combine_prefill, gather_prefill_view,
+                  gather_quantize, swiglu, swiglu_quantize, topk_device)
 from .sink import Async, Dry, Eager, Graph, Traced
 from .synth import synth_normal
 from .weights import (NVFP4_GROUP, Q8_BLOCK, FormatError, HostNvfp4Matrix, Nvfp4Matrix, current_stream_handle,

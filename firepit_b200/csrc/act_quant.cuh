@@ -1,0 +1,75 @@
+// NVFP4 activation encoding shared by the GEMM's quantizer and the MoE
+// gather / SwiGLU quantizers: the tensor cores' tiled scale-factor layout and
+// the per-16-column group encode (same arithmetic as fpb_nvfp4_quantize).
+//
+// Tiled factor layout: for each 128-row block and each 64-column block, 512
+// bytes holding the factor of row r, 16-column group s at byte
+// (r % 32) * 16 + (r / 32) * 4 + s; K blocks are padded to a multiple of four
+// (256 columns) with zero factors.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+
+#include "common.cuh"
+#include "nvfp4_matrix.cuh"
+
+namespace fpb {
+
+constexpr int kSfChunk = 512;  // bytes per (128 rows, 64 columns)
+
+__host__ __device__ inline size_t sf_tiled_bytes(size_t rows, size_t cols) {
+  size_t rb = (rows + 127) / 128, kb = (cols + 255) / 256;
+  return rb * kb * 4 * kSfChunk;
+}
+
+// Byte offset of the factor of (row, group) in the tiled layout.
+__host__ __device__ inline size_t sf_tiled_offset(size_t row, size_t group, size_t cols) {
+  size_t kb64_per_rb = (cols + 255) / 256 * 4;
+  size_t rb = row / 128, r = row % 128, kb64 = group / 4, s = group % 4;
+  return (rb * kb64_per_rb + kb64) * kSfChunk + (r % 32) * 16 + (r / 32) * 4 + s;
+}
+
+template <typename T>
+__device__ __forceinline__ float act_load(const T *p, size_t i);
+template <>
+__device__ __forceinline__ float act_load<float>(const float *p, size_t i) { return p[i]; }
+template <>
+__device__ __forceinline__ float act_load<uint16_t>(const uint16_t *p, size_t i) {
+  return bf16_bits_to_f32(p[i]);
+}
+
+// atomicMax of |x| bits over x[0, n) (amax_bits zeroed by the caller).
+template <typename T>
+__global__ void act_amax_kernel(const T *x, size_t n, uint32_t *amax_bits) {
+  uint32_t m = 0;
+  size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+    m = max(m, __float_as_uint(act_load(x, i)) & 0x7fffffffu);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) atomicMax(amax_bits, m);
+}
+
+// One 16-value group: s = RN_e4m3((bmax / 6) / global), codes =
+// RN_e2m1(v / (e4m3(s) * global)); writes 8 code bytes and the factor.
+__device__ __forceinline__ void encode_group16(const float v[16], float global, uint8_t *packed_dst,
+                                               uint8_t *sf_dst) {
+  float bmax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) bmax = fmaxf(bmax, fabsf(v[i]));
+  uint8_t s = 0;
+  if (global > 0.0f) s = f32_to_e4m3(__fdiv_rn(__fdiv_rn(bmax, 6.0f), global));
+  const float denom = __fmul_rn(e4m3_to_f32(s), global);
+  uint32_t lo = 0, hi = 0;
+  if (denom > 0.0f) {
+    float q[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) q[i] = __fdiv_rn(v[i], denom);
+    lo = f32x8_to_e2m1x8(q);
+    hi = f32x8_to_e2m1x8(q + 8);
+  }
+  *reinterpret_cast<uint2 *>(packed_dst) = make_uint2(lo, hi);
+  *sf_dst = s;
+}
+
+}  // namespace fpb

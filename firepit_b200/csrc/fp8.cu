@@ -150,6 +150,7 @@ __global__ void __launch_bounds__(kF8Threads, 1)
   int n_base = p.n_base;
   if (p.tile_experts) {
     const int e = p.tile_experts[m_tile];
+    if (e == -1) return;  // a row tile past the end of a device-built layout
     if (e < 0 || e >= p.n_experts) {
       if (threadIdx.x == 0 && p.error) atomicCAS(p.error, 0, 306);
       return;

@@ -26,6 +26,7 @@
 #include <mutex>
 #include <vector>
 
+#include "act_quant.cuh"
 #include "common.cuh"
 #include "matrix_extras.cuh"
 #include "nvfp4_matrix.cuh"
@@ -38,19 +39,6 @@ __device__ int g_device_error;  // first failing kernel's error code (0 = none)
 
 constexpr int kBM = 128, kBN = 128, kBKBytes = 128;  // K block = 256 fp4 columns
 constexpr int kStages = 4;
-constexpr int kSfChunk = 512;  // bytes per (128 rows, 64 columns)
-
-__host__ __device__ inline size_t sf_tiled_bytes(size_t rows, size_t cols) {
-  size_t rb = (rows + 127) / 128, kb = (cols + 255) / 256;
-  return rb * kb * 4 * kSfChunk;
-}
-
-// Byte offset of the factor of (row, group) in the tiled layout.
-__host__ __device__ inline size_t sf_tiled_offset(size_t row, size_t group, size_t cols) {
-  size_t kb64_per_rb = (cols + 255) / 256 * 4;
-  size_t rb = row / 128, r = row % 128, kb64 = group / 4, s = group % 4;
-  return (rb * kb64_per_rb + kb64) * kSfChunk + (r % 32) * 16 + (r / 32) * 4 + s;
-}
 
 // Row-major e4m3 scales [rows, cols/16] -> tiled, sign cleared (UE4M3).
 // Padding entries are written as zero.  One thread per output byte.
@@ -91,26 +79,6 @@ __global__ void any_negative_kernel(const uint8_t *scales, size_t n, int *flag) 
 }
 
 // ---- activation quantize: amax, then codes + tiled factors --------------------------
-template <typename T>
-__device__ __forceinline__ float act_load(const T *p, size_t i);
-template <>
-__device__ __forceinline__ float act_load<float>(const float *p, size_t i) { return p[i]; }
-template <>
-__device__ __forceinline__ float act_load<uint16_t>(const uint16_t *p, size_t i) {
-  return bf16_bits_to_f32(p[i]);
-}
-
-template <typename T>
-__global__ void act_amax_kernel(const T *x, size_t n, uint32_t *amax_bits) {
-  uint32_t m = 0;
-  size_t stride = (size_t)gridDim.x * blockDim.x;
-  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
-    m = max(m, __float_as_uint(act_load(x, i)) & 0x7fffffffu);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
-  if ((threadIdx.x & 31) == 0) atomicMax(amax_bits, m);
-}
-
 // One thread per 16-column group: same arithmetic as fpb_nvfp4_quantize, the
 // factor written to the tiled layout and the global to *global_out.
 template <typename T>
@@ -126,22 +94,7 @@ __global__ void act_encode_kernel(const T *x, size_t rows, size_t cols, const ui
     const T *src = x + r * cols + g * kNvfp4Group;
 #pragma unroll
     for (int i = 0; i < kNvfp4Group; ++i) v[i] = act_load(src, i);
-    float bmax = 0.0f;
-#pragma unroll
-    for (int i = 0; i < kNvfp4Group; ++i) bmax = fmaxf(bmax, fabsf(v[i]));
-    uint8_t s = 0;
-    if (global > 0.0f) s = f32_to_e4m3(__fdiv_rn(__fdiv_rn(bmax, 6.0f), global));
-    float denom = __fmul_rn(e4m3_to_f32(s), global);
-    uint32_t lo = 0, hi = 0;
-    if (denom > 0.0f) {
-      float q[kNvfp4Group];
-#pragma unroll
-      for (int i = 0; i < kNvfp4Group; ++i) q[i] = __fdiv_rn(v[i], denom);
-      lo = f32x8_to_e2m1x8(q);
-      hi = f32x8_to_e2m1x8(q + 8);
-    }
-    *reinterpret_cast<uint2 *>(packed + r * (cols / 2) + g * (kNvfp4Group / 2)) = make_uint2(lo, hi);
-    sf_tiled[sf_tiled_offset(r, g, cols)] = s;
+    encode_group16(v, global, packed + r * (cols / 2) + g * (kNvfp4Group / 2), sf_tiled + sf_tiled_offset(r, g, cols));
   }
 }
 
@@ -201,6 +154,7 @@ __global__ void __launch_bounds__(192, 1)
   int n_base = p.n_base;
   if (p.tile_experts) {
     const int e = p.tile_experts[m_tile];
+    if (e == -1) return;  // a row tile past the end of a device-built layout
     if (e < 0 || e >= p.n_experts) {  // a malformed layout: leave this tile, report it
       if (threadIdx.x == 0) atomicCAS(p.error, 0, 106);
       return;

@@ -1,0 +1,561 @@
+// MoE routing, layout, gather, SwiGLU and combine on the device
+// (crates/firepit-kernels/src/moe.rs:15-147, 397-859; src/swiglu.rs).
+//
+// The reference computes the router's top-k on the GPU, downloads the ids,
+// builds the expert-sorted layout on the host (a counting sort) and uploads it
+// again (PrefillPlan::top_k, moe.rs:545-585).  Here every step stays on the
+// device, so a prefill MoE is one stream of launches with no host round trip:
+//   top-k (one warp per token) -> layout (one CTA: stable counting sort) ->
+//   gather + NVFP4 quantize -> grouped gate/up GEMM -> SwiGLU + NVFP4
+//   quantize -> grouped down GEMM -> combine (+ residual + RMSNorm).
+// The layout is written into buffers sized for the largest possible padding
+// (PrefillLayout::max_padded_rows); row tiles past the actual end carry
+// expert id -1, which the grouped GEMMs skip.
+#include <algorithm>
+#include <mutex>
+#include <vector>
+
+#include "act_quant.cuh"
+#include "common.cuh"
+#include "nvfp4_matrix.cuh"
+
+namespace fpb {
+
+// ---- router top-k (moe.rs:15-68) -------------------------------------------------------
+// One warp per token; lane l holds logits l, l + 32, ...  Each of the k
+// rounds takes the largest remaining logit, the lowest expert id among equal
+// ones; scores exp(l - max) are normalised by their sum over the k winners
+// (softmax restricted to the top k).  With a shared-expert gate, slot k is
+// expert `experts` with weight sigmoid(gate).  Slots past that are id 0,
+// weight 0.
+template <int PER_LANE>
+__global__ void moe_topk_kernel(const float *logits, long long ld, const float *shared_gate, int tokens,
+                                int experts, int k, int width, int32_t *ids, float *weights) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= tokens) return;
+  const float *row = logits + (long long)warp * ld;
+  float v[PER_LANE];
+  float m = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < PER_LANE; ++i) {
+    const int p = lane + 32 * i;
+    v[i] = p < experts ? row[p] : -INFINITY;
+    m = fmaxf(m, v[i]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  const float origin = m;
+  float total = 0.0f, my_score = 0.0f;
+  int my_id = 0;
+  for (int rank = 0; rank < k; ++rank) {
+    float bv = -INFINITY;
+    int bp = experts - 1;
+#pragma unroll
+    for (int i = 0; i < PER_LANE; ++i) {
+      const int p = lane + 32 * i;
+      if (p < experts && (v[i] > bv || (v[i] == bv && p < bp))) {
+        bv = v[i];
+        bp = p;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int op = __shfl_xor_sync(0xffffffffu, bp, o);
+      if (ov > bv || (ov == bv && op < bp)) {
+        bv = ov;
+        bp = op;
+      }
+    }
+    const float score = expf(bv - origin);
+    total = total + score;
+    if (lane == rank) {
+      my_score = score;
+      my_id = bp;
+    }
+    if ((bp & 31) == lane) {
+#pragma unroll
+      for (int i = 0; i < PER_LANE; ++i)
+        if (lane + 32 * i == bp) v[i] = -INFINITY;
+    }
+  }
+  if (lane < width) {
+    int id = 0;
+    float w = 0.0f;
+    if (lane < k) {
+      id = my_id;
+      w = my_score / total;
+    } else if (lane == k && shared_gate) {
+      id = experts;
+      const float g = shared_gate[warp];
+      w = 1.0f / (1.0f + expf(g * -1.0f));
+    }
+    ids[(long long)warp * width + lane] = id;
+    weights[(long long)warp * width + lane] = w;
+  }
+}
+
+// ---- layout: stable counting sort (moe.rs:452-516) -------------------------------------
+// One CTA of 32 warps.  Warp w owns a contiguous segment of the flattened
+// (token, slot) entries; per-warp counts per expert in shared memory turn into
+// each warp's first row per expert, so that rows keep the entries' order
+// within every expert (the reference's stable sort).
+constexpr int kLayoutWarps = 32;
+
+__global__ void __launch_bounds__(kLayoutWarps * 32, 1)
+    moe_layout_kernel(const int32_t *ids, int tokens, int width, int kk, int experts, int tile_rows, int cap,
+                      int32_t *token_rows, int32_t *tile_experts, int32_t *inverse, int64_t *ranges,
+                      int32_t *padded_out, int *error) {
+  extern __shared__ int smem_i[];
+  int *counts = smem_i;                             // [kLayoutWarps][experts]
+  int *offsets = counts + kLayoutWarps * experts;  // [experts + 1]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int n = tokens * kk;
+  const int seg = (n + kLayoutWarps - 1) / kLayoutWarps;
+  const int e_lo = min(n, warp * seg), e_hi = min(n, e_lo + seg);
+
+  for (int i = tid; i < cap; i += blockDim.x) token_rows[i] = -1;
+  for (int i = tid; i < cap / tile_rows; i += blockDim.x) tile_experts[i] = -1;
+  for (int i = tid; i < tokens * width; i += blockDim.x) inverse[i] = 0;
+  for (int i = tid; i < kLayoutWarps * experts; i += blockDim.x) counts[i] = 0;
+  __syncthreads();
+
+  // per-warp counts
+  for (int b = e_lo; b < e_hi; b += 32) {
+    const int e = b + lane;
+    int id = -1;
+    if (e < e_hi) {
+      id = ids[(long long)(e / kk) * width + e % kk];
+      if (id < 0 || id >= experts) {
+        if (error) atomicCAS(error, 0, 401);
+        id = -1;
+      }
+    }
+    const unsigned grp = __match_any_sync(0xffffffffu, id);
+    if (id >= 0 && lane == __ffs(grp) - 1) counts[warp * experts + id] += __popc(grp);
+    __syncwarp();
+  }
+  __syncthreads();
+
+  // per expert: total, then each warp's exclusive prefix within the expert
+  for (int x = tid; x < experts; x += blockDim.x) {
+    int run = 0;
+    for (int w = 0; w < kLayoutWarps; ++w) {
+      const int c = counts[w * experts + x];
+      counts[w * experts + x] = run;
+      run += c;
+    }
+    offsets[x] = run;  // the expert's total for now
+  }
+  __syncthreads();
+  // exclusive scan over experts of the padded sizes (warp 0, 32 at a time)
+  if (warp == 0) {
+    int carry = 0;
+    for (int base = 0; base < experts; base += 32) {
+      const int x = base + lane;
+      const int total = x < experts ? offsets[x] : 0;
+      const int padded = (total + tile_rows - 1) / tile_rows * tile_rows;
+      int incl = padded;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+      }
+      if (x < experts) {
+        ranges[2 * x] = carry + incl - padded;
+        ranges[2 * x + 1] = total;
+      }
+      carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) {
+      *padded_out = carry;
+      if (carry > cap && error) atomicCAS(error, 0, 402);
+    }
+  }
+  __syncthreads();
+  for (int x = tid; x < experts; x += blockDim.x) offsets[x] = (int)ranges[2 * x];
+  __syncthreads();
+
+  // rows: each warp walks its segment again, in order
+  for (int b = e_lo; b < e_hi; b += 32) {
+    const int e = b + lane;
+    int id = -1;
+    if (e < e_hi) {
+      id = ids[(long long)(e / kk) * width + e % kk];
+      if (id < 0 || id >= experts) id = -1;
+    }
+    const unsigned grp = __match_any_sync(0xffffffffu, id);
+    const int rank = __popc(grp & ((1u << lane) - 1));
+    int pos = -1;
+    if (id >= 0) pos = offsets[id] + counts[warp * experts + id] + rank;
+    __syncwarp();
+    if (id >= 0 && lane == __ffs(grp) - 1) counts[warp * experts + id] += __popc(grp);
+    if (id >= 0 && pos < cap) {
+      token_rows[pos] = e / kk;
+      inverse[(long long)(e / kk) * width + e % kk] = pos;
+    }
+    __syncwarp();
+  }
+  // tiles
+  for (int x = tid; x < experts; x += blockDim.x) {
+    const int start = (int)ranges[2 * x], count = (int)ranges[2 * x + 1];
+    const int padded = (count + tile_rows - 1) / tile_rows * tile_rows;
+    for (int t = start / tile_rows; t < (start + padded) / tile_rows && t < cap / tile_rows; ++t)
+      tile_experts[t] = x;
+  }
+}
+
+// ---- row loaders for the NVFP4 activation encode ----------------------------------------
+// Gathered rows (moe.rs:71-89): sorted row r is token token_rows[r], or zeros.
+template <typename T>
+struct GatherRows {
+  const T *x;
+  const int32_t *token_rows;
+  size_t cols;
+  int tokens;
+  __device__ __forceinline__ void load16(size_t r, size_t g, float v[16]) const {
+    const int t = token_rows[r];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = 0.0f;
+    if (t < 0 || t >= tokens) return;  // padding (or an id outside x)
+    const T *src = x + (size_t)t * cols + g * 16;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = act_load(src, i);
+  }
+};
+
+// SwiGLU rows (swiglu.rs:16): gate = first `cols` columns, up = next `cols`.
+__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + expf(g * -1.0f)) * u; }
+
+template <typename T>
+struct SwigluRows {
+  const T *gu;
+  size_t cols;  // intermediate size
+  __device__ __forceinline__ void load16(size_t r, size_t g, float v[16]) const {
+    const T *gate = gu + r * 2 * cols + g * 16;
+    const T *up = gate + cols;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = silu_mul(act_load(gate, i), act_load(up, i));
+  }
+};
+
+template <class Rows>
+__global__ void rows_amax_kernel(Rows rows_src, size_t rows, size_t cols, uint32_t *amax_bits) {
+  const size_t gpr = cols / 16, n = rows * gpr;
+  uint32_t m = 0;
+  size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t gi = (size_t)blockIdx.x * blockDim.x + threadIdx.x; gi < n; gi += stride) {
+    float v[16];
+    rows_src.load16(gi / gpr, gi % gpr, v);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) m = max(m, __float_as_uint(v[i]) & 0x7fffffffu);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) atomicMax(amax_bits, m);
+}
+
+template <class Rows>
+__global__ void rows_encode_kernel(Rows rows_src, size_t rows, size_t cols, const uint32_t *amax_bits,
+                                   uint8_t *packed, uint8_t *sf_tiled, float *global_out) {
+  const float global = __fdiv_rn(__uint_as_float(*amax_bits), 2688.0f);
+  if (blockIdx.x == 0 && threadIdx.x == 0) *global_out = global;
+  const size_t gpr = cols / 16, n = rows * gpr;
+  size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t gi = (size_t)blockIdx.x * blockDim.x + threadIdx.x; gi < n; gi += stride) {
+    const size_t r = gi / gpr, g = gi % gpr;
+    float v[16];
+    rows_src.load16(r, g, v);
+    encode_group16(v, global, packed + r * (cols / 2) + g * 8, sf_tiled + sf_tiled_offset(r, g, cols));
+  }
+}
+
+// Plain gather (gather_prefill_view, moe.rs:71-89, 673-733): f32 or bf16 out.
+template <typename T, typename O>
+__global__ void gather_rows_kernel(const T *x, int tokens, const int32_t *token_rows, size_t rows, size_t cols,
+                                   O *out) {
+  size_t n = rows * cols, stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const size_t r = i / cols, c = i % cols;
+    const int t = token_rows[r];
+    const float v = (t < 0 || t >= tokens) ? 0.0f : act_load(x, (size_t)t * cols + c);
+    if constexpr (sizeof(O) == 4)
+      out[i] = v;
+    else
+      out[i] = __float2bfloat16_rn(v);
+  }
+}
+
+template <typename T, typename O>
+__global__ void swiglu_kernel(const T *gu, size_t rows, size_t cols, O *out) {
+  size_t n = rows * cols, stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const size_t r = i / cols, c = i % cols;
+    const float v = silu_mul(act_load(gu, r * 2 * cols + c), act_load(gu, r * 2 * cols + cols + c));
+    if constexpr (sizeof(O) == 4)
+      out[i] = v;
+    else
+      out[i] = __float2bfloat16_rn(v);
+  }
+}
+
+// ---- combine (moe.rs:91-147) -------------------------------------------------------------
+// One CTA per token: sum over slots (in slot order) of weight * routed row;
+// with a residual, out = residual + sum and normed = out * rsqrt(mean(out^2) +
+// eps) * gamma (combine_add_norm_kernel).
+template <typename R, typename O>
+__global__ void combine_kernel(const R *routed, int routed_rows, size_t cols, const int32_t *inverse,
+                               const float *weights, int width, int slots, const float *residual, const float *gamma,
+                               float inv_h, float eps, O *out, float *normed) {
+  extern __shared__ float red[];
+  const int t = blockIdx.x;
+  float ss = 0.0f;
+  for (size_t c = threadIdx.x; c < cols; c += blockDim.x) {
+    float sum = 0.0f;
+    for (int s = 0; s < slots; ++s) {
+      const int row = inverse[(size_t)t * width + s];
+      if (row < 0 || row >= routed_rows) continue;  // a slot outside routed adds nothing
+      sum = sum + act_load(routed, (size_t)row * cols + c) * weights[(size_t)t * width + s];
+    }
+    if (residual) {
+      sum = residual[(size_t)t * cols + c] + sum;
+      ss = fmaf(sum, sum, ss);
+    }
+    if constexpr (sizeof(O) == 4)
+      out[(size_t)t * cols + c] = sum;
+    else
+      out[(size_t)t * cols + c] = __float2bfloat16_rn(sum);
+  }
+  if (!residual) return;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float scale = rsqrtf(red[0] * inv_h + eps);
+  for (size_t c = threadIdx.x; c < cols; c += blockDim.x) {
+    float x;
+    if constexpr (sizeof(O) == 4)
+      x = out[(size_t)t * cols + c];
+    else
+      x = __bfloat162float(out[(size_t)t * cols + c]);
+    normed[(size_t)t * cols + c] = x * scale * gamma[c];
+  }
+}
+
+static unsigned stride_grid(size_t n) {
+  size_t g = (n + 255) / 256, cap = (size_t)sm_count() * 8;
+  return (unsigned)std::max<size_t>(1, std::min(g, cap));
+}
+
+}  // namespace fpb
+
+// ---- host side -------------------------------------------------------------------------
+using namespace fpb;
+
+namespace {
+template <typename F>
+int with_dtype(int dtype, F &&f) {
+  if (dtype == FPB_F32) return f(static_cast<const float *>(nullptr));
+  if (dtype == FPB_BF16) return f(static_cast<const uint16_t *>(nullptr));
+  return fail(FPB_ERR_INVALID_ARGUMENT, "dtype %d", dtype);
+}
+}  // namespace
+
+extern "C" int fpb_moe_topk(const float *logits, size_t ld, const float *shared_gate, size_t tokens, size_t experts,
+                            size_t top_k, size_t width, int32_t *ids, float *weights, void *stream) {
+  if (!logits || !ids || !weights) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_moe_topk: null pointer");
+  const size_t need = top_k + (shared_gate ? 1 : 0);
+  if (tokens == 0 || experts == 0 || top_k == 0 || top_k > experts || width < need || width > 32 || ld < experts ||
+      experts > 2048 || tokens > 0x7fffffffu / 32)
+    return fail(FPB_ERR_SHAPE, "fpb_moe_topk: tokens %zu experts %zu top_k %zu width %zu ld %zu", tokens, experts,
+                top_k, width, ld);
+  cudaStream_t s = as_stream(stream);
+  const unsigned grid = (unsigned)((tokens * 32 + 255) / 256);
+  const int per = (int)((experts + 31) / 32);
+  auto go = [&](auto kernel) {
+    kernel<<<grid, 256, 0, s>>>(logits, (long long)ld, shared_gate, (int)tokens, (int)experts, (int)top_k,
+                                (int)width, ids, weights);
+  };
+  if (per <= 4)
+    go(moe_topk_kernel<4>);
+  else if (per <= 8)
+    go(moe_topk_kernel<8>);
+  else if (per <= 16)
+    go(moe_topk_kernel<16>);
+  else if (per <= 32)
+    go(moe_topk_kernel<32>);
+  else
+    go(moe_topk_kernel<64>);
+  FPB_LAUNCH_CHECK("moe_topk_kernel");
+  return FPB_OK;
+}
+
+extern "C" int fpb_moe_layout(const int32_t *ids, size_t tokens, size_t width, size_t slots, size_t experts,
+                              size_t tile_rows, size_t cap, int32_t *token_rows, int32_t *tile_experts,
+                              int32_t *inverse, size_t *ranges, int32_t *padded_rows, void *stream) {
+  if (!ids || !token_rows || !tile_experts || !inverse || !ranges || !padded_rows)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_moe_layout: null pointer");
+  if (tokens == 0 || slots == 0 || slots > width || experts == 0 || tile_rows == 0 || (tile_rows & (tile_rows - 1)))
+    return fail(FPB_ERR_SELECTION, "invalid expert selection: shape");
+  size_t max_rows = 0;
+  int st = fpb_prefill_layout_max_padded_rows(tokens, experts, slots, tile_rows, &max_rows);
+  if (st) return st;
+  if (cap < max_rows || cap % tile_rows || cap > 0x7fffffffu || tokens * width > 0x7fffffffu)
+    return fail(FPB_ERR_WORKSPACE, "fpb_moe_layout: capacity %zu below %zu (or not a multiple of tile_rows)", cap,
+                max_rows);
+  const size_t smem = ((size_t)kLayoutWarps * experts + experts + 1) * sizeof(int);
+  if (smem > 200 * 1024) return fail(FPB_ERR_UNSUPPORTED, "fpb_moe_layout: %zu experts", experts);
+  {
+    static std::mutex mu;
+    static std::vector<int> done;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (std::find(done.begin(), done.end(), dev) == done.end()) {
+      FPB_CUDA_TRY(cudaFuncSetAttribute(moe_layout_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+      done.push_back(dev);
+    }
+  }
+  moe_layout_kernel<<<1, kLayoutWarps * 32, smem, as_stream(stream)>>>(
+      ids, (int)tokens, (int)width, (int)slots, (int)experts, (int)tile_rows, (int)cap, token_rows, tile_experts,
+      inverse, reinterpret_cast<int64_t *>(ranges), padded_rows, device_error_ptr());
+  FPB_LAUNCH_CHECK("moe_layout_kernel");
+  return FPB_OK;
+}
+
+extern "C" int fpb_moe_gather(const void *x, int x_dtype, size_t tokens, size_t cols, const int32_t *token_rows,
+                              size_t rows, void *out, int out_dtype, void *stream) {
+  if (!x || !token_rows || !out) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_moe_gather: null pointer");
+  if (tokens == 0 || cols == 0 || rows == 0) return fail(FPB_ERR_SHAPE, "fpb_moe_gather: empty");
+  cudaStream_t s = as_stream(stream);
+  const unsigned grid = stride_grid(rows * cols);
+  return with_dtype(x_dtype, [&](auto tp) {
+    using T = std::remove_const_t<std::remove_pointer_t<decltype(tp)>>;
+    const T *xs = static_cast<const T *>(x);
+    if (out_dtype == FPB_F32)
+      gather_rows_kernel<T, float><<<grid, 256, 0, s>>>(xs, (int)tokens, token_rows, rows, cols,
+                                                         static_cast<float *>(out));
+    else if (out_dtype == FPB_BF16)
+      gather_rows_kernel<T, __nv_bfloat16><<<grid, 256, 0, s>>>(xs, (int)tokens, token_rows, rows, cols,
+                                                                 static_cast<__nv_bfloat16 *>(out));
+    else
+      return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_moe_gather: out dtype");
+    FPB_LAUNCH_CHECK("gather_rows_kernel");
+    return (int)FPB_OK;
+  });
+}
+
+extern "C" int fpb_moe_gather_quantize(const void *x, int x_dtype, size_t tokens, size_t cols,
+                                       const int32_t *token_rows, size_t rows, uint8_t *packed, uint8_t *sf_tiled,
+                                       float *global_out, float *amax_scratch, void *stream) {
+  if (!x || !token_rows || !packed || !sf_tiled || !global_out || !amax_scratch)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_moe_gather_quantize: null pointer");
+  if (tokens == 0 || rows == 0 || cols == 0 || cols % 32) return fail(FPB_ERR_SHAPE, "fpb_moe_gather_quantize: shape");
+  cudaStream_t s = as_stream(stream);
+  uint32_t *amax = reinterpret_cast<uint32_t *>(amax_scratch);
+  FPB_CUDA_TRY(cudaMemsetAsync(amax, 0, sizeof(uint32_t), s));
+  // Factors of the K padding up to a multiple of 256 columns are read by the
+  // tensor cores (times zero codes) and must be zero, not stale bytes.
+  if (cols % 256) FPB_CUDA_TRY(cudaMemsetAsync(sf_tiled, 0, sf_tiled_bytes(rows, cols), s));
+  return with_dtype(x_dtype, [&](auto tp) {
+    using T = std::remove_const_t<std::remove_pointer_t<decltype(tp)>>;
+    const T *xs = static_cast<const T *>(x);
+    act_amax_kernel<T><<<stride_grid(tokens * cols), 256, 0, s>>>(xs, tokens * cols, amax);
+    FPB_LAUNCH_CHECK("act_amax_kernel");
+    GatherRows<T> src{xs, token_rows, cols, (int)tokens};
+    rows_encode_kernel<<<stride_grid(rows * cols / 16), 256, 0, s>>>(src, rows, cols, amax, packed, sf_tiled,
+                                                                      global_out);
+    FPB_LAUNCH_CHECK("rows_encode_kernel(gather)");
+    return (int)FPB_OK;
+  });
+}
+
+extern "C" int fpb_swiglu(const void *gate_up, int dtype, size_t rows, size_t inter, void *out, int out_dtype,
+                          void *stream) {
+  if (!gate_up || !out) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_swiglu: null pointer");
+  if (rows == 0 || inter == 0) return fail(FPB_ERR_SHAPE, "fpb_swiglu: empty");
+  cudaStream_t s = as_stream(stream);
+  const unsigned grid = stride_grid(rows * inter);
+  return with_dtype(dtype, [&](auto tp) {
+    using T = std::remove_const_t<std::remove_pointer_t<decltype(tp)>>;
+    const T *g = static_cast<const T *>(gate_up);
+    if (out_dtype == FPB_F32)
+      swiglu_kernel<T, float><<<grid, 256, 0, s>>>(g, rows, inter, static_cast<float *>(out));
+    else if (out_dtype == FPB_BF16)
+      swiglu_kernel<T, __nv_bfloat16><<<grid, 256, 0, s>>>(g, rows, inter, static_cast<__nv_bfloat16 *>(out));
+    else
+      return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_swiglu: out dtype");
+    FPB_LAUNCH_CHECK("swiglu_kernel");
+    return (int)FPB_OK;
+  });
+}
+
+extern "C" int fpb_swiglu_quantize(const void *gate_up, int dtype, size_t rows, size_t inter, uint8_t *packed,
+                                   uint8_t *sf_tiled, float *global_out, float *amax_scratch, void *stream) {
+  if (!gate_up || !packed || !sf_tiled || !global_out || !amax_scratch)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_swiglu_quantize: null pointer");
+  if (rows == 0 || inter == 0 || inter % 32) return fail(FPB_ERR_SHAPE, "fpb_swiglu_quantize: shape");
+  cudaStream_t s = as_stream(stream);
+  uint32_t *amax = reinterpret_cast<uint32_t *>(amax_scratch);
+  FPB_CUDA_TRY(cudaMemsetAsync(amax, 0, sizeof(uint32_t), s));
+  if (inter % 256) FPB_CUDA_TRY(cudaMemsetAsync(sf_tiled, 0, sf_tiled_bytes(rows, inter), s));
+  return with_dtype(dtype, [&](auto tp) {
+    using T = std::remove_const_t<std::remove_pointer_t<decltype(tp)>>;
+    SwigluRows<T> src{static_cast<const T *>(gate_up), inter};
+    const unsigned grid = stride_grid(rows * inter / 16);
+    rows_amax_kernel<<<grid, 256, 0, s>>>(src, rows, inter, amax);
+    FPB_LAUNCH_CHECK("rows_amax_kernel(swiglu)");
+    rows_encode_kernel<<<grid, 256, 0, s>>>(src, rows, inter, amax, packed, sf_tiled, global_out);
+    FPB_LAUNCH_CHECK("rows_encode_kernel(swiglu)");
+    return (int)FPB_OK;
+  });
+}
+
+static int combine_impl(const void *routed, int r_dtype, size_t routed_rows, size_t cols, const int32_t *inverse,
+                        const float *weights, size_t tokens, size_t width, size_t slots, const float *residual,
+                        const float *gamma, float eps, void *out, int out_dtype, float *normed, cudaStream_t s) {
+  if (!routed || !inverse || !weights || !out) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_moe_combine: null pointer");
+  if (tokens == 0 || cols == 0 || slots == 0 || slots > width || tokens > 0x7fffffffu || routed_rows > 0x7fffffffu)
+    return fail(FPB_ERR_SHAPE, "fpb_moe_combine: shape");
+  const int threads = cols >= 1024 ? 512 : 256;
+  const float inv_h = 1.0f / (float)cols;
+  return with_dtype(r_dtype, [&](auto tp) {
+    using R = std::remove_const_t<std::remove_pointer_t<decltype(tp)>>;
+    const R *rs = static_cast<const R *>(routed);
+    if (out_dtype == FPB_F32)
+      combine_kernel<R, float><<<(unsigned)tokens, threads, 32 * sizeof(float), s>>>(
+          rs, (int)routed_rows, cols, inverse, weights, (int)width, (int)slots, residual, gamma, inv_h, eps,
+          static_cast<float *>(out), normed);
+    else if (out_dtype == FPB_BF16)
+      combine_kernel<R, __nv_bfloat16><<<(unsigned)tokens, threads, 32 * sizeof(float), s>>>(
+          rs, (int)routed_rows, cols, inverse, weights, (int)width, (int)slots, residual, gamma, inv_h, eps,
+          static_cast<__nv_bfloat16 *>(out), normed);
+    else
+      return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_moe_combine: out dtype");
+    FPB_LAUNCH_CHECK("combine_kernel");
+    return (int)FPB_OK;
+  });
+}
+
+extern "C" int fpb_moe_combine(const void *routed, int r_dtype, size_t routed_rows, size_t cols,
+                               const int32_t *inverse, const float *weights, size_t tokens, size_t width,
+                               size_t slots, void *out, int out_dtype, void *stream) {
+  return combine_impl(routed, r_dtype, routed_rows, cols, inverse, weights, tokens, width, slots, nullptr, nullptr,
+                      0.0f, out, out_dtype, nullptr, as_stream(stream));
+}
+
+extern "C" int fpb_moe_combine_add_norm(const void *routed, int r_dtype, size_t routed_rows, size_t cols,
+                                        const int32_t *inverse, const float *weights, size_t tokens, size_t width,
+                                        size_t slots, const float *residual, const float *gamma, float eps,
+                                        float *out, float *normed, void *stream) {
+  if (!residual || !gamma || !normed) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_moe_combine_add_norm: null pointer");
+  return combine_impl(routed, r_dtype, routed_rows, cols, inverse, weights, tokens, width, slots, residual, gamma,
+                      eps, out, FPB_F32, normed, as_stream(stream));
+}

@@ -252,6 +252,58 @@ int fpb_fp8_grouped_gemm_q(fpb_fp8_matrix *w, const uint8_t *a_bits, const float
                            size_t padded_rows, const int32_t *tile_experts, size_t rows_per_expert,
                            void *y, int y_dtype, void *stream);
 
+/* ---- MoE on the device ----------------------------------------------------
+ * The reference runs the router top-k on the GPU but builds the sorted layout
+ * on the host (PrefillPlan::top_k, moe.rs:545-585); here it stays on the
+ * device.  Layout arrays are sized `cap` >= fpb_prefill_layout_max_padded_rows
+ * (a multiple of tile_rows); row tiles past the real end get expert id -1,
+ * which fpb_nvfp4_grouped_gemm_q / fpb_fp8_grouped_gemm_q skip. */
+/* top_k_prefill (moe.rs:15-68): logits f32 [tokens, ld >= experts] ->
+ * ids int32 / weights f32 [tokens, width]: k rounds of the largest remaining
+ * logit (lowest id among equals), weight exp(l - max) / sum over the k; with
+ * shared_gate (f32 [tokens]) slot k is expert `experts`, weight sigmoid(gate).
+ * width <= 32, experts <= 2048.  One warp per token. */
+int fpb_moe_topk(const float *logits, size_t ld, const float *shared_gate, size_t tokens, size_t experts,
+                 size_t top_k, size_t width, int32_t *ids, float *weights, void *stream);
+/* PrefillLayout::from_indices (moe.rs:452-516) on the device, over the first
+ * `slots` entries of each row of ids [tokens, width]: stable counting sort by
+ * expert (experts ids in [0, experts)), each padded to tile_rows (a power of
+ * two).  Outputs: token_rows [cap] (-1 = padding), tile_experts [cap/tile_rows]
+ * (-1 past the end), inverse [tokens, width] (0 in unused slots), ranges
+ * [experts][2] (start, count), padded_rows (device int32).  One CTA. Device
+ * error 401 on an id out of range. */
+int fpb_moe_layout(const int32_t *ids, size_t tokens, size_t width, size_t slots, size_t experts,
+                   size_t tile_rows, size_t cap, int32_t *token_rows, int32_t *tile_experts,
+                   int32_t *inverse, size_t *ranges, int32_t *padded_rows, void *stream);
+/* gather_prefill_view (moe.rs:71-89, 705-733): out [rows, cols] (f32/bf16),
+ * row r = x[token_rows[r]] or zeros. */
+int fpb_moe_gather(const void *x, int x_dtype, size_t tokens, size_t cols, const int32_t *token_rows,
+                   size_t rows, void *out, int out_dtype, void *stream);
+/* The gather fused with the NVFP4 activation quantize of fpb_nvfp4_quantize_act
+ * (global from amax over x): packed [rows, cols/2], tiled factors, global. */
+int fpb_moe_gather_quantize(const void *x, int x_dtype, size_t tokens, size_t cols, const int32_t *token_rows,
+                            size_t rows, uint8_t *packed, uint8_t *sf_tiled, float *global_out,
+                            float *amax_scratch, void *stream);
+/* swiglu (swiglu.rs:5-20): out [rows, inter] = gate / (1 + exp(-gate)) * up,
+ * gate = gate_up[:, :inter], up = gate_up[:, inter:]. */
+int fpb_swiglu(const void *gate_up, int dtype, size_t rows, size_t inter, void *out, int out_dtype,
+               void *stream);
+/* SwiGLU fused with the NVFP4 activation quantize (input of the down GEMM). */
+int fpb_swiglu_quantize(const void *gate_up, int dtype, size_t rows, size_t inter, uint8_t *packed,
+                        uint8_t *sf_tiled, float *global_out, float *amax_scratch, void *stream);
+/* combine / combine_prefill (moe.rs:91-109, 779-822): out [tokens, cols] =
+ * sum over the first `slots` slots of weights[t, s] * routed[inverse[t, s]]
+ * (routed [routed_rows, cols]; a row index outside it adds nothing). */
+int fpb_moe_combine(const void *routed, int r_dtype, size_t routed_rows, size_t cols, const int32_t *inverse,
+                    const float *weights, size_t tokens, size_t width, size_t slots, void *out, int out_dtype,
+                    void *stream);
+/* combine_add_norm_{view,prefill} (moe.rs:111-147, 824-859): out = residual +
+ * combine, normed = out * rsqrt(mean(out^2) + eps) * gamma (f32). */
+int fpb_moe_combine_add_norm(const void *routed, int r_dtype, size_t routed_rows, size_t cols,
+                             const int32_t *inverse, const float *weights, size_t tokens, size_t width,
+                             size_t slots, const float *residual, const float *gamma, float eps, float *out,
+                             float *normed, void *stream);
+
 /* ---- MoE host bookkeeping (no GPU needed) -------------------------------- */
 /* MoeDims::new (moe.rs:172-225): FPB_ERR_SHAPE on invalid dimensions. */
 int fpb_moe_dims_validate(size_t hidden, size_t intermediate, size_t shared_intermediate,

@@ -105,6 +105,29 @@ void orc_fp8_gemm_f64(const uint8_t *a_bits, const float *a_scales, size_t m, co
                       const float *w_scales, size_t n, size_t k, size_t block_n, size_t block_k,
                       double *expected, double *magnitude);
 
+/* ---- MoE (oracle/moe.c) ---------------------------------------------------
+ * top_k_prefill (kernels src/moe.rs:15-68): per token, k rounds of "largest
+ * remaining logit, lowest id among equals"; weight exp(l - max) / sum over
+ * the k winners; slot k = expert `experts` with sigmoid(gate) when
+ * shared_gate is given; other slots id 0 weight 0.  ids/weights [tokens, width]. */
+void orc_moe_topk(const float *logits, size_t ld, const float *shared_gate, size_t tokens, size_t experts,
+                  size_t k, size_t width, int32_t *ids, float *weights);
+/* PrefillLayout::from_indices (kernels src/moe.rs:452-516) over the first kk
+ * slots of each row of ids [tokens, width]: stable counting sort by expert,
+ * each expert padded to tile_rows; token_rows [cap] (-1 padding), tile_experts
+ * [cap / tile_rows] (-1 past the end), inverse [tokens, width] (0 padding),
+ * ranges [experts][2] (start, count).  Returns 0, or -1 on a bad id/capacity. */
+int orc_moe_layout(const int32_t *ids, size_t tokens, size_t width, size_t kk, size_t experts, size_t tile_rows,
+                   size_t cap, int32_t *token_rows, int32_t *tile_experts, int32_t *inverse, int64_t *ranges,
+                   int32_t *padded);
+/* swiglu (kernels src/swiglu.rs:16): gate / (1 + exp(-gate)) * up. */
+void orc_swiglu(const float *gate_up, size_t rows, size_t inter, float *out);
+/* combine_prefill_kernel (moe.rs:91-109); with residual, combine_add_norm_kernel
+ * (moe.rs:111-147): out = residual + sum, normed = out * rsqrt(mean(out^2) + eps) * gamma. */
+void orc_moe_combine(const float *routed, size_t cols, const int32_t *inverse, const float *weights, size_t tokens,
+                     size_t width, size_t slots, const float *residual, const float *gamma, float eps, float *out,
+                     float *normed);
+
 /* ---- error model (kernels tests/common/check.rs:19-38) ------------------- */
 double orc_gamma_tilde(size_t n);
 double orc_inner_product_excess(const float *actual, const double *expected,

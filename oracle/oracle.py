@@ -50,6 +50,10 @@ for name, res, args in [
     ("orc_fp8_quantize", C.c_int, [_vp, _sz, _sz, _sz, _sz, _vp, _vp]),
     ("orc_fp8_dequantize", None, [_vp, _vp, _sz, _sz, _sz, _sz, _vp]),
     ("orc_fp8_gemm_f64", None, [_vp, _vp, _sz, _vp, _vp, _sz, _sz, _sz, _sz, _vp, _vp]),
+    ("orc_moe_topk", None, [_vp, _sz, _vp, _sz, _sz, _sz, _sz, _vp, _vp]),
+    ("orc_moe_layout", C.c_int, [_vp, _sz, _sz, _sz, _sz, _sz, _sz, _vp, _vp, _vp, _vp, _vp]),
+    ("orc_swiglu", None, [_vp, _sz, _sz, _vp]),
+    ("orc_moe_combine", None, [_vp, _sz, _vp, _vp, _sz, _sz, _sz, _vp, _vp, C.c_float, _vp, _vp]),
     ("orc_gamma_tilde", C.c_double, [_sz]),
     ("orc_inner_product_excess", C.c_double, [_vp, _vp, _vp, _sz, _sz]),
     ("orc_num_threads", C.c_int, []),
@@ -182,6 +186,54 @@ def fp8_gemm_f64(a_bits, a_scales, w_bits, w_scales, block_n: int = 0, block_k: 
     lib.orc_fp8_gemm_f64(_p(a_bits), _p(f32(a_scales)), m, _p(w_bits), _p(f32(w_scales)), n, k, block_n, block_k,
                          _p(e), _p(mag))
     return e, mag
+
+
+# ---- MoE ---------------------------------------------------------------------------------
+def moe_topk(logits, k: int, width: int, shared_gate=None):
+    logits = f32(logits)
+    tokens, experts = logits.shape
+    ids = np.empty((tokens, width), np.int32)
+    w = np.empty((tokens, width), np.float32)
+    g = None if shared_gate is None else f32(shared_gate).reshape(-1)
+    lib.orc_moe_topk(_p(logits), experts, None if g is None else _p(g), tokens, experts, k, width, _p(ids), _p(w))
+    return ids, w
+
+
+def moe_layout(ids, kk: int, experts: int, tile_rows: int, cap: int):
+    ids = np.ascontiguousarray(ids, np.int32)
+    tokens, width = ids.shape
+    token_rows = np.empty(cap, np.int32)
+    tile_experts = np.empty(cap // tile_rows, np.int32)
+    inverse = np.empty((tokens, width), np.int32)
+    ranges = np.empty((experts, 2), np.int64)
+    padded = np.zeros(1, np.int32)
+    rc = lib.orc_moe_layout(_p(ids), tokens, width, kk, experts, tile_rows, cap, _p(token_rows), _p(tile_experts),
+                            _p(inverse), _p(ranges), _p(padded))
+    if rc != 0:
+        raise ValueError("orc_moe_layout: invalid ids or capacity")
+    return token_rows, tile_experts, inverse, ranges, int(padded[0])
+
+
+def swiglu(gate_up):
+    gate_up = f32(gate_up)
+    rows, two_i = gate_up.shape
+    out = np.empty((rows, two_i // 2), np.float32)
+    lib.orc_swiglu(_p(gate_up), rows, two_i // 2, _p(out))
+    return out
+
+
+def moe_combine(routed, inverse, weights, slots: int, residual=None, gamma=None, eps: float = 1e-6):
+    routed = f32(routed)
+    inverse = np.ascontiguousarray(inverse, np.int32)
+    weights = f32(weights)
+    tokens, width = inverse.shape
+    cols = routed.shape[1]
+    out = np.empty((tokens, cols), np.float32)
+    normed = np.empty((tokens, cols), np.float32) if residual is not None else None
+    lib.orc_moe_combine(_p(routed), cols, _p(inverse), _p(weights), tokens, width, slots,
+                        None if residual is None else _p(f32(residual)), None if gamma is None else _p(f32(gamma)),
+                        eps, _p(out), None if normed is None else _p(normed))
+    return (out, normed) if residual is not None else out
 
 
 def gamma_tilde(n: int) -> float:

@@ -46,9 +46,10 @@ def parse_args():
     p.add_argument("--steps", type=int, default=2000)
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--config", choices=["gemv", "nvfp4_gemm_m128", "nvfp4_gemm_m2048", "fp8_gemm"], default="gemv",
+    p.add_argument("--config", choices=["gemv", "nvfp4_gemm_m128", "nvfp4_gemm_m2048", "fp8_gemm", "moe_t4096",
+                                        "moe_t64"], default="gemv",
                    help="gemv: config 0 (default); nvfp4_gemm_m*: config 2 GEMM at M=128 / M=2048; "
-                        "fp8_gemm: config 1")
+                        "fp8_gemm: config 1; moe_t*: config 3 MoE layer at T=4096 / T=64")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the cpu_baseline sample")
     return p.parse_args()
 
@@ -749,9 +750,255 @@ def fp8_arm(args):
         dist.destroy_process_group()
 
 
+# ---- config 3: grouped MoE NVFP4 layer ---------------------------------------------------
+MOE_E, MOE_K, MOE_H, MOE_I = 512, 10, 2048, 512
+MOE_GU_BYTES = 2 * MOE_I * MOE_H // 2 + 2 * MOE_I * MOE_H // 16 + 4   # 1,179,652 per expert (one global)
+MOE_DN_BYTES = MOE_H * MOE_I // 2 + MOE_H * MOE_I // 16 + 4           # 589,828 per expert
+
+
+def moe_tokens(args):
+    return 4096 if args.config == "moe_t4096" else 64
+
+
+def moe_flops(tokens):
+    """Useful FLOPs: router x.Wr^T plus, per route, gate/up and down."""
+    return 2.0 * tokens * MOE_E * MOE_H + tokens * MOE_K * 2.0 * (2 * MOE_I * MOE_H + MOE_H * MOE_I)
+
+
+def moe_bytes(tokens, touched):
+    """Algorithmic HBM bytes: touched experts' weights, bf16 router, x and y (bf16)."""
+    return touched * (MOE_GU_BYTES + MOE_DN_BYTES) + MOE_E * MOE_H * 2 + 2 * tokens * MOE_H * 2
+
+
+def moe_cpu_sample(seconds: float, tokens_sample: int = 256):
+    """The host path restated on a sample of tokens: f32 router, top-k, then per
+    routed expert the dequantized NVFP4 gate/up -> SwiGLU -> down over the
+    tokens routed to it (numpy/BLAS on all host cores).  Expert weights are
+    dequantized once, outside the timed region.  Returns (TFLOP/s of useful
+    work, sample description)."""
+    import numpy as np
+
+    from oracle import oracle as O
+    x = O.bf16_to_f32(O.bf16_bits(O.synth_normal(tokens_sample * MOE_H, seed=0, stream=0))).reshape(
+        tokens_sample, MOE_H)
+    wr = O.bf16_to_f32(O.bf16_bits(O.synth_normal(MOE_E * MOE_H, seed=0, stream=99, std=0.02))).reshape(MOE_E, MOE_H)
+    ids, w = O.moe_topk(x @ wr.T, MOE_K, 16)
+    cache = {}
+    for e in np.unique(ids[:, :MOE_K]):
+        g = O.synth_normal(2 * MOE_I * MOE_H, seed=0, stream=1000 + int(e), std=0.02).reshape(2 * MOE_I, MOE_H)
+        d = O.synth_normal(MOE_H * MOE_I, seed=0, stream=5000 + int(e), std=0.02).reshape(MOE_H, MOE_I)
+        pg, sg, gg = O.nvfp4_quantize(g)
+        pd, sd, gd = O.nvfp4_quantize(d)
+        cache[int(e)] = (O.nvfp4_dequantize(pg, sg, gg, 2 * MOE_I, MOE_H), O.nvfp4_dequantize(pd, sd, gd, MOE_H, MOE_I))
+
+    def layer():
+        idx, wts = O.moe_topk(x @ wr.T, MOE_K, 16)
+        out = np.zeros_like(x)
+        for e, (w1, w2) in cache.items():
+            tok, slot = np.nonzero(idx[:, :MOE_K] == e)
+            if tok.size == 0:
+                continue
+            gu = x[tok] @ w1.T
+            act = gu[:, :MOE_I] / (1.0 + np.exp(-gu[:, :MOE_I])) * gu[:, MOE_I:]
+            np.add.at(out, tok, wts[tok, slot][:, None] * (act @ w2.T))
+        return out
+
+    layer()
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        layer()
+        reps += 1
+        if time.perf_counter() - t0 > seconds:
+            break
+    dt = (time.perf_counter() - t0) / reps
+    return moe_flops(tokens_sample) / dt / 1e12, (
+        f"{reps} x {tokens_sample} tokens through f32 router + top-{MOE_K} of {MOE_E} + dequantized NVFP4 expert "
+        f"MLPs grouped by expert (f32 BLAS; weights dequantized beforehand)")
+
+
+def moe_reference_arm(args):
+    rank, _, _ = dist_env()
+    if rank != 0:
+        return
+    v, sample = moe_cpu_sample(min(60.0, max(5.0, 2.0 * (args.steps + args.warmup))))
+    emit({"impl": "reference", "metric": "NVFP4 MoE layer TFLOPS", "value": v, "unit": "TFLOP/s",
+          "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+          "ms_per_step": moe_flops(moe_tokens(args)) / (v * 1e12) * 1e3, "higher_is_better": True,
+          "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded Philox)",
+          "config": {"workload": f"config3 MoE E=512 top-10 H=2048 I=512 T={moe_tokens(args)}"},
+          "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port", "sample": sample},
+          "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
+
+
+def moe_arm(args):
+    """Config 3 at T = 4096 (prefill) or 64 (decode batch), one GPU: bf16 x
+    [T, 2048], bf16 router [512, 2048] (cuBLAS, f32 logits), device top-10,
+    device layout (128-row tiles), gather + NVFP4 quantize, grouped gate/up
+    GEMM [512 x 1024, 2048], SwiGLU + NVFP4 quantize, grouped down GEMM
+    [512 x 2048, 512], weighted combine; one CUDA graph per step."""
+    import torch
+
+    import firepit_b200 as F
+    N_ = F._native
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    T = moe_tokens(args)
+    # weights: each expert its own global; streams 1000+e / 5000+e as in the CPU sample
+    gu_parts, dn_parts = [], []
+    chunk = 64
+    gp = torch.empty(MOE_E * 2 * MOE_I, MOE_H // 2, dtype=torch.uint8, device=dev)
+    gs = torch.empty(MOE_E * 2 * MOE_I, MOE_H // 16, dtype=torch.uint8, device=dev)
+    gg = torch.empty(MOE_E * 2 * MOE_I, dtype=torch.float32, device=dev)
+    dp = torch.empty(MOE_E * MOE_H, MOE_I // 2, dtype=torch.uint8, device=dev)
+    ds = torch.empty(MOE_E * MOE_H, MOE_I // 16, dtype=torch.uint8, device=dev)
+    dg = torch.empty(MOE_E * MOE_H, dtype=torch.float32, device=dev)
+    for e0 in range(0, MOE_E, chunk):
+        g = torch.empty(chunk, 2 * MOE_I, MOE_H, device=dev)
+        d = torch.empty(chunk, MOE_H, MOE_I, device=dev)
+        for j in range(chunk):
+            F.synth_normal(g[j].shape, seed=0, stream_id=1000 + e0 + j, std=0.02, out=g[j])
+            F.synth_normal(d[j].shape, seed=0, stream_id=5000 + e0 + j, std=0.02, out=d[j])
+        a, b, c = F.quantize_nvfp4(g.view(-1, MOE_H), 2 * MOE_I)
+        r0, r1 = e0 * 2 * MOE_I, (e0 + chunk) * 2 * MOE_I
+        gp[r0:r1], gs[r0:r1], gg[r0:r1] = a, b, c
+        a, b, c = F.quantize_nvfp4(d.view(-1, MOE_I), MOE_H)
+        r0, r1 = e0 * MOE_H, (e0 + chunk) * MOE_H
+        dp[r0:r1], ds[r0:r1], dg[r0:r1] = a, b, c
+        del g, d
+    W1 = F.Nvfp4Matrix.from_device(gp, gs, gg, MOE_E * 2 * MOE_I, MOE_H)
+    W2 = F.Nvfp4Matrix.from_device(dp, ds, dg, MOE_E * MOE_H, MOE_I)
+    del gp, gs, gg, dp, ds, dg
+    s0 = torch.cuda.current_stream().cuda_stream
+    N_.call("fpb_nvfp4_matrix_prepare_gemm", W1.handle, s0)
+    N_.call("fpb_nvfp4_matrix_prepare_gemm", W2.handle, s0)
+    wr = F.synth_normal((MOE_E, MOE_H), seed=0, stream_id=99, std=0.02, dtype=torch.bfloat16, device=dev)
+    x = F.synth_normal((T, MOE_H), seed=0, stream_id=0, dtype=torch.bfloat16, device=dev)
+    router = F.MoeDims.new(MOE_H, MOE_I, MOE_I, MOE_E, MOE_K)
+    width = router.width()
+    cap = F.PrefillPlan.capacity(T, router, 128)
+    i32 = dict(dtype=torch.int32, device=dev)
+    buf = dict(logits=torch.empty(T, MOE_E, device=dev), ids=torch.empty(T, width, **i32),
+               w=torch.empty(T, width, device=dev), tr=torch.empty(cap, **i32), te=torch.empty(cap // 128, **i32),
+               inv=torch.empty(T, width, **i32), rg=torch.empty(MOE_E, 2, dtype=torch.int64, device=dev),
+               pad=torch.empty(1, **i32),
+               a1=torch.empty(cap, MOE_H // 2, dtype=torch.uint8, device=dev),
+               sf1=torch.empty(int(N_.lib.fpb_nvfp4_act_sf_bytes(cap, MOE_H)), dtype=torch.uint8, device=dev),
+               y1=torch.empty(cap, 2 * MOE_I, dtype=torch.bfloat16, device=dev),
+               a2=torch.empty(cap, MOE_I // 2, dtype=torch.uint8, device=dev),
+               sf2=torch.empty(int(N_.lib.fpb_nvfp4_act_sf_bytes(cap, MOE_I)), dtype=torch.uint8, device=dev),
+               y2=torch.empty(cap, MOE_H, dtype=torch.bfloat16, device=dev),
+               out=torch.empty(T, MOE_H, dtype=torch.bfloat16, device=dev),
+               scal=torch.zeros(4, dtype=torch.float32, device=dev))
+    b = buf
+    BF = N_.FPB_BF16
+
+    def moe(sh, xin, ev=None):
+        def mark(i):
+            if ev is not None:
+                ev[i].record()
+        mark(0)
+        torch.mm(xin, wr.t(), out_dtype=torch.float32, out=b["logits"])
+        mark(1)
+        N_.call("fpb_moe_topk", b["logits"].data_ptr(), MOE_E, None, T, MOE_E, MOE_K, width, b["ids"].data_ptr(),
+                b["w"].data_ptr(), sh)
+        N_.call("fpb_moe_layout", b["ids"].data_ptr(), T, width, MOE_K, MOE_E, 128, cap, b["tr"].data_ptr(),
+                b["te"].data_ptr(), b["inv"].data_ptr(), b["rg"].data_ptr(), b["pad"].data_ptr(), sh)
+        N_.call("fpb_moe_gather_quantize", xin.data_ptr(), BF, T, MOE_H, b["tr"].data_ptr(), cap, b["pad"].data_ptr(),
+                b["a1"].data_ptr(), b["sf1"].data_ptr(), b["scal"].data_ptr(), b["scal"][1:].data_ptr(), sh)
+        mark(2)
+        N_.call("fpb_nvfp4_grouped_gemm_q", W1.handle, b["a1"].data_ptr(), b["sf1"].data_ptr(), b["scal"].data_ptr(),
+                cap, b["te"].data_ptr(), 2 * MOE_I, b["y1"].data_ptr(), BF, sh)
+        mark(3)
+        N_.call("fpb_swiglu_quantize", b["y1"].data_ptr(), BF, cap, b["pad"].data_ptr(), MOE_I, b["a2"].data_ptr(),
+                b["sf2"].data_ptr(), b["scal"][2:].data_ptr(), b["scal"][3:].data_ptr(), sh)
+        mark(4)
+        N_.call("fpb_nvfp4_grouped_gemm_q", W2.handle, b["a2"].data_ptr(), b["sf2"].data_ptr(),
+                b["scal"][2:].data_ptr(), cap, b["te"].data_ptr(), MOE_H, b["y2"].data_ptr(), BF, sh)
+        mark(5)
+        N_.call("fpb_moe_combine", b["y2"].data_ptr(), BF, cap, MOE_H, b["inv"].data_ptr(), b["w"].data_ptr(), T,
+                width, MOE_K, b["out"].data_ptr(), BF, sh)
+        mark(6)
+
+    s = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(s):
+        moe(s.cuda_stream, x)
+    torch.cuda.synchronize()
+    assert F.device_error() == 0
+    touched = int((b["rg"][:, 1] > 0).sum().item())
+    before = F.launch_count()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        moe(torch.cuda.current_stream().cuda_stream, x)
+    launches_per_step = F.launch_count() - before
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record()
+        for _ in range(args.steps):
+            graph.replay()
+        end.record()
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / args.steps
+    # per-stage breakdown (eager launches with events)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(7)]
+    with torch.cuda.stream(s):
+        moe(s.cuda_stream, x, evs)
+    torch.cuda.synchronize()
+    names = ["router_gemm", "topk_layout_gather_quant", "gate_up_gemm", "swiglu_quant", "down_gemm", "combine"]
+    breakdown = {n: evs[i].elapsed_time(evs[i + 1]) for i, n in enumerate(names)}
+    flops = moe_flops(T)
+    value = flops / (ms * 1e-3) / 1e12
+    nbytes = moe_bytes(T, touched)
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    achieved = nbytes / (ms * 1e-3) / 1e9
+    # end to end: x from pinned host, out back to pinned host, the same launches
+    xh = x.cpu().pin_memory()
+    oh = torch.empty(T, MOE_H, dtype=torch.bfloat16, pin_memory=True)
+    xd = torch.empty_like(x)
+    e2e_steps = max(1, min(args.steps, 20))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(s):
+        for i in range(e2e_steps + 2):
+            if i == 2:
+                e0.record()
+            xd.copy_(xh, non_blocking=True)
+            moe(s.cuda_stream, xd)
+            oh.copy_(b["out"], non_blocking=True)
+        e1.record()
+    torch.cuda.synchronize()
+    e2e = flops / (e0.elapsed_time(e1) / e2e_steps * 1e-3) / 1e12
+    line = {"metric": "NVFP4 MoE layer TFLOPS", "value": value, "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "nvfp4 x nvfp4 experts (f32 accumulate), bf16 router (f32 logits), bf16 activations",
+            "data": "synthetic (seeded Philox: W N(0,0.02) per expert, x N(0,1) seed 0)",
+            "config": {"workload": f"config3 MoE E=512 top-10 H=2048 I=512 T={T}, no shared expert",
+                       "touched_experts": touched, "l2": f"{nbytes / 1e6:.0f} MB of weights per step (> L2)",
+                       "parallelism": "single GPU", "tile_rows": 128},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                         "traffic": None, "algorithmic_bytes": nbytes, "peak_kind": "measured hbm_gbs",
+                         "note": "whole MoE layer time; the grouped GEMMs are the dominant kernels"},
+            "e2e": {"value": e2e, "unit": "TFLOP/s", "h2d_bytes_per_step": T * MOE_H * 2,
+                    "d2h_bytes_per_step": T * MOE_H * 2},
+            "gpu_launches": launches_per_step * args.steps, "clocks": clocks.summary(), "breakdown_ms": breakdown}
+    if args.cpu_seconds > 0:
+        v, sample = moe_cpu_sample(args.cpu_seconds)
+        line["cpu_baseline"] = {"value": v, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
+                                "sample": sample}
+    if rank == 0:
+        emit(line)
+    del graph
+
+
 def main():
     args = parse_args()
-    if args.config == "fp8_gemm":
+    if args.config.startswith("moe_"):
+        (moe_reference_arm if args.impl == "reference" else moe_arm)(args)
+    elif args.config == "fp8_gemm":
         (fp8_reference_arm if args.impl == "reference" else fp8_arm)(args)
     elif args.config.startswith("nvfp4_gemm"):
         (gemm_reference_arm if args.impl == "reference" else gemm_arm)(args)

@@ -102,9 +102,9 @@ SIGNATURES: dict[str, tuple] = {
     "fpb_moe_topk": (i32, [vp, sz, vp, sz, sz, sz, sz, vp, vp, vp]),
     "fpb_moe_layout": (i32, [vp, sz, sz, sz, sz, sz, sz, vp, vp, vp, vp, vp, vp]),
     "fpb_moe_gather": (i32, [vp, i32, sz, sz, vp, sz, vp, i32, vp]),
-    "fpb_moe_gather_quantize": (i32, [vp, i32, sz, sz, vp, sz, vp, vp, vp, vp, vp]),
+    "fpb_moe_gather_quantize": (i32, [vp, i32, sz, sz, vp, sz, vp, vp, vp, vp, vp, vp]),
     "fpb_swiglu": (i32, [vp, i32, sz, sz, vp, i32, vp]),
-    "fpb_swiglu_quantize": (i32, [vp, i32, sz, sz, vp, vp, vp, vp, vp]),
+    "fpb_swiglu_quantize": (i32, [vp, i32, sz, vp, sz, vp, vp, vp, vp, vp]),
     "fpb_moe_combine": (i32, [vp, i32, sz, sz, vp, vp, sz, sz, sz, vp, i32, vp]),
     "fpb_moe_combine_add_norm": (i32, [vp, i32, sz, sz, vp, vp, sz, sz, sz, vp, vp, C.c_float, vp, vp, vp]),
     "fpb_moe_dims_validate": (i32, [sz, sz, sz, sz, sz]),

@@ -239,9 +239,15 @@ struct SwigluRows {
   }
 };
 
+// `valid` (nullable, device): rows at or past *valid are neither read nor
+// written (row tiles past a device layout's end, which the GEMMs skip).
+__device__ __forceinline__ size_t valid_rows(size_t rows, const int32_t *valid) {
+  return valid ? min(rows, (size_t)max(*valid, 0)) : rows;
+}
+
 template <class Rows>
-__global__ void rows_amax_kernel(Rows rows_src, size_t rows, size_t cols, uint32_t *amax_bits) {
-  const size_t gpr = cols / 16, n = rows * gpr;
+__global__ void rows_amax_kernel(Rows rows_src, size_t rows, const int32_t *valid, size_t cols, uint32_t *amax_bits) {
+  const size_t gpr = cols / 16, n = valid_rows(rows, valid) * gpr;
   uint32_t m = 0;
   size_t stride = (size_t)gridDim.x * blockDim.x;
   for (size_t gi = (size_t)blockIdx.x * blockDim.x + threadIdx.x; gi < n; gi += stride) {
@@ -256,11 +262,11 @@ __global__ void rows_amax_kernel(Rows rows_src, size_t rows, size_t cols, uint32
 }
 
 template <class Rows>
-__global__ void rows_encode_kernel(Rows rows_src, size_t rows, size_t cols, const uint32_t *amax_bits,
-                                   uint8_t *packed, uint8_t *sf_tiled, float *global_out) {
+__global__ void rows_encode_kernel(Rows rows_src, size_t rows, const int32_t *valid, size_t cols,
+                                   const uint32_t *amax_bits, uint8_t *packed, uint8_t *sf_tiled, float *global_out) {
   const float global = __fdiv_rn(__uint_as_float(*amax_bits), 2688.0f);
   if (blockIdx.x == 0 && threadIdx.x == 0) *global_out = global;
-  const size_t gpr = cols / 16, n = rows * gpr;
+  const size_t gpr = cols / 16, n = valid_rows(rows, valid) * gpr;
   size_t stride = (size_t)gridDim.x * blockDim.x;
   for (size_t gi = (size_t)blockIdx.x * blockDim.x + threadIdx.x; gi < n; gi += stride) {
     const size_t r = gi / gpr, g = gi % gpr;
@@ -453,8 +459,9 @@ extern "C" int fpb_moe_gather(const void *x, int x_dtype, size_t tokens, size_t 
 }
 
 extern "C" int fpb_moe_gather_quantize(const void *x, int x_dtype, size_t tokens, size_t cols,
-                                       const int32_t *token_rows, size_t rows, uint8_t *packed, uint8_t *sf_tiled,
-                                       float *global_out, float *amax_scratch, void *stream) {
+                                       const int32_t *token_rows, size_t rows, const int32_t *valid_rows,
+                                       uint8_t *packed, uint8_t *sf_tiled, float *global_out, float *amax_scratch,
+                                       void *stream) {
   if (!x || !token_rows || !packed || !sf_tiled || !global_out || !amax_scratch)
     return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_moe_gather_quantize: null pointer");
   if (tokens == 0 || rows == 0 || cols == 0 || cols % 32) return fail(FPB_ERR_SHAPE, "fpb_moe_gather_quantize: shape");
@@ -470,8 +477,8 @@ extern "C" int fpb_moe_gather_quantize(const void *x, int x_dtype, size_t tokens
     act_amax_kernel<T><<<stride_grid(tokens * cols), 256, 0, s>>>(xs, tokens * cols, amax);
     FPB_LAUNCH_CHECK("act_amax_kernel");
     GatherRows<T> src{xs, token_rows, cols, (int)tokens};
-    rows_encode_kernel<<<stride_grid(rows * cols / 16), 256, 0, s>>>(src, rows, cols, amax, packed, sf_tiled,
-                                                                      global_out);
+    rows_encode_kernel<<<stride_grid(rows * cols / 16), 256, 0, s>>>(src, rows, valid_rows, cols, amax, packed,
+                                                                      sf_tiled, global_out);
     FPB_LAUNCH_CHECK("rows_encode_kernel(gather)");
     return (int)FPB_OK;
   });
@@ -497,8 +504,9 @@ extern "C" int fpb_swiglu(const void *gate_up, int dtype, size_t rows, size_t in
   });
 }
 
-extern "C" int fpb_swiglu_quantize(const void *gate_up, int dtype, size_t rows, size_t inter, uint8_t *packed,
-                                   uint8_t *sf_tiled, float *global_out, float *amax_scratch, void *stream) {
+extern "C" int fpb_swiglu_quantize(const void *gate_up, int dtype, size_t rows, const int32_t *valid_rows,
+                                   size_t inter, uint8_t *packed, uint8_t *sf_tiled, float *global_out,
+                                   float *amax_scratch, void *stream) {
   if (!gate_up || !packed || !sf_tiled || !global_out || !amax_scratch)
     return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_swiglu_quantize: null pointer");
   if (rows == 0 || inter == 0 || inter % 32) return fail(FPB_ERR_SHAPE, "fpb_swiglu_quantize: shape");
@@ -510,9 +518,9 @@ extern "C" int fpb_swiglu_quantize(const void *gate_up, int dtype, size_t rows, 
     using T = std::remove_const_t<std::remove_pointer_t<decltype(tp)>>;
     SwigluRows<T> src{static_cast<const T *>(gate_up), inter};
     const unsigned grid = stride_grid(rows * inter / 16);
-    rows_amax_kernel<<<grid, 256, 0, s>>>(src, rows, inter, amax);
+    rows_amax_kernel<<<grid, 256, 0, s>>>(src, rows, valid_rows, inter, amax);
     FPB_LAUNCH_CHECK("rows_amax_kernel(swiglu)");
-    rows_encode_kernel<<<grid, 256, 0, s>>>(src, rows, inter, amax, packed, sf_tiled, global_out);
+    rows_encode_kernel<<<grid, 256, 0, s>>>(src, rows, valid_rows, inter, amax, packed, sf_tiled, global_out);
     FPB_LAUNCH_CHECK("rows_encode_kernel(swiglu)");
     return (int)FPB_OK;
   });

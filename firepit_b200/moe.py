@@ -305,7 +305,8 @@ def gather_quantize(x, plan: PrefillPlan, stream=None):
     sf = torch.empty(int(N.lib.fpb_nvfp4_act_sf_bytes(plan.cap, h)), dtype=torch.uint8, device=x.device)
     scal = torch.empty(2, dtype=torch.float32, device=x.device)
     N.call("fpb_moe_gather_quantize", x.data_ptr(), _dt(x), tokens, h, plan.token_rows.data_ptr(), plan.cap,
-           packed.data_ptr(), sf.data_ptr(), scal.data_ptr(), scal[1:].data_ptr(), _stream(x, stream))
+           plan.padded_rows_dev.data_ptr(), packed.data_ptr(), sf.data_ptr(), scal.data_ptr(), scal[1:].data_ptr(),
+           _stream(x, stream))
     return packed, sf, scal[:1]
 
 
@@ -318,15 +319,17 @@ def swiglu(out, gate_up, stream=None) -> None:
            _stream(gate_up, stream))
 
 
-def swiglu_quantize(gate_up, stream=None):
-    """SwiGLU fused with the NVFP4 activation quantize (for the down GEMM)."""
+def swiglu_quantize(gate_up, stream=None, valid_rows=None):
+    """SwiGLU fused with the NVFP4 activation quantize (for the down GEMM);
+    ``valid_rows``: device int32 row count (a plan's ``padded_rows_dev``)."""
     import torch
     rows, two_i = gate_up.shape
     inter = two_i // 2
     packed = torch.empty(rows, inter // 2, dtype=torch.uint8, device=gate_up.device)
     sf = torch.empty(int(N.lib.fpb_nvfp4_act_sf_bytes(rows, inter)), dtype=torch.uint8, device=gate_up.device)
     scal = torch.empty(2, dtype=torch.float32, device=gate_up.device)
-    N.call("fpb_swiglu_quantize", gate_up.data_ptr(), _dt(gate_up), rows, inter, packed.data_ptr(), sf.data_ptr(),
+    N.call("fpb_swiglu_quantize", gate_up.data_ptr(), _dt(gate_up), rows,
+           None if valid_rows is None else valid_rows.data_ptr(), inter, packed.data_ptr(), sf.data_ptr(),
            scal.data_ptr(), scal[1:].data_ptr(), _stream(gate_up, stream))
     return packed, sf, scal[:1]
 

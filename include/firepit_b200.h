@@ -280,17 +280,20 @@ int fpb_moe_layout(const int32_t *ids, size_t tokens, size_t width, size_t slots
 int fpb_moe_gather(const void *x, int x_dtype, size_t tokens, size_t cols, const int32_t *token_rows,
                    size_t rows, void *out, int out_dtype, void *stream);
 /* The gather fused with the NVFP4 activation quantize of fpb_nvfp4_quantize_act
- * (global from amax over x): packed [rows, cols/2], tiled factors, global. */
+ * (global from amax over x): packed [rows, cols/2], tiled factors, global.
+ * valid_rows (nullable device int32, e.g. fpb_moe_layout's padded_rows):
+ * rows at or past it are not written (their row tiles are skipped). */
 int fpb_moe_gather_quantize(const void *x, int x_dtype, size_t tokens, size_t cols, const int32_t *token_rows,
-                            size_t rows, uint8_t *packed, uint8_t *sf_tiled, float *global_out,
-                            float *amax_scratch, void *stream);
+                            size_t rows, const int32_t *valid_rows, uint8_t *packed, uint8_t *sf_tiled,
+                            float *global_out, float *amax_scratch, void *stream);
 /* swiglu (swiglu.rs:5-20): out [rows, inter] = gate / (1 + exp(-gate)) * up,
  * gate = gate_up[:, :inter], up = gate_up[:, inter:]. */
 int fpb_swiglu(const void *gate_up, int dtype, size_t rows, size_t inter, void *out, int out_dtype,
                void *stream);
-/* SwiGLU fused with the NVFP4 activation quantize (input of the down GEMM). */
-int fpb_swiglu_quantize(const void *gate_up, int dtype, size_t rows, size_t inter, uint8_t *packed,
-                        uint8_t *sf_tiled, float *global_out, float *amax_scratch, void *stream);
+/* SwiGLU fused with the NVFP4 activation quantize (input of the down GEMM);
+ * global from amax over the first valid_rows rows (nullable: all rows). */
+int fpb_swiglu_quantize(const void *gate_up, int dtype, size_t rows, const int32_t *valid_rows, size_t inter,
+                        uint8_t *packed, uint8_t *sf_tiled, float *global_out, float *amax_scratch, void *stream);
 /* combine / combine_prefill (moe.rs:91-109, 779-822): out [tokens, cols] =
  * sum over the first `slots` slots of weights[t, s] * routed[inverse[t, s]]
  * (routed [routed_rows, cols]; a row index outside it adds nothing). */

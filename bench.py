@@ -47,9 +47,10 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--config", choices=["gemv", "nvfp4_gemm_m128", "nvfp4_gemm_m2048", "fp8_gemm", "moe_t4096",
-                                        "moe_t64"], default="gemv",
+                                        "moe_t64", "moe_ep"], default="gemv",
                    help="gemv: config 0 (default); nvfp4_gemm_m*: config 2 GEMM at M=128 / M=2048; "
-                        "fp8_gemm: config 1; moe_t*: config 3 MoE layer at T=4096 / T=64")
+                        "fp8_gemm: config 1; moe_t*: config 3 MoE layer at T=4096 / T=64; "
+                        "moe_ep: config 3 expert-parallel over the ranks (NCCL all-to-all), T=4096 per rank")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the cpu_baseline sample")
     return p.parse_args()
 
@@ -905,13 +906,13 @@ def moe_arm(args):
         N_.call("fpb_moe_layout", b["ids"].data_ptr(), T, width, MOE_K, MOE_E, 128, cap, b["tr"].data_ptr(),
                 b["te"].data_ptr(), b["inv"].data_ptr(), b["rg"].data_ptr(), b["pad"].data_ptr(), sh)
         N_.call("fpb_moe_gather_quantize", xin.data_ptr(), BF, T, MOE_H, b["tr"].data_ptr(), cap, b["pad"].data_ptr(),
-                b["a1"].data_ptr(), b["sf1"].data_ptr(), b["scal"].data_ptr(), b["scal"][1:].data_ptr(), sh)
+                b["a1"].data_ptr(), b["sf1"].data_ptr(), b["scal"].data_ptr(), b["scal"][1:].data_ptr(), 0, sh)
         mark(2)
         N_.call("fpb_nvfp4_grouped_gemm_q", W1.handle, b["a1"].data_ptr(), b["sf1"].data_ptr(), b["scal"].data_ptr(),
                 cap, b["te"].data_ptr(), 2 * MOE_I, b["y1"].data_ptr(), BF, sh)
         mark(3)
         N_.call("fpb_swiglu_quantize", b["y1"].data_ptr(), BF, cap, b["pad"].data_ptr(), MOE_I, b["a2"].data_ptr(),
-                b["sf2"].data_ptr(), b["scal"][2:].data_ptr(), b["scal"][3:].data_ptr(), sh)
+                b["sf2"].data_ptr(), b["scal"][2:].data_ptr(), b["scal"][3:].data_ptr(), 0, sh)
         mark(4)
         N_.call("fpb_nvfp4_grouped_gemm_q", W2.handle, b["a2"].data_ptr(), b["sf2"].data_ptr(),
                 b["scal"][2:].data_ptr(), cap, b["te"].data_ptr(), MOE_H, b["y2"].data_ptr(), BF, sh)
@@ -994,9 +995,108 @@ def moe_arm(args):
     del graph
 
 
+def moe_ep_arm(args):
+    """Config 3 expert-parallel: E=512 experts split over the ranks (64 per GPU
+    at 8), T=4096 tokens per rank (weak scaling), NCCL all-to-all dispatch and
+    combine (firepit_b200.ep); activation globals all-reduced so every rank
+    encodes like the single-GPU layer.  Eager launches: the per-destination
+    counts are read by the host to size the all-to-all splits."""
+    import torch
+    import torch.distributed as dist
+
+    import firepit_b200 as F
+    from firepit_b200.ep import DeviceOps, ep_moe_forward
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    T = 4096
+    per = MOE_E // world
+    e0 = rank * per
+    gp = torch.empty(per * 2 * MOE_I, MOE_H // 2, dtype=torch.uint8, device=dev)
+    gs = torch.empty(per * 2 * MOE_I, MOE_H // 16, dtype=torch.uint8, device=dev)
+    gg = torch.empty(per * 2 * MOE_I, dtype=torch.float32, device=dev)
+    dp = torch.empty(per * MOE_H, MOE_I // 2, dtype=torch.uint8, device=dev)
+    ds = torch.empty(per * MOE_H, MOE_I // 16, dtype=torch.uint8, device=dev)
+    dg = torch.empty(per * MOE_H, dtype=torch.float32, device=dev)
+    chunk = min(64, per)
+    for c0 in range(0, per, chunk):
+        g = torch.empty(chunk, 2 * MOE_I, MOE_H, device=dev)
+        d = torch.empty(chunk, MOE_H, MOE_I, device=dev)
+        for j in range(chunk):
+            F.synth_normal(g[j].shape, seed=0, stream_id=1000 + e0 + c0 + j, std=0.02, out=g[j])
+            F.synth_normal(d[j].shape, seed=0, stream_id=5000 + e0 + c0 + j, std=0.02, out=d[j])
+        a, b_, c = F.quantize_nvfp4(g.view(-1, MOE_H), 2 * MOE_I)
+        gp[c0 * 2 * MOE_I:(c0 + chunk) * 2 * MOE_I], gs[c0 * 2 * MOE_I:(c0 + chunk) * 2 * MOE_I] = a, b_
+        gg[c0 * 2 * MOE_I:(c0 + chunk) * 2 * MOE_I] = c
+        a, b_, c = F.quantize_nvfp4(d.view(-1, MOE_I), MOE_H)
+        dp[c0 * MOE_H:(c0 + chunk) * MOE_H], ds[c0 * MOE_H:(c0 + chunk) * MOE_H], dg[c0 * MOE_H:(c0 + chunk) * MOE_H] = (
+            a, b_, c)
+        del g, d
+    W1 = F.Nvfp4Matrix.from_device(gp, gs, gg, per * 2 * MOE_I, MOE_H)
+    W2 = F.Nvfp4Matrix.from_device(dp, ds, dg, per * MOE_H, MOE_I)
+    del gp, gs, gg, dp, ds, dg
+    wr = F.synth_normal((MOE_E, MOE_H), seed=0, stream_id=99, std=0.02, dtype=torch.bfloat16, device=dev)
+    x = F.synth_normal((T, MOE_H), seed=rank, stream_id=0, dtype=torch.bfloat16, device=dev)
+    ops = DeviceOps(dev)
+
+    def step():
+        logits = torch.mm(x, wr.t(), out_dtype=torch.float32)
+        return ep_moe_forward(ops, x, logits, MOE_K, MOE_E, W1, W2, world=world)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    assert F.device_error() == 0
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches = F.launch_count()
+    with ClockSampler(local) as clocks:
+        start.record()
+        for _ in range(args.steps):
+            step()
+        end.record()
+        torch.cuda.synchronize()
+    launches = F.launch_count() - launches
+    t = torch.tensor([start.elapsed_time(end)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = t.item() / args.steps
+    flops = world * moe_flops(T)
+    value = flops / (ms * 1e-3) / 1e12
+    nbytes = world * moe_bytes(T, per)
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    achieved = nbytes / world / (ms * 1e-3) / 1e9
+    if rank == 0:
+        emit({"metric": "NVFP4 MoE layer TFLOPS", "value": value, "unit": "TFLOP/s", "n_gpus": world,
+              "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+              "scaling": "weak", "vs_baseline": None,
+              "dtype": "nvfp4 x nvfp4 experts (f32 accumulate), bf16 router and dispatch",
+              "data": "synthetic (seeded Philox: W N(0,0.02) per expert, x N(0,1) per rank)",
+              "config": {"workload": f"config3 MoE E=512 top-10 H=2048 I=512, T=4096 per rank, EP x{world}",
+                         "experts_per_gpu": per, "parallelism": f"EP x{world} + NCCL all-to-all" if world > 1
+                         else "single GPU (no exchange)",
+                         "l2": "inputs larger than L2 (all local experts' weights per step)"},
+              "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                           "traffic": None, "peak_kind": "measured hbm_gbs",
+                           "note": "per GPU: local experts' weights + router + x + y over the layer time"},
+              "e2e": None, "gpu_launches": launches, "clocks": clocks.summary()})
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
-    if args.config.startswith("moe_"):
+    if args.config == "moe_ep":
+        (moe_reference_arm if args.impl == "reference" else moe_ep_arm)(args)
+    elif args.config.startswith("moe_"):
         (moe_reference_arm if args.impl == "reference" else moe_arm)(args)
     elif args.config == "fp8_gemm":
         (fp8_reference_arm if args.impl == "reference" else fp8_arm)(args)

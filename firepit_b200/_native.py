@@ -24,6 +24,7 @@ FPB_ERR_NO_DEVICE = 8
 
 FPB_F32 = 0
 FPB_BF16 = 1
+FPB_QUANT_AMAX_GIVEN = 1
 
 
 class FpbError(RuntimeError):
@@ -102,11 +103,15 @@ SIGNATURES: dict[str, tuple] = {
     "fpb_moe_topk": (i32, [vp, sz, vp, sz, sz, sz, sz, vp, vp, vp]),
     "fpb_moe_layout": (i32, [vp, sz, sz, sz, sz, sz, sz, vp, vp, vp, vp, vp, vp]),
     "fpb_moe_gather": (i32, [vp, i32, sz, sz, vp, sz, vp, i32, vp]),
-    "fpb_moe_gather_quantize": (i32, [vp, i32, sz, sz, vp, sz, vp, vp, vp, vp, vp, vp]),
+    "fpb_moe_gather_quantize": (i32, [vp, i32, sz, sz, vp, sz, vp, vp, vp, vp, vp, i32, vp]),
     "fpb_swiglu": (i32, [vp, i32, sz, sz, vp, i32, vp]),
-    "fpb_swiglu_quantize": (i32, [vp, i32, sz, vp, sz, vp, vp, vp, vp, vp]),
+    "fpb_swiglu_quantize": (i32, [vp, i32, sz, vp, sz, vp, vp, vp, vp, i32, vp]),
+    "fpb_act_amax": (i32, [vp, i32, sz, vp, i32, vp]),
+    "fpb_swiglu_amax": (i32, [vp, i32, sz, vp, sz, vp, i32, vp]),
     "fpb_moe_combine": (i32, [vp, i32, sz, sz, vp, vp, sz, sz, sz, vp, i32, vp]),
     "fpb_moe_combine_add_norm": (i32, [vp, i32, sz, sz, vp, vp, sz, sz, sz, vp, vp, C.c_float, vp, vp, vp]),
+    "fpb_moe_route_dest": (i32, [vp, sz, sz, sz, sz, vp, vp]),
+    "fpb_moe_route_meta": (i32, [vp, vp, sz, sz, sz, sz, sz, vp, vp]),
     "fpb_moe_dims_validate": (i32, [sz, sz, sz, sz, sz]),
     "fpb_expert_selection_validate": (i32, [vp, vp, sz, sz, sz]),
     "fpb_prefill_layout_max_padded_rows": (i32, [sz, sz, sz, sz, C.POINTER(sz)]),

@@ -30,7 +30,8 @@
 // (the promotion of per-block partial sums in f32, as in the reference's
 // per-part scale).  With row scales the tensor cores accumulate the whole K
 // range in TMEM.  Every mbarrier wait is bounded; a wait that gives up records
-// an error code (fpb_device_error) and ends its role.  No TMA multicast.
+// an error code (fpb_device_error) and ends its role.  Every TMA load lands in
+// the issuing CTA alone.
 #include <algorithm>
 #include <cstring>
 #include <mutex>

@@ -15,7 +15,7 @@
 //               accumulating in TMEM; tcgen05.commit frees the stage;
 //   warps 2-5   epilogue: tcgen05.ld of the f32 accumulator, times ga * g[n],
 //               stored as bf16 or f32.
-// No TMA load uses cluster multicast.
+// Every TMA load lands in the issuing CTA alone.
 //
 // Scale factors live in the tensor cores' tiled layout: for each 128-row
 // block and each 64-column block, 512 bytes with the factor of row r,

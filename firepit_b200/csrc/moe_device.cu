@@ -355,6 +355,29 @@ __global__ void combine_kernel(const R *routed, int routed_rows, size_t cols, co
   }
 }
 
+// Expert-parallel dispatch: the local expert id of every send row.  The send
+// order is the layout of the routes by destination rank (fpb_moe_layout with
+// ranks as "experts" and one-row tiles), so route (t, s) sits at row
+// inverse[t, s] and goes to rank ids[t, s] / per_rank.
+__global__ void moe_route_meta_kernel(const int32_t *ids, const int32_t *inverse, int tokens, int width, int slots,
+                                      int per_rank, int rows, int32_t *send_expert) {
+  const int n = tokens * slots;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const int t = i / slots, s = i % slots;
+    const int id = ids[(size_t)t * width + s], row = inverse[(size_t)t * width + s];
+    if (row >= 0 && row < rows) send_expert[row] = id % per_rank;
+  }
+}
+
+// Destination rank of every route: dest[t, s] = ids[t, s] / per_rank (slots
+// past `slots` copy 0).
+__global__ void moe_route_dest_kernel(const int32_t *ids, int tokens, int width, int slots, int per_rank,
+                                      int32_t *dest) {
+  const int n = tokens * width;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    dest[i] = (i % width) < slots ? ids[i] / per_rank : 0;
+}
+
 static unsigned stride_grid(size_t n) {
   size_t g = (n + 255) / 256, cap = (size_t)sm_count() * 8;
   return (unsigned)std::max<size_t>(1, std::min(g, cap));
@@ -461,21 +484,24 @@ extern "C" int fpb_moe_gather(const void *x, int x_dtype, size_t tokens, size_t 
 extern "C" int fpb_moe_gather_quantize(const void *x, int x_dtype, size_t tokens, size_t cols,
                                        const int32_t *token_rows, size_t rows, const int32_t *valid_rows,
                                        uint8_t *packed, uint8_t *sf_tiled, float *global_out, float *amax_scratch,
-                                       void *stream) {
+                                       int flags, void *stream) {
   if (!x || !token_rows || !packed || !sf_tiled || !global_out || !amax_scratch)
     return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_moe_gather_quantize: null pointer");
   if (tokens == 0 || rows == 0 || cols == 0 || cols % 32) return fail(FPB_ERR_SHAPE, "fpb_moe_gather_quantize: shape");
   cudaStream_t s = as_stream(stream);
   uint32_t *amax = reinterpret_cast<uint32_t *>(amax_scratch);
-  FPB_CUDA_TRY(cudaMemsetAsync(amax, 0, sizeof(uint32_t), s));
+  const bool given = flags & FPB_QUANT_AMAX_GIVEN;
+  if (!given) FPB_CUDA_TRY(cudaMemsetAsync(amax, 0, sizeof(uint32_t), s));
   // Factors of the K padding up to a multiple of 256 columns are read by the
   // tensor cores (times zero codes) and must be zero, not stale bytes.
   if (cols % 256) FPB_CUDA_TRY(cudaMemsetAsync(sf_tiled, 0, sf_tiled_bytes(rows, cols), s));
   return with_dtype(x_dtype, [&](auto tp) {
     using T = std::remove_const_t<std::remove_pointer_t<decltype(tp)>>;
     const T *xs = static_cast<const T *>(x);
-    act_amax_kernel<T><<<stride_grid(tokens * cols), 256, 0, s>>>(xs, tokens * cols, amax);
-    FPB_LAUNCH_CHECK("act_amax_kernel");
+    if (!given) {
+      act_amax_kernel<T><<<stride_grid(tokens * cols), 256, 0, s>>>(xs, tokens * cols, amax);
+      FPB_LAUNCH_CHECK("act_amax_kernel");
+    }
     GatherRows<T> src{xs, token_rows, cols, (int)tokens};
     rows_encode_kernel<<<stride_grid(rows * cols / 16), 256, 0, s>>>(src, rows, valid_rows, cols, amax, packed,
                                                                       sf_tiled, global_out);
@@ -506,20 +532,23 @@ extern "C" int fpb_swiglu(const void *gate_up, int dtype, size_t rows, size_t in
 
 extern "C" int fpb_swiglu_quantize(const void *gate_up, int dtype, size_t rows, const int32_t *valid_rows,
                                    size_t inter, uint8_t *packed, uint8_t *sf_tiled, float *global_out,
-                                   float *amax_scratch, void *stream) {
+                                   float *amax_scratch, int flags, void *stream) {
   if (!gate_up || !packed || !sf_tiled || !global_out || !amax_scratch)
     return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_swiglu_quantize: null pointer");
   if (rows == 0 || inter == 0 || inter % 32) return fail(FPB_ERR_SHAPE, "fpb_swiglu_quantize: shape");
   cudaStream_t s = as_stream(stream);
   uint32_t *amax = reinterpret_cast<uint32_t *>(amax_scratch);
-  FPB_CUDA_TRY(cudaMemsetAsync(amax, 0, sizeof(uint32_t), s));
+  const bool given = flags & FPB_QUANT_AMAX_GIVEN;
+  if (!given) FPB_CUDA_TRY(cudaMemsetAsync(amax, 0, sizeof(uint32_t), s));
   if (inter % 256) FPB_CUDA_TRY(cudaMemsetAsync(sf_tiled, 0, sf_tiled_bytes(rows, inter), s));
   return with_dtype(dtype, [&](auto tp) {
     using T = std::remove_const_t<std::remove_pointer_t<decltype(tp)>>;
     SwigluRows<T> src{static_cast<const T *>(gate_up), inter};
     const unsigned grid = stride_grid(rows * inter / 16);
-    rows_amax_kernel<<<grid, 256, 0, s>>>(src, rows, valid_rows, inter, amax);
-    FPB_LAUNCH_CHECK("rows_amax_kernel(swiglu)");
+    if (!given) {
+      rows_amax_kernel<<<grid, 256, 0, s>>>(src, rows, valid_rows, inter, amax);
+      FPB_LAUNCH_CHECK("rows_amax_kernel(swiglu)");
+    }
     rows_encode_kernel<<<grid, 256, 0, s>>>(src, rows, valid_rows, inter, amax, packed, sf_tiled, global_out);
     FPB_LAUNCH_CHECK("rows_encode_kernel(swiglu)");
     return (int)FPB_OK;
@@ -566,4 +595,59 @@ extern "C" int fpb_moe_combine_add_norm(const void *routed, int r_dtype, size_t 
   if (!residual || !gamma || !normed) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_moe_combine_add_norm: null pointer");
   return combine_impl(routed, r_dtype, routed_rows, cols, inverse, weights, tokens, width, slots, residual, gamma,
                       eps, out, FPB_F32, normed, as_stream(stream));
+}
+
+extern "C" int fpb_moe_route_meta(const int32_t *ids, const int32_t *inverse, size_t tokens, size_t width,
+                                  size_t slots, size_t experts_per_rank, size_t rows, int32_t *send_expert,
+                                  void *stream) {
+  if (!ids || !inverse || !send_expert) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_moe_route_meta: null pointer");
+  if (tokens == 0 || slots == 0 || slots > width || experts_per_rank == 0 || tokens * width > 0x7fffffffu ||
+      rows > 0x7fffffffu)
+    return fail(FPB_ERR_SHAPE, "fpb_moe_route_meta: shape");
+  moe_route_meta_kernel<<<stride_grid(tokens * slots), 256, 0, as_stream(stream)>>>(
+      ids, inverse, (int)tokens, (int)width, (int)slots, (int)experts_per_rank, (int)rows, send_expert);
+  FPB_LAUNCH_CHECK("moe_route_meta_kernel");
+  return FPB_OK;
+}
+
+extern "C" int fpb_moe_route_dest(const int32_t *ids, size_t tokens, size_t width, size_t slots,
+                                  size_t experts_per_rank, int32_t *dest, void *stream) {
+  if (!ids || !dest) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_moe_route_dest: null pointer");
+  if (tokens == 0 || slots == 0 || slots > width || experts_per_rank == 0 || tokens * width > 0x7fffffffu)
+    return fail(FPB_ERR_SHAPE, "fpb_moe_route_dest: shape");
+  moe_route_dest_kernel<<<stride_grid(tokens * width), 256, 0, as_stream(stream)>>>(
+      ids, (int)tokens, (int)width, (int)slots, (int)experts_per_rank, dest);
+  FPB_LAUNCH_CHECK("moe_route_dest_kernel");
+  return FPB_OK;
+}
+
+extern "C" int fpb_act_amax(const void *x, int dtype, size_t n, float *amax_scratch, int accumulate, void *stream) {
+  if (!x || !amax_scratch) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_act_amax: null pointer");
+  cudaStream_t s = as_stream(stream);
+  uint32_t *amax = reinterpret_cast<uint32_t *>(amax_scratch);
+  if (!accumulate) FPB_CUDA_TRY(cudaMemsetAsync(amax, 0, sizeof(uint32_t), s));
+  if (n == 0) return FPB_OK;
+  return with_dtype(dtype, [&](auto tp) {
+    using T = std::remove_const_t<std::remove_pointer_t<decltype(tp)>>;
+    act_amax_kernel<T><<<stride_grid(n), 256, 0, s>>>(static_cast<const T *>(x), n, amax);
+    FPB_LAUNCH_CHECK("act_amax_kernel");
+    return (int)FPB_OK;
+  });
+}
+
+extern "C" int fpb_swiglu_amax(const void *gate_up, int dtype, size_t rows, const int32_t *valid_rows, size_t inter,
+                               float *amax_scratch, int accumulate, void *stream) {
+  if (!gate_up || !amax_scratch) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_swiglu_amax: null pointer");
+  if (inter == 0 || inter % 16) return fail(FPB_ERR_SHAPE, "fpb_swiglu_amax: shape");
+  cudaStream_t s = as_stream(stream);
+  uint32_t *amax = reinterpret_cast<uint32_t *>(amax_scratch);
+  if (!accumulate) FPB_CUDA_TRY(cudaMemsetAsync(amax, 0, sizeof(uint32_t), s));
+  if (rows == 0) return FPB_OK;
+  return with_dtype(dtype, [&](auto tp) {
+    using T = std::remove_const_t<std::remove_pointer_t<decltype(tp)>>;
+    SwigluRows<T> src{static_cast<const T *>(gate_up), inter};
+    rows_amax_kernel<<<stride_grid(rows * inter / 16), 256, 0, s>>>(src, rows, valid_rows, inter, amax);
+    FPB_LAUNCH_CHECK("rows_amax_kernel(swiglu)");
+    return (int)FPB_OK;
+  });
 }

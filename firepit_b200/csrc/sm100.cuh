@@ -1,5 +1,5 @@
 // Thin wrappers over the sm_100a PTX used by the tensor-core kernels:
-// mbarriers, TMA (cp.async.bulk.tensor, no multicast), 1-D bulk copies,
+// mbarriers, TMA (cp.async.bulk.tensor, each load into its own CTA), 1-D bulk copies,
 // tcgen05 (TMEM alloc, MMA, commit, cp, ld) and shared-memory matrix
 // descriptors.  Every wait is bounded: after kSpinLimit polls it gives up and
 // reports failure, so a lost arrival ends a kernel with an error flag instead
@@ -65,7 +65,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
   return false;
 }
 
-// ---- TMA and bulk copies (no multicast) -------------------------------------------
+// ---- TMA and bulk copies (each into the issuing CTA only) ---------------------------
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y,
                                             uint64_t *bar) {
   asm volatile(

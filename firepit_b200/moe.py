@@ -305,7 +305,7 @@ def gather_quantize(x, plan: PrefillPlan, stream=None):
     sf = torch.empty(int(N.lib.fpb_nvfp4_act_sf_bytes(plan.cap, h)), dtype=torch.uint8, device=x.device)
     scal = torch.empty(2, dtype=torch.float32, device=x.device)
     N.call("fpb_moe_gather_quantize", x.data_ptr(), _dt(x), tokens, h, plan.token_rows.data_ptr(), plan.cap,
-           plan.padded_rows_dev.data_ptr(), packed.data_ptr(), sf.data_ptr(), scal.data_ptr(), scal[1:].data_ptr(),
+           plan.padded_rows_dev.data_ptr(), packed.data_ptr(), sf.data_ptr(), scal.data_ptr(), scal[1:].data_ptr(), 0,
            _stream(x, stream))
     return packed, sf, scal[:1]
 
@@ -330,7 +330,7 @@ def swiglu_quantize(gate_up, stream=None, valid_rows=None):
     scal = torch.empty(2, dtype=torch.float32, device=gate_up.device)
     N.call("fpb_swiglu_quantize", gate_up.data_ptr(), _dt(gate_up), rows,
            None if valid_rows is None else valid_rows.data_ptr(), inter, packed.data_ptr(), sf.data_ptr(),
-           scal.data_ptr(), scal[1:].data_ptr(), _stream(gate_up, stream))
+           scal.data_ptr(), scal[1:].data_ptr(), 0, _stream(gate_up, stream))
     return packed, sf, scal[:1]
 
 

@@ -46,6 +46,12 @@ enum {
 
 enum { FPB_F32 = 0, FPB_BF16 = 1 };
 
+/* Quantizer flags: FPB_QUANT_AMAX_GIVEN = the amax scratch already holds the
+ * |x| maximum (float bits) to derive the global from, e.g. reduced over ranks
+ * (fpb_act_amax / fpb_swiglu_amax, then an all-reduce MAX), so that every
+ * rank encodes with the same global. */
+enum { FPB_QUANT_AMAX_GIVEN = 1 };
+
 /* Library / error reporting ------------------------------------------------ */
 const char *fpb_version(void);
 const char *fpb_status_string(int status);
@@ -285,7 +291,7 @@ int fpb_moe_gather(const void *x, int x_dtype, size_t tokens, size_t cols, const
  * rows at or past it are not written (their row tiles are skipped). */
 int fpb_moe_gather_quantize(const void *x, int x_dtype, size_t tokens, size_t cols, const int32_t *token_rows,
                             size_t rows, const int32_t *valid_rows, uint8_t *packed, uint8_t *sf_tiled,
-                            float *global_out, float *amax_scratch, void *stream);
+                            float *global_out, float *amax_scratch, int flags, void *stream);
 /* swiglu (swiglu.rs:5-20): out [rows, inter] = gate / (1 + exp(-gate)) * up,
  * gate = gate_up[:, :inter], up = gate_up[:, inter:]. */
 int fpb_swiglu(const void *gate_up, int dtype, size_t rows, size_t inter, void *out, int out_dtype,
@@ -293,7 +299,13 @@ int fpb_swiglu(const void *gate_up, int dtype, size_t rows, size_t inter, void *
 /* SwiGLU fused with the NVFP4 activation quantize (input of the down GEMM);
  * global from amax over the first valid_rows rows (nullable: all rows). */
 int fpb_swiglu_quantize(const void *gate_up, int dtype, size_t rows, const int32_t *valid_rows, size_t inter,
-                        uint8_t *packed, uint8_t *sf_tiled, float *global_out, float *amax_scratch, void *stream);
+                        uint8_t *packed, uint8_t *sf_tiled, float *global_out, float *amax_scratch, int flags,
+                        void *stream);
+/* |x| maximum over x[0, n) (f32/bf16) or over SwiGLU(gate_up) rows, as float
+ * bits in *amax_scratch (zeroed first unless accumulate != 0). */
+int fpb_act_amax(const void *x, int dtype, size_t n, float *amax_scratch, int accumulate, void *stream);
+int fpb_swiglu_amax(const void *gate_up, int dtype, size_t rows, const int32_t *valid_rows, size_t inter,
+                    float *amax_scratch, int accumulate, void *stream);
 /* combine / combine_prefill (moe.rs:91-109, 779-822): out [tokens, cols] =
  * sum over the first `slots` slots of weights[t, s] * routed[inverse[t, s]]
  * (routed [routed_rows, cols]; a row index outside it adds nothing). */
@@ -306,6 +318,18 @@ int fpb_moe_combine_add_norm(const void *routed, int r_dtype, size_t routed_rows
                              const int32_t *inverse, const float *weights, size_t tokens, size_t width,
                              size_t slots, const float *residual, const float *gamma, float eps, float *out,
                              float *normed, void *stream);
+
+/* Expert-parallel dispatch (no reference counterpart: the reference runs on
+ * one GPU).  Experts are sharded `experts_per_rank` per rank.
+ * fpb_moe_route_dest: dest [tokens, width] = ids / experts_per_rank (first
+ * `slots` slots, 0 after).  Laying dest out with fpb_moe_layout (ranks as
+ * experts, tile_rows 1) gives the send order and its `inverse`; then
+ * fpb_moe_route_meta writes send_expert[inverse[t, s]] = ids[t, s] %
+ * experts_per_rank (the receiver's local expert id; rows >= `rows` skipped). */
+int fpb_moe_route_dest(const int32_t *ids, size_t tokens, size_t width, size_t slots, size_t experts_per_rank,
+                       int32_t *dest, void *stream);
+int fpb_moe_route_meta(const int32_t *ids, const int32_t *inverse, size_t tokens, size_t width, size_t slots,
+                       size_t experts_per_rank, size_t rows, int32_t *send_expert, void *stream);
 
 /* ---- MoE host bookkeeping (no GPU needed) -------------------------------- */
 /* MoeDims::new (moe.rs:172-225): FPB_ERR_SHAPE on invalid dimensions. */

@@ -1,0 +1,84 @@
+"""Expert-parallel MoE on 2 GPUs over NCCL (skipped with fewer GPUs).
+
+Two ranks, 16 experts (8 per rank), top-4, each rank routing its own 300
+tokens.  The quantizers' globals are all-reduced over the ranks, so each
+rank's output must equal, bit for bit, the single-GPU layer run over both
+ranks' tokens with all experts (NVLS is kept off; collectives use a short
+timeout)."""
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+E, K, H, I, T = 16, 4, 256, 128, 300
+
+
+def _rank(rank, world, port, q):
+    sys.path[:0] = [ROOT, HERE]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    import firepit_b200 as F
+    from firepit_b200.ep import DeviceOps, ep_moe_forward
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    try:
+        w1 = F.synth_normal((E * 2 * I, H), seed=1, stream_id=1, std=0.02, device=dev)
+        w2 = F.synth_normal((E * H, I), seed=2, stream_id=1, std=0.02, device=dev)
+        p1, s1, g1 = F.quantize_nvfp4(w1, 2 * I)
+        p2, s2, g2 = F.quantize_nvfp4(w2, H)
+        per = E // world
+        r1 = slice(rank * per * 2 * I, (rank + 1) * per * 2 * I)
+        r2 = slice(rank * per * H, (rank + 1) * per * H)
+        L1 = F.Nvfp4Matrix.from_device(p1[r1].contiguous(), s1[r1].contiguous(), g1[r1].contiguous(), per * 2 * I, H)
+        L2 = F.Nvfp4Matrix.from_device(p2[r2].contiguous(), s2[r2].contiguous(), g2[r2].contiguous(), per * H, I)
+        A1 = F.Nvfp4Matrix.from_device(p1, s1, g1, E * 2 * I, H)
+        A2 = F.Nvfp4Matrix.from_device(p2, s2, g2, E * H, I)
+        x_all = F.synth_normal((world * T, H), seed=0, stream_id=0, dtype=torch.bfloat16, device=dev)
+        lg_all = F.synth_normal((world * T, E), seed=0, stream_id=7, device=dev)
+        rows = slice(rank * T, (rank + 1) * T)
+        ops = DeviceOps(dev)
+        y_ep = ep_moe_forward(ops, x_all[rows].contiguous(), lg_all[rows].contiguous(), K, E, L1, L2)
+        y_one = ep_moe_forward(ops, x_all, lg_all, K, E, A1, A2, world=1)[rows]
+        torch.cuda.synchronize()
+        q.put((rank, F.device_error(), y_ep.float().cpu().numpy().tobytes(), y_one.float().cpu().numpy().tobytes()))
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_expert_parallel_two_gpus_matches_single_gpu():
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, err, ep, one in results:
+        a = np.frombuffer(ep, np.float32)
+        b = np.frombuffer(one, np.float32)
+        assert err == 0
+        assert np.all(np.isfinite(a)) and np.abs(b).max() > 0
+        assert np.array_equal(a, b), f"rank {rank}: max diff {np.abs(a - b).max()}"

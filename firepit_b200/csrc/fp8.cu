@@ -21,8 +21,9 @@
 //    256 x 128-byte B tile per 128-wide K block (128-byte swizzle);
 //  * warp 1: TMEM allocation and MMA issue, four
 //    tcgen05.mma.cta_group::1.kind::f8f6f4 (M 128, N 256, K 32) per K block;
-//  * warps 2..9: epilogue, two warps per 32-lane TMEM quadrant (128 columns
-//    each).
+//  * warps 4..11: epilogue, two warps per 32-lane TMEM quadrant (128 columns
+//    each), with the registers of warpgroup 0 (setmaxnreg) so that each TMEM
+//    load overlaps the previous chunk's scale-and-add.
 // Block scales vary along K every 128 columns, so with block scaling each K
 // block's product goes to one of two TMEM accumulators (double-buffered): the
 // epilogue warps read it, multiply it by that block's scale and add it to
@@ -102,8 +103,13 @@ constexpr int kF8BN = 256;                        // N of a tile
 constexpr int kF8Stages = 4;
 constexpr int kF8ABytes = kF8Tile * kF8Tile;      // 16 KB of A per stage
 constexpr int kF8BBytes = kF8BN * kF8Tile;        // 32 KB of B per stage
-constexpr int kF8EpiWarps = 8;
-constexpr int kF8Threads = 64 + 32 * kF8EpiWarps;
+constexpr int kF8EpiWarps = 8;                    // warpgroups 1 and 2
+constexpr int kF8Threads = 128 + 32 * kF8EpiWarps;  // warpgroup 0: producer, MMA, two idle warps
+// Register split (setmaxnreg): the launch gives every thread 168; warpgroup 0
+// drops to 56 and the epilogue warpgroups take the rest (128*56 + 256*224 =
+// 384*168), enough for a row's 128 f32 sums plus two 32-register TMEM buffers.
+constexpr int kF8CtrlRegs = 56, kF8EpiRegs = 224;
+static_assert(128 * kF8CtrlRegs + 32 * kF8EpiWarps * kF8EpiRegs <= kF8Threads * 168, "register split");
 constexpr uint32_t kF8TmemCols = 512;             // two 256-column accumulators
 constexpr size_t kF8Smem = 1024 + kF8Stages * (kF8ABytes + kF8BBytes) + 256;
 
@@ -182,6 +188,8 @@ __global__ void __launch_bounds__(kF8Threads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_base_s;
 
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kF8CtrlRegs));
   if (warp == 0) {
     // ---- TMA producer ----------------------------------------------------------
     if (elect_one()) {
@@ -231,10 +239,13 @@ __global__ void __launch_bounds__(kF8Threads, 1)
       }
       if (!kBlocks && ok) tc_commit(&acc_full[0]);
     }
+  }
   } else {
-    // ---- epilogue: quadrant (warp % 4), column half (warp - 2) / 4 -------------
-    constexpr int kCols = kF8BN / 2;  // columns per epilogue warp
-    const int qd = warp & 3, half = (warp - 2) >> 2;
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kF8EpiRegs));
+    // ---- epilogue: quadrant (warp % 4), column part (warp - 4) / 4 -------------
+    constexpr int kParts = kF8EpiWarps / 4;
+    constexpr int kCols = kF8BN / kParts;  // columns per epilogue warp
+    const int qd = warp & 3, half = (warp - 4) >> 2;
     const int row = m0 + qd * 32 + lane;
     const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
     const int c_base = half * kCols;
@@ -247,7 +258,7 @@ __global__ void __launch_bounds__(kF8Threads, 1)
     // huge) do not overflow or underflow in between.
     const float as = row < p.M ? __ldg(p.a_scale + row) : 0.0f;
     if (kBlocks) {
-      // A half's 128 columns lie in one block of bn (a multiple of 128) rows.
+      // A part's columns lie in one block of bn (a multiple of 128) rows.
       const int nb = (n_base + n0 + c_base) / p.bn;
       const float *ws_row = p.w_scale + (size_t)nb * p.ws_cols;
       for (int kb = 0; kb < p.kb_count; ++kb) {
@@ -259,14 +270,26 @@ __global__ void __launch_bounds__(kF8Threads, 1)
         }
         tc_fence_after();
         const float ws = __ldg(ws_row + (kb * kF8Tile) / p.bk) * as;
+        const uint32_t taddr = tmem + lane_base + b * kF8BN + c_base;
+        // Each chunk's TMEM load overlaps the previous chunk's scale-and-add.
+        static_assert(kCols == 128, "four 32-column chunks per epilogue warp");
+        uint32_t ra[32], rb[32];
+        tmem_ld32(taddr, ra);
+        tmem_ld_wait(ra);
+        tmem_ld32(taddr + 32, rb);
 #pragma unroll
-        for (int c = 0; c < kCols / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(tmem + lane_base + b * kF8BN + c_base + c * 32, r);
-          tmem_ld_wait();
+        for (int j = 0; j < 32; ++j) acc[j] = fmaf(__uint_as_float(ra[j]), ws, acc[j]);
+        tmem_ld_wait(rb);
+        tmem_ld32(taddr + 64, ra);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) acc[c * 32 + j] = fmaf(__uint_as_float(r[j]), ws, acc[c * 32 + j]);
-        }
+        for (int j = 0; j < 32; ++j) acc[32 + j] = fmaf(__uint_as_float(rb[j]), ws, acc[32 + j]);
+        tmem_ld_wait(ra);
+        tmem_ld32(taddr + 96, rb);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[64 + j] = fmaf(__uint_as_float(ra[j]), ws, acc[64 + j]);
+        tmem_ld_wait(rb);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[96 + j] = fmaf(__uint_as_float(rb[j]), ws, acc[96 + j]);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[b]);
@@ -278,7 +301,7 @@ __global__ void __launch_bounds__(kF8Threads, 1)
         for (int c = 0; c < kCols / 32; ++c) {
           uint32_t r[32];
           tmem_ld32(tmem + lane_base + c_base + c * 32, r);
-          tmem_ld_wait();
+          tmem_ld_wait(r);
 #pragma unroll
           for (int j = 0; j < 32; ++j) acc[c * 32 + j] = __uint_as_float(r[j]);
         }

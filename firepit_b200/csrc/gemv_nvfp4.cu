@@ -472,7 +472,7 @@ __device__ __forceinline__ void stream_issue(const StreamArgs &a, uint8_t *stage
 
 template <bool XLO>
 __global__ void __launch_bounds__(256, 2) gemv_nvfp4_stream_kernel(StreamArgs a) {
-  extern __shared__ __align__(128) unsigned char smem[];
+  extern __shared__ __align__(16) unsigned char smem[];
   const int S = a.stages;
   uint8_t *stages = smem;
   __half *xh = reinterpret_cast<__half *>(smem + (size_t)S * a.stage_bytes);

@@ -124,7 +124,10 @@ struct GemmParams {
 
 constexpr int kTileBytes = kBM * kBKBytes;   // 16 KB per operand per stage
 constexpr int kSfStageBytes = 4 * kSfChunk;  // 2 KB per operand per stage
-constexpr uint32_t kTmemCols = 256;          // accumulator 128 + SFA 64 + SFB 64
+// TMEM: two 128-column accumulators (tiles alternate), then per stage 16
+// columns of A factors (256..319) and 16 of B factors (320..383).
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemSfa = 256, kTmemSfb = 320;
 constexpr size_t kGemmSmem = 1024 + kStages * (2 * kTileBytes + 2 * kSfStageBytes) + 256;
 
 __device__ __forceinline__ void report(int *error, volatile int *abort, int code) {
@@ -132,6 +135,30 @@ __device__ __forceinline__ void report(int *error, volatile int *abort, int code
   if (error) atomicCAS(error, 0, code);
 }
 
+// Tile t of the launch: m-major over (m_tiles, n_tiles); false when it is a
+// grouped row tile past the layout's end (expert -1), which every role skips.
+// A malformed expert id records device error 106 and is skipped too.
+__device__ __forceinline__ bool gemm_tile(const GemmParams &p, int t, int n_tiles, int &m_tile, int &n_tile,
+                                          int &n_base) {
+  m_tile = t / n_tiles;
+  n_tile = t - m_tile * n_tiles;
+  n_base = p.n_base;
+  if (p.tile_experts) {
+    const int e = p.tile_experts[m_tile];
+    if (e == -1) return false;
+    if (e < 0 || e >= p.n_experts) {
+      if (threadIdx.x == 0 && p.error) atomicCAS(p.error, 0, 106);
+      return false;
+    }
+    n_base = e * p.N;
+  }
+  return true;
+}
+
+// Persistent: one CTA per SM walks the tiles t = blockIdx.x, + gridDim.x, ...
+// The producer and the MMA issuer share one ring counter across tiles; the
+// accumulator alternates between two TMEM buffers, so the epilogue of one
+// tile overlaps the main loop of the next.
 __global__ void __launch_bounds__(192, 1)
     nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                       GemmParams p) {
@@ -144,23 +171,14 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t *sSFB = sSFA + kStages * kSfStageBytes;
   uint64_t *full = reinterpret_cast<uint64_t *>(sSFB + kStages * kSfStageBytes);
   uint64_t *empty = full + kStages;
-  uint64_t *tmem_full = empty + kStages;
-  uint32_t *tmem_base_s = reinterpret_cast<uint32_t *>(tmem_full + 1);
+  uint64_t *acc_full = empty + kStages;  // [2]
+  uint64_t *acc_empty = acc_full + 2;    // [2]
+  uint32_t *tmem_base_s = reinterpret_cast<uint32_t *>(acc_empty + 2);
   volatile int *abort_s = reinterpret_cast<volatile int *>(tmem_base_s + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_tile = blockIdx.x, m_tile = blockIdx.y;
-  const int m0 = m_tile * kBM, n0 = n_tile * kBN;
-  int n_base = p.n_base;
-  if (p.tile_experts) {
-    const int e = p.tile_experts[m_tile];
-    if (e == -1) return;  // a row tile past the end of a device-built layout
-    if (e < 0 || e >= p.n_experts) {  // a malformed layout: leave this tile, report it
-      if (threadIdx.x == 0) atomicCAS(p.error, 0, 106);
-      return;
-    }
-    n_base = e * p.N;
-  }
+  const int n_tiles = (p.N + kBN - 1) / kBN, m_tiles = (p.M + kBM - 1) / kBM;
+  const int total = n_tiles * m_tiles;
   const int kb64_per_rb = p.kb_count * 4;
 
   if (threadIdx.x == 0) {
@@ -168,7 +186,10 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(tmem_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
     *abort_s = 0;
     fence_barrier_init();
     prefetch_tensormap(&tmap_a);
@@ -182,118 +203,153 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_base_s;
-  const uint32_t tmem_acc = tmem;
-  auto tmem_sfa = [&](int s, int kk) { return tmem + 128 + s * 16 + kk * 4; };
-  auto tmem_sfb = [&](int s, int kk) { return tmem + 192 + s * 16 + kk * 4; };
 
   if (warp == 0) {
     // ---- TMA producer ----------------------------------------------------------
     if (elect_one()) {
-      const int nb_global = n_base / 128 + n_tile;
-      int issued = 0;
-      for (int kb = 0; kb < p.kb_count; ++kb) {
-        const int s = kb % kStages, round = kb / kStages;
-        if (kb >= kStages && !mbar_wait(&empty[s], (round - 1) & 1, abort_s)) {
-          report(p.error, abort_s, 101);
-          break;
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        int m_tile, n_tile, n_base;
+        if (!gemm_tile(p, t, n_tiles, m_tile, n_tile, n_base)) continue;
+        const int nb_global = n_base / 128 + n_tile;
+        for (int kb = 0; kb < p.kb_count; ++kb, ++it) {
+          const int s = it % kStages;
+          if (it >= kStages && !mbar_wait(&empty[s], ((it / kStages) - 1) & 1, abort_s)) {
+            report(p.error, abort_s, 101);
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], 2 * kTileBytes + 2 * kSfStageBytes);
+          tma_load_2d(sA + s * kTileBytes, &tmap_a, kb * kBKBytes, m_tile * kBM, &full[s]);
+          tma_load_2d(sB + s * kTileBytes, &tmap_b, kb * kBKBytes, n_base + n_tile * kBN, &full[s]);
+          bulk_load(sSFA + s * kSfStageBytes, p.a_sf + ((size_t)m_tile * kb64_per_rb + kb * 4) * kSfChunk,
+                    kSfStageBytes, &full[s]);
+          bulk_load(sSFB + s * kSfStageBytes, p.b_sf + ((size_t)nb_global * kb64_per_rb + kb * 4) * kSfChunk,
+                    kSfStageBytes, &full[s]);
         }
-        mbar_arrive_expect_tx(&full[s], 2 * kTileBytes + 2 * kSfStageBytes);
-        tma_load_2d(sA + s * kTileBytes, &tmap_a, kb * kBKBytes, m0, &full[s]);
-        tma_load_2d(sB + s * kTileBytes, &tmap_b, kb * kBKBytes, n_base + n0, &full[s]);
-        bulk_load(sSFA + s * kSfStageBytes, p.a_sf + ((size_t)m_tile * kb64_per_rb + kb * 4) * kSfChunk,
-                  kSfStageBytes, &full[s]);
-        bulk_load(sSFB + s * kSfStageBytes, p.b_sf + ((size_t)nb_global * kb64_per_rb + kb * 4) * kSfChunk,
-                  kSfStageBytes, &full[s]);
-        issued = kb + 1;
       }
       // Our own copies must have landed before the CTA may exit.
-      for (int kb = (issued > kStages ? issued - kStages : 0); kb < issued; ++kb)
-        if (!mbar_wait(&full[kb % kStages], (kb / kStages) & 1, abort_s)) report(p.error, abort_s, 102);
+      const uint32_t issued = it;
+      for (uint32_t j = (issued > kStages ? issued - kStages : 0); j < issued; ++j)
+        if (!mbar_wait(&full[j % kStages], (j / kStages) & 1, abort_s)) report(p.error, abort_s, 102);
     }
   } else if (warp == 1) {
     // ---- MMA issuer -------------------------------------------------------------
     if (elect_one()) {
       const uint32_t idesc = idesc_nvf4(kBM, kBN);
-      for (int kb = 0; kb < p.kb_count; ++kb) {
-        const int s = kb % kStages, round = kb / kStages;
-        if (!mbar_wait(&full[s], round & 1, abort_s)) {
-          report(p.error, abort_s, 103);
+      uint32_t it = 0, lt = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        int m_tile, n_tile, n_base;
+        if (!gemm_tile(p, t, n_tiles, m_tile, n_tile, n_base)) continue;
+        const uint32_t buf = lt & 1;
+        if (lt >= 2 && !mbar_wait(&acc_empty[buf], ((lt >> 1) - 1) & 1, abort_s)) {
+          report(p.error, abort_s, 107);
           break;
         }
         tc_fence_after();
+        const uint32_t tmem_acc = tmem + buf * kBN;
+        for (int kb = 0; kb < p.kb_count; ++kb, ++it) {
+          const int s = it % kStages;
+          if (!mbar_wait(&full[s], (it / kStages) & 1, abort_s)) {
+            report(p.error, abort_s, 103);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          tmem_cp_sf(tmem_sfa(s, kk), smem_desc(smem_u32(sSFA + s * kSfStageBytes + kk * kSfChunk), 0, 128, 0));
-          tmem_cp_sf(tmem_sfb(s, kk), smem_desc(smem_u32(sSFB + s * kSfStageBytes + kk * kSfChunk), 0, 128, 0));
-        }
+          for (int kk = 0; kk < 4; ++kk) {
+            tmem_cp_sf(tmem + kTmemSfa + s * 16 + kk * 4,
+                       smem_desc(smem_u32(sSFA + s * kSfStageBytes + kk * kSfChunk), 0, 128, 0));
+            tmem_cp_sf(tmem + kTmemSfb + s * 16 + kk * 4,
+                       smem_desc(smem_u32(sSFB + s * kSfStageBytes + kk * kSfChunk), 0, 128, 0));
+          }
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          const uint64_t a_desc = smem_desc(smem_u32(sA + s * kTileBytes) + kk * 32, 16, 1024, 2);
-          const uint64_t b_desc = smem_desc(smem_u32(sB + s * kTileBytes) + kk * 32, 16, 1024, 2);
-          mma_nvf4(tmem_acc, a_desc, b_desc, idesc, tmem_sfa(s, kk), tmem_sfb(s, kk), (kb | kk) != 0);
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t a_desc = smem_desc(smem_u32(sA + s * kTileBytes) + kk * 32, 16, 1024, 2);
+            const uint64_t b_desc = smem_desc(smem_u32(sB + s * kTileBytes) + kk * 32, 16, 1024, 2);
+            mma_nvf4(tmem_acc, a_desc, b_desc, idesc, tmem + kTmemSfa + s * 16 + kk * 4,
+                     tmem + kTmemSfb + s * 16 + kk * 4, (kb | kk) != 0);
+          }
+          tc_commit(&empty[s]);
         }
-        tc_commit(&empty[s]);
+        if (!ok) break;
+        tc_commit(&acc_full[buf]);
+        ++lt;
       }
-      tc_commit(tmem_full);
-      // Every MMA of this CTA has finished once tmem_full completes.
-      if (!mbar_wait(tmem_full, 0, abort_s)) report(p.error, abort_s, 104);
     }
   } else {
     // ---- epilogue: warps 2..5 cover TMEM lanes (warp % 4) * 32 .. +31 ---------
     const int qw = warp & 3;
-    const int row = m0 + qw * 32 + lane;
-    if (mbar_wait(tmem_full, 0, abort_s)) {
+    const uint32_t lane_base = (uint32_t)(qw * 32) << 16;
+    const float ga = __ldg(p.a_global);
+    uint32_t lt = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      int m_tile, n_tile, n_base;
+      if (!gemm_tile(p, t, n_tiles, m_tile, n_tile, n_base)) continue;
+      const uint32_t buf = lt & 1;
+      if (!mbar_wait(&acc_full[buf], (lt >> 1) & 1, abort_s)) {
+        report(p.error, abort_s, 105);
+        break;
+      }
       tc_fence_after();
-      const float ga = __ldg(p.a_global);
-#pragma unroll 1
-      for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tmem_acc + ((uint32_t)(qw * 32) << 16) + c * 32, r);
-        tmem_ld_wait();
+      // Drain the whole accumulator row into registers, free the buffer, then
+      // scale and store while the tensor cores fill the other buffer.
+      uint32_t r[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(tmem + lane_base + buf * kBN + c * 32, r[c]);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld_wait(r[c]);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      ++lt;
+      const int row = m_tile * kBM + qw * 32 + lane;
+      const int n0 = n_tile * kBN;
+      if (row >= p.M) continue;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
         const int nc = n0 + c * 32;
-        if (row < p.M) {
-          float v[32];
+        float v[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int n = nc + j;
-            const float g = n < p.N ? __ldg(p.b_globals + n_base + n) : 0.0f;
-            v[j] = (__uint_as_float(r[j]) * ga) * g;
-          }
-          const long long off = (long long)row * p.ldy + nc;
-          const bool full_cols = nc + 32 <= p.N;
-          if (p.y_bf16) {
-            __nv_bfloat16 *yp = reinterpret_cast<__nv_bfloat16 *>(p.y) + off;
-            if (full_cols && (reinterpret_cast<uintptr_t>(yp) & 15) == 0) {
+        for (int j = 0; j < 32; ++j) {
+          const int n = nc + j;
+          const float g = n < p.N ? __ldg(p.b_globals + n_base + n) : 0.0f;
+          v[j] = (__uint_as_float(r[c][j]) * ga) * g;
+        }
+        const long long off = (long long)row * p.ldy + nc;
+        const bool full_cols = nc + 32 <= p.N;
+        if (p.y_bf16) {
+          __nv_bfloat16 *yp = reinterpret_cast<__nv_bfloat16 *>(p.y) + off;
+          if (full_cols && (reinterpret_cast<uintptr_t>(yp) & 15) == 0) {
 #pragma unroll
-              for (int j = 0; j < 32; j += 8) {
-                uint4 pk;
-                pk.x = pack_bf16x2(v[j], v[j + 1]);
-                pk.y = pack_bf16x2(v[j + 2], v[j + 3]);
-                pk.z = pack_bf16x2(v[j + 4], v[j + 5]);
-                pk.w = pack_bf16x2(v[j + 6], v[j + 7]);
-                *reinterpret_cast<uint4 *>(yp + j) = pk;
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (nc + j < p.N) yp[j] = __float2bfloat16_rn(v[j]);
+            for (int j = 0; j < 32; j += 8) {
+              uint4 pk;
+              pk.x = pack_bf16x2(v[j], v[j + 1]);
+              pk.y = pack_bf16x2(v[j + 2], v[j + 3]);
+              pk.z = pack_bf16x2(v[j + 4], v[j + 5]);
+              pk.w = pack_bf16x2(v[j + 6], v[j + 7]);
+              *reinterpret_cast<uint4 *>(yp + j) = pk;
             }
           } else {
-            float *yp = reinterpret_cast<float *>(p.y) + off;
-            if (full_cols && (reinterpret_cast<uintptr_t>(yp) & 15) == 0) {
 #pragma unroll
-              for (int j = 0; j < 32; j += 4)
-                *reinterpret_cast<float4 *>(yp + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-            } else {
+            for (int j = 0; j < 32; ++j)
+              if (nc + j < p.N) yp[j] = __float2bfloat16_rn(v[j]);
+          }
+        } else {
+          float *yp = reinterpret_cast<float *>(p.y) + off;
+          if (full_cols && (reinterpret_cast<uintptr_t>(yp) & 15) == 0) {
 #pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (nc + j < p.N) yp[j] = v[j];
-            }
+            for (int j = 0; j < 32; j += 4)
+              *reinterpret_cast<float4 *>(yp + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (nc + j < p.N) yp[j] = v[j];
           }
         }
       }
-    } else {
-      report(p.error, abort_s, 105);
     }
   }
   tc_fence_before();
@@ -487,7 +543,8 @@ extern "C" int fpb_nvfp4_gemm_q(fpb_nvfp4_matrix *w, size_t row_begin, size_t ro
   p.n_base = (int)row_begin;
   p.kb_count = (int)((w->cols + 255) / 256);
   p.error = err;
-  dim3 grid((unsigned)((p.N + kBN - 1) / kBN), (unsigned)((m + kBM - 1) / kBM));
+  const size_t tiles = (size_t)((p.N + kBN - 1) / kBN) * ((m + kBM - 1) / kBM);
+  const unsigned grid = (unsigned)std::min<size_t>(tiles, (size_t)std::max(1, sm_count()));
   nvfp4_gemm_kernel<<<grid, 192, kGemmSmem, s>>>(tmap_a, *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b),
                                                  p);
   FPB_LAUNCH_CHECK("nvfp4_gemm_kernel");
@@ -559,7 +616,8 @@ extern "C" int fpb_nvfp4_grouped_gemm_q(fpb_nvfp4_matrix *w, const uint8_t *a_pa
   p.error = err;
   p.tile_experts = tile_experts;
   p.n_experts = (int)(w->rows / rows_per_expert);
-  dim3 grid((unsigned)(rows_per_expert / kBN), (unsigned)(padded_rows / kBM));
+  const size_t tiles = (rows_per_expert / kBN) * (padded_rows / kBM);
+  const unsigned grid = (unsigned)std::min<size_t>(tiles, (size_t)std::max(1, sm_count()));
   nvfp4_gemm_kernel<<<grid, 192, kGemmSmem, s>>>(tmap_a, *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b),
                                                  p);
   FPB_LAUNCH_CHECK("nvfp4_gemm_kernel(grouped)");

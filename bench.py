@@ -890,7 +890,9 @@ def moe_arm(args):
                sf2=torch.empty(int(N_.lib.fpb_nvfp4_act_sf_bytes(cap, MOE_I)), dtype=torch.uint8, device=dev),
                y2=torch.empty(cap, MOE_H, dtype=torch.bfloat16, device=dev),
                out=torch.empty(T, MOE_H, dtype=torch.bfloat16, device=dev),
-               scal=torch.zeros(4, dtype=torch.float32, device=dev))
+               scal=torch.zeros(4, dtype=torch.float32, device=dev),
+               lscr=torch.empty(int(N_.lib.fpb_moe_layout_scratch_bytes(T, MOE_K, MOE_E)), dtype=torch.uint8,
+                                device=dev))
     b = buf
     BF = N_.FPB_BF16
 
@@ -904,7 +906,8 @@ def moe_arm(args):
         N_.call("fpb_moe_topk", b["logits"].data_ptr(), MOE_E, None, T, MOE_E, MOE_K, width, b["ids"].data_ptr(),
                 b["w"].data_ptr(), sh)
         N_.call("fpb_moe_layout", b["ids"].data_ptr(), T, width, MOE_K, MOE_E, 128, cap, b["tr"].data_ptr(),
-                b["te"].data_ptr(), b["inv"].data_ptr(), b["rg"].data_ptr(), b["pad"].data_ptr(), sh)
+                b["te"].data_ptr(), b["inv"].data_ptr(), b["rg"].data_ptr(), b["pad"].data_ptr(), b["lscr"].data_ptr(),
+                b["lscr"].numel(), sh)
         N_.call("fpb_moe_gather_quantize", xin.data_ptr(), BF, T, MOE_H, b["tr"].data_ptr(), cap, b["pad"].data_ptr(),
                 b["a1"].data_ptr(), b["sf1"].data_ptr(), b["scal"].data_ptr(), b["scal"][1:].data_ptr(), 0, sh)
         mark(2)

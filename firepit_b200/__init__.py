@@ -10,6 +10,7 @@ from ._native import FpbError, launch_count
 from .gemv import (DEFAULT_GEMV_TILE, ExpertGemvView, Gemv, GemvTile, ShapeError, expert_gemv_weight_view,
                    fp8_tile, gemv, row_scaled_tile)
 from .moe import (ExpertSelection, ExpertSelectionError, MoeDimensionError, MoeDims, PrefillLayout, PrefillPlan,
+                  layout_scratch,
                   combine, combine_add_norm_prefill, combine_add_norm_view, combine_prefill, gather_prefill_view,
                   gather_quantize, swiglu, swiglu_quantize, topk_device)
 from .sink import Async, Dry, Eager, Graph, Traced

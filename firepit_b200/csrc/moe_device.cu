@@ -5,7 +5,7 @@
 // builds the expert-sorted layout on the host (a counting sort) and uploads it
 // again (PrefillPlan::top_k, moe.rs:545-585).  Here every step stays on the
 // device, so a prefill MoE is one stream of launches with no host round trip:
-//   top-k (one warp per token) -> layout (one CTA: stable counting sort) ->
+//   top-k (one warp per token) -> layout (stable counting sort over CTAs) ->
 //   gather + NVFP4 quantize -> grouped gate/up GEMM -> SwiGLU + NVFP4
 //   quantize -> grouped down GEMM -> combine (+ residual + RMSNorm).
 // The layout is written into buffers sized for the largest possible padding
@@ -96,64 +96,60 @@ __global__ void moe_topk_kernel(const float *logits, long long ld, const float *
 }
 
 // ---- layout: stable counting sort (moe.rs:452-516) -------------------------------------
-// One CTA of 32 warps.  Warp w owns a contiguous segment of the flattened
-// (token, slot) entries; per-warp counts per expert in shared memory turn into
-// each warp's first row per expert, so that rows keep the entries' order
-// within every expert (the reference's stable sort).
-constexpr int kLayoutWarps = 32;
+// Multi-CTA: CTA g owns the contiguous route range [g * kLayoutChunk, ...).
+//  1. count: per-CTA histogram of expert ids (shared-memory atomics) -> cnt[g][e];
+//  2. scan (one CTA): per expert, cnt[g][e] -> the CTA's first row within the
+//     expert (exclusive over g); padded expert ranges (exclusive over e); tile
+//     experts; the row count;
+//  3. place: per CTA, ranks that keep the routes' order (per-warp counts over
+//     contiguous warp segments, __match_any_sync within a batch), so every
+//     expert's rows follow the (token, slot) order: the reference's stable sort.
+// The fills (token_rows = -1, tile_experts = -1, inverse = 0) are memsets.
+constexpr int kLayoutChunk = 4096;  // routes per CTA
+constexpr int kLayoutWarpsPerCta = 8;
 
-__global__ void __launch_bounds__(kLayoutWarps * 32, 1)
-    moe_layout_kernel(const int32_t *ids, int tokens, int width, int kk, int experts, int tile_rows, int cap,
-                      int32_t *token_rows, int32_t *tile_experts, int32_t *inverse, int64_t *ranges,
-                      int32_t *padded_out, int *error) {
-  extern __shared__ int smem_i[];
-  int *counts = smem_i;                             // [kLayoutWarps][experts]
-  int *offsets = counts + kLayoutWarps * experts;  // [experts + 1]
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int n = tokens * kk;
-  const int seg = (n + kLayoutWarps - 1) / kLayoutWarps;
-  const int e_lo = min(n, warp * seg), e_hi = min(n, e_lo + seg);
+__device__ __forceinline__ int layout_id(const int32_t *ids, int e, int kk, int width, int experts) {
+  const int id = ids[(long long)(e / kk) * width + e % kk];
+  return (id >= 0 && id < experts) ? id : -1;
+}
 
-  for (int i = tid; i < cap; i += blockDim.x) token_rows[i] = -1;
-  for (int i = tid; i < cap / tile_rows; i += blockDim.x) tile_experts[i] = -1;
-  for (int i = tid; i < tokens * width; i += blockDim.x) inverse[i] = 0;
-  for (int i = tid; i < kLayoutWarps * experts; i += blockDim.x) counts[i] = 0;
+__global__ void __launch_bounds__(256) moe_layout_count_kernel(const int32_t *ids, int n, int kk, int width,
+                                                               int experts, int *cnt, int *error) {
+  extern __shared__ int hist[];
+  for (int e = threadIdx.x; e < experts; e += blockDim.x) hist[e] = 0;
   __syncthreads();
-
-  // per-warp counts
-  for (int b = e_lo; b < e_hi; b += 32) {
-    const int e = b + lane;
-    int id = -1;
-    if (e < e_hi) {
-      id = ids[(long long)(e / kk) * width + e % kk];
-      if (id < 0 || id >= experts) {
-        if (error) atomicCAS(error, 0, 401);
-        id = -1;
-      }
-    }
-    const unsigned grp = __match_any_sync(0xffffffffu, id);
-    if (id >= 0 && lane == __ffs(grp) - 1) counts[warp * experts + id] += __popc(grp);
-    __syncwarp();
+  const int lo = blockIdx.x * kLayoutChunk, hi = min(n, lo + kLayoutChunk);
+  for (int e = lo + threadIdx.x; e < hi; e += blockDim.x) {
+    const int id = layout_id(ids, e, kk, width, experts);
+    if (id >= 0)
+      atomicAdd(&hist[id], 1);
+    else if (error)
+      atomicCAS(error, 0, 401);
   }
   __syncthreads();
+  for (int e = threadIdx.x; e < experts; e += blockDim.x) cnt[(size_t)blockIdx.x * experts + e] = hist[e];
+}
 
-  // per expert: total, then each warp's exclusive prefix within the expert
+__global__ void __launch_bounds__(1024) moe_layout_scan_kernel(int *cnt, int groups, int experts, int tile_rows,
+                                                               int cap, int32_t *tile_experts, int64_t *ranges,
+                                                               int32_t *padded_out, int *error) {
+  extern __shared__ int totals[];  // [experts]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   for (int x = tid; x < experts; x += blockDim.x) {
     int run = 0;
-    for (int w = 0; w < kLayoutWarps; ++w) {
-      const int c = counts[w * experts + x];
-      counts[w * experts + x] = run;
+    for (int g = 0; g < groups; ++g) {
+      const int c = cnt[(size_t)g * experts + x];
+      cnt[(size_t)g * experts + x] = run;
       run += c;
     }
-    offsets[x] = run;  // the expert's total for now
+    totals[x] = run;
   }
   __syncthreads();
-  // exclusive scan over experts of the padded sizes (warp 0, 32 at a time)
   if (warp == 0) {
     int carry = 0;
     for (int base = 0; base < experts; base += 32) {
       const int x = base + lane;
-      const int total = x < experts ? offsets[x] : 0;
+      const int total = x < experts ? totals[x] : 0;
       const int padded = (total + tile_rows - 1) / tile_rows * tile_rows;
       int incl = padded;
 #pragma unroll
@@ -173,39 +169,82 @@ __global__ void __launch_bounds__(kLayoutWarps * 32, 1)
     }
   }
   __syncthreads();
-  for (int x = tid; x < experts; x += blockDim.x) offsets[x] = (int)ranges[2 * x];
-  __syncthreads();
-
-  // rows: each warp walks its segment again, in order
-  for (int b = e_lo; b < e_hi; b += 32) {
-    const int e = b + lane;
-    int id = -1;
-    if (e < e_hi) {
-      id = ids[(long long)(e / kk) * width + e % kk];
-      if (id < 0 || id >= experts) id = -1;
-    }
-    const unsigned grp = __match_any_sync(0xffffffffu, id);
-    const int rank = __popc(grp & ((1u << lane) - 1));
-    int pos = -1;
-    if (id >= 0) pos = offsets[id] + counts[warp * experts + id] + rank;
-    __syncwarp();
-    if (id >= 0 && lane == __ffs(grp) - 1) counts[warp * experts + id] += __popc(grp);
-    if (id >= 0 && pos < cap) {
-      token_rows[pos] = e / kk;
-      inverse[(long long)(e / kk) * width + e % kk] = pos;
-    }
-    __syncwarp();
-  }
-  // tiles
   for (int x = tid; x < experts; x += blockDim.x) {
-    const int start = (int)ranges[2 * x], count = (int)ranges[2 * x + 1];
+    const int start = (int)ranges[2 * x], count = totals[x];
     const int padded = (count + tile_rows - 1) / tile_rows * tile_rows;
     for (int t = start / tile_rows; t < (start + padded) / tile_rows && t < cap / tile_rows; ++t)
       tile_experts[t] = x;
   }
 }
 
+__global__ void __launch_bounds__(kLayoutWarpsPerCta * 32) moe_layout_place_kernel(
+    const int32_t *ids, int n, int kk, int width, int experts, int cap, const int *cnt, const int64_t *ranges,
+    int32_t *token_rows, int32_t *inverse) {
+  extern __shared__ int wcount[];  // [kLayoutWarpsPerCta][experts]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int i = tid; i < kLayoutWarpsPerCta * experts; i += blockDim.x) wcount[i] = 0;
+  __syncthreads();
+  const int lo = blockIdx.x * kLayoutChunk, hi = min(n, lo + kLayoutChunk);
+  constexpr int kWarpSpan = kLayoutChunk / kLayoutWarpsPerCta;
+  const int w_lo = min(hi, lo + warp * kWarpSpan), w_hi = min(hi, w_lo + kWarpSpan);
+  for (int b = w_lo; b < w_hi; b += 32) {
+    const int e = b + lane;
+    const int id = e < w_hi ? layout_id(ids, e, kk, width, experts) : -1;
+    const unsigned grp = __match_any_sync(0xffffffffu, id);
+    if (id >= 0 && lane == __ffs(grp) - 1) wcount[warp * experts + id] += __popc(grp);
+    __syncwarp();
+  }
+  __syncthreads();
+  // each warp's first row per expert: expert start + earlier CTAs' rows + earlier warps'
+  for (int x = tid; x < experts; x += blockDim.x) {
+    int run = (int)ranges[2 * x] + cnt[(size_t)blockIdx.x * experts + x];
+    for (int w = 0; w < kLayoutWarpsPerCta; ++w) {
+      const int c = wcount[w * experts + x];
+      wcount[w * experts + x] = run;
+      run += c;
+    }
+  }
+  __syncthreads();
+  for (int b = w_lo; b < w_hi; b += 32) {
+    const int e = b + lane;
+    const int id = e < w_hi ? layout_id(ids, e, kk, width, experts) : -1;
+    const unsigned grp = __match_any_sync(0xffffffffu, id);
+    const int rank = __popc(grp & ((1u << lane) - 1));
+    int pos = -1;
+    if (id >= 0) pos = wcount[warp * experts + id] + rank;
+    __syncwarp();
+    if (id >= 0 && lane == __ffs(grp) - 1) wcount[warp * experts + id] += __popc(grp);
+    if (id >= 0 && pos < cap) {
+      token_rows[pos] = e / kk;
+      inverse[(long long)(e / kk) * width + e % kk] = pos;
+    }
+    __syncwarp();
+  }
+}
+
 // ---- row loaders for the NVFP4 activation encode ----------------------------------------
+// 16 consecutive values as f32 with 16-byte loads (p 16-byte aligned: rows of
+// a multiple of 32 columns, groups of 16).
+__device__ __forceinline__ void load16_vec(const float *p, float v[16]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float4 f = reinterpret_cast<const float4 *>(p)[q];
+    v[4 * q] = f.x; v[4 * q + 1] = f.y; v[4 * q + 2] = f.z; v[4 * q + 3] = f.w;
+  }
+}
+__device__ __forceinline__ void load16_vec(const uint16_t *p, float v[16]) {
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const uint4 u = reinterpret_cast<const uint4 *>(p)[q];
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      v[8 * q + 2 * t] = __uint_as_float(w[t] << 16);
+      v[8 * q + 2 * t + 1] = __uint_as_float(w[t] & 0xffff0000u);
+    }
+  }
+}
+
 // Gathered rows (moe.rs:71-89): sorted row r is token token_rows[r], or zeros.
 template <typename T>
 struct GatherRows {
@@ -218,9 +257,7 @@ struct GatherRows {
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = 0.0f;
     if (t < 0 || t >= tokens) return;  // padding (or an id outside x)
-    const T *src = x + (size_t)t * cols + g * 16;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = act_load(src, i);
+    load16_vec(x + (size_t)t * cols + g * 16, v);
   }
 };
 
@@ -233,9 +270,11 @@ struct SwigluRows {
   size_t cols;  // intermediate size
   __device__ __forceinline__ void load16(size_t r, size_t g, float v[16]) const {
     const T *gate = gu + r * 2 * cols + g * 16;
-    const T *up = gate + cols;
+    float gv[16], uv[16];
+    load16_vec(gate, gv);
+    load16_vec(gate + cols, uv);
 #pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = silu_mul(act_load(gate, i), act_load(up, i));
+    for (int i = 0; i < 16; ++i) v[i] = silu_mul(gv[i], uv[i]);
   }
 };
 
@@ -308,7 +347,8 @@ __global__ void swiglu_kernel(const T *gu, size_t rows, size_t cols, O *out) {
 // ---- combine (moe.rs:91-147) -------------------------------------------------------------
 // One CTA per token: sum over slots (in slot order) of weight * routed row;
 // with a residual, out = residual + sum and normed = out * rsqrt(mean(out^2) +
-// eps) * gamma (combine_add_norm_kernel).
+// eps) * gamma (combine_add_norm_kernel).  Each thread owns 8 consecutive
+// columns (16-byte vectors; cols is a multiple of 32).
 template <typename R, typename O>
 __global__ void combine_kernel(const R *routed, int routed_rows, size_t cols, const int32_t *inverse,
                                const float *weights, int width, int slots, const float *residual, const float *gamma,
@@ -316,21 +356,48 @@ __global__ void combine_kernel(const R *routed, int routed_rows, size_t cols, co
   extern __shared__ float red[];
   const int t = blockIdx.x;
   float ss = 0.0f;
-  for (size_t c = threadIdx.x; c < cols; c += blockDim.x) {
-    float sum = 0.0f;
+  for (size_t c8 = threadIdx.x; c8 < cols / 8; c8 += blockDim.x) {
+    const size_t c = c8 * 8;
+    float sum[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) sum[j] = 0.0f;
     for (int s = 0; s < slots; ++s) {
       const int row = inverse[(size_t)t * width + s];
       if (row < 0 || row >= routed_rows) continue;  // a slot outside routed adds nothing
-      sum = sum + act_load(routed, (size_t)row * cols + c) * weights[(size_t)t * width + s];
+      const float w = weights[(size_t)t * width + s];
+      float v[8];
+      if constexpr (sizeof(R) == 4) {
+        const float4 a = *reinterpret_cast<const float4 *>(routed + (size_t)row * cols + c);
+        const float4 b = *reinterpret_cast<const float4 *>(routed + (size_t)row * cols + c + 4);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+      } else {
+        const uint4 u = *reinterpret_cast<const uint4 *>(routed + (size_t)row * cols + c);
+        const uint32_t q[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          v[2 * j] = __uint_as_float(q[j] << 16);
+          v[2 * j + 1] = __uint_as_float(q[j] & 0xffff0000u);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) sum[j] = sum[j] + v[j] * w;
     }
     if (residual) {
-      sum = residual[(size_t)t * cols + c] + sum;
-      ss = fmaf(sum, sum, ss);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        sum[j] = residual[(size_t)t * cols + c + j] + sum[j];
+        ss = fmaf(sum[j], sum[j], ss);
+      }
     }
-    if constexpr (sizeof(O) == 4)
-      out[(size_t)t * cols + c] = sum;
-    else
-      out[(size_t)t * cols + c] = __float2bfloat16_rn(sum);
+    if constexpr (sizeof(O) == 4) {
+      float4 *o = reinterpret_cast<float4 *>(out + (size_t)t * cols + c);
+      o[0] = make_float4(sum[0], sum[1], sum[2], sum[3]);
+      o[1] = make_float4(sum[4], sum[5], sum[6], sum[7]);
+    } else {
+      *reinterpret_cast<uint4 *>(out + (size_t)t * cols + c) =
+          make_uint4(pack_bf16x2(sum[0], sum[1]), pack_bf16x2(sum[2], sum[3]), pack_bf16x2(sum[4], sum[5]),
+                     pack_bf16x2(sum[6], sum[7]));
+    }
   }
   if (!residual) return;
 #pragma unroll
@@ -426,10 +493,16 @@ extern "C" int fpb_moe_topk(const float *logits, size_t ld, const float *shared_
   return FPB_OK;
 }
 
+extern "C" size_t fpb_moe_layout_scratch_bytes(size_t tokens, size_t slots, size_t experts) {
+  const size_t groups = (tokens * slots + kLayoutChunk - 1) / kLayoutChunk;
+  return std::max<size_t>(1, groups) * experts * sizeof(int);
+}
+
 extern "C" int fpb_moe_layout(const int32_t *ids, size_t tokens, size_t width, size_t slots, size_t experts,
                               size_t tile_rows, size_t cap, int32_t *token_rows, int32_t *tile_experts,
-                              int32_t *inverse, size_t *ranges, int32_t *padded_rows, void *stream) {
-  if (!ids || !token_rows || !tile_experts || !inverse || !ranges || !padded_rows)
+                              int32_t *inverse, size_t *ranges, int32_t *padded_rows, void *scratch,
+                              size_t scratch_bytes, void *stream) {
+  if (!ids || !token_rows || !tile_experts || !inverse || !ranges || !padded_rows || !scratch)
     return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_moe_layout: null pointer");
   if (tokens == 0 || slots == 0 || slots > width || experts == 0 || tile_rows == 0 || (tile_rows & (tile_rows - 1)))
     return fail(FPB_ERR_SELECTION, "invalid expert selection: shape");
@@ -439,8 +512,11 @@ extern "C" int fpb_moe_layout(const int32_t *ids, size_t tokens, size_t width, s
   if (cap < max_rows || cap % tile_rows || cap > 0x7fffffffu || tokens * width > 0x7fffffffu)
     return fail(FPB_ERR_WORKSPACE, "fpb_moe_layout: capacity %zu below %zu (or not a multiple of tile_rows)", cap,
                 max_rows);
-  const size_t smem = ((size_t)kLayoutWarps * experts + experts + 1) * sizeof(int);
-  if (smem > 200 * 1024) return fail(FPB_ERR_UNSUPPORTED, "fpb_moe_layout: %zu experts", experts);
+  if (scratch_bytes < fpb_moe_layout_scratch_bytes(tokens, slots, experts))
+    return fail(FPB_ERR_WORKSPACE, "fpb_moe_layout: scratch of %zu bytes needed",
+                fpb_moe_layout_scratch_bytes(tokens, slots, experts));
+  const size_t wsmem = (size_t)kLayoutWarpsPerCta * experts * sizeof(int);
+  if (wsmem > 200 * 1024) return fail(FPB_ERR_UNSUPPORTED, "fpb_moe_layout: %zu experts", experts);
   {
     static std::mutex mu;
     static std::vector<int> done;
@@ -448,14 +524,34 @@ extern "C" int fpb_moe_layout(const int32_t *ids, size_t tokens, size_t width, s
     cudaGetDevice(&dev);
     std::lock_guard<std::mutex> lock(mu);
     if (std::find(done.begin(), done.end(), dev) == done.end()) {
-      FPB_CUDA_TRY(cudaFuncSetAttribute(moe_layout_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+      FPB_CUDA_TRY(cudaFuncSetAttribute(moe_layout_place_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        200 * 1024));
+      FPB_CUDA_TRY(cudaFuncSetAttribute(moe_layout_count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        200 * 1024));
+      FPB_CUDA_TRY(cudaFuncSetAttribute(moe_layout_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        200 * 1024));
       done.push_back(dev);
     }
   }
-  moe_layout_kernel<<<1, kLayoutWarps * 32, smem, as_stream(stream)>>>(
-      ids, (int)tokens, (int)width, (int)slots, (int)experts, (int)tile_rows, (int)cap, token_rows, tile_experts,
-      inverse, reinterpret_cast<int64_t *>(ranges), padded_rows, device_error_ptr());
-  FPB_LAUNCH_CHECK("moe_layout_kernel");
+  cudaStream_t s = as_stream(stream);
+  const int n = (int)(tokens * slots);
+  const int groups = (n + kLayoutChunk - 1) / kLayoutChunk;
+  int *cnt = static_cast<int *>(scratch);
+  int *err = device_error_ptr();
+  FPB_CUDA_TRY(cudaMemsetAsync(token_rows, 0xff, cap * sizeof(int32_t), s));
+  FPB_CUDA_TRY(cudaMemsetAsync(tile_experts, 0xff, cap / tile_rows * sizeof(int32_t), s));
+  FPB_CUDA_TRY(cudaMemsetAsync(inverse, 0, tokens * width * sizeof(int32_t), s));
+  moe_layout_count_kernel<<<groups, 256, experts * sizeof(int), s>>>(ids, n, (int)slots, (int)width, (int)experts,
+                                                                     cnt, err);
+  FPB_LAUNCH_CHECK("moe_layout_count_kernel");
+  moe_layout_scan_kernel<<<1, 1024, experts * sizeof(int), s>>>(cnt, groups, (int)experts, (int)tile_rows, (int)cap,
+                                                                tile_experts, reinterpret_cast<int64_t *>(ranges),
+                                                                padded_rows, err);
+  FPB_LAUNCH_CHECK("moe_layout_scan_kernel");
+  moe_layout_place_kernel<<<groups, kLayoutWarpsPerCta * 32, wsmem, s>>>(
+      ids, n, (int)slots, (int)width, (int)experts, (int)cap, cnt, reinterpret_cast<const int64_t *>(ranges),
+      token_rows, inverse);
+  FPB_LAUNCH_CHECK("moe_layout_place_kernel");
   return FPB_OK;
 }
 
@@ -488,6 +584,8 @@ extern "C" int fpb_moe_gather_quantize(const void *x, int x_dtype, size_t tokens
   if (!x || !token_rows || !packed || !sf_tiled || !global_out || !amax_scratch)
     return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_moe_gather_quantize: null pointer");
   if (tokens == 0 || rows == 0 || cols == 0 || cols % 32) return fail(FPB_ERR_SHAPE, "fpb_moe_gather_quantize: shape");
+  if (reinterpret_cast<uintptr_t>(x) & 15)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_moe_gather_quantize: x must be 16-byte aligned");
   cudaStream_t s = as_stream(stream);
   uint32_t *amax = reinterpret_cast<uint32_t *>(amax_scratch);
   const bool given = flags & FPB_QUANT_AMAX_GIVEN;
@@ -536,6 +634,8 @@ extern "C" int fpb_swiglu_quantize(const void *gate_up, int dtype, size_t rows, 
   if (!gate_up || !packed || !sf_tiled || !global_out || !amax_scratch)
     return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_swiglu_quantize: null pointer");
   if (rows == 0 || inter == 0 || inter % 32) return fail(FPB_ERR_SHAPE, "fpb_swiglu_quantize: shape");
+  if (reinterpret_cast<uintptr_t>(gate_up) & 15)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_swiglu_quantize: gate_up must be 16-byte aligned");
   cudaStream_t s = as_stream(stream);
   uint32_t *amax = reinterpret_cast<uint32_t *>(amax_scratch);
   const bool given = flags & FPB_QUANT_AMAX_GIVEN;
@@ -559,9 +659,12 @@ static int combine_impl(const void *routed, int r_dtype, size_t routed_rows, siz
                         const float *weights, size_t tokens, size_t width, size_t slots, const float *residual,
                         const float *gamma, float eps, void *out, int out_dtype, float *normed, cudaStream_t s) {
   if (!routed || !inverse || !weights || !out) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_moe_combine: null pointer");
-  if (tokens == 0 || cols == 0 || slots == 0 || slots > width || tokens > 0x7fffffffu || routed_rows > 0x7fffffffu)
+  if (tokens == 0 || cols == 0 || cols % 32 || slots == 0 || slots > width || tokens > 0x7fffffffu ||
+      routed_rows > 0x7fffffffu)
     return fail(FPB_ERR_SHAPE, "fpb_moe_combine: shape");
-  const int threads = cols >= 1024 ? 512 : 256;
+  if ((reinterpret_cast<uintptr_t>(routed) | reinterpret_cast<uintptr_t>(out)) & 15)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_moe_combine: routed and out must be 16-byte aligned");
+  const int threads = std::min<int>(256, std::max<int>(32, (int)(cols / 8 + 31) / 32 * 32));
   const float inv_h = 1.0f / (float)cols;
   return with_dtype(r_dtype, [&](auto tp) {
     using R = std::remove_const_t<std::remove_pointer_t<decltype(tp)>>;
@@ -638,7 +741,9 @@ extern "C" int fpb_act_amax(const void *x, int dtype, size_t n, float *amax_scra
 extern "C" int fpb_swiglu_amax(const void *gate_up, int dtype, size_t rows, const int32_t *valid_rows, size_t inter,
                                float *amax_scratch, int accumulate, void *stream) {
   if (!gate_up || !amax_scratch) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_swiglu_amax: null pointer");
-  if (inter == 0 || inter % 16) return fail(FPB_ERR_SHAPE, "fpb_swiglu_amax: shape");
+  if (inter == 0 || inter % 32) return fail(FPB_ERR_SHAPE, "fpb_swiglu_amax: shape");
+  if (reinterpret_cast<uintptr_t>(gate_up) & 15)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_swiglu_amax: gate_up must be 16-byte aligned");
   cudaStream_t s = as_stream(stream);
   uint32_t *amax = reinterpret_cast<uint32_t *>(amax_scratch);
   if (!accumulate) FPB_CUDA_TRY(cudaMemsetAsync(amax, 0, sizeof(uint32_t), s));

@@ -65,8 +65,11 @@ class DeviceOps:
         out = dict(tr=self.empty((cap,), t.int32), te=self.empty((cap // tile_rows,), t.int32),
                    inv=self.empty((tokens, width), t.int32), rg=self.empty((experts, 2), t.int64),
                    pad=self.empty((1,), t.int32))
+        from .moe import layout_scratch
+        scratch = layout_scratch(tokens, slots, experts, self.device)
         N.call("fpb_moe_layout", ids.data_ptr(), tokens, width, slots, experts, tile_rows, cap, out["tr"].data_ptr(),
-               out["te"].data_ptr(), out["inv"].data_ptr(), out["rg"].data_ptr(), out["pad"].data_ptr(), self._s())
+               out["te"].data_ptr(), out["inv"].data_ptr(), out["rg"].data_ptr(), out["pad"].data_ptr(),
+               scratch.data_ptr(), scratch.numel(), self._s())
         return out
 
     def route_meta(self, ids, inverse, slots, per_rank, rows):

@@ -202,6 +202,13 @@ ExpertSelection.empty = classmethod(_selection_empty)
 ExpertSelection.top_k = classmethod(_selection_top_k)
 
 
+def layout_scratch(tokens: int, slots: int, experts: int, device):
+    """Device scratch for ``fpb_moe_layout`` (per-CTA expert counts), as bytes."""
+    import torch
+    n = int(N.lib.fpb_moe_layout_scratch_bytes(tokens, slots, experts))
+    return torch.empty(n, dtype=torch.uint8, device=device)
+
+
 class PrefillPlan:
     """PrefillPlan (moe.rs:519-671) with every array on the device.
 
@@ -232,7 +239,8 @@ class PrefillPlan:
                     tile_experts=torch.empty(cap // tile_rows, dtype=torch.int32, device=device),
                     inverse=torch.empty(tokens, width, dtype=torch.int32, device=device),
                     ranges=torch.empty(dims.experts, 2, dtype=torch.int64, device=device),
-                    padded_rows_dev=torch.zeros(1, dtype=torch.int32, device=device))
+                    padded_rows_dev=torch.zeros(1, dtype=torch.int32, device=device),
+                    scratch=layout_scratch(tokens, dims.top_k, dims.experts, device))
 
     @classmethod
     def top_k(cls, logits, shared_gate, router: MoeDims, tile_rows: int, stream=None) -> "PrefillPlan":
@@ -246,7 +254,8 @@ class PrefillPlan:
         a = cls._alloc(dims, tokens, tile_rows, logits.device)
         N.call("fpb_moe_layout", ids.data_ptr(), tokens, dims.width(), dims.top_k, dims.experts, tile_rows, a["cap"],
                a["token_rows"].data_ptr(), a["tile_experts"].data_ptr(), a["inverse"].data_ptr(),
-               a["ranges"].data_ptr(), a["padded_rows_dev"].data_ptr(), _stream(logits, stream))
+               a["ranges"].data_ptr(), a["padded_rows_dev"].data_ptr(), a["scratch"].data_ptr(),
+               a["scratch"].numel(), _stream(logits, stream))
         return cls(dims, tokens, tile_rows, a["cap"], ids, w, a["token_rows"], a["tile_experts"], a["inverse"],
                    a["ranges"], a["padded_rows_dev"])
 

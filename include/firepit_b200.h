@@ -276,11 +276,15 @@ int fpb_moe_topk(const float *logits, size_t ld, const float *shared_gate, size_
  * expert (experts ids in [0, experts)), each padded to tile_rows (a power of
  * two).  Outputs: token_rows [cap] (-1 = padding), tile_experts [cap/tile_rows]
  * (-1 past the end), inverse [tokens, width] (0 in unused slots), ranges
- * [experts][2] (start, count), padded_rows (device int32).  One CTA. Device
- * error 401 on an id out of range. */
+ * [experts][2] (start, count), padded_rows (device int32).  Three launches
+ * and three memsets, no host synchronisation; device error 401 on an id out
+ * of range. */
 int fpb_moe_layout(const int32_t *ids, size_t tokens, size_t width, size_t slots, size_t experts,
                    size_t tile_rows, size_t cap, int32_t *token_rows, int32_t *tile_experts,
-                   int32_t *inverse, size_t *ranges, int32_t *padded_rows, void *stream);
+                   int32_t *inverse, size_t *ranges, int32_t *padded_rows, void *scratch,
+                   size_t scratch_bytes, void *stream);
+/* Device scratch fpb_moe_layout needs (per-CTA expert counts). */
+size_t fpb_moe_layout_scratch_bytes(size_t tokens, size_t slots, size_t experts);
 /* gather_prefill_view (moe.rs:71-89, 705-733): out [rows, cols] (f32/bf16),
  * row r = x[token_rows[r]] or zeros. */
 int fpb_moe_gather(const void *x, int x_dtype, size_t tokens, size_t cols, const int32_t *token_rows,

@@ -67,7 +67,8 @@ def test_topk_vs_oracle(F, torch, tokens, experts, k, shared, ties):
 
 
 @pytest.mark.parametrize("tokens,experts,k,tile", [(4096, 512, 10, 128), (64, 512, 10, 128), (300, 513, 11, 32),
-                                                   (1000, 17, 3, 128), (5, 4, 4, 128)])
+                                                   (1000, 17, 3, 128), (5, 4, 4, 128), (5000, 4, 4, 128),
+                                                   (20000, 160, 8, 128)])
 def test_layout_vs_oracle(F, torch, tokens, experts, k, tile):
     rng = np.random.default_rng(tokens)
     width = 1 << (k - 1).bit_length()
@@ -79,9 +80,10 @@ def test_layout_vs_oracle(F, torch, tokens, experts, k, tile):
     out = {n: torch.empty(sz, dtype=dt, device="cuda") for n, sz, dt in
            [("tr", (cap,), torch.int32), ("te", (cap // tile,), torch.int32), ("inv", (tokens, width), torch.int32),
             ("rg", (experts, 2), torch.int64), ("pad", (1,), torch.int32)]}
+    scratch = F.moe.layout_scratch(tokens, k, experts, "cuda")
     F._native.call("fpb_moe_layout", torch.from_numpy(ids).cuda().data_ptr(), tokens, width, k, experts, tile, cap,
                    out["tr"].data_ptr(), out["te"].data_ptr(), out["inv"].data_ptr(), out["rg"].data_ptr(),
-                   out["pad"].data_ptr(), torch.cuda.current_stream().cuda_stream)
+                   out["pad"].data_ptr(), scratch.data_ptr(), scratch.numel(), torch.cuda.current_stream().cuda_stream)
     assert F.device_error() == 0
     tr, te, inv, rg, pad = O.moe_layout(ids, k, experts, tile, cap)
     assert int(out["pad"].item()) == pad

@@ -835,8 +835,11 @@ def moe_arm(args):
     """Config 3 at T = 4096 (prefill) or 64 (decode batch), one GPU: bf16 x
     [T, 2048], bf16 router [512, 2048] (cuBLAS, f32 logits), device top-10,
     device layout (128-row tiles), gather + NVFP4 quantize, grouped gate/up
-    GEMM [512 x 1024, 2048], SwiGLU + NVFP4 quantize, grouped down GEMM
-    [512 x 2048, 512], weighted combine; one CUDA graph per step."""
+    GEMM [512 x 1024, 2048] with SwiGLU in its epilogue (h in bf16 and its
+    amax), NVFP4 quantize of h, grouped down GEMM [512 x 2048, 512], weighted
+    combine; one CUDA graph per step.  The layout's padding rows (each
+    expert's rows rounded up to the 128-row tile) are skipped by the encoders
+    and not stored by the GEMMs."""
     import torch
 
     import firepit_b200 as F
@@ -885,7 +888,7 @@ def moe_arm(args):
                pad=torch.empty(1, **i32),
                a1=torch.empty(cap, MOE_H // 2, dtype=torch.uint8, device=dev),
                sf1=torch.empty(int(N_.lib.fpb_nvfp4_act_sf_bytes(cap, MOE_H)), dtype=torch.uint8, device=dev),
-               y1=torch.empty(cap, 2 * MOE_I, dtype=torch.bfloat16, device=dev),
+               h=torch.empty(cap, MOE_I, dtype=torch.bfloat16, device=dev),
                a2=torch.empty(cap, MOE_I // 2, dtype=torch.uint8, device=dev),
                sf2=torch.empty(int(N_.lib.fpb_nvfp4_act_sf_bytes(cap, MOE_I)), dtype=torch.uint8, device=dev),
                y2=torch.empty(cap, MOE_H, dtype=torch.bfloat16, device=dev),
@@ -908,17 +911,22 @@ def moe_arm(args):
         N_.call("fpb_moe_layout", b["ids"].data_ptr(), T, width, MOE_K, MOE_E, 128, cap, b["tr"].data_ptr(),
                 b["te"].data_ptr(), b["inv"].data_ptr(), b["rg"].data_ptr(), b["pad"].data_ptr(), b["lscr"].data_ptr(),
                 b["lscr"].numel(), sh)
+        # padding rows of the layout (token -1) are skipped by every stage below
+        skip = N_.FPB_QUANT_SKIP_PADDING
         N_.call("fpb_moe_gather_quantize", xin.data_ptr(), BF, T, MOE_H, b["tr"].data_ptr(), cap, b["pad"].data_ptr(),
-                b["a1"].data_ptr(), b["sf1"].data_ptr(), b["scal"].data_ptr(), b["scal"][1:].data_ptr(), 0, sh)
+                b["a1"].data_ptr(), b["sf1"].data_ptr(), b["scal"].data_ptr(), b["scal"][1:].data_ptr(), skip, sh)
         mark(2)
-        N_.call("fpb_nvfp4_grouped_gemm_q", W1.handle, b["a1"].data_ptr(), b["sf1"].data_ptr(), b["scal"].data_ptr(),
-                cap, b["te"].data_ptr(), 2 * MOE_I, b["y1"].data_ptr(), BF, sh)
+        N_.call("fpb_nvfp4_grouped_gemm_swiglu_q", W1.handle, b["a1"].data_ptr(), b["sf1"].data_ptr(),
+                b["scal"].data_ptr(), cap, b["te"].data_ptr(), b["tr"].data_ptr(), MOE_I, b["h"].data_ptr(), BF,
+                b["scal"][3:].data_ptr(), sh)
         mark(3)
-        N_.call("fpb_swiglu_quantize", b["y1"].data_ptr(), BF, cap, b["pad"].data_ptr(), MOE_I, b["a2"].data_ptr(),
-                b["sf2"].data_ptr(), b["scal"][2:].data_ptr(), b["scal"][3:].data_ptr(), 0, sh)
+        N_.call("fpb_rows_quantize", b["h"].data_ptr(), BF, cap, b["pad"].data_ptr(), b["tr"].data_ptr(), MOE_I,
+                b["a2"].data_ptr(), b["sf2"].data_ptr(), b["scal"][2:].data_ptr(), b["scal"][3:].data_ptr(),
+                N_.FPB_QUANT_AMAX_GIVEN | skip, sh)
         mark(4)
         N_.call("fpb_nvfp4_grouped_gemm_q", W2.handle, b["a2"].data_ptr(), b["sf2"].data_ptr(),
-                b["scal"][2:].data_ptr(), cap, b["te"].data_ptr(), MOE_H, b["y2"].data_ptr(), BF, sh)
+                b["scal"][2:].data_ptr(), cap, b["te"].data_ptr(), b["tr"].data_ptr(), MOE_H, b["y2"].data_ptr(), BF,
+                sh)
         mark(5)
         N_.call("fpb_moe_combine", b["y2"].data_ptr(), BF, cap, MOE_H, b["inv"].data_ptr(), b["w"].data_ptr(), T,
                 width, MOE_K, b["out"].data_ptr(), BF, sh)
@@ -951,7 +959,7 @@ def moe_arm(args):
     with torch.cuda.stream(s):
         moe(s.cuda_stream, x, evs)
     torch.cuda.synchronize()
-    names = ["router_gemm", "topk_layout_gather_quant", "gate_up_gemm", "swiglu_quant", "down_gemm", "combine"]
+    names = ["router_gemm", "topk_layout_gather_quant", "gate_up_swiglu_gemm", "h_quant", "down_gemm", "combine"]
     breakdown = {n: evs[i].elapsed_time(evs[i + 1]) for i, n in enumerate(names)}
     flops = moe_flops(T)
     value = flops / (ms * 1e-3) / 1e12

@@ -19,8 +19,8 @@ from .weights import (NVFP4_GROUP, Q8_BLOCK, FormatError, HostNvfp4Matrix, Nvfp4
                       quantize_nvfp4)
 
 from .gemm import (DEFAULT_GEMM_TILE, DEFAULT_GROUPED_GEMM_TILE, GemmTile, Nvfp4Gemm, Nvfp4GroupedGemmView,
-                   device_error, nvfp4_gemm, nvfp4_gemm_view, nvfp4_grouped_gemm_q, nvfp4_grouped_gemm_view,
-                   quantize_act)
+                   device_error, nvfp4_gemm, nvfp4_gemm_view, nvfp4_grouped_gemm_q, nvfp4_grouped_gemm_swiglu_q,
+                   nvfp4_grouped_gemm_view, quantize_act, rows_quantize)
 from .fp8 import (Fp8Gemm, Fp8GroupedGemmView, Fp8Matrix, Fp8Scaling, HostFp8Matrix, fp8_gemm, fp8_gemm_view,
                   fp8_grouped_gemm_q, fp8_grouped_gemm_view, quantize_fp8)
 

@@ -25,6 +25,7 @@ FPB_ERR_NO_DEVICE = 8
 FPB_F32 = 0
 FPB_BF16 = 1
 FPB_QUANT_AMAX_GIVEN = 1
+FPB_QUANT_SKIP_PADDING = 2
 
 
 class FpbError(RuntimeError):
@@ -87,7 +88,7 @@ SIGNATURES: dict[str, tuple] = {
     "fpb_nvfp4_matrix_prepare_gemm": (i32, [vp, vp]),
     "fpb_nvfp4_gemm_q": (i32, [vp, sz, sz, vp, vp, vp, sz, vp, i32, vp]),
     "fpb_nvfp4_gemm": (i32, [vp, sz, sz, vp, i32, sz, vp, i32, vp, sz, vp]),
-    "fpb_nvfp4_grouped_gemm_q": (i32, [vp, vp, vp, vp, sz, vp, sz, vp, i32, vp]),
+    "fpb_nvfp4_grouped_gemm_q": (i32, [vp, vp, vp, vp, sz, vp, vp, sz, vp, i32, vp]),
     "fpb_device_error": (i32, [C.POINTER(i32), i32]),
     "fpb_fp8_validate": (i32, [sz, vp, sz, sz, sz, sz, sz]),
     "fpb_fp8_matrix_create": (i32, [vp, vp, sz, sz, sz, sz, vp, C.POINTER(vp)]),
@@ -107,6 +108,8 @@ SIGNATURES: dict[str, tuple] = {
     "fpb_moe_gather_quantize": (i32, [vp, i32, sz, sz, vp, sz, vp, vp, vp, vp, vp, i32, vp]),
     "fpb_swiglu": (i32, [vp, i32, sz, sz, vp, i32, vp]),
     "fpb_swiglu_quantize": (i32, [vp, i32, sz, vp, sz, vp, vp, vp, vp, i32, vp]),
+    "fpb_nvfp4_grouped_gemm_swiglu_q": (i32, [vp, vp, vp, vp, sz, vp, vp, sz, vp, i32, vp, vp]),
+    "fpb_rows_quantize": (i32, [vp, i32, sz, vp, vp, sz, vp, vp, vp, vp, i32, vp]),
     "fpb_act_amax": (i32, [vp, i32, sz, vp, i32, vp]),
     "fpb_swiglu_amax": (i32, [vp, i32, sz, vp, sz, vp, i32, vp]),
     "fpb_moe_combine": (i32, [vp, i32, sz, sz, vp, vp, sz, sz, sz, vp, i32, vp]),

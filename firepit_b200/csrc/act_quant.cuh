@@ -39,12 +39,30 @@ __device__ __forceinline__ float act_load<uint16_t>(const uint16_t *p, size_t i)
 }
 
 // atomicMax of |x| bits over x[0, n) (amax_bits zeroed by the caller).
+// 16-byte loads when x is 16-byte aligned, element loads for the tail.
 template <typename T>
 __global__ void act_amax_kernel(const T *x, size_t n, uint32_t *amax_bits) {
   uint32_t m = 0;
-  size_t stride = (size_t)gridDim.x * blockDim.x;
-  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
-    m = max(m, __float_as_uint(act_load(x, i)) & 0x7fffffffu);
+  const size_t tid = (size_t)blockIdx.x * blockDim.x + threadIdx.x, stride = (size_t)gridDim.x * blockDim.x;
+  constexpr size_t kVec = 16 / sizeof(T);
+  size_t head = 0;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    const size_t nv = n / kVec;
+    const uint4 *xv = reinterpret_cast<const uint4 *>(x);
+    for (size_t i = tid; i < nv; i += stride) {
+      const uint4 u = xv[i];
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        if constexpr (sizeof(T) == 4)
+          m = max(m, w[k] & 0x7fffffffu);
+        else
+          m = max(m, max((w[k] << 16) & 0x7fffffffu, w[k] & 0x7fff0000u));
+      }
+    }
+    head = nv * kVec;
+  }
+  for (size_t i = head + tid; i < n; i += stride) m = max(m, __float_as_uint(act_load(x, i)) & 0x7fffffffu);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
   if ((threadIdx.x & 31) == 0) atomicMax(amax_bits, m);
@@ -52,6 +70,10 @@ __global__ void act_amax_kernel(const T *x, size_t n, uint32_t *amax_bits) {
 
 // One 16-value group: s = RN_e4m3((bmax / 6) / global), codes =
 // RN_e2m1(v / (e4m3(s) * global)); writes 8 code bytes and the factor.
+// SwiGLU of one element in the reference's order (swiglu.rs:16):
+// gate / (1 + exp(gate * -1)) * up.
+__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + expf(g * -1.0f)) * u; }
+
 __device__ __forceinline__ void encode_group16(const float v[16], float global, uint8_t *packed_dst,
                                                uint8_t *sf_dst) {
   float bmax = 0.0f;

@@ -14,7 +14,9 @@
 //               tcgen05.mma.kind::mxf4nvf4.block_scale.block16 (K = 64 each)
 //               accumulating in TMEM; tcgen05.commit frees the stage;
 //   warps 2-5   epilogue: tcgen05.ld of the f32 accumulator, times ga * g[n],
-//               stored as bf16 or f32.
+//               staged as bf16 or f32 in shared memory (128-byte swizzle,
+//               32 rows per warp) and written by TMA tiled stores, so each
+//               row segment leaves as whole 128-byte lines.
 // Every TMA load lands in the issuing CTA alone.
 //
 // Scale factors live in the tensor cores' tiled layout: for each 128-row
@@ -41,9 +43,15 @@ constexpr int kBM = 128, kBN = 128, kBKBytes = 128;  // K block = 256 fp4 column
 constexpr int kStages = 4;
 
 // Row-major e4m3 scales [rows, cols/16] -> tiled, sign cleared (UE4M3).
-// Padding entries are written as zero.  One thread per output byte.
+// Padding entries are written as zero.  One thread per output byte.  With
+// glu_inter > 0 tiled row v holds source row glu_source_row(v, glu_inter).
+__host__ __device__ inline size_t glu_source_row(size_t v, size_t inter) {
+  const size_t e = v / (2 * inter), w = v % (2 * inter);
+  return e * 2 * inter + ((w % 128) / 64) * inter + (w / 128) * 64 + w % 64;
+}
+
 __global__ void sf_tile_kernel(const uint8_t *scales, size_t rows, size_t cols, uint8_t *tiled,
-                               size_t total) {
+                               size_t total, size_t glu_inter) {
   size_t kb64_per_rb = (cols + 255) / 256 * 4;
   size_t stride = (size_t)gridDim.x * blockDim.x;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
@@ -52,7 +60,10 @@ __global__ void sf_tile_kernel(const uint8_t *scales, size_t rows, size_t cols, 
     size_t r = (b / 16) + 32 * ((b % 16) / 4), s = b % 4;
     size_t row = rb * 128 + r, group = kb64 * 4 + s;
     uint8_t v = 0;
-    if (row < rows && group < cols / 16) v = scales[row * (cols / 16) + group] & 0x7f;
+    if (row < rows && group < cols / 16) {
+      const size_t src = glu_inter ? glu_source_row(row, glu_inter) : row;
+      v = scales[src * (cols / 16) + group] & 0x7f;
+    }
     tiled[i] = v;
   }
 }
@@ -86,15 +97,18 @@ __global__ void act_encode_kernel(const T *x, size_t rows, size_t cols, const ui
                                   uint8_t *packed, uint8_t *sf_tiled, float *global_out) {
   const float global = __fdiv_rn(__uint_as_float(*amax_bits), 2688.0f);
   if (blockIdx.x == 0 && threadIdx.x == 0) *global_out = global;
-  size_t gpr = cols / kNvfp4Group, n_groups = rows * gpr;
-  size_t stride = (size_t)gridDim.x * blockDim.x;
-  for (size_t gi = (size_t)blockIdx.x * blockDim.x + threadIdx.x; gi < n_groups; gi += stride) {
-    size_t r = gi / gpr, g = gi - r * gpr;
-    float v[kNvfp4Group];
-    const T *src = x + r * cols + g * kNvfp4Group;
+  // One warp per row (grid-stride over rows); lane l takes groups l, l + 32, ...
+  const int gpr = (int)(cols / kNvfp4Group), lane = threadIdx.x & 31;
+  const size_t warps = (size_t)gridDim.x * (blockDim.x / 32);
+  for (size_t r = (size_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; r < rows; r += warps) {
+    for (int g = lane; g < gpr; g += 32) {
+      float v[kNvfp4Group];
+      const T *src = x + r * cols + (size_t)g * kNvfp4Group;
 #pragma unroll
-    for (int i = 0; i < kNvfp4Group; ++i) v[i] = act_load(src, i);
-    encode_group16(v, global, packed + r * (cols / 2) + g * (kNvfp4Group / 2), sf_tiled + sf_tiled_offset(r, g, cols));
+      for (int i = 0; i < kNvfp4Group; ++i) v[i] = act_load(src, i);
+      encode_group16(v, global, packed + r * (cols / 2) + (size_t)g * (kNvfp4Group / 2),
+                     sf_tiled + sf_tiled_offset(r, g, cols));
+    }
   }
 }
 
@@ -120,6 +134,19 @@ struct GemmParams {
   // [e * rows_per_expert, (e + 1) * rows_per_expert); N = rows_per_expert.
   const int32_t *tile_experts;  // null for a dense GEMM
   int n_experts;
+  int tma_store;  // y through tmap_y (else direct per-row stores: unaligned y)
+  // Fused SwiGLU (grouped mode only): N = 2 * inter rows per expert, gate rows
+  // first; B tiles are gate rows [64b, 64b+64) + up rows [64b, 64b+64) (two
+  // 64-row loads through tmap_b64, factors from the interleaved tiled copy)
+  // and the epilogue writes h = silu(gate) * up [M, inter] through tmap_y,
+  // with max |h| (as stored) into *amax_bits.
+  int glu;
+  uint32_t *amax_bits;
+  // Grouped mode, nullable: the layout's token of each row (-1 = padding row).
+  // Padding rows' outputs are not needed: a warp whose 32 rows are all padding
+  // stores nothing, and padding rows are left out of the amax (so their
+  // activations may hold anything, e.g. rows an encoder skipped).
+  const int32_t *row_tokens;
 };
 
 constexpr int kTileBytes = kBM * kBKBytes;   // 16 KB per operand per stage
@@ -128,7 +155,11 @@ constexpr int kSfStageBytes = 4 * kSfChunk;  // 2 KB per operand per stage
 // columns of A factors (256..319) and 16 of B factors (320..383).
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemSfa = 256, kTmemSfb = 320;
-constexpr size_t kGemmSmem = 1024 + kStages * (2 * kTileBytes + 2 * kSfStageBytes) + 256;
+// Epilogue staging: per epilogue warp 32 rows x 128 columns (f32: four 32-column
+// boxes; bf16: two 64-column boxes), each box 32 rows x 128 bytes.
+constexpr int kOutBoxBytes = 32 * 128;
+constexpr int kOutWarpBytes = 4 * kOutBoxBytes;
+constexpr size_t kGemmSmem = 1024 + kStages * (2 * kTileBytes + 2 * kSfStageBytes) + 4 * kOutWarpBytes + 256;
 
 __device__ __forceinline__ void report(int *error, volatile int *abort, int code) {
   *abort = 1;
@@ -161,6 +192,7 @@ __device__ __forceinline__ bool gemm_tile(const GemmParams &p, int t, int n_tile
 // tile overlaps the main loop of the next.
 __global__ void __launch_bounds__(192, 1)
     nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                      const __grid_constant__ CUtensorMap tmap_y, const __grid_constant__ CUtensorMap tmap_b64,
                       GemmParams p) {
   using namespace sm100;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -169,7 +201,8 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t *sB = sA + kStages * kTileBytes;
   uint8_t *sSFA = sB + kStages * kTileBytes;
   uint8_t *sSFB = sSFA + kStages * kSfStageBytes;
-  uint64_t *full = reinterpret_cast<uint64_t *>(sSFB + kStages * kSfStageBytes);
+  uint8_t *sOut = sSFB + kStages * kSfStageBytes;  // 1024-byte aligned
+  uint64_t *full = reinterpret_cast<uint64_t *>(sOut + 4 * kOutWarpBytes);
   uint64_t *empty = full + kStages;
   uint64_t *acc_full = empty + kStages;  // [2]
   uint64_t *acc_empty = acc_full + 2;    // [2]
@@ -194,6 +227,8 @@ __global__ void __launch_bounds__(192, 1)
     fence_barrier_init();
     prefetch_tensormap(&tmap_a);
     prefetch_tensormap(&tmap_b);
+    if (p.tma_store) prefetch_tensormap(&tmap_y);
+    if (p.glu) prefetch_tensormap(&tmap_b64);
   }
   if (warp == 1) {
     tmem_alloc(tmem_base_s, kTmemCols);
@@ -222,7 +257,14 @@ __global__ void __launch_bounds__(192, 1)
           }
           mbar_arrive_expect_tx(&full[s], 2 * kTileBytes + 2 * kSfStageBytes);
           tma_load_2d(sA + s * kTileBytes, &tmap_a, kb * kBKBytes, m_tile * kBM, &full[s]);
-          tma_load_2d(sB + s * kTileBytes, &tmap_b, kb * kBKBytes, n_base + n_tile * kBN, &full[s]);
+          if (p.glu) {
+            const int row_gate = n_base + n_tile * 64;
+            tma_load_2d(sB + s * kTileBytes, &tmap_b64, kb * kBKBytes, row_gate, &full[s]);
+            tma_load_2d(sB + s * kTileBytes + kTileBytes / 2, &tmap_b64, kb * kBKBytes, row_gate + p.N / 2,
+                        &full[s]);
+          } else {
+            tma_load_2d(sB + s * kTileBytes, &tmap_b, kb * kBKBytes, n_base + n_tile * kBN, &full[s]);
+          }
           bulk_load(sSFA + s * kSfStageBytes, p.a_sf + ((size_t)m_tile * kb64_per_rb + kb * 4) * kSfChunk,
                     kSfStageBytes, &full[s]);
           bulk_load(sSFB + s * kSfStageBytes, p.b_sf + ((size_t)nb_global * kb64_per_rb + kb * 4) * kSfChunk,
@@ -284,6 +326,7 @@ __global__ void __launch_bounds__(192, 1)
     const int qw = warp & 3;
     const uint32_t lane_base = (uint32_t)(qw * 32) << 16;
     const float ga = __ldg(p.a_global);
+    uint8_t *stage = sOut + qw * kOutWarpBytes;  // this warp's 32 rows
     uint32_t lt = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       int m_tile, n_tile, n_base;
@@ -293,7 +336,80 @@ __global__ void __launch_bounds__(192, 1)
         report(p.error, abort_s, 105);
         break;
       }
+      __syncwarp();  // the TMEM loads below are warp-collective
       tc_fence_after();
+      if (p.glu) {
+        // TMEM columns 0..63: gate of h columns j0..j0+63; 64..127: up.  A
+        // rolled loop over 8-column groups keeps the code small (the SwiGLU
+        // is long); the buffer is released after the loop.
+        const int row0 = m_tile * kBM + qw * 32;
+        const bool row_live = row0 + lane < p.M && (!p.row_tokens || p.row_tokens[row0 + lane] >= 0);
+        const bool any_live = __any_sync(0xffffffffu, row_live);
+        const int inter = p.N / 2, j0 = n_tile * 64;
+        uint32_t mx = 0;
+        if (any_live) {
+          float g_gate[2], g_up[2];
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            g_gate[c] = __ldg(p.b_globals + n_base + j0 + c * 32 + lane);
+            g_up[c] = __ldg(p.b_globals + n_base + inter + j0 + c * 32 + lane);
+          }
+          if (lane == 0) bulk_wait_read_all();
+          __syncwarp();
+          uint8_t *row_s = stage + lane * 128;
+          const uint32_t tacc = tmem + lane_base + buf * kBN;
+#pragma unroll 1
+          for (int q = 0; q < 8; ++q) {
+            uint32_t gr[8], ur[8];
+            tmem_ld8x2_wait(tacc + q * 8, tacc + 64 + q * 8, gr, ur);
+            const float gg = q < 4 ? g_gate[0] : g_gate[1], gu = q < 4 ? g_up[0] : g_up[1];
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int src = (q & 3) * 8 + j;
+              const float gate = (__uint_as_float(gr[j]) * ga) * __shfl_sync(0xffffffffu, gg, src);
+              const float up = (__uint_as_float(ur[j]) * ga) * __shfl_sync(0xffffffffu, gu, src);
+              v[j] = silu_mul(gate, up);
+            }
+            if (p.y_bf16) {
+              uint4 pk;
+              pk.x = pack_bf16x2(v[0], v[1]);
+              pk.y = pack_bf16x2(v[2], v[3]);
+              pk.z = pack_bf16x2(v[4], v[5]);
+              pk.w = pack_bf16x2(v[6], v[7]);
+              const uint32_t w4[4] = {pk.x, pk.y, pk.z, pk.w};
+#pragma unroll
+              for (int i = 0; i < 4; ++i) mx = max(mx, max((w4[i] << 16) & 0x7fffffffu, w4[i] & 0x7fff0000u));
+              *reinterpret_cast<uint4 *>(row_s + ((q ^ (lane & 7)) * 16)) = pk;
+            } else {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) mx = max(mx, __float_as_uint(v[j]) & 0x7fffffffu);
+              uint8_t *box = row_s + (q >> 2) * kOutBoxBytes;
+              const int c0 = (q & 3) * 2;
+              *reinterpret_cast<float4 *>(box + ((c0 ^ (lane & 7)) * 16)) = make_float4(v[0], v[1], v[2], v[3]);
+              *reinterpret_cast<float4 *>(box + (((c0 + 1) ^ (lane & 7)) * 16)) =
+                  make_float4(v[4], v[5], v[6], v[7]);
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[buf]);
+        ++lt;
+        if (!any_live) continue;
+        if (!row_live) mx = 0;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (lane == 0) atomicMax(p.amax_bits, mx);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmap_y, stage, j0, row0);
+          if (!p.y_bf16) tma_store_2d(&tmap_y, stage + kOutBoxBytes, j0 + 32, row0);
+          bulk_commit_group();
+        }
+        continue;
+      }
       // Drain the whole accumulator row into registers, free the buffer, then
       // scale and store while the tensor cores fill the other buffer.
       uint32_t r[4][32];
@@ -305,19 +421,72 @@ __global__ void __launch_bounds__(192, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
       ++lt;
-      const int row = m_tile * kBM + qw * 32 + lane;
+      const int row0 = m_tile * kBM + qw * 32;
       const int n0 = n_tile * kBN;
-      if (row >= p.M) continue;
+      if (row0 >= p.M) continue;  // the warp's rows are all past the end
+      const bool row_live = row0 + lane < p.M && (!p.row_tokens || p.row_tokens[row0 + lane] >= 0);
+      if (!__any_sync(0xffffffffu, row_live)) continue;  // nothing of these 32 rows is needed
+      // Lane l holds the weight global of column n0 + 32c + l.
+      float gl[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int n = n0 + c * 32 + lane;
+        gl[c] = n < p.N ? __ldg(p.b_globals + n_base + n) : 0.0f;
+      }
+      if (p.tma_store) {
+        if (lane == 0) bulk_wait_read_all();  // the previous tile's stores have left the stage
+        __syncwarp();
+        uint8_t *row_s = stage + lane * 128;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = (__uint_as_float(r[c][j]) * ga) * __shfl_sync(0xffffffffu, gl[c], j);
+          if (p.y_bf16) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint4 pk;
+              pk.x = pack_bf16x2(v[8 * q], v[8 * q + 1]);
+              pk.y = pack_bf16x2(v[8 * q + 2], v[8 * q + 3]);
+              pk.z = pack_bf16x2(v[8 * q + 4], v[8 * q + 5]);
+              pk.w = pack_bf16x2(v[8 * q + 6], v[8 * q + 7]);
+              const int chunk = ((c & 1) * 4 + q) ^ (lane & 7);
+              *reinterpret_cast<uint4 *>(row_s + (c >> 1) * kOutBoxBytes + chunk * 16) = pk;
+            }
+          } else {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const int chunk = q ^ (lane & 7);
+              *reinterpret_cast<float4 *>(row_s + c * kOutBoxBytes + chunk * 16) =
+                  make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+            }
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          const int boxes = p.y_bf16 ? 2 : 4, box_cols = p.y_bf16 ? 64 : 32;
+          for (int b = 0; b < boxes; ++b)
+            if (n0 + b * box_cols < p.N) tma_store_2d(&tmap_y, stage + b * kOutBoxBytes, n0 + b * box_cols, row0);
+          bulk_commit_group();
+        }
+        continue;
+      }
+      // Direct stores (y not addressable by a tensor map).  Every lane takes
+      // part in the shuffles; only the stores depend on the lane's row.
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          r[c][j] = __float_as_uint((__uint_as_float(r[c][j]) * ga) * __shfl_sync(0xffffffffu, gl[c], j));
+      const int row = row0 + lane;
+      if (!row_live) continue;  // no warp-collective operation follows in this iteration
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const int nc = n0 + c * 32;
         float v[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int n = nc + j;
-          const float g = n < p.N ? __ldg(p.b_globals + n_base + n) : 0.0f;
-          v[j] = (__uint_as_float(r[c][j]) * ga) * g;
-        }
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[c][j]);
         const long long off = (long long)row * p.ldy + nc;
         const bool full_cols = nc + 32 <= p.N;
         if (p.y_bf16) {
@@ -351,6 +520,8 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
     }
+    // Stores in flight read this CTA's shared memory: complete them before exit.
+    if (lane == 0 && p.tma_store) bulk_wait_all();
   }
   tc_fence_before();
   __syncthreads();
@@ -404,6 +575,21 @@ int encode_rows_u8(CUtensorMap *map, const void *base, uint64_t rows, uint64_t r
   return FPB_OK;
 }
 
+bool encode_store_map(CUtensorMap *map, void *y, bool bf16, uint64_t rows, uint64_t cols, uint64_t ld,
+                      uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  const uint64_t esize = bf16 ? 2 : 4;
+  if (!fn || (reinterpret_cast<uintptr_t>(y) & 15) || ((ld * esize) & 15) || ld < cols || rows == 0 || cols == 0)
+    return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * esize};
+  cuuint32_t box[2] = {(cuuint32_t)(128 / esize), box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, y, dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 static unsigned grid_for(size_t n) {
   size_t g = (n + 255) / 256, cap = (size_t)sm_count() * 16;
   return (unsigned)std::max<size_t>(1, std::min(g, cap));
@@ -423,7 +609,7 @@ int prepare_gemm_weights(fpb_nvfp4_matrix *m, cudaStream_t s) {
     FPB_CUDA_TRY(cudaMalloc(&x->sf_tiled, bytes));
     x->sf_tiled_bytes = bytes;
   }
-  sf_tile_kernel<<<grid_for(bytes), 256, 0, s>>>(m->scales, m->rows, m->cols, x->sf_tiled, bytes);
+  sf_tile_kernel<<<grid_for(bytes), 256, 0, s>>>(m->scales, m->rows, m->cols, x->sf_tiled, bytes, 0);
   FPB_LAUNCH_CHECK("sf_tile_kernel");
   int *flag = nullptr;
   int neg = 0;
@@ -461,7 +647,7 @@ static int quantize_act_impl(const T *x, size_t rows, size_t cols, uint8_t *pack
   uint32_t *amax = reinterpret_cast<uint32_t *>(amax_scratch);
   act_amax_kernel<T><<<grid_for(rows * cols), 256, 0, s>>>(x, rows * cols, amax);
   FPB_LAUNCH_CHECK("act_amax_kernel");
-  act_encode_kernel<T><<<grid_for(rows * cols / 16), 256, 0, s>>>(x, rows, cols, amax, packed, sf_tiled,
+  act_encode_kernel<T><<<grid_for(rows * 32), 256, 0, s>>>(x, rows, cols, amax, packed, sf_tiled,
                                                                    global_out);
   FPB_LAUNCH_CHECK("act_encode_kernel");
   return FPB_OK;
@@ -543,10 +729,12 @@ extern "C" int fpb_nvfp4_gemm_q(fpb_nvfp4_matrix *w, size_t row_begin, size_t ro
   p.n_base = (int)row_begin;
   p.kb_count = (int)((w->cols + 255) / 256);
   p.error = err;
+  CUtensorMap tmap_y{};
+  p.tma_store = encode_store_map(&tmap_y, y, p.y_bf16, m, p.N, p.ldy, 32);
   const size_t tiles = (size_t)((p.N + kBN - 1) / kBN) * ((m + kBM - 1) / kBM);
   const unsigned grid = (unsigned)std::min<size_t>(tiles, (size_t)std::max(1, sm_count()));
   nvfp4_gemm_kernel<<<grid, 192, kGemmSmem, s>>>(tmap_a, *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b),
-                                                 p);
+                                                 tmap_y, *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b), p);
   FPB_LAUNCH_CHECK("nvfp4_gemm_kernel");
   return FPB_OK;
 }
@@ -571,7 +759,8 @@ extern "C" int fpb_nvfp4_gemm(fpb_nvfp4_matrix *w, size_t row_begin, size_t row_
 
 extern "C" int fpb_nvfp4_grouped_gemm_q(fpb_nvfp4_matrix *w, const uint8_t *a_packed, const uint8_t *a_sf_tiled,
                                         const float *a_global, size_t padded_rows, const int32_t *tile_experts,
-                                        size_t rows_per_expert, void *y, int y_dtype, void *stream) {
+                                        const int32_t *token_rows, size_t rows_per_expert, void *y, int y_dtype,
+                                        void *stream) {
   if (!w || !a_packed || !a_sf_tiled || !a_global || !tile_experts || !y)
     return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_grouped_gemm_q: null pointer");
   if (padded_rows == 0 || padded_rows % kBM || padded_rows / kBM > 65535)
@@ -615,12 +804,100 @@ extern "C" int fpb_nvfp4_grouped_gemm_q(fpb_nvfp4_matrix *w, const uint8_t *a_pa
   p.kb_count = (int)((w->cols + 255) / 256);
   p.error = err;
   p.tile_experts = tile_experts;
+  p.row_tokens = token_rows;
   p.n_experts = (int)(w->rows / rows_per_expert);
+  CUtensorMap tmap_y{};
+  p.tma_store = encode_store_map(&tmap_y, y, p.y_bf16, padded_rows, p.N, p.ldy, 32);
   const size_t tiles = (rows_per_expert / kBN) * (padded_rows / kBM);
   const unsigned grid = (unsigned)std::min<size_t>(tiles, (size_t)std::max(1, sm_count()));
   nvfp4_gemm_kernel<<<grid, 192, kGemmSmem, s>>>(tmap_a, *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b),
-                                                 p);
+                                                 tmap_y, *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b), p);
   FPB_LAUNCH_CHECK("nvfp4_gemm_kernel(grouped)");
+  return FPB_OK;
+}
+
+// Fused gate/up copies (interleaved factors, 64-row code map) for an
+// intermediate size `inter`; built once per matrix, synchronises `s`.
+static int prepare_glu_weights(fpb_nvfp4_matrix *m, size_t inter, cudaStream_t s) {
+  int st = prepare_gemm_weights(m, s);
+  if (st) return st;
+  MatrixExtras *x = m->extras;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  if (x->sf_tiled_glu && x->glu_inter == inter) return FPB_OK;
+  const size_t bytes = sf_tiled_bytes(m->rows, m->cols);
+  if (!x->sf_tiled_glu) FPB_CUDA_TRY(cudaMalloc(&x->sf_tiled_glu, bytes));
+  x->glu_inter = 0;
+  sf_tile_kernel<<<grid_for(bytes), 256, 0, s>>>(m->scales, m->rows, m->cols, x->sf_tiled_glu, bytes, inter);
+  FPB_LAUNCH_CHECK("sf_tile_kernel(glu)");
+  const uint8_t *codes = x->packed_folded ? x->packed_folded : m->packed;
+  if ((st = encode_rows_u8(reinterpret_cast<CUtensorMap *>(x->tmap_b64), codes, m->rows, m->cols / 2, 64))) return st;
+  FPB_CUDA_TRY(cudaStreamSynchronize(s));
+  x->glu_inter = inter;
+  return FPB_OK;
+}
+
+extern "C" int fpb_nvfp4_grouped_gemm_swiglu_q(fpb_nvfp4_matrix *w, const uint8_t *a_packed,
+                                               const uint8_t *a_sf_tiled, const float *a_global, size_t padded_rows,
+                                               const int32_t *tile_experts, const int32_t *token_rows, size_t inter,
+                                               void *h, int h_dtype, uint32_t *amax_bits, void *stream) {
+  if (!w || !a_packed || !a_sf_tiled || !a_global || !tile_experts || !h || !amax_bits)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_grouped_gemm_swiglu_q: null pointer");
+  if (padded_rows == 0 || padded_rows % kBM || padded_rows / kBM > 65535)
+    return fail(FPB_ERR_SHAPE, "fpb_nvfp4_grouped_gemm_swiglu_q: padded_rows %zu must be a positive multiple of %d",
+                padded_rows, kBM);
+  if (inter == 0 || inter % 64 || w->rows % (2 * inter))
+    return fail(FPB_ERR_SHAPE, "fpb_nvfp4_grouped_gemm_swiglu_q: inter %zu must be a multiple of 64 with 2*inter "
+                "dividing %zu", inter, w->rows);
+  if (h_dtype != FPB_F32 && h_dtype != FPB_BF16)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_grouped_gemm_swiglu_q: dtype");
+  if (reinterpret_cast<uintptr_t>(h) & 15)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_grouped_gemm_swiglu_q: h must be 16-byte aligned");
+  cudaStream_t s = as_stream(stream);
+  int st = prepare_glu_weights(w, inter, s);
+  if (st) return st;
+  CUtensorMap tmap_a, tmap_y{};
+  if ((st = encode_rows_u8(&tmap_a, a_packed, padded_rows, w->cols / 2, kBM))) return st;
+  if (!encode_store_map(&tmap_y, h, h_dtype == FPB_BF16, padded_rows, inter, inter, 32))
+    return fail(FPB_ERR_CUDA, "fpb_nvfp4_grouped_gemm_swiglu_q: cannot encode the output map");
+  {
+    static std::mutex mu;
+    static std::vector<int> attr_devs;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (std::find(attr_devs.begin(), attr_devs.end(), dev) == attr_devs.end()) {
+      FPB_CUDA_TRY(
+          cudaFuncSetAttribute(nvfp4_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem));
+      attr_devs.push_back(dev);
+    }
+  }
+  FPB_CUDA_TRY(cudaMemsetAsync(amax_bits, 0, sizeof(uint32_t), s));
+  GemmParams p{};
+  p.a_sf = a_sf_tiled;
+  p.b_sf = w->extras->sf_tiled_glu;
+  p.a_global = a_global;
+  p.b_globals = w->row_globals;
+  p.y = h;
+  p.N = (int)(2 * inter);
+  p.ldy = (long long)inter;
+  p.y_bf16 = h_dtype == FPB_BF16;
+  p.M = (int)padded_rows;
+  p.n_base = 0;
+  p.kb_count = (int)((w->cols + 255) / 256);
+  p.error = device_error_ptr();
+  p.tile_experts = tile_experts;
+  p.row_tokens = token_rows;
+  p.n_experts = (int)(w->rows / (2 * inter));
+  p.tma_store = 1;
+  p.glu = 1;
+  p.amax_bits = amax_bits;
+  const size_t tiles = (2 * inter / kBN) * (padded_rows / kBM);
+  const unsigned grid = (unsigned)std::min<size_t>(tiles, (size_t)std::max(1, sm_count()));
+  nvfp4_gemm_kernel<<<grid, 192, kGemmSmem, s>>>(tmap_a, *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b),
+                                                 tmap_y, *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b64),
+                                                 p);
+  FPB_LAUNCH_CHECK("nvfp4_gemm_kernel(grouped swiglu)");
   return FPB_OK;
 }
 

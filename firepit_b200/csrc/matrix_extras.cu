@@ -9,6 +9,7 @@ void release_matrix_extras(fpb_nvfp4_matrix *m) {
   if (!m || !m->extras) return;
   cudaFree(m->extras->sf_tiled);
   cudaFree(m->extras->packed_folded);
+  cudaFree(m->extras->sf_tiled_glu);
   delete m->extras;
   m->extras = nullptr;
 }

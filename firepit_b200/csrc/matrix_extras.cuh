@@ -17,5 +17,13 @@ struct MatrixExtras {
   // TMA descriptor of the codes as read by the GEMM (opaque 128 bytes).
   alignas(64) unsigned char tmap_b[128];
   bool tmap_valid = false;
+  // Fused gate/up + SwiGLU GEMM (stacked experts of 2*glu_inter rows, gate
+  // rows first): the factors tiled over rows reordered so that each 128-row
+  // tile holds gate rows [64b, 64b+64) then up rows [64b, 64b+64) of one
+  // expert, and a TMA map of the codes in 64-row boxes (the two halves of a
+  // tile are loaded separately, so the codes are not copied).
+  uint8_t *sf_tiled_glu = nullptr;
+  size_t glu_inter = 0;
+  alignas(64) unsigned char tmap_b64[128];
 };
 }  // namespace fpb

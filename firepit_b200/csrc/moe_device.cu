@@ -261,8 +261,15 @@ struct GatherRows {
   }
 };
 
+// Plain rows [rows, cols] (e.g. the fused gate/up GEMM's SwiGLU output).
+template <typename T>
+struct PlainRows {
+  const T *x;
+  size_t cols;
+  __device__ __forceinline__ void load16(size_t r, size_t g, float v[16]) const { load16_vec(x + r * cols + g * 16, v); }
+};
+
 // SwiGLU rows (swiglu.rs:16): gate = first `cols` columns, up = next `cols`.
-__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + expf(g * -1.0f)) * u; }
 
 template <typename T>
 struct SwigluRows {
@@ -284,34 +291,43 @@ __device__ __forceinline__ size_t valid_rows(size_t rows, const int32_t *valid) 
   return valid ? min(rows, (size_t)max(*valid, 0)) : rows;
 }
 
+// Both row kernels: one warp per row (grid-stride over rows), lane l encodes
+// the 16-column groups l, l + 32, ... of the row.  skip (nullable): rows r
+// with skip[r] < 0 (a layout's padding rows) are neither read nor written.
 template <class Rows>
-__global__ void rows_amax_kernel(Rows rows_src, size_t rows, const int32_t *valid, size_t cols, uint32_t *amax_bits) {
-  const size_t gpr = cols / 16, n = valid_rows(rows, valid) * gpr;
+__global__ void rows_amax_kernel(Rows rows_src, size_t rows, const int32_t *valid, const int32_t *skip, size_t cols,
+                                 uint32_t *amax_bits) {
+  const int gpr = (int)(cols / 16), lane = threadIdx.x & 31;
+  const size_t n = valid_rows(rows, valid), warps = (size_t)gridDim.x * (blockDim.x / 32);
   uint32_t m = 0;
-  size_t stride = (size_t)gridDim.x * blockDim.x;
-  for (size_t gi = (size_t)blockIdx.x * blockDim.x + threadIdx.x; gi < n; gi += stride) {
-    float v[16];
-    rows_src.load16(gi / gpr, gi % gpr, v);
+  for (size_t r = (size_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; r < n; r += warps) {
+    if (skip && skip[r] < 0) continue;
+    for (int g = lane; g < gpr; g += 32) {
+      float v[16];
+      rows_src.load16(r, g, v);
 #pragma unroll
-    for (int i = 0; i < 16; ++i) m = max(m, __float_as_uint(v[i]) & 0x7fffffffu);
+      for (int i = 0; i < 16; ++i) m = max(m, __float_as_uint(v[i]) & 0x7fffffffu);
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
-  if ((threadIdx.x & 31) == 0) atomicMax(amax_bits, m);
+  if (lane == 0 && m) atomicMax(amax_bits, m);
 }
 
 template <class Rows>
-__global__ void rows_encode_kernel(Rows rows_src, size_t rows, const int32_t *valid, size_t cols,
+__global__ void rows_encode_kernel(Rows rows_src, size_t rows, const int32_t *valid, const int32_t *skip, size_t cols,
                                    const uint32_t *amax_bits, uint8_t *packed, uint8_t *sf_tiled, float *global_out) {
   const float global = __fdiv_rn(__uint_as_float(*amax_bits), 2688.0f);
   if (blockIdx.x == 0 && threadIdx.x == 0) *global_out = global;
-  const size_t gpr = cols / 16, n = valid_rows(rows, valid) * gpr;
-  size_t stride = (size_t)gridDim.x * blockDim.x;
-  for (size_t gi = (size_t)blockIdx.x * blockDim.x + threadIdx.x; gi < n; gi += stride) {
-    const size_t r = gi / gpr, g = gi % gpr;
-    float v[16];
-    rows_src.load16(r, g, v);
-    encode_group16(v, global, packed + r * (cols / 2) + g * 8, sf_tiled + sf_tiled_offset(r, g, cols));
+  const int gpr = (int)(cols / 16), lane = threadIdx.x & 31;
+  const size_t n = valid_rows(rows, valid), warps = (size_t)gridDim.x * (blockDim.x / 32);
+  for (size_t r = (size_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; r < n; r += warps) {
+    if (skip && skip[r] < 0) continue;
+    for (int g = lane; g < gpr; g += 32) {
+      float v[16];
+      rows_src.load16(r, g, v);
+      encode_group16(v, global, packed + r * (cols / 2) + g * 8, sf_tiled + sf_tiled_offset(r, g, cols));
+    }
   }
 }
 
@@ -447,6 +463,13 @@ __global__ void moe_route_dest_kernel(const int32_t *ids, int tokens, int width,
 
 static unsigned stride_grid(size_t n) {
   size_t g = (n + 255) / 256, cap = (size_t)sm_count() * 8;
+  return (unsigned)std::max<size_t>(1, std::min(g, cap));
+}
+
+// Row kernels: one warp per row, 8 rows per 256-thread block, at most 8
+// blocks per SM resident (grid-stride beyond).
+static unsigned row_grid(size_t rows) {
+  size_t g = (rows + 7) / 8, cap = (size_t)sm_count() * 8;
   return (unsigned)std::max<size_t>(1, std::min(g, cap));
 }
 
@@ -601,8 +624,9 @@ extern "C" int fpb_moe_gather_quantize(const void *x, int x_dtype, size_t tokens
       FPB_LAUNCH_CHECK("act_amax_kernel");
     }
     GatherRows<T> src{xs, token_rows, cols, (int)tokens};
-    rows_encode_kernel<<<stride_grid(rows * cols / 16), 256, 0, s>>>(src, rows, valid_rows, cols, amax, packed,
-                                                                      sf_tiled, global_out);
+    const int32_t *skip = (flags & FPB_QUANT_SKIP_PADDING) ? token_rows : nullptr;
+    rows_encode_kernel<<<row_grid(rows), 256, 0, s>>>(src, rows, valid_rows, skip, cols, amax, packed, sf_tiled,
+                                                       global_out);
     FPB_LAUNCH_CHECK("rows_encode_kernel(gather)");
     return (int)FPB_OK;
   });
@@ -644,13 +668,44 @@ extern "C" int fpb_swiglu_quantize(const void *gate_up, int dtype, size_t rows, 
   return with_dtype(dtype, [&](auto tp) {
     using T = std::remove_const_t<std::remove_pointer_t<decltype(tp)>>;
     SwigluRows<T> src{static_cast<const T *>(gate_up), inter};
-    const unsigned grid = stride_grid(rows * inter / 16);
+    const unsigned grid = row_grid(rows);
     if (!given) {
-      rows_amax_kernel<<<grid, 256, 0, s>>>(src, rows, valid_rows, inter, amax);
+      rows_amax_kernel<<<grid, 256, 0, s>>>(src, rows, valid_rows, nullptr, inter, amax);
       FPB_LAUNCH_CHECK("rows_amax_kernel(swiglu)");
     }
-    rows_encode_kernel<<<grid, 256, 0, s>>>(src, rows, valid_rows, inter, amax, packed, sf_tiled, global_out);
+    rows_encode_kernel<<<grid, 256, 0, s>>>(src, rows, valid_rows, nullptr, inter, amax, packed, sf_tiled,
+                                             global_out);
     FPB_LAUNCH_CHECK("rows_encode_kernel(swiglu)");
+    return (int)FPB_OK;
+  });
+}
+
+extern "C" int fpb_rows_quantize(const void *x, int dtype, size_t rows, const int32_t *valid_rows,
+                                 const int32_t *token_rows, size_t cols, uint8_t *packed, uint8_t *sf_tiled,
+                                 float *global_out, float *amax_scratch, int flags, void *stream) {
+  if (!x || !packed || !sf_tiled || !global_out || !amax_scratch)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_rows_quantize: null pointer");
+  if (rows == 0 || cols == 0 || cols % 32) return fail(FPB_ERR_SHAPE, "fpb_rows_quantize: shape");
+  if ((flags & FPB_QUANT_SKIP_PADDING) && !token_rows)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_rows_quantize: FPB_QUANT_SKIP_PADDING needs token_rows");
+  if (reinterpret_cast<uintptr_t>(x) & 15)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_rows_quantize: x must be 16-byte aligned");
+  cudaStream_t s = as_stream(stream);
+  uint32_t *amax = reinterpret_cast<uint32_t *>(amax_scratch);
+  const bool given = flags & FPB_QUANT_AMAX_GIVEN;
+  if (!given) FPB_CUDA_TRY(cudaMemsetAsync(amax, 0, sizeof(uint32_t), s));
+  if (cols % 256) FPB_CUDA_TRY(cudaMemsetAsync(sf_tiled, 0, sf_tiled_bytes(rows, cols), s));
+  return with_dtype(dtype, [&](auto tp) {
+    using T = std::remove_const_t<std::remove_pointer_t<decltype(tp)>>;
+    PlainRows<T> src{static_cast<const T *>(x), cols};
+    const int32_t *skip = (flags & FPB_QUANT_SKIP_PADDING) ? token_rows : nullptr;
+    const unsigned grid = row_grid(rows);
+    if (!given) {
+      rows_amax_kernel<<<grid, 256, 0, s>>>(src, rows, valid_rows, skip, cols, amax);
+      FPB_LAUNCH_CHECK("rows_amax_kernel(rows)");
+    }
+    rows_encode_kernel<<<grid, 256, 0, s>>>(src, rows, valid_rows, skip, cols, amax, packed, sf_tiled, global_out);
+    FPB_LAUNCH_CHECK("rows_encode_kernel(rows)");
     return (int)FPB_OK;
   });
 }
@@ -751,7 +806,7 @@ extern "C" int fpb_swiglu_amax(const void *gate_up, int dtype, size_t rows, cons
   return with_dtype(dtype, [&](auto tp) {
     using T = std::remove_const_t<std::remove_pointer_t<decltype(tp)>>;
     SwigluRows<T> src{static_cast<const T *>(gate_up), inter};
-    rows_amax_kernel<<<stride_grid(rows * inter / 16), 256, 0, s>>>(src, rows, valid_rows, inter, amax);
+    rows_amax_kernel<<<row_grid(rows), 256, 0, s>>>(src, rows, valid_rows, nullptr, inter, amax);
     FPB_LAUNCH_CHECK("rows_amax_kernel(swiglu)");
     return (int)FPB_OK;
   });

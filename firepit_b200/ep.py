@@ -122,7 +122,7 @@ class DeviceOps:
                    lay["pad"].data_ptr(), a1.data_ptr(), sf1.data_ptr(), scal.data_ptr(), scal[1:].data_ptr(),
                    N.FPB_QUANT_AMAX_GIVEN, self._s())
             N.call("fpb_nvfp4_grouped_gemm_q", w1.handle, a1.data_ptr(), sf1.data_ptr(), scal.data_ptr(), cap,
-                   lay["te"].data_ptr(), 2 * inter, y1.data_ptr(), N.FPB_BF16, self._s())
+                   lay["te"].data_ptr(), None, 2 * inter, y1.data_ptr(), N.FPB_BF16, self._s())
         pad = lay["pad"] if n else t.zeros(1, dtype=t.int32, device=self.device)
         a_act = amax_reduce(self.swiglu_amax(y1, pad) if n else t.zeros(1, dtype=t.int32, device=self.device))
         if n:
@@ -134,7 +134,7 @@ class DeviceOps:
                    self._s())
             y2 = self.empty((cap, h), t.bfloat16)
             N.call("fpb_nvfp4_grouped_gemm_q", w2.handle, a2.data_ptr(), sf2.data_ptr(), scal[2:].data_ptr(), cap,
-                   lay["te"].data_ptr(), h, y2.data_ptr(), N.FPB_BF16, self._s())
+                   lay["te"].data_ptr(), None, h, y2.data_ptr(), N.FPB_BF16, self._s())
             ones = t.ones(n, 1, dtype=t.float32, device=self.device)
             N.call("fpb_moe_combine", y2.data_ptr(), N.FPB_BF16, cap, h, lay["inv"].data_ptr(), ones.data_ptr(), n, 1,
                    1, y.data_ptr(), _dt(y), self._s())

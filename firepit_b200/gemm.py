@@ -107,11 +107,13 @@ def device_error(reset: bool = True) -> int:
 
 
 def nvfp4_grouped_gemm_q(weight: Nvfp4Matrix, a_packed, a_sf, a_global, tile_experts, rows_per_expert: int, y,
-                         stream=None) -> None:
+                         stream=None, token_rows=None) -> None:
     """Grouped GEMM on quantized activations (fpb_nvfp4_grouped_gemm_q).
 
     a_packed: [padded_rows, K/2] u8; a_sf: tiled factors; a_global: f32 [1];
     tile_experts: device int32 [padded_rows / 128]; y: [padded_rows, rows_per_expert].
+    token_rows (device int32 [padded_rows], optional): the layout's tokens;
+    padding rows' outputs are then unspecified.
     """
     from .weights import current_stream_handle
     padded_rows = a_packed.shape[0]
@@ -121,7 +123,61 @@ def nvfp4_grouped_gemm_q(weight: Nvfp4Matrix, a_packed, a_sf, a_global, tile_exp
         raise ShapeError(f"{tile_experts.numel()} tile experts for {padded_rows} rows (128-row tiles)")
     s = current_stream_handle(y.device) if stream is None else stream
     N.call("fpb_nvfp4_grouped_gemm_q", weight.handle, a_packed.data_ptr(), a_sf.data_ptr(), a_global.data_ptr(),
-           padded_rows, tile_experts.data_ptr(), rows_per_expert, y.data_ptr(), _dtype_code(y), s)
+           padded_rows, tile_experts.data_ptr(), None if token_rows is None else token_rows.data_ptr(),
+           rows_per_expert, y.data_ptr(), _dtype_code(y), s)
+
+
+def nvfp4_grouped_gemm_swiglu_q(weight: Nvfp4Matrix, a_packed, a_sf, a_global, tile_experts, inter: int, h,
+                                amax=None, stream=None, token_rows=None):
+    """The gate/up grouped GEMM fused with SwiGLU (fpb_nvfp4_grouped_gemm_swiglu_q).
+
+    weight: experts of 2 * inter rows (gate rows, then up rows); h: [padded_rows,
+    inter] f32/bf16.  Returns ``amax`` (device int32 [1]): max |h| as float bits,
+    the input of ``rows_quantize(..., amax=...)``.  token_rows as in
+    ``nvfp4_grouped_gemm_q`` (padding rows also left out of the amax).
+    """
+    import torch
+    from .weights import current_stream_handle
+    padded_rows = a_packed.shape[0]
+    if tuple(h.shape) != (padded_rows, inter) or not h.is_contiguous():
+        raise ShapeError(f"h shape {tuple(h.shape)} != ({padded_rows}, {inter})")
+    if tile_experts.numel() * 128 != padded_rows:
+        raise ShapeError(f"{tile_experts.numel()} tile experts for {padded_rows} rows (128-row tiles)")
+    if amax is None:
+        amax = torch.zeros(1, dtype=torch.int32, device=h.device)
+    s = current_stream_handle(h.device) if stream is None else stream
+    N.call("fpb_nvfp4_grouped_gemm_swiglu_q", weight.handle, a_packed.data_ptr(), a_sf.data_ptr(),
+           a_global.data_ptr(), padded_rows, tile_experts.data_ptr(),
+           None if token_rows is None else token_rows.data_ptr(), inter, h.data_ptr(), _dtype_code(h),
+           amax.data_ptr(), s)
+    return amax
+
+
+def rows_quantize(x, valid_rows=None, amax=None, stream=None, token_rows=None, out=None):
+    """NVFP4-quantizes rows x [rows, cols] (fpb_rows_quantize): (packed, tiled
+    factors, global f32 [1]).  ``amax`` (device int32 [1], float bits) gives
+    the |x| maximum to derive the global from; ``valid_rows`` (device int32
+    [1]) limits the rows written; with ``token_rows`` padding rows (-1) are
+    skipped.  ``out``: optional (packed, sf) buffers to write into."""
+    import torch
+    from .weights import current_stream_handle
+    rows, cols = x.shape
+    if out is None:
+        packed = torch.empty(rows, cols // 2, dtype=torch.uint8, device=x.device)
+        sf = torch.empty(int(N.lib.fpb_nvfp4_act_sf_bytes(rows, cols)), dtype=torch.uint8, device=x.device)
+    else:
+        packed, sf = out
+    scal = torch.zeros(2, dtype=torch.float32, device=x.device)
+    flags = 0 if token_rows is None else N.FPB_QUANT_SKIP_PADDING
+    if amax is not None:
+        scal[1:].view(torch.int32).copy_(amax.view(torch.int32).reshape(1))
+        flags |= N.FPB_QUANT_AMAX_GIVEN
+    s = current_stream_handle(x.device) if stream is None else stream
+    N.call("fpb_rows_quantize", x.data_ptr(), _dtype_code(x), rows,
+           None if valid_rows is None else valid_rows.data_ptr(),
+           None if token_rows is None else token_rows.data_ptr(), cols, packed.data_ptr(), sf.data_ptr(),
+           scal.data_ptr(), scal[1:].data_ptr(), flags, s)
+    return packed, sf, scal[:1]
 
 
 class Nvfp4GroupedGemmView:

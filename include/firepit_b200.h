@@ -51,6 +51,11 @@ enum { FPB_F32 = 0, FPB_BF16 = 1 };
  * (fpb_act_amax / fpb_swiglu_amax, then an all-reduce MAX), so that every
  * rank encodes with the same global. */
 enum { FPB_QUANT_AMAX_GIVEN = 1 };
+/* FPB_QUANT_SKIP_PADDING: rows of a MoE layout whose token is -1 (padding)
+ * are neither read nor written nor counted in the amax; for activations
+ * whose GEMM gets the same token_rows (fpb_nvfp4_grouped_gemm_q), which
+ * then ignores those rows. */
+enum { FPB_QUANT_SKIP_PADDING = 2 };
 
 /* Library / error reporting ------------------------------------------------ */
 const char *fpb_version(void);
@@ -202,10 +207,15 @@ int fpb_nvfp4_gemm(fpb_nvfp4_matrix *w, size_t row_begin, size_t row_end, const 
  * of w:  y[t*128 + i, n] = ga * g[e*rpe + n] * sum_k a(t*128+i, k) w(e*rpe+n, k).
  * y: [padded_rows, rows_per_expert]; rows_per_expert % 128 == 0.  An expert
  * id outside [0, w.rows / rows_per_expert) leaves that tile unwritten and
- * records device error 106 (fpb_device_error). */
+ * records device error 106 (fpb_device_error).  token_rows (nullable, the
+ * layout's token of each row, -1 = padding): padding rows' outputs are then
+ * not needed (rows of a 32-row group that is all padding are not written,
+ * the others hold unspecified values), so their activations may be anything
+ * (see FPB_QUANT_SKIP_PADDING). */
 int fpb_nvfp4_grouped_gemm_q(fpb_nvfp4_matrix *w, const uint8_t *a_packed, const uint8_t *a_sf_tiled,
                              const float *a_global, size_t padded_rows, const int32_t *tile_experts,
-                             size_t rows_per_expert, void *y, int y_dtype, void *stream);
+                             const int32_t *token_rows, size_t rows_per_expert, void *y, int y_dtype,
+                             void *stream);
 /* First error code a tensor-core kernel recorded (0: none; bounded waits
  * that gave up); synchronises the device; reset != 0 clears it. */
 int fpb_device_error(int *out, int reset);
@@ -292,7 +302,8 @@ int fpb_moe_gather(const void *x, int x_dtype, size_t tokens, size_t cols, const
 /* The gather fused with the NVFP4 activation quantize of fpb_nvfp4_quantize_act
  * (global from amax over x): packed [rows, cols/2], tiled factors, global.
  * valid_rows (nullable device int32, e.g. fpb_moe_layout's padded_rows):
- * rows at or past it are not written (their row tiles are skipped). */
+ * rows at or past it are not written (their row tiles are skipped); with
+ * FPB_QUANT_SKIP_PADDING neither are padding rows (token -1). */
 int fpb_moe_gather_quantize(const void *x, int x_dtype, size_t tokens, size_t cols, const int32_t *token_rows,
                             size_t rows, const int32_t *valid_rows, uint8_t *packed, uint8_t *sf_tiled,
                             float *global_out, float *amax_scratch, int flags, void *stream);
@@ -305,6 +316,27 @@ int fpb_swiglu(const void *gate_up, int dtype, size_t rows, size_t inter, void *
 int fpb_swiglu_quantize(const void *gate_up, int dtype, size_t rows, const int32_t *valid_rows, size_t inter,
                         uint8_t *packed, uint8_t *sf_tiled, float *global_out, float *amax_scratch, int flags,
                         void *stream);
+/* The gate/up GEMM fused with SwiGLU (gemm/nvfp4.rs:57-105 grouped GEMM, then
+ * swiglu.rs:16 on its f32 output): w holds experts of 2*inter rows each
+ * (gate rows, then up rows); h [padded_rows, inter] (f32/bf16, 16-byte
+ * aligned) = silu(gate) * up computed from the f32 accumulators (no rounding
+ * of gate/up, as the reference's f32 swiglu input); *amax_bits = max |h| as
+ * stored (float bits; zeroed first).  inter % 64 == 0.  The first call on a
+ * matrix builds its interleaved factor copy and synchronises `stream`.
+ * token_rows as in fpb_nvfp4_grouped_gemm_q; padding rows are also left out
+ * of the amax. */
+int fpb_nvfp4_grouped_gemm_swiglu_q(fpb_nvfp4_matrix *w, const uint8_t *a_packed, const uint8_t *a_sf_tiled,
+                                    const float *a_global, size_t padded_rows, const int32_t *tile_experts,
+                                    const int32_t *token_rows, size_t inter, void *h, int h_dtype,
+                                    uint32_t *amax_bits, void *stream);
+/* NVFP4 activation quantize of rows x [rows, cols] (f32/bf16, 16-byte
+ * aligned) as fpb_swiglu_quantize without the SwiGLU: with
+ * FPB_QUANT_AMAX_GIVEN the global comes from *amax_scratch (e.g. the fused
+ * GEMM's amax_bits); rows at or past *valid_rows are not written, nor (with
+ * FPB_QUANT_SKIP_PADDING) rows whose token_rows entry is -1. */
+int fpb_rows_quantize(const void *x, int dtype, size_t rows, const int32_t *valid_rows,
+                      const int32_t *token_rows, size_t cols, uint8_t *packed, uint8_t *sf_tiled,
+                      float *global_out, float *amax_scratch, int flags, void *stream);
 /* |x| maximum over x[0, n) (f32/bf16) or over SwiGLU(gate_up) rows, as float
  * bits in *amax_scratch (zeroed first unless accumulate != 0). */
 int fpb_act_amax(const void *x, int dtype, size_t n, float *amax_scratch, int accumulate, void *stream);

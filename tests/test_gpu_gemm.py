@@ -78,6 +78,26 @@ def test_gemm_vs_oracle(F, torch, m, n, k):
     assert np.all(np.abs(got - exp) <= 1e-5 * mag + 1e-30)
 
 
+@pytest.mark.parametrize("m,n,dtype", [(200, 200, "f32"), (130, 200, "bf16"), (130, 98, "bf16"), (77, 99, "f32"),
+                                       (300, 520, "bf16")])
+def test_gemm_ragged_output(F, torch, m, n, dtype):
+    """Ragged M and N: tiled stores clipped at the edges (row pitch a multiple
+    of 16 bytes) and direct stores (unaligned pitch, e.g. 98 bf16 columns)."""
+    k = 512
+    W, h = make_weight(F, n, k, seed=n + 7)
+    x = F.synth_normal((m, k), seed=m + 1, stream_id=2, dtype=torch.bfloat16)
+    tdt = torch.bfloat16 if dtype == "bf16" else torch.float32
+    y = torch.full((m + 1, n), float("nan"), dtype=tdt, device="cuda")  # one guard row past the output
+    F.nvfp4_gemm(W, x, y[:m], F.GemmTile(1, 1, 32)).submit(F.Eager())
+    assert F.device_error() == 0
+    exp, mag = expected_gemm(h, x.float().cpu().numpy(), range(0, n))
+    got = y[:m].float().cpu().numpy().astype(np.float64)
+    assert np.all(np.isfinite(got))
+    assert torch.isnan(y[m].float()).all()  # nothing written past the last row
+    tol = 1e-5 if dtype == "f32" else 4e-3
+    assert np.all(np.abs(got - exp) <= tol * mag + 1e-30)
+
+
 def test_gemm_view_bf16_output(F, torch):
     W, h = make_weight(F, 512, 1024, seed=9)
     x = F.synth_normal((128, 1024), seed=4, stream_id=2, dtype=torch.bfloat16)

@@ -169,10 +169,13 @@ def cpu_baseline(seconds: float):
 
 # ---- our arm ---------------------------------------------------------------------------------
 def load_traffic():
-    f = ROOT / "profiles" / "gemv_nvfp4_config0.json"
+    """DRAM bytes per GEMV launch from the committed ncu summary (first line:
+    `dram_bytes_per_launch <bytes>`), or None."""
+    f = ROOT / "profiles" / "gemv_nvfp4_config0_traffic.txt"
     if f.exists():
         try:
-            return json.loads(f.read_text()).get("dram_bytes_per_launch")
+            key, val = f.read_text().split("\n", 1)[0].split()
+            return int(val) if key == "dram_bytes_per_launch" else None
         except Exception:
             return None
     return None
@@ -273,22 +276,30 @@ def ours_arm(args):
     total_bytes = mats * GEMV_BYTES  # all ranks together, per step
     value = total_bytes / (ms_per_step * 1e-3) / 1e9
 
-    # ---- end to end through the public API, host buffers, no graph ------------
+    # ---- end to end through the public API, host buffers ----------------------
+    # The reference's Graph sink (sink.rs:94-105): one CUDA graph holds the
+    # copy of x from pinned host memory, the `gemv(...).submit(sink)` calls
+    # and (one GPU) the copy of y back to pinned host memory.
     xh = torch.empty(1, COLS, dtype=torch.bfloat16, pin_memory=True)
     xh.copy_(x.cpu())
     yh = torch.empty(g, mats, rows_per_rank, dtype=torch.bfloat16, pin_memory=True)
-    sink = F.Async()
     xd = torch.empty_like(x)
-
-    def e2e_step():
+    for c in range(mats):  # eager once: every code path initialised outside capture
+        F.gemv(slices[c], x, y_local[c:c + 1], F.DEFAULT_GEMV_TILE).submit(F.Async())
+    torch.cuda.synchronize()
+    gsink = F.Graph()
+    with gsink:
         xd.copy_(xh, non_blocking=True)
         for c in range(mats):
-            F.gemv(slices[c], xd, y_local[c:c + 1], F.DEFAULT_GEMV_TILE).submit(sink)
+            F.gemv(slices[c], xd, y_local[c:c + 1], F.DEFAULT_GEMV_TILE).submit(gsink)
+        if g == 1:
+            yh[0].copy_(y_local, non_blocking=True)
+
+    def e2e_step():
+        gsink.replay()
         if g > 1:
             dist.all_gather_into_tensor(y_all, y_local)
-        else:
-            y_all[0].copy_(y_local)
-        yh.copy_(y_all, non_blocking=True)
+            yh.copy_(y_all, non_blocking=True)
 
     e2e_steps = max(1, min(args.steps, 50))
     for _ in range(3):
@@ -330,7 +341,9 @@ def ours_arm(args):
                          "per_launch_us": per_launch_ms * 1e3,
                          "note": "per-launch time = GEMV region / launches (inter-kernel gaps included)"},
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": COLS * 2,
-                    "d2h_bytes_per_step": g * mats * rows_per_rank * 2},
+                    "d2h_bytes_per_step": g * mats * rows_per_rank * 2,
+                    "path": "firepit_b200.gemv(...).submit(Graph sink): H2D x, the GEMVs and D2H y in one CUDA "
+                            "graph" + (" + NCCL all-gather" if g > 1 else "")},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks.summary(),
             "breakdown_ms": {"gemv": gemv_ms / args.steps, "all_gather": gather_ms / args.steps},
@@ -338,7 +351,7 @@ def ours_arm(args):
         if g == 1:
             out["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
         emit(out)
-    del graph
+    del graph, gsink
     if g > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -496,13 +509,19 @@ def gemm_arm(args):
     xh = x.cpu().pin_memory()
     yh = torch.empty(GEMM_MATS, m, n_rank, dtype=torch.bfloat16, pin_memory=True)
     xd = torch.empty_like(x)
-    sink = F.Async()
-
-    def e2e_step():
+    # the reference's Graph sink: H2D x, the GEMMs and D2H y in one CUDA graph
+    for c in range(GEMM_MATS):
+        F.nvfp4_gemm(mats[c], x, ys[c], F.GemmTile(8, 128, 32), workspace=ws).submit(F.Async())
+    torch.cuda.synchronize()
+    gsink = F.Graph()
+    with gsink:
         xd.copy_(xh, non_blocking=True)
         for c in range(GEMM_MATS):
-            F.nvfp4_gemm(mats[c], xd, ys[c], F.GemmTile(8, 128, 32), workspace=ws).submit(sink)
+            F.nvfp4_gemm(mats[c], xd, ys[c], F.GemmTile(8, 128, 32), workspace=ws).submit(gsink)
         yh.copy_(ys, non_blocking=True)
+
+    def e2e_step():
+        gsink.replay()
 
     e2e_steps = max(1, min(args.steps, 20))
     for _ in range(2):
@@ -544,7 +563,9 @@ def gemm_arm(args):
                          "parallelism": f"N-split x{g} + NCCL all-gather" if g > 1 else "single GPU"},
               "roofline": roof,
               "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": m * GEMM_K * 2,
-                      "d2h_bytes_per_step": GEMM_MATS * m * n_rank * 2},
+                      "d2h_bytes_per_step": GEMM_MATS * m * n_rank * 2,
+                      "path": "firepit_b200.nvfp4_gemm(...).submit(Graph sink): H2D x, quantize + GEMMs, D2H y in "
+                              "one CUDA graph"},
               "gpu_launches": launches_per_step * args.steps, "clocks": clocks.summary(),
               "breakdown_ms": {"quantize_act": quant_ms / args.steps, "gemms": gemm_ms / args.steps}})
     del gq, gg
@@ -695,13 +716,19 @@ def fp8_arm(args):
     xh = x.cpu().pin_memory()
     yh = torch.empty(FP8_MATS, FP8_M, n_rank, dtype=torch.bfloat16, pin_memory=True)
     xd = torch.empty_like(x)
-    sink = F.Async()
-
-    def e2e_step():
+    # the reference's Graph sink: H2D x, the GEMMs and D2H y in one CUDA graph
+    for c in range(FP8_MATS):
+        F.fp8_gemm(mats[c], x, ys[c], workspace=ws).submit(F.Async())
+    torch.cuda.synchronize()
+    gsink = F.Graph()
+    with gsink:
         xd.copy_(xh, non_blocking=True)
         for c in range(FP8_MATS):
-            F.fp8_gemm(mats[c], xd, ys[c], workspace=ws).submit(sink)
+            F.fp8_gemm(mats[c], xd, ys[c], workspace=ws).submit(gsink)
         yh.copy_(ys, non_blocking=True)
+
+    def e2e_step():
+        gsink.replay()
 
     e2e_steps = max(1, min(args.steps, 20))
     for _ in range(2):
@@ -737,7 +764,9 @@ def fp8_arm(args):
                            "parallelism": f"N-split x{g} + NCCL all-gather" if g > 1 else "single GPU"},
                 "roofline": roof,
                 "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": FP8_M * FP8_K * 2,
-                        "d2h_bytes_per_step": FP8_MATS * FP8_M * n_rank * 2},
+                        "d2h_bytes_per_step": FP8_MATS * FP8_M * n_rank * 2,
+                        "path": "firepit_b200.fp8_gemm(...).submit(Graph sink): H2D x, quantize + GEMMs, D2H y in "
+                                "one CUDA graph"},
                 "gpu_launches": launches_per_step * args.steps, "clocks": clocks.summary(),
                 "breakdown_ms": {"quantize_act": quant_ms / args.steps, "gemms": gemm_ms / args.steps}}
         if g == 1 and args.cpu_seconds > 0:
@@ -967,22 +996,26 @@ def moe_arm(args):
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
     hbm = float(peaks.get("hbm_gbs", 6650.0))
     achieved = nbytes / (ms * 1e-3) / 1e9
-    # end to end: x from pinned host, out back to pinned host, the same launches
+    # end to end: x from pinned host, out back to pinned host, the same C-ABI
+    # calls; copies and layer in one CUDA graph (the engine's graph sink)
     xh = x.cpu().pin_memory()
     oh = torch.empty(T, MOE_H, dtype=torch.bfloat16, pin_memory=True)
     xd = torch.empty_like(x)
+    e2e_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(e2e_graph, stream=s):
+        xd.copy_(xh, non_blocking=True)
+        moe(torch.cuda.current_stream().cuda_stream, xd)
+        oh.copy_(b["out"], non_blocking=True)
     e2e_steps = max(1, min(args.steps, 20))
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(s):
-        for i in range(e2e_steps + 2):
-            if i == 2:
-                e0.record()
-            xd.copy_(xh, non_blocking=True)
-            moe(s.cuda_stream, xd)
-            oh.copy_(b["out"], non_blocking=True)
-        e1.record()
+    for i in range(e2e_steps + 2):
+        if i == 2:
+            e0.record()
+        e2e_graph.replay()
+    e1.record()
     torch.cuda.synchronize()
     e2e = flops / (e0.elapsed_time(e1) / e2e_steps * 1e-3) / 1e12
+    del e2e_graph
     line = {"metric": "NVFP4 MoE layer TFLOPS", "value": value, "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None,
@@ -995,6 +1028,7 @@ def moe_arm(args):
                          "traffic": None, "algorithmic_bytes": nbytes, "peak_kind": "measured hbm_gbs",
                          "note": "whole MoE layer time; the grouped GEMMs are the dominant kernels"},
             "e2e": {"value": e2e, "unit": "TFLOP/s", "h2d_bytes_per_step": T * MOE_H * 2,
+                    "path": "C-ABI calls of the layer with H2D x and D2H out in one CUDA graph",
                     "d2h_bytes_per_step": T * MOE_H * 2},
             "gpu_launches": launches_per_step * args.steps, "clocks": clocks.summary(), "breakdown_ms": breakdown}
     if args.cpu_seconds > 0:

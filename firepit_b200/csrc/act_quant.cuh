@@ -68,12 +68,14 @@ __global__ void act_amax_kernel(const T *x, size_t n, uint32_t *amax_bits) {
   if ((threadIdx.x & 31) == 0) atomicMax(amax_bits, m);
 }
 
-// One 16-value group: s = RN_e4m3((bmax / 6) / global), codes =
-// RN_e2m1(v / (e4m3(s) * global)); writes 8 code bytes and the factor.
 // SwiGLU of one element in the reference's order (swiglu.rs:16):
-// gate / (1 + exp(gate * -1)) * up.
+// gate / (1 + exp(gate * -1)) * up, IEEE division and CUDA's expf (the
+// unfused SwiGLU kernels; the fused GEMM epilogue uses exp2 / reciprocal
+// approximations).
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + expf(g * -1.0f)) * u; }
 
+// One 16-value group: s = RN_e4m3((bmax / 6) / global), codes =
+// RN_e2m1(v / (e4m3(s) * global)); writes 8 code bytes and the factor.
 __device__ __forceinline__ void encode_group16(const float v[16], float global, uint8_t *packed_dst,
                                                uint8_t *sf_dst) {
   float bmax = 0.0f;
@@ -85,8 +87,7 @@ __device__ __forceinline__ void encode_group16(const float v[16], float global, 
   uint32_t lo = 0, hi = 0;
   if (denom > 0.0f) {
     float q[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) q[i] = __fdiv_rn(v[i], denom);
+    e2m1_quotients16(v, denom, q);
     lo = f32x8_to_e2m1x8(q);
     hi = f32x8_to_e2m1x8(q + 8);
   }

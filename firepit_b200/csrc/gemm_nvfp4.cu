@@ -13,10 +13,11 @@
 //               (tcgen05.cp) and issues four
 //               tcgen05.mma.kind::mxf4nvf4.block_scale.block16 (K = 64 each)
 //               accumulating in TMEM; tcgen05.commit frees the stage;
-//   warps 2-5   epilogue: tcgen05.ld of the f32 accumulator, times ga * g[n],
-//               staged as bf16 or f32 in shared memory (128-byte swizzle,
-//               32 rows per warp) and written by TMA tiled stores, so each
-//               row segment leaves as whole 128-byte lines.
+//   warps 2-9   epilogue, two per TMEM lane quadrant (64 columns each):
+//               tcgen05.ld of the f32 accumulator, times ga * g[n], staged
+//               as bf16 or f32 in shared memory (128-byte swizzle) and
+//               written by TMA tiled stores, so each row segment leaves as
+//               whole 128-byte lines.
 // Every TMA load lands in the issuing CTA alone.
 //
 // Scale factors live in the tensor cores' tiled layout: for each 128-row
@@ -158,7 +159,9 @@ constexpr uint32_t kTmemSfa = 256, kTmemSfb = 320;
 // Epilogue staging: per epilogue warp 32 rows x 128 columns (f32: four 32-column
 // boxes; bf16: two 64-column boxes), each box 32 rows x 128 bytes.
 constexpr int kOutBoxBytes = 32 * 128;
-constexpr int kOutWarpBytes = 4 * kOutBoxBytes;
+constexpr int kOutWarpBytes = 4 * kOutBoxBytes;  // per TMEM lane quadrant
+constexpr int kEpiWarps = 8;                      // two per quadrant
+constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
 constexpr size_t kGemmSmem = 1024 + kStages * (2 * kTileBytes + 2 * kSfStageBytes) + 4 * kOutWarpBytes + 256;
 
 __device__ __forceinline__ void report(int *error, volatile int *abort, int code) {
@@ -190,7 +193,7 @@ __device__ __forceinline__ bool gemm_tile(const GemmParams &p, int t, int n_tile
 // The producer and the MMA issuer share one ring counter across tiles; the
 // accumulator alternates between two TMEM buffers, so the epilogue of one
 // tile overlaps the main loop of the next.
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kGemmThreads, 1)
     nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                       const __grid_constant__ CUtensorMap tmap_y, const __grid_constant__ CUtensorMap tmap_b64,
                       GemmParams p) {
@@ -221,7 +224,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);
+      mbar_init(&acc_empty[b], kEpiWarps);
     }
     *abort_s = 0;
     fence_barrier_init();
@@ -322,11 +325,15 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else {
-    // ---- epilogue: warps 2..5 cover TMEM lanes (warp % 4) * 32 .. +31 ---------
-    const int qw = warp & 3;
+    // ---- epilogue: warps 2..9, two per TMEM lane quadrant (warp % 4) ---------
+    // Warp (quadrant qw, half ch) owns rows qw*32 .. +31 of the tile and
+    // accumulator columns ch*64 .. +63 (glu: gate and up columns of h
+    // columns ch*32 .. +31); each warp stages and stores its own boxes.
+    const int qw = warp & 3, ch = (warp - 2) >> 2;
     const uint32_t lane_base = (uint32_t)(qw * 32) << 16;
     const float ga = __ldg(p.a_global);
-    uint8_t *stage = sOut + qw * kOutWarpBytes;  // this warp's 32 rows
+    uint8_t *stage = sOut + qw * kOutWarpBytes;
+    uint8_t *row_s = stage + lane * 128;
     uint32_t lt = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       int m_tile, n_tile, n_base;
@@ -338,85 +345,19 @@ __global__ void __launch_bounds__(192, 1)
       }
       __syncwarp();  // the TMEM loads below are warp-collective
       tc_fence_after();
+      // Drain this warp's 64 accumulator columns (glu: 32 gate + the 32 up
+      // columns of the same h columns), then free the buffer.
+      uint32_t r[2][32];
+      const uint32_t tacc = tmem + lane_base + buf * kBN;
       if (p.glu) {
-        // TMEM columns 0..63: gate of h columns j0..j0+63; 64..127: up.  A
-        // rolled loop over 8-column groups keeps the code small (the SwiGLU
-        // is long); the buffer is released after the loop.
-        const int row0 = m_tile * kBM + qw * 32;
-        const bool row_live = row0 + lane < p.M && (!p.row_tokens || p.row_tokens[row0 + lane] >= 0);
-        const bool any_live = __any_sync(0xffffffffu, row_live);
-        const int inter = p.N / 2, j0 = n_tile * 64;
-        uint32_t mx = 0;
-        if (any_live) {
-          float g_gate[2], g_up[2];
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            g_gate[c] = __ldg(p.b_globals + n_base + j0 + c * 32 + lane);
-            g_up[c] = __ldg(p.b_globals + n_base + inter + j0 + c * 32 + lane);
-          }
-          if (lane == 0) bulk_wait_read_all();
-          __syncwarp();
-          uint8_t *row_s = stage + lane * 128;
-          const uint32_t tacc = tmem + lane_base + buf * kBN;
-#pragma unroll 1
-          for (int q = 0; q < 8; ++q) {
-            uint32_t gr[8], ur[8];
-            tmem_ld8x2_wait(tacc + q * 8, tacc + 64 + q * 8, gr, ur);
-            const float gg = q < 4 ? g_gate[0] : g_gate[1], gu = q < 4 ? g_up[0] : g_up[1];
-            float v[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const int src = (q & 3) * 8 + j;
-              const float gate = (__uint_as_float(gr[j]) * ga) * __shfl_sync(0xffffffffu, gg, src);
-              const float up = (__uint_as_float(ur[j]) * ga) * __shfl_sync(0xffffffffu, gu, src);
-              v[j] = silu_mul(gate, up);
-            }
-            if (p.y_bf16) {
-              uint4 pk;
-              pk.x = pack_bf16x2(v[0], v[1]);
-              pk.y = pack_bf16x2(v[2], v[3]);
-              pk.z = pack_bf16x2(v[4], v[5]);
-              pk.w = pack_bf16x2(v[6], v[7]);
-              const uint32_t w4[4] = {pk.x, pk.y, pk.z, pk.w};
-#pragma unroll
-              for (int i = 0; i < 4; ++i) mx = max(mx, max((w4[i] << 16) & 0x7fffffffu, w4[i] & 0x7fff0000u));
-              *reinterpret_cast<uint4 *>(row_s + ((q ^ (lane & 7)) * 16)) = pk;
-            } else {
-#pragma unroll
-              for (int j = 0; j < 8; ++j) mx = max(mx, __float_as_uint(v[j]) & 0x7fffffffu);
-              uint8_t *box = row_s + (q >> 2) * kOutBoxBytes;
-              const int c0 = (q & 3) * 2;
-              *reinterpret_cast<float4 *>(box + ((c0 ^ (lane & 7)) * 16)) = make_float4(v[0], v[1], v[2], v[3]);
-              *reinterpret_cast<float4 *>(box + (((c0 + 1) ^ (lane & 7)) * 16)) =
-                  make_float4(v[4], v[5], v[6], v[7]);
-            }
-          }
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[buf]);
-        ++lt;
-        if (!any_live) continue;
-        if (!row_live) mx = 0;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        if (lane == 0) atomicMax(p.amax_bits, mx);
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_2d(&tmap_y, stage, j0, row0);
-          if (!p.y_bf16) tma_store_2d(&tmap_y, stage + kOutBoxBytes, j0 + 32, row0);
-          bulk_commit_group();
-        }
-        continue;
+        tmem_ld32(tacc + ch * 32, r[0]);
+        tmem_ld32(tacc + 64 + ch * 32, r[1]);
+      } else {
+        tmem_ld32(tacc + ch * 64, r[0]);
+        tmem_ld32(tacc + ch * 64 + 32, r[1]);
       }
-      // Drain the whole accumulator row into registers, free the buffer, then
-      // scale and store while the tensor cores fill the other buffer.
-      uint32_t r[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(tmem + lane_base + buf * kBN + c * 32, r[c]);
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld_wait(r[c]);
+      tmem_ld_wait(r[0]);
+      tmem_ld_wait(r[1]);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
@@ -425,65 +366,119 @@ __global__ void __launch_bounds__(192, 1)
       const int n0 = n_tile * kBN;
       if (row0 >= p.M) continue;  // the warp's rows are all past the end
       const bool row_live = row0 + lane < p.M && (!p.row_tokens || p.row_tokens[row0 + lane] >= 0);
-      if (!__any_sync(0xffffffffu, row_live)) continue;  // nothing of these 32 rows is needed
-      // Lane l holds the weight global of column n0 + 32c + l.
-      float gl[4];
+      if (!__any_sync(0xffffffffu, row_live)) continue;  // nothing of these 32 rows is needed (both warps agree)
+      if (p.glu) {
+        // h columns j0 + ch*32 + i: silu(gate) * up, gate / up scaled by ga
+        // and their weight rows' globals.  exp2 and reciprocal approximations
+        // (no branches, so the 32 evaluations interleave): relative error
+        // about 1e-6 against the exact formula, far below the NVFP4 encode
+        // that follows.
+        const int inter = p.N / 2, j0 = n_tile * 64;
+        const float g_gate = __ldg(p.b_globals + n_base + j0 + ch * 32 + lane);
+        const float g_up = __ldg(p.b_globals + n_base + inter + j0 + ch * 32 + lane);
+        float v[32];
+        uint32_t mx = 0;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const int n = n0 + c * 32 + lane;
-        gl[c] = n < p.N ? __ldg(p.b_globals + n_base + n) : 0.0f;
-      }
-      if (p.tma_store) {
-        if (lane == 0) bulk_wait_read_all();  // the previous tile's stores have left the stage
+        for (int j = 0; j < 32; ++j) {
+          const float gate = (__uint_as_float(r[0][j]) * ga) * __shfl_sync(0xffffffffu, g_gate, j);
+          const float up = (__uint_as_float(r[1][j]) * ga) * __shfl_sync(0xffffffffu, g_up, j);
+          v[j] = __fdividef(gate, 1.0f + __expf(-gate)) * up;
+        }
+        if (lane == 0) bulk_wait_read_all();  // this warp's previous store has left its box
         __syncwarp();
-        uint8_t *row_s = stage + lane * 128;
+        if (p.y_bf16) {
+          // the warp's own box: 32 rows x 64 bytes, unswizzled (tmap_y's box
+          // is 32 x 32 bf16 in this mode)
+          uint8_t *row64 = stage + ch * kOutBoxBytes + lane * 64;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          float v[32];
+          for (int q = 0; q < 4; ++q) {
+            uint4 pk;
+            pk.x = pack_bf16x2(v[8 * q], v[8 * q + 1]);
+            pk.y = pack_bf16x2(v[8 * q + 2], v[8 * q + 3]);
+            pk.z = pack_bf16x2(v[8 * q + 4], v[8 * q + 5]);
+            pk.w = pack_bf16x2(v[8 * q + 6], v[8 * q + 7]);
+            const uint32_t w4[4] = {pk.x, pk.y, pk.z, pk.w};
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = (__uint_as_float(r[c][j]) * ga) * __shfl_sync(0xffffffffu, gl[c], j);
-          if (p.y_bf16) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              uint4 pk;
-              pk.x = pack_bf16x2(v[8 * q], v[8 * q + 1]);
-              pk.y = pack_bf16x2(v[8 * q + 2], v[8 * q + 3]);
-              pk.z = pack_bf16x2(v[8 * q + 4], v[8 * q + 5]);
-              pk.w = pack_bf16x2(v[8 * q + 6], v[8 * q + 7]);
-              const int chunk = ((c & 1) * 4 + q) ^ (lane & 7);
-              *reinterpret_cast<uint4 *>(row_s + (c >> 1) * kOutBoxBytes + chunk * 16) = pk;
-            }
-          } else {
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              const int chunk = q ^ (lane & 7);
-              *reinterpret_cast<float4 *>(row_s + c * kOutBoxBytes + chunk * 16) =
-                  make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-            }
+            for (int i = 0; i < 4; ++i) mx = max(mx, max((w4[i] << 16) & 0x7fffffffu, w4[i] & 0x7fff0000u));
+            *reinterpret_cast<uint4 *>(row64 + q * 16) = pk;
           }
+        } else {
+          // f32: the warp's 32 columns are one 128-byte-swizzled box
+#pragma unroll
+          for (int j = 0; j < 32; ++j) mx = max(mx, __float_as_uint(v[j]) & 0x7fffffffu);
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            *reinterpret_cast<float4 *>(row_s + ch * kOutBoxBytes + ((q ^ (lane & 7)) * 16)) =
+                make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
         }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          const int boxes = p.y_bf16 ? 2 : 4, box_cols = p.y_bf16 ? 64 : 32;
-          for (int b = 0; b < boxes; ++b)
-            if (n0 + b * box_cols < p.N) tma_store_2d(&tmap_y, stage + b * kOutBoxBytes, n0 + b * box_cols, row0);
+          tma_store_2d(&tmap_y, stage + ch * kOutBoxBytes, j0 + ch * 32, row0);
+          bulk_commit_group();
+        }
+        if (!row_live) mx = 0;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (lane == 0) atomicMax(p.amax_bits, mx);
+        continue;
+      }
+      // Lane l holds the weight global of column n0 + ch*64 + 32c + l; the
+      // products are scaled in place by every lane (shuffles are warp-wide).
+      const int nw = n0 + ch * 64;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int n = nw + c * 32 + lane;
+        const float gl = n < p.N ? __ldg(p.b_globals + n_base + n) : 0.0f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          r[c][j] = __float_as_uint((__uint_as_float(r[c][j]) * ga) * __shfl_sync(0xffffffffu, gl, j));
+      }
+      if (p.tma_store) {
+        if (lane == 0) bulk_wait_read_all();  // this warp's previous stores have left its boxes
+        __syncwarp();
+        if (p.y_bf16) {
+          // box ch: this warp's 64 columns
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint4 pk;
+              pk.x = pack_bf16x2(__uint_as_float(r[c][8 * q]), __uint_as_float(r[c][8 * q + 1]));
+              pk.y = pack_bf16x2(__uint_as_float(r[c][8 * q + 2]), __uint_as_float(r[c][8 * q + 3]));
+              pk.z = pack_bf16x2(__uint_as_float(r[c][8 * q + 4]), __uint_as_float(r[c][8 * q + 5]));
+              pk.w = pack_bf16x2(__uint_as_float(r[c][8 * q + 6]), __uint_as_float(r[c][8 * q + 7]));
+              *reinterpret_cast<uint4 *>(row_s + ch * kOutBoxBytes + (((c * 4 + q) ^ (lane & 7)) * 16)) = pk;
+            }
+        } else {
+          // boxes 2ch and 2ch + 1: 32 columns each
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              *reinterpret_cast<uint4 *>(row_s + (2 * ch + c) * kOutBoxBytes + ((q ^ (lane & 7)) * 16)) =
+                  make_uint4(r[c][4 * q], r[c][4 * q + 1], r[c][4 * q + 2], r[c][4 * q + 3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (p.y_bf16) {
+            if (nw < p.N) tma_store_2d(&tmap_y, stage + ch * kOutBoxBytes, nw, row0);
+          } else {
+            for (int c = 0; c < 2; ++c)
+              if (nw + c * 32 < p.N)
+                tma_store_2d(&tmap_y, stage + (2 * ch + c) * kOutBoxBytes, nw + c * 32, row0);
+          }
           bulk_commit_group();
         }
         continue;
       }
-      // Direct stores (y not addressable by a tensor map).  Every lane takes
-      // part in the shuffles; only the stores depend on the lane's row.
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-#pragma unroll
-        for (int j = 0; j < 32; ++j)
-          r[c][j] = __float_as_uint((__uint_as_float(r[c][j]) * ga) * __shfl_sync(0xffffffffu, gl[c], j));
+      // Direct stores (y not addressable by a tensor map).
       const int row = row0 + lane;
       if (!row_live) continue;  // no warp-collective operation follows in this iteration
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const int nc = n0 + c * 32;
+      for (int c = 0; c < 2; ++c) {
+        const int nc = nw + c * 32;
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[c][j]);
@@ -576,18 +571,21 @@ int encode_rows_u8(CUtensorMap *map, const void *base, uint64_t rows, uint64_t r
 }
 
 bool encode_store_map(CUtensorMap *map, void *y, bool bf16, uint64_t rows, uint64_t cols, uint64_t ld,
-                      uint32_t box_rows) {
+                      uint32_t box_rows, uint32_t box_cols) {
   EncodeTiledFn fn = encode_fn();
   const uint64_t esize = bf16 ? 2 : 4;
   if (!fn || (reinterpret_cast<uintptr_t>(y) & 15) || ((ld * esize) & 15) || ld < cols || rows == 0 || cols == 0)
     return false;
+  if (box_cols == 0) box_cols = (uint32_t)(128 / esize);
+  // 128-byte boxes are stored from 128-byte-swizzled staging; narrower boxes unswizzled
+  const bool swz = box_cols * esize == 128;
   cuuint64_t dims[2] = {cols, rows};
   cuuint64_t strides[1] = {ld * esize};
-  cuuint32_t box[2] = {(cuuint32_t)(128 / esize), box_rows};
+  cuuint32_t box[2] = {box_cols, box_rows};
   cuuint32_t estr[2] = {1, 1};
   return fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, y, dims, strides, box,
-            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 static unsigned grid_for(size_t n) {
@@ -730,10 +728,10 @@ extern "C" int fpb_nvfp4_gemm_q(fpb_nvfp4_matrix *w, size_t row_begin, size_t ro
   p.kb_count = (int)((w->cols + 255) / 256);
   p.error = err;
   CUtensorMap tmap_y{};
-  p.tma_store = encode_store_map(&tmap_y, y, p.y_bf16, m, p.N, p.ldy, 32);
+  p.tma_store = encode_store_map(&tmap_y, y, p.y_bf16, m, p.N, p.ldy, 32, 0);
   const size_t tiles = (size_t)((p.N + kBN - 1) / kBN) * ((m + kBM - 1) / kBM);
   const unsigned grid = (unsigned)std::min<size_t>(tiles, (size_t)std::max(1, sm_count()));
-  nvfp4_gemm_kernel<<<grid, 192, kGemmSmem, s>>>(tmap_a, *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b),
+  nvfp4_gemm_kernel<<<grid, kGemmThreads, kGemmSmem, s>>>(tmap_a, *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b),
                                                  tmap_y, *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b), p);
   FPB_LAUNCH_CHECK("nvfp4_gemm_kernel");
   return FPB_OK;
@@ -807,10 +805,10 @@ extern "C" int fpb_nvfp4_grouped_gemm_q(fpb_nvfp4_matrix *w, const uint8_t *a_pa
   p.row_tokens = token_rows;
   p.n_experts = (int)(w->rows / rows_per_expert);
   CUtensorMap tmap_y{};
-  p.tma_store = encode_store_map(&tmap_y, y, p.y_bf16, padded_rows, p.N, p.ldy, 32);
+  p.tma_store = encode_store_map(&tmap_y, y, p.y_bf16, padded_rows, p.N, p.ldy, 32, 0);
   const size_t tiles = (rows_per_expert / kBN) * (padded_rows / kBM);
   const unsigned grid = (unsigned)std::min<size_t>(tiles, (size_t)std::max(1, sm_count()));
-  nvfp4_gemm_kernel<<<grid, 192, kGemmSmem, s>>>(tmap_a, *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b),
+  nvfp4_gemm_kernel<<<grid, kGemmThreads, kGemmSmem, s>>>(tmap_a, *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b),
                                                  tmap_y, *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b), p);
   FPB_LAUNCH_CHECK("nvfp4_gemm_kernel(grouped)");
   return FPB_OK;
@@ -858,7 +856,9 @@ extern "C" int fpb_nvfp4_grouped_gemm_swiglu_q(fpb_nvfp4_matrix *w, const uint8_
   if (st) return st;
   CUtensorMap tmap_a, tmap_y{};
   if ((st = encode_rows_u8(&tmap_a, a_packed, padded_rows, w->cols / 2, kBM))) return st;
-  if (!encode_store_map(&tmap_y, h, h_dtype == FPB_BF16, padded_rows, inter, inter, 32))
+  // h boxes: 32 rows x 32 columns per epilogue warp (bf16 unswizzled, f32
+  // with 128-byte swizzle)
+  if (!encode_store_map(&tmap_y, h, h_dtype == FPB_BF16, padded_rows, inter, inter, 32, 32))
     return fail(FPB_ERR_CUDA, "fpb_nvfp4_grouped_gemm_swiglu_q: cannot encode the output map");
   {
     static std::mutex mu;
@@ -894,7 +894,7 @@ extern "C" int fpb_nvfp4_grouped_gemm_swiglu_q(fpb_nvfp4_matrix *w, const uint8_
   p.amax_bits = amax_bits;
   const size_t tiles = (2 * inter / kBN) * (padded_rows / kBM);
   const unsigned grid = (unsigned)std::min<size_t>(tiles, (size_t)std::max(1, sm_count()));
-  nvfp4_gemm_kernel<<<grid, 192, kGemmSmem, s>>>(tmap_a, *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b),
+  nvfp4_gemm_kernel<<<grid, kGemmThreads, kGemmSmem, s>>>(tmap_a, *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b),
                                                  tmap_y, *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b64),
                                                  p);
   FPB_LAUNCH_CHECK("nvfp4_gemm_kernel(grouped swiglu)");

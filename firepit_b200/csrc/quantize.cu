@@ -78,8 +78,7 @@ __global__ void nvfp4_encode_kernel(const T *w, size_t rows, size_t cols, size_t
     uint32_t lo = 0, hi = 0;
     if (denom > 0.0f) {
       float q[kNvfp4Group];
-#pragma unroll
-      for (int i = 0; i < kNvfp4Group; ++i) q[i] = __fdiv_rn(v[i], denom);
+      e2m1_quotients16(v, denom, q);
       lo = f32x8_to_e2m1x8(q);
       hi = f32x8_to_e2m1x8(q + 8);
     }

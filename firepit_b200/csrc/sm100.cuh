@@ -203,6 +203,25 @@ __device__ __forceinline__ void tmem_ld8x2_wait(uint32_t taddr_a, uint32_t taddr
       : "memory");
 }
 
+// The two loads of tmem_ld8x2_wait without the wait; tmem_wait_ld8x2 waits
+// with the 16 destination registers tied to the wait.
+__device__ __forceinline__ void tmem_ld8x2(uint32_t taddr_a, uint32_t taddr_b, uint32_t (&a)[8], uint32_t (&b)[8]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%16];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%8,%9,%10,%11,%12,%13,%14,%15}, [%17];"
+      : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3]), "=r"(a[4]), "=r"(a[5]), "=r"(a[6]), "=r"(a[7]),
+        "=r"(b[0]), "=r"(b[1]), "=r"(b[2]), "=r"(b[3]), "=r"(b[4]), "=r"(b[5]), "=r"(b[6]), "=r"(b[7])
+      : "r"(taddr_a), "r"(taddr_b)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld8x2(uint32_t (&a)[8], uint32_t (&b)[8]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(a[4]), "+r"(a[5]), "+r"(a[6]), "+r"(a[7]),
+                 "+r"(b[0]), "+r"(b[1]), "+r"(b[2]), "+r"(b[3]), "+r"(b[4]), "+r"(b[5]), "+r"(b[6]), "+r"(b[7])
+               :
+               : "memory");
+}
+
 // ---- descriptors -----------------------------------------------------------------------
 // Shared-memory matrix descriptor (tcgen05 format, version 1).
 //   layout 2 = 128-byte swizzle (K-major tiles of 128-byte rows, 8-row atoms

@@ -14,7 +14,8 @@ tokens.  One layer:
    them to size the variable splits), then rows and tags (all-to-all);
 4. the receiver runs its local experts on the rows it got (the single-GPU MoE
    path: layout by local expert, gather + NVFP4 quantize, grouped gate/up
-   GEMM, SwiGLU + quantize, grouped down GEMM, un-permute);
+   GEMM with SwiGLU in its epilogue, h quantize, grouped down GEMM,
+   un-permute);
 5. results go back the reverse way (all-to-all) and the source rank combines
    them with its routing weights (``fpb_moe_combine`` over the dispatch
    layout's ``inverse``).
@@ -98,7 +99,12 @@ class DeviceOps:
 
     def expert_mlp(self, x, local_e, w1, w2, per_rank, amax_reduce):
         """The local experts on received rows x [n, H] (bf16): rows in, rows
-        out, in the same order.  amax_reduce(tensor int32 [1]) -> reduced."""
+        out, in the same order.  amax_reduce(tensor int32 [1]) -> reduced.
+
+        Layout by local expert (128-row tiles), gather + NVFP4 quantize,
+        gate/up GEMM with SwiGLU in its epilogue (h bf16 and its amax), h
+        quantize, down GEMM, un-permute; the layout's padding rows are skipped
+        by every stage."""
         t = self.torch
         from .moe import PrefillLayout, MoeDims
         n, h = x.shape
@@ -110,31 +116,33 @@ class DeviceOps:
             cap = (PrefillLayout.max_padded_rows(n, dims, 128) + 127) // 128 * 128
         ids = local_e.view(-1, 1) if n else t.zeros(1, 1, dtype=t.int32, device=self.device)
         lay = self.layout(ids, 1, per_rank, 128, cap) if n else None
+        skip = N.FPB_QUANT_SKIP_PADDING
         # collectives are taken by every rank in the same order, even with no rows
         a_x = amax_reduce(self.amax(x))
         scal = t.zeros(4, dtype=t.float32, device=self.device)
         scal[1:2].view(t.int32).copy_(a_x)
         a1 = self.empty((cap, h // 2), t.uint8)
         sf1 = self.empty((int(N.lib.fpb_nvfp4_act_sf_bytes(cap, h)),), t.uint8)
-        y1 = self.empty((cap, 2 * inter), t.bfloat16)
+        hbuf = self.empty((cap, inter), t.bfloat16)
+        a_h = t.zeros(1, dtype=t.int32, device=self.device)
         if n:
             N.call("fpb_moe_gather_quantize", x.data_ptr(), _dt(x), n, h, lay["tr"].data_ptr(), cap,
                    lay["pad"].data_ptr(), a1.data_ptr(), sf1.data_ptr(), scal.data_ptr(), scal[1:].data_ptr(),
-                   N.FPB_QUANT_AMAX_GIVEN, self._s())
-            N.call("fpb_nvfp4_grouped_gemm_q", w1.handle, a1.data_ptr(), sf1.data_ptr(), scal.data_ptr(), cap,
-                   lay["te"].data_ptr(), None, 2 * inter, y1.data_ptr(), N.FPB_BF16, self._s())
-        pad = lay["pad"] if n else t.zeros(1, dtype=t.int32, device=self.device)
-        a_act = amax_reduce(self.swiglu_amax(y1, pad) if n else t.zeros(1, dtype=t.int32, device=self.device))
+                   N.FPB_QUANT_AMAX_GIVEN | skip, self._s())
+            N.call("fpb_nvfp4_grouped_gemm_swiglu_q", w1.handle, a1.data_ptr(), sf1.data_ptr(), scal.data_ptr(), cap,
+                   lay["te"].data_ptr(), lay["tr"].data_ptr(), inter, hbuf.data_ptr(), N.FPB_BF16, a_h.data_ptr(),
+                   self._s())
+        a_act = amax_reduce(a_h)
         if n:
             scal[3:4].view(t.int32).copy_(a_act)
             a2 = self.empty((cap, inter // 2), t.uint8)
             sf2 = self.empty((int(N.lib.fpb_nvfp4_act_sf_bytes(cap, inter)),), t.uint8)
-            N.call("fpb_swiglu_quantize", y1.data_ptr(), N.FPB_BF16, cap, lay["pad"].data_ptr(), inter,
-                   a2.data_ptr(), sf2.data_ptr(), scal[2:].data_ptr(), scal[3:].data_ptr(), N.FPB_QUANT_AMAX_GIVEN,
-                   self._s())
+            N.call("fpb_rows_quantize", hbuf.data_ptr(), N.FPB_BF16, cap, lay["pad"].data_ptr(), lay["tr"].data_ptr(),
+                   inter, a2.data_ptr(), sf2.data_ptr(), scal[2:].data_ptr(), scal[3:].data_ptr(),
+                   N.FPB_QUANT_AMAX_GIVEN | skip, self._s())
             y2 = self.empty((cap, h), t.bfloat16)
             N.call("fpb_nvfp4_grouped_gemm_q", w2.handle, a2.data_ptr(), sf2.data_ptr(), scal[2:].data_ptr(), cap,
-                   lay["te"].data_ptr(), None, h, y2.data_ptr(), N.FPB_BF16, self._s())
+                   lay["te"].data_ptr(), lay["tr"].data_ptr(), h, y2.data_ptr(), N.FPB_BF16, self._s())
             ones = t.ones(n, 1, dtype=t.float32, device=self.device)
             N.call("fpb_moe_combine", y2.data_ptr(), N.FPB_BF16, cap, h, lay["inv"].data_ptr(), ones.data_ptr(), n, 1,
                    1, y.data_ptr(), _dt(y), self._s())

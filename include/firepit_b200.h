@@ -320,7 +320,8 @@ int fpb_swiglu_quantize(const void *gate_up, int dtype, size_t rows, const int32
  * swiglu.rs:16 on its f32 output): w holds experts of 2*inter rows each
  * (gate rows, then up rows); h [padded_rows, inter] (f32/bf16, 16-byte
  * aligned) = silu(gate) * up computed from the f32 accumulators (no rounding
- * of gate/up, as the reference's f32 swiglu input); *amax_bits = max |h| as
+ * of gate/up, as the reference's f32 swiglu input; exp and the division by
+ * hardware approximations, relative error about 1e-6); *amax_bits = max |h| as
  * stored (float bits; zeroed first).  inter % 64 == 0.  The first call on a
  * matrix builds its interleaved factor copy and synchronises `stream`.
  * token_rows as in fpb_nvfp4_grouped_gemm_q; padding rows are also left out

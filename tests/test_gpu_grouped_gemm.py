@@ -139,9 +139,10 @@ def test_grouped_gemm_swiglu_vs_oracle(F, torch, tokens, experts, top_k, inter, 
         g, u = at @ wg.T, at @ wu.T
         eg, eu = 1e-5 * (np.abs(at) @ np.abs(wg).T), 1e-5 * (np.abs(at) @ np.abs(wu).T)
         exp[t * 128:(t + 1) * 128] = _silu_mul(g, u)
-        # |d silu/dg| <= 1.1; f32 exp and the two roundings of the formula: 1e-6 relative
+        # |d silu/dg| <= 1.1
         tol[t * 128:(t + 1) * 128] = 1.1 * eg * (np.abs(u) + eu) + (np.abs(g) + eg) * eu
-    tol += 1e-6 * np.abs(exp) + 1e-30
+    # the epilogue's exp2 / reciprocal approximations and roundings: 4e-6 relative
+    tol += 4e-6 * np.abs(exp) + 1e-30
     if out == "bf16":
         tol += 2.0 ** -8 * np.abs(exp)
     assert np.all(np.abs(got - exp) <= tol)

@@ -78,6 +78,49 @@ def test_quantize_edge_values(F, torch):
     assert np.array_equal(packed.cpu().numpy().reshape(-1), p_ref)
 
 
+def _boundary_blocks(rows: int, cols: int, seed: int) -> np.ndarray:
+    """Blocks whose quotients v / d land exactly on every e2m1 rounding
+    boundary (ties), and one representable value either side of it.  With
+    global = 2^-6 (amax 42 = 2688 * 2^-6) and a block maximum of 6 * d for an
+    e4m3 value S = d / global, the block's factor is S and d = S * 2^-6 is
+    exact, so m * d is exact for every boundary m."""
+    rng = np.random.default_rng(seed)
+    s_vals = np.array([0.5, 0.75, 1.0, 1.125, 1.75, 3.0, 6.5, 13.0, 0.015625, 0.0234375, 240.0], np.float32)
+    marks = np.array([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, 6.0, 0.5, 1.0, 3.0], np.float32)
+    w = np.zeros((rows, cols), np.float32)
+    for r in range(rows):
+        for b in range(cols // 16):
+            d = np.float32(rng.choice(s_vals)) * np.float32(2.0 ** -6)
+            blk = np.empty(16, np.float32)
+            blk[0] = np.float32(6.0) * d
+            for i in range(1, 16):
+                v = np.float32(rng.choice(marks)) * d
+                step = rng.integers(-1, 2)  # below, on, above the boundary
+                if step:
+                    v = np.nextafter(v, np.float32(np.inf) if step > 0 else np.float32(0))
+                blk[i] = -v if rng.random() < 0.3 else v
+            w[r, b * 16:(b + 1) * 16] = blk
+    w[0, 0] = np.float32(42.0)  # amax: global = 2^-6 exactly (its block: S = 448)
+    return w
+
+
+def test_quantize_rounding_boundaries(F, torch):
+    """Weights and activations whose quotients sit on or next to the e2m1
+    rounding boundaries: the device's shortcut (one reciprocal per group,
+    correctly rounded division only near a boundary) must give the oracle's
+    codes bit for bit."""
+    w = _boundary_blocks(64, 256, seed=3)
+    packed, scales, g = F.quantize_nvfp4(torch.from_numpy(w).cuda())
+    p_ref, s_ref, g_ref = O.nvfp4_quantize(w)
+    assert g_ref[0] == np.float32(2.0 ** -6)
+    assert np.array_equal(g.cpu().numpy().view(np.uint32), g_ref.view(np.uint32))
+    assert np.array_equal(scales.cpu().numpy().reshape(-1), s_ref)
+    assert np.array_equal(packed.cpu().numpy().reshape(-1), p_ref)
+    a_packed, a_sf, a_g = F.quantize_act(torch.from_numpy(w).cuda())
+    assert a_g.item() == g_ref[0]
+    assert np.array_equal(a_packed.cpu().numpy().reshape(-1), p_ref)
+
+
 def test_dequantize_bit_exact_and_roundtrip(F, torch):
     packed, scales, g, rows, cols = R.kernels_case(1, 29)[:5]
     m = host_matrix(F, packed, scales, g, rows, cols).upload()

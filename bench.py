@@ -655,16 +655,19 @@ def fp8_arm(args):
     qs = torch.empty(FP8_M, dtype=torch.float32, device=dev)
     ys = torch.empty(FP8_MATS, FP8_M, n_rank, dtype=torch.bfloat16, device=dev)
     y_all = torch.empty(g, FP8_MATS, FP8_M, n_rank, dtype=torch.bfloat16, device=dev)
-    ws_bytes = int(N_.lib.fpb_fp8_gemm_workspace_bytes(FP8_M, FP8_K))
+    ws_bytes = int(N_.lib.fpb_fp8_gemm_workspace_bytes(FP8_M, FP8_K)) + int(
+        N_.lib.fpb_fp8_gemm_split_bytes(FP8_M, FP8_K, n_rank))
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    split = torch.empty(int(N_.lib.fpb_fp8_gemm_split_bytes(FP8_M, FP8_K, n_rank)), dtype=torch.uint8, device=dev)
 
     def quant(sh):
         N_.call("fpb_fp8_quantize", x.data_ptr(), N_.FPB_BF16, FP8_M, FP8_K, 0, 0, qa.data_ptr(), qs.data_ptr(), sh)
 
     def gemms(sh):
+        # stream-K schedule (one CTA per SM over all tiles' K blocks)
         for c in range(FP8_MATS):
-            N_.call("fpb_fp8_gemm_q", mats[c].handle, 0, 0, qa.data_ptr(), qs.data_ptr(), FP8_M, ys[c].data_ptr(),
-                    N_.FPB_BF16, sh)
+            N_.call("fpb_fp8_gemm_q_split", mats[c].handle, 0, 0, qa.data_ptr(), qs.data_ptr(), FP8_M,
+                    ys[c].data_ptr(), N_.FPB_BF16, split.data_ptr(), split.numel(), sh)
 
     s = torch.cuda.Stream(device=dev)
     with torch.cuda.stream(s):
@@ -863,7 +866,8 @@ def moe_reference_arm(args):
 def moe_arm(args):
     """Config 3 at T = 4096 (prefill) or 64 (decode batch), one GPU: bf16 x
     [T, 2048], bf16 router [512, 2048] (cuBLAS, f32 logits), device top-10,
-    device layout (128-row tiles), gather + NVFP4 quantize, grouped gate/up
+    device layout (128-row tiles), NVFP4 quantize of each token once + copy
+    of its codes to the rows that route it, grouped gate/up
     GEMM [512 x 1024, 2048] with SwiGLU in its epilogue (h in bf16 and its
     amax), NVFP4 quantize of h, grouped down GEMM [512 x 2048, 512], weighted
     combine; one CUDA graph per step.  The layout's padding rows (each
@@ -924,7 +928,9 @@ def moe_arm(args):
                out=torch.empty(T, MOE_H, dtype=torch.bfloat16, device=dev),
                scal=torch.zeros(4, dtype=torch.float32, device=dev),
                lscr=torch.empty(int(N_.lib.fpb_moe_layout_scratch_bytes(T, MOE_K, MOE_E)), dtype=torch.uint8,
-                                device=dev))
+                                device=dev),
+               gws=torch.empty(int(N_.lib.fpb_moe_gather_quantize_workspace_bytes(T, MOE_H)), dtype=torch.uint8,
+                               device=dev))
     b = buf
     BF = N_.FPB_BF16
 
@@ -943,7 +949,8 @@ def moe_arm(args):
         # padding rows of the layout (token -1) are skipped by every stage below
         skip = N_.FPB_QUANT_SKIP_PADDING
         N_.call("fpb_moe_gather_quantize", xin.data_ptr(), BF, T, MOE_H, b["tr"].data_ptr(), cap, b["pad"].data_ptr(),
-                b["a1"].data_ptr(), b["sf1"].data_ptr(), b["scal"].data_ptr(), b["scal"][1:].data_ptr(), skip, sh)
+                b["a1"].data_ptr(), b["sf1"].data_ptr(), b["scal"].data_ptr(), b["scal"][1:].data_ptr(), skip,
+                b["gws"].data_ptr(), b["gws"].numel(), sh)
         mark(2)
         N_.call("fpb_nvfp4_grouped_gemm_swiglu_q", W1.handle, b["a1"].data_ptr(), b["sf1"].data_ptr(),
                 b["scal"].data_ptr(), cap, b["te"].data_ptr(), b["tr"].data_ptr(), MOE_I, b["h"].data_ptr(), BF,

@@ -99,13 +99,16 @@ SIGNATURES: dict[str, tuple] = {
     "fpb_fp8_quantize": (i32, [vp, i32, sz, sz, sz, sz, vp, vp, vp]),
     "fpb_fp8_gemm_workspace_bytes": (sz, [sz, sz]),
     "fpb_fp8_gemm_q": (i32, [vp, sz, sz, vp, vp, sz, vp, i32, vp]),
+    "fpb_fp8_gemm_q_split": (i32, [vp, sz, sz, vp, vp, sz, vp, i32, vp, sz, vp]),
+    "fpb_fp8_gemm_split_bytes": (sz, [sz, sz, sz]),
     "fpb_fp8_gemm": (i32, [vp, sz, sz, vp, i32, sz, vp, i32, vp, sz, vp]),
     "fpb_fp8_grouped_gemm_q": (i32, [vp, vp, vp, sz, vp, sz, vp, i32, vp]),
     "fpb_moe_topk": (i32, [vp, sz, vp, sz, sz, sz, sz, vp, vp, vp]),
     "fpb_moe_layout": (i32, [vp, sz, sz, sz, sz, sz, sz, vp, vp, vp, vp, vp, vp, sz, vp]),
     "fpb_moe_layout_scratch_bytes": (sz, [sz, sz, sz]),
     "fpb_moe_gather": (i32, [vp, i32, sz, sz, vp, sz, vp, i32, vp]),
-    "fpb_moe_gather_quantize": (i32, [vp, i32, sz, sz, vp, sz, vp, vp, vp, vp, vp, i32, vp]),
+    "fpb_moe_gather_quantize": (i32, [vp, i32, sz, sz, vp, sz, vp, vp, vp, vp, vp, i32, vp, sz, vp]),
+    "fpb_moe_gather_quantize_workspace_bytes": (sz, [sz, sz]),
     "fpb_swiglu": (i32, [vp, i32, sz, sz, vp, i32, vp]),
     "fpb_swiglu_quantize": (i32, [vp, i32, sz, vp, sz, vp, vp, vp, vp, i32, vp]),
     "fpb_nvfp4_grouped_gemm_swiglu_q": (i32, [vp, vp, vp, vp, sz, vp, vp, sz, vp, i32, vp, vp]),

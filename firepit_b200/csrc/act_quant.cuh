@@ -29,6 +29,16 @@ __host__ __device__ inline size_t sf_tiled_offset(size_t row, size_t group, size
   return (rb * kb64_per_rb + kb64) * kSfChunk + (r % 32) * 16 + (r / 32) * 4 + s;
 }
 
+// sf_tiled_offset split into its row part (64-bit, once per row) and its
+// group part (32-bit): offset = row part + group part.
+__host__ __device__ inline size_t sf_tiled_row_offset(size_t row, size_t cols) {
+  const size_t r = row % 128;
+  return (row / 128) * ((cols + 255) / 256 * 4) * kSfChunk + (r % 32) * 16 + (r / 32) * 4;
+}
+__host__ __device__ inline uint32_t sf_tiled_group_offset(uint32_t group) {
+  return (group / 4) * kSfChunk + group % 4;
+}
+
 template <typename T>
 __device__ __forceinline__ float act_load(const T *p, size_t i);
 template <>
@@ -87,7 +97,8 @@ __device__ __forceinline__ void encode_group16(const float v[16], float global, 
   uint32_t lo = 0, hi = 0;
   if (denom > 0.0f) {
     float q[16];
-    e2m1_quotients16(v, denom, q);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) q[i] = __fdiv_rn(v[i], denom);
     lo = f32x8_to_e2m1x8(q);
     hi = f32x8_to_e2m1x8(q + 8);
   }

@@ -101,34 +101,6 @@ __device__ __forceinline__ uint32_t f32x8_to_e2m1x8(const float v[8]) {
 }
 
 // f32 -> e4m3 byte, RNE satfinite.
-// The quotients v[i] / d (d > 0) as they enter RN_e2m1: equal to the
-// correctly rounded RN(v[i] / d) wherever that can change the e2m1 code, with
-// one reciprocal instead of sixteen divisions.  a = RN(v * RN(1/d)) differs
-// from v / d by at most 2^-23 relative (two roundings of 2^-24), so from
-// RN(v / d) by at most three units in the last place.  e2m1's rounding
-// boundaries (0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5) and its top value 6 have
-// at most three significant bits: their f32 mantissa field is a multiple of
-// 2^21.  A quotient more than eight representable values away from every
-// such value is on the same side of every boundary as RN(v / d) and rounds to
-// the same code; one nearer is recomputed with the correctly rounded
-// division, as are all quotients when 1/d is not a normal number.  Quotients
-// below 2^-100 round to (signed) zero either way.
-__device__ __forceinline__ void e2m1_quotients16(const float v[16], float d, float q[16]) {
-  const uint32_t de = __float_as_uint(d) >> 23;
-  if (de < 2 || de > 251) {  // d outside [2^-125, 2^125)
-#pragma unroll
-    for (int i = 0; i < 16; ++i) q[i] = __fdiv_rn(v[i], d);
-    return;
-  }
-  const float r = __frcp_rn(d);
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const float a = __fmul_rn(v[i], r);
-    const uint32_t b = __float_as_uint(a) & 0x7fffffffu;
-    q[i] = (b >= 0x0d800000u && ((b + 8u) & 0x1fffffu) <= 16u) ? __fdiv_rn(v[i], d) : a;
-  }
-}
-
 __device__ __forceinline__ uint8_t f32_to_e4m3(float v) {
   uint16_t out;
   asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(out) : "f"(0.0f), "f"(v));

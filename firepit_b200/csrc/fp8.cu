@@ -128,12 +128,58 @@ struct Fp8GemmParams {
   int *error;
   const int32_t *tile_experts;  // grouped mode (gemm/mod.rs:103-140), else null
   int n_experts;
+  // Schedule.  Tile t = n_tile * m_tiles + m_tile (neighbouring CTAs share a
+  // weight tile).  CTA c runs the K blocks [c*T/G, (c+1)*T/G) of the
+  // concatenation of all tiles' K blocks (T = tiles * kb_count, G = grid):
+  // whole tiles, or a tile's K range split between consecutive CTAs
+  // (stream-K).  A CTA with part of a tile writes its f32 partial sums to
+  // `partials` [tiles][max_seg][128][256]; the last of the tile's parts to
+  // finish (per epilogue warp, a counter per tile and warp) adds them in part
+  // order and stores the tile.  No CTA waits for another.
+  int m_tiles, tiles;
+  long long total_kb;
+  int ctas, max_seg;
+  float *partials;      // null: every CTA runs whole tiles (G = tiles)
+  int *tile_counters;   // [tiles][kF8EpiWarps], zero at launch, left zero
 };
 
 __device__ __forceinline__ void f8_report(int *error, volatile int *abort, int code) {
   *abort = 1;
   if (error) atomicCAS(error, 0, code);
 }
+
+// The CTA whose K-block range holds global K block x.
+__host__ __device__ __forceinline__ long long f8_cta_of(long long x, long long total, long long ctas) {
+  return ((x + 1) * ctas - 1) / total;
+}
+
+// One tile's part in a CTA's range: K blocks [kb0, kb1) of tile `tile`,
+// part `seg` of `nseg`.
+struct F8Seg {
+  int tile, kb0, kb1, seg, nseg;
+};
+
+// Iterates the CTA's parts.
+struct F8Sched {
+  long long gk, end;
+  __device__ __forceinline__ F8Sched(const Fp8GemmParams &p) {
+    gk = (long long)blockIdx.x * p.total_kb / p.ctas;
+    end = ((long long)blockIdx.x + 1) * p.total_kb / p.ctas;
+  }
+  __device__ __forceinline__ bool next(const Fp8GemmParams &p, F8Seg &g) {
+    if (gk >= end) return false;
+    g.tile = (int)(gk / p.kb_count);
+    g.kb0 = (int)(gk - (long long)g.tile * p.kb_count);
+    g.kb1 = (int)min((long long)p.kb_count, g.kb0 + (end - gk));
+    const long long t0 = (long long)g.tile * p.kb_count;
+    const long long first = f8_cta_of(t0, p.total_kb, p.ctas);
+    const long long last = f8_cta_of(t0 + p.kb_count - 1, p.total_kb, p.ctas);
+    g.seg = (int)(blockIdx.x - first);
+    g.nseg = (int)(last - first + 1);
+    gk += g.kb1 - g.kb0;
+    return true;
+  }
+};
 
 template <bool kBlocks>
 __global__ void __launch_bounds__(kF8Threads, 1)
@@ -152,17 +198,27 @@ __global__ void __launch_bounds__(kF8Threads, 1)
   volatile int *abort_s = reinterpret_cast<volatile int *>(tmem_base_s + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_tile = blockIdx.x, m_tile = blockIdx.y;
-  const int m0 = m_tile * kF8Tile, n0 = n_tile * kF8BN;
-  int n_base = p.n_base;
-  if (p.tile_experts) {
-    const int e = p.tile_experts[m_tile];
-    if (e == -1) return;  // a row tile past the end of a device-built layout
-    if (e < 0 || e >= p.n_experts) {
-      if (threadIdx.x == 0 && p.error) atomicCAS(p.error, 0, 306);
-      return;
+  // Weight row base of a tile (grouped: its expert's rows); false for a row
+  // tile past the end of a device-built layout (expert -1) or a bad id.
+  auto tile_rows = [&](int tile, int &m0, int &n0, int &n_base) -> bool {
+    const int m_tile = tile % p.m_tiles, n_tile = tile / p.m_tiles;
+    m0 = m_tile * kF8Tile;
+    n0 = n_tile * kF8BN;
+    n_base = p.n_base;
+    if (p.tile_experts) {
+      const int e = p.tile_experts[m_tile];
+      if (e == -1) return false;
+      if (e < 0 || e >= p.n_experts) {
+        if (threadIdx.x == 0 && p.error) atomicCAS(p.error, 0, 306);
+        return false;
+      }
+      n_base = e * p.N;
     }
-    n_base = e * p.N;
+    return true;
+  };
+  if (p.tile_experts) {  // grouped: one whole tile per CTA; a dead tile's CTA leaves at once
+    int m0, n0, nb;
+    if (!tile_rows((int)blockIdx.x, m0, n0, nb)) return;
   }
 
   if (threadIdx.x == 0) {
@@ -191,53 +247,75 @@ __global__ void __launch_bounds__(kF8Threads, 1)
   if (warp < 4) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kF8CtrlRegs));
   if (warp == 0) {
-    // ---- TMA producer ----------------------------------------------------------
+    // ---- TMA producer: the CTA's K blocks, one ring across parts ----------------
     if (elect_one()) {
-      int issued = 0;
-      for (int kb = 0; kb < p.kb_count; ++kb) {
-        const int s = kb % kF8Stages, round = kb / kF8Stages;
-        if (kb >= kF8Stages && !mbar_wait(&empty[s], (round - 1) & 1, abort_s)) {
-          f8_report(p.error, abort_s, 301);
-          break;
+      uint32_t g = 0;
+      bool ok = true;
+      F8Sched sched(p);
+      F8Seg sg;
+      while (ok && sched.next(p, sg)) {
+        int m0, n0, n_base;
+        tile_rows(sg.tile, m0, n0, n_base);
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++g) {
+          const uint32_t s = g % kF8Stages;
+          if (g >= kF8Stages && !mbar_wait(&empty[s], ((g / kF8Stages) - 1) & 1, abort_s)) {
+            f8_report(p.error, abort_s, 301);
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], kF8ABytes + kF8BBytes);
+          tma_load_2d(sA + s * kF8ABytes, &tmap_a, kb * kF8Tile, m0, &full[s]);
+          tma_load_2d(sB + s * kF8BBytes, &tmap_b, kb * kF8Tile, n_base + n0, &full[s]);
         }
-        mbar_arrive_expect_tx(&full[s], kF8ABytes + kF8BBytes);
-        tma_load_2d(sA + s * kF8ABytes, &tmap_a, kb * kF8Tile, m0, &full[s]);
-        tma_load_2d(sB + s * kF8BBytes, &tmap_b, kb * kF8Tile, n_base + n0, &full[s]);
-        issued = kb + 1;
       }
-      for (int kb = (issued > kF8Stages ? issued - kF8Stages : 0); kb < issued; ++kb)
-        if (!mbar_wait(&full[kb % kF8Stages], (kb / kF8Stages) & 1, abort_s)) f8_report(p.error, abort_s, 302);
+      // Our own copies must have landed before the CTA may exit.
+      for (uint32_t j = (g > kF8Stages ? g - kF8Stages : 0); j < g; ++j)
+        if (!mbar_wait(&full[j % kF8Stages], (j / kF8Stages) & 1, abort_s)) f8_report(p.error, abort_s, 302);
     }
   } else if (warp == 1) {
     // ---- MMA issuer -------------------------------------------------------------
+    // Blocks: each K block into TMEM buffer (g & 1); rows: each part into
+    // buffer (part & 1), accumulated over its K blocks.
     if (elect_one()) {
       const uint32_t idesc = idesc_f8(kF8Tile, kF8BN);
+      uint32_t g = 0, part = 0;
       bool ok = true;
-      for (int kb = 0; kb < p.kb_count && ok; ++kb) {
-        const int s = kb % kF8Stages, round = kb / kF8Stages;
-        if (!mbar_wait(&full[s], round & 1, abort_s)) {
-          f8_report(p.error, abort_s, 303);
-          ok = false;
-          break;
-        }
-        const int b = kBlocks ? (kb & 1) : 0;
-        if (kBlocks && kb >= 2 && !mbar_wait(&acc_empty[b], ((kb >> 1) - 1) & 1, abort_s)) {
+      F8Sched sched(p);
+      F8Seg sg;
+      while (ok && sched.next(p, sg)) {
+        const uint32_t pb = part & 1;
+        if (!kBlocks && part >= 2 && !mbar_wait(&acc_empty[pb], ((part >> 1) - 1) & 1, abort_s)) {
           f8_report(p.error, abort_s, 304);
-          ok = false;
           break;
         }
-        tc_fence_after();
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++g) {
+          const uint32_t s = g % kF8Stages;
+          if (!mbar_wait(&full[s], (g / kF8Stages) & 1, abort_s)) {
+            f8_report(p.error, abort_s, 303);
+            ok = false;
+            break;
+          }
+          const uint32_t b = kBlocks ? (g & 1) : pb;
+          if (kBlocks && g >= 2 && !mbar_wait(&acc_empty[b], ((g >> 1) - 1) & 1, abort_s)) {
+            f8_report(p.error, abort_s, 304);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          const uint64_t a_desc = smem_desc(smem_u32(sA + s * kF8ABytes) + kk * 32, 16, 1024, 2);
-          const uint64_t b_desc = smem_desc(smem_u32(sB + s * kF8BBytes) + kk * 32, 16, 1024, 2);
-          const uint32_t acc = kBlocks ? (kk != 0) : ((kb | kk) != 0);
-          mma_f8(tmem + b * kF8BN, a_desc, b_desc, idesc, acc);
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t a_desc = smem_desc(smem_u32(sA + s * kF8ABytes) + kk * 32, 16, 1024, 2);
+            const uint64_t b_desc = smem_desc(smem_u32(sB + s * kF8BBytes) + kk * 32, 16, 1024, 2);
+            const uint32_t acc = kBlocks ? (kk != 0) : (kb != sg.kb0 || kk != 0);
+            mma_f8(tmem + b * kF8BN, a_desc, b_desc, idesc, acc);
+          }
+          tc_commit(&empty[s]);
+          if (kBlocks) tc_commit(&acc_full[b]);
         }
-        tc_commit(&empty[s]);
-        if (kBlocks) tc_commit(&acc_full[b]);
+        if (!ok) break;
+        if (!kBlocks) tc_commit(&acc_full[pb]);
+        ++part;
       }
-      if (!kBlocks && ok) tc_commit(&acc_full[0]);
     }
   }
   } else {
@@ -245,77 +323,119 @@ __global__ void __launch_bounds__(kF8Threads, 1)
     // ---- epilogue: quadrant (warp % 4), column part (warp - 4) / 4 -------------
     constexpr int kParts = kF8EpiWarps / 4;
     constexpr int kCols = kF8BN / kParts;  // columns per epilogue warp
+    static_assert(kCols == 128, "four 32-column chunks per epilogue warp");
     const int qd = warp & 3, half = (warp - 4) >> 2;
-    const int row = m0 + qd * 32 + lane;
     const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
     const int c_base = half * kCols;
-    float acc[kCols];
-#pragma unroll
-    for (int j = 0; j < kCols; ++j) acc[j] = 0.0f;
+    uint32_t g = 0, part = 0;
     bool ok = true;
-    // The token scale is folded into each block scale before it meets the
-    // partial sums, so that extreme but finite scale pairs (one tiny, one
-    // huge) do not overflow or underflow in between.
-    const float as = row < p.M ? __ldg(p.a_scale + row) : 0.0f;
-    if (kBlocks) {
-      // A part's columns lie in one block of bn (a multiple of 128) rows.
-      const int nb = (n_base + n0 + c_base) / p.bn;
-      const float *ws_row = p.w_scale + (size_t)nb * p.ws_cols;
-      for (int kb = 0; kb < p.kb_count; ++kb) {
-        const int b = kb & 1;
-        if (!mbar_wait(&acc_full[b], (kb >> 1) & 1, abort_s)) {
+    F8Sched sched(p);
+    F8Seg sg;
+    while (ok && sched.next(p, sg)) {
+      int m0, n0, n_base;
+      tile_rows(sg.tile, m0, n0, n_base);
+      const int row = m0 + qd * 32 + lane;
+      float acc[kCols];
+#pragma unroll
+      for (int j = 0; j < kCols; ++j) acc[j] = 0.0f;
+      // The token scale is folded into each block scale before it meets the
+      // partial sums, so that extreme but finite scale pairs (one tiny, one
+      // huge) do not overflow or underflow in between.
+      const float as = row < p.M ? __ldg(p.a_scale + row) : 0.0f;
+      if (kBlocks) {
+        // A part's columns lie in one block of bn (a multiple of 128) rows.
+        const int nb = (n_base + n0 + c_base) / p.bn;
+        const float *ws_row = p.w_scale + (size_t)nb * p.ws_cols;
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++g) {
+          const uint32_t b = g & 1;
+          if (!mbar_wait(&acc_full[b], (g >> 1) & 1, abort_s)) {
+            f8_report(p.error, abort_s, 305);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const float ws = __ldg(ws_row + (kb * kF8Tile) / p.bk) * as;
+          const uint32_t taddr = tmem + lane_base + b * kF8BN + c_base;
+          // Each chunk's TMEM load overlaps the previous chunk's scale-and-add.
+          uint32_t ra[32], rb[32];
+          tmem_ld32(taddr, ra);
+          tmem_ld_wait(ra);
+          tmem_ld32(taddr + 32, rb);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[j] = fmaf(__uint_as_float(ra[j]), ws, acc[j]);
+          tmem_ld_wait(rb);
+          tmem_ld32(taddr + 64, ra);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[32 + j] = fmaf(__uint_as_float(rb[j]), ws, acc[32 + j]);
+          tmem_ld_wait(ra);
+          tmem_ld32(taddr + 96, rb);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[64 + j] = fmaf(__uint_as_float(ra[j]), ws, acc[64 + j]);
+          tmem_ld_wait(rb);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[96 + j] = fmaf(__uint_as_float(rb[j]), ws, acc[96 + j]);
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[b]);
+        }
+        if (!ok) break;
+      } else {
+        const uint32_t pb = part & 1;
+        if (!mbar_wait(&acc_full[pb], (part >> 1) & 1, abort_s)) {
           f8_report(p.error, abort_s, 305);
-          ok = false;
           break;
         }
-        tc_fence_after();
-        const float ws = __ldg(ws_row + (kb * kF8Tile) / p.bk) * as;
-        const uint32_t taddr = tmem + lane_base + b * kF8BN + c_base;
-        // Each chunk's TMEM load overlaps the previous chunk's scale-and-add.
-        static_assert(kCols == 128, "four 32-column chunks per epilogue warp");
-        uint32_t ra[32], rb[32];
-        tmem_ld32(taddr, ra);
-        tmem_ld_wait(ra);
-        tmem_ld32(taddr + 32, rb);
-#pragma unroll
-        for (int j = 0; j < 32; ++j) acc[j] = fmaf(__uint_as_float(ra[j]), ws, acc[j]);
-        tmem_ld_wait(rb);
-        tmem_ld32(taddr + 64, ra);
-#pragma unroll
-        for (int j = 0; j < 32; ++j) acc[32 + j] = fmaf(__uint_as_float(rb[j]), ws, acc[32 + j]);
-        tmem_ld_wait(ra);
-        tmem_ld32(taddr + 96, rb);
-#pragma unroll
-        for (int j = 0; j < 32; ++j) acc[64 + j] = fmaf(__uint_as_float(ra[j]), ws, acc[64 + j]);
-        tmem_ld_wait(rb);
-#pragma unroll
-        for (int j = 0; j < 32; ++j) acc[96 + j] = fmaf(__uint_as_float(rb[j]), ws, acc[96 + j]);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[b]);
-      }
-    } else {
-      if (mbar_wait(&acc_full[0], 0, abort_s)) {
         tc_fence_after();
 #pragma unroll
         for (int c = 0; c < kCols / 32; ++c) {
           uint32_t r[32];
-          tmem_ld32(tmem + lane_base + c_base + c * 32, r);
+          tmem_ld32(tmem + lane_base + pb * kF8BN + c_base + c * 32, r);
           tmem_ld_wait(r);
 #pragma unroll
           for (int j = 0; j < 32; ++j) acc[c * 32 + j] = __uint_as_float(r[j]);
         }
-      } else {
-        f8_report(p.error, abort_s, 305);
-        ok = false;
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[pb]);
+        ++part;
       }
-    }
-    if (ok && row < p.M) {
       const int nc = n0 + c_base;
-      // Final scale in place (rows mode: token x weight-row scale).
+      if (sg.nseg > 1) {
+        // Part of a split tile: publish this warp's 32 x 128 partial sums; the
+        // warp that completes the tile's count adds all parts in order.
+        const size_t slot_row = ((size_t)sg.tile * p.max_seg + sg.seg) * kF8Tile + qd * 32 + lane;
+        float4 *mine = reinterpret_cast<float4 *>(p.partials + slot_row * kF8BN + c_base);
 #pragma unroll
-      for (int j = 0; j < kCols; ++j) {
-        if (!kBlocks) {
+        for (int j = 0; j < kCols / 4; ++j) mine[j] = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
+        __threadfence();
+        __syncwarp();
+        int done = 0;
+        int *counter = p.tile_counters + (size_t)sg.tile * kF8EpiWarps + (warp - 4);
+        if (lane == 0) done = atomicAdd(counter, 1);
+        done = __shfl_sync(0xffffffffu, done, 0);
+        if (done != sg.nseg - 1) continue;  // another part finishes this tile
+        __threadfence();
+#pragma unroll
+        for (int j = 0; j < kCols; ++j) acc[j] = 0.0f;
+        for (int q = 0; q < sg.nseg; ++q) {
+          const size_t r_q = ((size_t)sg.tile * p.max_seg + q) * kF8Tile + qd * 32 + lane;
+          const float4 *src = reinterpret_cast<const float4 *>(p.partials + r_q * kF8BN + c_base);
+#pragma unroll
+          for (int j = 0; j < kCols / 4; ++j) {
+            const float4 v = __ldcg(src + j);
+            acc[4 * j] += v.x;
+            acc[4 * j + 1] += v.y;
+            acc[4 * j + 2] += v.z;
+            acc[4 * j + 3] += v.w;
+          }
+        }
+        if (lane == 0) *counter = 0;  // ready for the next launch
+      }
+      if (row >= p.M) continue;
+      // Final scale in place (rows mode: token x weight-row scale).
+      if (!kBlocks) {
+#pragma unroll
+        for (int j = 0; j < kCols; ++j) {
           const float ws = (nc + j < p.N) ? __ldg(p.w_scale + n_base + nc + j) : 0.0f;
           acc[j] = acc[j] * (as * ws);
         }
@@ -454,9 +574,27 @@ static int fp8_prepare(fpb_fp8_matrix *w) {
   return FPB_OK;
 }
 
+// Stream-K schedule of a dense GEMM: grid, parts per tile at most, bytes of
+// partial sums and counters.
+struct F8Split {
+  int ctas, max_seg;
+  size_t partial_bytes, counter_bytes;
+};
+static F8Split fp8_split_plan(size_t m, size_t n_rows, size_t k) {
+  const size_t tiles = ((m + kF8Tile - 1) / kF8Tile) * ((n_rows + kF8BN - 1) / kF8BN);
+  const size_t kb = (k + kF8Tile - 1) / kF8Tile, total = tiles * kb;
+  F8Split sp{};
+  sp.ctas = (int)std::max<size_t>(1, std::min<size_t>((size_t)std::max(1, sm_count()), total));
+  const size_t range = std::max<size_t>(1, total / sp.ctas);  // shortest CTA range
+  sp.max_seg = (int)std::min<size_t>((kb + range - 1) / range + 1, kb);
+  sp.partial_bytes = tiles * (size_t)sp.max_seg * kF8Tile * kF8BN * sizeof(float);
+  sp.counter_bytes = tiles * kF8EpiWarps * sizeof(int);
+  return sp;
+}
+
 static int fp8_gemm_launch(fpb_fp8_matrix *w, const uint8_t *a_bits, const float *a_scale, size_t m,
                            size_t n_base, size_t n_rows, const int32_t *tile_experts, void *y, int y_dtype,
-                           cudaStream_t s) {
+                           cudaStream_t s, void *split_ws = nullptr, size_t split_bytes = 0) {
   if (y_dtype != FPB_F32 && y_dtype != FPB_BF16) return fail(FPB_ERR_INVALID_ARGUMENT, "FP8 GEMM: dtype");
   const bool blocks = !(w->block_n == 0 && w->block_k == 0);
   if (blocks && (w->block_n % kF8Tile != 0 || w->block_k % kF8Tile != 0))
@@ -487,8 +625,20 @@ static int fp8_gemm_launch(fpb_fp8_matrix *w, const uint8_t *a_bits, const float
   p.error = device_error_ptr();
   p.tile_experts = tile_experts;
   p.n_experts = tile_experts ? (int)(w->rows / n_rows) : 0;
-  dim3 grid((unsigned)((n_rows + kF8BN - 1) / kF8BN), (unsigned)((m + kF8Tile - 1) / kF8Tile));
-  kernel<<<grid, kF8Threads, kF8Smem, s>>>(tmap_a, *reinterpret_cast<const CUtensorMap *>(w->tmap), p);
+  p.m_tiles = (int)((m + kF8Tile - 1) / kF8Tile);
+  p.tiles = p.m_tiles * (int)((n_rows + kF8BN - 1) / kF8BN);
+  p.total_kb = (long long)p.tiles * p.kb_count;
+  p.ctas = p.tiles;  // whole tiles
+  p.max_seg = 1;
+  const F8Split sp = fp8_split_plan(m, n_rows, w->cols);
+  if (!tile_experts && split_ws && split_bytes >= sp.partial_bytes + sp.counter_bytes && sp.ctas < p.total_kb) {
+    p.ctas = sp.ctas;
+    p.max_seg = sp.max_seg;
+    p.partials = static_cast<float *>(split_ws);
+    p.tile_counters = reinterpret_cast<int *>(static_cast<uint8_t *>(split_ws) + sp.partial_bytes);
+    FPB_CUDA_TRY(cudaMemsetAsync(p.tile_counters, 0, sp.counter_bytes, s));
+  }
+  kernel<<<p.ctas, kF8Threads, kF8Smem, s>>>(tmap_a, *reinterpret_cast<const CUtensorMap *>(w->tmap), p);
   FPB_LAUNCH_CHECK("fp8_gemm_kernel");
   return FPB_OK;
 }
@@ -599,6 +749,11 @@ extern "C" int fpb_fp8_quantize(const void *w, int dtype, size_t rows, size_t co
 
 extern "C" size_t fpb_fp8_gemm_workspace_bytes(size_t m, size_t k) { return align256(m * k) + align256(4 * m); }
 
+extern "C" size_t fpb_fp8_gemm_split_bytes(size_t m, size_t k, size_t n) {
+  const F8Split sp = fp8_split_plan(m, n, k);
+  return align256(sp.partial_bytes + sp.counter_bytes);
+}
+
 extern "C" int fpb_fp8_gemm_q(fpb_fp8_matrix *w, size_t row_begin, size_t row_end, const uint8_t *a_bits,
                               const float *a_scales, size_t m, void *y, int y_dtype, void *stream) {
   if (!w || !a_bits || !a_scales || !y) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_fp8_gemm_q: null pointer");
@@ -614,6 +769,20 @@ extern "C" int fpb_fp8_gemm_q(fpb_fp8_matrix *w, size_t row_begin, size_t row_en
                          as_stream(stream));
 }
 
+extern "C" int fpb_fp8_gemm_q_split(fpb_fp8_matrix *w, size_t row_begin, size_t row_end, const uint8_t *a_bits,
+                                    const float *a_scales, size_t m, void *y, int y_dtype, void *split_ws,
+                                    size_t split_bytes, void *stream) {
+  if (!w || !a_bits || !a_scales || !y) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_fp8_gemm_q_split: null pointer");
+  if (row_end == 0) row_end = w->rows;
+  if (row_begin >= row_end || row_end > w->rows || row_begin % kF8Tile ||
+      (w->block_n && (row_begin % w->block_n || row_end % w->block_n)))
+    return fpb_fp8_gemm_q(w, row_begin, row_end, a_bits, a_scales, m, y, y_dtype, stream);  // its errors
+  if (split_ws && (reinterpret_cast<uintptr_t>(split_ws) & 255))
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_fp8_gemm_q_split: workspace must be 256-byte aligned");
+  return fp8_gemm_launch(w, a_bits, a_scales, m, row_begin, row_end - row_begin, nullptr, y, y_dtype,
+                         as_stream(stream), split_ws, split_bytes);
+}
+
 extern "C" int fpb_fp8_gemm(fpb_fp8_matrix *w, size_t row_begin, size_t row_end, const void *x, int x_dtype,
                             size_t m, void *y, int y_dtype, void *workspace, size_t workspace_bytes, void *stream) {
   if (!w || !x || !y || !workspace) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_fp8_gemm: null pointer");
@@ -625,7 +794,10 @@ extern "C" int fpb_fp8_gemm(fpb_fp8_matrix *w, size_t row_begin, size_t row_end,
   cudaStream_t s = as_stream(stream);
   int st = fp8_quantize_impl(x, x_dtype, m, w->cols, 0, 0, a_bits, a_scales, s);
   if (st) return st;
-  return fpb_fp8_gemm_q(w, row_begin, row_end, a_bits, a_scales, m, y, y_dtype, stream);
+  // Room past the activations (fpb_fp8_gemm_split_bytes): the stream-K partial sums.
+  const size_t base = fpb_fp8_gemm_workspace_bytes(m, w->cols);
+  return fpb_fp8_gemm_q_split(w, row_begin, row_end, a_bits, a_scales, m, y, y_dtype,
+                              static_cast<uint8_t *>(workspace) + base, workspace_bytes - base, stream);
 }
 
 extern "C" int fpb_fp8_grouped_gemm_q(fpb_fp8_matrix *w, const uint8_t *a_bits, const float *a_scales,

@@ -41,7 +41,7 @@ namespace fpb {
 __device__ int g_device_error;  // first failing kernel's error code (0 = none)
 
 constexpr int kBM = 128, kBN = 128, kBKBytes = 128;  // K block = 256 fp4 columns
-constexpr int kStages = 4;
+constexpr int kStages = 5;
 
 // Row-major e4m3 scales [rows, cols/16] -> tiled, sign cleared (UE4M3).
 // Padding entries are written as zero.  One thread per output byte.  With
@@ -102,13 +102,15 @@ __global__ void act_encode_kernel(const T *x, size_t rows, size_t cols, const ui
   const int gpr = (int)(cols / kNvfp4Group), lane = threadIdx.x & 31;
   const size_t warps = (size_t)gridDim.x * (blockDim.x / 32);
   for (size_t r = (size_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; r < rows; r += warps) {
+    const T *xrow = x + r * cols;
+    uint8_t *prow = packed + r * (cols / 2);
+    uint8_t *srow = sf_tiled + sf_tiled_row_offset(r, cols);
     for (int g = lane; g < gpr; g += 32) {
       float v[kNvfp4Group];
-      const T *src = x + r * cols + (size_t)g * kNvfp4Group;
+      const T *src = xrow + g * kNvfp4Group;
 #pragma unroll
       for (int i = 0; i < kNvfp4Group; ++i) v[i] = act_load(src, i);
-      encode_group16(v, global, packed + r * (cols / 2) + (size_t)g * (kNvfp4Group / 2),
-                     sf_tiled + sf_tiled_offset(r, g, cols));
+      encode_group16(v, global, prow + g * (kNvfp4Group / 2), srow + sf_tiled_group_offset(g));
     }
   }
 }
@@ -153,13 +155,14 @@ struct GemmParams {
 constexpr int kTileBytes = kBM * kBKBytes;   // 16 KB per operand per stage
 constexpr int kSfStageBytes = 4 * kSfChunk;  // 2 KB per operand per stage
 // TMEM: two 128-column accumulators (tiles alternate), then per stage 16
-// columns of A factors (256..319) and 16 of B factors (320..383).
+// columns of A factors (256..) and 16 of B factors (after the A ones).
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemSfa = 256, kTmemSfb = 320;
-// Epilogue staging: per epilogue warp 32 rows x 128 columns (f32: four 32-column
-// boxes; bf16: two 64-column boxes), each box 32 rows x 128 bytes.
+constexpr uint32_t kTmemSfa = 256, kTmemSfb = 256 + 16 * kStages;
+static_assert(kTmemSfb + 16 * kStages <= kTmemCols, "TMEM columns");
+// Epilogue staging: one 32-row x 128-byte box per epilogue warp (bf16: its
+// 64 columns; f32: 32 columns at a time), two per TMEM lane quadrant.
 constexpr int kOutBoxBytes = 32 * 128;
-constexpr int kOutWarpBytes = 4 * kOutBoxBytes;  // per TMEM lane quadrant
+constexpr int kOutWarpBytes = 2 * kOutBoxBytes;  // per TMEM lane quadrant
 constexpr int kEpiWarps = 8;                      // two per quadrant
 constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
 constexpr size_t kGemmSmem = 1024 + kStages * (2 * kTileBytes + 2 * kSfStageBytes) + 4 * kOutWarpBytes + 256;
@@ -435,7 +438,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           r[c][j] = __float_as_uint((__uint_as_float(r[c][j]) * ga) * __shfl_sync(0xffffffffu, gl, j));
       }
       if (p.tma_store) {
-        if (lane == 0) bulk_wait_read_all();  // this warp's previous stores have left its boxes
+        if (lane == 0) bulk_wait_read_all();  // this warp's previous stores have left its box
         __syncwarp();
         if (p.y_bf16) {
           // box ch: this warp's 64 columns
@@ -450,26 +453,31 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               pk.w = pack_bf16x2(__uint_as_float(r[c][8 * q + 6]), __uint_as_float(r[c][8 * q + 7]));
               *reinterpret_cast<uint4 *>(row_s + ch * kOutBoxBytes + (((c * 4 + q) ^ (lane & 7)) * 16)) = pk;
             }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if (nw < p.N) tma_store_2d(&tmap_y, stage + ch * kOutBoxBytes, nw, row0);
+            bulk_commit_group();
+          }
         } else {
-          // boxes 2ch and 2ch + 1: 32 columns each
+          // f32: the warp's box takes 32 columns at a time
 #pragma unroll
-          for (int c = 0; c < 2; ++c)
+          for (int c = 0; c < 2; ++c) {
+            if (c) {
+              if (lane == 0) bulk_wait_read_all();
+              __syncwarp();
+            }
 #pragma unroll
             for (int q = 0; q < 8; ++q)
-              *reinterpret_cast<uint4 *>(row_s + (2 * ch + c) * kOutBoxBytes + ((q ^ (lane & 7)) * 16)) =
+              *reinterpret_cast<uint4 *>(row_s + ch * kOutBoxBytes + ((q ^ (lane & 7)) * 16)) =
                   make_uint4(r[c][4 * q], r[c][4 * q + 1], r[c][4 * q + 2], r[c][4 * q + 3]);
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          if (p.y_bf16) {
-            if (nw < p.N) tma_store_2d(&tmap_y, stage + ch * kOutBoxBytes, nw, row0);
-          } else {
-            for (int c = 0; c < 2; ++c)
-              if (nw + c * 32 < p.N)
-                tma_store_2d(&tmap_y, stage + (2 * ch + c) * kOutBoxBytes, nw + c * 32, row0);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              if (nw + c * 32 < p.N) tma_store_2d(&tmap_y, stage + ch * kOutBoxBytes, nw + c * 32, row0);
+              bulk_commit_group();
+            }
           }
-          bulk_commit_group();
         }
         continue;
       }

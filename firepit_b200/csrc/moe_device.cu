@@ -105,7 +105,7 @@ __global__ void moe_topk_kernel(const float *logits, long long ld, const float *
 //     contiguous warp segments, __match_any_sync within a batch), so every
 //     expert's rows follow the (token, slot) order: the reference's stable sort.
 // The fills (token_rows = -1, tile_experts = -1, inverse = 0) are memsets.
-constexpr int kLayoutChunk = 4096;  // routes per CTA
+constexpr int kLayoutChunk = 1024;  // routes per CTA
 constexpr int kLayoutWarpsPerCta = 8;
 
 __device__ __forceinline__ int layout_id(const int32_t *ids, int e, int kk, int width, int experts) {
@@ -136,8 +136,18 @@ __global__ void __launch_bounds__(1024) moe_layout_scan_kernel(int *cnt, int gro
   extern __shared__ int totals[];  // [experts]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   for (int x = tid; x < experts; x += blockDim.x) {
-    int run = 0;
-    for (int g = 0; g < groups; ++g) {
+    int run = 0, g = 0;
+    for (; g + 8 <= groups; g += 8) {  // eight independent loads in flight
+      int c[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) c[u] = cnt[(size_t)(g + u) * experts + x];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        cnt[(size_t)(g + u) * experts + x] = run;
+        run += c[u];
+      }
+    }
+    for (; g < groups; ++g) {
       const int c = cnt[(size_t)g * experts + x];
       cnt[(size_t)g * experts + x] = run;
       run += c;
@@ -247,17 +257,25 @@ __device__ __forceinline__ void load16_vec(const uint16_t *p, float v[16]) {
 
 // Gathered rows (moe.rs:71-89): sorted row r is token token_rows[r], or zeros.
 template <typename T>
+// Row loaders: row(r) resolves row r once (64-bit address arithmetic), then
+// load16(row, g, v) reads its 16-column group g.
 struct GatherRows {
   const T *x;
   const int32_t *token_rows;
   size_t cols;
   int tokens;
-  __device__ __forceinline__ void load16(size_t r, size_t g, float v[16]) const {
+  using Row = const T *;  // null: a zero row
+  __device__ __forceinline__ Row row(size_t r) const {
     const int t = token_rows[r];
+    return (t < 0 || t >= tokens) ? nullptr : x + (size_t)t * cols;  // padding (or an id outside x)
+  }
+  __device__ __forceinline__ void load16(Row p, int g, float v[16]) const {
+    if (!p) {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = 0.0f;
-    if (t < 0 || t >= tokens) return;  // padding (or an id outside x)
-    load16_vec(x + (size_t)t * cols + g * 16, v);
+      for (int i = 0; i < 16; ++i) v[i] = 0.0f;
+      return;
+    }
+    load16_vec(p + g * 16, v);
   }
 };
 
@@ -266,7 +284,9 @@ template <typename T>
 struct PlainRows {
   const T *x;
   size_t cols;
-  __device__ __forceinline__ void load16(size_t r, size_t g, float v[16]) const { load16_vec(x + r * cols + g * 16, v); }
+  using Row = const T *;
+  __device__ __forceinline__ Row row(size_t r) const { return x + r * cols; }
+  __device__ __forceinline__ void load16(Row p, int g, float v[16]) const { load16_vec(p + g * 16, v); }
 };
 
 // SwiGLU rows (swiglu.rs:16): gate = first `cols` columns, up = next `cols`.
@@ -275,8 +295,10 @@ template <typename T>
 struct SwigluRows {
   const T *gu;
   size_t cols;  // intermediate size
-  __device__ __forceinline__ void load16(size_t r, size_t g, float v[16]) const {
-    const T *gate = gu + r * 2 * cols + g * 16;
+  using Row = const T *;
+  __device__ __forceinline__ Row row(size_t r) const { return gu + r * 2 * cols; }
+  __device__ __forceinline__ void load16(Row p, int g, float v[16]) const {
+    const T *gate = p + g * 16;
     float gv[16], uv[16];
     load16_vec(gate, gv);
     load16_vec(gate + cols, uv);
@@ -302,9 +324,10 @@ __global__ void rows_amax_kernel(Rows rows_src, size_t rows, const int32_t *vali
   uint32_t m = 0;
   for (size_t r = (size_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; r < n; r += warps) {
     if (skip && skip[r] < 0) continue;
+    const auto src = rows_src.row(r);
     for (int g = lane; g < gpr; g += 32) {
       float v[16];
-      rows_src.load16(r, g, v);
+      rows_src.load16(src, g, v);
 #pragma unroll
       for (int i = 0; i < 16; ++i) m = max(m, __float_as_uint(v[i]) & 0x7fffffffu);
     }
@@ -314,7 +337,8 @@ __global__ void rows_amax_kernel(Rows rows_src, size_t rows, const int32_t *vali
   if (lane == 0 && m) atomicMax(amax_bits, m);
 }
 
-template <class Rows>
+// kRowMajorSf: factors to sf[rows, cols/16] (row-major) instead of the tiled layout.
+template <class Rows, bool kRowMajorSf = false>
 __global__ void rows_encode_kernel(Rows rows_src, size_t rows, const int32_t *valid, const int32_t *skip, size_t cols,
                                    const uint32_t *amax_bits, uint8_t *packed, uint8_t *sf_tiled, float *global_out) {
   const float global = __fdiv_rn(__uint_as_float(*amax_bits), 2688.0f);
@@ -323,11 +347,40 @@ __global__ void rows_encode_kernel(Rows rows_src, size_t rows, const int32_t *va
   const size_t n = valid_rows(rows, valid), warps = (size_t)gridDim.x * (blockDim.x / 32);
   for (size_t r = (size_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; r < n; r += warps) {
     if (skip && skip[r] < 0) continue;
+    const auto src = rows_src.row(r);
+    uint8_t *prow = packed + r * (cols / 2);
+    uint8_t *srow = sf_tiled + (kRowMajorSf ? r * gpr : sf_tiled_row_offset(r, cols));
     for (int g = lane; g < gpr; g += 32) {
       float v[16];
-      rows_src.load16(r, g, v);
-      encode_group16(v, global, packed + r * (cols / 2) + g * 8, sf_tiled + sf_tiled_offset(r, g, cols));
+      rows_src.load16(src, g, v);
+      encode_group16(v, global, prow + g * 8, srow + (kRowMajorSf ? (uint32_t)g : sf_tiled_group_offset(g)));
     }
+  }
+}
+
+// Gathered NVFP4 rows from token rows quantized once (codes [tokens, cols/2],
+// row-major factors [tokens, cols/16], cols % 64 == 0): one warp per layout
+// row copies the token's codes (16-byte vectors) and its factors, four groups
+// (one 4-byte word) at a time, into the tiled layout; padding rows get zeros,
+// or nothing with `skip`.  NVFP4 encoding is row-local and every gathered row
+// shares the one global, so the copies equal encoding the gathered rows.
+__global__ void gather_codes_kernel(const uint8_t *tok_packed, const uint8_t *tok_sf, int tokens,
+                                    const int32_t *token_rows, size_t rows, const int32_t *valid,
+                                    const int32_t *skip, size_t cols, uint8_t *packed, uint8_t *sf_tiled) {
+  const int lane = threadIdx.x & 31;
+  const int code_vecs = (int)(cols / 32), sf_words = (int)(cols / 64);
+  const size_t n = valid_rows(rows, valid), warps = (size_t)gridDim.x * (blockDim.x / 32);
+  for (size_t r = (size_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; r < n; r += warps) {
+    const int t = token_rows[r];
+    if (skip && t < 0) continue;
+    const bool zero = t < 0 || t >= tokens;
+    const uint4 *csrc = reinterpret_cast<const uint4 *>(tok_packed + (size_t)max(t, 0) * (cols / 2));
+    uint4 *cdst = reinterpret_cast<uint4 *>(packed + r * (cols / 2));
+    for (int i = lane; i < code_vecs; i += 32) cdst[i] = zero ? make_uint4(0, 0, 0, 0) : csrc[i];
+    const uint32_t *ssrc = reinterpret_cast<const uint32_t *>(tok_sf + (size_t)max(t, 0) * (cols / 16));
+    uint8_t *srow = sf_tiled + sf_tiled_row_offset(r, cols);
+    for (int j = lane; j < sf_words; j += 32)
+      *reinterpret_cast<uint32_t *>(srow + (size_t)j * kSfChunk) = zero ? 0u : ssrc[j];
   }
 }
 
@@ -473,6 +526,14 @@ static unsigned row_grid(size_t rows) {
   return (unsigned)std::max<size_t>(1, std::min(g, cap));
 }
 
+// The row encode (one warp per row).
+template <class Rows>
+static void launch_rows_encode(const Rows &src, size_t rows, const int32_t *valid, const int32_t *skip, size_t cols,
+                               const uint32_t *amax, uint8_t *packed, uint8_t *sf_tiled, float *global_out,
+                               cudaStream_t s) {
+  rows_encode_kernel<<<row_grid(rows), 256, 0, s>>>(src, rows, valid, skip, cols, amax, packed, sf_tiled, global_out);
+}
+
 }  // namespace fpb
 
 // ---- host side -------------------------------------------------------------------------
@@ -600,10 +661,16 @@ extern "C" int fpb_moe_gather(const void *x, int x_dtype, size_t tokens, size_t 
   });
 }
 
+static size_t align256_sz(size_t n) { return (n + 255) / 256 * 256; }
+
+extern "C" size_t fpb_moe_gather_quantize_workspace_bytes(size_t tokens, size_t cols) {
+  return align256_sz(tokens * cols / 2) + tokens * cols / 16;
+}
+
 extern "C" int fpb_moe_gather_quantize(const void *x, int x_dtype, size_t tokens, size_t cols,
                                        const int32_t *token_rows, size_t rows, const int32_t *valid_rows,
                                        uint8_t *packed, uint8_t *sf_tiled, float *global_out, float *amax_scratch,
-                                       int flags, void *stream) {
+                                       int flags, void *workspace, size_t workspace_bytes, void *stream) {
   if (!x || !token_rows || !packed || !sf_tiled || !global_out || !amax_scratch)
     return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_moe_gather_quantize: null pointer");
   if (tokens == 0 || rows == 0 || cols == 0 || cols % 32) return fail(FPB_ERR_SHAPE, "fpb_moe_gather_quantize: shape");
@@ -625,9 +692,25 @@ extern "C" int fpb_moe_gather_quantize(const void *x, int x_dtype, size_t tokens
     }
     GatherRows<T> src{xs, token_rows, cols, (int)tokens};
     const int32_t *skip = (flags & FPB_QUANT_SKIP_PADDING) ? token_rows : nullptr;
-    rows_encode_kernel<<<row_grid(rows), 256, 0, s>>>(src, rows, valid_rows, skip, cols, amax, packed, sf_tiled,
-                                                       global_out);
-    FPB_LAUNCH_CHECK("rows_encode_kernel(gather)");
+    const bool via_tokens = workspace && workspace_bytes >= fpb_moe_gather_quantize_workspace_bytes(tokens, cols) &&
+                            cols % 64 == 0 && tokens <= 0x7fffffffu &&
+                            !(reinterpret_cast<uintptr_t>(workspace) & 255) &&
+                            !(reinterpret_cast<uintptr_t>(packed) & 15);
+    if (!via_tokens) {
+      launch_rows_encode(src, rows, valid_rows, skip, cols, amax, packed, sf_tiled, global_out, s);
+      FPB_LAUNCH_CHECK("rows_encode_kernel(gather)");
+      return (int)FPB_OK;
+    }
+    // each token once, then copies into the layout's rows
+    uint8_t *tok_packed = static_cast<uint8_t *>(workspace);
+    uint8_t *tok_sf = tok_packed + align256_sz(tokens * cols / 2);
+    PlainRows<T> tok{xs, cols};
+    rows_encode_kernel<PlainRows<T>, true><<<row_grid(tokens), 256, 0, s>>>(tok, tokens, nullptr, nullptr, cols, amax,
+                                                                             tok_packed, tok_sf, global_out);
+    FPB_LAUNCH_CHECK("rows_encode_kernel(tokens)");
+    gather_codes_kernel<<<row_grid(rows), 256, 0, s>>>(tok_packed, tok_sf, (int)tokens, token_rows, rows, valid_rows,
+                                                        skip, cols, packed, sf_tiled);
+    FPB_LAUNCH_CHECK("gather_codes_kernel");
     return (int)FPB_OK;
   });
 }
@@ -673,8 +756,7 @@ extern "C" int fpb_swiglu_quantize(const void *gate_up, int dtype, size_t rows, 
       rows_amax_kernel<<<grid, 256, 0, s>>>(src, rows, valid_rows, nullptr, inter, amax);
       FPB_LAUNCH_CHECK("rows_amax_kernel(swiglu)");
     }
-    rows_encode_kernel<<<grid, 256, 0, s>>>(src, rows, valid_rows, nullptr, inter, amax, packed, sf_tiled,
-                                             global_out);
+    launch_rows_encode(src, rows, valid_rows, nullptr, inter, amax, packed, sf_tiled, global_out, s);
     FPB_LAUNCH_CHECK("rows_encode_kernel(swiglu)");
     return (int)FPB_OK;
   });
@@ -704,7 +786,7 @@ extern "C" int fpb_rows_quantize(const void *x, int dtype, size_t rows, const in
       rows_amax_kernel<<<grid, 256, 0, s>>>(src, rows, valid_rows, skip, cols, amax);
       FPB_LAUNCH_CHECK("rows_amax_kernel(rows)");
     }
-    rows_encode_kernel<<<grid, 256, 0, s>>>(src, rows, valid_rows, skip, cols, amax, packed, sf_tiled, global_out);
+    launch_rows_encode(src, rows, valid_rows, skip, cols, amax, packed, sf_tiled, global_out, s);
     FPB_LAUNCH_CHECK("rows_encode_kernel(rows)");
     return (int)FPB_OK;
   });

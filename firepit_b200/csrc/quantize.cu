@@ -78,7 +78,8 @@ __global__ void nvfp4_encode_kernel(const T *w, size_t rows, size_t cols, size_t
     uint32_t lo = 0, hi = 0;
     if (denom > 0.0f) {
       float q[kNvfp4Group];
-      e2m1_quotients16(v, denom, q);
+  #pragma unroll
+    for (int i = 0; i < 16; ++i) q[i] = __fdiv_rn(v[i], denom);
       lo = f32x8_to_e2m1x8(q);
       hi = f32x8_to_e2m1x8(q + 8);
     }

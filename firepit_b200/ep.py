@@ -128,7 +128,7 @@ class DeviceOps:
         if n:
             N.call("fpb_moe_gather_quantize", x.data_ptr(), _dt(x), n, h, lay["tr"].data_ptr(), cap,
                    lay["pad"].data_ptr(), a1.data_ptr(), sf1.data_ptr(), scal.data_ptr(), scal[1:].data_ptr(),
-                   N.FPB_QUANT_AMAX_GIVEN | skip, self._s())
+                   N.FPB_QUANT_AMAX_GIVEN | skip, None, 0, self._s())
             N.call("fpb_nvfp4_grouped_gemm_swiglu_q", w1.handle, a1.data_ptr(), sf1.data_ptr(), scal.data_ptr(), cap,
                    lay["te"].data_ptr(), lay["tr"].data_ptr(), inter, hbuf.data_ptr(), N.FPB_BF16, a_h.data_ptr(),
                    self._s())

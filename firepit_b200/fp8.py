@@ -201,7 +201,9 @@ class Fp8Gemm:
         import torch
         sink = sink or Eager()
         m = self.x.shape[0]
-        need = int(N.lib.fpb_fp8_gemm_workspace_bytes(m, self.weight.cols))
+        # activations + the stream-K partial sums of this row range
+        need = int(N.lib.fpb_fp8_gemm_workspace_bytes(m, self.weight.cols)) + int(
+            N.lib.fpb_fp8_gemm_split_bytes(m, self.weight.cols, len(self.rows)))
         ws = self.workspace
         if ws is None or ws.numel() * ws.element_size() < need:
             ws = torch.empty(need, dtype=torch.uint8, device=self.x.device)

@@ -305,17 +305,23 @@ def gather_prefill_view(sorted_out, x, plan: PrefillPlan, stream=None) -> None:
            sorted_out.data_ptr(), _dt(sorted_out), _stream(x, stream))
 
 
-def gather_quantize(x, plan: PrefillPlan, stream=None):
+def gather_quantize(x, plan: PrefillPlan, stream=None, per_token: bool = True):
     """Gather fused with the NVFP4 activation quantize: (packed [cap, H/2],
-    tiled factors, global f32 [1]) for the grouped NVFP4 GEMM."""
+    tiled factors, global f32 [1]) for the grouped NVFP4 GEMM.  per_token:
+    encode each token row once and copy its codes to the rows that route it
+    (H % 64 == 0; the bytes equal encoding every gathered row)."""
     import torch
     tokens, h = x.shape
     packed = torch.empty(plan.cap, h // 2, dtype=torch.uint8, device=x.device)
     sf = torch.empty(int(N.lib.fpb_nvfp4_act_sf_bytes(plan.cap, h)), dtype=torch.uint8, device=x.device)
     scal = torch.empty(2, dtype=torch.float32, device=x.device)
+    ws, ws_bytes = None, 0
+    if per_token:
+        ws_bytes = int(N.lib.fpb_moe_gather_quantize_workspace_bytes(tokens, h))
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
     N.call("fpb_moe_gather_quantize", x.data_ptr(), _dt(x), tokens, h, plan.token_rows.data_ptr(), plan.cap,
            plan.padded_rows_dev.data_ptr(), packed.data_ptr(), sf.data_ptr(), scal.data_ptr(), scal[1:].data_ptr(), 0,
-           _stream(x, stream))
+           None if ws is None else ws.data_ptr(), ws_bytes, _stream(x, stream))
     return packed, sf, scal[:1]
 
 

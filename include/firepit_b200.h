@@ -258,7 +258,19 @@ size_t fpb_fp8_gemm_workspace_bytes(size_t m, size_t k);
  * 128 and of block_n; y [m, row_end - row_begin]. */
 int fpb_fp8_gemm_q(fpb_fp8_matrix *w, size_t row_begin, size_t row_end, const uint8_t *a_bits,
                    const float *a_scales, size_t m, void *y, int y_dtype, void *stream);
-/* Quantize x [m, K] (f32 or bf16) into `workspace` and run the GEMM. */
+/* The same with a stream-K schedule when `split_ws` (256-byte aligned, at
+ * least fpb_fp8_gemm_split_bytes(m, K, rows) bytes) is given: one CTA per SM,
+ * each taking an equal share of all tiles' 128-wide K blocks; a tile split
+ * between two CTAs is finished by the last of them from f32 partial sums in
+ * the workspace (no CTA waits for another; the two parts are added in a fixed
+ * order).  Too small or null: as fpb_fp8_gemm_q. */
+int fpb_fp8_gemm_q_split(fpb_fp8_matrix *w, size_t row_begin, size_t row_end, const uint8_t *a_bits,
+                         const float *a_scales, size_t m, void *y, int y_dtype, void *split_ws,
+                         size_t split_bytes, void *stream);
+size_t fpb_fp8_gemm_split_bytes(size_t m, size_t k, size_t n);
+/* Quantize x [m, K] (f32 or bf16) into `workspace` and run the GEMM; a
+ * workspace of fpb_fp8_gemm_workspace_bytes(m, K) + fpb_fp8_gemm_split_bytes(m,
+ * K, rows) bytes also gets the stream-K schedule. */
 int fpb_fp8_gemm(fpb_fp8_matrix *w, size_t row_begin, size_t row_end, const void *x, int x_dtype, size_t m,
                  void *y, int y_dtype, void *workspace, size_t workspace_bytes, void *stream);
 /* Grouped (MoE) GEMM, as fpb_nvfp4_grouped_gemm_q: row tile t (128 rows) of
@@ -303,10 +315,17 @@ int fpb_moe_gather(const void *x, int x_dtype, size_t tokens, size_t cols, const
  * (global from amax over x): packed [rows, cols/2], tiled factors, global.
  * valid_rows (nullable device int32, e.g. fpb_moe_layout's padded_rows):
  * rows at or past it are not written (their row tiles are skipped); with
- * FPB_QUANT_SKIP_PADDING neither are padding rows (token -1). */
+ * FPB_QUANT_SKIP_PADDING neither are padding rows (token -1).  workspace
+ * (nullable, 256-byte aligned, fpb_moe_gather_quantize_workspace_bytes):
+ * when given and cols % 64 == 0, each token row is encoded once and its codes
+ * and factors are copied to every layout row that routes it (same bytes:
+ * the encode is row-local with one global), instead of encoding each
+ * gathered row. */
 int fpb_moe_gather_quantize(const void *x, int x_dtype, size_t tokens, size_t cols, const int32_t *token_rows,
                             size_t rows, const int32_t *valid_rows, uint8_t *packed, uint8_t *sf_tiled,
-                            float *global_out, float *amax_scratch, int flags, void *stream);
+                            float *global_out, float *amax_scratch, int flags, void *workspace,
+                            size_t workspace_bytes, void *stream);
+size_t fpb_moe_gather_quantize_workspace_bytes(size_t tokens, size_t cols);
 /* swiglu (swiglu.rs:5-20): out [rows, inter] = gate / (1 + exp(-gate)) * up,
  * gate = gate_up[:, :inter], up = gate_up[:, inter:]. */
 int fpb_swiglu(const void *gate_up, int dtype, size_t rows, size_t inter, void *out, int out_dtype,

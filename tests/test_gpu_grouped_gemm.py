@@ -170,7 +170,8 @@ def test_grouped_gemm_swiglu_rejects_bad_inter(F, torch):
     assert e.value.status == 2
 
 
-def test_moe_chain_skips_padding_rows(F, torch):
+@pytest.mark.parametrize("per_token", [False, True])
+def test_moe_chain_skips_padding_rows(F, torch, per_token):
     """FPB_QUANT_SKIP_PADDING + token_rows: the gather encoder leaves padding
     rows untouched (here: garbage, including NaN factors), the fused GEMM keeps
     them out of h's amax and does not need them, the row quantizer skips them,
@@ -197,8 +198,11 @@ def test_moe_chain_skips_padding_rows(F, torch):
         sf1 = garbage(int(N.lib.fpb_nvfp4_act_sf_bytes(pad, hid)))
         scal = torch.zeros(4, dtype=torch.float32, device="cuda")
         flags = N.FPB_QUANT_SKIP_PADDING if skip else 0
+        ws_bytes = int(N.lib.fpb_moe_gather_quantize_workspace_bytes(tokens, hid)) if per_token else 0
+        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device="cuda")
         N.call("fpb_moe_gather_quantize", x.data_ptr(), N.FPB_BF16, tokens, hid, tr.data_ptr(), pad, None,
-               a1.data_ptr(), sf1.data_ptr(), scal.data_ptr(), scal[1:].data_ptr(), flags, None)
+               a1.data_ptr(), sf1.data_ptr(), scal.data_ptr(), scal[1:].data_ptr(), flags,
+               ws.data_ptr() if per_token else None, ws_bytes, None)
         h = torch.full((pad, inter), float("nan"), dtype=torch.bfloat16, device="cuda")
         amax = F.nvfp4_grouped_gemm_swiglu_q(W1, a1, sf1, scal[:1], te, inter, h, token_rows=tr if skip else None)
         a2 = garbage(pad * inter // 2).view(pad, inter // 2)

@@ -112,8 +112,9 @@ def test_plan_top_k_matches_host_parse(F, torch):
     assert np.all(ids[:, k] == experts)
 
 
-@pytest.mark.parametrize("dtype,h", [("f32", 512), ("bf16", 512), ("bf16", 384)])
-def test_gather_and_gather_quantize(F, torch, dtype, h):
+@pytest.mark.parametrize("per_token", [True, False])
+@pytest.mark.parametrize("dtype,h", [("f32", 512), ("bf16", 512), ("bf16", 384), ("bf16", 2048), ("f32", 1024)])
+def test_gather_and_gather_quantize(F, torch, dtype, h, per_token):
     tokens, experts, k = 300, 16, 4
     router = F.MoeDims(h, 128, 128, experts, k)  # routing reads experts and top_k only (h = 384 is not a MoeDims)
     rng = np.random.default_rng(11)
@@ -128,7 +129,7 @@ def test_gather_and_gather_quantize(F, torch, dtype, h):
     xc = x.float().cpu().numpy()
     want = np.where((tr >= 0)[:, None], xc[np.maximum(tr, 0)], 0).astype(np.float32)
     assert np.array_equal(sorted_.cpu().numpy(), want)
-    packed, sf, g = F.gather_quantize(x, plan)
+    packed, sf, g = F.gather_quantize(x, plan, per_token=per_token)
     pad = plan.padded_rows()  # rows past the layout's end are left unwritten
     pa, sa, ga = O.nvfp4_quantize(want[:pad])
     assert g.cpu().numpy()[0] == ga[0]
@@ -137,7 +138,8 @@ def test_gather_and_gather_quantize(F, torch, dtype, h):
     assert np.all(tiled_padding(sf.cpu().numpy(), plan.cap, h) == 0)
 
 
-@pytest.mark.parametrize("dtype,inter", [("f32", 256), ("bf16", 256), ("f32", 128), ("bf16", 96)])
+@pytest.mark.parametrize("dtype,inter", [("f32", 256), ("bf16", 256), ("f32", 128), ("bf16", 96), ("bf16", 512),
+                                         ("f32", 1024), ("bf16", 2048)])
 def test_swiglu_and_swiglu_quantize(F, torch, dtype, inter):
     rows = 384
     gu = F.synth_normal((rows, 2 * inter), seed=2, stream_id=5, std=3.0)

@@ -59,6 +59,7 @@ __global__ void act_amax_kernel(const T *x, size_t n, uint32_t *amax_bits) {
   if ((reinterpret_cast<uintptr_t>(x) & 15) == 0) {
     const size_t nv = n / kVec;
     const uint4 *xv = reinterpret_cast<const uint4 *>(x);
+#pragma unroll 4
     for (size_t i = tid; i < nv; i += stride) {
       const uint4 u = xv[i];
       const uint32_t w[4] = {u.x, u.y, u.z, u.w};

@@ -631,7 +631,13 @@ static int fp8_gemm_launch(fpb_fp8_matrix *w, const uint8_t *a_bits, const float
   p.ctas = p.tiles;  // whole tiles
   p.max_seg = 1;
   const F8Split sp = fp8_split_plan(m, n_rows, w->cols);
-  if (!tile_experts && split_ws && split_bytes >= sp.partial_bytes + sp.counter_bytes && sp.ctas < p.total_kb) {
+  // Split only a GEMM of less than one wave of tiles: the epilogue promotes
+  // every K block, so a tile boundary inside a CTA's range (store, or partial
+  // sums and their fix-up) stalls the tensor cores for as long as the stores
+  // take; with 224 tiles on 148 SMs (config 1) that cost 19 us more than the
+  // 1.5-wave tail it removes (49 -> 69 us per launch).
+  if (!tile_experts && split_ws && split_bytes >= sp.partial_bytes + sp.counter_bytes && sp.ctas < p.total_kb &&
+      p.tiles < sm_count()) {
     p.ctas = sp.ctas;
     p.max_seg = sp.max_seg;
     p.partials = static_cast<float *>(split_ws);

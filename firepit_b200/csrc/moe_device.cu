@@ -28,6 +28,17 @@ namespace fpb {
 // (softmax restricted to the top k).  With a shared-expert gate, slot k is
 // expert `experts` with weight sigmoid(gate).  Slots past that are id 0,
 // weight 0.
+// Float -> unsigned key with the same order (-inf lowest); NaN is never
+// offered (the loads below turn it into -inf, so it is never chosen, as with
+// the comparisons of the reference's loop).
+__device__ __forceinline__ uint32_t order_key(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float order_key_value(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
 template <int PER_LANE>
 __global__ void moe_topk_kernel(const float *logits, long long ld, const float *shared_gate, int tokens,
                                 int experts, int k, int width, int32_t *ids, float *weights) {
@@ -40,6 +51,7 @@ __global__ void moe_topk_kernel(const float *logits, long long ld, const float *
   for (int i = 0; i < PER_LANE; ++i) {
     const int p = lane + 32 * i;
     v[i] = p < experts ? row[p] : -INFINITY;
+    if (v[i] != v[i]) v[i] = -INFINITY;  // NaN never wins a comparison
     m = fmaxf(m, v[i]);
   }
 #pragma unroll
@@ -58,15 +70,12 @@ __global__ void moe_topk_kernel(const float *logits, long long ld, const float *
         bp = p;
       }
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int op = __shfl_xor_sync(0xffffffffu, bp, o);
-      if (ov > bv || (ov == bv && op < bp)) {
-        bv = ov;
-        bp = op;
-      }
-    }
+    // Warp arg-max in two hardware reductions: the largest value (as an
+    // order-preserving unsigned key), then the lowest id holding it.
+    const uint32_t key = order_key(bv);
+    const uint32_t kmax = __reduce_max_sync(0xffffffffu, key);
+    bp = (int)__reduce_min_sync(0xffffffffu, key == kmax ? (uint32_t)bp : 0xffffffffu);
+    bv = order_key_value(kmax);
     const float score = expf(bv - origin);
     total = total + score;
     if (lane == rank) {

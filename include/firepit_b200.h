@@ -259,11 +259,12 @@ size_t fpb_fp8_gemm_workspace_bytes(size_t m, size_t k);
 int fpb_fp8_gemm_q(fpb_fp8_matrix *w, size_t row_begin, size_t row_end, const uint8_t *a_bits,
                    const float *a_scales, size_t m, void *y, int y_dtype, void *stream);
 /* The same with a stream-K schedule when `split_ws` (256-byte aligned, at
- * least fpb_fp8_gemm_split_bytes(m, K, rows) bytes) is given: one CTA per SM,
- * each taking an equal share of all tiles' 128-wide K blocks; a tile split
- * between two CTAs is finished by the last of them from f32 partial sums in
- * the workspace (no CTA waits for another; the two parts are added in a fixed
- * order).  Too small or null: as fpb_fp8_gemm_q. */
+ * least fpb_fp8_gemm_split_bytes(m, K, rows) bytes) is given and the GEMM has
+ * fewer 128 x 256 tiles than the GPU has SMs: one CTA per SM, each taking an
+ * equal share of all tiles' 128-wide K blocks; a tile split between CTAs is
+ * finished by the last of them from f32 partial sums in the workspace (no CTA
+ * waits for another; the parts are added in a fixed order).  Otherwise, or
+ * with a too small or null workspace: as fpb_fp8_gemm_q. */
 int fpb_fp8_gemm_q_split(fpb_fp8_matrix *w, size_t row_begin, size_t row_end, const uint8_t *a_bits,
                          const float *a_scales, size_t m, void *y, int y_dtype, void *split_ws,
                          size_t split_bytes, void *stream);

@@ -356,24 +356,22 @@ __global__ void __launch_bounds__(kF8Threads, 1)
           tc_fence_after();
           const float ws = __ldg(ws_row + (kb * kF8Tile) / p.bk) * as;
           const uint32_t taddr = tmem + lane_base + b * kF8BN + c_base;
-          // Each chunk's TMEM load overlaps the previous chunk's scale-and-add.
-          uint32_t ra[32], rb[32];
-          tmem_ld32(taddr, ra);
-          tmem_ld_wait(ra);
-          tmem_ld32(taddr + 32, rb);
+          // Two TMEM loads per wait (a wait covers every load in flight, and a
+          // TMEM round trip costs more than 64 FMAs): two round trips per K
+          // block instead of four.
 #pragma unroll
-          for (int j = 0; j < 32; ++j) acc[j] = fmaf(__uint_as_float(ra[j]), ws, acc[j]);
-          tmem_ld_wait(rb);
-          tmem_ld32(taddr + 64, ra);
+          for (int h = 0; h < 2; ++h) {
+            uint32_t ra[32], rb[32];
+            tmem_ld32(taddr + h * 64, ra);
+            tmem_ld32(taddr + h * 64 + 32, rb);
+            tmem_ld_wait(ra);
+            tmem_ld_wait(rb);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) acc[32 + j] = fmaf(__uint_as_float(rb[j]), ws, acc[32 + j]);
-          tmem_ld_wait(ra);
-          tmem_ld32(taddr + 96, rb);
+            for (int j = 0; j < 32; ++j) acc[h * 64 + j] = fmaf(__uint_as_float(ra[j]), ws, acc[h * 64 + j]);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) acc[64 + j] = fmaf(__uint_as_float(ra[j]), ws, acc[64 + j]);
-          tmem_ld_wait(rb);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) acc[96 + j] = fmaf(__uint_as_float(rb[j]), ws, acc[96 + j]);
+            for (int j = 0; j < 32; ++j)
+              acc[h * 64 + 32 + j] = fmaf(__uint_as_float(rb[j]), ws, acc[h * 64 + 32 + j]);
+          }
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&acc_empty[b]);

@@ -346,15 +346,19 @@ __global__ void __launch_bounds__(kF8Threads, 1)
         // A part's columns lie in one block of bn (a multiple of 128) rows.
         const int nb = (n_base + n0 + c_base) / p.bn;
         const float *ws_row = p.w_scale + (size_t)nb * p.ws_cols;
+        // The next K block's scale is loaded before this block's wait, so its
+        // latency hides behind the wait and the promotion (the FMAs need it).
+        float ws_next = __ldg(ws_row + (sg.kb0 * kF8Tile) / p.bk);
         for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++g) {
           const uint32_t b = g & 1;
+          const float ws = ws_next * as;
+          if (kb + 1 < sg.kb1) ws_next = __ldg(ws_row + ((kb + 1) * kF8Tile) / p.bk);
           if (!mbar_wait(&acc_full[b], (g >> 1) & 1, abort_s)) {
             f8_report(p.error, abort_s, 305);
             ok = false;
             break;
           }
           tc_fence_after();
-          const float ws = __ldg(ws_row + (kb * kF8Tile) / p.bk) * as;
           const uint32_t taddr = tmem + lane_base + b * kF8BN + c_base;
           // Two TMEM loads per wait (a wait covers every load in flight, and a
           // TMEM round trip costs more than 64 FMAs): two round trips per K

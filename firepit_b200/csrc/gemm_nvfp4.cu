@@ -342,6 +342,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int m_tile, n_tile, n_base;
       if (!gemm_tile(p, t, n_tiles, m_tile, n_tile, n_base)) continue;
       const uint32_t buf = lt & 1;
+      // What the tile's epilogue reads from memory besides the accumulator
+      // (the rows' tokens, the weight rows' globals) is loaded before the
+      // wait, so its latency hides behind the main loop.
+      const int row0 = m_tile * kBM + qw * 32;
+      const int n0 = n_tile * kBN;
+      const bool row_live = row0 + lane < p.M && (!p.row_tokens || p.row_tokens[row0 + lane] >= 0);
+      float gl[2];
+      if (p.glu) {
+        const int j0 = n_tile * 64;
+        gl[0] = __ldg(p.b_globals + n_base + j0 + ch * 32 + lane);                // gate rows
+        gl[1] = __ldg(p.b_globals + n_base + p.N / 2 + j0 + ch * 32 + lane);  // up rows
+      } else {
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int n = n0 + ch * 64 + c * 32 + lane;
+          gl[c] = n < p.N ? __ldg(p.b_globals + n_base + n) : 0.0f;
+        }
+      }
       if (!mbar_wait(&acc_full[buf], (lt >> 1) & 1, abort_s)) {
         report(p.error, abort_s, 105);
         break;
@@ -365,10 +383,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
       ++lt;
-      const int row0 = m_tile * kBM + qw * 32;
-      const int n0 = n_tile * kBN;
       if (row0 >= p.M) continue;  // the warp's rows are all past the end
-      const bool row_live = row0 + lane < p.M && (!p.row_tokens || p.row_tokens[row0 + lane] >= 0);
       if (!__any_sync(0xffffffffu, row_live)) continue;  // nothing of these 32 rows is needed (both warps agree)
       if (p.glu) {
         // h columns j0 + ch*32 + i: silu(gate) * up, gate / up scaled by ga
@@ -376,9 +391,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // (no branches, so the 32 evaluations interleave): relative error
         // about 1e-6 against the exact formula, far below the NVFP4 encode
         // that follows.
-        const int inter = p.N / 2, j0 = n_tile * 64;
-        const float g_gate = __ldg(p.b_globals + n_base + j0 + ch * 32 + lane);
-        const float g_up = __ldg(p.b_globals + n_base + inter + j0 + ch * 32 + lane);
+        const int j0 = n_tile * 64;
+        const float g_gate = gl[0], g_up = gl[1];
         float v[32];
         uint32_t mx = 0;
 #pragma unroll
@@ -430,13 +444,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // products are scaled in place by every lane (shuffles are warp-wide).
       const int nw = n0 + ch * 64;
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const int n = nw + c * 32 + lane;
-        const float gl = n < p.N ? __ldg(p.b_globals + n_base + n) : 0.0f;
+      for (int c = 0; c < 2; ++c)
 #pragma unroll
         for (int j = 0; j < 32; ++j)
-          r[c][j] = __float_as_uint((__uint_as_float(r[c][j]) * ga) * __shfl_sync(0xffffffffu, gl, j));
-      }
+          r[c][j] = __float_as_uint((__uint_as_float(r[c][j]) * ga) * __shfl_sync(0xffffffffu, gl[c], j));
       if (p.tma_store) {
         if (lane == 0) bulk_wait_read_all();  // this warp's previous stores have left its box
         __syncwarp();

@@ -111,7 +111,11 @@ constexpr int kF8Threads = 128 + 32 * kF8EpiWarps;  // warpgroup 0: producer, MM
 constexpr int kF8CtrlRegs = 56, kF8EpiRegs = 224;
 static_assert(128 * kF8CtrlRegs + 32 * kF8EpiWarps * kF8EpiRegs <= kF8Threads * 168, "register split");
 constexpr uint32_t kF8TmemCols = 512;             // two 256-column accumulators
-constexpr size_t kF8Smem = 1024 + kF8Stages * (kF8ABytes + kF8BBytes) + 256;
+// Epilogue staging: one 32-row x 128-byte box per epilogue warp (128-byte
+// swizzle), stored by TMA while the warp goes on with the next tile.
+constexpr int kF8OutBoxBytes = 32 * 128;
+constexpr size_t kF8Smem = 1024 + kF8Stages * (kF8ABytes + kF8BBytes) + kF8EpiWarps * kF8OutBoxBytes + 256;
+static_assert(kF8Smem <= 232448, "shared memory per CTA");
 
 struct Fp8GemmParams {
   const float *a_scale;  // [M] per token
@@ -126,6 +130,7 @@ struct Fp8GemmParams {
   int bn, bk;      // block scaling: multiples of 128
   int ws_cols;     // columns of the scale grid
   int *error;
+  int tma_store;                // y through tmap_y (else direct per-row stores: unaligned y)
   const int32_t *tile_experts;  // grouped mode (gemm/mod.rs:103-140), else null
   int n_experts;
   // Schedule.  Tile t = n_tile * m_tiles + m_tile (neighbouring CTAs share a
@@ -159,15 +164,31 @@ struct F8Seg {
   int tile, kb0, kb1, seg, nseg;
 };
 
-// Iterates the CTA's parts.
+// Iterates the CTA's parts.  Without partial-sum storage every part is a
+// whole tile: tiles blockIdx.x, blockIdx.x + ctas, ... (persistent CTAs, so a
+// tile's loads and MMAs start while the previous tile's epilogue runs).
 struct F8Sched {
   long long gk, end;
   __device__ __forceinline__ F8Sched(const Fp8GemmParams &p) {
-    gk = (long long)blockIdx.x * p.total_kb / p.ctas;
-    end = ((long long)blockIdx.x + 1) * p.total_kb / p.ctas;
+    if (p.partials) {
+      gk = (long long)blockIdx.x * p.total_kb / p.ctas;
+      end = ((long long)blockIdx.x + 1) * p.total_kb / p.ctas;
+    } else {
+      gk = blockIdx.x;
+      end = p.tiles;
+    }
   }
   __device__ __forceinline__ bool next(const Fp8GemmParams &p, F8Seg &g) {
     if (gk >= end) return false;
+    if (!p.partials) {
+      g.tile = (int)gk;
+      g.kb0 = 0;
+      g.kb1 = p.kb_count;
+      g.seg = 0;
+      g.nseg = 1;
+      gk += p.ctas;
+      return true;
+    }
     g.tile = (int)(gk / p.kb_count);
     g.kb0 = (int)(gk - (long long)g.tile * p.kb_count);
     g.kb1 = (int)min((long long)p.kb_count, g.kb0 + (end - gk));
@@ -184,17 +205,19 @@ struct F8Sched {
 template <bool kBlocks>
 __global__ void __launch_bounds__(kF8Threads, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                    Fp8GemmParams p) {
+                    const __grid_constant__ CUtensorMap tmap_y, Fp8GemmParams p) {
   using namespace sm100;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t *sA = base;
   uint8_t *sB = sA + kF8Stages * kF8ABytes;
-  uint64_t *full = reinterpret_cast<uint64_t *>(sB + kF8Stages * kF8BBytes);
+  uint8_t *sOut = sB + kF8Stages * kF8BBytes;  // [kF8EpiWarps][32 rows][128 bytes]
+  uint64_t *full = reinterpret_cast<uint64_t *>(sOut + kF8EpiWarps * kF8OutBoxBytes);
   uint64_t *empty = full + kF8Stages;
-  uint64_t *acc_full = empty + kF8Stages;  // [2]
-  uint64_t *acc_empty = acc_full + 2;      // [2]
-  uint32_t *tmem_base_s = reinterpret_cast<uint32_t *>(acc_empty + 2);
+  // Accumulator barriers per (buffer, column half): [b * 2 + h].
+  uint64_t *acc_full = empty + kF8Stages;  // [4]
+  uint64_t *acc_empty = acc_full + 4;      // [4]
+  uint32_t *tmem_base_s = reinterpret_cast<uint32_t *>(acc_empty + 4);
   volatile int *abort_s = reinterpret_cast<volatile int *>(tmem_base_s + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -226,14 +249,15 @@ __global__ void __launch_bounds__(kF8Threads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < 4; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], kF8EpiWarps);
+      mbar_init(&acc_empty[b], kF8EpiWarps / 2);  // the four warps of a column half
     }
     *abort_s = 0;
     fence_barrier_init();
     prefetch_tensormap(&tmap_a);
     prefetch_tensormap(&tmap_b);
+    if (p.tma_store) prefetch_tensormap(&tmap_y);
   }
   if (warp == 1) {
     tmem_alloc(tmem_base_s, kF8TmemCols);
@@ -275,20 +299,28 @@ __global__ void __launch_bounds__(kF8Threads, 1)
   } else if (warp == 1) {
     // ---- MMA issuer -------------------------------------------------------------
     // Blocks: each K block into TMEM buffer (g & 1); rows: each part into
-    // buffer (part & 1), accumulated over its K blocks.
+    // buffer (part & 1), accumulated over its K blocks.  Each K block runs as
+    // two N = 128 halves (B rows 0-127, then 128-255) with their own
+    // barriers, so the epilogue warps of a column half take their columns as
+    // soon as those are done, and hand them back independently: the half
+    // has one and a half K blocks of MMA time to be read and released.
     if (elect_one()) {
-      const uint32_t idesc = idesc_f8(kF8Tile, kF8BN);
+      constexpr int kHalf = kF8BN / 2;
+      const uint32_t idesc = idesc_f8(kF8Tile, kHalf);
       uint32_t g = 0, part = 0;
       bool ok = true;
       F8Sched sched(p);
       F8Seg sg;
       while (ok && sched.next(p, sg)) {
         const uint32_t pb = part & 1;
-        if (!kBlocks && part >= 2 && !mbar_wait(&acc_empty[pb], ((part >> 1) - 1) & 1, abort_s)) {
-          f8_report(p.error, abort_s, 304);
-          break;
-        }
-        for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++g) {
+        if (!kBlocks && part >= 2)
+          for (int h = 0; h < 2 && ok; ++h)
+            if (!mbar_wait(&acc_empty[pb * 2 + h], ((part >> 1) - 1) & 1, abort_s)) {
+              f8_report(p.error, abort_s, 304);
+              ok = false;
+            }
+        if (!ok) break;
+        for (int kb = sg.kb0; kb < sg.kb1 && ok; ++kb, ++g) {
           const uint32_t s = g % kF8Stages;
           if (!mbar_wait(&full[s], (g / kF8Stages) & 1, abort_s)) {
             f8_report(p.error, abort_s, 303);
@@ -296,24 +328,32 @@ __global__ void __launch_bounds__(kF8Threads, 1)
             break;
           }
           const uint32_t b = kBlocks ? (g & 1) : pb;
-          if (kBlocks && g >= 2 && !mbar_wait(&acc_empty[b], ((g >> 1) - 1) & 1, abort_s)) {
-            f8_report(p.error, abort_s, 304);
-            ok = false;
-            break;
-          }
-          tc_fence_after();
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t a_desc = smem_desc(smem_u32(sA + s * kF8ABytes) + kk * 32, 16, 1024, 2);
-            const uint64_t b_desc = smem_desc(smem_u32(sB + s * kF8BBytes) + kk * 32, 16, 1024, 2);
-            const uint32_t acc = kBlocks ? (kk != 0) : (kb != sg.kb0 || kk != 0);
-            mma_f8(tmem + b * kF8BN, a_desc, b_desc, idesc, acc);
+          for (int h = 0; h < 2; ++h) {
+            if (kBlocks && g >= 2 && !mbar_wait(&acc_empty[b * 2 + h], ((g >> 1) - 1) & 1, abort_s)) {
+              f8_report(p.error, abort_s, 304);
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t a_desc = smem_desc(smem_u32(sA + s * kF8ABytes) + kk * 32, 16, 1024, 2);
+              const uint64_t b_desc =
+                  smem_desc(smem_u32(sB + s * kF8BBytes + h * (kHalf * kF8Tile)) + kk * 32, 16, 1024, 2);
+              const uint32_t acc = kBlocks ? (kk != 0) : (kb != sg.kb0 || kk != 0);
+              mma_f8(tmem + b * kF8BN + h * kHalf, a_desc, b_desc, idesc, acc);
+            }
+            if (kBlocks) tc_commit(&acc_full[b * 2 + h]);
           }
+          if (!ok) break;
           tc_commit(&empty[s]);
-          if (kBlocks) tc_commit(&acc_full[b]);
         }
         if (!ok) break;
-        if (!kBlocks) tc_commit(&acc_full[pb]);
+        if (!kBlocks) {
+          tc_commit(&acc_full[pb * 2]);
+          tc_commit(&acc_full[pb * 2 + 1]);
+        }
         ++part;
       }
     }
@@ -353,11 +393,12 @@ __global__ void __launch_bounds__(kF8Threads, 1)
           const uint32_t b = g & 1;
           const float ws = ws_next * as;
           if (kb + 1 < sg.kb1) ws_next = __ldg(ws_row + ((kb + 1) * kF8Tile) / p.bk);
-          if (!mbar_wait(&acc_full[b], (g >> 1) & 1, abort_s)) {
+          if (!mbar_wait(&acc_full[b * 2 + half], (g >> 1) & 1, abort_s)) {
             f8_report(p.error, abort_s, 305);
             ok = false;
             break;
           }
+          __syncwarp();  // the TMEM loads below are warp-collective
           tc_fence_after();
           const uint32_t taddr = tmem + lane_base + b * kF8BN + c_base;
           // Two TMEM loads per wait (a wait covers every load in flight, and a
@@ -370,23 +411,28 @@ __global__ void __launch_bounds__(kF8Threads, 1)
             tmem_ld32(taddr + h * 64 + 32, rb);
             tmem_ld_wait(ra);
             tmem_ld_wait(rb);
+            if (h == 1) {
+              // The whole buffer is in registers: hand it back to the tensor
+              // cores before the last 64 FMAs, which then overlap the next MMA.
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&acc_empty[b * 2 + half]);
+            }
 #pragma unroll
             for (int j = 0; j < 32; ++j) acc[h * 64 + j] = fmaf(__uint_as_float(ra[j]), ws, acc[h * 64 + j]);
 #pragma unroll
             for (int j = 0; j < 32; ++j)
               acc[h * 64 + 32 + j] = fmaf(__uint_as_float(rb[j]), ws, acc[h * 64 + 32 + j]);
           }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&acc_empty[b]);
         }
         if (!ok) break;
       } else {
         const uint32_t pb = part & 1;
-        if (!mbar_wait(&acc_full[pb], (part >> 1) & 1, abort_s)) {
+        if (!mbar_wait(&acc_full[pb * 2 + half], (part >> 1) & 1, abort_s)) {
           f8_report(p.error, abort_s, 305);
           break;
         }
+        __syncwarp();
         tc_fence_after();
 #pragma unroll
         for (int c = 0; c < kCols / 32; ++c) {
@@ -398,7 +444,7 @@ __global__ void __launch_bounds__(kF8Threads, 1)
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[pb]);
+        if (lane == 0) mbar_arrive(&acc_empty[pb * 2 + half]);
         ++part;
       }
       const int nc = n0 + c_base;
@@ -433,8 +479,8 @@ __global__ void __launch_bounds__(kF8Threads, 1)
         }
         if (lane == 0) *counter = 0;  // ready for the next launch
       }
-      if (row >= p.M) continue;
-      // Final scale in place (rows mode: token x weight-row scale).
+      // Final scale in place (rows mode: token x weight-row scale; rows past
+      // M have a zero token scale and are not stored).
       if (!kBlocks) {
 #pragma unroll
         for (int j = 0; j < kCols; ++j) {
@@ -442,6 +488,58 @@ __global__ void __launch_bounds__(kF8Threads, 1)
           acc[j] = acc[j] * (as * ws);
         }
       }
+      if (p.tma_store) {
+        // The warp's 32 rows x 128 columns leave as 128-byte-wide boxes (64
+        // bf16 or 32 f32 columns) through its own staging box: each lane
+        // writes its row (16-byte chunks XOR-swizzled by row, the 128-byte
+        // swizzle), then one lane issues the tiled store, which clips rows
+        // past M and columns past N.  Every lane takes every step.
+        const int row0 = m0 + qd * 32;
+        if (row0 >= p.M) continue;  // warp-uniform
+        uint8_t *box = sOut + (warp - 4) * kF8OutBoxBytes;
+        uint8_t *row_s = box + lane * 128;
+        auto store_box = [&](int col) {
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if (col < p.N) tma_store_2d(&tmap_y, box, col, row0);
+            bulk_commit_group();
+          }
+        };
+        if (p.y_bf16) {
+#pragma unroll
+          for (int bx = 0; bx < 2; ++bx) {  // 64 columns per box
+            if (lane == 0) bulk_wait_read_all();  // the previous box has left the staging
+            __syncwarp();
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const int j = bx * 64 + 8 * q;
+              uint4 pk;
+              pk.x = pack_bf16x2(acc[j], acc[j + 1]);
+              pk.y = pack_bf16x2(acc[j + 2], acc[j + 3]);
+              pk.z = pack_bf16x2(acc[j + 4], acc[j + 5]);
+              pk.w = pack_bf16x2(acc[j + 6], acc[j + 7]);
+              *reinterpret_cast<uint4 *>(row_s + ((q ^ (lane & 7)) * 16)) = pk;
+            }
+            store_box(nc + bx * 64);
+          }
+        } else {
+#pragma unroll
+          for (int bx = 0; bx < 4; ++bx) {  // 32 columns per box
+            if (lane == 0) bulk_wait_read_all();
+            __syncwarp();
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const int j = bx * 32 + 4 * q;
+              *reinterpret_cast<float4 *>(row_s + ((q ^ (lane & 7)) * 16)) =
+                  make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+            }
+            store_box(nc + bx * 32);
+          }
+        }
+        continue;
+      }
+      if (row >= p.M) continue;  // direct stores only below: no warp-collective step follows
       const long long off = (long long)row * p.ldy + nc;
       const bool full_cols = nc + kCols <= p.N;
       if (p.y_bf16) {
@@ -474,6 +572,8 @@ __global__ void __launch_bounds__(kF8Threads, 1)
         }
       }
     }
+    // Stores in flight read this CTA's shared memory: complete them before exit.
+    if (lane == 0 && p.tma_store) bulk_wait_all();
   }
   tc_fence_before();
   __syncthreads();
@@ -630,7 +730,9 @@ static int fp8_gemm_launch(fpb_fp8_matrix *w, const uint8_t *a_bits, const float
   p.m_tiles = (int)((m + kF8Tile - 1) / kF8Tile);
   p.tiles = p.m_tiles * (int)((n_rows + kF8BN - 1) / kF8BN);
   p.total_kb = (long long)p.tiles * p.kb_count;
-  p.ctas = p.tiles;  // whole tiles
+  // Whole tiles, one persistent CTA per SM (grouped: one CTA per tile, so
+  // that a CTA whose row tile is dead can leave at once).
+  p.ctas = tile_experts ? p.tiles : std::min(p.tiles, std::max(1, sm_count()));
   p.max_seg = 1;
   const F8Split sp = fp8_split_plan(m, n_rows, w->cols);
   // Split only a GEMM of less than one wave of tiles: the epilogue promotes
@@ -646,7 +748,10 @@ static int fp8_gemm_launch(fpb_fp8_matrix *w, const uint8_t *a_bits, const float
     p.tile_counters = reinterpret_cast<int *>(static_cast<uint8_t *>(split_ws) + sp.partial_bytes);
     FPB_CUDA_TRY(cudaMemsetAsync(p.tile_counters, 0, sp.counter_bytes, s));
   }
-  kernel<<<p.ctas, kF8Threads, kF8Smem, s>>>(tmap_a, *reinterpret_cast<const CUtensorMap *>(w->tmap), p);
+  CUtensorMap tmap_y;
+  std::memset(&tmap_y, 0, sizeof(tmap_y));
+  p.tma_store = encode_store_map(&tmap_y, y, p.y_bf16, m, n_rows, (uint64_t)p.ldy, 32, 0);
+  kernel<<<p.ctas, kF8Threads, kF8Smem, s>>>(tmap_a, *reinterpret_cast<const CUtensorMap *>(w->tmap), tmap_y, p);
   FPB_LAUNCH_CHECK("fp8_gemm_kernel");
   return FPB_OK;
 }

@@ -134,18 +134,20 @@ struct Fp8GemmParams {
   const int32_t *tile_experts;  // grouped mode (gemm/mod.rs:103-140), else null
   int n_experts;
   // Schedule.  Tile t = n_tile * m_tiles + m_tile (neighbouring CTAs share a
-  // weight tile).  CTA c runs the K blocks [c*T/G, (c+1)*T/G) of the
-  // concatenation of all tiles' K blocks (T = tiles * kb_count, G = grid):
-  // whole tiles, or a tile's K range split between consecutive CTAs
-  // (stream-K).  A CTA with part of a tile writes its f32 partial sums to
-  // `partials` [tiles][max_seg][128][256]; the last of the tile's parts to
-  // finish (per epilogue warp, a counter per tile and warp) adds them in part
-  // order and stores the tile.  No CTA waits for another.
+  // weight tile).  CTA c first runs whole tiles c, c + G, ... below
+  // whole_tiles (G = grid), then the K blocks [c*T/G, (c+1)*T/G) of the
+  // concatenation of the remaining tiles' K blocks (T = total_kb): whole
+  // tiles, or a tile's K range split between consecutive CTAs (stream-K
+  // over the last, partial wave).  A CTA with part of a tile writes its f32
+  // partial sums to `partials`; the last of the tile's parts to finish (per
+  // epilogue warp, a counter per tile and warp) adds them in part order and
+  // stores the tile.  No CTA waits for another.
   int m_tiles, tiles;
-  long long total_kb;
+  int whole_tiles;      // tiles [0, whole_tiles) run whole, strided over the CTAs
+  long long total_kb;   // K blocks of the remaining (split) tiles
   int ctas, max_seg;
-  float *partials;      // null: every CTA runs whole tiles (G = tiles)
-  int *tile_counters;   // [tiles][kF8EpiWarps], zero at launch, left zero
+  float *partials;      // [split tiles][max_seg][kF8EpiWarps][32][32 lanes] float4; null: no split
+  int *tile_counters;   // [split tiles][kF8EpiWarps], zero at launch, left zero
 };
 
 __device__ __forceinline__ void f8_report(int *error, volatile int *abort, int code) {
@@ -169,30 +171,27 @@ struct F8Seg {
 // tile's loads and MMAs start while the previous tile's epilogue runs).
 struct F8Sched {
   long long gk, end;
+  int t;
   __device__ __forceinline__ F8Sched(const Fp8GemmParams &p) {
-    if (p.partials) {
-      gk = (long long)blockIdx.x * p.total_kb / p.ctas;
-      end = ((long long)blockIdx.x + 1) * p.total_kb / p.ctas;
-    } else {
-      gk = blockIdx.x;
-      end = p.tiles;
-    }
+    t = blockIdx.x;
+    gk = p.partials ? (long long)blockIdx.x * p.total_kb / p.ctas : 0;
+    end = p.partials ? ((long long)blockIdx.x + 1) * p.total_kb / p.ctas : 0;
   }
   __device__ __forceinline__ bool next(const Fp8GemmParams &p, F8Seg &g) {
-    if (gk >= end) return false;
-    if (!p.partials) {
-      g.tile = (int)gk;
+    if (t < p.whole_tiles) {
+      g.tile = t;
       g.kb0 = 0;
       g.kb1 = p.kb_count;
       g.seg = 0;
       g.nseg = 1;
-      gk += p.ctas;
+      t += p.ctas;
       return true;
     }
-    g.tile = (int)(gk / p.kb_count);
-    g.kb0 = (int)(gk - (long long)g.tile * p.kb_count);
+    if (gk >= end) return false;
+    g.tile = p.whole_tiles + (int)(gk / p.kb_count);
+    g.kb0 = (int)(gk - (long long)(g.tile - p.whole_tiles) * p.kb_count);
     g.kb1 = (int)min((long long)p.kb_count, g.kb0 + (end - gk));
-    const long long t0 = (long long)g.tile * p.kb_count;
+    const long long t0 = (long long)(g.tile - p.whole_tiles) * p.kb_count;
     const long long first = f8_cta_of(t0, p.total_kb, p.ctas);
     const long long last = f8_cta_of(t0 + p.kb_count - 1, p.total_kb, p.ctas);
     g.seg = (int)(blockIdx.x - first);
@@ -450,15 +449,23 @@ __global__ void __launch_bounds__(kF8Threads, 1)
       const int nc = n0 + c_base;
       if (sg.nseg > 1) {
         // Part of a split tile: publish this warp's 32 x 128 partial sums; the
-        // warp that completes the tile's count adds all parts in order.
-        const size_t slot_row = ((size_t)sg.tile * p.max_seg + sg.seg) * kF8Tile + qd * 32 + lane;
-        float4 *mine = reinterpret_cast<float4 *>(p.partials + slot_row * kF8BN + c_base);
+        // warp that completes the tile's count adds all parts in order.  The
+        // layout is private to this kernel and lane-major (float4 j of lane l
+        // at [j][l]), so every store and load of a warp is 512 contiguous
+        // bytes; the warp of the same role reads it back.
+        const int st = sg.tile - p.whole_tiles;
+        auto slot = [&](int q) {
+          return reinterpret_cast<float4 *>(p.partials) +
+                 (((size_t)st * p.max_seg + q) * kF8EpiWarps + (warp - 4)) * (kCols / 4) * 32 + lane;
+        };
+        float4 *mine = slot(sg.seg);
 #pragma unroll
-        for (int j = 0; j < kCols / 4; ++j) mine[j] = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
+        for (int j = 0; j < kCols / 4; ++j)
+          mine[j * 32] = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
         __threadfence();
         __syncwarp();
         int done = 0;
-        int *counter = p.tile_counters + (size_t)sg.tile * kF8EpiWarps + (warp - 4);
+        int *counter = p.tile_counters + (size_t)st * kF8EpiWarps + (warp - 4);
         if (lane == 0) done = atomicAdd(counter, 1);
         done = __shfl_sync(0xffffffffu, done, 0);
         if (done != sg.nseg - 1) continue;  // another part finishes this tile
@@ -466,11 +473,10 @@ __global__ void __launch_bounds__(kF8Threads, 1)
 #pragma unroll
         for (int j = 0; j < kCols; ++j) acc[j] = 0.0f;
         for (int q = 0; q < sg.nseg; ++q) {
-          const size_t r_q = ((size_t)sg.tile * p.max_seg + q) * kF8Tile + qd * 32 + lane;
-          const float4 *src = reinterpret_cast<const float4 *>(p.partials + r_q * kF8BN + c_base);
+          const float4 *src = slot(q);
 #pragma unroll
           for (int j = 0; j < kCols / 4; ++j) {
-            const float4 v = __ldcg(src + j);
+            const float4 v = __ldcg(src + j * 32);
             acc[4 * j] += v.x;
             acc[4 * j + 1] += v.y;
             acc[4 * j + 2] += v.z;
@@ -679,18 +685,36 @@ static int fp8_prepare(fpb_fp8_matrix *w) {
 // Stream-K schedule of a dense GEMM: grid, parts per tile at most, bytes of
 // partial sums and counters.
 struct F8Split {
-  int ctas, max_seg;
+  int ctas, whole, max_seg;
+  long long tail_kb;
+  bool split;
   size_t partial_bytes, counter_bytes;
 };
+// Whole tiles in waves over the SMs.  A GEMM of less than one wave of tiles
+// has its K blocks split evenly over the SMs instead (stream-K).  Splitting
+// only the last partial wave of a larger GEMM is supported by the kernel
+// (whole_tiles > 0) but not planned: the promotion epilogue makes each
+// partial tile's fix-up cost more than the wave tail it removes (config 1,
+// 224 tiles: 46.1 us whole, 51.9 us with the 76-tile tail split).
 static F8Split fp8_split_plan(size_t m, size_t n_rows, size_t k) {
   const size_t tiles = ((m + kF8Tile - 1) / kF8Tile) * ((n_rows + kF8BN - 1) / kF8BN);
-  const size_t kb = (k + kF8Tile - 1) / kF8Tile, total = tiles * kb;
+  const size_t kb = (k + kF8Tile - 1) / kF8Tile;
+  const size_t sms = (size_t)std::max(1, sm_count());
   F8Split sp{};
-  sp.ctas = (int)std::max<size_t>(1, std::min<size_t>((size_t)std::max(1, sm_count()), total));
-  const size_t range = std::max<size_t>(1, total / sp.ctas);  // shortest CTA range
+  sp.ctas = (int)std::max<size_t>(1, std::min(tiles, sms));
+  sp.whole = (int)tiles;
+  const size_t whole = tiles >= sms ? (tiles / sms) * sms : 0;
+  const size_t tail = tiles - whole, tail_kb = tail * kb;
+  if (whole || tail_kb < 2) return sp;
+  const size_t ctas = std::min(sms, tail_kb);
+  const size_t range = tail_kb / ctas;  // shortest CTA range
+  sp.ctas = (int)ctas;
+  sp.whole = (int)whole;
+  sp.tail_kb = (long long)tail_kb;
+  sp.split = true;
   sp.max_seg = (int)std::min<size_t>((kb + range - 1) / range + 1, kb);
-  sp.partial_bytes = tiles * (size_t)sp.max_seg * kF8Tile * kF8BN * sizeof(float);
-  sp.counter_bytes = tiles * kF8EpiWarps * sizeof(int);
+  sp.partial_bytes = tail * (size_t)sp.max_seg * kF8Tile * kF8BN * sizeof(float);
+  sp.counter_bytes = tail * kF8EpiWarps * sizeof(int);
   return sp;
 }
 
@@ -729,20 +753,18 @@ static int fp8_gemm_launch(fpb_fp8_matrix *w, const uint8_t *a_bits, const float
   p.n_experts = tile_experts ? (int)(w->rows / n_rows) : 0;
   p.m_tiles = (int)((m + kF8Tile - 1) / kF8Tile);
   p.tiles = p.m_tiles * (int)((n_rows + kF8BN - 1) / kF8BN);
-  p.total_kb = (long long)p.tiles * p.kb_count;
   // Whole tiles, one persistent CTA per SM (grouped: one CTA per tile, so
   // that a CTA whose row tile is dead can leave at once).
   p.ctas = tile_experts ? p.tiles : std::min(p.tiles, std::max(1, sm_count()));
+  p.whole_tiles = p.tiles;
+  p.total_kb = 0;
   p.max_seg = 1;
   const F8Split sp = fp8_split_plan(m, n_rows, w->cols);
-  // Split only a GEMM of less than one wave of tiles: the epilogue promotes
-  // every K block, so a tile boundary inside a CTA's range (store, or partial
-  // sums and their fix-up) stalls the tensor cores for as long as the stores
-  // take; with 224 tiles on 148 SMs (config 1) that cost 19 us more than the
-  // 1.5-wave tail it removes (49 -> 69 us per launch).
-  if (!tile_experts && split_ws && split_bytes >= sp.partial_bytes + sp.counter_bytes && sp.ctas < p.total_kb &&
-      p.tiles < sm_count()) {
+  // With a workspace, the last partial wave of tiles is split along K.
+  if (!tile_experts && sp.split && split_ws && split_bytes >= sp.partial_bytes + sp.counter_bytes) {
     p.ctas = sp.ctas;
+    p.whole_tiles = sp.whole;
+    p.total_kb = sp.tail_kb;
     p.max_seg = sp.max_seg;
     p.partials = static_cast<float *>(split_ws);
     p.tile_counters = reinterpret_cast<int *>(static_cast<uint8_t *>(split_ws) + sp.partial_bytes);

@@ -123,6 +123,31 @@ def test_fp8_gemm_config1_full_size(F, torch):
            out_bf16=True)
 
 
+@pytest.mark.parametrize("out", ["f32", "bf16"])
+def test_fp8_gemm_persistent_ragged(F, torch, out):
+    """168 tiles of 128 x 256 on 148 persistent CTAs (20 run a second tile),
+    a ragged last row tile, TMA-stored output.  Checked against the oracle on
+    a row sample, and bit for bit between two runs."""
+    m, n, k = 300, 14336, 4096
+    w = F.synth_normal((n, k), seed=5, stream_id=1, std=0.02)
+    W = F.Fp8Matrix.quantize(w, F.Fp8Scaling(128, 128))
+    h = W.to_host()
+    x = F.synth_normal((m, k), seed=6, stream_id=2, dtype=torch.bfloat16)
+    ydt = torch.bfloat16 if out == "bf16" else torch.float32
+    ys = []
+    for _ in range(2):
+        y = torch.full((m, n), float("nan"), dtype=ydt, device="cuda")
+        F.fp8_gemm(W, x, y, F.GemmTile(m, 128, 32)).submit(F.Eager())
+        assert F.device_error() == 0
+        ys.append(y)
+    assert torch.equal(ys[0].view(torch.int16 if out == "bf16" else torch.int32),
+                       ys[1].view(torch.int16 if out == "bf16" else torch.int32))
+    rows = np.concatenate([np.arange(0, m, 9), np.arange(m - 4, m)])
+    a_bits, a_s = O.fp8_quantize(x.float().cpu().numpy())
+    _check(ys[0].float().cpu().numpy()[rows], a_bits[rows], a_s[rows], h.bits.reshape(n, k), h.scales, 128, 128, k,
+           out_bf16=out == "bf16")
+
+
 def test_fp8_gemm_view_and_errors(F, torch):
     n, k = 1024, 512
     w = F.synth_normal((n, k), seed=3, stream_id=1, std=0.02)

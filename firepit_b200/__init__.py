@@ -23,5 +23,8 @@ from .gemm import (DEFAULT_GEMM_TILE, DEFAULT_GROUPED_GEMM_TILE, GemmTile, Nvfp4
                    nvfp4_grouped_gemm_view, quantize_act, rows_quantize)
 from .fp8 import (Fp8Gemm, Fp8GroupedGemmView, Fp8Matrix, Fp8Scaling, HostFp8Matrix, fp8_gemm, fp8_gemm_view,
                   fp8_grouped_gemm_q, fp8_grouped_gemm_view, quantize_fp8)
+from .checkpoint import (Checkpoint, CheckpointError, Fp8Config, HostBf16Weight, ModelOptConfig, Quantization,
+                         SafetensorsFile, WeightFormat, check_companions, load_experts, load_weight, stack_weights,
+                         verify_formats)
 
 __version__ = _native.lib.fpb_version().decode()

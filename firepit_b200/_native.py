@@ -21,6 +21,7 @@ FPB_ERR_UNSUPPORTED = 5
 FPB_ERR_SELECTION = 6
 FPB_ERR_WORKSPACE = 7
 FPB_ERR_NO_DEVICE = 8
+FPB_ERR_IO = 9
 
 FPB_F32 = 0
 FPB_BF16 = 1
@@ -61,6 +62,16 @@ f32p = C.POINTER(C.c_float)
 
 # name -> (restype, argtypes)
 SIGNATURES: dict[str, tuple] = {
+    "fpb_safetensors_open": (i32, [C.c_char_p, C.POINTER(vp)]),
+    "fpb_safetensors_close": (None, [vp]),
+    "fpb_safetensors_count": (sz, [vp]),
+    "fpb_safetensors_name": (C.c_char_p, [vp, sz]),
+    "fpb_safetensors_has": (i32, [vp, C.c_char_p]),
+    "fpb_safetensors_metadata": (C.c_char_p, [vp, C.c_char_p]),
+    "fpb_safetensors_dtype_name": (C.c_char_p, [i32]),
+    "fpb_safetensors_info": (i32, [vp, C.c_char_p, C.POINTER(i32), C.POINTER(C.c_int64), i32, C.POINTER(i32),
+                                   C.POINTER(sz)]),
+    "fpb_safetensors_read": (i32, [vp, C.c_char_p, i32, sz, vp, sz]),
     "fpb_version": (C.c_char_p, []),
     "fpb_status_string": (C.c_char_p, [i32]),
     "fpb_last_error": (C.c_char_p, []),

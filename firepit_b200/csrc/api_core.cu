@@ -173,6 +173,7 @@ const char *fpb_status_string(int s) {
     case FPB_ERR_SELECTION: return "invalid expert selection";
     case FPB_ERR_WORKSPACE: return "workspace too small";
     case FPB_ERR_NO_DEVICE: return "no CUDA device";
+    case FPB_ERR_IO: return "I/O error";
     default: return "unknown status";
   }
 }

@@ -41,7 +41,8 @@ enum {
   FPB_ERR_UNSUPPORTED = 5,      /* shape outside this build's kernels       */
   FPB_ERR_SELECTION = 6,        /* ExpertSelectionError (moe.rs:262-269)    */
   FPB_ERR_WORKSPACE = 7,        /* workspace too small                      */
-  FPB_ERR_NO_DEVICE = 8         /* no CUDA device visible                   */
+  FPB_ERR_NO_DEVICE = 8,        /* no CUDA device visible                   */
+  FPB_ERR_IO = 9                /* a checkpoint file could not be read      */
 };
 
 enum { FPB_F32 = 0, FPB_BF16 = 1 };
@@ -404,6 +405,45 @@ int fpb_prefill_layout_host(const int32_t *indices, const float *weights, size_t
                             size_t experts, size_t top_k, size_t tile_rows, int32_t *token_rows,
                             size_t token_rows_cap, size_t *padded_rows, int32_t *tile_experts,
                             size_t tile_cap, size_t *n_tiles, int32_t *inverse, size_t *ranges);
+
+/* ---- checkpoint files (crates/firepit/src/checkpoint.rs) -------------------
+ * Safetensors reader: the on-disk format the reference loads NVFP4 / FP8
+ * weights from (ModelOpt NVFP4: U8 [N, K/2] codes low nibble first, F8_E4M3
+ * [N, K/16] scales, F32 scalar weight_scale_2; Qwen FP8: F8_E4M3 [N, K]
+ * with BF16 [N/bn, K/bk] weight_scale_inv).  Host only; reads with pread.
+ * The handle is read-only after open and may be shared between threads. */
+typedef struct fpb_safetensors fpb_safetensors;
+
+/* Stored dtypes (safetensors' Dtype names). */
+enum {
+  FPB_ST_BOOL = 0, FPB_ST_U8 = 1, FPB_ST_I8 = 2, FPB_ST_F8_E5M2 = 3, FPB_ST_F8_E4M3 = 4,
+  FPB_ST_I16 = 5, FPB_ST_U16 = 6, FPB_ST_F16 = 7, FPB_ST_BF16 = 8, FPB_ST_I32 = 9,
+  FPB_ST_U32 = 10, FPB_ST_F32 = 11, FPB_ST_F64 = 12, FPB_ST_I64 = 13, FPB_ST_U64 = 14
+};
+
+/* SafetensorsFile::open (checkpoint.rs:63-76): parses and validates the
+ * header (every tensor's byte range against its dtype, shape and the file
+ * size).  FPB_ERR_IO if the file cannot be opened, FPB_ERR_FORMAT if the
+ * header is malformed. */
+int fpb_safetensors_open(const char *path, fpb_safetensors **out);
+void fpb_safetensors_close(fpb_safetensors *f);
+/* Tensor names in data-offset order. */
+size_t fpb_safetensors_count(const fpb_safetensors *f);
+const char *fpb_safetensors_name(const fpb_safetensors *f, size_t i);
+/* SafetensorsFile::has_tensor (checkpoint.rs:86-88): 1 or 0. */
+int fpb_safetensors_has(const fpb_safetensors *f, const char *name);
+/* SafetensorsFile::metadata (checkpoint.rs:78-84): NULL when absent. */
+const char *fpb_safetensors_metadata(const fpb_safetensors *f, const char *key);
+const char *fpb_safetensors_dtype_name(int dtype);
+/* TensorInfo (checkpoint.rs:187-191): dtype code, shape (up to max_dims),
+ * number of dimensions and byte size.  FPB_ERR_FORMAT "unknown tensor". */
+int fpb_safetensors_info(const fpb_safetensors *f, const char *name, int *dtype, int64_t *shape,
+                         int max_dims, int *ndim, size_t *nbytes);
+/* SafetensorsFile::bytes (checkpoint.rs:158-167): `bytes` raw bytes of the
+ * tensor from byte `byte_begin` of its range into host memory, after checking
+ * that it is stored as `dtype` (FPB_ERR_FORMAT "expected X, got Y"). */
+int fpb_safetensors_read(const fpb_safetensors *f, const char *name, int dtype, size_t byte_begin, void *dst,
+                         size_t bytes);
 
 #ifdef __cplusplus
 }

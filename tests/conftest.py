@@ -10,6 +10,9 @@ sys.path.insert(0, str(ROOT / "tests"))
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200, sm_100a)")
+    # Temporary files (checkpoint fixtures) stay inside the repository tree.
+    if not config.option.basetemp:
+        config.option.basetemp = str(ROOT / ".pytest_tmp")
 
 
 def pytest_collection_modifyitems(config, items):

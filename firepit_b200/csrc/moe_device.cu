@@ -241,6 +241,98 @@ __global__ void __launch_bounds__(kLayoutWarpsPerCta * 32) moe_layout_place_kern
   }
 }
 
+// Single-CTA layout for launches of at most kLayoutChunk routes (decode-size
+// batches): the fills, the per-warp counts, both scans and the stable
+// placement of the three kernels above in one launch (one graph node instead
+// of three memsets and three kernels).  Same outputs and device errors.
+constexpr int kLayoutSmallThreads = 1024;
+__global__ void __launch_bounds__(kLayoutSmallThreads) moe_layout_small_kernel(
+    const int32_t *ids, int n, int kk, int width, int tokens, int experts, int tile_rows, int cap,
+    int32_t *token_rows, int32_t *tile_experts, int32_t *inverse, int64_t *ranges, int32_t *padded_out, int *error) {
+  extern __shared__ int sm_small[];
+  constexpr int kWarps = kLayoutSmallThreads / 32;
+  int *wcount = sm_small;                     // [kWarps][experts]
+  int *totals = sm_small + kWarps * experts;  // [experts]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // fills (token_rows = -1, tile_experts = -1, inverse = 0) and zeroed counts
+  for (int i = tid; i < cap; i += blockDim.x) token_rows[i] = -1;
+  for (int i = tid; i < cap / tile_rows; i += blockDim.x) tile_experts[i] = -1;
+  for (int i = tid; i < tokens * width; i += blockDim.x) inverse[i] = 0;
+  for (int i = tid; i < kWarps * experts; i += blockDim.x) wcount[i] = 0;
+  __syncthreads();
+  // each warp counts a contiguous segment of the routes
+  const int span = (n + kWarps - 1) / kWarps;
+  const int w_lo = min(n, warp * span), w_hi = min(n, w_lo + span);
+  for (int b = w_lo; b < w_hi; b += 32) {
+    const int e = b + lane;
+    const int id = e < w_hi ? layout_id(ids, e, kk, width, experts) : -1;
+    if (e < w_hi && id < 0 && error) atomicCAS(error, 0, 401);
+    const unsigned grp = __match_any_sync(0xffffffffu, id);
+    if (id >= 0 && lane == __ffs(grp) - 1) wcount[warp * experts + id] += __popc(grp);
+    __syncwarp();
+  }
+  __syncthreads();
+  // per expert: each warp's first row within the expert, and the total
+  for (int x = tid; x < experts; x += blockDim.x) {
+    int run = 0;
+    for (int w = 0; w < kWarps; ++w) {
+      const int c = wcount[w * experts + x];
+      wcount[w * experts + x] = run;
+      run += c;
+    }
+    totals[x] = run;
+  }
+  __syncthreads();
+  // padded expert ranges (exclusive over experts), the row count
+  if (warp == 0) {
+    int carry = 0;
+    for (int base = 0; base < experts; base += 32) {
+      const int x = base + lane;
+      const int total = x < experts ? totals[x] : 0;
+      const int padded = (total + tile_rows - 1) / tile_rows * tile_rows;
+      int incl = padded;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+      }
+      if (x < experts) {
+        ranges[2 * x] = carry + incl - padded;
+        ranges[2 * x + 1] = total;
+      }
+      carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) {
+      *padded_out = carry;
+      if (carry > cap && error) atomicCAS(error, 0, 402);
+    }
+  }
+  __syncthreads();
+  for (int x = tid; x < experts; x += blockDim.x) {
+    const int start = (int)ranges[2 * x], count = totals[x];
+    const int padded = (count + tile_rows - 1) / tile_rows * tile_rows;
+    for (int t = start / tile_rows; t < (start + padded) / tile_rows && t < cap / tile_rows; ++t) tile_experts[t] = x;
+    for (int w = 0; w < kWarps; ++w) wcount[w * experts + x] += start;
+  }
+  __syncthreads();
+  // stable placement: (token, slot) order within each expert
+  for (int b = w_lo; b < w_hi; b += 32) {
+    const int e = b + lane;
+    const int id = e < w_hi ? layout_id(ids, e, kk, width, experts) : -1;
+    const unsigned grp = __match_any_sync(0xffffffffu, id);
+    const int rank = __popc(grp & ((1u << lane) - 1));
+    int pos = -1;
+    if (id >= 0) pos = wcount[warp * experts + id] + rank;
+    __syncwarp();
+    if (id >= 0 && lane == __ffs(grp) - 1) wcount[warp * experts + id] += __popc(grp);
+    if (id >= 0 && pos < cap) {
+      token_rows[pos] = e / kk;
+      inverse[(long long)(e / kk) * width + e % kk] = pos;
+    }
+    __syncwarp();
+  }
+}
+
 // ---- row loaders for the NVFP4 activation encode ----------------------------------------
 // 16 consecutive values as f32 with 16-byte loads (p 16-byte aligned: rows of
 // a multiple of 32 columns, groups of 16).
@@ -322,6 +414,33 @@ __device__ __forceinline__ size_t valid_rows(size_t rows, const int32_t *valid) 
   return valid ? min(rows, (size_t)max(*valid, 0)) : rows;
 }
 
+// Calls f(r, skip_r) for every row r < n of this warp's grid-stride share
+// (rows w, w + W, w + 2W, ... for warp w of W) whose skip entry is >= 0 (every
+// row when skip is null; skip_r is then 0).  With skip, the entries of 32 of
+// the warp's rows are read in one load per lane and only the live rows are
+// visited, so a sparse layout (decode-size batches, where most rows are
+// padding) costs one load latency per 32 rows instead of one per row.
+template <class Fn>
+__device__ __forceinline__ void for_live_rows(size_t n, const int32_t *skip, Fn &&f) {
+  const int lane = threadIdx.x & 31;
+  const size_t warps = (size_t)gridDim.x * (blockDim.x / 32);
+  const size_t w = (size_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  if (!skip) {
+    for (size_t r = w; r < n; r += warps) f(r, 0);
+    return;
+  }
+  for (size_t base = w; base < n; base += 32 * warps) {
+    const size_t r_l = base + (size_t)lane * warps;
+    const int s_l = r_l < n ? skip[r_l] : -1;
+    unsigned live = __ballot_sync(0xffffffffu, s_l >= 0);
+    while (live) {
+      const int i = __ffs(live) - 1;
+      live &= live - 1;
+      f(base + (size_t)i * warps, __shfl_sync(0xffffffffu, s_l, i));
+    }
+  }
+}
+
 // Both row kernels: one warp per row (grid-stride over rows), lane l encodes
 // the 16-column groups l, l + 32, ... of the row.  skip (nullable): rows r
 // with skip[r] < 0 (a layout's padding rows) are neither read nor written.
@@ -331,8 +450,8 @@ __global__ void rows_amax_kernel(Rows rows_src, size_t rows, const int32_t *vali
   const int gpr = (int)(cols / 16), lane = threadIdx.x & 31;
   const size_t n = valid_rows(rows, valid), warps = (size_t)gridDim.x * (blockDim.x / 32);
   uint32_t m = 0;
-  for (size_t r = (size_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; r < n; r += warps) {
-    if (skip && skip[r] < 0) continue;
+  (void)warps;
+  for_live_rows(n, skip, [&](size_t r, int) {
     const auto src = rows_src.row(r);
     for (int g = lane; g < gpr; g += 32) {
       float v[16];
@@ -340,7 +459,7 @@ __global__ void rows_amax_kernel(Rows rows_src, size_t rows, const int32_t *vali
 #pragma unroll
       for (int i = 0; i < 16; ++i) m = max(m, __float_as_uint(v[i]) & 0x7fffffffu);
     }
-  }
+  });
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
   if (lane == 0 && m) atomicMax(amax_bits, m);
@@ -354,8 +473,8 @@ __global__ void rows_encode_kernel(Rows rows_src, size_t rows, const int32_t *va
   if (blockIdx.x == 0 && threadIdx.x == 0) *global_out = global;
   const int gpr = (int)(cols / 16), lane = threadIdx.x & 31;
   const size_t n = valid_rows(rows, valid), warps = (size_t)gridDim.x * (blockDim.x / 32);
-  for (size_t r = (size_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; r < n; r += warps) {
-    if (skip && skip[r] < 0) continue;
+  (void)warps;
+  for_live_rows(n, skip, [&](size_t r, int) {
     const auto src = rows_src.row(r);
     uint8_t *prow = packed + r * (cols / 2);
     uint8_t *srow = sf_tiled + (kRowMajorSf ? r * gpr : sf_tiled_row_offset(r, cols));
@@ -364,7 +483,7 @@ __global__ void rows_encode_kernel(Rows rows_src, size_t rows, const int32_t *va
       rows_src.load16(src, g, v);
       encode_group16(v, global, prow + g * 8, srow + (kRowMajorSf ? (uint32_t)g : sf_tiled_group_offset(g)));
     }
-  }
+  });
 }
 
 // Gathered NVFP4 rows from token rows quantized once (codes [tokens, cols/2],
@@ -378,10 +497,9 @@ __global__ void gather_codes_kernel(const uint8_t *tok_packed, const uint8_t *to
                                     const int32_t *skip, size_t cols, uint8_t *packed, uint8_t *sf_tiled) {
   const int lane = threadIdx.x & 31;
   const int code_vecs = (int)(cols / 32), sf_words = (int)(cols / 64);
-  const size_t n = valid_rows(rows, valid), warps = (size_t)gridDim.x * (blockDim.x / 32);
-  for (size_t r = (size_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; r < n; r += warps) {
+  const size_t n = valid_rows(rows, valid);
+  for_live_rows(n, skip, [&](size_t r, int) {
     const int t = token_rows[r];
-    if (skip && t < 0) continue;
     const bool zero = t < 0 || t >= tokens;
     const uint4 *csrc = reinterpret_cast<const uint4 *>(tok_packed + (size_t)max(t, 0) * (cols / 2));
     uint4 *cdst = reinterpret_cast<uint4 *>(packed + r * (cols / 2));
@@ -390,7 +508,7 @@ __global__ void gather_codes_kernel(const uint8_t *tok_packed, const uint8_t *to
     uint8_t *srow = sf_tiled + sf_tiled_row_offset(r, cols);
     for (int j = lane; j < sf_words; j += 32)
       *reinterpret_cast<uint32_t *>(srow + (size_t)j * kSfChunk) = zero ? 0u : ssrc[j];
-  }
+  });
 }
 
 // Plain gather (gather_prefill_view, moe.rs:71-89, 673-733): f32 or bf16 out.
@@ -631,6 +749,26 @@ extern "C" int fpb_moe_layout(const int32_t *ids, size_t tokens, size_t width, s
   const int groups = (n + kLayoutChunk - 1) / kLayoutChunk;
   int *cnt = static_cast<int *>(scratch);
   int *err = device_error_ptr();
+  const size_t small_smem = (size_t)(kLayoutSmallThreads / 32 + 1) * experts * sizeof(int);
+  if (groups == 1 && small_smem <= 200 * 1024) {
+    static std::mutex mu_small;
+    static std::vector<int> done_small;
+    {
+      int dev = 0;
+      cudaGetDevice(&dev);
+      std::lock_guard<std::mutex> lock(mu_small);
+      if (std::find(done_small.begin(), done_small.end(), dev) == done_small.end()) {
+        FPB_CUDA_TRY(cudaFuncSetAttribute(moe_layout_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          200 * 1024));
+        done_small.push_back(dev);
+      }
+    }
+    moe_layout_small_kernel<<<1, kLayoutSmallThreads, small_smem, s>>>(
+        ids, n, (int)slots, (int)width, (int)tokens, (int)experts, (int)tile_rows, (int)cap, token_rows,
+        tile_experts, inverse, reinterpret_cast<int64_t *>(ranges), padded_rows, err);
+    FPB_LAUNCH_CHECK("moe_layout_small_kernel");
+    return FPB_OK;
+  }
   FPB_CUDA_TRY(cudaMemsetAsync(token_rows, 0xff, cap * sizeof(int32_t), s));
   FPB_CUDA_TRY(cudaMemsetAsync(tile_experts, 0xff, cap / tile_rows * sizeof(int32_t), s));
   FPB_CUDA_TRY(cudaMemsetAsync(inverse, 0, tokens * width * sizeof(int32_t), s));

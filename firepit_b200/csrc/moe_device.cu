@@ -448,9 +448,8 @@ template <class Rows>
 __global__ void rows_amax_kernel(Rows rows_src, size_t rows, const int32_t *valid, const int32_t *skip, size_t cols,
                                  uint32_t *amax_bits) {
   const int gpr = (int)(cols / 16), lane = threadIdx.x & 31;
-  const size_t n = valid_rows(rows, valid), warps = (size_t)gridDim.x * (blockDim.x / 32);
+  const size_t n = valid_rows(rows, valid);
   uint32_t m = 0;
-  (void)warps;
   for_live_rows(n, skip, [&](size_t r, int) {
     const auto src = rows_src.row(r);
     for (int g = lane; g < gpr; g += 32) {
@@ -472,8 +471,7 @@ __global__ void rows_encode_kernel(Rows rows_src, size_t rows, const int32_t *va
   const float global = __fdiv_rn(__uint_as_float(*amax_bits), 2688.0f);
   if (blockIdx.x == 0 && threadIdx.x == 0) *global_out = global;
   const int gpr = (int)(cols / 16), lane = threadIdx.x & 31;
-  const size_t n = valid_rows(rows, valid), warps = (size_t)gridDim.x * (blockDim.x / 32);
-  (void)warps;
+  const size_t n = valid_rows(rows, valid);
   for_live_rows(n, skip, [&](size_t r, int) {
     const auto src = rows_src.row(r);
     uint8_t *prow = packed + r * (cols / 2);

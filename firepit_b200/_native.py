@@ -93,6 +93,8 @@ SIGNATURES: dict[str, tuple] = {
     "fpb_nvfp4_dequantize": (i32, [vp, vp, vp]),
     "fpb_nvfp4_gemv": (i32, [vp, sz, sz, vp, i32, vp, i32, i32, vp]),
     "fpb_nvfp4_expert_gemv": (i32, [vp, vp, i32, vp, i32, sz, i32, vp, i32, vp]),
+    "fpb_fp8_gemv": (i32, [vp, sz, sz, vp, i32, vp, i32, i32, vp]),
+    "fpb_fp8_expert_gemv": (i32, [vp, vp, i32, vp, i32, sz, i32, vp, i32, vp]),
     "fpb_nvfp4_act_sf_bytes": (sz, [sz, sz]),
     "fpb_nvfp4_gemm_workspace_bytes": (sz, [sz, sz]),
     "fpb_nvfp4_quantize_act": (i32, [vp, i32, sz, sz, vp, vp, vp, vp, vp]),

@@ -40,20 +40,10 @@
 #include <vector>
 
 #include "common.cuh"
+#include "fp8_matrix.cuh"
 #include "sm100.cuh"
 #include "tma_host.cuh"
 
-// Device-side FP8 weight matrix (Fp8Matrix, weights/fp8.rs:14-19).
-struct fpb_fp8_matrix {
-  size_t rows = 0, cols = 0;
-  int block_n = 0, block_k = 0;  // 0, 0: one scale per row
-  int device = 0;
-  uint8_t *bits = nullptr;
-  float *scales = nullptr;
-  size_t n_scales = 0;
-  alignas(64) unsigned char tmap[128];
-  bool tmap_valid = false;
-};
 
 namespace fpb {
 

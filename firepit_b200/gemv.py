@@ -67,16 +67,30 @@ def _dtype_code(t) -> int:
     raise TypeError(f"unsupported dtype {t.dtype}")
 
 
-class Gemv:
-    """gemv/mod.rs:66-123 for ``Weight::Nvfp4``."""
+def _is_fp8(weight) -> bool:
+    return getattr(weight, "scaling", None) is not None
 
-    def __init__(self, weight: Nvfp4Matrix, x, y, tile: GemvTile, rows: range | None = None):
+
+def _check_fp8_tile(weight, tile: GemvTile) -> None:
+    """gemv/fp8.rs:205-229: block scales must be whole tiles."""
+    sc = weight.scaling
+    if not sc.is_rows and (sc.block_n % tile.rows != 0 or sc.block_k % (tile.blocks * Q8_BLOCK) != 0):
+        raise ShapeError(f"GEMV tile {tile} does not divide the FP8 blocks {sc.block_n}x{sc.block_k}")
+
+
+class Gemv:
+    """gemv/mod.rs:66-123: the weight-format dispatch, ``Weight::Nvfp4``
+    (gemv/nvfp4.rs) or ``Weight::Fp8`` (gemv/fp8.rs:186-246)."""
+
+    def __init__(self, weight, x, y, tile: GemvTile, rows: range | None = None):
         self.weight, self.x, self.y, self.tile = weight, x, y, tile
         self.rows = rows if rows is not None else range(0, weight.rows)
         n = len(self.rows)
         batch = x.shape[0]
         if batch <= 0 or not tile.fits(n, weight.cols):
             raise ShapeError(f"GEMV tile {tile} does not fit {n}x{weight.cols}")
+        if _is_fp8(weight):
+            _check_fp8_tile(weight, tile)
         if x.numel() != batch * weight.cols:
             raise ShapeError(f"x has {x.numel()} elements, expected {batch}x{weight.cols}")
         if y.numel() != batch * n:
@@ -88,30 +102,37 @@ class Gemv:
         sink = sink or Eager()
         batch = self.x.shape[0]
 
+        fn = "fpb_fp8_gemv" if _is_fp8(self.weight) else "fpb_nvfp4_gemv"
+
         def launch(stream):
-            N.call("fpb_nvfp4_gemv", self.weight.handle, self.rows.start, self.rows.stop,
+            N.call(fn, self.weight.handle, self.rows.start, self.rows.stop,
                    self.x.data_ptr(), _dtype_code(self.x), self.y.data_ptr(), _dtype_code(self.y),
                    batch, stream)
 
         sink.run("gemv", launch)
 
 
-def gemv(weight: Nvfp4Matrix, x, y, tile: GemvTile = DEFAULT_GEMV_TILE, rows: range | None = None) -> Gemv:
+def gemv(weight, x, y, tile: GemvTile = DEFAULT_GEMV_TILE, rows: range | None = None) -> Gemv:
     """gemv/mod.rs:74-87.  x: [batch, cols] (the reference's [B, K/32, 32]
     is the same memory), y: [batch, rows]."""
     return Gemv(weight, x, y, tile, rows)
 
 
 class ExpertGemvView:
-    """gemv/mod.rs:126-206 for ``Weight::Nvfp4``."""
+    """gemv/mod.rs:126-206 for ``Weight::Nvfp4`` or ``Weight::Fp8``
+    (gemv/fp8.rs:248-281)."""
 
-    def __init__(self, weight: Nvfp4Matrix, x, selection, y, rows_per_expert: int, input_stride: int,
+    def __init__(self, weight, x, selection, y, rows_per_expert: int, input_stride: int,
                  tile: GemvTile):
         dims = selection.dims
         if weight.rows != dims.experts * rows_per_expert:
             raise ShapeError("expert GEMV: weight rows != experts * rows_per_expert")
         if not tile.fits(rows_per_expert, weight.cols):
             raise ShapeError(f"GEMV tile {tile} does not fit {rows_per_expert}x{weight.cols}")
+        if _is_fp8(weight):
+            _check_fp8_tile(weight, tile)
+            if not weight.scaling.is_rows and rows_per_expert % weight.scaling.block_n != 0:
+                raise ShapeError("expert GEMV: rows per expert not a multiple of the FP8 block rows")
         self.weight, self.x, self.selection, self.y = weight, x, selection, y
         self.rows_per_expert, self.input_stride = rows_per_expert, input_stride
         self.slots = selection.slots
@@ -119,15 +140,17 @@ class ExpertGemvView:
     def submit(self, sink: Sink | None = None) -> None:
         sink = sink or Eager()
 
+        fn = "fpb_fp8_expert_gemv" if _is_fp8(self.weight) else "fpb_nvfp4_expert_gemv"
+
         def launch(stream):
-            N.call("fpb_nvfp4_expert_gemv", self.weight.handle, self.x.data_ptr(), _dtype_code(self.x),
+            N.call(fn, self.weight.handle, self.x.data_ptr(), _dtype_code(self.x),
                    self.selection.indices.data_ptr(), self.slots, self.rows_per_expert, self.input_stride,
                    self.y.data_ptr(), _dtype_code(self.y), stream)
 
         sink.run("expert_gemv", launch)
 
 
-def expert_gemv_weight_view(weight: Nvfp4Matrix, x, selection, y, rows_per_expert: int, input_stride: int,
+def expert_gemv_weight_view(weight, x, selection, y, rows_per_expert: int, input_stride: int,
                             tile: GemvTile = DEFAULT_GEMV_TILE) -> ExpertGemvView:
     """gemv/mod.rs:137-156."""
     return ExpertGemvView(weight, x, selection, y, rows_per_expert, input_stride, tile)

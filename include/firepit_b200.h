@@ -169,6 +169,27 @@ int fpb_nvfp4_expert_gemv(const fpb_nvfp4_matrix *w, const void *x, int x_dtype,
                           size_t rows_per_expert, int input_stride, void *y,
                           int y_dtype, void *stream);
 
+/* gemv(&Weight::Fp8, x, y, tile).submit(sink) (gemv/mod.rs:74-123 ->
+ * gemv/fp8.rs:186-246, kernels dense_fp8_kernel :13-54 and
+ * dense_fp8_rows_kernel :108-132), over an FP8 matrix handle (declared
+ * below with the FP8 GEMM).  Block scales:
+ *   y[b, r] = sum_kb s[r / block_n, kb] * sum_{k in kb} w[r, k] * x[b, k];
+ * row scales: y[b, r] = s[r] * sum_k w[r, k] * x[b, k].  Rows [row_begin,
+ * row_end) (row_end == 0: all), x [batch, cols], y [batch, row_end -
+ * row_begin], contiguous, 1 <= batch <= 16; cols % 32 == 0 (the reference's
+ * GemvTile::fits), block_k % 16 == 0. */
+struct fpb_fp8_matrix;
+int fpb_fp8_gemv(const struct fpb_fp8_matrix *w, size_t row_begin, size_t row_end, const void *x, int x_dtype,
+                 void *y, int y_dtype, int batch, void *stream);
+/* expert_gemv_weight_view(&Weight::Fp8, ...) (gemv/mod.rs:137-206 ->
+ * gemv/fp8.rs:248-281, kernels expert_fp8_kernel :56-106 and
+ * expert_fp8_rows_kernel :134-160): for slot s, y[s, r] = the GEMV of rows
+ * expert_ids[s] * rows_per_expert + r with x row s * input_stride.  Block
+ * scales need rows_per_expert % block_n == 0 (gemv/fp8.rs:264).  An id
+ * outside [0, rows / rows_per_expert) gives a zero row. */
+int fpb_fp8_expert_gemv(const struct fpb_fp8_matrix *w, const void *x, int x_dtype, const int32_t *expert_ids,
+                        int slots, size_t rows_per_expert, int input_stride, void *y, int y_dtype, void *stream);
+
 /* ---- prefill NVFP4 GEMM (tcgen05, NVFP4 x NVFP4 -> f32 accumulate) --------
  * Replaces nvfp4_gemm / nvfp4_gemm_view (gemm/nvfp4.rs:119-207, kernel
  * :12-55).  The reference keeps activations in f32 (bf16 hi/lo MMAs); this

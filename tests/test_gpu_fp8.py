@@ -193,3 +193,98 @@ def test_fp8_grouped_gemm(F, torch, block):
         ws_e = ws[e * rpe:(e + 1) * rpe] if block == (0, 0) else ws[e * rpe // 128:(e + 1) * rpe // 128].reshape(-1)
         _check(got[sl], a_bits[sl], a_s[sl], wb[e * rpe:(e + 1) * rpe], ws_e, *block, k)
     assert np.all(got[layout.token_rows < 0] == 0.0)
+
+
+# ---- decode GEMV on FP8 weights (gemv/fp8.rs) -----------------------------------------
+def _fp8_gemv_expected(h, rows, cols, block, x):
+    """f64 product of the dequantized weights (e4m3 x scale in f32, the
+    reference's dequant) with x, and the magnitudes |W| |x| for the bound."""
+    if block == (0, 0):
+        wd = O.fp8_dequantize(h.bits.reshape(rows, cols), h.scales, 0, 0)
+    else:
+        wd = O.fp8_dequantize(h.bits.reshape(rows, cols), h.scales.reshape(rows // block[0], cols // block[1]),
+                              *block)
+    wd = np.asarray(wd, np.float64).reshape(rows, cols)
+    return x.astype(np.float64) @ wd.T, np.abs(x.astype(np.float64)) @ np.abs(wd).T
+
+
+@pytest.mark.parametrize("rows,cols,block", [(4096, 4096, (128, 128)), (1024, 2048, (0, 0)),
+                                             (512, 1536, (256, 128)), (96, 96 * 4, (0, 0))])
+@pytest.mark.parametrize("batch", [1, 3, 8, 16])
+@pytest.mark.parametrize("xdt", ["bf16", "f32"])
+def test_fp8_gemv_dense(F, torch, rows, cols, block, batch, xdt):
+    """gemv(&Weight::Fp8, ...) (gemv/fp8.rs:186-246) against the f64 product
+    of the dequantized weights: the inner-product error bound and the
+    relative Frobenius tolerance."""
+    w = F.synth_normal((rows, cols), seed=rows + cols, stream_id=1, std=0.02)
+    W = F.Fp8Matrix.quantize(w, F.Fp8Scaling(*block))
+    h = W.to_host()
+    x = O.synth_normal(batch * cols, seed=batch, stream=2).reshape(batch, cols).astype(np.float32)
+    if xdt == "bf16":
+        x = O.bf16_to_f32(O.bf16_bits(x)).reshape(batch, cols)
+    xt = torch.from_numpy(x).cuda().to(torch.bfloat16 if xdt == "bf16" else torch.float32)
+    y = torch.full((batch, rows), float("nan"), device="cuda")
+    tile = F.GemvTile(16 if rows % 16 == 0 else 8, 4 if cols % 128 == 0 else 1)
+    F.gemv(W, xt, y, tile).submit(F.Eager())
+    e, mag = _fp8_gemv_expected(h, rows, cols, block, x)
+    got = y.cpu().numpy()
+    assert O.rel_frobenius(got, e) <= REL_FROB_TOL
+    assert O.inner_product_excess(got, e, mag, cols + 2) <= 1.0
+
+
+def test_fp8_gemv_row_range_and_bf16_out(F, torch):
+    rows, cols = 2048, 4096
+    w = F.synth_normal((rows, cols), seed=9, stream_id=1, std=0.02)
+    W = F.Fp8Matrix.quantize(w, F.Fp8Scaling(128, 128))
+    h = W.to_host()
+    x = O.bf16_to_f32(O.bf16_bits(O.synth_normal(cols, seed=0, stream=0))).reshape(1, cols)
+    e, mag = _fp8_gemv_expected(h, rows, cols, (128, 128), x)
+    xt = torch.from_numpy(x).cuda().to(torch.bfloat16)
+    y = torch.full((1, 768), float("nan"), device="cuda")
+    F.gemv(W, xt, y, rows=range(256, 1024)).submit(F.Eager())
+    assert O.inner_product_excess(y.cpu().numpy(), e[:, 256:1024], mag[:, 256:1024], cols + 2) <= 1.0
+    yb = torch.full((1, rows), float("nan"), dtype=torch.bfloat16, device="cuda")
+    F.gemv(W, xt, yb).submit(F.Eager())
+    assert O.rel_frobenius(yb.float().cpu().numpy(), e) <= 4e-3  # bf16 output rounding
+
+
+@pytest.mark.parametrize("block", [(128, 128), (0, 0)])
+def test_fp8_expert_gemv(F, torch, block):
+    """expert_gemv_weight_view(&Weight::Fp8, ...) (gemv/fp8.rs:248-281): x row
+    s * input_stride, weight rows of expert ids[s]."""
+    experts, rpe, cols = 6, 512, 2048
+    w = F.synth_normal((experts * rpe, cols), seed=13, stream_id=1, std=0.02)
+    W = F.Fp8Matrix.quantize(w, F.Fp8Scaling(*block))
+    h = W.to_host()
+    ids = np.array([3, 0, 5, 2, 1], np.int32)
+    x = O.bf16_to_f32(O.bf16_bits(O.synth_normal(len(ids) * cols, seed=4, stream=2))).reshape(len(ids), cols)
+    e_all, mag_all = _fp8_gemv_expected(h, experts * rpe, cols, block, x)
+    for stride in (0, 1):
+        xt = torch.from_numpy(x).cuda().to(torch.bfloat16)
+        y = torch.full((len(ids), rpe), float("nan"), device="cuda")
+        dims = F.MoeDims.new(cols, 512, 512, experts, len(ids))
+        sel = F.ExpertSelection.parse(ids, np.full(len(ids), 0.2, np.float32), dims)
+        F.expert_gemv_weight_view(W, xt, sel, y, rpe, stride).submit(F.Eager())
+        got = y.cpu().numpy()
+        for s, e in enumerate(ids):
+            xr = s * stride
+            rows = slice(e * rpe, (e + 1) * rpe)
+            assert O.inner_product_excess(got[s:s + 1], e_all[xr:xr + 1, rows], mag_all[xr:xr + 1, rows],
+                                          cols + 2) <= 1.0
+
+
+def test_fp8_gemv_errors(F, torch):
+    from firepit_b200 import _native as N
+    W = F.Fp8Matrix.quantize(F.synth_normal((256, 256), seed=1, stream_id=1, std=0.02), F.Fp8Scaling(128, 128))
+    x = torch.zeros(1, 256, device="cuda")
+    y = torch.zeros(1, 256, device="cuda")
+    assert N.lib.fpb_fp8_gemv(W.handle, 10, 5, x.data_ptr(), 0, y.data_ptr(), 0, 1, None) == N.FPB_ERR_SHAPE
+    assert N.lib.fpb_fp8_gemv(W.handle, 0, 0, x.data_ptr(), 0, y.data_ptr(), 0, 17, None) == N.FPB_ERR_SHAPE
+    assert N.lib.fpb_fp8_gemv(W.handle, 0, 257, x.data_ptr(), 0, y.data_ptr(), 0, 1, None) == N.FPB_ERR_SHAPE
+    assert N.lib.fpb_fp8_expert_gemv(W.handle, x.data_ptr(), 0, None, 1, 128, 0, y.data_ptr(), 0,
+                                     None) == N.FPB_ERR_INVALID_ARGUMENT
+    ids = torch.zeros(1, dtype=torch.int32, device="cuda")
+    assert N.lib.fpb_fp8_expert_gemv(W.handle, x.data_ptr(), 0, ids.data_ptr(), 1, 64, 0, y.data_ptr(), 0,
+                                     None) == N.FPB_ERR_SHAPE  # 64 rows per expert, block_n 128
+    with pytest.raises(F.ShapeError):
+        F.gemv(W, x, y, F.GemvTile(256, 4))  # a tile taller than the 128-row scale block

@@ -80,7 +80,7 @@ __device__ __forceinline__ void decode16(const uint4 w, float f[16]) {
 }
 
 template <typename XT, typename YT, int B>
-__global__ void __launch_bounds__(kFp8GemvWarps * 32) fp8_gemv_kernel(Fp8GemvArgs a) {
+__global__ void __launch_bounds__(kFp8GemvWarps * 32, B == 1 ? 4 : 1) fp8_gemv_kernel(Fp8GemvArgs a) {
   const int lane = threadIdx.x & 31;
   const int r_local = blockIdx.x * kFp8GemvWarps + (threadIdx.x >> 5);
   if (r_local >= a.nrows) return;  // warp-uniform

@@ -83,7 +83,10 @@ template <typename XT, typename YT, int B>
 __global__ void __launch_bounds__(kFp8GemvWarps * 32, B == 1 ? 4 : 1) fp8_gemv_kernel(Fp8GemvArgs a) {
   const int lane = threadIdx.x & 31;
   const int r_local = blockIdx.x * kFp8GemvWarps + (threadIdx.x >> 5);
-  if (r_local >= a.nrows) return;  // warp-uniform
+  if (r_local >= a.nrows) {  // warp-uniform; still releases the next launch
+    asm volatile("griddepcontrol.launch_dependents;");
+    return;
+  }
   const int slot = blockIdx.y;
   long long row;
   bool ok = true;
@@ -103,13 +106,22 @@ __global__ void __launch_bounds__(kFp8GemvWarps * 32, B == 1 ? 4 : 1) fp8_gemv_k
   float acc[B];
 #pragma unroll
   for (int b = 0; b < B; ++b) acc[b] = 0.0f;
-  for (int c0 = lane; c0 < chunks; c0 += 32 * kFp8GemvUnroll) {
-    uint4 w[kFp8GemvUnroll];
+  // Programmatic dependent launch: the weights (and scales) are immutable while
+  // their handle exists, so the first chunks are requested before waiting for
+  // the previous kernel in the stream; x is read and y written only after it.
+  uint4 w[kFp8GemvUnroll];
+  auto load_w = [&](int c0) {
 #pragma unroll
     for (int u = 0; u < kFp8GemvUnroll; ++u) {
       const int c = c0 + 32 * u;
       w[u] = c < chunks ? __ldg(reinterpret_cast<const uint4 *>(wrow) + c) : make_uint4(0, 0, 0, 0);
     }
+  };
+  load_w(lane);
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  for (int c0 = lane; c0 < chunks; c0 += 32 * kFp8GemvUnroll) {
+    if (c0 != lane) load_w(c0);
 #pragma unroll
     for (int u = 0; u < kFp8GemvUnroll; ++u) {
       const int c = c0 + 32 * u;
@@ -151,18 +163,30 @@ __global__ void __launch_bounds__(kFp8GemvWarps * 32, B == 1 ? 4 : 1) fp8_gemv_k
 
 template <typename XT, typename YT>
 int launch_b(const Fp8GemvArgs &a, int slots, cudaStream_t s) {
-  const dim3 grid((unsigned)((a.nrows + kFp8GemvWarps - 1) / kFp8GemvWarps), (unsigned)slots);
-  const dim3 block(kFp8GemvWarps * 32);
-  if (a.batch <= 1)
-    fp8_gemv_kernel<XT, YT, 1><<<grid, block, 0, s>>>(a);
-  else if (a.batch <= 2)
-    fp8_gemv_kernel<XT, YT, 2><<<grid, block, 0, s>>>(a);
-  else if (a.batch <= 4)
-    fp8_gemv_kernel<XT, YT, 4><<<grid, block, 0, s>>>(a);
-  else if (a.batch <= 8)
-    fp8_gemv_kernel<XT, YT, 8><<<grid, block, 0, s>>>(a);
-  else
-    fp8_gemv_kernel<XT, YT, 16><<<grid, block, 0, s>>>(a);
+  void (*k)(Fp8GemvArgs) = a.batch <= 1   ? fp8_gemv_kernel<XT, YT, 1>
+                           : a.batch <= 2 ? fp8_gemv_kernel<XT, YT, 2>
+                           : a.batch <= 4 ? fp8_gemv_kernel<XT, YT, 4>
+                           : a.batch <= 8 ? fp8_gemv_kernel<XT, YT, 8>
+                                          : fp8_gemv_kernel<XT, YT, 16>;
+  cudaLaunchConfig_t lc{};
+  lc.gridDim = dim3((unsigned)((a.nrows + kFp8GemvWarps - 1) / kFp8GemvWarps), (unsigned)slots);
+  lc.blockDim = dim3(kFp8GemvWarps * 32);
+  lc.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  cudaError_t le = cudaLaunchKernelEx(&lc, k, a);
+  if (le == cudaErrorInvalidValue) {  // no programmatic launch here: a plain launch
+    cudaGetLastError();
+    lc.numAttrs = 0;
+    le = cudaLaunchKernelEx(&lc, k, a);
+  }
+  if (le != cudaSuccess) {
+    cudaGetLastError();
+    return fail(FPB_ERR_CUDA, "cudaLaunchKernelEx(fp8_gemv_kernel): %s", cudaGetErrorName(le));
+  }
   FPB_LAUNCH_CHECK("fp8_gemv_kernel");
   return FPB_OK;
 }

@@ -52,6 +52,7 @@ __device__ __forceinline__ float act_load<uint16_t>(const uint16_t *p, size_t i)
 // 16-byte loads when x is 16-byte aligned, element loads for the tail.
 template <typename T>
 __global__ void act_amax_kernel(const T *x, size_t n, uint32_t *amax_bits) {
+  pdl_enter();
   uint32_t m = 0;
   const size_t tid = (size_t)blockIdx.x * blockDim.x + threadIdx.x, stride = (size_t)gridDim.x * blockDim.x;
   constexpr size_t kVec = 16 / sizeof(T);

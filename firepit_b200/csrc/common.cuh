@@ -37,6 +37,42 @@ inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s
   } while (0)
 
 // Checks the launch that was just issued on this thread.
+// Programmatic dependent launch for short kernels that follow one another in
+// a stream.  pdl_enter(), first in such a kernel, waits until the previous
+// kernel in the stream has completed and its writes are visible (a no-op when
+// the kernel was launched without the attribute), then lets the next kernel
+// start launching; so nothing is read before its producer is done, and only
+// the launch latency overlaps the previous kernel.
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;");
+}
+
+// Launches a kernel whose body starts with pdl_enter() with the
+// programmatic-serialization attribute (a plain launch where the attribute is
+// refused).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args &&...args) {
+  cudaLaunchConfig_t lc{};
+  lc.gridDim = grid;
+  lc.blockDim = block;
+  lc.dynamicSmemBytes = smem;
+  lc.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&lc, kernel, args...);
+  if (e == cudaErrorInvalidValue) {
+    cudaGetLastError();
+    lc.numAttrs = 0;
+    e = cudaLaunchKernelEx(&lc, kernel, args...);
+  }
+  return e;
+}
+
 #define FPB_LAUNCH_CHECK(name)                                   \
   do {                                                           \
     cudaError_t fpb_err_ = cudaGetLastError();                   \

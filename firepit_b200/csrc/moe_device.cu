@@ -16,6 +16,8 @@
 #include <vector>
 
 #include "act_quant.cuh"
+#include <type_traits>
+
 #include "common.cuh"
 #include "nvfp4_matrix.cuh"
 
@@ -42,6 +44,7 @@ __device__ __forceinline__ float order_key_value(uint32_t k) {
 template <int PER_LANE>
 __global__ void moe_topk_kernel(const float *logits, long long ld, const float *shared_gate, int tokens,
                                 int experts, int k, int width, int32_t *ids, float *weights) {
+  pdl_enter();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= tokens) return;
   const float *row = logits + (long long)warp * ld;
@@ -249,6 +252,7 @@ constexpr int kLayoutSmallThreads = 1024;
 __global__ void __launch_bounds__(kLayoutSmallThreads) moe_layout_small_kernel(
     const int32_t *ids, int n, int kk, int width, int tokens, int experts, int tile_rows, int cap,
     int32_t *token_rows, int32_t *tile_experts, int32_t *inverse, int64_t *ranges, int32_t *padded_out, int *error) {
+  pdl_enter();
   extern __shared__ int sm_small[];
   constexpr int kWarps = kLayoutSmallThreads / 32;
   int *wcount = sm_small;                     // [kWarps][experts]
@@ -447,6 +451,7 @@ __device__ __forceinline__ void for_live_rows(size_t n, const int32_t *skip, Fn 
 template <class Rows>
 __global__ void rows_amax_kernel(Rows rows_src, size_t rows, const int32_t *valid, const int32_t *skip, size_t cols,
                                  uint32_t *amax_bits) {
+  pdl_enter();
   const int gpr = (int)(cols / 16), lane = threadIdx.x & 31;
   const size_t n = valid_rows(rows, valid);
   uint32_t m = 0;
@@ -468,6 +473,7 @@ __global__ void rows_amax_kernel(Rows rows_src, size_t rows, const int32_t *vali
 template <class Rows, bool kRowMajorSf = false>
 __global__ void rows_encode_kernel(Rows rows_src, size_t rows, const int32_t *valid, const int32_t *skip, size_t cols,
                                    const uint32_t *amax_bits, uint8_t *packed, uint8_t *sf_tiled, float *global_out) {
+  pdl_enter();
   const float global = __fdiv_rn(__uint_as_float(*amax_bits), 2688.0f);
   if (blockIdx.x == 0 && threadIdx.x == 0) *global_out = global;
   const int gpr = (int)(cols / 16), lane = threadIdx.x & 31;
@@ -493,6 +499,7 @@ __global__ void rows_encode_kernel(Rows rows_src, size_t rows, const int32_t *va
 __global__ void gather_codes_kernel(const uint8_t *tok_packed, const uint8_t *tok_sf, int tokens,
                                     const int32_t *token_rows, size_t rows, const int32_t *valid,
                                     const int32_t *skip, size_t cols, uint8_t *packed, uint8_t *sf_tiled) {
+  pdl_enter();
   const int lane = threadIdx.x & 31;
   const int code_vecs = (int)(cols / 32), sf_words = (int)(cols / 64);
   const size_t n = valid_rows(rows, valid);
@@ -547,6 +554,7 @@ template <typename R, typename O>
 __global__ void combine_kernel(const R *routed, int routed_rows, size_t cols, const int32_t *inverse,
                                const float *weights, int width, int slots, const float *residual, const float *gamma,
                                float inv_h, float eps, O *out, float *normed) {
+  pdl_enter();
   extern __shared__ float red[];
   const int t = blockIdx.x;
   float ss = 0.0f;
@@ -656,7 +664,7 @@ template <class Rows>
 static void launch_rows_encode(const Rows &src, size_t rows, const int32_t *valid, const int32_t *skip, size_t cols,
                                const uint32_t *amax, uint8_t *packed, uint8_t *sf_tiled, float *global_out,
                                cudaStream_t s) {
-  rows_encode_kernel<<<row_grid(rows), 256, 0, s>>>(src, rows, valid, skip, cols, amax, packed, sf_tiled, global_out);
+  launch_pdl(rows_encode_kernel<Rows>, row_grid(rows), 256, 0, s, src, rows, valid, skip, cols, amax, packed, sf_tiled, global_out);
 }
 
 }  // namespace fpb
@@ -685,7 +693,7 @@ extern "C" int fpb_moe_topk(const float *logits, size_t ld, const float *shared_
   const unsigned grid = (unsigned)((tokens * 32 + 255) / 256);
   const int per = (int)((experts + 31) / 32);
   auto go = [&](auto kernel) {
-    kernel<<<grid, 256, 0, s>>>(logits, (long long)ld, shared_gate, (int)tokens, (int)experts, (int)top_k,
+    launch_pdl(kernel, grid, 256, 0, s, logits, (long long)ld, shared_gate, (int)tokens, (int)experts, (int)top_k,
                                 (int)width, ids, weights);
   };
   if (per <= 4)
@@ -761,7 +769,7 @@ extern "C" int fpb_moe_layout(const int32_t *ids, size_t tokens, size_t width, s
         done_small.push_back(dev);
       }
     }
-    moe_layout_small_kernel<<<1, kLayoutSmallThreads, small_smem, s>>>(
+    launch_pdl(moe_layout_small_kernel, 1, kLayoutSmallThreads, small_smem, s,
         ids, n, (int)slots, (int)width, (int)tokens, (int)experts, (int)tile_rows, (int)cap, token_rows,
         tile_experts, inverse, reinterpret_cast<int64_t *>(ranges), padded_rows, err);
     FPB_LAUNCH_CHECK("moe_layout_small_kernel");
@@ -832,7 +840,7 @@ extern "C" int fpb_moe_gather_quantize(const void *x, int x_dtype, size_t tokens
     using T = std::remove_const_t<std::remove_pointer_t<decltype(tp)>>;
     const T *xs = static_cast<const T *>(x);
     if (!given) {
-      act_amax_kernel<T><<<stride_grid(tokens * cols), 256, 0, s>>>(xs, tokens * cols, amax);
+      launch_pdl(act_amax_kernel<T>, stride_grid(tokens * cols), 256, 0, s, xs, tokens * cols, amax);
       FPB_LAUNCH_CHECK("act_amax_kernel");
     }
     GatherRows<T> src{xs, token_rows, cols, (int)tokens};
@@ -850,10 +858,10 @@ extern "C" int fpb_moe_gather_quantize(const void *x, int x_dtype, size_t tokens
     uint8_t *tok_packed = static_cast<uint8_t *>(workspace);
     uint8_t *tok_sf = tok_packed + align256_sz(tokens * cols / 2);
     PlainRows<T> tok{xs, cols};
-    rows_encode_kernel<PlainRows<T>, true><<<row_grid(tokens), 256, 0, s>>>(tok, tokens, nullptr, nullptr, cols, amax,
+    launch_pdl(rows_encode_kernel<PlainRows<T>, true>, row_grid(tokens), 256, 0, s, tok, tokens, nullptr, nullptr, cols, amax,
                                                                              tok_packed, tok_sf, global_out);
     FPB_LAUNCH_CHECK("rows_encode_kernel(tokens)");
-    gather_codes_kernel<<<row_grid(rows), 256, 0, s>>>(tok_packed, tok_sf, (int)tokens, token_rows, rows, valid_rows,
+    launch_pdl(gather_codes_kernel, row_grid(rows), 256, 0, s, tok_packed, tok_sf, (int)tokens, token_rows, rows, valid_rows,
                                                         skip, cols, packed, sf_tiled);
     FPB_LAUNCH_CHECK("gather_codes_kernel");
     return (int)FPB_OK;
@@ -898,7 +906,7 @@ extern "C" int fpb_swiglu_quantize(const void *gate_up, int dtype, size_t rows, 
     SwigluRows<T> src{static_cast<const T *>(gate_up), inter};
     const unsigned grid = row_grid(rows);
     if (!given) {
-      rows_amax_kernel<<<grid, 256, 0, s>>>(src, rows, valid_rows, nullptr, inter, amax);
+      launch_pdl(rows_amax_kernel<std::decay_t<decltype(src)>>, grid, 256, 0, s, src, rows, valid_rows, nullptr, inter, amax);
       FPB_LAUNCH_CHECK("rows_amax_kernel(swiglu)");
     }
     launch_rows_encode(src, rows, valid_rows, nullptr, inter, amax, packed, sf_tiled, global_out, s);
@@ -928,7 +936,7 @@ extern "C" int fpb_rows_quantize(const void *x, int dtype, size_t rows, const in
     const int32_t *skip = (flags & FPB_QUANT_SKIP_PADDING) ? token_rows : nullptr;
     const unsigned grid = row_grid(rows);
     if (!given) {
-      rows_amax_kernel<<<grid, 256, 0, s>>>(src, rows, valid_rows, skip, cols, amax);
+      launch_pdl(rows_amax_kernel<std::decay_t<decltype(src)>>, grid, 256, 0, s, src, rows, valid_rows, skip, cols, amax);
       FPB_LAUNCH_CHECK("rows_amax_kernel(rows)");
     }
     launch_rows_encode(src, rows, valid_rows, skip, cols, amax, packed, sf_tiled, global_out, s);
@@ -952,11 +960,11 @@ static int combine_impl(const void *routed, int r_dtype, size_t routed_rows, siz
     using R = std::remove_const_t<std::remove_pointer_t<decltype(tp)>>;
     const R *rs = static_cast<const R *>(routed);
     if (out_dtype == FPB_F32)
-      combine_kernel<R, float><<<(unsigned)tokens, threads, 32 * sizeof(float), s>>>(
+      launch_pdl(combine_kernel<R, float>, (unsigned)tokens, threads, 32 * sizeof(float), s,
           rs, (int)routed_rows, cols, inverse, weights, (int)width, (int)slots, residual, gamma, inv_h, eps,
           static_cast<float *>(out), normed);
     else if (out_dtype == FPB_BF16)
-      combine_kernel<R, __nv_bfloat16><<<(unsigned)tokens, threads, 32 * sizeof(float), s>>>(
+      launch_pdl(combine_kernel<R, __nv_bfloat16>, (unsigned)tokens, threads, 32 * sizeof(float), s,
           rs, (int)routed_rows, cols, inverse, weights, (int)width, (int)slots, residual, gamma, inv_h, eps,
           static_cast<__nv_bfloat16 *>(out), normed);
     else
@@ -1014,7 +1022,7 @@ extern "C" int fpb_act_amax(const void *x, int dtype, size_t n, float *amax_scra
   if (n == 0) return FPB_OK;
   return with_dtype(dtype, [&](auto tp) {
     using T = std::remove_const_t<std::remove_pointer_t<decltype(tp)>>;
-    act_amax_kernel<T><<<stride_grid(n), 256, 0, s>>>(static_cast<const T *>(x), n, amax);
+    launch_pdl(act_amax_kernel<T>, stride_grid(n), 256, 0, s, static_cast<const T *>(x), n, amax);
     FPB_LAUNCH_CHECK("act_amax_kernel");
     return (int)FPB_OK;
   });
@@ -1033,7 +1041,7 @@ extern "C" int fpb_swiglu_amax(const void *gate_up, int dtype, size_t rows, cons
   return with_dtype(dtype, [&](auto tp) {
     using T = std::remove_const_t<std::remove_pointer_t<decltype(tp)>>;
     SwigluRows<T> src{static_cast<const T *>(gate_up), inter};
-    rows_amax_kernel<<<row_grid(rows), 256, 0, s>>>(src, rows, valid_rows, nullptr, inter, amax);
+    launch_pdl(rows_amax_kernel<std::decay_t<decltype(src)>>, row_grid(rows), 256, 0, s, src, rows, valid_rows, nullptr, inter, amax);
     FPB_LAUNCH_CHECK("rows_amax_kernel(swiglu)");
     return (int)FPB_OK;
   });

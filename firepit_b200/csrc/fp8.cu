@@ -196,6 +196,7 @@ __global__ void __launch_bounds__(kF8Threads, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                     const __grid_constant__ CUtensorMap tmap_y, Fp8GemmParams p) {
   using namespace sm100;
+  pdl_enter();  // programmatic dependent launch: nothing is read before the previous kernel is done
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t *sA = base;
@@ -763,7 +764,7 @@ static int fp8_gemm_launch(fpb_fp8_matrix *w, const uint8_t *a_bits, const float
   CUtensorMap tmap_y;
   std::memset(&tmap_y, 0, sizeof(tmap_y));
   p.tma_store = encode_store_map(&tmap_y, y, p.y_bf16, m, n_rows, (uint64_t)p.ldy, 32, 0);
-  kernel<<<p.ctas, kF8Threads, kF8Smem, s>>>(tmap_a, *reinterpret_cast<const CUtensorMap *>(w->tmap), tmap_y, p);
+  launch_pdl(kernel, p.ctas, kF8Threads, kF8Smem, s, tmap_a, *reinterpret_cast<const CUtensorMap *>(w->tmap), tmap_y, p);
   FPB_LAUNCH_CHECK("fp8_gemm_kernel");
   return FPB_OK;
 }

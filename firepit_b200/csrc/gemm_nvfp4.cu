@@ -244,6 +244,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_base_s;
+  // Programmatic dependent launch: the set-up above overlaps the previous
+  // kernel in the stream; nothing it wrote is read before this wait.
+  pdl_enter();
 
   if (warp == 0) {
     // ---- TMA producer ----------------------------------------------------------
@@ -750,7 +753,7 @@ extern "C" int fpb_nvfp4_gemm_q(fpb_nvfp4_matrix *w, size_t row_begin, size_t ro
   p.tma_store = encode_store_map(&tmap_y, y, p.y_bf16, m, p.N, p.ldy, 32, 0);
   const size_t tiles = (size_t)((p.N + kBN - 1) / kBN) * ((m + kBM - 1) / kBM);
   const unsigned grid = (unsigned)std::min<size_t>(tiles, (size_t)std::max(1, sm_count()));
-  nvfp4_gemm_kernel<<<grid, kGemmThreads, kGemmSmem, s>>>(tmap_a, *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b),
+  launch_pdl(nvfp4_gemm_kernel, grid, kGemmThreads, kGemmSmem, s, tmap_a, *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b),
                                                  tmap_y, *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b), p);
   FPB_LAUNCH_CHECK("nvfp4_gemm_kernel");
   return FPB_OK;
@@ -827,7 +830,7 @@ extern "C" int fpb_nvfp4_grouped_gemm_q(fpb_nvfp4_matrix *w, const uint8_t *a_pa
   p.tma_store = encode_store_map(&tmap_y, y, p.y_bf16, padded_rows, p.N, p.ldy, 32, 0);
   const size_t tiles = (rows_per_expert / kBN) * (padded_rows / kBM);
   const unsigned grid = (unsigned)std::min<size_t>(tiles, (size_t)std::max(1, sm_count()));
-  nvfp4_gemm_kernel<<<grid, kGemmThreads, kGemmSmem, s>>>(tmap_a, *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b),
+  launch_pdl(nvfp4_gemm_kernel, grid, kGemmThreads, kGemmSmem, s, tmap_a, *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b),
                                                  tmap_y, *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b), p);
   FPB_LAUNCH_CHECK("nvfp4_gemm_kernel(grouped)");
   return FPB_OK;
@@ -913,7 +916,7 @@ extern "C" int fpb_nvfp4_grouped_gemm_swiglu_q(fpb_nvfp4_matrix *w, const uint8_
   p.amax_bits = amax_bits;
   const size_t tiles = (2 * inter / kBN) * (padded_rows / kBM);
   const unsigned grid = (unsigned)std::min<size_t>(tiles, (size_t)std::max(1, sm_count()));
-  nvfp4_gemm_kernel<<<grid, kGemmThreads, kGemmSmem, s>>>(tmap_a, *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b),
+  launch_pdl(nvfp4_gemm_kernel, grid, kGemmThreads, kGemmSmem, s, tmap_a, *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b),
                                                  tmap_y, *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b64),
                                                  p);
   FPB_LAUNCH_CHECK("nvfp4_gemm_kernel(grouped swiglu)");

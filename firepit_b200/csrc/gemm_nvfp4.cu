@@ -96,6 +96,7 @@ __global__ void any_negative_kernel(const uint8_t *scales, size_t n, int *flag) 
 template <typename T>
 __global__ void act_encode_kernel(const T *x, size_t rows, size_t cols, const uint32_t *amax_bits,
                                   uint8_t *packed, uint8_t *sf_tiled, float *global_out) {
+  pdl_enter();
   const float global = __fdiv_rn(__uint_as_float(*amax_bits), 2688.0f);
   if (blockIdx.x == 0 && threadIdx.x == 0) *global_out = global;
   // One warp per row (grid-stride over rows); lane l takes groups l, l + 32, ...
@@ -665,10 +666,10 @@ static int quantize_act_impl(const T *x, size_t rows, size_t cols, uint8_t *pack
   FPB_CUDA_TRY(cudaMemsetAsync(amax_scratch, 0, sizeof(uint32_t), s));
   FPB_CUDA_TRY(cudaMemsetAsync(sf_tiled, 0, sf_tiled_bytes(rows, cols), s));
   uint32_t *amax = reinterpret_cast<uint32_t *>(amax_scratch);
-  act_amax_kernel<T><<<grid_for(rows * cols), 256, 0, s>>>(x, rows * cols, amax);
+  launch_pdl(act_amax_kernel<T>, grid_for(rows * cols), 256, 0, s, x, rows * cols, amax);
   FPB_LAUNCH_CHECK("act_amax_kernel");
-  act_encode_kernel<T><<<grid_for(rows * 32), 256, 0, s>>>(x, rows, cols, amax, packed, sf_tiled,
-                                                                   global_out);
+  launch_pdl(act_encode_kernel<T>, grid_for(rows * 32), 256, 0, s, x, rows, cols, amax, packed, sf_tiled,
+             global_out);
   FPB_LAUNCH_CHECK("act_encode_kernel");
   return FPB_OK;
 }

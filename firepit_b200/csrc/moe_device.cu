@@ -258,8 +258,14 @@ __global__ void __launch_bounds__(kLayoutSmallThreads) moe_layout_small_kernel(
   int *wcount = sm_small;                     // [kWarps][experts]
   int *totals = sm_small + kWarps * experts;  // [experts]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  // fills (token_rows = -1, tile_experts = -1, inverse = 0) and zeroed counts
-  for (int i = tid; i < cap; i += blockDim.x) token_rows[i] = -1;
+  // fills (token_rows = -1, tile_experts = -1, inverse = 0) and zeroed counts;
+  // token_rows (cap is a multiple of the tile rows) in 16-byte stores when aligned
+  if ((reinterpret_cast<uintptr_t>(token_rows) & 15) == 0 && (cap & 3) == 0) {
+    int4 *t4 = reinterpret_cast<int4 *>(token_rows);
+    for (int i = tid; i < cap / 4; i += blockDim.x) t4[i] = make_int4(-1, -1, -1, -1);
+  } else {
+    for (int i = tid; i < cap; i += blockDim.x) token_rows[i] = -1;
+  }
   for (int i = tid; i < cap / tile_rows; i += blockDim.x) tile_experts[i] = -1;
   for (int i = tid; i < tokens * width; i += blockDim.x) inverse[i] = 0;
   for (int i = tid; i < kWarps * experts; i += blockDim.x) wcount[i] = 0;

@@ -461,8 +461,40 @@ def stack_weights(parts: list):
 
 def load_experts(checkpoint: Checkpoint, names: list[str], shape: tuple[int, int], fmt: WeightFormat):
     """Experts stacked along rows, each keeping its own scales and global
-    (the stacking of the MoE expert weights, model.rs:619-660)."""
-    return stack_weights([load_weight(checkpoint, n, shape, fmt) for n in names])
+    (the stacking of the MoE expert weights, model.rs:619-660).  NVFP4
+    experts are read straight into the stacked arrays and validated once
+    (the same checks as loading each and stacking)."""
+    if fmt.kind != "nvfp4" or not names:
+        return stack_weights([load_weight(checkpoint, n, shape, fmt) for n in names])
+    rows, cols = shape
+    e = len(names)
+    packed = np.empty(e * rows * cols // 2, np.uint8)
+    scales = np.empty(e * rows * cols // NVFP4_GROUP, np.uint8)
+    row_globals = np.empty(e * rows, np.float32)
+    pb, sb = rows * cols // 2, rows * cols // NVFP4_GROUP
+    for i, name in enumerate(names):
+        check_companions(checkpoint, name, fmt)
+        scale_name = _companion(name, ".weight_scale")
+        f, fs = checkpoint._shard(name), checkpoint._shard(scale_name)
+        dt, s, nb = f.info(name)
+        sdt, ss, snb = fs.info(scale_name)
+        if s != (rows, cols // 2) or ss != (rows, cols // NVFP4_GROUP):
+            raise CheckpointError(f"{name}: invalid {fmt} data or scale shape")
+        if dt != "U8":
+            raise CheckpointError(f"{name}: expected U8, got {dt}")
+        if sdt != "F8_E4M3":
+            raise CheckpointError(f"{scale_name}: expected F8_E4M3, got {sdt}")
+        for fh, n, dtype, dst in ((f, name, "U8", packed[i * pb:(i + 1) * pb]),
+                                  (fs, scale_name, "F8_E4M3", scales[i * sb:(i + 1) * sb])):
+            st = N.lib.fpb_safetensors_read(fh._h, n.encode(), _CODE[dtype], 0, dst.ctypes.data, dst.size)
+            if st != N.FPB_OK:
+                _raise(st)
+        row_globals[i * rows:(i + 1) * rows] = checkpoint.scalar_f32(_companion(name, ".weight_scale_2"))
+    st = N.lib.fpb_nvfp4_validate(packed.ctypes.data, packed.size, scales.ctypes.data, scales.size,
+                                  row_globals.ctypes.data, e * rows, cols)
+    if st != N.FPB_OK:
+        raise FormatError(N.last_error())
+    return HostNvfp4Matrix(packed, scales, row_globals, e * rows, cols)
 
 
 def verify_formats(checkpoint: Checkpoint, quantization: "Quantization | None") -> list[tuple[str, WeightFormat, str,

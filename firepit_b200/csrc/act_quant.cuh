@@ -48,6 +48,24 @@ __device__ __forceinline__ float act_load<uint16_t>(const uint16_t *p, size_t i)
   return bf16_bits_to_f32(p[i]);
 }
 
+// Reduces each thread's |x| maximum over the CTA and adds it to *amax_bits
+// with one atomicMax per CTA (one per warp made thousands of atomics on a
+// single address, which the L2 serialises).  Every thread of the CTA calls it.
+__device__ __forceinline__ void block_amax_to(uint32_t m, uint32_t *amax_bits) {
+  __shared__ uint32_t warp_max[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) warp_max[warp] = m;
+  __syncthreads();
+  if (warp == 0) {
+    m = lane < (int)((blockDim.x + 31) >> 5) ? warp_max[lane] : 0u;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0 && m) atomicMax(amax_bits, m);
+  }
+}
+
 // atomicMax of |x| bits over x[0, n) (amax_bits zeroed by the caller).
 // 16-byte loads when x is 16-byte aligned, element loads for the tail.
 template <typename T>
@@ -75,9 +93,7 @@ __global__ void act_amax_kernel(const T *x, size_t n, uint32_t *amax_bits) {
     head = nv * kVec;
   }
   for (size_t i = head + tid; i < n; i += stride) m = max(m, __float_as_uint(act_load(x, i)) & 0x7fffffffu);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
-  if ((threadIdx.x & 31) == 0) atomicMax(amax_bits, m);
+  block_amax_to(m, amax_bits);
 }
 
 // SwiGLU of one element in the reference's order (swiglu.rs:16):

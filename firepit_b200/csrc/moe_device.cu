@@ -470,9 +470,7 @@ __global__ void rows_amax_kernel(Rows rows_src, size_t rows, const int32_t *vali
       for (int i = 0; i < 16; ++i) m = max(m, __float_as_uint(v[i]) & 0x7fffffffu);
     }
   });
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
-  if (lane == 0 && m) atomicMax(amax_bits, m);
+  block_amax_to(m, amax_bits);
 }
 
 // kRowMajorSf: factors to sf[rows, cols/16] (row-major) instead of the tiled layout.

@@ -342,6 +342,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint8_t *stage = sOut + qw * kOutWarpBytes;
     uint8_t *row_s = stage + lane * 128;
     uint32_t lt = 0;
+    uint32_t glu_max = 0;  // glu: this lane's max |h| bits over its live rows and tiles
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       int m_tile, n_tile, n_base;
       if (!gemm_tile(p, t, n_tiles, m_tile, n_tile, n_base)) continue;
@@ -438,10 +439,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           tma_store_2d(&tmap_y, stage + ch * kOutBoxBytes, j0 + ch * 32, row0);
           bulk_commit_group();
         }
-        if (!row_live) mx = 0;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        if (lane == 0) atomicMax(p.amax_bits, mx);
+        if (row_live) glu_max = max(glu_max, mx);
         continue;
       }
       // Lane l holds the weight global of column n0 + ch*64 + 32c + l; the
@@ -537,6 +535,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
       }
+    }
+    if (p.glu) {  // one atomicMax per warp and launch (per tile made same-address atomics pile up in L2)
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) glu_max = max(glu_max, __shfl_xor_sync(0xffffffffu, glu_max, o));
+      if (lane == 0 && glu_max) atomicMax(p.amax_bits, glu_max);
     }
     // Stores in flight read this CTA's shared memory: complete them before exit.
     if (lane == 0 && p.tma_store) bulk_wait_all();

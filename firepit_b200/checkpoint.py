@@ -493,6 +493,13 @@ def load_experts(checkpoint: Checkpoint, names: list[str], shape: tuple[int, int
     st = N.lib.fpb_nvfp4_validate(packed.ctypes.data, packed.size, scales.ctypes.data, scales.size,
                                   row_globals.ctypes.data, e * rows, cols)
     if st != N.FPB_OK:
+        # Name the checkpoint tensor at fault, as loading each expert on its
+        # own would (HostWeight::load per expert, model.rs:619-660).
+        for i, name in enumerate(names):
+            st_i = N.lib.fpb_nvfp4_validate(packed[i * pb:].ctypes.data, pb, scales[i * sb:].ctypes.data, sb,
+                                            row_globals[i * rows:].ctypes.data, rows, cols)
+            if st_i != N.FPB_OK:
+                raise FormatError(f"{name}: {N.last_error()}")
         raise FormatError(N.last_error())
     return HostNvfp4Matrix(packed, scales, row_globals, e * rows, cols)
 

@@ -88,9 +88,18 @@ __global__ void __launch_bounds__(kFp8GemvWarps * 32, B == 1 ? 4 : 1) fp8_gemv_k
     return;
   }
   const int slot = blockIdx.y;
+  // In expert mode the ids that pick the weight rows may come from the
+  // previous kernel in the stream (the router top-k), so they are read only
+  // after griddepcontrol.wait; the dense path requests its first weight
+  // chunks before the wait (weights are immutable while their handle exists).
+  const bool dense = a.expert_ids == nullptr;
+  if (!dense) {
+    asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+  }
   long long row;
   bool ok = true;
-  if (a.expert_ids) {
+  if (!dense) {
     const int e = a.expert_ids[slot];
     ok = e >= 0 && e < a.n_experts;  // a bad id yields zeros, as the NVFP4 expert GEMV
     row = (long long)(ok ? e : 0) * a.nrows + r_local;
@@ -106,9 +115,10 @@ __global__ void __launch_bounds__(kFp8GemvWarps * 32, B == 1 ? 4 : 1) fp8_gemv_k
   float acc[B];
 #pragma unroll
   for (int b = 0; b < B; ++b) acc[b] = 0.0f;
-  // Programmatic dependent launch: the weights (and scales) are immutable while
-  // their handle exists, so the first chunks are requested before waiting for
-  // the previous kernel in the stream; x is read and y written only after it.
+  // Programmatic dependent launch (dense): the weights (and scales) are
+  // immutable while their handle exists, so the first chunks are requested
+  // before waiting for the previous kernel in the stream; x is read and y
+  // written only after it.
   uint4 w[kFp8GemvUnroll];
   auto load_w = [&](int c0) {
 #pragma unroll
@@ -118,8 +128,10 @@ __global__ void __launch_bounds__(kFp8GemvWarps * 32, B == 1 ? 4 : 1) fp8_gemv_k
     }
   };
   load_w(lane);
-  asm volatile("griddepcontrol.launch_dependents;");
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (dense) {
+    asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+  }
   for (int c0 = lane; c0 < chunks; c0 += 32 * kFp8GemvUnroll) {
     if (c0 != lane) load_w(c0);
 #pragma unroll

@@ -32,9 +32,11 @@
 //  * The warps sharing a row block add their partials in shared memory (one
 //    barrier per row block, double-buffered), then the sum times the row
 //    global is stored as f32 or bf16.
-//  * Programmatic dependent launch: weights are immutable once their handle
-//    exists (handle creation synchronises its stream), so their loads are
-//    issued before griddepcontrol.wait; x is read and y written only after it.
+//  * Programmatic dependent launch: the register variant waits for the
+//    previous kernel before it reads anything (x, and in expert mode the
+//    expert ids that pick the weight rows).  The streaming variant (dense
+//    only) issues its weight copies before the wait: weights are immutable
+//    once their handle exists (handle creation synchronises its stream).
 #include <algorithm>
 #include <mutex>
 #include <utility>
@@ -143,6 +145,12 @@ __global__ void __launch_bounds__(512, 1) gemv_nvfp4_kernel(GemvArgs a) {
   // hi/lo fragments already fill the register budget.
   constexpr bool kPrefetch = !(XLO && C >= 2);
 
+  // Programmatic dependent launch: nothing this kernel reads may be written
+  // by the previous kernel before this wait, and that includes the expert
+  // ids (a router top-k launched just before writes them).
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+
   long long base_row = 0;
   bool slot_ok = true;
   if (a.expert_ids) {
@@ -183,9 +191,6 @@ __global__ void __launch_bounds__(512, 1) gemv_nvfp4_kernel(GemvArgs a) {
       }
     }
   };
-
-  asm volatile("griddepcontrol.launch_dependents;");
-  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   // ---- this warp's slice of x as B fragments, in registers -------------------
   // Lane (g, q) feeds batch rows n = ng*8 + g; for chunk cc and MMA j it holds

@@ -173,7 +173,10 @@ extern "C" int fpb_nvfp4_dequantize(const fpb_nvfp4_matrix *m, float *out, void 
 // device mid-step.  For them the same quantizer runs on a fixed scratch array
 // compiled into this library: kNoAllocMaxBlocks words, 64 KiB, which every
 // GPU that loads the library keeps until the process exits.
+#include <cuda.h>
+
 #include <mutex>
+#include <utility>
 #include <vector>
 
 namespace fpb {
@@ -181,24 +184,61 @@ namespace fpb {
 constexpr size_t kNoAllocMaxBlocks = 16384;  // row blocks (one global each) per call
 static __device__ __align__(256) uint32_t g_noalloc_amax[kNoAllocMaxBlocks];
 
-// The array's device address on the current device.  In host code the
-// array's name only stands in for it, so the address is looked up once per
-// device (with that device current) and cached.
+// The array's device address in the current context.  In host code the
+// array's name only stands in for it, so the address is looked up with
+// cudaGetSymbolAddress (the device current) and cached per context: the key
+// is the driver's unique context id (cuCtxGetId, never reused within a
+// process), so a context re-created after cudaDeviceReset gets a fresh
+// lookup instead of a stale address.
+using CtxGetCurrentFn = CUresult (*)(CUcontext *);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long *);
+
+static int current_context_id(unsigned long long *id) {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(p);
+  });
+  if (!get_current || !get_id) return fail(FPB_ERR_CUDA, "cuCtxGetCurrent / cuCtxGetId unavailable");
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS || !ctx) return fail(FPB_ERR_CUDA, "no current CUDA context");
+  if (get_id(ctx, id) != CUDA_SUCCESS) return fail(FPB_ERR_CUDA, "cuCtxGetId failed");
+  return FPB_OK;
+}
+
 static int noalloc_scratch(float **out) {
   static std::mutex mu;
-  static std::vector<float *> by_device;
+  static std::vector<std::pair<unsigned long long, float *>> by_context;
+  // cudaSetDevice makes the device's primary context current (initialising
+  // it if needed), so the driver's current context is the runtime's.
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  e = cudaSetDevice(dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  unsigned long long ctx = 0;
+  int st = current_context_id(&ctx);
+  if (st) return st;
   std::lock_guard<std::mutex> lock(mu);
-  if ((int)by_device.size() <= dev) by_device.resize(dev + 1, nullptr);
-  if (!by_device[dev]) {
-    void *p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_amax);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc quantize scratch)");
-    by_device[dev] = static_cast<float *>(p);
-  }
-  *out = by_device[dev];
+  for (auto &entry : by_context)
+    if (entry.first == ctx) {
+      *out = entry.second;
+      return FPB_OK;
+    }
+  void *p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_noalloc_amax);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc quantize scratch)");
+  by_context.push_back({ctx, static_cast<float *>(p)});
+  *out = static_cast<float *>(p);
   return FPB_OK;
 }
 

@@ -135,10 +135,12 @@ int fpb_nvfp4_quantize(const void *w, int w_dtype, size_t rows, size_t cols,
  * that must not call cudaMalloc).  The per-block amax scratch is a fixed
  * array inside the library (64 KiB on every GPU that loads it, kept until
  * exit), so rows / rows_per_global may be at most 16384; larger requests
- * return FPB_ERR_UNSUPPORTED.  Allocates nothing.  The first call on a
- * device looks up the array's device address, so make it before any stream
- * capture.  All calls share the array: calls that overlap on the GPU (other
- * streams, other threads) race and must be serialised by the caller. */
+ * return FPB_ERR_UNSUPPORTED.  Allocates nothing.  The first call in a CUDA
+ * context looks up the array's device address (cached per context, so a
+ * context re-created after cudaDeviceReset looks it up again), so make that
+ * first call before any stream capture.  All calls share the array: calls
+ * that overlap on the GPU (other streams, other threads) race and must be
+ * serialised by the caller. */
 int fpb_nvfp4_quantize_noalloc(const void *w, int w_dtype, size_t rows, size_t cols,
                                size_t rows_per_global, uint8_t *packed, uint8_t *scales,
                                float *row_globals, void *stream);

@@ -9,7 +9,8 @@ crates/firepit/src/checkpoint.rs:349-429).  The checkpoints themselves are
 not available, so the tests use these values for structural checks of the
 decode tables (tests/test_oracle_pins.py).
 
-Usage: python tests/golden/make_dequant_fixture.py [reference_root]
+Usage: python tests/golden/make_dequant_fixture.py <reference_root>
+(reference_root: the root of an almightychang/firepit checkout)
 """
 import json
 import sys
@@ -27,7 +28,7 @@ def parse(path: Path):
     return out
 
 
-def main(ref_root: str = "/root/reference") -> None:
+def main(ref_root: str) -> None:
     tests = Path(ref_root) / "crates" / "firepit" / "tests"
     data = {
         "source": "almightychang/firepit crates/firepit/tests/{modelopt,fp8}_dequant_samples.txt",
@@ -38,4 +39,6 @@ def main(ref_root: str = "/root/reference") -> None:
 
 
 if __name__ == "__main__":
-    main(*sys.argv[1:])
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_dequant_fixture.py <reference_root>")
+    main(sys.argv[1])

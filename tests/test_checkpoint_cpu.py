@@ -229,6 +229,29 @@ def test_expert_stacking_keeps_per_row_globals(tmp_path):
         CK.stack_weights([h, CK.HostBf16Weight(np.zeros((1, cols), np.uint16), 1, cols)])
 
 
+def test_expert_loader_names_the_corrupt_expert(tmp_path):
+    """One expert with a NaN block scale (0x7f) among several: the error names
+    that expert's tensor, as a per-expert load would."""
+    rows, cols = 32, 128
+    tensors = {}
+    for e in range(4):
+        packed, scales, glob = _nvfp4_parts(rows, cols, 20 + e)
+        if e == 2:
+            scales = scales.copy()
+            scales[5] = 0x7F
+        base = f"model.layers.0.mlp.experts.{e}.down_proj"
+        tensors[f"{base}.weight"] = _t_u8(packed, (rows, cols // 2))
+        tensors[f"{base}.weight_scale"] = _t_e4m3(scales, (rows, cols // 16))
+        tensors[f"{base}.weight_scale_2"] = torch.tensor(glob, dtype=torch.float32)
+    _write(tmp_path / "s.safetensors", tensors)
+    (tmp_path / "model.safetensors.index.json").write_text(
+        json.dumps({"weight_map": {n: "s.safetensors" for n in tensors}}))
+    ck = CK.Checkpoint.open(tmp_path)
+    names = [f"model.layers.0.mlp.experts.{e}.down_proj.weight" for e in range(4)]
+    with pytest.raises(CK.FormatError, match=r"experts\.2\.down_proj\.weight"):
+        CK.load_experts(ck, names, (rows, cols), CK.WeightFormat.NVFP4)
+
+
 def test_quantization_configs(tmp_path):
     q = CK.Quantization.parse({"quantization_config": {
         "quant_method": "fp8", "fmt": "e4m3", "activation_scheme": "dynamic", "weight_block_size": [128, 128],

@@ -60,6 +60,12 @@ i32 = C.c_int
 u8p = C.POINTER(C.c_uint8)
 f32p = C.POINTER(C.c_float)
 
+class GemvSegment(C.Structure):
+    """fpb_gemv_segment (include/firepit_b200.h)."""
+    _fields_ = [("w", C.c_void_p), ("row_begin", C.c_size_t), ("row_end", C.c_size_t), ("x", C.c_void_p),
+                ("y", C.c_void_p)]
+
+
 # name -> (restype, argtypes)
 SIGNATURES: dict[str, tuple] = {
     "fpb_safetensors_open": (i32, [C.c_char_p, C.POINTER(vp)]),
@@ -92,6 +98,7 @@ SIGNATURES: dict[str, tuple] = {
     "fpb_nvfp4_quantize_noalloc": (i32, [vp, i32, sz, sz, sz, vp, vp, vp, vp]),
     "fpb_nvfp4_dequantize": (i32, [vp, vp, vp]),
     "fpb_nvfp4_gemv": (i32, [vp, sz, sz, vp, i32, vp, i32, i32, vp]),
+    "fpb_nvfp4_gemv_batched": (i32, [C.POINTER(GemvSegment), i32, i32, i32, i32, vp]),
     "fpb_nvfp4_expert_gemv": (i32, [vp, vp, i32, vp, i32, sz, i32, vp, i32, vp]),
     "fpb_fp8_gemv": (i32, [vp, sz, sz, vp, i32, vp, i32, i32, vp]),
     "fpb_fp8_expert_gemv": (i32, [vp, vp, i32, vp, i32, sz, i32, vp, i32, vp]),

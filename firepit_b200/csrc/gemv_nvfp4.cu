@@ -409,33 +409,55 @@ __global__ void __launch_bounds__(512, 1) gemv_nvfp4_kernel(GemvArgs a) {
 
 // ---- streaming variant: weights staged in shared memory ahead of the wait ----
 //
-// Dense GEMV with K % 128 == 0, K <= 4096, batch <= 8, rows and the first row
-// a multiple of 4.  A CTA (8 warps) owns a contiguous range of `rpc` rows
-// and is sized so that two fit on an SM: one of this GEMV and one of the next
-// launch in the stream.  Before griddepcontrol.wait, warp 0 issues 1-D bulk
-// copies of the CTA's first row blocks (16 rows x K codes, their factors and
-// globals) into a ring of shared-memory stages, so the weights of launch i+1
-// stream from HBM while launch i computes.  After the wait each warp stages
-// its K slice of x (f16, prescaled as in the register variant) and runs the
-// same cvt / mul.f16x2 / m16n8k16 arithmetic on every row block, reading codes
-// from shared memory (row pitch = 64 mod 128 bytes: conflict-free).  Partial
-// sums of the 8 K slices meet in shared memory; the last warp to finish a row
-// block (a shared counter) adds them, stores y and refills the stage with the
-// row block S stages ahead.
-struct StreamArgs {
+// Dense GEMV with K % 128 == 0, K <= 4096, batch <= 8, over one or several
+// matrices ("segments": each a row range of one matrix with its own x and y,
+// all with the same K).  The segments' rows are laid end to end in a virtual
+// row space; CTA c owns the contiguous virtual rows [c*rpc, (c+1)*rpc) (rpc a
+// multiple of 4) and walks them in units of at most UR rows that never cross
+// a segment.  Warp 0 issues 1-D bulk copies of the CTA's first units (codes,
+// factors and row globals) into a ring of shared-memory stages before
+// griddepcontrol.wait, so with one segment the weights of launch i+1 stream
+// from HBM while launch i computes (two CTAs fit on an SM).  After the wait
+// each warp stages its K slice of the unit's x (f16, prescaled as in the
+// register variant; again only when the segment's x changes) and runs the
+// cvt / mul.f16x2 / m16n8k16 arithmetic on every unit, reading codes from
+// shared memory (row pitch = 64 mod 128 bytes: conflict-free).  Partial sums
+// of the 8 K slices meet in shared memory; the last warp to finish a unit (a
+// shared counter) adds them, stores y and refills the stage with the unit S
+// stages ahead.  Every warp walks the CTA's units itself (one iterator for
+// the unit it computes, one S units ahead for refills), so no unit table is
+// shared.  Units are 16 rows (UR = 16) in every launch: 8-row units (MMA
+// rows 8-15 zero, stages half the size, a ring twice as deep in the same
+// shared memory) measured 1.43x slower on 64 config-0 matrices per launch,
+// and one 16-warp CTA per SM 1.65x slower: the warps' instruction stream, not
+// the arrival of the weights, bounds this kernel (the same launches over
+// weights resident in L2 run at the same speed).
+struct StreamSeg {
   const uint8_t *packed;  // first addressed row
   const uint8_t *scales;
   const float *globals;
-  const void *x;
-  void *y;
+  const void *x;   // [batch, K]
+  void *y;         // [batch, rows]
+  long long vbeg;  // first virtual row
+  int rows;
+  int pad_;
+};
+
+constexpr int kStreamMaxSegs = 128;
+
+template <int NSEG>
+struct StreamArgs {
+  StreamSeg seg[NSEG];
+  int nseg;
+  int rpc;  // virtual rows per CTA (multiple of 4)
+  long long total_rows;
   int *error;
-  int rows, K, batch;
-  int rpc;          // rows per CTA (multiple of 4)
+  int K, batch;
   int stages;       // ring depth
   int wpitch;       // shared bytes per staged code row (64 mod 128)
   int spitch;       // shared bytes per staged factor row
-  int scale_rows;   // 1: one copy per factor row; 0: one contiguous copy per row block
-  int stage_bytes;  // 16 * wpitch + 16 * spitch + 64
+  int scale_rows;   // 1: one copy per factor row; 0: one contiguous copy per unit
+  int stage_bytes;  // UR * wpitch + UR * spitch + 64
   int xpitch;       // f16 elements per staged input row
   int y_bf16;
 };
@@ -456,43 +478,85 @@ __device__ __forceinline__ uint16_t lds16(const void *p) {
   return v;
 }
 
-// Issues (one warp) the copies of one row block of `nrows` rows (a multiple of
-// 4, at most 16) starting at row `row0` of the addressed rows into `stage`.
-__device__ __forceinline__ void stream_issue(const StreamArgs &a, uint8_t *stage, uint64_t *bar, int row0,
-                                             int nrows, int lane) {
+// Position of the next unit of a CTA's virtual row range.  The segment's row
+// count is cached so that the segment table (kernel parameters, read with a
+// computed index) is consulted only when a unit starts a new segment.
+struct UnitIter {
+  int seg;       // segment of the next unit
+  int row;       // its first row within the segment
+  int seg_rows;  // rows of that segment
+  long long v;   // its virtual row
+};
+
+struct Unit {
+  int seg, row0, nrows;
+};
+
+// Takes the next unit (at most UR rows, within one segment and below v_hi);
+// false once the range is exhausted.
+template <int UR, int NSEG>
+__device__ __forceinline__ bool next_unit(const StreamArgs<NSEG> &a, UnitIter &it, long long v_hi, Unit &u) {
+  if (it.v >= v_hi) return false;
+  while (it.row >= it.seg_rows) {
+    ++it.seg;
+    it.row = 0;
+    it.seg_rows = a.seg[it.seg].rows;
+  }
+  u.seg = it.seg;
+  u.row0 = it.row;
+  u.nrows = (int)min((long long)min(UR, it.seg_rows - it.row), v_hi - it.v);
+  it.row += u.nrows;
+  it.v += u.nrows;
+  return true;
+}
+
+// Issues (one warp) the copies of one unit of `u.nrows` rows (a multiple of
+// 4, at most UR) into `stage`.
+template <int UR, int NSEG>
+__device__ __forceinline__ void stream_issue(const StreamArgs<NSEG> &a, uint8_t *stage, uint64_t *bar,
+                                             const Unit &u, int lane) {
   const uint32_t kb2 = (uint32_t)a.K >> 1, kb16 = (uint32_t)a.K >> 4;
+  const StreamSeg &sg = a.seg[u.seg];
+  const int nrows = u.nrows, row0 = u.row0;
   if (lane == 0) sm100::mbar_arrive_expect_tx(bar, (uint32_t)nrows * (kb2 + kb16 + 4));
   __syncwarp();
   if (lane < nrows)
-    sm100::bulk_load(stage + lane * a.wpitch, a.packed + (size_t)(row0 + lane) * kb2, kb2, bar);
-  uint8_t *sc = stage + 16 * a.wpitch;
+    sm100::bulk_load(stage + lane * a.wpitch, sg.packed + (size_t)(row0 + lane) * kb2, kb2, bar);
+  uint8_t *sc = stage + UR * a.wpitch;
   if (a.scale_rows) {
     if (lane >= 16 && lane - 16 < nrows)
-      sm100::bulk_load(sc + (lane - 16) * a.spitch, a.scales + (size_t)(row0 + lane - 16) * kb16, kb16, bar);
+      sm100::bulk_load(sc + (lane - 16) * a.spitch, sg.scales + (size_t)(row0 + lane - 16) * kb16, kb16, bar);
   } else if (lane == 16) {
-    sm100::bulk_load(sc, a.scales + (size_t)row0 * kb16, (uint32_t)nrows * kb16, bar);
+    sm100::bulk_load(sc, sg.scales + (size_t)row0 * kb16, (uint32_t)nrows * kb16, bar);
   }
-  if (lane == 31) sm100::bulk_load(sc + 16 * a.spitch, a.globals + row0, (uint32_t)nrows * 4, bar);
+  if (lane == 31) sm100::bulk_load(sc + UR * a.spitch, sg.globals + row0, (uint32_t)nrows * 4, bar);
 }
 
-template <bool XLO>
-__global__ void __launch_bounds__(256, 2) gemv_nvfp4_stream_kernel(StreamArgs a) {
+template <bool XLO, int NSEG, int UR>
+__global__ void __launch_bounds__(kStreamWarps * 32, 2)
+    gemv_nvfp4_stream_kernel(const __grid_constant__ StreamArgs<NSEG> a) {
+  constexpr int W = kStreamWarps;
   extern __shared__ __align__(16) unsigned char smem[];
   const int S = a.stages;
   uint8_t *stages = smem;
   __half *xh = reinterpret_cast<__half *>(smem + (size_t)S * a.stage_bytes);
   __half *xl = xh + (size_t)a.batch * a.xpitch;
   float4 *red = reinterpret_cast<float4 *>(xh + (size_t)a.batch * a.xpitch * (XLO ? 2 : 1));
-  uint64_t *full = reinterpret_cast<uint64_t *>(red + (size_t)S * kStreamWarps * 32);
+  uint64_t *full = reinterpret_cast<uint64_t *>(red + (size_t)S * W * 32);
   int *count = reinterpret_cast<int *>(full + S);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, q = lane & 3;
-  if (blockDim.x != kStreamWarps * 32) return;  // the layout below assumes 8 warps
-  const int row_lo = blockIdx.x * a.rpc;
-  const int row_hi = min(a.rows, row_lo + a.rpc);
-  if (row_lo >= row_hi) return;
-  const int nrb = (row_hi - row_lo + 15) >> 4;
+  if (blockDim.x != W * 32) return;  // the layout below assumes W warps
+  const long long v_lo = (long long)blockIdx.x * a.rpc;
+  const long long v_hi = min(a.total_rows, v_lo + a.rpc);
+  if (v_lo >= v_hi) return;
+  // The segment holding v_lo (segments are in virtual-row order).
+  UnitIter it_c{0, 0, 0, v_lo};
+  while (it_c.seg + 1 < a.nseg && a.seg[it_c.seg + 1].vbeg <= v_lo) ++it_c.seg;
+  it_c.row = (int)(v_lo - a.seg[it_c.seg].vbeg);
+  it_c.seg_rows = a.seg[it_c.seg].rows;
+  UnitIter it_a = it_c;  // S units ahead of it_c once the ring is primed
 
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
@@ -503,87 +567,107 @@ __global__ void __launch_bounds__(256, 2) gemv_nvfp4_stream_kernel(StreamArgs a)
   }
   __syncthreads();
   // Weights are immutable while their handle exists: copy them before the wait.
-  if (warp == 0)
-    for (int s = 0; s < S && s < nrb; ++s)
-      stream_issue(a, stages + (size_t)s * a.stage_bytes, &full[s], row_lo + 16 * s,
-                   min(16, row_hi - row_lo - 16 * s), lane);
+  for (int s = 0; s < S; ++s) {
+    Unit u;
+    if (!next_unit<UR>(a, it_a, v_hi, u)) break;
+    if (warp == 0) stream_issue<UR>(a, stages + (size_t)s * a.stage_bytes, &full[s], u, lane);
+  }
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
-  // ---- this warp's K slice of x, prescaled to f16 in shared memory ----------
   const int chunks = a.K >> 7;
-  const int cpw = (chunks + kStreamWarps - 1) / kStreamWarps;
+  const int cpw = (chunks + W - 1) / W;
   const int c_lo = min(chunks, warp * cpw), c_hi = min(chunks, c_lo + cpw);
   const int k_lo = c_lo * 128, pieces = (c_hi - c_lo) * 16;  // 8-element pieces
-  float my_unscale = 1.0f;                                    // lane b: batch row b
-  for (int b = 0; b < a.batch; ++b) {
-    float v[2][8];
-    uint32_t m = 0;
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const int p = lane + 32 * i;
-      const long long off = (long long)b * a.K + k_lo + p * 8;
-      if (p < pieces) {
-        if (XLO) {
-          const float4 f0 = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(a.x) + off);
-          const float4 f1 = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(a.x) + off + 4);
-          v[i][0] = f0.x; v[i][1] = f0.y; v[i][2] = f0.z; v[i][3] = f0.w;
-          v[i][4] = f1.x; v[i][5] = f1.y; v[i][6] = f1.z; v[i][7] = f1.w;
-        } else {
-          const uint4 r = *reinterpret_cast<const uint4 *>(reinterpret_cast<const uint16_t *>(a.x) + off);
-          const uint32_t wv[4] = {r.x, r.y, r.z, r.w};
-#pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            v[i][2 * t] = __uint_as_float(wv[t] << 16);
-            v[i][2 * t + 1] = __uint_as_float(wv[t] & 0xffff0000u);
-          }
-        }
-      } else {
-#pragma unroll
-        for (int t = 0; t < 8; ++t) v[i][t] = 0.0f;
-      }
-#pragma unroll
-      for (int t = 0; t < 8; ++t) m = max(m, __float_as_uint(v[i][t]) & 0x7fffffffu);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
-    const int F = prescale_exponent(m);
-    const float up = __uint_as_float((uint32_t)(127 + F) << 23);
-    if (lane == b) my_unscale = __uint_as_float((uint32_t)(127 - F) << 23);
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const int p = lane + 32 * i;
-      if (p >= pieces) continue;
-      uint32_t h[4], l[4];
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const float v0 = v[i][2 * t] * up, v1 = v[i][2 * t + 1] * up;
-        h[t] = pack_half2(v0, v1);
-        if (XLO) {
-          const float2 f = __half22float2(*reinterpret_cast<__half2 *>(&h[t]));
-          l[t] = pack_half2(v0 - f.x, v1 - f.y);
-        }
-      }
-      const size_t o = (size_t)b * a.xpitch + k_lo + p * 8;
-      *reinterpret_cast<uint4 *>(xh + o) = make_uint4(h[0], h[1], h[2], h[3]);
-      if (XLO) *reinterpret_cast<uint4 *>(xl + o) = make_uint4(l[0], l[1], l[2], l[3]);
-    }
-  }
-  __syncwarp();
-  // Unscale of accumulator columns n = 2q, 2q + 1.
-  const float us0 = __shfl_sync(0xffffffffu, my_unscale, 2 * q);
-  const float us1 = __shfl_sync(0xffffffffu, my_unscale, 2 * q + 1);
   const bool n_ok = g < a.batch;
   const __half *xrow = xh + (size_t)(n_ok ? g : 0) * a.xpitch;
   const __half *xrow_lo = xl + (size_t)(n_ok ? g : 0) * a.xpitch;
+  const void *staged_x = nullptr;
+  float us0 = 1.0f, us1 = 1.0f;
+  int cur_seg = -1;
+  const void *seg_x = nullptr;  // input, output and row count of segment cur_seg
+  void *y_seg = nullptr;
+  int y_rows = 0;
 
-  // ---- row blocks ------------------------------------------------------------
-  for (int rb = 0; rb < nrb; ++rb) {
-    const int s = rb % S;
-    const uint32_t parity = (uint32_t)(rb / S) & 1u;
+  // ---- units -------------------------------------------------------------------
+  Unit u;
+  for (int i = 0; next_unit<UR>(a, it_c, v_hi, u); ++i) {
+    if (u.seg != cur_seg) {
+      cur_seg = u.seg;
+      seg_x = a.seg[u.seg].x;
+      y_seg = a.seg[u.seg].y;
+      y_rows = it_c.seg_rows;
+    }
+    if (seg_x != staged_x) {
+      // ---- this warp's K slice of the segment's x, prescaled to f16 ----------
+      staged_x = seg_x;
+      float my_unscale = 1.0f;  // lane b: batch row b
+      for (int b = 0; b < a.batch; ++b) {
+        float v[2][8];
+        uint32_t m = 0;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int p = lane + 32 * h;
+          const long long off = (long long)b * a.K + k_lo + p * 8;
+          if (p < pieces) {
+            if (XLO) {
+              const float4 f0 = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(seg_x) + off);
+              const float4 f1 =
+                  *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(seg_x) + off + 4);
+              v[h][0] = f0.x; v[h][1] = f0.y; v[h][2] = f0.z; v[h][3] = f0.w;
+              v[h][4] = f1.x; v[h][5] = f1.y; v[h][6] = f1.z; v[h][7] = f1.w;
+            } else {
+              const uint4 r =
+                  *reinterpret_cast<const uint4 *>(reinterpret_cast<const uint16_t *>(seg_x) + off);
+              const uint32_t wv[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+              for (int t = 0; t < 4; ++t) {
+                v[h][2 * t] = __uint_as_float(wv[t] << 16);
+                v[h][2 * t + 1] = __uint_as_float(wv[t] & 0xffff0000u);
+              }
+            }
+          } else {
+#pragma unroll
+            for (int t = 0; t < 8; ++t) v[h][t] = 0.0f;
+          }
+#pragma unroll
+          for (int t = 0; t < 8; ++t) m = max(m, __float_as_uint(v[h][t]) & 0x7fffffffu);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+        const int F = prescale_exponent(m);
+        const float up = __uint_as_float((uint32_t)(127 + F) << 23);
+        if (lane == b) my_unscale = __uint_as_float((uint32_t)(127 - F) << 23);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int p = lane + 32 * h;
+          if (p >= pieces) continue;
+          uint32_t hv[4], lv[4];
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const float v0 = v[h][2 * t] * up, v1 = v[h][2 * t + 1] * up;
+            hv[t] = pack_half2(v0, v1);
+            if (XLO) {
+              const float2 f = __half22float2(*reinterpret_cast<__half2 *>(&hv[t]));
+              lv[t] = pack_half2(v0 - f.x, v1 - f.y);
+            }
+          }
+          const size_t o = (size_t)b * a.xpitch + k_lo + p * 8;
+          *reinterpret_cast<uint4 *>(xh + o) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+          if (XLO) *reinterpret_cast<uint4 *>(xl + o) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+        }
+      }
+      __syncwarp();
+      // Unscale of accumulator columns n = 2q, 2q + 1.
+      us0 = __shfl_sync(0xffffffffu, my_unscale, 2 * q);
+      us1 = __shfl_sync(0xffffffffu, my_unscale, 2 * q + 1);
+    }
+
+    const int s = i % S;
+    const uint32_t parity = (uint32_t)(i / S) & 1u;
     uint8_t *st = stages + (size_t)s * a.stage_bytes;
     bool ready = false;
-    for (uint32_t i = 0; i < sm100::kSpinLimit && !ready; ++i) ready = sm100::mbar_try_wait(&full[s], parity);
+    for (uint32_t t = 0; t < sm100::kSpinLimit && !ready; ++t) ready = sm100::mbar_try_wait(&full[s], parity);
     if (!ready) {  // copies that never landed: record it and leave
       if (lane == 0 && a.error) atomicCAS(a.error, 0, 201);
       return;
@@ -594,19 +678,24 @@ __global__ void __launch_bounds__(256, 2) gemv_nvfp4_stream_kernel(StreamArgs a)
 #pragma unroll
       for (int t = 0; t < 4; ++t) acc[c4][t] = 0.0f;
 
+    const uint8_t *sc = st + UR * a.wpitch;
     for (int c = c_lo; c < c_hi; ++c) {
       const uint4 wa = lds128(st + g * a.wpitch + c * 64 + q * 16);
-      const uint4 wb = lds128(st + (g + 8) * a.wpitch + c * 64 + q * 16);
-      const uint8_t *sc = st + 16 * a.wpitch;
+      const uint4 wb = UR == 16 ? lds128(st + (g + 8) * a.wpitch + c * 64 + q * 16) : make_uint4(0, 0, 0, 0);
       const uint16_t sa = lds16(sc + g * a.spitch + c * 8 + 2 * q);
-      const uint16_t sb = lds16(sc + (g + 8) * a.spitch + c * 8 + 2 * q);
+      const uint16_t sb = UR == 16 ? lds16(sc + (g + 8) * a.spitch + c * 8 + 2 * q) : (uint16_t)0;
       uint32_t s_lo[2], s_hi[2];
       {
-        const uint32_t fa = e4m3x2_to_f16x2(sa), fb = e4m3x2_to_f16x2(sb);
+        const uint32_t fa = e4m3x2_to_f16x2(sa);
         s_lo[0] = __byte_perm(fa, fa, 0x1010);
         s_hi[0] = __byte_perm(fa, fa, 0x3232);
-        s_lo[1] = __byte_perm(fb, fb, 0x1010);
-        s_hi[1] = __byte_perm(fb, fb, 0x3232);
+        if (UR == 16) {
+          const uint32_t fb = e4m3x2_to_f16x2(sb);
+          s_lo[1] = __byte_perm(fb, fb, 0x1010);
+          s_hi[1] = __byte_perm(fb, fb, 0x3232);
+        } else {
+          s_lo[1] = s_hi[1] = 0;
+        }
       }
       const uint32_t w0[4] = {wa.x, wa.y, wa.z, wa.w};
       const uint32_t w1[4] = {wb.x, wb.y, wb.z, wb.w};
@@ -618,13 +707,13 @@ __global__ void __launch_bounds__(256, 2) gemv_nvfp4_stream_kernel(StreamArgs a)
           xv = lds128(xrow + k0 + 8 * wi);
           if (XLO) xlv = lds128(xrow_lo + k0 + 8 * wi);
         }
-        uint32_t f0[4], f1[4];
+        uint32_t f0[4], f1[4] = {0, 0, 0, 0};
         e2m1x8_to_f16x8(w0[wi], f0);
-        e2m1x8_to_f16x8(w1[wi], f1);
+        if (UR == 16) e2m1x8_to_f16x8(w1[wi], f1);
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
           f0[t] = hmul2(f0[t], wi < 2 ? s_lo[0] : s_hi[0]);
-          f1[t] = hmul2(f1[t], wi < 2 ? s_lo[1] : s_hi[1]);
+          if (UR == 16) f1[t] = hmul2(f1[t], wi < 2 ? s_lo[1] : s_hi[1]);
         }
         // MMA 2wi + jj takes codes 4jj..4jj+3 of this word and x words 2jj, 2jj+1.
         const int ch = (wi & 1) * 2;
@@ -636,18 +725,22 @@ __global__ void __launch_bounds__(256, 2) gemv_nvfp4_stream_kernel(StreamArgs a)
         }
       }
     }
-    float4 *slot = red + (size_t)s * kStreamWarps * 32;
+    float4 *slot = red + (size_t)s * W * 32;
     slot[warp * 32 + lane] = make_float4((acc[0][0] + acc[1][0] + acc[2][0] + acc[3][0]) * us0,
                                          (acc[0][1] + acc[1][1] + acc[2][1] + acc[3][1]) * us1,
                                          (acc[0][2] + acc[1][2] + acc[2][2] + acc[3][2]) * us0,
                                          (acc[0][3] + acc[1][3] + acc[2][3] + acc[3][3]) * us1);
-    // The last of the 8 warps to finish this row block reduces it, stores y
-    // and refills the stage (the counter only grows: last = 8th arrival).
+    // The unit S ahead, which the last warp to finish this one copies into
+    // its stage (every warp advances its look-ahead iterator in step).
+    Unit ahead;
+    const bool has_ahead = next_unit<UR>(a, it_a, v_hi, ahead);
+    // The last of the W warps to finish this unit reduces it, stores y and
+    // refills the stage (the counter only grows: last = W-th arrival).
     __syncwarp();
     int last = 0;
     if (lane == 0) {
       __threadfence_block();
-      last = (atomicAdd(&count[s], 1) % kStreamWarps) == kStreamWarps - 1;
+      last = (atomicAdd(&count[s], 1) % W) == W - 1;
       __threadfence_block();
     }
     last = __shfl_sync(0xffffffffu, last, 0);
@@ -655,29 +748,28 @@ __global__ void __launch_bounds__(256, 2) gemv_nvfp4_stream_kernel(StreamArgs a)
     if (!last) continue;
     float4 sum = slot[lane];
 #pragma unroll
-    for (int w = 1; w < kStreamWarps; ++w) {
+    for (int w = 1; w < W; ++w) {
       const float4 p = slot[w * 32 + lane];
       sum.x += p.x; sum.y += p.y; sum.z += p.z; sum.w += p.w;
     }
-    const float *gl = reinterpret_cast<const float *>(st + 16 * a.wpitch + 16 * a.spitch);
+    const float *gl = reinterpret_cast<const float *>(sc + UR * a.spitch);
     const float vals[4] = {sum.x, sum.y, sum.z, sum.w};
-    const int rbase = row_lo + rb * 16;
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
-      const int rl = g + ((t >> 1) << 3), r = rbase + rl, n = 2 * q + (t & 1);
-      if (r < row_hi && n < a.batch) {
+      const int rl = g + ((t >> 1) << 3), n = 2 * q + (t & 1);
+      if (rl < u.nrows && n < a.batch) {
         const float v = vals[t] * gl[rl];
-        const size_t off = (size_t)n * a.rows + r;
+        const size_t off = (size_t)n * y_rows + u.row0 + rl;
         if (a.y_bf16)
-          reinterpret_cast<__nv_bfloat16 *>(a.y)[off] = __float2bfloat16_rn(v);
+          reinterpret_cast<__nv_bfloat16 *>(y_seg)[off] = __float2bfloat16_rn(v);
         else
-          reinterpret_cast<float *>(a.y)[off] = v;
+          reinterpret_cast<float *>(y_seg)[off] = v;
       }
     }
-    if (rb + S < nrb) {
+    if (has_ahead) {
       __syncwarp();
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      stream_issue(a, st, &full[s], row_lo + 16 * (rb + S), min(16, row_hi - row_lo - 16 * (rb + S)), lane);
+      stream_issue<UR>(a, st, &full[s], ahead, lane);
     }
   }
 }
@@ -814,55 +906,41 @@ static int run_gemv(GemvArgs args, int slots, bool x_f32, cudaStream_t stream) {
 // reservations) fit in the 228 KB of an SM.
 constexpr int kStreamSmemBudget = 110 * 1024;
 
-struct StreamPlan {
-  StreamArgs a;
-  int grid;
-  size_t smem;
-};
-
-// Fills `plan` when the streaming kernel serves this call; false otherwise.
-static bool plan_stream(const uint8_t *packed, const uint8_t *scales, const float *globals, int rows, int K,
-                        int batch, bool x_f32, StreamPlan *plan) {
-  if (K % 128 != 0 || K > 4096 || batch < 1 || batch > 8 || rows % 4 != 0 || rows <= 0) return false;
-  if (reinterpret_cast<uintptr_t>(packed) % 16 || reinterpret_cast<uintptr_t>(scales) % 16 ||
-      reinterpret_cast<uintptr_t>(globals) % 16)
-    return false;
-  StreamArgs a{};
-  a.packed = packed;
-  a.scales = scales;
-  a.globals = globals;
-  a.rows = rows;
-  a.K = K;
-  a.batch = batch;
+// Ring and staging geometry of the streaming kernel for (K, batch, x dtype,
+// unit rows); false when the streaming kernel cannot serve that shape.
+template <int NSEG>
+static bool stream_geometry(int K, int batch, bool x_f32, int unit_rows, long long max_units_per_cta,
+                            StreamArgs<NSEG> *a, size_t *smem) {
+  if (K % 128 != 0 || K > 4096 || batch < 1 || batch > 8) return false;
+  a->K = K;
+  a->batch = batch;
   const int kb2 = K / 2, kb16 = K / 16;
-  a.wpitch = kb2 + ((kb2 % 128 == 0) ? 64 : 0);  // 64 mod 128
-  a.scale_rows = kb16 % 16 == 0;
-  a.spitch = a.scale_rows ? kb16 + (16 - kb16 % 128 + 128) % 128 : kb16;  // 16 mod 128 when per row
-  a.stage_bytes = 16 * a.wpitch + 16 * a.spitch + 64;
-  a.xpitch = K + 32;
-  const int nsm = std::max(1, sm_count());
-  int rpc = (rows + nsm - 1) / nsm;
-  rpc = (rpc + 3) / 4 * 4;
-  a.rpc = rpc;
-  const int nrb_max = (rpc + 15) / 16;
-  const size_t x_bytes = (size_t)batch * a.xpitch * 2 * (x_f32 ? 2 : 1);
-  const size_t per_stage = (size_t)a.stage_bytes + kStreamWarps * 32 * sizeof(float4) + 12;
+  a->wpitch = kb2 + ((kb2 % 128 == 0) ? 64 : 0);  // 64 mod 128
+  a->scale_rows = kb16 % 16 == 0;
+  a->spitch = a->scale_rows ? kb16 + (16 - kb16 % 128 + 128) % 128 : kb16;  // 16 mod 128 when per row
+  a->stage_bytes = unit_rows * a->wpitch + unit_rows * a->spitch + 64;
+  a->xpitch = K + 32;
+  const size_t x_bytes = (size_t)batch * a->xpitch * 2 * (x_f32 ? 2 : 1);
+  const size_t per_stage = (size_t)a->stage_bytes + kStreamWarps * 32 * sizeof(float4) + 12;
   if (x_bytes + per_stage + 16 > (size_t)kStreamSmemBudget) return false;
-  int S = (int)((kStreamSmemBudget - x_bytes - 16) / per_stage);
-  S = std::max(1, std::min({S, 8, nrb_max}));
-  a.stages = S;
-  plan->a = a;
-  plan->grid = (rows + rpc - 1) / rpc;
-  plan->smem = (size_t)S * per_stage + x_bytes + 16;
+  long long S = (long long)((kStreamSmemBudget - x_bytes - 16) / per_stage);
+  S = std::max(1LL, std::min({S, 8LL, max_units_per_cta}));
+  a->stages = (int)S;
+  *smem = (size_t)S * per_stage + x_bytes + 16;
   return true;
 }
 
-static int launch_stream(StreamPlan &plan, const void *x, bool x_f32, void *y, bool y_bf16, cudaStream_t stream) {
-  plan.a.x = x;
-  plan.a.y = y;
-  plan.a.y_bf16 = y_bf16;
-  plan.a.error = device_error_ptr();
-  auto k = x_f32 ? gemv_nvfp4_stream_kernel<true> : gemv_nvfp4_stream_kernel<false>;
+// A segment the streaming kernel can read with 16-byte bulk copies: rows and
+// the first row a multiple of 4 (so every unit's factor and global copies are
+// whole 16-byte pieces) and aligned row pointers.
+static bool stream_segment_ok(const uint8_t *packed, const uint8_t *scales, const float *globals, long long rows) {
+  return rows > 0 && rows % 4 == 0 && rows <= 0x7fffffff && reinterpret_cast<uintptr_t>(packed) % 16 == 0 &&
+         reinterpret_cast<uintptr_t>(scales) % 16 == 0 && reinterpret_cast<uintptr_t>(globals) % 16 == 0;
+}
+
+template <int NSEG, int UR>
+static int launch_stream(const StreamArgs<NSEG> &a, int grid, size_t smem, bool x_f32, cudaStream_t stream) {
+  auto k = x_f32 ? gemv_nvfp4_stream_kernel<true, NSEG, UR> : gemv_nvfp4_stream_kernel<false, NSEG, UR>;
   {
     // Raised once per device and kernel to the budget, never lowered.
     static std::mutex mu;
@@ -877,28 +955,53 @@ static int launch_stream(StreamPlan &plan, const void *x, bool x_f32, void *y, b
     }
   }
   cudaLaunchConfig_t lc{};
-  lc.gridDim = dim3(plan.grid);
+  lc.gridDim = dim3(grid);
   lc.blockDim = dim3(kStreamWarps * 32);
-  lc.dynamicSmemBytes = plan.smem;
+  lc.dynamicSmemBytes = smem;
   lc.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   lc.attrs = attr;
   lc.numAttrs = 1;
-  cudaError_t le = cudaLaunchKernelEx(&lc, k, plan.a);
+  cudaError_t le = cudaLaunchKernelEx(&lc, k, a);
   if (le == cudaErrorInvalidValue) {
     cudaGetLastError();
     lc.numAttrs = 0;
-    le = cudaLaunchKernelEx(&lc, k, plan.a);
+    le = cudaLaunchKernelEx(&lc, k, a);
   }
   if (le != cudaSuccess) {
     cudaGetLastError();
-    return fail(FPB_ERR_CUDA, "cudaLaunchKernelEx(gemv_nvfp4_stream_kernel): %s; grid %d smem %zu stages %d",
-                cudaGetErrorName(le), plan.grid, plan.smem, plan.a.stages);
+    return fail(FPB_ERR_CUDA,
+                "cudaLaunchKernelEx(gemv_nvfp4_stream_kernel): %s; grid %d smem %zu stages %d segments %d",
+                cudaGetErrorName(le), grid, smem, a.stages, a.nseg);
   }
   FPB_LAUNCH_CHECK("gemv_nvfp4_stream_kernel");
   return FPB_OK;
+}
+
+// One matrix: one CTA per SM, each owning ceil(rows / SMs) rows rounded up to
+// 4, so that a CTA of the next launch in the stream fits beside it and
+// streams its weights while this launch computes.
+static int try_stream_single(const uint8_t *packed, const uint8_t *scales, const float *globals, int rows, int K,
+                             const void *x, bool x_f32, void *y, bool y_bf16, int batch, cudaStream_t stream,
+                             bool *served) {
+  *served = false;
+  if (!stream_segment_ok(packed, scales, globals, rows)) return FPB_OK;
+  StreamArgs<1> a{};
+  const int nsm = std::max(1, sm_count());
+  int rpc = (rows + nsm - 1) / nsm;
+  rpc = (rpc + 3) / 4 * 4;
+  size_t smem = 0;
+  if (!stream_geometry(K, batch, x_f32, 16, (rpc + 15) / 16, &a, &smem)) return FPB_OK;
+  a.seg[0] = StreamSeg{packed, scales, globals, x, y, 0, rows, 0};
+  a.nseg = 1;
+  a.rpc = rpc;
+  a.total_rows = rows;
+  a.error = device_error_ptr();
+  a.y_bf16 = y_bf16;
+  *served = true;
+  return launch_stream<1, 16>(a, (rows + rpc - 1) / rpc, smem, x_f32, stream);
 }
 
 }  // namespace fpb
@@ -931,9 +1034,10 @@ extern "C" int fpb_nvfp4_gemv(const fpb_nvfp4_matrix *w, size_t row_begin, size_
   a.y_bf16 = y_dtype == FPB_BF16;
   a.y_batch_stride = a.rows;
   const bool x_f32 = x_dtype == FPB_F32;
-  StreamPlan plan;
-  if (plan_stream(a.packed, a.scales, a.globals, a.rows, a.K, batch, x_f32, &plan))
-    return launch_stream(plan, x, x_f32, y, a.y_bf16 != 0, as_stream(stream));
+  bool served = false;
+  int st0 = try_stream_single(a.packed, a.scales, a.globals, a.rows, a.K, x, x_f32, y, a.y_bf16 != 0, batch,
+                              as_stream(stream), &served);
+  if (served || st0) return st0;
   // More input rows than one launch holds in registers run as several
   // launches over row groups of x (each re-reads W).
   const int step = std::min(batch, gemv_max_batch((int)w->cols, x_f32));
@@ -979,4 +1083,80 @@ extern "C" int fpb_nvfp4_expert_gemv(const fpb_nvfp4_matrix *w, const void *x, i
   a.x_slot_stride = (long long)input_stride * (long long)w->cols;
   a.y_slot_stride = (long long)rows_per_expert;
   return run_gemv(a, slots, x_dtype == FPB_F32, as_stream(stream));
+}
+
+// Several dense GEMVs in one launch (see fpb_nvfp4_gemv_batched in the
+// header).  Served by the streaming kernel over up to kStreamMaxSegs
+// segments, two CTAs per SM, each owning an equal share of the segments'
+// rows laid end to end; shapes it cannot take run as one fpb_nvfp4_gemv per
+// segment.
+extern "C" int fpb_nvfp4_gemv_batched(const fpb_gemv_segment *segs, int count, int x_dtype, int y_dtype,
+                                      int batch, void *stream) {
+  if (!segs || count < 1) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_gemv_batched: no segments");
+  if (count > kStreamMaxSegs)
+    return fail(FPB_ERR_UNSUPPORTED, "fpb_nvfp4_gemv_batched: %d segments exceed %d", count, kStreamMaxSegs);
+  if ((x_dtype != FPB_F32 && x_dtype != FPB_BF16) || (y_dtype != FPB_F32 && y_dtype != FPB_BF16))
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_gemv_batched: dtype");
+  if (batch < 1 || batch > 16)
+    return fail(FPB_ERR_SHAPE, "fpb_nvfp4_gemv_batched: batch %d not in [1, 16]", batch);
+  if (!segs[0].w) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_gemv_batched: null matrix in segment 0");
+  const size_t K = segs[0].w->cols;
+  for (int i = 0; i < count; ++i) {
+    const fpb_gemv_segment &sg = segs[i];
+    if (!sg.w || !sg.x || !sg.y)
+      return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_gemv_batched: null pointer in segment %d", i);
+    if (sg.w->cols != K)
+      return fail(FPB_ERR_SHAPE, "fpb_nvfp4_gemv_batched: segment %d has %zu columns, segment 0 has %zu", i,
+                  sg.w->cols, K);
+    const size_t end = sg.row_end ? sg.row_end : sg.w->rows;
+    if (sg.row_begin >= end || end > sg.w->rows)
+      return fail(FPB_ERR_SHAPE, "fpb_nvfp4_gemv_batched: segment %d row range [%zu, %zu) outside %zu rows", i,
+                  sg.row_begin, end, sg.w->rows);
+    if (reinterpret_cast<uintptr_t>(sg.x) % 16 != 0)
+      return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_gemv_batched: x of segment %d not 16-byte aligned", i);
+  }
+  const bool x_f32 = x_dtype == FPB_F32;
+  cudaStream_t s = as_stream(stream);
+
+  StreamArgs<kStreamMaxSegs> a{};
+  bool streamable = K <= 4096;
+  long long total = 0;
+  for (int i = 0; i < count && streamable; ++i) {
+    const fpb_gemv_segment &sg = segs[i];
+    const size_t end = sg.row_end ? sg.row_end : sg.w->rows;
+    const long long rows = (long long)(end - sg.row_begin);
+    const uint8_t *packed = sg.w->packed + sg.row_begin * (K / 2);
+    const uint8_t *scales = sg.w->scales + sg.row_begin * (K / kNvfp4Group);
+    const float *globals = sg.w->row_globals + sg.row_begin;
+    streamable = stream_segment_ok(packed, scales, globals, rows);
+    a.seg[i] = StreamSeg{packed, scales, globals, sg.x, sg.y, total, (int)rows, 0};
+    total += rows;
+  }
+  if (streamable) {
+    constexpr int unit_rows = 16;
+    const int grid_target = 2 * std::max(1, sm_count());
+    long long rpc = (total + grid_target - 1) / grid_target;
+    rpc = (rpc + 3) / 4 * 4;
+    size_t smem = 0;
+    // A CTA's rows split into at most one more unit per segment they touch;
+    // its ring never needs more stages than units.
+    streamable = rpc <= 0x7fffffff &&
+                 stream_geometry((int)K, batch, x_f32, unit_rows, (rpc + unit_rows - 1) / unit_rows + count, &a,
+                                 &smem);
+    if (streamable) {
+      a.nseg = count;
+      a.rpc = (int)rpc;
+      a.total_rows = total;
+      a.error = device_error_ptr();
+      a.y_bf16 = y_dtype == FPB_BF16;
+      const int grid = (int)((total + rpc - 1) / rpc);
+      return launch_stream<kStreamMaxSegs, unit_rows>(a, grid, smem, x_f32, s);
+    }
+  }
+  for (int i = 0; i < count; ++i) {
+    const fpb_gemv_segment &sg = segs[i];
+    int st = fpb_nvfp4_gemv(sg.w, sg.row_begin, sg.row_end, sg.x, x_dtype, sg.y, y_dtype, batch, stream);
+    if (st) return st;
+  }
+  return FPB_OK;
 }

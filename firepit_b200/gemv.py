@@ -118,6 +118,49 @@ def gemv(weight, x, y, tile: GemvTile = DEFAULT_GEMV_TILE, rows: range | None = 
     return Gemv(weight, x, y, tile, rows)
 
 
+class BatchedGemv:
+    """Several NVFP4 decode GEMVs in one launch (fpb_nvfp4_gemv_batched).
+
+    The reference saves decode launches by stacking the projections that
+    read one input into a single matrix at load time (firepit
+    src/model.rs:407-444); here each ``(weight, x, y[, rows])`` keeps its own
+    handle and input, and every member's result equals ``gemv(weight, x, y,
+    rows=rows)``.  All members share the column count, dtypes and batch."""
+
+    def __init__(self, members, tile: GemvTile = DEFAULT_GEMV_TILE):
+        if not members:
+            raise ShapeError("batched GEMV: no members")
+        self.gemvs = [Gemv(m[0], m[1], m[2], tile, m[3] if len(m) > 3 else None) for m in members]
+        first = self.gemvs[0]
+        for g in self.gemvs:
+            if _is_fp8(g.weight):
+                raise ShapeError("batched GEMV: NVFP4 weights only")
+            if g.weight.cols != first.weight.cols or g.x.shape[0] != first.x.shape[0]:
+                raise ShapeError("batched GEMV: members differ in columns or batch")
+            if g.x.dtype != first.x.dtype or g.y.dtype != first.y.dtype:
+                raise ShapeError("batched GEMV: members differ in dtypes")
+        arr = (N.GemvSegment * len(self.gemvs))()
+        for i, g in enumerate(self.gemvs):
+            arr[i] = N.GemvSegment(g.weight.handle.value, g.rows.start, g.rows.stop, g.x.data_ptr(),
+                                   g.y.data_ptr())
+        self._segs = arr
+
+    def submit(self, sink: Sink | None = None) -> None:
+        sink = sink or Eager()
+        first = self.gemvs[0]
+
+        def launch(stream):
+            N.call("fpb_nvfp4_gemv_batched", self._segs, len(self.gemvs), _dtype_code(first.x),
+                   _dtype_code(first.y), first.x.shape[0], stream)
+
+        sink.run("gemv_batched", launch)
+
+
+def gemv_batched(members, tile: GemvTile = DEFAULT_GEMV_TILE) -> BatchedGemv:
+    """members: ``(weight, x, y)`` or ``(weight, x, y, rows)`` tuples."""
+    return BatchedGemv(members, tile)
+
+
 class ExpertGemvView:
     """gemv/mod.rs:126-206 for ``Weight::Nvfp4`` or ``Weight::Fp8``
     (gemv/fp8.rs:248-281)."""
@@ -156,5 +199,6 @@ def expert_gemv_weight_view(weight, x, selection, y, rows_per_expert: int, input
     return ExpertGemvView(weight, x, selection, y, rows_per_expert, input_stride, tile)
 
 
-__all__ = ["GemvTile", "DEFAULT_GEMV_TILE", "fp8_tile", "row_scaled_tile", "gemv", "Gemv",
+__all__ = ["GemvTile", "DEFAULT_GEMV_TILE", "fp8_tile", "row_scaled_tile", "gemv", "Gemv", "gemv_batched",
+           "BatchedGemv",
            "expert_gemv_weight_view", "ExpertGemvView", "ShapeError", "current_stream_handle"]

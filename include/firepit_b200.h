@@ -159,6 +159,29 @@ int fpb_nvfp4_gemv(const fpb_nvfp4_matrix *w, size_t row_begin, size_t row_end,
                    const void *x, int x_dtype, void *y, int y_dtype, int batch,
                    void *stream);
 
+/* Several dense NVFP4 GEMVs in one launch.  Replaces what the reference does
+ * at load time to save launches on decode: it stacks projections that read
+ * the same input into one matrix (stack_group, firepit src/model.rs:407-444;
+ * measured in docs/research/measurements/gemv-probe-gb10.md:98-102, which
+ * also notes that independent GEMVs could not run concurrently there).  Here
+ * the matrices stay separate handles: segment i computes
+ *   segs[i].y[b, r - row_begin] = GEMV of rows [row_begin, row_end) of
+ *   segs[i].w with segs[i].x[b, :]
+ * as fpb_nvfp4_gemv does, with its own x [batch, cols] and y [batch,
+ * row_end - row_begin] (x may be shared).  All segments have the same cols;
+ * 1 <= count <= 128, 1 <= batch <= 16.  One launch when cols % 128 == 0,
+ * cols <= 4096, batch <= 8 and every segment's row_begin and row count are
+ * multiples of 4; otherwise one fpb_nvfp4_gemv launch per segment.  `segs`
+ * is read on the host during the call only. */
+typedef struct fpb_gemv_segment {
+  const fpb_nvfp4_matrix *w;
+  size_t row_begin, row_end; /* row_end == 0: all rows */
+  const void *x;
+  void *y;
+} fpb_gemv_segment;
+int fpb_nvfp4_gemv_batched(const fpb_gemv_segment *segs, int count, int x_dtype, int y_dtype, int batch,
+                           void *stream);
+
 /* expert_gemv_weight_view(&Weight::Nvfp4, x, selection, y, rows_per_expert,
  * input_stride, tile) (gemv/mod.rs:137-206 -> gemv/nvfp4.rs:151-182,
  * kernel :62-107).  For slot s in [0, slots):

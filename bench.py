@@ -2,19 +2,26 @@
 
 Default workload ("gemv"): NVFP4 decode GEMV, W [4096 x
 4096] from N(0, 0.02) quantized to NVFP4 (one global per matrix), x bf16
-[1, 4096] from N(0, 1) seed 0, y bf16.  One step is one decode-style sweep
-over 64*g distinct weight matrices (g = number of GPUs): each matrix is split
-along N (rows) over the g ranks, every rank computes its row slice of all
-64*g GEMVs and the slices are all-gathered once per step (NCCL).  Each rank
-therefore streams 64 * 9.45 MB = 605 MB of weights per step at every g
-(inputs larger than L2: nothing is re-read from L2 across steps); per-GPU work
-is fixed as g grows ("weak").
+rows from N(0, 1) seed 0, y bf16.  One step is one decode-style sweep over
+64*g distinct weight matrices (g = number of GPUs), each with its own x row:
+every matrix is split along N (rows) over the g ranks; each rank computes its
+row slices of all 64*g GEMVs with batched launches (fpb_nvfp4_gemv_batched, at
+most 128 matrices' slices per launch) and the slices of each launch group are
+all-gathered after it (NCCL).  Each rank streams 64 * 9.45 MB = 605 MB of
+weights per step at every g (inputs larger than L2); per-GPU work is fixed as
+g grows ("weak").
 
   value  device-resident GB/s (algorithmic bytes of all ranks / max step time),
-         the step replayed as one CUDA graph per rank;
-  e2e    the same metric through the public Python API (firepit_b200.gemv,
-         ctypes C ABI) with x copied from pinned host memory each step and y
-         copied back, no graph.
+         the launches replayed as CUDA graphs;
+  e2e    the same metric through the public Python API
+         (firepit_b200.gemv_batched(...).submit(Graph sink)) with x copied from
+         pinned host memory each step and y copied back.
+
+The default line also carries "sub_records" for the other BASELINE configs
+(config 1 FP8 GEMM; config 2 NVFP4 GEMM at M = 1, 16, 128, 2048; config 3 MoE
+layer at T = 64 and 4096 on one GPU, expert-parallel over the ranks when g >
+1), each with its own roofline, cpu_baseline (rank 0, one GPU), e2e and clocks;
+--no-sub leaves them out, --config runs one of them as the main line.
 
 --impl reference times the reference's host path (the CPU restatement of
 kernels src/gemv/nvfp4.rs:34-59 in oracle/, OpenMP over all host cores) on a
@@ -46,12 +53,16 @@ def parse_args():
     p.add_argument("--steps", type=int, default=2000)
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--config", choices=["gemv", "nvfp4_gemm_m128", "nvfp4_gemm_m2048", "fp8_gemm", "moe_t4096",
-                                        "moe_t64", "moe_ep"], default="gemv",
-                   help="gemv: config 0 (default); nvfp4_gemm_m*: config 2 GEMM at M=128 / M=2048; "
-                        "fp8_gemm: config 1; moe_t*: config 3 MoE layer at T=4096 / T=64; "
-                        "moe_ep: config 3 expert-parallel over the ranks (NCCL all-to-all), T=4096 per rank")
-    p.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the cpu_baseline sample")
+    p.add_argument("--config", choices=["gemv", "nvfp4_gemm_m1", "nvfp4_gemm_m16", "nvfp4_gemm_m128",
+                                        "nvfp4_gemm_m2048", "fp8_gemm", "moe_t4096", "moe_t64", "moe_ep"],
+                   default="gemv",
+                   help="gemv: config 0 (default); nvfp4_gemm_m*: config 2 at M=1 / 16 (decode GEMV entry) and "
+                        "M=128 / 2048 (tcgen05 GEMM); fp8_gemm: config 1; moe_t*: config 3 MoE layer at T=4096 / "
+                        "T=64; moe_ep: config 3 expert-parallel over the ranks (NCCL all-to-all), T=4096 per rank")
+    p.add_argument("--cpu-seconds", type=float, default=10.0, help="budget of the cpu_baseline sample")
+    p.add_argument("--no-sub", action="store_true", help="default line without the other configs' sub-records")
+    p.add_argument("--sub-steps", type=int, default=20, help="timed steps of each sub-record")
+    p.add_argument("--sub-cpu-seconds", type=float, default=3.0, help="cpu_baseline budget of each sub-record")
     return p.parse_args()
 
 
@@ -61,6 +72,68 @@ def dist_env():
 
 def emit(obj):
     print(json.dumps(obj), flush=True)
+
+
+_DIST = {}
+
+
+def dist_init():
+    """(rank, world, local_rank, device) with the NCCL process group set up
+    once per process (short timeout, so ranks that wait on each other end
+    with an error instead of hanging)."""
+    import torch
+    import torch.distributed as dist
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1 and not _DIST:
+        from datetime import timedelta
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+        _DIST["up"] = True
+    return rank, world, local, dev
+
+
+def comm():
+    """The library's NCCL communicator (fpb_comm_*) for this process, made
+    once after the torch.distributed group (which only hands out rank 0's
+    unique id); None on one GPU."""
+    if not _DIST:
+        return None
+    if "comm" not in _DIST:
+        from firepit_b200.comm import Comm
+        _DIST["comm"] = Comm.from_torch()
+    return _DIST["comm"]
+
+
+def dist_sync():
+    import torch.distributed as dist
+    if _DIST:
+        dist.barrier()
+
+
+def dist_finish():
+    import torch.distributed as dist
+    if _DIST:
+        dist.barrier()
+        if "comm" in _DIST:
+            _DIST["comm"].destroy()
+        dist.destroy_process_group()
+        _DIST.clear()
+
+
+def use_all_cores():
+    """The CPU legs use every host core: under torch.distributed.run the
+    launcher sets OMP_NUM_THREADS=1 for each rank."""
+    n = os.cpu_count() or 1
+    from oracle import oracle as O
+    O.set_num_threads(n)
+    return n
+
+
+def peaks_json():
+    f = ROOT / "MEASURED_PEAKS.json"
+    return json.loads(f.read_text()) if f.exists() else {}
 
 
 # ---- clocks -------------------------------------------------------------------------------
@@ -112,13 +185,25 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(loaded)}
 
 
-# ---- reference arm -------------------------------------------------------------------------
+# ---- config 0 -----------------------------------------------------------------------------
+MAX_SEGS = 128  # fpb_nvfp4_gemv_batched's segments per launch
+
+
+def gemv_config(g: int) -> dict:
+    return {"workload": "config0 NVFP4 GEMV 4096x4096 (x bf16 [1,4096] N(0,1), y bf16)",
+            "matrices_per_step": MATS_PER_GPU * g, "rows_per_rank": ROWS // g,
+            "launch": f"each rank's slices of the {MATS_PER_GPU * g} matrices in batched launches of at most "
+                      f"{MAX_SEGS} (fpb_nvfp4_gemv_batched), every matrix with its own x row",
+            "parallelism": f"N-split x{g} + NCCL all-gather after each launch" if g > 1 else "single GPU",
+            "l2": "inputs larger than L2: 605 MB of distinct weights per rank per step",
+            "timing": "CUDA graph replay per launch, CUDA events, max over ranks"}
+
+
 def reference_arm(args):
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    import numpy as np
-
+    cores = use_all_cores()
     from oracle import oracle as O
     w = O.synth_normal(ROWS * COLS, seed=0, stream=1, std=0.02).reshape(ROWS, COLS)
     packed, scales, g = O.nvfp4_quantize(w)
@@ -139,13 +224,12 @@ def reference_arm(args):
     dt = (time.perf_counter() - t0) / max(args.steps, 1)
     bytes_ = rows * COLS // 2 + rows * COLS // 16 + 4 + COLS * 2 + rows * 2
     gbs = bytes_ / dt / 1e9
-    cores = O.num_threads()
-    sample = f"{rows} of {ROWS} rows of one {ROWS}x{COLS} NVFP4 GEMV per step (oracle f32 kernel order, OpenMP)"
+    sample = (f"{rows} of {ROWS} rows of one {ROWS}x{COLS} NVFP4 GEMV per step (oracle f32 kernel order, OpenMP "
+              f"on {cores} threads)")
     emit({"impl": "reference", "metric": "NVFP4 GEMV HBM GB/s", "value": gbs, "unit": "GB/s", "n_gpus": args.gpus,
           "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
           "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded Philox N(0,1)/N(0,0.02))",
-          "config": {"workload": "config0 NVFP4 GEMV 4096x4096, x bf16 [1,4096] N(0,1) seed 0, W N(0,0.02)",
-                     "sample_rows": rows},
+          "config": gemv_config(args.gpus),
           "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample},
           "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
 
@@ -153,6 +237,7 @@ def reference_arm(args):
 def cpu_baseline(seconds: float):
     """The reference's host path (oracle port) on this box's cores: full
     config-0 GEMVs repeated for about `seconds`."""
+    cores = use_all_cores()
     from oracle import oracle as O
     w = O.synth_normal(ROWS * COLS, seed=0, stream=1, std=0.02).reshape(ROWS, COLS)
     packed, scales, g = O.nvfp4_quantize(w)
@@ -163,15 +248,14 @@ def cpu_baseline(seconds: float):
         O.nvfp4_gemv_f32(packed, scales, g, ROWS, COLS, x)
         n += 1
     dt = (time.perf_counter() - t0) / n
-    return {"value": GEMV_BYTES / dt / 1e9, "unit": "GB/s", "cores": O.num_threads(), "kind": "port",
+    return {"value": GEMV_BYTES / dt / 1e9, "unit": "GB/s", "cores": cores, "kind": "port",
             "sample": f"{n} full 4096x4096 NVFP4 GEMVs (oracle f32 kernel order, OpenMP), {dt * 1e3:.2f} ms each"}
 
 
-# ---- our arm ---------------------------------------------------------------------------------
-def load_traffic():
-    """DRAM bytes per GEMV launch from the committed ncu summary (first line:
+def load_traffic(name: str):
+    """DRAM bytes per launch from a committed ncu summary (first line:
     `dram_bytes_per_launch <bytes>`), or None."""
-    f = ROOT / "profiles" / "gemv_nvfp4_config0_traffic.txt"
+    f = ROOT / "profiles" / name
     if f.exists():
         try:
             key, val = f.read_text().split("\n", 1)[0].split()
@@ -191,18 +275,22 @@ def measured_peak():
     return 6650.0, "fallback"
 
 
+def graph_of(torch, fn, stream):
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        fn(torch.cuda.current_stream().cuda_stream)
+    return g
+
+
 def ours_arm(args):
     import torch
     import torch.distributed as dist
 
     import firepit_b200 as F
+    N_ = F._native
+    BF = N_.FPB_BF16
 
-    rank, world, local = dist_env()
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    rank, world, local, dev = dist_init()
     g = world
     mats = MATS_PER_GPU * g
     rows_per_rank = ROWS // g
@@ -220,43 +308,45 @@ def ours_arm(args):
                                                 globals_[r0:r0 + rows_per_rank].contiguous(), rows_per_rank, COLS))
         del packed, scales, globals_
     torch.cuda.synchronize()
-    x = F.synth_normal((1, COLS), seed=0, stream_id=0, dtype=torch.bfloat16, device=dev)
+    # x row c (of one seed-0 N(0,1) stream) is matrix c's input; row 0 is config 0's x.
+    x = F.synth_normal((mats, COLS), seed=0, stream_id=0, dtype=torch.bfloat16, device=dev)
     y_local = torch.empty(mats, rows_per_rank, dtype=torch.bfloat16, device=dev)
-    y_all = torch.empty(g, mats, rows_per_rank, dtype=torch.bfloat16, device=dev)
+    groups = [range(i, min(i + MAX_SEGS, mats)) for i in range(0, mats, MAX_SEGS)]
+    y_all = [torch.empty(g, len(gr), rows_per_rank, dtype=torch.bfloat16, device=dev) for gr in groups]
 
-    def gemvs(stream_handle):
-        for c in range(mats):
-            F._native.call("fpb_nvfp4_gemv", slices[c].handle, 0, 0, x.data_ptr(), F._native.FPB_BF16,
-                           y_local[c].data_ptr(), F._native.FPB_BF16, 1, stream_handle)
+    def batched(xsrc):
+        return [F.gemv_batched([(slices[c], xsrc[c:c + 1], y_local[c:c + 1]) for c in gr]) for gr in groups]
 
-    # warm every code path once outside capture
+    launches_b = batched(x)
+
+    def launch(i, sh):
+        N_.call("fpb_nvfp4_gemv_batched", launches_b[i]._segs, len(groups[i]), BF, BF, 1, sh)
+
     s = torch.cuda.Stream(device=dev)
-    with torch.cuda.stream(s):
-        gemvs(s.cuda_stream)
+    with torch.cuda.stream(s):  # every code path initialised outside capture
+        for i in range(len(groups)):
+            launch(i, s.cuda_stream)
     torch.cuda.synchronize()
-    launches_before = F.launch_count()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=s):
-        gemvs(torch.cuda.current_stream().cuda_stream)
-    launches_per_step = F.launch_count() - launches_before
+    before = F.launch_count()
+    graphs = [graph_of(torch, lambda sh, i=i: launch(i, sh), s) for i in range(len(groups))]
+    launches_per_step = F.launch_count() - before
 
-    def step(timing=None):
-        if timing is not None:
-            timing[0].record()
-        graph.replay()
-        if timing is not None:
-            timing[1].record()
-        if g > 1:
-            dist.all_gather_into_tensor(y_all, y_local)
-        if timing is not None:
-            timing[2].record()
+    def step(ev=None):
+        for i, gr in enumerate(graphs):
+            if ev is not None:
+                ev[2 * i].record()
+            gr.replay()
+            if ev is not None:
+                ev[2 * i + 1].record()
+            if g > 1:
+                comm().all_gather_into(y_all[i], y_local[groups[i].start:groups[i].stop])
 
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize()
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
-    if g > 1:
-        dist.barrier()
+    ng = len(groups)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2 * ng)] for _ in range(args.steps)]
+    dist_sync()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
@@ -266,47 +356,74 @@ def ours_arm(args):
         end.record()
         torch.cuda.synchronize()
     total_ms = start.elapsed_time(end)
-    gemv_ms = sum(e[0].elapsed_time(e[1]) for e in evs)
-    gather_ms = sum(e[1].elapsed_time(e[2]) for e in evs)
-    t = torch.tensor([total_ms, gemv_ms, gather_ms], device=dev, dtype=torch.float64)
+    gemv_ms = sum(e[2 * i].elapsed_time(e[2 * i + 1]) for e in evs for i in range(ng))
+    t = torch.tensor([total_ms, gemv_ms], device=dev, dtype=torch.float64)
     if g > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    total_ms, gemv_ms, gather_ms = t.tolist()
+    total_ms, gemv_ms = t.tolist()
     ms_per_step = total_ms / args.steps
     total_bytes = mats * GEMV_BYTES  # all ranks together, per step
     value = total_bytes / (ms_per_step * 1e-3) / 1e9
 
+    # ---- one launch per GEMV (the single-matrix entry fpb_nvfp4_gemv) --------
+    single_n = min(mats, MATS_PER_GPU)
+
+    def singles(sh):
+        for c in range(single_n):
+            N_.call("fpb_nvfp4_gemv", slices[c].handle, 0, 0, x[c].data_ptr(), BF, y_local[c].data_ptr(), BF, 1, sh)
+
+    with torch.cuda.stream(s):
+        singles(s.cuda_stream)
+    torch.cuda.synchronize()
+    gs = graph_of(torch, singles, s)
+    for _ in range(3):
+        gs.replay()
+    torch.cuda.synchronize()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    single_steps = max(1, min(args.steps, 200))
+    s0.record()
+    for _ in range(single_steps):
+        gs.replay()
+    s1.record()
+    torch.cuda.synchronize()
+    ts = torch.tensor([s0.elapsed_time(s1)], device=dev, dtype=torch.float64)
+    if g > 1:
+        dist.all_reduce(ts, op=dist.ReduceOp.MAX)
+    single_launch_ms = ts.item() / (single_steps * single_n)
+    del gs
+
     # ---- end to end through the public API, host buffers ----------------------
     # The reference's Graph sink (sink.rs:94-105): one CUDA graph holds the
-    # copy of x from pinned host memory, the `gemv(...).submit(sink)` calls
-    # and (one GPU) the copy of y back to pinned host memory.
-    xh = torch.empty(1, COLS, dtype=torch.bfloat16, pin_memory=True)
+    # copy of x from pinned host memory, the batched GEMV submits and (one
+    # GPU) the copy of y back to pinned host memory.
+    xh = torch.empty(mats, COLS, dtype=torch.bfloat16, pin_memory=True)
     xh.copy_(x.cpu())
     yh = torch.empty(g, mats, rows_per_rank, dtype=torch.bfloat16, pin_memory=True)
     xd = torch.empty_like(x)
-    for c in range(mats):  # eager once: every code path initialised outside capture
-        F.gemv(slices[c], x, y_local[c:c + 1], F.DEFAULT_GEMV_TILE).submit(F.Async())
+    e2e_b = batched(xd)
+    for b in e2e_b:  # eager once: every code path initialised outside capture
+        b.submit(F.Async())
     torch.cuda.synchronize()
     gsink = F.Graph()
     with gsink:
         xd.copy_(xh, non_blocking=True)
-        for c in range(mats):
-            F.gemv(slices[c], xd, y_local[c:c + 1], F.DEFAULT_GEMV_TILE).submit(gsink)
+        for b in e2e_b:
+            b.submit(gsink)
         if g == 1:
             yh[0].copy_(y_local, non_blocking=True)
 
     def e2e_step():
         gsink.replay()
         if g > 1:
-            dist.all_gather_into_tensor(y_all, y_local)
-            yh.copy_(y_all, non_blocking=True)
+            for i, gr in enumerate(groups):
+                comm().all_gather_into(y_all[i], y_local[gr.start:gr.stop])
+                yh[:, gr.start:gr.stop].copy_(y_all[i], non_blocking=True)
 
     e2e_steps = max(1, min(args.steps, 50))
     for _ in range(3):
         e2e_step()
     torch.cuda.synchronize()
-    if g > 1:
-        dist.barrier()
+    dist_sync()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(e2e_steps):
@@ -318,43 +435,48 @@ def ours_arm(args):
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_value = total_bytes / (te.item() / e2e_steps * 1e-3) / 1e9
 
-    per_launch_ms = gemv_ms / (args.steps * mats)
-    launch_bytes = rows_per_rank * COLS // 2 + rows_per_rank * COLS // 16 + 4 + COLS * 2 + rows_per_rank * 2
+    slice_bytes = rows_per_rank * COLS // 2 + rows_per_rank * COLS // 16 + 4 + COLS * 2 + rows_per_rank * 2
+    launch_bytes = len(groups[0]) * slice_bytes
+    per_launch_ms = gemv_ms / (args.steps * ng)
     peak, peak_kind = measured_peak()
     achieved = launch_bytes / (per_launch_ms * 1e-3) / 1e9
-    traffic = load_traffic() if g == 1 else None
+    single_achieved = slice_bytes / (single_launch_ms * 1e-3) / 1e9
+    traffic = None
+    if g == 1:
+        per_matrix = load_traffic("gemv_nvfp4_batched_config0_traffic.txt")
+        traffic = per_matrix * len(groups[0]) if per_matrix else None
+    out = None
     if rank == 0:
         out = {
             "metric": "NVFP4 GEMV HBM GB/s", "value": value, "unit": "GB/s", "n_gpus": g, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "e2m1xe4m3 weights, bf16 x/y, f32 accumulate",
             "data": "synthetic (seeded Philox: W N(0,0.02), x N(0,1) seed 0)",
-            "config": {"workload": "config0 NVFP4 GEMV 4096x4096 (x bf16 [1,4096], y bf16)",
-                       "matrices_per_step": mats, "rows_per_rank": rows_per_rank,
-                       "parallelism": f"N-split x{g} + NCCL all-gather" if g > 1 else "single GPU",
-                       "l2": "inputs larger than L2: 605 MB of distinct weights per rank per step",
-                       "timing": "CUDA graph replay per step, CUDA events, max over ranks"},
+            "config": gemv_config(g),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
                          "peak_kind": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)" if peak_kind == "measured"
                          else "fallback 6650 GB/s",
-                         "per_launch_us": per_launch_ms * 1e3,
-                         "note": "per-launch time = GEMV region / launches (inter-kernel gaps included)"},
-            "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": COLS * 2,
+                         "per_launch_us": per_launch_ms * 1e3, "algorithmic_bytes_per_launch": launch_bytes,
+                         "note": "dominant kernel gemv_nvfp4_stream_kernel; one launch = the rank's slices of "
+                                 f"{len(groups[0])} matrices; traffic = ncu DRAM bytes per matrix x matrices"},
+            "single_gemv": {"per_launch_us": single_launch_ms * 1e3, "achieved_gbs": single_achieved,
+                            "frac": single_achieved / peak,
+                            "note": f"{single_n} fpb_nvfp4_gemv launches (one matrix slice each) in one CUDA graph"},
+            "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": mats * COLS * 2,
                     "d2h_bytes_per_step": g * mats * rows_per_rank * 2,
-                    "path": "firepit_b200.gemv(...).submit(Graph sink): H2D x, the GEMVs and D2H y in one CUDA "
-                            "graph" + (" + NCCL all-gather" if g > 1 else "")},
+                    "path": "firepit_b200.gemv_batched(...).submit(Graph sink): H2D x, the batched GEMVs and D2H y "
+                            "in one CUDA graph" + (" + NCCL all-gathers" if g > 1 else "")},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks.summary(),
-            "breakdown_ms": {"gemv": gemv_ms / args.steps, "all_gather": gather_ms / args.steps},
+            "breakdown_ms": {"gemv": gemv_ms / args.steps,
+                             "all_gather": (total_ms - gemv_ms) / args.steps if g > 1 else 0.0},
         }
-        if g == 1:
+        if g == 1 and args.cpu_seconds > 0:
             out["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
-        emit(out)
-    del graph, gsink
-    if g > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    del graphs, gsink
+    dist_sync()
+    return out
 
 
 # ---- config 2: NVFP4 GEMM (tcgen05) ------------------------------------------------------
@@ -362,7 +484,7 @@ GEMM_N, GEMM_K, GEMM_MATS = 8192, 2048, 16
 
 
 def gemm_shape(args):
-    return 128 if args.config.endswith("m128") else 2048
+    return int(args.config.rsplit("_m", 1)[1])
 
 
 def gemm_bytes(m, n, k):
@@ -371,43 +493,196 @@ def gemm_bytes(m, n, k):
     return n * k // 2 + n * k // 16 + 4 * n + m * k // 2 + m * k // 16 + 2 * m * n
 
 
-def gemm_reference_arm(args):
-    """The host path restated: dequantize both NVFP4 operands and multiply in
-    f32 (numpy/BLAS on all host cores), on a sample of activation rows."""
-    rank, _, _ = dist_env()
-    if rank != 0:
-        return
+def gemv_batch_bytes(m, n, k):
+    """Algorithmic bytes of one decode-GEMV launch of m input rows (the M <= 16
+    cases of config 2): weight codes, factors and row globals, x and y bf16."""
+    return n * k // 2 + n * k // 16 + 4 * n + 2 * m * k + 2 * m * n
+
+
+def gemm_config(m: int, g: int) -> dict:
+    if m <= 16:
+        how = (f"x bf16 [{m},2048] through the decode GEMV entry (fpb_nvfp4_gemv_batched over the 16 matrices, "
+               f"batch {m}); weights NVFP4, x kept in bf16 (W4A16)")
+    else:
+        how = "x bf16 quantized on the device to NVFP4 (W4A4), tcgen05 block-scaled GEMM"
+    return {"workload": f"config2 NVFP4 GEMM M={m} K=2048 N=8192, {how}",
+            "matrices_per_step": GEMM_MATS, "n_per_rank": GEMM_N // g,
+            "l2": "inputs larger than L2 (16 distinct weights, 151 MB per step at one GPU)",
+            "parallelism": f"N-split x{g} + NCCL all-gather" if g > 1 else "single GPU"}
+
+
+def gemm_cpu_sample(m: int, seconds: float):
+    """The host path restated on a bounded sample: the oracle's f32 kernel-order
+    GEMV (M <= 16, gemv/nvfp4.rs:34-59) or dequantized NVFP4 operands times
+    each other in f32 BLAS (M >= 128).  Returns (value, sample, cores); value in
+    GB/s for M <= 16, TFLOP/s otherwise."""
+    cores = use_all_cores()
     import numpy as np
 
     from oracle import oracle as O
-    m = gemm_shape(args)
     w = O.synth_normal(GEMM_N * GEMM_K, seed=0, stream=1, std=0.02).reshape(GEMM_N, GEMM_K)
     pw, sw, gw = O.nvfp4_quantize(w)
-    wd = O.nvfp4_dequantize(pw, sw, gw, GEMM_N, GEMM_K)
     x = O.bf16_to_f32(O.bf16_bits(O.synth_normal(m * GEMM_K, seed=0, stream=0))).reshape(m, GEMM_K)
-    pa, sa, ga = O.nvfp4_quantize(x)
-    xd = O.nvfp4_dequantize(pa, sa, ga, m, GEMM_K)
-    rows = min(m, 32)
-    t0 = time.perf_counter()
-    _ = xd[:rows] @ wd.T
-    one = max(time.perf_counter() - t0, 1e-4)
-    budget = 60.0 / max(args.steps + args.warmup, 1)
-    rows = max(1, min(m, int(rows * budget / one)))
-    for _ in range(args.warmup):
-        _ = xd[:rows] @ wd.T
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        _ = xd[:rows] @ wd.T
-    dt = (time.perf_counter() - t0) / max(args.steps, 1)
-    tflops = 2.0 * rows * GEMM_N * GEMM_K / dt / 1e12
-    sample = f"{rows} of {m} activation rows x W[{GEMM_N},{GEMM_K}] per step, dequantized NVFP4, f32 BLAS"
-    emit({"impl": "reference", "metric": "NVFP4 GEMM TFLOPS", "value": tflops, "unit": "TFLOP/s",
-          "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
-          "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-          "data": "synthetic (seeded Philox)", "config": {"workload": f"config2 NVFP4 GEMM M={m} K=2048 N=8192"},
-          "cpu_baseline": {"value": tflops, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
+    if m <= 16:
+        fn = lambda: O.nvfp4_gemv_f32(pw, sw, gw, GEMM_N, GEMM_K, x)
+    else:
+        wd = O.nvfp4_dequantize(pw, sw, gw, GEMM_N, GEMM_K)
+        pa, sa, ga = O.nvfp4_quantize(x)
+        xd = O.nvfp4_dequantize(pa, sa, ga, m, GEMM_K)
+        rows = min(m, 128)
+        fn = lambda: xd[:rows] @ wd.T
+    fn()
+    n, t0 = 0, time.perf_counter()
+    while n < 2 or time.perf_counter() - t0 < seconds:
+        fn()
+        n += 1
+    dt = (time.perf_counter() - t0) / n
+    if m <= 16:
+        return (gemv_batch_bytes(m, GEMM_N, GEMM_K) / dt / 1e9,
+                f"{n} x one W[8192,2048] NVFP4 GEMV of {m} rows (oracle f32 kernel order, OpenMP)", cores)
+    rows = min(m, 128)
+    return (2.0 * rows * GEMM_N * GEMM_K / dt / 1e12,
+            f"{n} x ({rows} of {m} activation rows x W[8192,2048]^T), dequantized NVFP4, f32 BLAS", cores)
+
+
+def gemm_reference_arm(args):
+    """The host path restated (gemm_cpu_sample) on the box's cores, rank 0 only."""
+    rank, _, _ = dist_env()
+    if rank != 0:
+        return
+    m = gemm_shape(args)
+    budget = min(60.0, max(5.0, 0.5 * (args.steps + args.warmup)))
+    v, sample, cores = gemm_cpu_sample(m, budget)
+    gbs = m <= 16
+    ms = (gemv_batch_bytes(m, GEMM_N, GEMM_K) / (v * 1e9) if gbs else 2.0 * m * GEMM_N * GEMM_K / (v * 1e12)) * 1e3
+    emit({"impl": "reference", "metric": "NVFP4 GEMM HBM GB/s" if gbs else "NVFP4 GEMM TFLOPS", "value": v,
+          "unit": "GB/s" if gbs else "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+          "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+          "data": "synthetic (seeded Philox)", "config": gemm_config(m, args.gpus),
+          "cpu_baseline": {"value": v, "unit": "GB/s" if gbs else "TFLOP/s", "cores": cores, "kind": "port",
                            "sample": sample},
-          "e2e": {"value": tflops, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
+          "e2e": {"value": v, "unit": "GB/s" if gbs else "TFLOP/s", "h2d_bytes_per_step": 0,
+                  "d2h_bytes_per_step": 0}})
+
+
+def gemm_small_arm(args):
+    """Config 2 at M = 1 and 16: x bf16 [M, 2048] N(0,1) times 16 distinct NVFP4
+    weights [8192, 2048] (N-split over the ranks) through the decode GEMV entry,
+    one batched launch per step (batch M); HBM-bound."""
+    import torch
+    import torch.distributed as dist
+
+    import firepit_b200 as F
+    N_ = F._native
+    BF = N_.FPB_BF16
+    rank, world, local, dev = dist_init()
+    g = world
+    m = gemm_shape(args)
+    n_rank = GEMM_N // g
+    r0 = rank * n_rank
+    mats = []
+    for c in range(GEMM_MATS):
+        w = F.synth_normal((GEMM_N, GEMM_K), seed=0, stream_id=1 + c, std=0.02, device=dev)
+        packed, scales, globals_ = F.quantize_nvfp4(w)
+        del w
+        mats.append(F.Nvfp4Matrix.from_device(packed[r0:r0 + n_rank].contiguous(),
+                                              scales[r0:r0 + n_rank].contiguous(),
+                                              globals_[r0:r0 + n_rank].contiguous(), n_rank, GEMM_K))
+    x = F.synth_normal((m, GEMM_K), seed=0, stream_id=0, dtype=torch.bfloat16, device=dev)
+    ys = torch.empty(GEMM_MATS, m, n_rank, dtype=torch.bfloat16, device=dev)
+    y_all = torch.empty(g, GEMM_MATS, m, n_rank, dtype=torch.bfloat16, device=dev)
+    bat = F.gemv_batched([(mats[c], x, ys[c]) for c in range(GEMM_MATS)])
+
+    def launch(sh):
+        N_.call("fpb_nvfp4_gemv_batched", bat._segs, GEMM_MATS, BF, BF, m, sh)
+
+    s = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(s):
+        launch(s.cuda_stream)
+    torch.cuda.synchronize()
+    before = F.launch_count()
+    gr = graph_of(torch, launch, s)
+    launches_per_step = F.launch_count() - before
+
+    def step(ev=None):
+        if ev:
+            ev[0].record()
+        gr.replay()
+        if ev:
+            ev[1].record()
+        if g > 1:
+            comm().all_gather_into(y_all, ys)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
+    dist_sync()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record()
+        for i in range(args.steps):
+            step(evs[i])
+        end.record()
+        torch.cuda.synchronize()
+    t = torch.tensor([start.elapsed_time(end), sum(e[0].elapsed_time(e[1]) for e in evs)], device=dev,
+                     dtype=torch.float64)
+    if g > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms, gemv_ms = t.tolist()
+    ms_per_step = total_ms / args.steps
+    bytes_step = GEMM_MATS * gemv_batch_bytes(m, GEMM_N, GEMM_K)  # all ranks
+    value = bytes_step / (ms_per_step * 1e-3) / 1e9
+
+    xh = x.cpu().pin_memory()
+    yh = torch.empty(GEMM_MATS, m, n_rank, dtype=torch.bfloat16, pin_memory=True)
+    xd = torch.empty_like(x)
+    e2e_b = F.gemv_batched([(mats[c], xd, ys[c]) for c in range(GEMM_MATS)])
+    e2e_b.submit(F.Async())
+    torch.cuda.synchronize()
+    gsink = F.Graph()
+    with gsink:
+        xd.copy_(xh, non_blocking=True)
+        e2e_b.submit(gsink)
+        yh.copy_(ys, non_blocking=True)
+    e2e_steps = max(1, min(args.steps, 20))
+    for _ in range(2):
+        gsink.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e2e_steps):
+        gsink.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    te = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+    if g > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = bytes_step / (te.item() / e2e_steps * 1e-3) / 1e9
+
+    per_launch_ms = gemv_ms / args.steps
+    hbm, kind = measured_peak()
+    achieved = GEMM_MATS * gemv_batch_bytes(m, n_rank, GEMM_K) / (per_launch_ms * 1e-3) / 1e9
+    out = None
+    if rank == 0:
+        out = {"metric": "NVFP4 GEMM HBM GB/s", "value": value, "unit": "GB/s", "n_gpus": g, "steps": args.steps,
+               "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+               "vs_baseline": None, "dtype": "e2m1xe4m3 weights, bf16 x/y, f32 accumulate",
+               "data": "synthetic (seeded Philox: W N(0,0.02), x N(0,1) seed 0)", "config": gemm_config(m, g),
+               "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                            "frac": achieved / hbm, "traffic": None, "per_launch_us": per_launch_ms * 1e3,
+                            "peak_kind": f"{kind} hbm_gbs"},
+               "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": m * GEMM_K * 2,
+                       "d2h_bytes_per_step": GEMM_MATS * m * n_rank * 2,
+                       "path": "firepit_b200.gemv_batched(...).submit(Graph sink): H2D x, GEMVs, D2H y in one "
+                               "CUDA graph"},
+               "gpu_launches": launches_per_step * args.steps, "clocks": clocks.summary()}
+        if g == 1 and args.cpu_seconds > 0:
+            v, sample, cores = gemm_cpu_sample(m, args.cpu_seconds)
+            out["cpu_baseline"] = {"value": v, "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample}
+    del gr, gsink
+    dist_sync()
+    return out
 
 
 def gemm_arm(args):
@@ -420,12 +695,7 @@ def gemm_arm(args):
     import firepit_b200 as F
     N_ = F._native
 
-    rank, world, local = dist_env()
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    rank, world, local, dev = dist_init()
     g = world
     m = gemm_shape(args)
     n_rank = GEMM_N // g
@@ -437,7 +707,6 @@ def gemm_arm(args):
         del w
         mat = F.Nvfp4Matrix.from_device(packed[r0:r0 + n_rank].contiguous(), scales[r0:r0 + n_rank].contiguous(),
                                         globals_[r0:r0 + n_rank].contiguous(), n_rank, GEMM_K)
-        N_.call("fpb_nvfp4_matrix_prepare_gemm", mat.handle, torch.cuda.current_stream().cuda_stream)
         mats.append(mat)
     x = F.synth_normal((m, GEMM_K), seed=0, stream_id=0, dtype=torch.bfloat16, device=dev)
     ws_bytes = int(N_.lib.fpb_nvfp4_gemm_workspace_bytes(m, GEMM_K))
@@ -481,7 +750,7 @@ def gemm_arm(args):
         if ev:
             ev[2].record()
         if g > 1:
-            dist.all_gather_into_tensor(y_all, ys)
+            comm().all_gather_into(y_all, ys)
 
     for _ in range(max(args.warmup, 3)):
         step()
@@ -552,15 +821,13 @@ def gemm_arm(args):
         roof = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                 "traffic": None, "peak_kind": "measured hbm_gbs"}
     roof["per_launch_us"] = per_launch_ms * 1e3
+    out = None
     if rank == 0:
-        emit({"metric": "NVFP4 GEMM TFLOPS", "value": value, "unit": "TFLOP/s", "n_gpus": g, "steps": args.steps,
+        out = ({"metric": "NVFP4 GEMM TFLOPS", "value": value, "unit": "TFLOP/s", "n_gpus": g, "steps": args.steps,
               "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
               "vs_baseline": None, "dtype": "nvfp4 x nvfp4 (e2m1, ue4m3/16), f32 accumulate, bf16 out",
               "data": "synthetic (seeded Philox: W N(0,0.02), x N(0,1) seed 0)",
-              "config": {"workload": f"config2 NVFP4 GEMM M={m} K=2048 N=8192, x bf16 quantized on device",
-                         "matrices_per_step": GEMM_MATS, "n_per_rank": n_rank,
-                         "l2": "inputs larger than L2 (16 distinct weights per step)",
-                         "parallelism": f"N-split x{g} + NCCL all-gather" if g > 1 else "single GPU"},
+              "config": gemm_config(m, g),
               "roofline": roof,
               "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": m * GEMM_K * 2,
                       "d2h_bytes_per_step": GEMM_MATS * m * n_rank * 2,
@@ -568,10 +835,12 @@ def gemm_arm(args):
                               "one CUDA graph"},
               "gpu_launches": launches_per_step * args.steps, "clocks": clocks.summary(),
               "breakdown_ms": {"quantize_act": quant_ms / args.steps, "gemms": gemm_ms / args.steps}})
+        if g == 1 and args.cpu_seconds > 0:
+            v, sample, cores = gemm_cpu_sample(m, args.cpu_seconds)
+            out["cpu_baseline"] = {"value": v, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample}
     del gq, gg
-    if g > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    dist_sync()
+    return out
 
 
 # ---- config 1: FP8 E4M3 GEMM (tcgen05 kind::f8f6f4) -------------------------------------
@@ -605,18 +874,26 @@ def fp8_cpu_sample(seconds: float):
         f"f32 BLAS")
 
 
+def fp8_config(g: int) -> dict:
+    return {"workload": "config1 FP8 GEMM M=512 K=4096 N=14336, A bf16 quantized per token on device (W8A8)",
+            "matrices_per_step": FP8_MATS, "n_per_rank": FP8_N // g,
+            "l2": "inputs larger than L2 (4 distinct weights, 235 MB per step at one GPU)",
+            "parallelism": f"N-split x{g} + NCCL all-gather" if g > 1 else "single GPU"}
+
+
 def fp8_reference_arm(args):
     rank, _, _ = dist_env()
     if rank != 0:
         return
+    cores = use_all_cores()
     budget = max(5.0, min(60.0, 3.0 * (args.steps + args.warmup)))
     tflops, sample = fp8_cpu_sample(budget)
     emit({"impl": "reference", "metric": "FP8 GEMM TFLOPS", "value": tflops, "unit": "TFLOP/s",
           "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
           "ms_per_step": 2.0 * FP8_M * FP8_N * FP8_K / (tflops * 1e12) * 1e3, "higher_is_better": True,
           "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded Philox)",
-          "config": {"workload": "config1 FP8 GEMM M=512 K=4096 N=14336"},
-          "cpu_baseline": {"value": tflops, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
+          "config": fp8_config(args.gpus),
+          "cpu_baseline": {"value": tflops, "unit": "TFLOP/s", "cores": cores, "kind": "port",
                            "sample": sample},
           "e2e": {"value": tflops, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
 
@@ -632,12 +909,7 @@ def fp8_arm(args):
     import firepit_b200 as F
     N_ = F._native
 
-    rank, world, local = dist_env()
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    rank, world, local, dev = dist_init()
     g = world
     n_rank = FP8_N // g
     r0 = rank * n_rank
@@ -692,7 +964,7 @@ def fp8_arm(args):
         if ev:
             ev[2].record()
         if g > 1:
-            dist.all_gather_into_tensor(y_all, ys)
+            comm().all_gather_into(y_all, ys)
 
     for _ in range(max(args.warmup, 3)):
         step()
@@ -761,10 +1033,7 @@ def fp8_arm(args):
                 "vs_baseline": None, "dtype": "e4m3 x e4m3 (128x128 block / per-token f32 scales), f32 accumulate, "
                                               "bf16 out",
                 "data": "synthetic (seeded Philox: W N(0,0.02), A N(0,1) seed 0)",
-                "config": {"workload": "config1 FP8 GEMM M=512 K=4096 N=14336, A bf16 quantized per token on device",
-                           "matrices_per_step": FP8_MATS, "n_per_rank": n_rank,
-                           "l2": "inputs larger than L2 (4 distinct weights, 235 MB per step)",
-                           "parallelism": f"N-split x{g} + NCCL all-gather" if g > 1 else "single GPU"},
+                "config": fp8_config(g),
                 "roofline": roof,
                 "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": FP8_M * FP8_K * 2,
                         "d2h_bytes_per_step": FP8_MATS * FP8_M * n_rank * 2,
@@ -774,13 +1043,11 @@ def fp8_arm(args):
                 "breakdown_ms": {"quantize_act": quant_ms / args.steps, "gemms": gemm_ms / args.steps}}
         if g == 1 and args.cpu_seconds > 0:
             v, sample = fp8_cpu_sample(args.cpu_seconds)
-            line["cpu_baseline"] = {"value": v, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
+            line["cpu_baseline"] = {"value": v, "unit": "TFLOP/s", "cores": use_all_cores(), "kind": "port",
                                     "sample": sample}
-        emit(line)
     del gq, gg
-    if g > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    dist_sync()
+    return line if rank == 0 else None
 
 
 # ---- config 3: grouped MoE NVFP4 layer ---------------------------------------------------
@@ -849,17 +1116,30 @@ def moe_cpu_sample(seconds: float, tokens_sample: int = 256):
         f"MLPs grouped by expert (f32 BLAS; weights dequantized beforehand)")
 
 
+def moe_config(tokens: int, g: int, ep: bool = False) -> dict:
+    if ep:
+        return {"workload": f"config3 MoE E=512 top-10 H=2048 I=512, T=4096 per rank, EP x{g}",
+                "experts_per_gpu": MOE_E // g,
+                "parallelism": f"EP x{g} + NCCL all-to-all" if g > 1 else "single GPU (no exchange)",
+                "l2": "inputs larger than L2 (all local experts' weights per step)"}
+    return {"workload": f"config3 MoE E=512 top-10 H=2048 I=512 T={tokens}, no shared expert",
+            "l2": "inputs larger than L2 (the touched experts' weights per step)",
+            "parallelism": "single GPU", "tile_rows": 128}
+
+
 def moe_reference_arm(args):
     rank, _, _ = dist_env()
     if rank != 0:
         return
+    cores = use_all_cores()
     v, sample = moe_cpu_sample(min(60.0, max(5.0, 2.0 * (args.steps + args.warmup))))
+    T = 4096 if args.config == "moe_ep" else moe_tokens(args)
     emit({"impl": "reference", "metric": "NVFP4 MoE layer TFLOPS", "value": v, "unit": "TFLOP/s",
           "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-          "ms_per_step": moe_flops(moe_tokens(args)) / (v * 1e12) * 1e3, "higher_is_better": True,
+          "ms_per_step": moe_flops(T) / (v * 1e12) * 1e3, "higher_is_better": True,
           "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded Philox)",
-          "config": {"workload": f"config3 MoE E=512 top-10 H=2048 I=512 T={moe_tokens(args)}"},
-          "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port", "sample": sample},
+          "config": moe_config(T, args.gpus, args.config == "moe_ep"),
+          "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample},
           "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
 
 
@@ -877,9 +1157,7 @@ def moe_arm(args):
 
     import firepit_b200 as F
     N_ = F._native
-    rank, world, local = dist_env()
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
+    rank, world, local, dev = dist_init()
     T = moe_tokens(args)
     # weights: each expert its own global; streams 1000+e / 5000+e as in the CPU sample
     gu_parts, dn_parts = [], []
@@ -907,8 +1185,7 @@ def moe_arm(args):
     W2 = F.Nvfp4Matrix.from_device(dp, ds, dg, MOE_E * MOE_H, MOE_I)
     del gp, gs, gg, dp, ds, dg
     s0 = torch.cuda.current_stream().cuda_stream
-    N_.call("fpb_nvfp4_matrix_prepare_gemm", W1.handle, s0)
-    N_.call("fpb_nvfp4_matrix_prepare_gemm", W2.handle, s0)
+    W1.prepare_glu(MOE_I, s0)  # load time: the layer's calls allocate nothing
     wr = F.synth_normal((MOE_E, MOE_H), seed=0, stream_id=99, std=0.02, dtype=torch.bfloat16, device=dev)
     x = F.synth_normal((T, MOE_H), seed=0, stream_id=0, dtype=torch.bfloat16, device=dev)
     router = F.MoeDims.new(MOE_H, MOE_I, MOE_I, MOE_E, MOE_K)
@@ -1028,23 +1305,21 @@ def moe_arm(args):
             "vs_baseline": None,
             "dtype": "nvfp4 x nvfp4 experts (f32 accumulate), bf16 router (f32 logits), bf16 activations",
             "data": "synthetic (seeded Philox: W N(0,0.02) per expert, x N(0,1) seed 0)",
-            "config": {"workload": f"config3 MoE E=512 top-10 H=2048 I=512 T={T}, no shared expert",
-                       "touched_experts": touched, "l2": f"{nbytes / 1e6:.0f} MB of weights per step (> L2)",
-                       "parallelism": "single GPU", "tile_rows": 128},
+            "config": moe_config(T, 1),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                          "traffic": None, "algorithmic_bytes": nbytes, "peak_kind": "measured hbm_gbs",
                          "note": "whole MoE layer time; the grouped GEMMs are the dominant kernels"},
             "e2e": {"value": e2e, "unit": "TFLOP/s", "h2d_bytes_per_step": T * MOE_H * 2,
                     "path": "C-ABI calls of the layer with H2D x and D2H out in one CUDA graph",
                     "d2h_bytes_per_step": T * MOE_H * 2},
-            "gpu_launches": launches_per_step * args.steps, "clocks": clocks.summary(), "breakdown_ms": breakdown}
-    if args.cpu_seconds > 0:
+            "gpu_launches": launches_per_step * args.steps, "clocks": clocks.summary(), "breakdown_ms": breakdown,
+            "touched_experts": touched}
+    if args.cpu_seconds > 0 and rank == 0:
         v, sample = moe_cpu_sample(args.cpu_seconds)
-        line["cpu_baseline"] = {"value": v, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
+        line["cpu_baseline"] = {"value": v, "unit": "TFLOP/s", "cores": use_all_cores(), "kind": "port",
                                 "sample": sample}
-    if rank == 0:
-        emit(line)
     del graph
+    return line if rank == 0 else None
 
 
 def moe_ep_arm(args):
@@ -1058,13 +1333,7 @@ def moe_ep_arm(args):
 
     import firepit_b200 as F
     from firepit_b200.ep import DeviceOps, ep_moe_forward
-    rank, world, local = dist_env()
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    rank, world, local, dev = dist_init()
     T = 4096
     per = MOE_E // world
     e0 = rank * per
@@ -1090,6 +1359,7 @@ def moe_ep_arm(args):
         del g, d
     W1 = F.Nvfp4Matrix.from_device(gp, gs, gg, per * 2 * MOE_I, MOE_H)
     W2 = F.Nvfp4Matrix.from_device(dp, ds, dg, per * MOE_H, MOE_I)
+    W1.prepare_glu(MOE_I)
     del gp, gs, gg, dp, ds, dg
     wr = F.synth_normal((MOE_E, MOE_H), seed=0, stream_id=99, std=0.02, dtype=torch.bfloat16, device=dev)
     x = F.synth_normal((T, MOE_H), seed=rank, stream_id=0, dtype=torch.bfloat16, device=dev)
@@ -1097,14 +1367,13 @@ def moe_ep_arm(args):
 
     def step():
         logits = torch.mm(x, wr.t(), out_dtype=torch.float32)
-        return ep_moe_forward(ops, x, logits, MOE_K, MOE_E, W1, W2, world=world)
+        return ep_moe_forward(ops, x, logits, MOE_K, MOE_E, W1, W2, world=world, comm=comm())
 
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize()
     assert F.device_error() == 0
-    if world > 1:
-        dist.barrier()
+    dist_sync()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     launches = F.launch_count()
@@ -1125,39 +1394,88 @@ def moe_ep_arm(args):
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
     hbm = float(peaks.get("hbm_gbs", 6650.0))
     achieved = nbytes / world / (ms * 1e-3) / 1e9
+    out = None
     if rank == 0:
-        emit({"metric": "NVFP4 MoE layer TFLOPS", "value": value, "unit": "TFLOP/s", "n_gpus": world,
-              "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-              "scaling": "weak", "vs_baseline": None,
-              "dtype": "nvfp4 x nvfp4 experts (f32 accumulate), bf16 router and dispatch",
-              "data": "synthetic (seeded Philox: W N(0,0.02) per expert, x N(0,1) per rank)",
-              "config": {"workload": f"config3 MoE E=512 top-10 H=2048 I=512, T=4096 per rank, EP x{world}",
-                         "experts_per_gpu": per, "parallelism": f"EP x{world} + NCCL all-to-all" if world > 1
-                         else "single GPU (no exchange)",
-                         "l2": "inputs larger than L2 (all local experts' weights per step)"},
-              "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                           "traffic": None, "peak_kind": "measured hbm_gbs",
-                           "note": "per GPU: local experts' weights + router + x + y over the layer time"},
-              "e2e": None, "gpu_launches": launches, "clocks": clocks.summary()})
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+        out = {"metric": "NVFP4 MoE layer TFLOPS", "value": value, "unit": "TFLOP/s", "n_gpus": world,
+               "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+               "scaling": "weak", "vs_baseline": None,
+               "dtype": "nvfp4 x nvfp4 experts (f32 accumulate), bf16 router and dispatch",
+               "data": "synthetic (seeded Philox: W N(0,0.02) per expert, x N(0,1) per rank)",
+               "config": moe_config(T, world, ep=True),
+               "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                            "frac": achieved / hbm, "traffic": None, "peak_kind": "measured hbm_gbs",
+                            "note": "per GPU: local experts' weights + router + x + y over the layer time"},
+               "e2e": None, "gpu_launches": launches, "clocks": clocks.summary()}
+    dist_sync()
+    return out
+
+
+SUB_RECORDS = [
+    # (name, config, runs at one GPU, runs at several GPUs)
+    ("config1_fp8_gemm", "fp8_gemm", True, True),
+    ("config2_m1", "nvfp4_gemm_m1", True, True),
+    ("config2_m16", "nvfp4_gemm_m16", True, True),
+    ("config2_m128", "nvfp4_gemm_m128", True, True),
+    ("config2_m2048", "nvfp4_gemm_m2048", True, True),
+    ("config3_moe_t64", "moe_t64", True, False),
+    ("config3_moe_t4096", "moe_t4096", True, False),
+    ("config3_moe_ep", "moe_ep", False, True),
+]
+
+
+def product_arm(config: str):
+    if config == "moe_ep":
+        return moe_ep_arm
+    if config.startswith("moe_"):
+        return moe_arm
+    if config == "fp8_gemm":
+        return fp8_arm
+    if config in ("nvfp4_gemm_m1", "nvfp4_gemm_m16"):
+        return gemm_small_arm
+    if config.startswith("nvfp4_gemm"):
+        return gemm_arm
+    return ours_arm
+
+
+def reference_for(config: str):
+    if config.startswith("moe_"):
+        return moe_reference_arm
+    if config == "fp8_gemm":
+        return fp8_reference_arm
+    if config.startswith("nvfp4_gemm"):
+        return gemm_reference_arm
+    return reference_arm
 
 
 def main():
     args = parse_args()
-    if args.config == "moe_ep":
-        (moe_reference_arm if args.impl == "reference" else moe_ep_arm)(args)
-    elif args.config.startswith("moe_"):
-        (moe_reference_arm if args.impl == "reference" else moe_arm)(args)
-    elif args.config == "fp8_gemm":
-        (fp8_reference_arm if args.impl == "reference" else fp8_arm)(args)
-    elif args.config.startswith("nvfp4_gemm"):
-        (gemm_reference_arm if args.impl == "reference" else gemm_arm)(args)
-    elif args.impl == "reference":
-        reference_arm(args)
-    else:
-        ours_arm(args)
+    if args.impl == "reference":
+        # The CPU legs use every host core (numpy's BLAS reads this at import).
+        os.environ["OMP_NUM_THREADS"] = str(os.cpu_count() or 1)
+        reference_for(args.config)(args)
+        return
+    import copy
+
+    import torch
+    line = product_arm(args.config)(args)
+    if args.config == "gemv" and not args.no_sub:
+        _, world, _ = dist_env()
+        subs = {}
+        for name, config, one, many in SUB_RECORDS:
+            if not (one if world == 1 else many):
+                continue
+            sub = copy.copy(args)
+            sub.config, sub.steps, sub.warmup, sub.cpu_seconds = config, args.sub_steps, 3, args.sub_cpu_seconds
+            rec = product_arm(config)(sub)
+            torch.cuda.synchronize()
+            torch.cuda.empty_cache()
+            if line is not None:
+                subs[name] = rec
+        if line is not None:
+            line["sub_records"] = subs
+    if line is not None:
+        emit(line)
+    dist_finish()
 
 
 if __name__ == "__main__":

@@ -22,11 +22,14 @@ FPB_ERR_SELECTION = 6
 FPB_ERR_WORKSPACE = 7
 FPB_ERR_NO_DEVICE = 8
 FPB_ERR_IO = 9
+FPB_ERR_COMM = 10
 
 FPB_F32 = 0
 FPB_BF16 = 1
 FPB_QUANT_AMAX_GIVEN = 1
 FPB_QUANT_SKIP_PADDING = 2
+FPB_COMM_U32, FPB_COMM_I32, FPB_COMM_BYTES = 2, 3, 4
+FPB_COMM_SUM, FPB_COMM_MAX = 0, 1
 
 
 class FpbError(RuntimeError):
@@ -65,6 +68,9 @@ class GemvSegment(C.Structure):
     _fields_ = [("w", C.c_void_p), ("row_begin", C.c_size_t), ("row_end", C.c_size_t), ("x", C.c_void_p),
                 ("y", C.c_void_p)]
 
+
+FPB_COMM_ID_BYTES = 128
+sizep = C.POINTER(C.c_size_t)
 
 # name -> (restype, argtypes)
 SIGNATURES: dict[str, tuple] = {
@@ -106,6 +112,7 @@ SIGNATURES: dict[str, tuple] = {
     "fpb_nvfp4_gemm_workspace_bytes": (sz, [sz, sz]),
     "fpb_nvfp4_quantize_act": (i32, [vp, i32, sz, sz, vp, vp, vp, vp, vp]),
     "fpb_nvfp4_matrix_prepare_gemm": (i32, [vp, vp]),
+    "fpb_nvfp4_matrix_prepare_glu": (i32, [vp, sz, vp]),
     "fpb_nvfp4_gemm_q": (i32, [vp, sz, sz, vp, vp, vp, sz, vp, i32, vp]),
     "fpb_nvfp4_gemm": (i32, [vp, sz, sz, vp, i32, sz, vp, i32, vp, sz, vp]),
     "fpb_nvfp4_grouped_gemm_q": (i32, [vp, vp, vp, vp, sz, vp, vp, sz, vp, i32, vp]),
@@ -139,6 +146,17 @@ SIGNATURES: dict[str, tuple] = {
     "fpb_moe_combine_add_norm": (i32, [vp, i32, sz, sz, vp, vp, sz, sz, sz, vp, vp, C.c_float, vp, vp, vp]),
     "fpb_moe_route_dest": (i32, [vp, sz, sz, sz, sz, vp, vp]),
     "fpb_moe_route_meta": (i32, [vp, vp, sz, sz, sz, sz, sz, vp, vp]),
+    "fpb_comm_available": (i32, []),
+    "fpb_comm_version": (i32, [C.POINTER(i32)]),
+    "fpb_comm_unique_id": (i32, [vp]),
+    "fpb_comm_init": (i32, [vp, i32, i32, i32, C.POINTER(vp)]),
+    "fpb_comm_destroy": (i32, [vp]),
+    "fpb_comm_abort": (i32, [vp]),
+    "fpb_comm_status": (i32, [vp]),
+    "fpb_comm_size": (i32, [vp, C.POINTER(i32), C.POINTER(i32)]),
+    "fpb_comm_all_gather": (i32, [vp, vp, vp, sz, i32, vp]),
+    "fpb_comm_all_reduce": (i32, [vp, vp, vp, sz, i32, i32, vp]),
+    "fpb_comm_all_to_all": (i32, [vp, vp, sizep, sizep, vp, sizep, sizep, i32, vp]),
     "fpb_moe_dims_validate": (i32, [sz, sz, sz, sz, sz]),
     "fpb_expert_selection_validate": (i32, [vp, vp, sz, sz, sz]),
     "fpb_prefill_layout_max_padded_rows": (i32, [sz, sz, sz, sz, C.POINTER(sz)]),

@@ -8,6 +8,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "matrix_extras.cuh"
 #include "nvfp4_matrix.cuh"
 
 namespace fpb {
@@ -174,6 +175,7 @@ const char *fpb_status_string(int s) {
     case FPB_ERR_WORKSPACE: return "workspace too small";
     case FPB_ERR_NO_DEVICE: return "no CUDA device";
     case FPB_ERR_IO: return "I/O error";
+    case FPB_ERR_COMM: return "communication error";
     default: return "unknown status";
   }
 }
@@ -215,6 +217,12 @@ int fpb_nvfp4_matrix_create(const uint8_t *packed, const uint8_t *scales, const 
   if (e != cudaSuccess) {
     fpb_nvfp4_matrix_destroy(m);
     return cuda_fail(e, "fpb_nvfp4_matrix_create upload");
+  }
+  // The GEMM-side copies are built here, at load time, so that no GEMM call
+  // allocates or synchronises (the calls can then be recorded into a graph).
+  if ((st = prepare_gemm_weights(m, s))) {
+    fpb_nvfp4_matrix_destroy(m);
+    return st;
   }
   *out = m;
   return FPB_OK;
@@ -260,6 +268,10 @@ int fpb_nvfp4_matrix_create_device(const uint8_t *packed, const uint8_t *scales,
     fpb_nvfp4_matrix_destroy(m);
     return fail(FPB_ERR_FORMAT, "invalid NVFP4 matrix, block scales, or global scale (%s)",
                 (host_bad & 1) ? "NaN e4m3 block scale" : "global scale not finite and >= 0");
+  }
+  if ((st = prepare_gemm_weights(m, s))) {  // load time: GEMM calls allocate nothing
+    fpb_nvfp4_matrix_destroy(m);
+    return st;
   }
   *out = m;
   return FPB_OK;

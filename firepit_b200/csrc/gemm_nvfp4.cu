@@ -619,9 +619,34 @@ static unsigned grid_for(size_t n) {
   return (unsigned)std::max<size_t>(1, std::min(g, cap));
 }
 
+// Raises the GEMM kernel's dynamic shared-memory limit once per device (at
+// matrix creation, so that no GEMM call makes the runtime call during a
+// stream capture).
+static int ensure_gemm_attr() {
+  static std::mutex mu;
+  static std::vector<int> attr_devs;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (std::find(attr_devs.begin(), attr_devs.end(), dev) == attr_devs.end()) {
+    FPB_CUDA_TRY(cudaFuncSetAttribute(nvfp4_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem));
+    attr_devs.push_back(dev);
+  }
+  return FPB_OK;
+}
+
+// A handle from fpb_nvfp4_matrix_create(_device) always has its GEMM-side
+// copies; this guards against handles built some other way.
+static int require_prepared(const fpb_nvfp4_matrix *m, const char *fn) {
+  if (!m->extras || !m->extras->tmap_valid)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "%s: matrix has no GEMM-side copies (fpb_nvfp4_matrix_prepare_gemm)", fn);
+  return FPB_OK;
+}
+
 // Builds the GEMM-side copies of a weight matrix once: tiled UE4M3 factors,
 // sign-folded codes when any factor is negative, and the codes' TMA map.
 int prepare_gemm_weights(fpb_nvfp4_matrix *m, cudaStream_t s) {
+  if (int st = ensure_gemm_attr()) return st;
   if (m->extras && m->extras->tmap_valid) return FPB_OK;
   static std::mutex mu;
   std::lock_guard<std::mutex> lock(mu);
@@ -703,9 +728,19 @@ extern "C" int fpb_nvfp4_quantize_act(const void *x, int x_dtype, size_t m, size
   return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_quantize_act: dtype %d", x_dtype);
 }
 
+static int prepare_glu_weights(fpb_nvfp4_matrix *m, size_t inter, cudaStream_t s);
+
 extern "C" int fpb_nvfp4_matrix_prepare_gemm(fpb_nvfp4_matrix *w, void *stream) {
   if (!w) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_matrix_prepare_gemm: null handle");
   return prepare_gemm_weights(w, as_stream(stream));
+}
+
+extern "C" int fpb_nvfp4_matrix_prepare_glu(fpb_nvfp4_matrix *w, size_t inter, void *stream) {
+  if (!w) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_matrix_prepare_glu: null handle");
+  if (inter == 0 || inter % 64 || w->rows % (2 * inter))
+    return fail(FPB_ERR_SHAPE, "fpb_nvfp4_matrix_prepare_glu: inter %zu must be a multiple of 64 with 2*inter "
+                "dividing %zu", inter, w->rows);
+  return prepare_glu_weights(w, inter, as_stream(stream));
 }
 
 extern "C" int fpb_nvfp4_gemm_q(fpb_nvfp4_matrix *w, size_t row_begin, size_t row_end, const uint8_t *a_packed,
@@ -722,7 +757,7 @@ extern "C" int fpb_nvfp4_gemm_q(fpb_nvfp4_matrix *w, size_t row_begin, size_t ro
   if (m == 0 || m > (size_t)65535 * kBM) return fail(FPB_ERR_SHAPE, "fpb_nvfp4_gemm_q: m = %zu", m);
   if (y_dtype != FPB_F32 && y_dtype != FPB_BF16) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_gemm_q: dtype");
   cudaStream_t s = as_stream(stream);
-  int st = prepare_gemm_weights(w, s);
+  int st = require_prepared(w, "fpb_nvfp4_gemm_q");
   if (st) return st;
   CUtensorMap tmap_a;
   if ((st = encode_rows_u8(&tmap_a, a_packed, m, w->cols / 2, kBM))) return st;
@@ -796,7 +831,7 @@ extern "C" int fpb_nvfp4_grouped_gemm_q(fpb_nvfp4_matrix *w, const uint8_t *a_pa
   if (y_dtype != FPB_F32 && y_dtype != FPB_BF16)
     return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_grouped_gemm_q: dtype");
   cudaStream_t s = as_stream(stream);
-  int st = prepare_gemm_weights(w, s);
+  int st = require_prepared(w, "fpb_nvfp4_grouped_gemm_q");
   if (st) return st;
   CUtensorMap tmap_a;
   if ((st = encode_rows_u8(&tmap_a, a_packed, padded_rows, w->cols / 2, kBM))) return st;
@@ -841,7 +876,8 @@ extern "C" int fpb_nvfp4_grouped_gemm_q(fpb_nvfp4_matrix *w, const uint8_t *a_pa
 }
 
 // Fused gate/up copies (interleaved factors, 64-row code map) for an
-// intermediate size `inter`; built once per matrix, synchronises `s`.
+// intermediate size `inter`; built once per matrix (fpb_nvfp4_matrix_prepare_glu,
+// at load time), allocates and synchronises `s`.
 static int prepare_glu_weights(fpb_nvfp4_matrix *m, size_t inter, cudaStream_t s) {
   int st = prepare_gemm_weights(m, s);
   if (st) return st;
@@ -878,8 +914,11 @@ extern "C" int fpb_nvfp4_grouped_gemm_swiglu_q(fpb_nvfp4_matrix *w, const uint8_
   if (reinterpret_cast<uintptr_t>(h) & 15)
     return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_grouped_gemm_swiglu_q: h must be 16-byte aligned");
   cudaStream_t s = as_stream(stream);
-  int st = prepare_glu_weights(w, inter, s);
+  int st = require_prepared(w, "fpb_nvfp4_grouped_gemm_swiglu_q");
   if (st) return st;
+  if (!w->extras->sf_tiled_glu || w->extras->glu_inter != inter)
+    return fail(FPB_ERR_INVALID_ARGUMENT,
+                "fpb_nvfp4_grouped_gemm_swiglu_q: call fpb_nvfp4_matrix_prepare_glu(w, %zu) at load time", inter);
   CUtensorMap tmap_a, tmap_y{};
   if ((st = encode_rows_u8(&tmap_a, a_packed, padded_rows, w->cols / 2, kBM))) return st;
   // h boxes: 32 rows x 32 columns per epilogue warp (bf16 unswizzled, f32

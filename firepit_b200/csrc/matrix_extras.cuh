@@ -1,5 +1,7 @@
 // Handle-owned GEMM-side layouts of an NVFP4 matrix (see matrix_extras.cu).
 #pragma once
+#include <cuda_runtime.h>
+
 #include <cstddef>
 #include <cstdint>
 
@@ -26,4 +28,9 @@ struct MatrixExtras {
   size_t glu_inter = 0;
   alignas(64) unsigned char tmap_b64[128];
 };
+
+// Builds the GEMM-side copies (tiled factors, sign-folded codes when a factor
+// is negative, the codes' TMA map) once; allocates and synchronises `s`.
+// Called when the matrix handle is created, so GEMM calls allocate nothing.
+int prepare_gemm_weights(fpb_nvfp4_matrix *m, cudaStream_t s);
 }  // namespace fpb

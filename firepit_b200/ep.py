@@ -125,6 +125,7 @@ class DeviceOps:
         sf1 = self.empty((int(N.lib.fpb_nvfp4_act_sf_bytes(cap, h)),), t.uint8)
         hbuf = self.empty((cap, inter), t.bfloat16)
         a_h = t.zeros(1, dtype=t.int32, device=self.device)
+        w1.prepare_glu(inter, self._s())  # load-time copy; a no-op after the first layer
         if n:
             N.call("fpb_moe_gather_quantize", x.data_ptr(), _dt(x), n, h, lay["tr"].data_ptr(), cap,
                    lay["pad"].data_ptr(), a1.data_ptr(), sf1.data_ptr(), scal.data_ptr(), scal[1:].data_ptr(),
@@ -162,13 +163,18 @@ def _dt(t) -> int:
     return _dtype_code(t)
 
 
-def ep_moe_forward(ops, x, logits, k: int, experts: int, w1, w2, group=None, world: int | None = None):
+def ep_moe_forward(ops, x, logits, k: int, experts: int, w1, w2, group=None, world: int | None = None,
+                   comm=None):
     """One expert-parallel MoE layer for this rank's tokens x [T, H] with
     router logits [T, experts]; w1 / w2 hold this rank's experts
     ([per_rank * 2I, H] and [per_rank * H, I]).  Returns [T, H] (x's dtype).
-    ``world = 1`` runs every expert locally (no collective)."""
+    ``world = 1`` runs every expert locally (no collective).  ``comm`` (a
+    firepit_b200.comm.Comm) carries the collectives through the library's
+    C ABI; without it they go through torch.distributed (``group``)."""
     import torch
     import torch.distributed as dist
+    if comm is not None:
+        world = comm.nranks
     if world is None:
         world = dist.get_world_size(group) if dist.is_initialized() else 1
     per_rank = experts // world
@@ -184,25 +190,40 @@ def ep_moe_forward(ops, x, logits, k: int, experts: int, w1, w2, group=None, wor
 
     def amax_reduce(a):
         if world > 1:
-            dist.all_reduce(a, op=dist.ReduceOp.MAX, group=group)
+            if comm is not None:
+                comm.all_reduce_max_bits(a)
+            else:
+                dist.all_reduce(a, op=dist.ReduceOp.MAX, group=group)
         return a
+
+    def a2a(out, inp, out_counts, in_counts):
+        if comm is not None:
+            comm.all_to_all(inp, in_counts, out, out_counts)
+        else:
+            dist.all_to_all_single(out, inp, out_counts, in_counts, group=group)
 
     if world == 1:
         recv_x, recv_e = send_x, send_e
         recv_counts = send_counts
     else:
-        recv_counts = torch.empty_like(send_counts)
-        dist.all_to_all_single(recv_counts, send_counts, group=group)
+        if comm is not None:
+            sc32 = send_counts.to(torch.int32)
+            rc32 = torch.empty_like(sc32)
+            comm.all_to_all(sc32, [1] * world, rc32, [1] * world)
+            recv_counts = rc32
+        else:
+            recv_counts = torch.empty_like(send_counts)
+            dist.all_to_all_single(recv_counts, send_counts, group=group)
         sc = [int(v) for v in send_counts.tolist()]
         rc = [int(v) for v in recv_counts.tolist()]
         recv_x = x.new_empty((sum(rc), x.shape[1]))
         recv_e = send_e.new_empty((sum(rc),))
-        dist.all_to_all_single(recv_x, send_x.contiguous(), rc, sc, group=group)
-        dist.all_to_all_single(recv_e, send_e.contiguous(), rc, sc, group=group)
+        a2a(recv_x, send_x.contiguous(), rc, sc)
+        a2a(recv_e, send_e.contiguous(), rc, sc)
     y_recv = ops.expert_mlp(recv_x, recv_e, w1, w2, per_rank, amax_reduce)
     if world == 1:
         back = y_recv
     else:
         back = y_recv.new_empty((n_send, y_recv.shape[1]))
-        dist.all_to_all_single(back, y_recv.contiguous(), sc, rc, group=group)
+        a2a(back, y_recv.contiguous(), sc, rc)
     return ops.combine(back, disp["inv"], w, k, x.dtype)

@@ -134,7 +134,9 @@ def nvfp4_grouped_gemm_swiglu_q(weight: Nvfp4Matrix, a_packed, a_sf, a_global, t
     weight: experts of 2 * inter rows (gate rows, then up rows); h: [padded_rows,
     inter] f32/bf16.  Returns ``amax`` (device int32 [1]): max |h| as float bits,
     the input of ``rows_quantize(..., amax=...)``.  token_rows as in
-    ``nvfp4_grouped_gemm_q`` (padding rows also left out of the amax).
+    ``nvfp4_grouped_gemm_q`` (padding rows also left out of the amax).  The
+    weight needs ``weight.prepare_glu(inter)`` once (done here on first use,
+    which synchronises: make that first use outside any graph capture).
     """
     import torch
     from .weights import current_stream_handle
@@ -146,6 +148,7 @@ def nvfp4_grouped_gemm_swiglu_q(weight: Nvfp4Matrix, a_packed, a_sf, a_global, t
     if amax is None:
         amax = torch.zeros(1, dtype=torch.int32, device=h.device)
     s = current_stream_handle(h.device) if stream is None else stream
+    weight.prepare_glu(inter, s)
     N.call("fpb_nvfp4_grouped_gemm_swiglu_q", weight.handle, a_packed.data_ptr(), a_sf.data_ptr(),
            a_global.data_ptr(), padded_rows, tile_experts.data_ptr(),
            None if token_rows is None else token_rows.data_ptr(), inter, h.data_ptr(), _dtype_code(h),

@@ -128,6 +128,16 @@ class Nvfp4Matrix:
         N.call("fpb_nvfp4_matrix_device_ptrs", self.handle, C.byref(p), C.byref(s), C.byref(g))
         return p.value, s.value, g.value
 
+    def prepare_glu(self, inter: int, stream=None) -> None:
+        """Builds the interleaved factor copy of the fused gate/up + SwiGLU
+        GEMM for experts of 2 * inter rows (fpb_nvfp4_matrix_prepare_glu):
+        allocates and synchronises, so call it at load time."""
+        if getattr(self, "_glu_inter", None) == inter:
+            return
+        s = current_stream_handle() if stream is None else stream
+        N.call("fpb_nvfp4_matrix_prepare_glu", self.handle, inter, s)
+        self._glu_inter = inter
+
     def to_host(self, stream=None) -> HostNvfp4Matrix:
         """Copies the device storage back (synchronises the stream)."""
         packed = np.empty(self.rows * self.cols // 2, np.uint8)

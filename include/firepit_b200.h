@@ -42,7 +42,8 @@ enum {
   FPB_ERR_SELECTION = 6,        /* ExpertSelectionError (moe.rs:262-269)    */
   FPB_ERR_WORKSPACE = 7,        /* workspace too small                      */
   FPB_ERR_NO_DEVICE = 8,        /* no CUDA device visible                   */
-  FPB_ERR_IO = 9                /* a checkpoint file could not be read      */
+  FPB_ERR_IO = 9,               /* a checkpoint file could not be read      */
+  FPB_ERR_COMM = 10             /* NCCL missing or a collective failed      */
 };
 
 enum { FPB_F32 = 0, FPB_BF16 = 1 };
@@ -97,8 +98,12 @@ int fpb_nvfp4_validate(const uint8_t *packed, size_t packed_len,
 
 /* HostNvfp4Matrix::{from_parts,stack} + upload (weights/nvfp4.rs:47-120).
  * Host arrays: packed [rows, cols/2] (even column in the low nibble),
- * scales [rows, cols/16] e4m3, row_globals [rows] f32.  Copies to device
- * and synchronises `stream`. */
+ * scales [rows, cols/16] e4m3, row_globals [rows] f32.  Copies to device,
+ * builds the GEMM-side copies (the factors in the tensor cores' tiled
+ * layout: cols/16 more bytes per row; codes with negative factors' signs
+ * folded in, only if a factor is negative) and synchronises `stream`.
+ * Building them here, at load time, is what lets every later GEMV and GEMM
+ * call run without allocating or synchronising. */
 int fpb_nvfp4_matrix_create(const uint8_t *packed, const uint8_t *scales,
                             const float *row_globals, size_t rows, size_t cols,
                             void *stream, fpb_nvfp4_matrix **out);
@@ -233,9 +238,16 @@ size_t fpb_nvfp4_gemm_workspace_bytes(size_t m, size_t k);
  * amax_scratch one float of device scratch.  Two launches plus two memsets. */
 int fpb_nvfp4_quantize_act(const void *x, int x_dtype, size_t m, size_t k, uint8_t *packed,
                            uint8_t *sf_tiled, float *global_out, float *amax_scratch, void *stream);
-/* Builds the matrix's GEMM-side copies once (tiled factors, TMA map);
- * allocates and synchronises `stream`.  Called by the first GEMM if needed. */
+/* Builds the matrix's GEMM-side copies (tiled factors, TMA map) if they are
+ * missing; matrix creation already builds them, so this is a no-op on every
+ * handle from fpb_nvfp4_matrix_create(_device).  The GEMM calls below never
+ * build anything: they allocate nothing and do not synchronise. */
 int fpb_nvfp4_matrix_prepare_gemm(fpb_nvfp4_matrix *w, void *stream);
+/* Builds the interleaved factor copy the fused gate/up + SwiGLU GEMM needs
+ * for experts of 2*inter rows (fpb_nvfp4_grouped_gemm_swiglu_q); allocates
+ * and synchronises `stream`: call it at load time, outside any capture.  A
+ * no-op when already built for `inter`. */
+int fpb_nvfp4_matrix_prepare_glu(fpb_nvfp4_matrix *w, size_t inter, void *stream);
 /* GEMM on already quantized activations. */
 int fpb_nvfp4_gemm_q(fpb_nvfp4_matrix *w, size_t row_begin, size_t row_end, const uint8_t *a_packed,
                      const uint8_t *a_sf_tiled, const float *a_global, size_t m, void *y, int y_dtype,
@@ -389,8 +401,9 @@ int fpb_swiglu_quantize(const void *gate_up, int dtype, size_t rows, const int32
  * aligned) = silu(gate) * up computed from the f32 accumulators (no rounding
  * of gate/up, as the reference's f32 swiglu input; exp and the division by
  * hardware approximations, relative error about 1e-6); *amax_bits = max |h| as
- * stored (float bits; zeroed first).  inter % 64 == 0.  The first call on a
- * matrix builds its interleaved factor copy and synchronises `stream`.
+ * stored (float bits; zeroed first).  inter % 64 == 0.  Needs the matrix's
+ * interleaved factor copy from fpb_nvfp4_matrix_prepare_glu(w, inter)
+ * (FPB_ERR_INVALID_ARGUMENT otherwise); allocates nothing.
  * token_rows as in fpb_nvfp4_grouped_gemm_q; padding rows are also left out
  * of the amax. */
 int fpb_nvfp4_grouped_gemm_swiglu_q(fpb_nvfp4_matrix *w, const uint8_t *a_packed, const uint8_t *a_sf_tiled,
@@ -434,6 +447,48 @@ int fpb_moe_route_dest(const int32_t *ids, size_t tokens, size_t width, size_t s
                        int32_t *dest, void *stream);
 int fpb_moe_route_meta(const int32_t *ids, const int32_t *inverse, size_t tokens, size_t width, size_t slots,
                        size_t experts_per_rank, size_t rows, int32_t *send_expert, void *stream);
+
+/* ---- collectives (NCCL) ------------------------------------------------------
+ * The reference runs on one GPU and has no collectives.  These are the
+ * exchange steps of the multi-GPU paths: the all-gather of each rank's output
+ * columns after an N-split GEMV/GEMM, and the all-to-all dispatch/combine and
+ * amax MAX all-reduce of the expert-parallel MoE layer.  One communicator per
+ * (process, GPU); rank 0 makes the unique id and the caller hands it to the
+ * other ranks (a TCP store, MPI, a file).  NCCL is opened at run time
+ * (libnccl.so.2); FPB_ERR_COMM when it is missing or a call fails.  The
+ * collectives are enqueued on `stream` (asynchronous, capturable like any
+ * NCCL call); every rank must make the same calls in the same order. */
+#define FPB_COMM_ID_BYTES 128
+typedef struct fpb_comm fpb_comm;
+/* Extra element types of the collectives (besides FPB_F32, FPB_BF16). */
+enum { FPB_COMM_U32 = 2, FPB_COMM_I32 = 3, FPB_COMM_BYTES = 4 };
+enum { FPB_COMM_SUM = 0, FPB_COMM_MAX = 1 };
+/* 1 if NCCL could be loaded, else 0. */
+int fpb_comm_available(void);
+int fpb_comm_version(int *version);
+int fpb_comm_unique_id(uint8_t id[FPB_COMM_ID_BYTES]);
+/* Joins the communicator of `nranks` ranks named by `id` as `rank`, on CUDA
+ * device `device` (blocks until every rank has joined). */
+int fpb_comm_init(const uint8_t id[FPB_COMM_ID_BYTES], int nranks, int rank, int device, fpb_comm **out);
+int fpb_comm_destroy(fpb_comm *c);
+/* Aborts pending operations and frees the communicator: the way out for a
+ * host watchdog when a peer died (no GPU-side wait is left behind). */
+int fpb_comm_abort(fpb_comm *c);
+/* FPB_ERR_COMM when the communicator recorded an asynchronous error. */
+int fpb_comm_status(const fpb_comm *c);
+int fpb_comm_size(const fpb_comm *c, int *nranks, int *rank);
+/* recv [nranks][count] = every rank's send [count] in rank order. */
+int fpb_comm_all_gather(fpb_comm *c, const void *send, void *recv, size_t count, int dtype, void *stream);
+/* recv [count] = SUM or MAX over ranks of send [count] (MAX of FPB_COMM_U32
+ * float bits of non-negative values is the float maximum). */
+int fpb_comm_all_reduce(fpb_comm *c, const void *send, void *recv, size_t count, int dtype, int op,
+                        void *stream);
+/* Variable all-to-all: to each rank p, send_counts[p] elements from
+ * send + send_offsets[p]; from each rank p, recv_counts[p] elements into
+ * recv + recv_offsets[p] (host arrays of nranks entries, in elements). */
+int fpb_comm_all_to_all(fpb_comm *c, const void *send, const size_t *send_counts, const size_t *send_offsets,
+                        void *recv, const size_t *recv_counts, const size_t *recv_offsets, int dtype,
+                        void *stream);
 
 /* ---- MoE host bookkeeping (no GPU needed) -------------------------------- */
 /* MoeDims::new (moe.rs:172-225): FPB_ERR_SHAPE on invalid dimensions. */

@@ -252,3 +252,13 @@ int orc_num_threads(void) {
   return 1;
 #endif
 }
+
+/* Sets the OpenMP thread count of the oracle's parallel loops (a launcher
+ * such as torch.distributed.run sets OMP_NUM_THREADS=1 for every rank). */
+void orc_set_num_threads(int n) {
+#ifdef _OPENMP
+  if (n > 0) omp_set_num_threads(n);
+#else
+  (void)n;
+#endif
+}

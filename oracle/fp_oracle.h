@@ -135,6 +135,7 @@ double orc_inner_product_excess(const float *actual, const double *expected,
 
 /* ---- CPU baseline helpers ------------------------------------------------- */
 int orc_num_threads(void);
+void orc_set_num_threads(int n);
 
 #ifdef __cplusplus
 }

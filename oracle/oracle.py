@@ -57,6 +57,7 @@ for name, res, args in [
     ("orc_gamma_tilde", C.c_double, [_sz]),
     ("orc_inner_product_excess", C.c_double, [_vp, _vp, _vp, _sz, _sz]),
     ("orc_num_threads", C.c_int, []),
+    ("orc_set_num_threads", None, [C.c_int]),
 ]:
     fn = getattr(lib, name)
     fn.restype = res
@@ -256,3 +257,7 @@ def rel_frobenius(actual, expected) -> float:
 
 def num_threads() -> int:
     return lib.orc_num_threads()
+
+
+def set_num_threads(n: int) -> None:
+    lib.orc_set_num_threads(int(n))

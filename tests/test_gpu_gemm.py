@@ -121,3 +121,34 @@ def test_gemm_negative_block_scales(F, torch):
     F.nvfp4_gemm(W, x, y).submit(F.Eager())
     exp, _ = expected_gemm(host, x.float().cpu().numpy(), range(0, rows))
     assert O.rel_frobenius(y.cpu().numpy(), exp) <= REL_FROB_TOL
+
+
+def test_first_gemm_call_on_fresh_handle_recorded_in_graph(F, torch):
+    """The GEMM-side copies are built when the handle is created, so the very
+    first GEMM (and GEMV) call on a fresh handle can be recorded by the
+    reference's Graph sink (sink.rs:94-105): nothing allocates or
+    synchronises inside the calls."""
+    m, n, k = 256, 1024, 2048
+    w = F.synth_normal((n, k), seed=77, stream_id=1, std=0.02)
+    packed, scales, g = F.quantize_nvfp4(w)
+    h = F.HostNvfp4Matrix(packed.cpu().numpy(), scales.cpu().numpy(), g.cpu().numpy(), n, k)
+    W = h.upload()  # fresh handle: no GEMM has run on it
+    x = F.synth_normal((m, k), seed=5, stream_id=2, dtype=torch.bfloat16)
+    ws = torch.empty(int(F._native.lib.fpb_nvfp4_gemm_workspace_bytes(m, k)), dtype=torch.uint8, device="cuda")
+    y = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
+    yv = torch.full((1, n), float("nan"), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    sink = F.Graph()
+    with sink:
+        F.nvfp4_gemm(W, x, y, F.GemmTile(8, 128, 32), workspace=ws).submit(sink)
+        F.gemv(W, x[:1], yv).submit(sink)
+    assert torch.isnan(y).all()  # recorded, not run
+    sink.replay()
+    torch.cuda.synchronize()
+    assert F.device_error() == 0
+    exp, mag = expected_gemm(W.to_host(), x.float().cpu().numpy(), range(0, n))
+    got = y.cpu().numpy().astype(np.float64)
+    assert O.rel_frobenius(got, exp) <= REL_FROB_TOL
+    hh = W.to_host()
+    ref_v = O.nvfp4_gemv_f32(hh.packed, hh.scales, hh.row_scales, n, k, x[:1].float().cpu().numpy())
+    assert O.rel_frobenius(yv.cpu().numpy(), ref_v) <= REL_FROB_TOL

@@ -150,3 +150,17 @@ def test_gpu_calls_fail_cleanly_without_a_device():
                                        C.byref(out))
     assert st in (N.FPB_ERR_NO_DEVICE, N.FPB_ERR_CUDA)
     assert out.value is None
+
+
+def test_comm_host_side():
+    """NCCL loads at run time; the unique id needs no GPU; bad ranks are
+    rejected before any NCCL call."""
+    if not N.lib.fpb_comm_available():
+        pytest.skip("libnccl.so.2 not present")
+    uid = (C.c_uint8 * N.FPB_COMM_ID_BYTES)()
+    assert N.lib.fpb_comm_unique_id(uid) == N.FPB_OK
+    assert any(uid)
+    h = C.c_void_p()
+    assert N.lib.fpb_comm_init(uid, 2, 2, 0, C.byref(h)) == N.FPB_ERR_INVALID_ARGUMENT
+    assert N.lib.fpb_comm_init(uid, 0, 0, 0, C.byref(h)) == N.FPB_ERR_INVALID_ARGUMENT
+    assert N.lib.fpb_status_string(N.FPB_ERR_COMM) == b"communication error"

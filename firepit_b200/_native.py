@@ -115,6 +115,10 @@ SIGNATURES: dict[str, tuple] = {
     "fpb_nvfp4_matrix_prepare_glu": (i32, [vp, sz, vp]),
     "fpb_nvfp4_gemm_q": (i32, [vp, sz, sz, vp, vp, vp, sz, vp, i32, vp]),
     "fpb_nvfp4_gemm": (i32, [vp, sz, sz, vp, i32, sz, vp, i32, vp, sz, vp]),
+    "fpb_nvfp4_gemm_hilo_workspace_bytes": (sz, [sz, sz, sz, i32]),
+    "fpb_nvfp4_gemm_hilo": (i32, [vp, sz, sz, vp, i32, sz, vp, i32, vp, sz, vp]),
+    "fpb_fp8_gemm_hilo_workspace_bytes": (sz, [sz, sz, sz, i32, i32]),
+    "fpb_fp8_gemm_hilo": (i32, [vp, sz, sz, vp, i32, sz, vp, i32, vp, sz, vp]),
     "fpb_nvfp4_grouped_gemm_q": (i32, [vp, vp, vp, vp, sz, vp, vp, sz, vp, i32, vp]),
     "fpb_device_error": (i32, [C.POINTER(i32), i32]),
     "fpb_fp8_validate": (i32, [sz, vp, sz, sz, sz, sz, sz]),

@@ -941,3 +941,103 @@ extern "C" int fpb_fp8_grouped_gemm_q(fpb_fp8_matrix *w, const uint8_t *a_bits, 
   return fp8_gemm_launch(w, a_bits, a_scales, padded_rows, 0, rows_per_expert, tile_experts, y, y_dtype,
                          as_stream(stream));
 }
+
+// ---- the reference's activation semantics (gemm/mod.rs:87-100, 155-168) -----------------
+// fp8_gemm_kernel multiplies the f32 activations by the weight block scale,
+// splits them into bf16 hi + lo and multiplies both by the e4m3 weights as
+// bf16 (exact); fp8_rows_gemm_kernel does the same without the scale and
+// multiplies the f32 sums by the row scale.  Here the weights go to bf16 in
+// the caller's workspace: with row scales the exact e4m3 values (the row
+// scale is applied in the epilogue); with block scales w * s split into hi
+// and lo (the scale folded into the weights instead of the activations: the
+// same product to within the bf16 hi + lo precision, about 2^-16 relative).
+// The GEMM is the tcgen05 bf16 mode of the NVFP4 kernel, one pass per (A, B)
+// pair: hi.W (+ lo.W) with row scales; hi.Whi + hi.Wlo + lo.Whi with blocks.
+namespace fpb {
+__global__ void fp8_to_bf16_kernel(const uint8_t *bits, const float *scales, size_t rows, size_t cols, int block_n,
+                                   int block_k, size_t scale_cols, __nv_bfloat16 *hi, __nv_bfloat16 *lo) {
+  pdl_enter();
+  const size_t n = rows * cols, stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const float v = e4m3_to_f32(bits[i]);
+    if (!lo) {
+      hi[i] = __float2bfloat16_rn(v);  // exact: e4m3 values are bf16 values
+      continue;
+    }
+    const size_t r = i / cols, c = i % cols;
+    const float w = v * scales[(r / block_n) * scale_cols + c / block_k];
+    const __nv_bfloat16 h = __float2bfloat16_rn(w);
+    hi[i] = h;
+    lo[i] = __float2bfloat16_rn(w - __bfloat162float(h));
+  }
+}
+
+static unsigned f8_grid_for(size_t n) {
+  size_t g = (n + 255) / 256, cap = (size_t)sm_count() * 16;
+  return (unsigned)std::max<size_t>(1, std::min(g, cap));
+}
+}  // namespace fpb
+
+extern "C" size_t fpb_fp8_gemm_hilo_workspace_bytes(size_t m, size_t rows, size_t k, int x_dtype, int blocks) {
+  return hilo_workspace_bytes(m, k, x_dtype) + (blocks ? 2 : 1) * align256(rows * k * 2) + 256;
+}
+
+extern "C" int fpb_fp8_gemm_hilo(fpb_fp8_matrix *w, size_t row_begin, size_t row_end, const void *x, int x_dtype,
+                                 size_t m, void *y, int y_dtype, void *workspace, size_t workspace_bytes,
+                                 void *stream) {
+  if (!w || !x || !y || !workspace) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_fp8_gemm_hilo: null pointer");
+  if (row_end == 0) row_end = w->rows;
+  if (row_begin >= row_end || row_end > w->rows)
+    return fail(FPB_ERR_SHAPE, "fpb_fp8_gemm_hilo: row range [%zu, %zu) outside %zu rows", row_begin, row_end,
+                w->rows);
+  const bool blocks = w->block_n != 0;
+  if (blocks && row_begin % (size_t)w->block_n)
+    return fail(FPB_ERR_SHAPE, "fpb_fp8_gemm_hilo: row_begin %zu not a multiple of block_n %d", row_begin,
+                w->block_n);
+  if (m == 0 || m > (size_t)65535 * 128) return fail(FPB_ERR_SHAPE, "fpb_fp8_gemm_hilo: m = %zu", m);
+  if ((x_dtype != FPB_F32 && x_dtype != FPB_BF16) || (y_dtype != FPB_F32 && y_dtype != FPB_BF16))
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_fp8_gemm_hilo: dtype");
+  if (w->cols % 8) return fail(FPB_ERR_SHAPE, "fpb_fp8_gemm_hilo: cols %zu not a multiple of 8", w->cols);
+  const size_t rows = row_end - row_begin, k = w->cols;
+  const size_t need = fpb_fp8_gemm_hilo_workspace_bytes(m, rows, k, x_dtype, blocks);
+  if (workspace_bytes < need)
+    return fail(FPB_ERR_WORKSPACE, "fpb_fp8_gemm_hilo: workspace %zu < %zu bytes", workspace_bytes, need);
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255) || (reinterpret_cast<uintptr_t>(x) & 15))
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_fp8_gemm_hilo: workspace 256-byte and x 16-byte aligned");
+  cudaStream_t s = as_stream(stream);
+  uint8_t *ws = static_cast<uint8_t *>(workspace);
+  const void *hi, *lo;
+  size_t used = 0;
+  int st = hilo_activations(x, x_dtype, m, k, ws, &hi, &lo, &used, s);
+  if (st) return st;
+  __nv_bfloat16 *whi = reinterpret_cast<__nv_bfloat16 *>(ws + used);
+  __nv_bfloat16 *wlo = blocks ? reinterpret_cast<__nv_bfloat16 *>(ws + used + align256(rows * k * 2)) : nullptr;
+  const float *sc = blocks ? w->scales + (row_begin / w->block_n) * (k / w->block_k) : w->scales;
+  launch_pdl(fp8_to_bf16_kernel, f8_grid_for(rows * k), 256, 0, s, w->bits + row_begin * k, sc, rows, k,
+             w->block_n, w->block_k, blocks ? k / w->block_k : 0, whi, wlo);
+  FPB_LAUNCH_CHECK("fp8_to_bf16_kernel");
+  F16Gemm g{};
+  g.m = m;
+  g.n = rows;
+  g.k = k;
+  g.a[0] = hi;
+  g.a[1] = lo;
+  g.b[0] = whi;
+  g.b[1] = wlo;
+  if (blocks) {
+    // hi.Whi, hi.Wlo, then lo.Whi (lo.Wlo is below f32 rounding of the sum)
+    g.passes = lo ? 3 : 2;
+    g.a_sel[0] = 0, g.b_sel[0] = 0;
+    g.a_sel[1] = 0, g.b_sel[1] = 1;
+    g.a_sel[2] = 1, g.b_sel[2] = 0;
+    g.b_globals = nullptr;
+  } else {
+    g.passes = lo ? 2 : 1;
+    g.a_sel[0] = 0, g.b_sel[0] = 0;
+    g.a_sel[1] = 1, g.b_sel[1] = 0;
+    g.b_globals = w->scales + row_begin;
+  }
+  g.y = y;
+  g.y_bf16 = y_dtype == FPB_BF16;
+  return run_f16_gemm(g, s);
+}

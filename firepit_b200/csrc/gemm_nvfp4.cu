@@ -151,6 +151,14 @@ struct GemmParams {
   // stores nothing, and padding rows are left out of the amax (so their
   // activations may hold anything, e.g. rows an encoder skipped).
   const int32_t *row_tokens;
+  // bf16 mode (tcgen05 kind::f16, the reference's hi/lo activations): tiles
+  // hold 64 bf16 per 128-byte row; each K block runs `passes` (A, B) pairs,
+  // A from tmap_a (a_sel 0) or tmap_a2 (1), B from tmap_b (b_sel 0) or
+  // tmap_b64 (1), all accumulated in the same TMEM accumulator; no scale
+  // factors, ga = 1, and b_globals may be null (factor 1).
+  int f16;
+  int passes;
+  int a_sel[3], b_sel[3];
 };
 
 constexpr int kTileBytes = kBM * kBKBytes;   // 16 KB per operand per stage
@@ -200,7 +208,7 @@ __device__ __forceinline__ bool gemm_tile(const GemmParams &p, int t, int n_tile
 __global__ void __launch_bounds__(kGemmThreads, 1)
     nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                       const __grid_constant__ CUtensorMap tmap_y, const __grid_constant__ CUtensorMap tmap_b64,
-                      GemmParams p) {
+                      const __grid_constant__ CUtensorMap tmap_a2, GemmParams p) {
   using namespace sm100;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -220,6 +228,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int n_tiles = (p.N + kBN - 1) / kBN, m_tiles = (p.M + kBM - 1) / kBM;
   const int total = n_tiles * m_tiles;
   const int kb64_per_rb = p.kb_count * 4;
+  // K blocks as the producer and the MMA issuer walk them (bf16 mode: each
+  // block once per (A, B) pass).
+  const int vblocks = p.f16 ? p.kb_count * p.passes : p.kb_count;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -235,7 +246,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     prefetch_tensormap(&tmap_a);
     prefetch_tensormap(&tmap_b);
     if (p.tma_store) prefetch_tensormap(&tmap_y);
-    if (p.glu) prefetch_tensormap(&tmap_b64);
+    if (p.glu || p.f16) prefetch_tensormap(&tmap_b64);
+    if (p.f16) prefetch_tensormap(&tmap_a2);
   }
   if (warp == 1) {
     tmem_alloc(tmem_base_s, kTmemCols);
@@ -258,13 +270,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         int m_tile, n_tile, n_base;
         if (!gemm_tile(p, t, n_tiles, m_tile, n_tile, n_base)) continue;
         const int nb_global = n_base / 128 + n_tile;
-        for (int kb = 0; kb < p.kb_count; ++kb, ++it) {
+        for (int vb = 0; vb < vblocks; ++vb, ++it) {
           const int s = it % kStages;
           if (it >= kStages && !mbar_wait(&empty[s], ((it / kStages) - 1) & 1, abort_s)) {
             report(p.error, abort_s, 101);
             ok = false;
             break;
           }
+          if (p.f16) {
+            const int kb = vb / p.passes, j = vb - kb * p.passes;
+            mbar_arrive_expect_tx(&full[s], 2 * kTileBytes);
+            tma_load_2d(sA + s * kTileBytes, p.a_sel[j] ? &tmap_a2 : &tmap_a, kb * kBKBytes, m_tile * kBM,
+                        &full[s]);
+            tma_load_2d(sB + s * kTileBytes, p.b_sel[j] ? &tmap_b64 : &tmap_b, kb * kBKBytes,
+                        n_base + n_tile * kBN, &full[s]);
+            continue;
+          }
+          const int kb = vb;
           mbar_arrive_expect_tx(&full[s], 2 * kTileBytes + 2 * kSfStageBytes);
           tma_load_2d(sA + s * kTileBytes, &tmap_a, kb * kBKBytes, m_tile * kBM, &full[s]);
           if (p.glu) {
@@ -289,7 +311,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 1) {
     // ---- MMA issuer -------------------------------------------------------------
     if (elect_one()) {
-      const uint32_t idesc = idesc_nvf4(kBM, kBN);
+      const uint32_t idesc = p.f16 ? idesc_bf16(kBM, kBN) : idesc_nvf4(kBM, kBN);
       uint32_t it = 0, lt = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
@@ -302,7 +324,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         tc_fence_after();
         const uint32_t tmem_acc = tmem + buf * kBN;
-        for (int kb = 0; kb < p.kb_count; ++kb, ++it) {
+        for (int vb = 0; vb < vblocks; ++vb, ++it) {
           const int s = it % kStages;
           if (!mbar_wait(&full[s], (it / kStages) & 1, abort_s)) {
             report(p.error, abort_s, 103);
@@ -310,6 +332,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             break;
           }
           tc_fence_after();
+          if (p.f16) {
+            // four K = 16 steps of bf16 over the stage's 64 columns
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t a_desc = smem_desc(smem_u32(sA + s * kTileBytes) + kk * 32, 16, 1024, 2);
+              const uint64_t b_desc = smem_desc(smem_u32(sB + s * kTileBytes) + kk * 32, 16, 1024, 2);
+              mma_bf16(tmem_acc, a_desc, b_desc, idesc, (vb | kk) != 0);
+            }
+            tc_commit(&empty[s]);
+            continue;
+          }
+          const int kb = vb;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             tmem_cp_sf(tmem + kTmemSfa + s * 16 + kk * 4,
@@ -338,7 +372,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // columns ch*32 .. +31); each warp stages and stores its own boxes.
     const int qw = warp & 3, ch = (warp - 2) >> 2;
     const uint32_t lane_base = (uint32_t)(qw * 32) << 16;
-    const float ga = __ldg(p.a_global);
+    const float ga = p.f16 ? 1.0f : __ldg(p.a_global);
     uint8_t *stage = sOut + qw * kOutWarpBytes;
     uint8_t *row_s = stage + lane * 128;
     uint32_t lt = 0;
@@ -362,7 +396,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           const int n = n0 + ch * 64 + c * 32 + lane;
-          gl[c] = n < p.N ? __ldg(p.b_globals + n_base + n) : 0.0f;
+          gl[c] = n < p.N ? (p.b_globals ? __ldg(p.b_globals + n_base + n) : 1.0f) : 0.0f;
         }
       }
       if (!mbar_wait(&acc_full[buf], (lt >> 1) & 1, abort_s)) {
@@ -793,7 +827,7 @@ extern "C" int fpb_nvfp4_gemm_q(fpb_nvfp4_matrix *w, size_t row_begin, size_t ro
   const size_t tiles = (size_t)((p.N + kBN - 1) / kBN) * ((m + kBM - 1) / kBM);
   const unsigned grid = (unsigned)std::min<size_t>(tiles, (size_t)std::max(1, sm_count()));
   launch_pdl(nvfp4_gemm_kernel, grid, kGemmThreads, kGemmSmem, s, tmap_a, *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b),
-                                                 tmap_y, *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b), p);
+                                                 tmap_y, *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b), tmap_a, p);
   FPB_LAUNCH_CHECK("nvfp4_gemm_kernel");
   return FPB_OK;
 }
@@ -870,7 +904,7 @@ extern "C" int fpb_nvfp4_grouped_gemm_q(fpb_nvfp4_matrix *w, const uint8_t *a_pa
   const size_t tiles = (rows_per_expert / kBN) * (padded_rows / kBM);
   const unsigned grid = (unsigned)std::min<size_t>(tiles, (size_t)std::max(1, sm_count()));
   launch_pdl(nvfp4_gemm_kernel, grid, kGemmThreads, kGemmSmem, s, tmap_a, *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b),
-                                                 tmap_y, *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b), p);
+                                                 tmap_y, *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b), tmap_a, p);
   FPB_LAUNCH_CHECK("nvfp4_gemm_kernel(grouped)");
   return FPB_OK;
 }
@@ -961,7 +995,7 @@ extern "C" int fpb_nvfp4_grouped_gemm_swiglu_q(fpb_nvfp4_matrix *w, const uint8_
   const unsigned grid = (unsigned)std::min<size_t>(tiles, (size_t)std::max(1, sm_count()));
   launch_pdl(nvfp4_gemm_kernel, grid, kGemmThreads, kGemmSmem, s, tmap_a, *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b),
                                                  tmap_y, *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b64),
-                                                 p);
+                                                 tmap_a, p);
   FPB_LAUNCH_CHECK("nvfp4_gemm_kernel(grouped swiglu)");
   return FPB_OK;
 }
@@ -991,4 +1025,149 @@ extern "C" int fpb_device_error(int *out, int reset) {
     FPB_CUDA_TRY(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)));
   }
   return FPB_OK;
+}
+
+// ---- the reference's activation semantics: bf16 hi + lo on bf16 weights ----------------
+// gemm/nvfp4.rs:33-50 keeps the activations in f32 and multiplies their bf16
+// hi and lo halves (hi = bf16(x), lo = bf16(x - hi)) by the weights
+// dequantized to bf16 (E2M1 * e4m3 scale, exact in bf16), accumulating in
+// f32, then scales by the row global.  Here: the split and the dequantized
+// weights go to the caller's workspace (two element-wise launches), then the
+// persistent GEMM kernel runs in its bf16 mode (tcgen05 kind::f16), one pass
+// per (A, B) pair of each K block.
+namespace fpb {
+
+// hi = bf16(x) (round to nearest even), lo = bf16(x - hi), x f32 [n].
+__global__ void split_hilo_kernel(const float *x, size_t n, __nv_bfloat16 *hi, __nv_bfloat16 *lo) {
+  pdl_enter();
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const float v = x[i];
+    const __nv_bfloat16 h = __float2bfloat16_rn(v);
+    hi[i] = h;
+    if (lo) lo[i] = __float2bfloat16_rn(v - __bfloat162float(h));
+  }
+}
+
+// Rows of an NVFP4 matrix as bf16 E2M1 * e4m3 scale (exact; no row global),
+// one thread per code byte.
+__global__ void nvfp4_to_bf16_kernel(const uint8_t *packed, const uint8_t *scales, size_t rows, size_t cols,
+                                     __nv_bfloat162 *out) {
+  pdl_enter();
+  const size_t n = rows * cols / 2, stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const size_t r = (2 * i) / cols, c = (2 * i) % cols;
+    const float s = e4m3_to_f32(scales[r * (cols / 16) + c / 16]);
+    const uint8_t b = packed[i];
+    out[i] = __floats2bfloat162_rn(e2m1_to_f32(b & 0xf) * s, e2m1_to_f32(b >> 4) * s);
+  }
+}
+
+int run_f16_gemm(const F16Gemm &g, cudaStream_t s) {
+  if (int st = ensure_gemm_attr()) return st;
+  CUtensorMap ta, ta2, tb, tb2, ty{};
+  int st;
+  if ((st = encode_rows_u8(&ta, g.a[0], g.m, g.k * 2, kBM))) return st;
+  if ((st = encode_rows_u8(&ta2, g.a[1] ? g.a[1] : g.a[0], g.m, g.k * 2, kBM))) return st;
+  if ((st = encode_rows_u8(&tb, g.b[0], g.n, g.k * 2, kBN))) return st;
+  if ((st = encode_rows_u8(&tb2, g.b[1] ? g.b[1] : g.b[0], g.n, g.k * 2, kBN))) return st;
+  int *err = nullptr;
+  FPB_CUDA_TRY(cudaGetSymbolAddress(reinterpret_cast<void **>(&err), g_device_error));
+  GemmParams p{};
+  p.b_globals = g.b_globals;
+  p.y = g.y;
+  p.N = (int)g.n;
+  p.ldy = p.N;
+  p.y_bf16 = g.y_bf16;
+  p.M = (int)g.m;
+  p.n_base = 0;
+  p.kb_count = (int)((g.k + 63) / 64);
+  p.error = err;
+  p.f16 = 1;
+  p.passes = g.passes;
+  for (int j = 0; j < 3; ++j) {
+    p.a_sel[j] = g.a_sel[j];
+    p.b_sel[j] = g.b_sel[j];
+  }
+  p.tma_store = encode_store_map(&ty, g.y, p.y_bf16, g.m, p.N, p.ldy, 32, 0);
+  const size_t tiles = (size_t)((p.N + kBN - 1) / kBN) * ((g.m + kBM - 1) / kBM);
+  const unsigned grid = (unsigned)std::min<size_t>(tiles, (size_t)std::max(1, sm_count()));
+  launch_pdl(nvfp4_gemm_kernel, grid, kGemmThreads, kGemmSmem, s, ta, tb, ty, tb2, ta2, p);
+  FPB_LAUNCH_CHECK("nvfp4_gemm_kernel(bf16)");
+  return FPB_OK;
+}
+
+// Activations for the bf16 mode: bf16 x is read in place (lo = 0: one
+// pass); f32 x is split into hi and lo in the workspace.  Returns the bytes
+// of workspace used.
+int hilo_activations(const void *x, int x_dtype, size_t m, size_t k, uint8_t *ws, const void **hi,
+                     const void **lo, size_t *used, cudaStream_t s) {
+  *used = 0;
+  if (x_dtype == FPB_BF16) {
+    *hi = x;
+    *lo = nullptr;
+    return FPB_OK;
+  }
+  __nv_bfloat16 *h = reinterpret_cast<__nv_bfloat16 *>(ws);
+  __nv_bfloat16 *l = reinterpret_cast<__nv_bfloat16 *>(ws + align256(m * k * 2));
+  launch_pdl(split_hilo_kernel, grid_for(m * k), 256, 0, s, static_cast<const float *>(x), m * k, h, l);
+  FPB_LAUNCH_CHECK("split_hilo_kernel");
+  *hi = h;
+  *lo = l;
+  *used = 2 * align256(m * k * 2);
+  return FPB_OK;
+}
+
+size_t hilo_workspace_bytes(size_t m, size_t k, int x_dtype) {
+  return x_dtype == FPB_BF16 ? 0 : 2 * align256(m * k * 2);
+}
+
+}  // namespace fpb
+
+extern "C" size_t fpb_nvfp4_gemm_hilo_workspace_bytes(size_t m, size_t rows, size_t k, int x_dtype) {
+  return hilo_workspace_bytes(m, k, x_dtype) + align256(rows * k * 2) + 256;
+}
+
+extern "C" int fpb_nvfp4_gemm_hilo(fpb_nvfp4_matrix *w, size_t row_begin, size_t row_end, const void *x,
+                                   int x_dtype, size_t m, void *y, int y_dtype, void *workspace,
+                                   size_t workspace_bytes, void *stream) {
+  if (!w || !x || !y || !workspace) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_gemm_hilo: null pointer");
+  if (row_end == 0) row_end = w->rows;
+  if (row_begin >= row_end || row_end > w->rows)
+    return fail(FPB_ERR_SHAPE, "fpb_nvfp4_gemm_hilo: row range [%zu, %zu) outside %zu rows", row_begin, row_end,
+                w->rows);
+  if (m == 0 || m > (size_t)65535 * kBM) return fail(FPB_ERR_SHAPE, "fpb_nvfp4_gemm_hilo: m = %zu", m);
+  if ((x_dtype != FPB_F32 && x_dtype != FPB_BF16) || (y_dtype != FPB_F32 && y_dtype != FPB_BF16))
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_gemm_hilo: dtype");
+  const size_t rows = row_end - row_begin, k = w->cols;
+  const size_t need = fpb_nvfp4_gemm_hilo_workspace_bytes(m, rows, k, x_dtype);
+  if (workspace_bytes < need)
+    return fail(FPB_ERR_WORKSPACE, "fpb_nvfp4_gemm_hilo: workspace %zu < %zu bytes", workspace_bytes, need);
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255) || (reinterpret_cast<uintptr_t>(x) & 15))
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_gemm_hilo: workspace 256-byte and x 16-byte aligned");
+  cudaStream_t s = as_stream(stream);
+  uint8_t *ws = static_cast<uint8_t *>(workspace);
+  const void *hi, *lo;
+  size_t used = 0;
+  int st = hilo_activations(x, x_dtype, m, k, ws, &hi, &lo, &used, s);
+  if (st) return st;
+  __nv_bfloat162 *wb = reinterpret_cast<__nv_bfloat162 *>(ws + used);
+  launch_pdl(nvfp4_to_bf16_kernel, grid_for(rows * k / 2), 256, 0, s, w->packed + row_begin * (k / 2),
+             w->scales + row_begin * (k / 16), rows, k, wb);
+  FPB_LAUNCH_CHECK("nvfp4_to_bf16_kernel");
+  F16Gemm g{};
+  g.m = m;
+  g.n = rows;
+  g.k = k;
+  g.a[0] = hi;
+  g.a[1] = lo;
+  g.b[0] = wb;
+  g.b[1] = nullptr;
+  g.passes = lo ? 2 : 1;  // hi x W, then lo x W (gemm/nvfp4.rs:47-48)
+  g.a_sel[0] = 0, g.b_sel[0] = 0;
+  g.a_sel[1] = 1, g.b_sel[1] = 0;
+  g.b_globals = w->row_globals + row_begin;
+  g.y = y;
+  g.y_bf16 = y_dtype == FPB_BF16;
+  return run_f16_gemm(g, s);
 }

@@ -155,6 +155,15 @@ __device__ __forceinline__ void mma_f8(uint32_t d_tmem, uint64_t a_desc, uint64_
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 
+// D(tmem) (+)= A(smem) x B(smem)^T for kind::f16 (bf16 x bf16 -> f32, K = 16).
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
 // Copies a 512-byte scale-factor chunk (32 rows x 16 bytes) from shared
 // memory to TMEM, replicated to the four 32-lane quarters.
 __device__ __forceinline__ void tmem_cp_sf(uint32_t taddr, uint64_t sdesc) {
@@ -254,6 +263,14 @@ __host__ __device__ constexpr uint32_t idesc_nvf4(int M, int N) {
 __host__ __device__ constexpr uint32_t idesc_f8(int M, int N) {
   return (1u << 4)                 // c_format F32
          | (0u << 7) | (0u << 10)  // E4M3, E4M3
+         | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// Instruction descriptor of kind::f16 with bf16 A and B (format 1), K-major,
+// D = f32 (c_format 1), M x N.
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
+  return (1u << 4)                 // c_format F32
+         | (1u << 7) | (1u << 10)  // a_format, b_format BF16
          | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 

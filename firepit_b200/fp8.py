@@ -191,7 +191,16 @@ def _check(weight: Fp8Matrix, tile: GemmTile, rows: range, m: int, x, y) -> None
 
 
 class Fp8Gemm:
-    def __init__(self, weight: Fp8Matrix, x, y, tile: GemmTile, rows: range | None = None, workspace=None):
+    """``act="e4m3"`` (default): activations quantized per
+    token to e4m3, tcgen05 kind::f8f6f4.  ``act="hilo"``: the reference's
+    numerics (gemm/mod.rs:87-100, 155-168), f32 activations as bf16 hi + lo
+    on tcgen05 kind::f16; any block sizes that divide the matrix."""
+
+    def __init__(self, weight: Fp8Matrix, x, y, tile: GemmTile, rows: range | None = None, workspace=None,
+                 act: str = "e4m3"):
+        if act not in ("e4m3", "hilo"):
+            raise ValueError(f"act must be 'e4m3' or 'hilo', not {act!r}")
+        self.act = act
         self.weight, self.x, self.y, self.tile = weight, x, y, tile
         self.rows = rows if rows is not None else range(0, weight.rows)
         _check(weight, tile, self.rows, x.shape[0], x, y)
@@ -201,30 +210,37 @@ class Fp8Gemm:
         import torch
         sink = sink or Eager()
         m = self.x.shape[0]
-        # activations + the stream-K partial sums of this row range
-        need = int(N.lib.fpb_fp8_gemm_workspace_bytes(m, self.weight.cols)) + int(
-            N.lib.fpb_fp8_gemm_split_bytes(m, self.weight.cols, len(self.rows)))
+        fn = "fpb_fp8_gemm"
+        if self.act == "hilo":
+            fn = "fpb_fp8_gemm_hilo"
+            need = int(N.lib.fpb_fp8_gemm_hilo_workspace_bytes(m, len(self.rows), self.weight.cols,
+                                                                _dtype_code(self.x), int(not self.weight.scaling.is_rows)))
+        else:
+            # activations + the stream-K partial sums of this row range
+            need = int(N.lib.fpb_fp8_gemm_workspace_bytes(m, self.weight.cols)) + int(
+                N.lib.fpb_fp8_gemm_split_bytes(m, self.weight.cols, len(self.rows)))
         ws = self.workspace
         if ws is None or ws.numel() * ws.element_size() < need:
             ws = torch.empty(need, dtype=torch.uint8, device=self.x.device)
             self.workspace = ws
 
         def launch(stream):
-            N.call("fpb_fp8_gemm", self.weight.handle, self.rows.start, self.rows.stop, self.x.data_ptr(),
+            N.call(fn, self.weight.handle, self.rows.start, self.rows.stop, self.x.data_ptr(),
                    _dtype_code(self.x), m, self.y.data_ptr(), _dtype_code(self.y), ws.data_ptr(), need, stream)
 
         sink.run("fp8_gemm", launch)
 
 
-def fp8_gemm(weight: Fp8Matrix, x, y, tile: GemmTile = GemmTile(64, 128, 32), workspace=None) -> Fp8Gemm:
+def fp8_gemm(weight: Fp8Matrix, x, y, tile: GemmTile = GemmTile(64, 128, 32), workspace=None,
+             act: str = "e4m3") -> Fp8Gemm:
     """gemm/mod.rs:424-442."""
-    return Fp8Gemm(weight, x, y, tile, None, workspace)
+    return Fp8Gemm(weight, x, y, tile, None, workspace, act)
 
 
 def fp8_gemm_view(weight: Fp8Matrix, rows: range, x, y, tile: GemmTile = GemmTile(64, 128, 32),
-                  workspace=None) -> Fp8Gemm:
+                  workspace=None, act: str = "e4m3") -> Fp8Gemm:
     """gemm/mod.rs:579-608."""
-    return Fp8Gemm(weight, x, y, tile, rows, workspace)
+    return Fp8Gemm(weight, x, y, tile, rows, workspace, act)
 
 
 def fp8_grouped_gemm_q(weight: Fp8Matrix, a_bits, a_scales, tile_experts, rows_per_expert: int, y,

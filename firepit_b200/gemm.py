@@ -2,10 +2,13 @@
 
 ``nvfp4_gemm(weight, x, y, tile).submit(sink)`` and
 ``nvfp4_gemm_view(weight, rows, x, y, tile).submit(sink)`` keep the
-reference's builder shape and its shape asserts (gemm/nvfp4.rs:119-206).  On
-B200 the activations are quantized to NVFP4 on the fly and both operands go
-through the block-scaled tensor cores (tcgen05.mma kind::mxf4nvf4); the tile
-argument is validated, the kernel tiles 128 x 128.
+reference's builder shape and its shape asserts (gemm/nvfp4.rs:119-206).  Two
+activation modes: ``act="nvfp4"`` (default) quantizes the
+activations to NVFP4 on the fly and both operands go through the block-scaled
+tensor cores (tcgen05.mma kind::mxf4nvf4); ``act="hilo"`` is the reference's
+own numerics (gemm/nvfp4.rs:33-50): f32 activations as bf16 hi + lo times the
+weights dequantized to bf16, on tcgen05 kind::f16.  The tile argument is
+validated; the kernel tiles 128 x 128.
 """
 from __future__ import annotations
 
@@ -45,7 +48,11 @@ def _check_tile(weight: Nvfp4Matrix, tile: GemmTile, rows: range, m: int) -> Non
 
 
 class Nvfp4Gemm:
-    def __init__(self, weight: Nvfp4Matrix, x, y, tile: GemmTile, rows: range | None = None, workspace=None):
+    def __init__(self, weight: Nvfp4Matrix, x, y, tile: GemmTile, rows: range | None = None, workspace=None,
+                 act: str = "nvfp4"):
+        if act not in ("nvfp4", "hilo"):
+            raise ValueError(f"act must be 'nvfp4' or 'hilo', not {act!r}")
+        self.act = act
         self.weight, self.x, self.y, self.tile = weight, x, y, tile
         self.rows = rows if rows is not None else range(0, weight.rows)
         m = x.shape[0]
@@ -60,28 +67,35 @@ class Nvfp4Gemm:
         import torch
         sink = sink or Eager()
         m = self.x.shape[0]
-        need = workspace_bytes(m, self.weight.cols)
+        if self.act == "hilo":
+            fn = "fpb_nvfp4_gemm_hilo"
+            need = int(N.lib.fpb_nvfp4_gemm_hilo_workspace_bytes(m, len(self.rows), self.weight.cols,
+                                                                  _dtype_code(self.x)))
+        else:
+            fn = "fpb_nvfp4_gemm"
+            need = workspace_bytes(m, self.weight.cols)
         ws = self.workspace
         if ws is None or ws.numel() * ws.element_size() < need:
             ws = torch.empty(need, dtype=torch.uint8, device=self.x.device)
             self.workspace = ws
 
         def launch(stream):
-            N.call("fpb_nvfp4_gemm", self.weight.handle, self.rows.start, self.rows.stop, self.x.data_ptr(),
+            N.call(fn, self.weight.handle, self.rows.start, self.rows.stop, self.x.data_ptr(),
                    _dtype_code(self.x), m, self.y.data_ptr(), _dtype_code(self.y), ws.data_ptr(), need, stream)
 
         sink.run("nvfp4_gemm", launch)
 
 
-def nvfp4_gemm(weight: Nvfp4Matrix, x, y, tile: GemmTile = DEFAULT_GEMM_TILE, workspace=None) -> Nvfp4Gemm:
+def nvfp4_gemm(weight: Nvfp4Matrix, x, y, tile: GemmTile = DEFAULT_GEMM_TILE, workspace=None,
+               act: str = "nvfp4") -> Nvfp4Gemm:
     """gemm/nvfp4.rs:131-143."""
-    return Nvfp4Gemm(weight, x, y, tile, None, workspace)
+    return Nvfp4Gemm(weight, x, y, tile, None, workspace, act)
 
 
 def nvfp4_gemm_view(weight: Nvfp4Matrix, rows: range, x, y, tile: GemmTile = DEFAULT_GEMM_TILE,
-                    workspace=None) -> Nvfp4Gemm:
+                    workspace=None, act: str = "nvfp4") -> Nvfp4Gemm:
     """gemm/nvfp4.rs:166-182."""
-    return Nvfp4Gemm(weight, x, y, tile, rows, workspace)
+    return Nvfp4Gemm(weight, x, y, tile, rows, workspace, act)
 
 
 def quantize_act(x, stream=None):

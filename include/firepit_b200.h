@@ -257,6 +257,17 @@ int fpb_nvfp4_gemm_q(fpb_nvfp4_matrix *w, size_t row_begin, size_t row_end, cons
 int fpb_nvfp4_gemm(fpb_nvfp4_matrix *w, size_t row_begin, size_t row_end, const void *x, int x_dtype,
                    size_t m, void *y, int y_dtype, void *workspace, size_t workspace_bytes,
                    void *stream);
+/* nvfp4_gemm / nvfp4_gemm_view with the reference's activation semantics
+ * (gemm/nvfp4.rs:33-50): x stays f32 (or bf16) and is split into bf16
+ * hi = bf16(x) and lo = bf16(x - hi); both multiply the weights dequantized
+ * to bf16 (E2M1 * e4m3, exact) with f32 accumulation on the tensor cores
+ * (tcgen05 kind::f16), then y[m, n] = g[n] * acc.  bf16 x has lo = 0 (one
+ * pass).  Any row_begin; x [m, K] 16-byte aligned; workspace 256-byte
+ * aligned, fpb_nvfp4_gemm_hilo_workspace_bytes(m, rows, K, x_dtype) bytes
+ * (the split activations and the rows' bf16 weights). */
+size_t fpb_nvfp4_gemm_hilo_workspace_bytes(size_t m, size_t rows, size_t k, int x_dtype);
+int fpb_nvfp4_gemm_hilo(fpb_nvfp4_matrix *w, size_t row_begin, size_t row_end, const void *x, int x_dtype,
+                        size_t m, void *y, int y_dtype, void *workspace, size_t workspace_bytes, void *stream);
 /* Grouped (MoE) GEMM on quantized activations; replaces
  * nvfp4_grouped_gemm_view (gemm/nvfp4.rs:209-264, kernel :56-107).  A holds
  * the prefill layout's padded_rows gathered rows (a multiple of 128: the
@@ -333,6 +344,17 @@ size_t fpb_fp8_gemm_split_bytes(size_t m, size_t k, size_t n);
  * K, rows) bytes also gets the stream-K schedule. */
 int fpb_fp8_gemm(fpb_fp8_matrix *w, size_t row_begin, size_t row_end, const void *x, int x_dtype, size_t m,
                  void *y, int y_dtype, void *workspace, size_t workspace_bytes, void *stream);
+/* fp8_gemm / fp8_gemm_view with the reference's activation semantics
+ * (gemm/mod.rs:87-100 blocks, 155-168 rows): f32 (or bf16) x as bf16 hi + lo
+ * times the e4m3 weights in bf16, f32 accumulation on the tensor cores.  Row
+ * scales multiply the sums (y = s[n] * acc); block scales (any block_n,
+ * block_k dividing the matrix) are folded into the weights, w * s split into
+ * bf16 hi + lo (the same product to about 2^-16).  row_begin a multiple of
+ * block_n; cols % 8 == 0; workspace 256-byte aligned,
+ * fpb_fp8_gemm_hilo_workspace_bytes(m, rows, K, x_dtype, blocks != 0). */
+size_t fpb_fp8_gemm_hilo_workspace_bytes(size_t m, size_t rows, size_t k, int x_dtype, int blocks);
+int fpb_fp8_gemm_hilo(fpb_fp8_matrix *w, size_t row_begin, size_t row_end, const void *x, int x_dtype, size_t m,
+                      void *y, int y_dtype, void *workspace, size_t workspace_bytes, void *stream);
 /* Grouped (MoE) GEMM, as fpb_nvfp4_grouped_gemm_q: row tile t (128 rows) of
  * a_bits [padded_rows, K] uses expert tile_experts[t]'s rows
  * [e*rows_per_expert, (e+1)*rows_per_expert); device error 306 on a bad id. */

@@ -59,7 +59,9 @@ struct GemvArgs {
   long long y_slot_stride;    // elements between the output rows of consecutive slots
   long long y_batch_stride;   // elements between output rows of consecutive batch rows
   int rows;                   // rows per slot
-  int K;
+  int K;                      // columns this launch covers (a slice of k_pitch when K > 4096)
+  int k_pitch;                // columns of a full weight row and of an x row
+  int accumulate;             // 1: y (f32) += this slice's sums
   int batch;
   int n_experts;  // expert mode: valid ids are [0, n_experts)
   int chunks;     // ceil(K / 128)
@@ -132,7 +134,7 @@ __global__ void __launch_bounds__(512, 1) gemv_nvfp4_kernel(GemvArgs a) {
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, q = lane & 3;
-  const int K = a.K, kb2 = K >> 1, kb16 = K >> 4;
+  const int K = a.K, kb2 = a.k_pitch >> 1, kb16 = a.k_pitch >> 4;  // kb2 / kb16: row pitches
   const int chunks = a.chunks, batch = a.batch;
   const int wk_count = a.wk, g_count = a.g;
   const int wk = warp % wk_count, gi = warp / wk_count;
@@ -208,7 +210,7 @@ __global__ void __launch_bounds__(512, 1) gemv_nvfp4_kernel(GemvArgs a) {
       const int k0 = (c_begin + cc) * 128 + q * 32;
       const bool ok = n < batch && k0 < K;
       const uint4 *src = reinterpret_cast<const uint4 *>(reinterpret_cast<const char *>(a.x) +
-                                                         (x_off + (long long)n * K + k0) * (XLO ? 4 : 2));
+                                                         (x_off + (long long)n * a.k_pitch + k0) * (XLO ? 4 : 2));
 #pragma unroll
       for (int v = 0; v < kVec; ++v) raw[ng][cc][v] = ok ? src[v] : make_uint4(0, 0, 0, 0);
     }
@@ -381,6 +383,7 @@ __global__ void __launch_bounds__(512, 1) gemv_nvfp4_kernel(GemvArgs a) {
           if (r < a.rows && n < batch) {
             float v = slot_ok ? vals[t] * gcur[t >> 1] : 0.0f;
             long long off = (long long)slot * a.y_slot_stride + (long long)n * a.y_batch_stride + r;
+            if (a.accumulate) v += reinterpret_cast<const float *>(a.y)[off];  // f32 y: later K slices
             if (a.y_bf16)
               reinterpret_cast<__nv_bfloat16 *>(a.y)[off] = __float2bfloat16_rn(v);
             else
@@ -819,7 +822,33 @@ static GemvKernel select_kernel(int C, int NG, bool xlo) {
   return nullptr;
 }
 
+static int run_gemv_slice(GemvArgs args, int slots, bool x_f32, cudaStream_t stream);
+
+// Rows longer than 4096 columns run as consecutive launches over 4096-column
+// slices of K, the later ones adding their sums to y (f32; every slice's sum
+// times the row global).
 static int run_gemv(GemvArgs args, int slots, bool x_f32, cudaStream_t stream) {
+  constexpr int kSlice = 4096;
+  args.k_pitch = args.K;
+  if (args.K <= kSlice) return run_gemv_slice(args, slots, x_f32, stream);
+  if (args.y_bf16)
+    return fail(FPB_ERR_UNSUPPORTED, "NVFP4 GEMV: K=%d > 4096 needs an f32 y (the sums of the K slices add there)",
+                args.K);
+  const int K = args.K;
+  for (int k0 = 0; k0 < K; k0 += kSlice) {
+    GemvArgs part = args;
+    part.K = std::min(kSlice, K - k0);
+    part.packed = args.packed + k0 / 2;
+    part.scales = args.scales + k0 / kNvfp4Group;
+    part.x = static_cast<const char *>(args.x) + (size_t)k0 * (x_f32 ? 4 : 2);
+    part.accumulate = k0 > 0;
+    int st = run_gemv_slice(part, slots, x_f32, stream);
+    if (st) return st;
+  }
+  return FPB_OK;
+}
+
+static int run_gemv_slice(GemvArgs args, int slots, bool x_f32, cudaStream_t stream) {
   GemvConfig cfg = pick_config(args.K);
   if (!cfg.C) return fail(FPB_ERR_UNSUPPORTED, "NVFP4 GEMV: K=%d exceeds 4096", args.K);
   args.chunks = (args.K + 127) / 128;
@@ -1023,7 +1052,6 @@ extern "C" int fpb_nvfp4_gemv(const fpb_nvfp4_matrix *w, size_t row_begin, size_
     return fail(FPB_ERR_UNSUPPORTED, "fpb_nvfp4_gemv: too many rows");
   if (reinterpret_cast<uintptr_t>(x) % 16 != 0)
     return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_gemv: x must be 16-byte aligned");
-  if (w->cols > 4096) return fail(FPB_ERR_UNSUPPORTED, "fpb_nvfp4_gemv: cols %zu > 4096", w->cols);
   GemvArgs a{};
   a.packed = w->packed + row_begin * (w->cols / 2);
   a.scales = w->scales + row_begin * (w->cols / kNvfp4Group);
@@ -1066,7 +1094,6 @@ extern "C" int fpb_nvfp4_expert_gemv(const fpb_nvfp4_matrix *w, const void *x, i
     return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_expert_gemv: dtype");
   if (reinterpret_cast<uintptr_t>(x) % 16 != 0)
     return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_expert_gemv: x must be 16-byte aligned");
-  if (w->cols > 4096) return fail(FPB_ERR_UNSUPPORTED, "fpb_nvfp4_expert_gemv: cols %zu > 4096", w->cols);
   GemvArgs a{};
   a.packed = w->packed;
   a.scales = w->scales;

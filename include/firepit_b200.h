@@ -159,7 +159,9 @@ int fpb_nvfp4_dequantize(const fpb_nvfp4_matrix *m, float *out, void *stream);
  * y[b, r] = g[r] * sum_k E2M1[w[r,k]] * e4m3(s[r,k/16]) * x[b,k]
  * for rows r in [row_begin, row_end) of the matrix (row_end == 0 means all
  * rows).  x: [batch, cols] (x_dtype), y: [batch, row_end-row_begin]
- * (y_dtype), both contiguous.  1 <= batch <= 16. */
+ * (y_dtype), both contiguous.  1 <= batch <= 16.  Any cols % 32 == 0: rows
+ * longer than 4096 columns run as consecutive launches over 4096-column
+ * slices that add their sums into y, which must then be f32. */
 int fpb_nvfp4_gemv(const fpb_nvfp4_matrix *w, size_t row_begin, size_t row_end,
                    const void *x, int x_dtype, void *y, int y_dtype, int batch,
                    void *stream);
@@ -193,7 +195,7 @@ int fpb_nvfp4_gemv_batched(const fpb_gemv_segment *segs, int count, int x_dtype,
  *   y[s, r] = sum over K of W[expert_ids[s]*rows_per_expert + r, :] . x[s*input_stride, :]
  * expert_ids: device int32 [slots] (ExpertSelection::indices, padding
  * entries beyond `slots` are not read).  x: [*, cols], y: [slots,
- * rows_per_expert]. */
+ * rows_per_expert].  cols > 4096 as fpb_nvfp4_gemv (f32 y). */
 int fpb_nvfp4_expert_gemv(const fpb_nvfp4_matrix *w, const void *x, int x_dtype,
                           const int32_t *expert_ids, int slots,
                           size_t rows_per_expert, int input_stride, void *y,

@@ -279,6 +279,39 @@ def test_gemv_errors_are_statuses(F, torch):
         F.gemv(m, torch.zeros(1, 96, device="cuda"), y)
     big, _ = _synthetic(F, torch, 32, 8192)
     xb = torch.zeros(1, 8192, device="cuda")
-    st = N.lib.fpb_nvfp4_gemv(big.handle, 0, 0, xb.data_ptr(), 0, y.data_ptr(), 0, 1, None)
+    # K > 4096 adds the K slices' sums in y, so it needs an f32 y
+    st = N.lib.fpb_nvfp4_gemv(big.handle, 0, 0, xb.data_ptr(), 0, y.data_ptr(), N.FPB_BF16, 1, None)
     assert st == N.FPB_ERR_UNSUPPORTED
     torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("rows,cols", [(512, 8192), (256, 4128), (128, 12288)])
+@pytest.mark.parametrize("batch", [1, 5])
+@pytest.mark.parametrize("xdt", ["bf16", "f32"])
+def test_gemv_long_rows(F, torch, rows, cols, batch, xdt):
+    """K > 4096 (the reference loops any K that is a multiple of 32,
+    gemv/nvfp4.rs:34): consecutive 4096-column slices add into f32 y."""
+    m, h = _synthetic(F, torch, rows, cols, seed=cols)
+    x = O.synth_normal(batch * cols, seed=batch, stream=2).reshape(batch, cols)
+    xt = torch.from_numpy(x).cuda().to(torch.bfloat16 if xdt == "bf16" else torch.float32)
+    xf = xt.float().cpu().numpy()
+    y = torch.full((batch, rows), float("nan"), device="cuda")
+    F.gemv(m, xt, y, F.GemvTile(16, 1)).submit(F.Eager())  # 4128 = 129 blocks of 32
+    ref = O.nvfp4_gemv_f32(h.packed, h.scales, h.row_scales, rows, cols, xf)
+    assert O.rel_frobenius(y.cpu().numpy(), ref) <= REL_FROB_TOL
+    e64, mag = O.nvfp4_gemv_f64(h.packed, h.scales, h.row_scales, rows, cols, xf)
+    assert O.inner_product_excess(y.cpu().numpy(), e64, mag, cols + 2) <= 1.0
+
+
+def test_expert_gemv_long_rows(F, torch):
+    experts, rpe, cols = 4, 256, 6144
+    m, h = _synthetic(F, torch, experts * rpe, cols, seed=17, rpg=rpe)
+    ids = np.array([2, 0, 3], np.int32)
+    x = O.bf16_to_f32(O.bf16_bits(O.synth_normal(len(ids) * cols, seed=6, stream=2))).reshape(len(ids), cols)
+    y_ref = O.nvfp4_expert_gemv_f32(h.packed, h.scales, h.row_scales, cols, ids, rpe, 1, x)
+    xt = torch.from_numpy(x).cuda().to(torch.bfloat16)
+    y = torch.full((len(ids), rpe), float("nan"), device="cuda")
+    dims = F.MoeDims.new(2048, 512, 512, experts, len(ids))
+    sel = F.ExpertSelection.parse(ids, np.full(len(ids), 0.2, np.float32), dims)
+    F.expert_gemv_weight_view(m, xt, sel, y, rpe, 1).submit(F.Eager())
+    assert O.rel_frobenius(y.cpu().numpy(), y_ref) <= REL_FROB_TOL

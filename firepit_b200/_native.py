@@ -150,6 +150,18 @@ SIGNATURES: dict[str, tuple] = {
     "fpb_moe_combine_add_norm": (i32, [vp, i32, sz, sz, vp, vp, sz, sz, sz, vp, vp, C.c_float, vp, vp, vp]),
     "fpb_moe_route_dest": (i32, [vp, sz, sz, sz, sz, vp, vp]),
     "fpb_moe_route_meta": (i32, [vp, vp, sz, sz, sz, sz, sz, vp, vp]),
+    "fpb_embedding": (i32, [vp, sz, sz, vp, sz, vp, vp]),
+    "fpb_rms_norm": (i32, [vp, i32, sz, vp, vp, sz, sz, vp, C.c_float, vp, i32, sz, vp]),
+    "fpb_attn_prepare": (i32, [vp, sz, vp, sz, vp, sz, vp, vp, vp, sz, sz, sz, sz, sz, C.c_float, C.c_float, sz,
+                               vp, vp, vp, vp]),
+    "fpb_attn_decode_workspace_bytes": (sz, [sz, sz, sz, sz, sz]),
+    "fpb_attn_decode": (i32, [vp, vp, vp, vp, vp, sz, sz, sz, sz, sz, sz, sz, C.c_float, vp, sz, vp, i32, vp]),
+    "fpb_gdn_conv": (i32, [vp, sz, vp, vp, sz, sz, sz, vp, vp]),
+    "fpb_gdn_delta": (i32, [vp, vp, vp, sz, vp, vp, vp, sz, sz, sz, sz, sz, C.c_float, vp, vp]),
+    "fpb_gdn_gated_norm": (i32, [vp, vp, sz, vp, sz, sz, sz, C.c_float, vp, i32, vp]),
+    "fpb_decode_combine_add_norm": (i32, [vp, vp, sz, sz, vp, vp, sz, sz, C.c_float, vp, vp, i32, vp]),
+    "fpb_argmax_advance": (i32, [vp, sz, sz, vp, vp, vp, sz, vp, vp]),
+    "fpb_nvfp4_expert_gemv_tokens": (i32, [vp, vp, i32, vp, i32, i32, sz, vp, i32, vp]),
     "fpb_comm_available": (i32, []),
     "fpb_comm_version": (i32, [C.POINTER(i32)]),
     "fpb_comm_unique_id": (i32, [vp]),

@@ -55,7 +55,8 @@ struct GemvArgs {
   const void *x;
   void *y;
   const int32_t *expert_ids;  // null for dense
-  long long x_slot_stride;    // elements between the input rows of consecutive slots
+  long long x_slot_stride;    // elements between the input rows of consecutive slots (or slot groups)
+  int x_div;                  // slots per input row: slot s reads input row s / x_div (1: one row per slot)
   long long y_slot_stride;    // elements between the output rows of consecutive slots
   long long y_batch_stride;   // elements between output rows of consecutive batch rows
   int rows;                   // rows per slot
@@ -163,7 +164,7 @@ __global__ void __launch_bounds__(512, 1) gemv_nvfp4_kernel(GemvArgs a) {
   const uint8_t *packed = a.packed + base_row * kb2;
   const uint8_t *scales = a.scales + base_row * kb16;
   const float *globals = a.globals + base_row;
-  const long long x_off = (long long)slot * a.x_slot_stride;
+  const long long x_off = (long long)(slot / a.x_div) * a.x_slot_stride;
 
   // Contiguous, balanced range of row-block groups for this CTA.
   const int total_groups = (a.nrb + g_count - 1) / g_count;
@@ -1053,6 +1054,7 @@ extern "C" int fpb_nvfp4_gemv(const fpb_nvfp4_matrix *w, size_t row_begin, size_
   if (reinterpret_cast<uintptr_t>(x) % 16 != 0)
     return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_gemv: x must be 16-byte aligned");
   GemvArgs a{};
+  a.x_div = 1;
   a.packed = w->packed + row_begin * (w->cols / 2);
   a.scales = w->scales + row_begin * (w->cols / kNvfp4Group);
   a.globals = w->row_globals + row_begin;
@@ -1108,8 +1110,44 @@ extern "C" int fpb_nvfp4_expert_gemv(const fpb_nvfp4_matrix *w, const void *x, i
   a.y_bf16 = y_dtype == FPB_BF16;
   a.y_batch_stride = 0;
   a.x_slot_stride = (long long)input_stride * (long long)w->cols;
+  a.x_div = 1;
   a.y_slot_stride = (long long)rows_per_expert;
   return run_gemv(a, slots, x_dtype == FPB_F32, as_stream(stream));
+}
+
+// The expert GEMV of several tokens at once (decode of a batch of sessions):
+// token t's slots t*slots_per_token .. +slots_per_token-1 use x row t.
+extern "C" int fpb_nvfp4_expert_gemv_tokens(const fpb_nvfp4_matrix *w, const void *x, int x_dtype,
+                                            const int32_t *expert_ids, int tokens, int slots_per_token,
+                                            size_t rows_per_expert, void *y, int y_dtype, void *stream) {
+  if (!w || !x || !y || !expert_ids)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_expert_gemv_tokens: null pointer");
+  if (tokens < 1 || slots_per_token < 1 || (long long)tokens * slots_per_token > 65535)
+    return fail(FPB_ERR_SHAPE, "fpb_nvfp4_expert_gemv_tokens: %d tokens x %d slots", tokens, slots_per_token);
+  if (rows_per_expert == 0 || w->rows % rows_per_expert != 0)
+    return fail(FPB_ERR_SHAPE, "fpb_nvfp4_expert_gemv_tokens: rows %zu not a multiple of rows_per_expert %zu",
+                w->rows, rows_per_expert);
+  if ((x_dtype != FPB_F32 && x_dtype != FPB_BF16) || (y_dtype != FPB_F32 && y_dtype != FPB_BF16))
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_expert_gemv_tokens: dtype");
+  if (reinterpret_cast<uintptr_t>(x) % 16 != 0)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_expert_gemv_tokens: x must be 16-byte aligned");
+  GemvArgs a{};
+  a.packed = w->packed;
+  a.scales = w->scales;
+  a.globals = w->row_globals;
+  a.x = x;
+  a.y = y;
+  a.expert_ids = expert_ids;
+  a.n_experts = (int)(w->rows / rows_per_expert);
+  a.rows = (int)rows_per_expert;
+  a.K = (int)w->cols;
+  a.batch = 1;
+  a.y_bf16 = y_dtype == FPB_BF16;
+  a.y_batch_stride = 0;
+  a.x_slot_stride = (long long)w->cols;
+  a.x_div = slots_per_token;
+  a.y_slot_stride = (long long)rows_per_expert;
+  return run_gemv(a, tokens * slots_per_token, x_dtype == FPB_F32, as_stream(stream));
 }
 
 // Several dense GEMVs in one launch (see fpb_nvfp4_gemv_batched in the
@@ -1145,21 +1183,27 @@ extern "C" int fpb_nvfp4_gemv_batched(const fpb_gemv_segment *segs, int count, i
   const bool x_f32 = x_dtype == FPB_F32;
   cudaStream_t s = as_stream(stream);
 
+  // Segments the streaming kernel can read go into one launch; any other
+  // segment (a row count or first row not a multiple of 4, an unaligned
+  // row) runs as its own fpb_nvfp4_gemv.
   StreamArgs<kStreamMaxSegs> a{};
-  bool streamable = K <= 4096;
+  bool alone[kStreamMaxSegs] = {};
+  int nstream = 0;
   long long total = 0;
-  for (int i = 0; i < count && streamable; ++i) {
+  for (int i = 0; i < count; ++i) {
     const fpb_gemv_segment &sg = segs[i];
     const size_t end = sg.row_end ? sg.row_end : sg.w->rows;
     const long long rows = (long long)(end - sg.row_begin);
     const uint8_t *packed = sg.w->packed + sg.row_begin * (K / 2);
     const uint8_t *scales = sg.w->scales + sg.row_begin * (K / kNvfp4Group);
     const float *globals = sg.w->row_globals + sg.row_begin;
-    streamable = stream_segment_ok(packed, scales, globals, rows);
-    a.seg[i] = StreamSeg{packed, scales, globals, sg.x, sg.y, total, (int)rows, 0};
+    alone[i] = K > 4096 || !stream_segment_ok(packed, scales, globals, rows);
+    if (alone[i]) continue;
+    a.seg[nstream++] = StreamSeg{packed, scales, globals, sg.x, sg.y, total, (int)rows, 0};
     total += rows;
   }
-  if (streamable) {
+  bool streamed = false;
+  if (nstream > 0) {
     constexpr int unit_rows = 16;
     const int grid_target = 2 * std::max(1, sm_count());
     long long rpc = (total + grid_target - 1) / grid_target;
@@ -1167,20 +1211,21 @@ extern "C" int fpb_nvfp4_gemv_batched(const fpb_gemv_segment *segs, int count, i
     size_t smem = 0;
     // A CTA's rows split into at most one more unit per segment they touch;
     // its ring never needs more stages than units.
-    streamable = rpc <= 0x7fffffff &&
-                 stream_geometry((int)K, batch, x_f32, unit_rows, (rpc + unit_rows - 1) / unit_rows + count, &a,
-                                 &smem);
-    if (streamable) {
-      a.nseg = count;
+    if (rpc <= 0x7fffffff &&
+        stream_geometry((int)K, batch, x_f32, unit_rows, (rpc + unit_rows - 1) / unit_rows + nstream, &a, &smem)) {
+      a.nseg = nstream;
       a.rpc = (int)rpc;
       a.total_rows = total;
       a.error = device_error_ptr();
       a.y_bf16 = y_dtype == FPB_BF16;
       const int grid = (int)((total + rpc - 1) / rpc);
-      return launch_stream<kStreamMaxSegs, unit_rows>(a, grid, smem, x_f32, s);
+      int st = launch_stream<kStreamMaxSegs, unit_rows>(a, grid, smem, x_f32, s);
+      if (st) return st;
+      streamed = true;
     }
   }
   for (int i = 0; i < count; ++i) {
+    if (streamed && !alone[i]) continue;
     const fpb_gemv_segment &sg = segs[i];
     int st = fpb_nvfp4_gemv(sg.w, sg.row_begin, sg.row_end, sg.x, x_dtype, sg.y, y_dtype, batch, stream);
     if (st) return st;

@@ -1,0 +1,626 @@
+// Decode-step kernels of the hybrid MoE decoder around the quantized-matmul
+// path: embedding, RMSNorm, the full-attention layer's
+// head norms + RoPE + KV-cache append and split-position GQA decode
+// attention with the output gate, the gated-delta-net layer's causal conv,
+// delta-rule step and gated norm, the decode MoE combine + residual + norm,
+// and greedy sampling.  The linear layers are the library's NVFP4 GEMVs.
+//
+// Each kernel restates one firepit-kernels operation (crate src/ paths):
+//   embedding        embedding.rs            rms_norm / add_norm   norm.rs
+//   attn_prepare     norm.rs (q/k head norms), rope.rs:6-22, attention.rs:6-30
+//   attn_decode      attention.rs:128-168 (online_attention), :170-190 (output_gate)
+//   gdn_conv         gdn.rs:6-63 (conv1d_silu)
+//   gdn_delta        gdn.rs:206-263 (delta_step)
+//   gdn_gated_norm   norm.rs rms_norm over each value head, gdn.rs:266-278 (gated_silu)
+//   combine_add_norm moe.rs:111-147 (combine_add_norm_view), normed in bf16
+//   argmax           firepit src/generation.rs:34-42 (greedy)
+// Every kernel starts with pdl_enter() (programmatic dependent launch: it waits
+// for the previous kernel before reading anything).
+#include <cmath>
+
+#include "common.cuh"
+
+namespace fpb {
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <typename T>
+__device__ __forceinline__ float load_f(const T *p, size_t i);
+template <>
+__device__ __forceinline__ float load_f<float>(const float *p, size_t i) {
+  return p[i];
+}
+template <>
+__device__ __forceinline__ float load_f<__nv_bfloat16>(const __nv_bfloat16 *p, size_t i) {
+  return __bfloat162float(p[i]);
+}
+
+__device__ __forceinline__ void store_f(void *p, int bf16, size_t i, float v) {
+  if (bf16)
+    reinterpret_cast<__nv_bfloat16 *>(p)[i] = __float2bfloat16_rn(v);
+  else
+    reinterpret_cast<float *>(p)[i] = v;
+}
+
+__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+// ---- embedding ----------------------------------------------------------------------------
+__global__ void embedding_kernel(const __nv_bfloat16 *table, const int32_t *ids, int rows, int hidden, int vocab,
+                                 float *out, int *error) {
+  pdl_enter();
+  const int r = blockIdx.y;
+  const int id = ids[r];
+  if (id < 0 || id >= vocab) {
+    if (threadIdx.x == 0 && blockIdx.x == 0 && error) atomicCAS(error, 0, 501);
+    for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < hidden; c += gridDim.x * blockDim.x)
+      out[(size_t)r * hidden + c] = 0.0f;
+    return;
+  }
+  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < hidden; c += gridDim.x * blockDim.x)
+    out[(size_t)r * hidden + c] = __bfloat162float(table[(size_t)id * hidden + c]);
+}
+
+// ---- RMSNorm (norm.rs): out = x * rsqrt(mean(x^2) + eps) * gamma -------------------------------
+// One warp per row; with `delta`, x = residual + delta is also stored to `sum_out`.
+template <typename T>
+__global__ void rms_norm_kernel(const T *x, size_t x_pitch, const float *delta, float *sum_out, int rows,
+                                int width, const float *gamma, float inv_w, float eps, void *out, int out_bf16,
+                                size_t out_pitch) {
+  pdl_enter();
+  const int warps = blockDim.x / 32, lane = threadIdx.x & 31;
+  const int r = blockIdx.x * warps + threadIdx.x / 32;
+  if (r >= rows) return;
+  const T *xr = x + (size_t)r * x_pitch;
+  float ss = 0.0f;
+  for (int c = lane; c < width; c += 32) {
+    float v = load_f(xr, c);
+    if (delta) {
+      v += delta[(size_t)r * width + c];
+      sum_out[(size_t)r * width + c] = v;
+    }
+    ss = fmaf(v, v, ss);
+  }
+  ss = warp_sum(ss);
+  const float scale = __frsqrt_rn(fmaf(ss, inv_w, eps));
+  for (int c = lane; c < width; c += 32) {
+    const float v = delta ? sum_out[(size_t)r * width + c] : load_f(xr, c);
+    store_f(out, out_bf16, (size_t)r * out_pitch + c, v * scale * gamma[c]);
+  }
+}
+
+// ---- full attention: head norms, RoPE, cache append --------------------------------------------
+struct AttnPrepArgs {
+  const float *q_gate;  // [B, q_heads * 2 * head_dim]: per head q then gate
+  const float *k;       // [B, k_pitch]: kv_heads * head_dim keys
+  const float *v;       // [B, v_pitch]
+  long long k_pitch, v_pitch, qg_pitch;
+  const float *q_gamma, *k_gamma;
+  const int32_t *positions;  // [B] position of this token
+  float *q_out;              // [B, q_heads, head_dim]
+  float *k_cache, *v_cache;  // [B, max_seq, kv_heads, head_dim]
+  int batch, q_heads, kv_heads, head_dim, rotary_dim, max_seq;
+  float inv_d, eps;
+  float inv_freq[64];  // 1 / theta^(i / half), i < rotary_dim / 2
+  int *error;
+};
+
+// One warp per (b, head) of q (heads [0, q_heads)) and k (heads [q_heads,
+// q_heads + kv_heads)); the k warps also append v.
+__global__ void attn_prepare_kernel(const __grid_constant__ AttnPrepArgs a) {
+  pdl_enter();
+  const int lane = threadIdx.x & 31;
+  const int item = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int per_b = a.q_heads + a.kv_heads;
+  if (item >= a.batch * per_b) return;
+  const int b = item / per_b, h = item % per_b;
+  const bool is_q = h < a.q_heads;
+  const int D = a.head_dim;
+  const float *src = is_q ? a.q_gate + (size_t)b * a.qg_pitch + (size_t)h * 2 * D
+                          : a.k + (size_t)b * a.k_pitch + (size_t)(h - a.q_heads) * D;
+  const float *gamma = is_q ? a.q_gamma : a.k_gamma;
+  const int pos = a.positions[b];
+  if (pos < 0 || pos >= a.max_seq) {
+    if (lane == 0 && a.error) atomicCAS(a.error, 0, 502);
+    return;
+  }
+  float ss = 0.0f;
+  for (int c = lane; c < D; c += 32) ss = fmaf(src[c], src[c], ss);
+  ss = warp_sum(ss);
+  const float scale = __frsqrt_rn(fmaf(ss, a.inv_d, a.eps));
+  float *dst = is_q ? a.q_out + ((size_t)b * a.q_heads + h) * D
+                    : a.k_cache + (((size_t)b * a.max_seq + pos) * a.kv_heads + (h - a.q_heads)) * D;
+  const int half = a.rotary_dim / 2;
+  for (int c = lane; c < D; c += 32) {
+    const float x = src[c] * scale * gamma[c];
+    float y = x;
+    if (c < a.rotary_dim) {
+      // rotate_half over the rotary dims: cat(-x1, x0) (rope.rs:17-20)
+      const int i = c < half ? c : c - half;
+      const int pair = c < half ? c + half : c - half;
+      const float xp = src[pair] * scale * gamma[pair];
+      float sn, cs;
+      sincosf((float)pos * a.inv_freq[i], &sn, &cs);
+      y = x * cs + (c < half ? -xp : xp) * sn;
+    }
+    dst[c] = y;
+  }
+  if (!is_q) {
+    const int kvh = h - a.q_heads;
+    const float *vs = a.v + (size_t)b * a.v_pitch + (size_t)kvh * D;
+    float *vd = a.v_cache + (((size_t)b * a.max_seq + pos) * a.kv_heads + kvh) * D;
+    for (int c = lane; c < D; c += 32) vd[c] = vs[c];
+  }
+}
+
+// ---- split-position GQA decode attention --------------------------------------------------------
+// Block (b, kv head, chunk): one warp per query head of the group, positions
+// [chunk * chunk_len, min(+chunk_len, pos + 1)), online softmax per warp
+// (attention.rs:128-168), partial (max, sum, numerator) to the workspace.
+constexpr int kAttnMaxD = 256;
+
+__global__ void attn_decode_partial_kernel(const float *q, const float *k_cache, const float *v_cache,
+                                           const int32_t *positions, int batch, int q_heads, int kv_heads, int D,
+                                           int max_seq, int chunk_len, int chunks, float scale, float *part) {
+  pdl_enter();
+  const int group = q_heads / kv_heads;
+  const int lane = threadIdx.x & 31, w = threadIdx.x / 32;
+  const int bk = blockIdx.x, chunk = blockIdx.y;
+  const int b = bk / kv_heads, kvh = bk % kv_heads;
+  const int qh = kvh * group + w;
+  if (w >= group) return;
+  const int limit = min(positions[b], max_seq - 1) + 1;  // positions 0 .. pos
+  const int t0 = chunk * chunk_len, t1 = min(limit, t0 + chunk_len);
+  float *out = part + (((size_t)b * q_heads + qh) * chunks + chunk) * (D + 2);
+  constexpr int kPer = kAttnMaxD / 32;
+  float qv[kPer], acc[kPer];
+  const float *qr = q + ((size_t)b * q_heads + qh) * D;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int c = lane + 32 * i;
+    qv[i] = c < D ? qr[c] : 0.0f;
+    acc[i] = 0.0f;
+  }
+  float m = -INFINITY, l = 0.0f;
+  for (int t = t0; t < t1; ++t) {
+    const float *kr = k_cache + (((size_t)b * max_seq + t) * kv_heads + kvh) * D;
+    float dot = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int c = lane + 32 * i;
+      if (c < D) dot = fmaf(qv[i], kr[c], dot);
+    }
+    const float score = warp_sum(dot) * scale;
+    const float mn = fmaxf(m, score);
+    const float old_w = expf(m - mn), new_w = expf(score - mn);
+    const float *vr = v_cache + (((size_t)b * max_seq + t) * kv_heads + kvh) * D;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int c = lane + 32 * i;
+      if (c < D) acc[i] = acc[i] * old_w + vr[c] * new_w;
+    }
+    l = l * old_w + new_w;
+    m = mn;
+  }
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int c = lane + 32 * i;
+    if (c < D) out[c] = acc[i];
+  }
+  if (lane == 0) {
+    out[D] = m;
+    out[D + 1] = l;
+  }
+}
+
+// Merges the chunks of each (b, q head) and applies the output gate
+// out = attn * sigmoid(gate) (attention.rs:170-190); one warp per (b, head).
+__global__ void attn_decode_combine_kernel(const float *part, const float *q_gate, long long qg_pitch,
+                                           const int32_t *positions, int batch, int q_heads, int D, int max_seq,
+                                           int chunk_len, int chunks, void *out, int out_bf16) {
+  pdl_enter();
+  const int lane = threadIdx.x & 31;
+  const int item = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  if (item >= batch * q_heads) return;
+  const int b = item / q_heads, h = item % q_heads;
+  const int limit = min(positions[b], max_seq - 1) + 1;
+  const int used = (limit + chunk_len - 1) / chunk_len;
+  const float *pp = part + (size_t)item * chunks * (D + 2);
+  float m = -INFINITY;
+  for (int c = 0; c < used; ++c) m = fmaxf(m, pp[(size_t)c * (D + 2) + D]);
+  float l = 0.0f;
+  for (int c = 0; c < used; ++c) l += pp[(size_t)c * (D + 2) + D + 1] * expf(pp[(size_t)c * (D + 2) + D] - m);
+  const float inv_l = 1.0f / l;
+  const float *gate = q_gate + (size_t)b * qg_pitch + (size_t)h * 2 * D + D;
+  for (int j = lane; j < D; j += 32) {
+    float num = 0.0f;
+    for (int c = 0; c < used; ++c)
+      num += pp[(size_t)c * (D + 2) + j] * expf(pp[(size_t)c * (D + 2) + D] - m);
+    const float attn = num * inv_l;
+    store_f(out, out_bf16, (size_t)b * q_heads * D + (size_t)h * D + j, attn * sigmoidf_(gate[j]));
+  }
+}
+
+// ---- gated delta net -----------------------------------------------------------------------------
+// Causal depthwise conv over the last `kernel` inputs of each channel, SiLU
+// (gdn.rs:6-63); state [B, channels, kernel - 1] holds the previous inputs.
+__global__ void gdn_conv_kernel(const float *x, long long x_pitch, float *state, const float *weight, int batch,
+                                int channels, int kernel, float *out) {
+  pdl_enter();
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (size_t)batch * channels) return;
+  const int b = (int)(i / channels), c = (int)(i % channels);
+  float *st = state + i * (kernel - 1);
+  const float *wr = weight + (size_t)c * kernel;
+  const float cur = x[(size_t)b * x_pitch + c];
+  float sum = 0.0f;
+  for (int j = 0; j < kernel - 1; ++j) sum = fmaf(st[j], wr[j], sum);
+  sum = fmaf(cur, wr[kernel - 1], sum);
+  out[i] = sum / (1.0f + expf(-sum));
+  for (int j = 0; j + 1 < kernel - 1; ++j) st[j] = st[j + 1];
+  st[kernel - 2] = cur;
+}
+
+// The delta rule for one token (gdn.rs:206-263).  Block (b, value head),
+// thread j = value column: memory_j = decay * sum_i S[i][j] k_i, delta_j =
+// (v_j - memory_j) * beta, S[i][j] = S[i][j] * decay + k_i delta_j, out_j =
+// sum_i S[i][j] q_i, with q, k L2-normalised (q also by 1/sqrt(dk)).
+__global__ void gdn_delta_kernel(const float *conv_out, int conv_dim, const float *a, const float *bgate,
+                                 long long ab_pitch, const float *a_log, const float *dt_bias, float *state,
+                                 int batch, int key_heads, int value_heads, int dk, int dv, float eps,
+                                 float inv_sqrt_dk, float *out) {
+  pdl_enter();
+  extern __shared__ float sh[];  // q[dk], k[dk], reduction scratch
+  float *qs = sh, *ks = sh + dk, *red = sh + 2 * dk;
+  const int b = blockIdx.x / value_heads, h = blockIdx.x % value_heads;
+  const int kh = h / (value_heads / key_heads);
+  const float *x = conv_out + (size_t)b * conv_dim;
+  const int key_dim = key_heads * dk;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid / 32, warps = blockDim.x / 32;
+  float sq = 0.0f, sk = 0.0f;
+  for (int i = tid; i < dk; i += blockDim.x) {
+    const float qv = x[kh * dk + i], kv = x[key_dim + kh * dk + i];
+    qs[i] = qv;
+    ks[i] = kv;
+    sq = fmaf(qv, qv, sq);
+    sk = fmaf(kv, kv, sk);
+  }
+  sq = warp_sum(sq);
+  sk = warp_sum(sk);
+  if (lane == 0) {
+    red[warp] = sq;
+    red[warps + warp] = sk;
+  }
+  __syncthreads();
+  float tq = 0.0f, tk = 0.0f;
+  for (int w = 0; w < warps; ++w) {
+    tq += red[w];
+    tk += red[warps + w];
+  }
+  const float q_scale = __frsqrt_rn(tq + eps) * inv_sqrt_dk, k_scale = __frsqrt_rn(tk + eps);
+  const float bv = bgate[(size_t)b * ab_pitch + h], av = a[(size_t)b * ab_pitch + h];
+  const float beta = 1.0f / (1.0f + expf(-bv));
+  const float xs = av + dt_bias[h];
+  const float tiny = expf(fminf(xs, 0.0f));
+  const float series = tiny - tiny * tiny * 0.5f + tiny * tiny * tiny * 0.33333334f;
+  const float ordinary = fmaxf(xs, 0.0f) + logf(1.0f + expf(-fabsf(xs)));
+  const float softplus = xs < -8.0f ? series : ordinary;
+  const float decay = expf(-(expf(a_log[h]) * softplus));
+  float *S = state + ((size_t)b * value_heads + h) * dk * dv;
+  const float *v = x + 2 * key_dim + (size_t)h * dv;
+  for (int j = tid; j < dv; j += blockDim.x) {
+    float mem = 0.0f;
+    for (int i = 0; i < dk; ++i) mem = fmaf(S[(size_t)i * dv + j], ks[i] * k_scale, mem);
+    mem *= decay;
+    const float delta = (v[j] - mem) * beta;
+    float o = 0.0f;
+    for (int i = 0; i < dk; ++i) {
+      const float nxt = fmaf(S[(size_t)i * dv + j], decay, ks[i] * k_scale * delta);
+      S[(size_t)i * dv + j] = nxt;
+      o = fmaf(nxt, qs[i] * q_scale, o);
+    }
+    out[((size_t)b * value_heads + h) * dv + j] = o;
+  }
+}
+
+// RMSNorm of each value head's output (gated_norm gamma [dv]) times SiLU(z)
+// (gdn.rs:266-278); one warp per (b, head); out [B, value_heads * dv].
+__global__ void gdn_gated_norm_kernel(const float *x, const float *z, long long z_pitch, const float *gamma,
+                                      int batch, int heads, int dv, float inv_dv, float eps, void *out,
+                                      int out_bf16) {
+  pdl_enter();
+  const int lane = threadIdx.x & 31;
+  const int item = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  if (item >= batch * heads) return;
+  const int b = item / heads, h = item % heads;
+  const float *xr = x + (size_t)item * dv;
+  float ss = 0.0f;
+  for (int c = lane; c < dv; c += 32) ss = fmaf(xr[c], xr[c], ss);
+  ss = warp_sum(ss);
+  const float scale = __frsqrt_rn(fmaf(ss, inv_dv, eps));
+  const float *zr = z + (size_t)b * z_pitch + (size_t)h * dv;
+  for (int c = lane; c < dv; c += 32) {
+    const float n = xr[c] * scale * gamma[c];
+    const float zz = zr[c];
+    store_f(out, out_bf16, (size_t)b * heads * dv + (size_t)h * dv + c, n * zz / (1.0f + expf(-zz)));
+  }
+}
+
+// ---- decode MoE combine + residual + RMSNorm ------------------------------------------------------
+// out[t] = residual[t] + sum_s w[t, s] * routed[t * slots + s] (slots in
+// order, moe.rs:111-147); normed = RMSNorm(out) * gamma in bf16.  One block
+// per token.
+__global__ void decode_combine_add_norm_kernel(const float *routed, const float *weights, int width, int slots,
+                                               const float *residual, const float *gamma, int hidden, float inv_h,
+                                               float eps, float *out, void *normed, int normed_bf16) {
+  pdl_enter();
+  __shared__ float red[32];
+  const int t = blockIdx.x;
+  float ss = 0.0f;
+  for (int c = threadIdx.x; c < hidden; c += blockDim.x) {
+    float acc = 0.0f;
+    for (int s = 0; s < slots; ++s)
+      acc = fmaf(weights[(size_t)t * width + s], routed[((size_t)t * slots + s) * hidden + c], acc);
+    const float v = residual[(size_t)t * hidden + c] + acc;
+    out[(size_t)t * hidden + c] = v;
+    ss = fmaf(v, v, ss);
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x / 32] = ss;
+  __syncthreads();
+  float tot = 0.0f;
+  for (int w = 0; w < (int)(blockDim.x / 32); ++w) tot += red[w];
+  const float scale = __frsqrt_rn(fmaf(tot, inv_h, eps));
+  for (int c = threadIdx.x; c < hidden; c += blockDim.x)
+    store_f(normed, normed_bf16, (size_t)t * hidden + c, out[(size_t)t * hidden + c] * scale * gamma[c]);
+}
+
+// ---- greedy sampling ----------------------------------------------------------------------------------
+// Largest finite logit of each row, lowest index among equals (greedy,
+// generation.rs:34-42); the token becomes the next input, its position
+// advances by one and it is appended to the history.
+__global__ void argmax_advance_kernel(const float *logits, int vocab, int32_t *tokens, int32_t *positions,
+                                      int32_t *history, int history_len, int32_t *step) {
+  pdl_enter();
+  __shared__ float bv[32];
+  __shared__ int bi[32];
+  const int b = blockIdx.x;
+  const float *row = logits + (size_t)b * vocab;
+  float best = -INFINITY;
+  int idx = 0x7fffffff;
+  for (int c = threadIdx.x; c < vocab; c += blockDim.x) {
+    const float v = row[c];
+    if (isfinite(v) && (v > best || (v == best && c < idx))) {
+      best = v;
+      idx = c;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (ov > best || (ov == best && oi < idx)) {
+      best = ov;
+      idx = oi;
+    }
+  }
+  const int lane = threadIdx.x & 31, w = threadIdx.x / 32;
+  if (lane == 0) {
+    bv[w] = best;
+    bi[w] = idx;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int i = 1; i < (int)(blockDim.x / 32); ++i)
+      if (bv[i] > best || (bv[i] == best && bi[i] < idx)) {
+        best = bv[i];
+        idx = bi[i];
+      }
+    if (idx == 0x7fffffff) idx = 0;  // no finite logit
+    tokens[b] = idx;
+    positions[b] += 1;
+    if (history) {
+      const int s = *step;
+      if (s < history_len) history[(size_t)b * history_len + s] = idx;
+    }
+  }
+  // the step counter advances once every row has read it: the last block does it
+  if (step && threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(step + 1, 1) == (int)gridDim.x - 1) {
+      step[1] = 0;
+      step[0] += 1;
+    }
+  }
+}
+
+unsigned blocks_for(size_t n, int per_block) { return (unsigned)((n + per_block - 1) / per_block); }
+
+}  // namespace
+}  // namespace fpb
+
+using namespace fpb;
+
+#define FPB_LAUNCH(kernel, grid, block, smem, s, ...)                            \
+  do {                                                                          \
+    cudaError_t e_ = launch_pdl(kernel, grid, block, smem, s, __VA_ARGS__);     \
+    if (e_ != cudaSuccess) return cuda_fail(e_, #kernel);                       \
+    FPB_LAUNCH_CHECK(#kernel);                                                  \
+  } while (0)
+
+extern "C" int fpb_embedding(const void *table_bf16, size_t vocab, size_t hidden, const int32_t *ids, size_t rows,
+                             float *out, void *stream) {
+  if (!table_bf16 || !ids || !out) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_embedding: null pointer");
+  if (rows == 0 || rows > 65535 || hidden == 0 || vocab == 0 || vocab > 0x7fffffff || hidden > 0x7fffffff)
+    return fail(FPB_ERR_SHAPE, "fpb_embedding: shape");
+  FPB_LAUNCH(embedding_kernel, dim3((unsigned)std::min<size_t>(8, (hidden + 255) / 256), (unsigned)rows), 256, 0,
+             as_stream(stream), static_cast<const __nv_bfloat16 *>(table_bf16), ids, (int)rows, (int)hidden,
+             (int)vocab, out, device_error_ptr());
+  return FPB_OK;
+}
+
+extern "C" int fpb_rms_norm(const void *x, int x_dtype, size_t x_pitch, const float *residual_delta,
+                            float *sum_out, size_t rows, size_t width, const float *gamma, float eps, void *out,
+                            int out_dtype, size_t out_pitch, void *stream) {
+  if (!x || !gamma || !out) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_rms_norm: null pointer");
+  if ((residual_delta != nullptr) != (sum_out != nullptr) || (residual_delta && x_dtype != FPB_F32))
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_rms_norm: delta and sum_out go together, with f32 x");
+  if (rows == 0 || width == 0 || rows > 0x7fffffff || width > 0x7fffffff || x_pitch < width || out_pitch < width)
+    return fail(FPB_ERR_SHAPE, "fpb_rms_norm: shape");
+  if ((x_dtype != FPB_F32 && x_dtype != FPB_BF16) || (out_dtype != FPB_F32 && out_dtype != FPB_BF16))
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_rms_norm: dtype");
+  const float inv_w = 1.0f / (float)width;
+  cudaStream_t s = as_stream(stream);
+  if (x_dtype == FPB_F32)
+    FPB_LAUNCH(rms_norm_kernel<float>, blocks_for(rows, 8), 256, 0, s, static_cast<const float *>(x), x_pitch,
+               residual_delta, sum_out, (int)rows, (int)width, gamma, inv_w, eps, out, out_dtype == FPB_BF16,
+               out_pitch);
+  else
+    FPB_LAUNCH(rms_norm_kernel<__nv_bfloat16>, blocks_for(rows, 8), 256, 0, s,
+               static_cast<const __nv_bfloat16 *>(x), x_pitch, residual_delta, sum_out, (int)rows, (int)width,
+               gamma, inv_w, eps, out, out_dtype == FPB_BF16, out_pitch);
+  return FPB_OK;
+}
+
+extern "C" int fpb_attn_prepare(const float *q_gate, size_t qg_pitch, const float *k, size_t k_pitch, const float *v,
+                                size_t v_pitch, const float *q_gamma, const float *k_gamma, const int32_t *positions,
+                                size_t batch, size_t q_heads, size_t kv_heads, size_t head_dim, size_t rotary_dim,
+                                float theta, float eps, size_t max_seq, float *q_out, float *k_cache, float *v_cache,
+                                void *stream) {
+  if (!q_gate || !k || !v || !q_gamma || !k_gamma || !positions || !q_out || !k_cache || !v_cache)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_attn_prepare: null pointer");
+  if (batch == 0 || q_heads == 0 || kv_heads == 0 || q_heads % kv_heads || head_dim == 0 ||
+      rotary_dim > head_dim || rotary_dim % 2 || rotary_dim / 2 > 64 || max_seq == 0 ||
+      batch * (q_heads + kv_heads) > 0x7fffffff)
+    return fail(FPB_ERR_SHAPE, "fpb_attn_prepare: shape");
+  AttnPrepArgs a{};
+  a.q_gate = q_gate;
+  a.k = k;
+  a.v = v;
+  a.qg_pitch = (long long)qg_pitch;
+  a.k_pitch = (long long)k_pitch;
+  a.v_pitch = (long long)v_pitch;
+  a.q_gamma = q_gamma;
+  a.k_gamma = k_gamma;
+  a.positions = positions;
+  a.q_out = q_out;
+  a.k_cache = k_cache;
+  a.v_cache = v_cache;
+  a.batch = (int)batch;
+  a.q_heads = (int)q_heads;
+  a.kv_heads = (int)kv_heads;
+  a.head_dim = (int)head_dim;
+  a.rotary_dim = (int)rotary_dim;
+  a.max_seq = (int)max_seq;
+  a.inv_d = 1.0f / (float)head_dim;
+  a.eps = eps;
+  const int half = (int)rotary_dim / 2;
+  for (int i = 0; i < half; ++i) a.inv_freq[i] = 1.0f / powf(theta, (float)i / (float)half);  // rope.rs:110-113
+  a.error = device_error_ptr();
+  FPB_LAUNCH(attn_prepare_kernel, blocks_for(batch * (q_heads + kv_heads), 8), 256, 0, as_stream(stream), a);
+  return FPB_OK;
+}
+
+extern "C" size_t fpb_attn_decode_workspace_bytes(size_t batch, size_t q_heads, size_t head_dim, size_t max_seq,
+                                                 size_t chunk_len) {
+  if (chunk_len == 0) chunk_len = 64;
+  const size_t chunks = (max_seq + chunk_len - 1) / chunk_len;
+  return batch * q_heads * chunks * (head_dim + 2) * sizeof(float);
+}
+
+extern "C" int fpb_attn_decode(const float *q, const float *k_cache, const float *v_cache, const int32_t *positions,
+                               const float *q_gate, size_t qg_pitch, size_t batch, size_t q_heads, size_t kv_heads,
+                               size_t head_dim, size_t max_seq, size_t chunk_len, float scale, void *workspace,
+                               size_t workspace_bytes, void *out, int out_dtype, void *stream) {
+  if (!q || !k_cache || !v_cache || !positions || !q_gate || !workspace || !out)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_attn_decode: null pointer");
+  if (chunk_len == 0) chunk_len = 64;
+  if (batch == 0 || q_heads == 0 || kv_heads == 0 || q_heads % kv_heads || q_heads / kv_heads > 32 ||
+      head_dim == 0 || head_dim > (size_t)kAttnMaxD || max_seq == 0 || batch * kv_heads > 0x7fffffff)
+    return fail(FPB_ERR_SHAPE, "fpb_attn_decode: shape (group <= 32, head_dim <= %d)", kAttnMaxD);
+  if (out_dtype != FPB_F32 && out_dtype != FPB_BF16)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_attn_decode: dtype");
+  const size_t need = fpb_attn_decode_workspace_bytes(batch, q_heads, head_dim, max_seq, chunk_len);
+  if (workspace_bytes < need)
+    return fail(FPB_ERR_WORKSPACE, "fpb_attn_decode: workspace %zu < %zu bytes", workspace_bytes, need);
+  const int chunks = (int)((max_seq + chunk_len - 1) / chunk_len);
+  cudaStream_t s = as_stream(stream);
+  float *part = static_cast<float *>(workspace);
+  // Chunks past a row's position write nothing and are not read.
+  FPB_LAUNCH(attn_decode_partial_kernel, dim3((unsigned)(batch * kv_heads), (unsigned)chunks),
+             (unsigned)(32 * (q_heads / kv_heads)), 0, s, q, k_cache, v_cache, positions, (int)batch, (int)q_heads,
+             (int)kv_heads, (int)head_dim, (int)max_seq, (int)chunk_len, chunks, scale, part);
+  FPB_LAUNCH(attn_decode_combine_kernel, blocks_for(batch * q_heads, 8), 256, 0, s, part, q_gate,
+             (long long)qg_pitch, positions, (int)batch, (int)q_heads, (int)head_dim, (int)max_seq, (int)chunk_len,
+             chunks, out, out_dtype == FPB_BF16);
+  return FPB_OK;
+}
+
+extern "C" int fpb_gdn_conv(const float *x, size_t x_pitch, float *state, const float *weight, size_t batch,
+                            size_t channels, size_t kernel, float *out, void *stream) {
+  if (!x || !state || !weight || !out) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_gdn_conv: null pointer");
+  if (batch == 0 || channels == 0 || kernel < 2 || kernel > 16 || x_pitch < channels ||
+      batch * channels > 0x7fffffff)
+    return fail(FPB_ERR_SHAPE, "fpb_gdn_conv: shape");
+  FPB_LAUNCH(gdn_conv_kernel, blocks_for(batch * channels, 256), 256, 0, as_stream(stream), x, (long long)x_pitch,
+             state, weight, (int)batch, (int)channels, (int)kernel, out);
+  return FPB_OK;
+}
+
+extern "C" int fpb_gdn_delta(const float *conv_out, const float *a, const float *b, size_t ab_pitch,
+                             const float *a_log, const float *dt_bias, float *state, size_t batch, size_t key_heads,
+                             size_t value_heads, size_t dk, size_t dv, float eps, float *out, void *stream) {
+  if (!conv_out || !a || !b || !a_log || !dt_bias || !state || !out)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_gdn_delta: null pointer");
+  if (batch == 0 || key_heads == 0 || value_heads % key_heads || dk == 0 || dv == 0 || dk > 1024 ||
+      batch * value_heads > 0x7fffffff)
+    return fail(FPB_ERR_SHAPE, "fpb_gdn_delta: shape");
+  const int conv_dim = (int)(2 * key_heads * dk + value_heads * dv);
+  FPB_LAUNCH(gdn_delta_kernel, (unsigned)(batch * value_heads), 128, (2 * dk + 16) * sizeof(float),
+             as_stream(stream), conv_out, conv_dim, a, b, (long long)ab_pitch, a_log, dt_bias, state, (int)batch,
+             (int)key_heads, (int)value_heads, (int)dk, (int)dv, eps, 1.0f / sqrtf((float)dk), out);
+  return FPB_OK;
+}
+
+extern "C" int fpb_gdn_gated_norm(const float *x, const float *z, size_t z_pitch, const float *gamma, size_t batch,
+                                  size_t heads, size_t dv, float eps, void *out, int out_dtype, void *stream) {
+  if (!x || !z || !gamma || !out) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_gdn_gated_norm: null pointer");
+  if (batch == 0 || heads == 0 || dv == 0 || batch * heads > 0x7fffffff)
+    return fail(FPB_ERR_SHAPE, "fpb_gdn_gated_norm: shape");
+  if (out_dtype != FPB_F32 && out_dtype != FPB_BF16)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_gdn_gated_norm: dtype");
+  FPB_LAUNCH(gdn_gated_norm_kernel, blocks_for(batch * heads, 8), 256, 0, as_stream(stream), x, z,
+             (long long)z_pitch, gamma, (int)batch, (int)heads, (int)dv, 1.0f / (float)dv, eps, out,
+             out_dtype == FPB_BF16);
+  return FPB_OK;
+}
+
+extern "C" int fpb_decode_combine_add_norm(const float *routed, const float *weights, size_t width, size_t slots,
+                                           const float *residual, const float *gamma, size_t tokens, size_t hidden,
+                                           float eps, float *out, void *normed, int normed_dtype, void *stream) {
+  if (!routed || !weights || !residual || !gamma || !out || !normed)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_decode_combine_add_norm: null pointer");
+  if (tokens == 0 || tokens > 0x7fffffff || hidden == 0 || slots == 0 || slots > width)
+    return fail(FPB_ERR_SHAPE, "fpb_decode_combine_add_norm: shape");
+  if (normed_dtype != FPB_F32 && normed_dtype != FPB_BF16)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_decode_combine_add_norm: dtype");
+  FPB_LAUNCH(decode_combine_add_norm_kernel, (unsigned)tokens, 256, 0, as_stream(stream), routed, weights, (int)width,
+             (int)slots, residual, gamma, (int)hidden, 1.0f / (float)hidden, eps, out, normed,
+             normed_dtype == FPB_BF16);
+  return FPB_OK;
+}
+
+extern "C" int fpb_argmax_advance(const float *logits, size_t rows, size_t vocab, int32_t *tokens,
+                                  int32_t *positions, int32_t *history, size_t history_len, int32_t *step,
+                                  void *stream) {
+  if (!logits || !tokens || !positions) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_argmax_advance: null pointer");
+  if (rows == 0 || rows > 65535 || vocab == 0 || vocab > 0x7fffffff || (history && !step))
+    return fail(FPB_ERR_SHAPE, "fpb_argmax_advance: shape");
+  FPB_LAUNCH(argmax_advance_kernel, (unsigned)rows, 1024, 0, as_stream(stream), logits, (int)vocab, tokens, positions,
+             history, (int)history_len, step);
+  return FPB_OK;
+}

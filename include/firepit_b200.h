@@ -176,10 +176,11 @@ int fpb_nvfp4_gemv(const fpb_nvfp4_matrix *w, size_t row_begin, size_t row_end,
  *   segs[i].w with segs[i].x[b, :]
  * as fpb_nvfp4_gemv does, with its own x [batch, cols] and y [batch,
  * row_end - row_begin] (x may be shared).  All segments have the same cols;
- * 1 <= count <= 128, 1 <= batch <= 16.  One launch when cols % 128 == 0,
- * cols <= 4096, batch <= 8 and every segment's row_begin and row count are
- * multiples of 4; otherwise one fpb_nvfp4_gemv launch per segment.  `segs`
- * is read on the host during the call only. */
+ * 1 <= count <= 128, 1 <= batch <= 16.  When cols % 128 == 0, cols <= 4096
+ * and batch <= 8, the segments whose row_begin and row count are multiples
+ * of 4 run in one launch and each other segment in its own fpb_nvfp4_gemv
+ * launch; other shapes run one fpb_nvfp4_gemv launch per segment.  `segs` is
+ * read on the host during the call only. */
 typedef struct fpb_gemv_segment {
   const fpb_nvfp4_matrix *w;
   size_t row_begin, row_end; /* row_end == 0: all rows */
@@ -471,6 +472,85 @@ int fpb_moe_route_dest(const int32_t *ids, size_t tokens, size_t width, size_t s
                        int32_t *dest, void *stream);
 int fpb_moe_route_meta(const int32_t *ids, const int32_t *inverse, size_t tokens, size_t width, size_t slots,
                        size_t experts_per_rank, size_t rows, int32_t *send_expert, void *stream);
+
+/* ---- decode step of the hybrid MoE decoder -----------------
+ * The operations around the quantized matmuls in firepit's decode step
+ * (firepit src/plan.rs:283-420, src/execute.rs:334-716); the linear layers
+ * are the NVFP4 GEMVs above.  All activations f32 unless a dtype says so;
+ * `pitch` arguments are elements between rows.  Positions are device int32
+ * [batch] (the token's index in its session). */
+/* embedding.rs: out [rows, hidden] f32 = table_bf16[ids[r]] (device error
+ * 501 on an id outside [0, vocab); that row is zeroed). */
+int fpb_embedding(const void *table_bf16, size_t vocab, size_t hidden, const int32_t *ids, size_t rows,
+                  float *out, void *stream);
+/* norm.rs rms_norm / add_norm: out = x * rsqrt(mean(x^2) + eps) * gamma over
+ * `width` columns of each row; with residual_delta, x = x + residual_delta
+ * is first stored to sum_out (f32, [rows, width] contiguous). */
+int fpb_rms_norm(const void *x, int x_dtype, size_t x_pitch, const float *residual_delta, float *sum_out,
+                 size_t rows, size_t width, const float *gamma, float eps, void *out, int out_dtype,
+                 size_t out_pitch, void *stream);
+/* The full-attention layer's per-head RMSNorms of q (the first head_dim of
+ * each 2*head_dim pitch of q_gate) and k, RoPE over the first rotary_dim
+ * dims (rope.rs:6-22, inverse frequencies 1 / theta^(i / half) as
+ * rope.rs:110-113, angles pos * inv_freq), q to q_out [batch, q_heads,
+ * head_dim], k and v appended to the caches [batch, max_seq, kv_heads,
+ * head_dim] at each row's position (attention.rs:6-30).  Device error 502 on
+ * a position outside [0, max_seq). */
+int fpb_attn_prepare(const float *q_gate, size_t qg_pitch, const float *k, size_t k_pitch, const float *v,
+                     size_t v_pitch, const float *q_gamma, const float *k_gamma, const int32_t *positions,
+                     size_t batch, size_t q_heads, size_t kv_heads, size_t head_dim, size_t rotary_dim, float theta,
+                     float eps, size_t max_seq, float *q_out, float *k_cache, float *v_cache, void *stream);
+/* online_attention + output_gate (attention.rs:128-190): each query head
+ * attends over cache positions 0 .. position of its row (GQA: q head h reads
+ * kv head h / (q_heads / kv_heads)), scores * scale, softmax, times the
+ * values; out [batch, q_heads * head_dim] = attn * sigmoid(gate) (gate: the
+ * second head_dim of each head's q_gate pitch).  Positions are split into
+ * chunks of chunk_len (0: 64) on separate blocks and merged.  head_dim <=
+ * 256, q_heads / kv_heads <= 32; workspace fpb_attn_decode_workspace_bytes. */
+size_t fpb_attn_decode_workspace_bytes(size_t batch, size_t q_heads, size_t head_dim, size_t max_seq,
+                                       size_t chunk_len);
+int fpb_attn_decode(const float *q, const float *k_cache, const float *v_cache, const int32_t *positions,
+                    const float *q_gate, size_t qg_pitch, size_t batch, size_t q_heads, size_t kv_heads,
+                    size_t head_dim, size_t max_seq, size_t chunk_len, float scale, void *workspace,
+                    size_t workspace_bytes, void *out, int out_dtype, void *stream);
+/* conv1d_silu (gdn.rs:6-63): per channel, SiLU of the causal conv of the
+ * last `kernel` inputs; state [batch, channels, kernel - 1] keeps the
+ * previous inputs and is shifted. */
+int fpb_gdn_conv(const float *x, size_t x_pitch, float *state, const float *weight, size_t batch,
+                 size_t channels, size_t kernel, float *out, void *stream);
+/* delta_step (gdn.rs:206-263) on conv_out [batch, 2*key_heads*dk +
+ * value_heads*dv] (q, k, v), gates a, b [batch, ab_pitch] (value_heads
+ * used): beta = sigmoid(b), decay = exp(-exp(a_log) * softplus(a + dt_bias))
+ * with the reference's series below -8; q, k L2-normalised (+ eps, q also
+ * / sqrt(dk)); state [batch, value_heads, dk, dv] updated in place; out
+ * [batch, value_heads, dv]. */
+int fpb_gdn_delta(const float *conv_out, const float *a, const float *b, size_t ab_pitch, const float *a_log,
+                  const float *dt_bias, float *state, size_t batch, size_t key_heads, size_t value_heads, size_t dk,
+                  size_t dv, float eps, float *out, void *stream);
+/* RMSNorm of each value head (gamma [dv]) times SiLU(z) (gdn.rs:266-278):
+ * out [batch, heads * dv]. */
+int fpb_gdn_gated_norm(const float *x, const float *z, size_t z_pitch, const float *gamma, size_t batch, size_t heads,
+                       size_t dv, float eps, void *out, int out_dtype, void *stream);
+/* combine_add_norm_view (moe.rs:111-147) for decode: out[t] = residual[t] +
+ * sum over slots s of weights[t, s] * routed[t * slots + s], normed =
+ * RMSNorm(out) * gamma (f32 or bf16). */
+int fpb_decode_combine_add_norm(const float *routed, const float *weights, size_t width, size_t slots,
+                                const float *residual, const float *gamma, size_t tokens, size_t hidden, float eps,
+                                float *out, void *normed, int normed_dtype, void *stream);
+/* greedy (firepit src/generation.rs:34-42): tokens[r] = index of the largest
+ * finite logit of row r (lowest index among equals), positions[r] += 1, and
+ * (history non-null) history[r * history_len + step[0]] = token, after which
+ * step[0] advances (step: device int32 [2], the second word for the blocks'
+ * arrivals, zero at start). */
+int fpb_argmax_advance(const float *logits, size_t rows, size_t vocab, int32_t *tokens, int32_t *positions,
+                       int32_t *history, size_t history_len, int32_t *step, void *stream);
+/* The expert GEMV of several tokens (a decode batch): slot s = t *
+ * slots_per_token + j of expert_ids [tokens, slots_per_token] reads x row t;
+ * y [tokens * slots_per_token, rows_per_expert].  Otherwise as
+ * fpb_nvfp4_expert_gemv. */
+int fpb_nvfp4_expert_gemv_tokens(const fpb_nvfp4_matrix *w, const void *x, int x_dtype, const int32_t *expert_ids,
+                                 int tokens, int slots_per_token, size_t rows_per_expert, void *y, int y_dtype,
+                                 void *stream);
 
 /* ---- collectives (NCCL) ------------------------------------------------------
  * The reference runs on one GPU and has no collectives.  These are the

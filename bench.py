@@ -54,15 +54,19 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--config", choices=["gemv", "nvfp4_gemm_m1", "nvfp4_gemm_m16", "nvfp4_gemm_m128",
-                                        "nvfp4_gemm_m2048", "fp8_gemm", "moe_t4096", "moe_t64", "moe_ep"],
+                                        "nvfp4_gemm_m2048", "fp8_gemm", "moe_t4096", "moe_t64", "moe_ep",
+                                        "decode"],
                    default="gemv",
                    help="gemv: config 0 (default); nvfp4_gemm_m*: config 2 at M=1 / 16 (decode GEMV entry) and "
                         "M=128 / 2048 (tcgen05 GEMM); fp8_gemm: config 1; moe_t*: config 3 MoE layer at T=4096 / "
-                        "T=64; moe_ep: config 3 expert-parallel over the ranks (NCCL all-to-all), T=4096 per rank")
+                        "T=64; moe_ep: config 3 expert-parallel over the ranks (NCCL all-to-all), T=4096 per rank; "
+                        "decode: config 4, the hybrid MoE decoder's decode tokens/s")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="budget of the cpu_baseline sample")
     p.add_argument("--no-sub", action="store_true", help="default line without the other configs' sub-records")
     p.add_argument("--sub-steps", type=int, default=20, help="timed steps of each sub-record")
     p.add_argument("--sub-cpu-seconds", type=float, default=3.0, help="cpu_baseline budget of each sub-record")
+    p.add_argument("--dec-prompt", type=int, default=2048, help="config 4 prompt tokens per session (2048)")
+    p.add_argument("--dec-steps", type=int, default=256, help="config 4 greedy tokens per session (256)")
     return p.parse_args()
 
 
@@ -813,7 +817,8 @@ def gemm_arm(args):
         bf16 = float(peaks.get("bf16_tflops", 1590.0))
         achieved = 2.0 * m * n_rank * GEMM_K / (per_launch_ms * 1e-3) / 1e12
         roof = {"bound": "tensor", "achieved": achieved, "peak": 4 * bf16, "unit": "TFLOP/s",
-                "frac": achieved / (4 * bf16), "traffic": None,
+                "frac": achieved / (4 * bf16),
+                "traffic": load_traffic("nvfp4_gemm_config2_m2048_traffic.txt") if (m, g) == (2048, 1) else None,
                 "peak_kind": "4 x measured bf16 burst (nominal dense FP4:BF16 ratio; no FP4 measurement)"}
     else:
         hbm = float(peaks.get("hbm_gbs", 6650.0))
@@ -1025,7 +1030,8 @@ def fp8_arm(args):
     bf16 = float(peaks.get("bf16_tflops", 1590.0))
     achieved = 2.0 * FP8_M * n_rank * FP8_K / (per_launch_ms * 1e-3) / 1e12
     roof = {"bound": "tensor", "achieved": achieved, "peak": 2 * bf16, "unit": "TFLOP/s",
-            "frac": achieved / (2 * bf16), "traffic": None, "per_launch_us": per_launch_ms * 1e3,
+            "frac": achieved / (2 * bf16), "traffic": load_traffic("fp8_gemm_config1_traffic.txt") if g == 1 else None,
+            "per_launch_us": per_launch_ms * 1e3,
             "peak_kind": "2 x measured bf16 burst (nominal dense FP8:BF16 ratio; no FP8 measurement)"}
     if rank == 0:
         line = {"metric": "FP8 GEMM TFLOPS", "value": value, "unit": "TFLOP/s", "n_gpus": g, "steps": args.steps,
@@ -1410,6 +1416,227 @@ def moe_ep_arm(args):
     return out
 
 
+# ---- config 4: decode of the random-init hybrid MoE decoder ------------------------------
+DEC_SESSIONS, DEC_PROMPT, DEC_STEPS = 8, 2048, 256
+
+
+def decode_config(g: int, prompt: int = DEC_PROMPT, steps: int = DEC_STEPS) -> dict:
+    return {"workload": "config4 48-layer hybrid MoE decoder (36 GDN + 12 full-attention layers, H=2048, vocab 151936,"
+                        f" 512 experts top-10 + shared, all linear weights NVFP4), 8 sessions x {prompt}-token random "
+                        f"prompt, {steps} greedy tokens",
+            "sessions_per_gpu": DEC_SESSIONS, "prompt": prompt, "decode_steps": steps,
+            "parallelism": f"replicas x{g}: each GPU decodes its own 8 sessions, no exchange" if g > 1
+            else "single GPU",
+            "prompt_path": "the decode step, one prompt token per step (untimed)",
+            "timing": "the 256 decode steps, one CUDA graph per step, CUDA events, max over ranks"}
+
+
+def decode_cpu_sample(seconds: float, layers_sample: int = 4):
+    """The host path restated (numpy): one decode step of one session at
+    position 0 through the first `layers_sample` layers of a model of the
+    same shapes (weights generated by the oracle, dequantized outside the
+    timed region), scaled to 48 layers; tokens/s = 1 / that step time."""
+    import numpy as np
+
+    from oracle import model_ops as R
+    from oracle import oracle as O
+    cores = use_all_cores()
+    H, I, E, K = 2048, 512, 512, 10
+    rng = np.random.default_rng(0)
+
+    def mat(rows, cols, sid):
+        w = O.synth_normal(rows * cols, seed=7, stream=sid, std=0.02).reshape(rows, cols)
+        p, sc, gl = O.nvfp4_quantize(w)
+        return O.nvfp4_dequantize(p, sc, gl, rows, cols)
+
+    Ls = []
+    for i in range(layers_sample):
+        L = {"g": np.ones(H, np.float32)}
+        if (i + 1) % 4 == 0:
+            L["qg"], L["k"], L["v"], L["o"] = mat(8192, H, 10 * i), mat(512, H, 10 * i + 1), mat(512, H, 10 * i + 2), \
+                mat(H, 4096, 10 * i + 3)
+        else:
+            L["qkv"], L["z"], L["ab"], L["out"] = mat(8192, H, 10 * i), mat(4096, H, 10 * i + 1), \
+                mat(64, H, 10 * i + 2), mat(H, 4096, 10 * i + 3)
+            L["conv"] = rng.standard_normal((8192, 4)).astype(np.float32) * 0.2
+        L["router"] = mat(E + 1, H, 10 * i + 4)
+        Ls.append(L)
+    experts = {}
+
+    def expert(e):
+        if e not in experts:
+            experts[e] = (mat(2 * I, H, 5000 + e), mat(H, I, 9000 + e))
+        return experts[e]
+
+    x0 = rng.standard_normal(H).astype(np.float32) * 0.02
+    for i in range(layers_sample):  # dequantize the experts the sample routes to
+        lg = (R.rms_norm(x0, Ls[i]["g"], 1e-6) @ Ls[i]["router"].T).astype(np.float32)
+        ids, _ = O.moe_topk(lg[None, :E], K, K + 1, lg[None, E:E + 1])
+        for e in ids[0]:
+            expert(int(e))
+
+    def step():
+        x = x0.astype(np.float64)
+        for i, L in enumerate(Ls):
+            n = R.rms_norm(x.astype(np.float32), L["g"], 1e-6)
+            if "qkv" in L:
+                qkv = n @ L["qkv"].T
+                z = n @ L["z"].T
+                ab = n @ L["ab"].T
+                co, _ = R.conv1d_silu(qkv, np.zeros((8192, 3), np.float32), L["conv"])
+                o, _ = R.delta_step(co[:2048].reshape(16, 128), co[2048:4096].reshape(16, 128),
+                                    co[4096:].reshape(32, 128), ab[:32], ab[32:], np.zeros(32), np.zeros(32),
+                                    np.zeros((32, 128, 128)), 1e-6, 16)
+                d = R.gated_norm(o.astype(np.float32), z.reshape(32, 128), np.ones(128, np.float32), 1e-6)
+                x = x + d.reshape(-1) @ L["out"].T
+            else:
+                qg = n @ L["qg"].T
+                vv = n @ L["v"].T
+                att = np.repeat(vv.reshape(2, 256), 8, axis=0)  # position 0: attention returns v
+                x = x + (att * R.sigmoid(qg.reshape(16, 512)[:, 256:])).reshape(-1) @ L["o"].T
+            n = R.rms_norm(x.astype(np.float32), L["g"], 1e-6)
+            lg = (n @ L["router"].T).astype(np.float32)
+            ids, w = O.moe_topk(lg[None, :E], K, K + 1, lg[None, E:E + 1])
+            moe = np.zeros(H)
+            for s_, e in enumerate(ids[0]):
+                w1, w2 = expert(int(e))
+                gu = n @ w1.T
+                moe += w[0, s_] * ((gu[:I] * R.sigmoid(gu[:I]) * gu[I:]) @ w2.T)
+            x = x + moe
+        return x
+
+    step()
+    reps, t0 = 0, time.perf_counter()
+    while reps < 2 or time.perf_counter() - t0 < seconds:
+        step()
+        reps += 1
+    per_layer = (time.perf_counter() - t0) / reps / layers_sample
+    step_s = per_layer * 48
+    return 1.0 / step_s, (f"{reps} x one decode step of one session through the first {layers_sample} layers "
+                          f"(numpy f64 on dequantized NVFP4 weights), scaled to 48 layers: {step_s * 1e3:.0f} ms "
+                          f"per token"), cores
+
+
+def decode_reference_arm(args):
+    rank, _, _ = dist_env()
+    if rank != 0:
+        return
+    v, sample, cores = decode_cpu_sample(min(60.0, max(5.0, 0.2 * (args.steps + args.warmup))))
+    emit({"impl": "reference", "metric": "decode tokens/s", "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
+          "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / v, "higher_is_better": True,
+          "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic (seeded)",
+          "config": decode_config(args.gpus, args.dec_prompt, args.dec_steps),
+          "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
+          "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
+
+
+def decode_arm(args):
+    """Config 4 on each GPU (replicas): build the model, run the 8 sessions'
+    2048-token prompts through the decode step (untimed), then time 256
+    greedy decode steps (CUDA graph replay)."""
+    import torch
+    import torch.distributed as dist
+
+    import firepit_b200 as F
+    from firepit_b200.model import Decoder, HybridConfig, HybridModel
+    rank, world, local, dev = dist_init()
+    cfg = HybridConfig()
+    t_build = time.perf_counter()
+    model = HybridModel(cfg, seed=0, device=dev)
+    build_s = time.perf_counter() - t_build
+    B, steps, plen = DEC_SESSIONS, args.dec_steps, args.dec_prompt
+    dec = Decoder(model, B, plen + steps, history_len=steps)
+    prompt = torch.randint(0, cfg.vocab, (B, plen), dtype=torch.int32, device=dev,
+                           generator=torch.Generator(device=dev).manual_seed(1000 + rank))
+    s = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(s):  # every code path once, outside capture
+        dec.step(s.cuda_stream)
+    torch.cuda.synchronize()
+    dec.reset()
+    before = F.launch_count()
+    dec.capture()
+    launches_per_step = F.launch_count() - before
+    dec.reset()
+    t_pre = time.perf_counter()
+    dec.prefill(prompt)
+    torch.cuda.synchronize()
+    prefill_s = time.perf_counter() - t_pre
+    dist_sync()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record()
+        dec.generate(steps)
+        end.record()
+        torch.cuda.synchronize()
+    t = torch.tensor([start.elapsed_time(end)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = t.item() / steps
+    value = world * B * steps / (t.item() * 1e-3)
+    assert F.device_error() == 0
+    # routes of one more step: distinct experts each layer reads
+    dec.route_log = torch.zeros(cfg.layers, B, cfg.slots, dtype=torch.int32, device=dev)
+    dec.step(torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    distinct = [int(torch.unique(dec.route_log[i]).numel()) for i in range(cfg.layers)]
+    dec.route_log = None
+    wb = model.weight_bytes()
+    pos = plen + steps // 2
+    kv_bytes = sum(1 for i in range(cfg.layers) if cfg.is_attention(i)) * B * pos * cfg.kv_heads * cfg.head_dim * 4 * 2
+    gdn_bytes = sum(1 for i in range(cfg.layers) if not cfg.is_attention(i)) * B * cfg.value_heads * \
+        cfg.key_head_dim * cfg.value_head_dim * 4 * 2
+    step_bytes = wb["dense"] + wb["lm_head"] + sum(distinct) * wb["expert"] + kv_bytes + gdn_bytes
+    hbm, kind = measured_peak()
+    achieved = step_bytes / (ms * 1e-3) / 1e9
+    # e2e: a serving loop that hands every step's tokens to the host and
+    # feeds them back (pinned buffers, a synchronisation per step)
+    tok_h = torch.zeros(B, dtype=torch.int32, pin_memory=True)
+    e2e_steps = 32
+    dec.reset()
+    dec.prefill(prompt[:, :min(64, plen)])
+    torch.cuda.synchronize()
+    e0 = time.perf_counter()
+    for i in range(e2e_steps):
+        if i:
+            dec.tokens.copy_(tok_h, non_blocking=True)
+        dec.graph.replay()
+        tok_h.copy_(dec.tokens, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    e2e_s = time.perf_counter() - e0
+    te = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = world * B * e2e_steps / te.item()
+    out = None
+    if rank == 0:
+        out = {"metric": "decode tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world, "steps": steps,
+               "warmup": plen, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+               "vs_baseline": None,
+               "dtype": "nvfp4 weights (e2m1 x e4m3, f32 accumulate), f32 activations and state, bf16 GEMV inputs",
+               "data": "synthetic (seeded Philox weights N(0,0.02) -> NVFP4; random prompt ids)",
+               "config": decode_config(world, plen, steps),
+               "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                            "frac": achieved / hbm, "traffic": None, "peak_kind": f"{kind} hbm_gbs",
+                            "algorithmic_bytes_per_step": step_bytes,
+                            "note": "per GPU per step: dense + LM-head NVFP4 weights, the distinct experts routed "
+                                    "in each layer (one sampled step), KV caches at the mid position, GDN states "
+                                    "read and written"},
+               "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": 4 * B,
+                       "d2h_bytes_per_step": 4 * B,
+                       "path": "Decoder graph step with each step's tokens copied to pinned host memory and back, "
+                               "a host synchronisation per step (32 steps after a 64-token prompt)"},
+               "gpu_launches": launches_per_step * steps, "clocks": clocks.summary(),
+               "breakdown": {"build_s": build_s, "prompt_s": prefill_s, "distinct_experts_per_layer_mean":
+                             sum(distinct) / len(distinct), "step_gb": step_bytes / 1e9}}
+        if world == 1 and args.cpu_seconds > 0:
+            v, sample, cores = decode_cpu_sample(args.cpu_seconds)
+            out["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
+    del dec, model
+    torch.cuda.empty_cache()
+    dist_sync()
+    return out
+
+
 SUB_RECORDS = [
     # (name, config, runs at one GPU, runs at several GPUs)
     ("config1_fp8_gemm", "fp8_gemm", True, True),
@@ -1420,10 +1647,13 @@ SUB_RECORDS = [
     ("config3_moe_t64", "moe_t64", True, False),
     ("config3_moe_t4096", "moe_t4096", True, False),
     ("config3_moe_ep", "moe_ep", False, True),
+    ("config4_decode", "decode", True, True),
 ]
 
 
 def product_arm(config: str):
+    if config == "decode":
+        return decode_arm
     if config == "moe_ep":
         return moe_ep_arm
     if config.startswith("moe_"):
@@ -1438,6 +1668,8 @@ def product_arm(config: str):
 
 
 def reference_for(config: str):
+    if config == "decode":
+        return decode_reference_arm
     if config.startswith("moe_"):
         return moe_reference_arm
     if config == "fp8_gemm":

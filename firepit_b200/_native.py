@@ -162,6 +162,9 @@ SIGNATURES: dict[str, tuple] = {
     "fpb_decode_combine_add_norm": (i32, [vp, vp, sz, sz, vp, vp, sz, sz, C.c_float, vp, vp, i32, vp]),
     "fpb_argmax_advance": (i32, [vp, sz, sz, vp, vp, vp, sz, vp, vp]),
     "fpb_nvfp4_expert_gemv_tokens": (i32, [vp, vp, i32, vp, i32, i32, sz, vp, i32, vp]),
+    "fpb_moe_decode_plan": (i32, [vp, sz, sz, sz, sz, vp, vp, sz, vp, vp]),
+    "fpb_nvfp4_moe_gemv": (i32, [vp, sz, vp, vp, i32, vp, i32, sz, i32, vp, i32, vp]),
+    "fpb_moe_decode_combine_add_norm": (i32, [vp, vp, vp, sz, sz, vp, vp, sz, sz, C.c_float, vp, vp, i32, vp]),
     "fpb_comm_available": (i32, []),
     "fpb_comm_version": (i32, [C.POINTER(i32)]),
     "fpb_comm_unique_id": (i32, [vp]),

@@ -73,6 +73,62 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   return e;
 }
 
+// launch_pdl with a thread-block cluster of `cluster_x` CTAs along x.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                                      unsigned cluster_x, Args &&...args) {
+  cudaLaunchConfig_t lc{};
+  lc.gridDim = grid;
+  lc.blockDim = block;
+  lc.dynamicSmemBytes = smem;
+  lc.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster_x;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 2;
+  cudaError_t e = cudaLaunchKernelEx(&lc, kernel, args...);
+  if (e == cudaErrorInvalidValue) {
+    cudaGetLastError();
+    lc.numAttrs = 1;
+    e = cudaLaunchKernelEx(&lc, kernel, args...);
+  }
+  return e;
+}
+
+// ---- thread-block clusters (distributed shared memory) ----------------------------
+__device__ __forceinline__ unsigned cluster_ctarank() {
+  unsigned r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ unsigned cluster_nctarank() {
+  unsigned n;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(n));
+  return n;
+}
+
+// Every thread of every CTA of the cluster arrives; writes before it are
+// visible to the cluster after it.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// The float at this CTA's shared-memory address `p`, read from the same
+// address in cluster CTA `rank`.
+__device__ __forceinline__ float dsmem_load(const float *p, unsigned rank) {
+  unsigned local = (unsigned)__cvta_generic_to_shared(p), remote;
+  float v;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local), "r"(rank));
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+  return v;
+}
+
 #define FPB_LAUNCH_CHECK(name)                                   \
   do {                                                           \
     cudaError_t fpb_err_ = cudaGetLastError();                   \

@@ -415,27 +415,28 @@ __global__ void __launch_bounds__(512, 1) gemv_nvfp4_kernel(GemvArgs a) {
 //
 // Dense GEMV with K % 128 == 0, K <= 4096, batch <= 8, over one or several
 // matrices ("segments": each a row range of one matrix with its own x and y,
-// all with the same K).  The segments' rows are laid end to end in a virtual
-// row space; CTA c owns the contiguous virtual rows [c*rpc, (c+1)*rpc) (rpc a
-// multiple of 4) and walks them in units of at most UR rows that never cross
-// a segment.  Warp 0 issues 1-D bulk copies of the CTA's first units (codes,
-// factors and row globals) into a ring of shared-memory stages before
-// griddepcontrol.wait, so with one segment the weights of launch i+1 stream
-// from HBM while launch i computes (two CTAs fit on an SM).  After the wait
-// each warp stages its K slice of the unit's x (f16, prescaled as in the
-// register variant; again only when the segment's x changes) and runs the
-// cvt / mul.f16x2 / m16n8k16 arithmetic on every unit, reading codes from
-// shared memory (row pitch = 64 mod 128 bytes: conflict-free).  Partial sums
-// of the 8 K slices meet in shared memory; the last warp to finish a unit (a
-// shared counter) adds them, stores y and refills the stage with the unit S
-// stages ahead.  Every warp walks the CTA's units itself (one iterator for
-// the unit it computes, one S units ahead for refills), so no unit table is
-// shared.  Units are 16 rows (UR = 16) in every launch: 8-row units (MMA
-// rows 8-15 zero, stages half the size, a ring twice as deep in the same
-// shared memory) measured 1.43x slower on 64 config-0 matrices per launch,
-// and one 16-warp CTA per SM 1.65x slower: the warps' instruction stream, not
-// the arrival of the weights, bounds this kernel (the same launches over
-// weights resident in L2 run at the same speed).
+// all with the same K), or over device-indirect expert segments (MOE, see
+// StreamMoe).  The segments' rows are laid end to end in a virtual row space;
+// CTA c owns the contiguous virtual rows [c*rpc, (c+1)*rpc) (rpc a multiple
+// of 4) and walks them in units of at most UR rows (16 or 32: one or two MMA
+// row blocks, independent chains that share each x fragment) that never
+// cross a segment.  Warp 0 issues the bulk copies of the CTA's first units
+// (codes, factors and row globals, one contiguous copy each) into a ring of
+// shared-memory stages before griddepcontrol.wait, so with dense segments the
+// weights of launch i+1 stream from HBM while launch i computes (two CTAs fit
+// on an SM).  After the wait each warp stages its K slice of the unit's x
+// (f16, prescaled as in the register variant; again only when the segment's
+// x changes; rows 16 mod 128 bytes apart, 16-byte slots swizzled so that the
+// MMA's x reads are conflict-free) and runs the cvt / mul.f16x2 / m16n8k16
+// arithmetic on every unit.  Partial sums of the 8 K slices meet in shared
+// memory; the last warp to finish a unit (a shared counter) adds them, stores
+// y and refills the stage with the unit S stages ahead.  Every warp walks the
+// CTA's units itself (one iterator for the unit it computes, one S units
+// ahead for refills), so no unit table is shared.  What bounds it: the
+// per-unit chain of each warp (wait, decode, MMAs, partial sums, reduction,
+// refill), not DRAM: per-row copies (two bulk copies a row) made the copy
+// issue rate the limit, 8-row units were 1.43x slower than 16-row ones and
+// one 16-warp CTA per SM 1.65x slower than two 8-warp CTAs.
 struct StreamSeg {
   const uint8_t *packed;  // first addressed row
   const uint8_t *scales;
@@ -449,9 +450,24 @@ struct StreamSeg {
 
 constexpr int kStreamMaxSegs = 128;
 
+// Device-indirect segments (the decode MoE GEMV): segment i is expert
+// ids[i]'s rows_per_expert rows, for i < *count, read after the dependency
+// wait.  seg[0] then holds the base pointers: expert 0's first row, x of
+// segment 0 and y of segment 0.
+struct StreamMoe {
+  const int32_t *ids;    // [cap] expert ids of the segments
+  const int32_t *count;  // live segments (device)
+  int cap;
+  int rpe;               // rows per expert = rows of every segment
+  int n_experts;
+  long long x_stride;    // input elements between consecutive segments' x
+  long long y_stride;    // output elements between consecutive segments' y
+};
+
 template <int NSEG>
 struct StreamArgs {
   StreamSeg seg[NSEG];
+  StreamMoe moe;
   int nseg;
   int rpc;  // virtual rows per CTA (multiple of 4)
   long long total_rows;
@@ -461,12 +477,20 @@ struct StreamArgs {
   int wpitch;       // shared bytes per staged code row (64 mod 128)
   int spitch;       // shared bytes per staged factor row
   int scale_rows;   // 1: one copy per factor row; 0: one contiguous copy per unit
-  int stage_bytes;  // UR * wpitch + UR * spitch + 64
-  int xpitch;       // f16 elements per staged input row
+  int contig;       // 1: a unit's codes also arrive as one contiguous copy (pitch K/2)
+  int stage_bytes;  // UR * wpitch + UR * spitch + max(64, 4 * UR)
+  int xpitch;       // f16 elements per staged input row (16 mod 128 bytes)
   int y_bf16;
 };
 
 constexpr int kStreamWarps = 8;
+
+// Position of input element k in its staged row.  Lane (g, q) of an MMA
+// reads the 16 bytes at k = c*128 + q*32 + 8*wi of row g; with rows 16 mod
+// 128 bytes apart and bit 4 of k flipped where bit 6 is set (q = 2, 3), the
+// 8 lanes of each quarter-warp phase (rows g, g + 1, q = 0..3) read 8
+// distinct 16-byte bank groups.
+__device__ __forceinline__ int xswz(int k) { return k ^ (((k >> 6) & 1) << 4); }
 
 __device__ __forceinline__ uint4 lds128(const void *p) {
   uint4 v;
@@ -498,13 +522,13 @@ struct Unit {
 
 // Takes the next unit (at most UR rows, within one segment and below v_hi);
 // false once the range is exhausted.
-template <int UR, int NSEG>
+template <int UR, bool MOE, int NSEG>
 __device__ __forceinline__ bool next_unit(const StreamArgs<NSEG> &a, UnitIter &it, long long v_hi, Unit &u) {
   if (it.v >= v_hi) return false;
   while (it.row >= it.seg_rows) {
     ++it.seg;
     it.row = 0;
-    it.seg_rows = a.seg[it.seg].rows;
+    it.seg_rows = MOE ? a.moe.rpe : a.seg[it.seg].rows;
   }
   u.seg = it.seg;
   u.row0 = it.row;
@@ -516,27 +540,52 @@ __device__ __forceinline__ bool next_unit(const StreamArgs<NSEG> &a, UnitIter &i
 
 // Issues (one warp) the copies of one unit of `u.nrows` rows (a multiple of
 // 4, at most UR) into `stage`.
-template <int UR, int NSEG>
+template <int UR, bool MOE, int NSEG>
 __device__ __forceinline__ void stream_issue(const StreamArgs<NSEG> &a, uint8_t *stage, uint64_t *bar,
                                              const Unit &u, int lane) {
   const uint32_t kb2 = (uint32_t)a.K >> 1, kb16 = (uint32_t)a.K >> 4;
-  const StreamSeg &sg = a.seg[u.seg];
+  const uint8_t *packed, *scales;
+  const float *globals;
+  if (MOE) {
+    int e = a.moe.ids[u.seg];
+    if (e < 0 || e >= a.moe.n_experts) {  // a bad id reads expert 0 and is recorded
+      if (lane == 0 && a.error) atomicCAS(a.error, 0, 203);
+      e = 0;
+    }
+    const size_t r = (size_t)e * a.moe.rpe;
+    packed = a.seg[0].packed + r * kb2;
+    scales = a.seg[0].scales + r * kb16;
+    globals = a.seg[0].globals + r;
+  } else {
+    const StreamSeg &sg = a.seg[u.seg];
+    packed = sg.packed;
+    scales = sg.scales;
+    globals = sg.globals;
+  }
   const int nrows = u.nrows, row0 = u.row0;
   if (lane == 0) sm100::mbar_arrive_expect_tx(bar, (uint32_t)nrows * (kb2 + kb16 + 4));
   __syncwarp();
-  if (lane < nrows)
-    sm100::bulk_load(stage + lane * a.wpitch, sg.packed + (size_t)(row0 + lane) * kb2, kb2, bar);
+  if (a.contig) {
+    if (lane == 0) sm100::bulk_load(stage, packed + (size_t)row0 * kb2, (uint32_t)nrows * kb2, bar);
+  } else {
+    for (int r = lane; r < nrows; r += 32)
+      sm100::bulk_load(stage + r * a.wpitch, packed + (size_t)(row0 + r) * kb2, kb2, bar);
+  }
   uint8_t *sc = stage + UR * a.wpitch;
   if (a.scale_rows) {
-    if (lane >= 16 && lane - 16 < nrows)
-      sm100::bulk_load(sc + (lane - 16) * a.spitch, sg.scales + (size_t)(row0 + lane - 16) * kb16, kb16, bar);
+    for (int r = (lane + 16) & 31; r < nrows; r += 32)  // lanes 16.. start, spreading the issue
+      sm100::bulk_load(sc + r * a.spitch, scales + (size_t)(row0 + r) * kb16, kb16, bar);
   } else if (lane == 16) {
-    sm100::bulk_load(sc, sg.scales + (size_t)row0 * kb16, (uint32_t)nrows * kb16, bar);
+    sm100::bulk_load(sc, scales + (size_t)row0 * kb16, (uint32_t)nrows * kb16, bar);
   }
-  if (lane == 31) sm100::bulk_load(sc + UR * a.spitch, sg.globals + row0, (uint32_t)nrows * 4, bar);
+  if (lane == 31) sm100::bulk_load(sc + UR * a.spitch, globals + row0, (uint32_t)nrows * 4, bar);
 }
 
-template <bool XLO, int NSEG, int UR>
+// MOE: the segments are device-indirect (StreamMoe): the expert ids and their
+// count come from the previous kernel, so nothing is copied before the
+// dependency wait, and each CTA's share of the rows is computed from the
+// count after it.
+template <bool XLO, int NSEG, int UR, bool MOE>
 __global__ void __launch_bounds__(kStreamWarps * 32, 2)
     gemv_nvfp4_stream_kernel(const __grid_constant__ StreamArgs<NSEG> a) {
   constexpr int W = kStreamWarps;
@@ -545,21 +594,38 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 2)
   uint8_t *stages = smem;
   __half *xh = reinterpret_cast<__half *>(smem + (size_t)S * a.stage_bytes);
   __half *xl = xh + (size_t)a.batch * a.xpitch;
+  // Row blocks of 16 per unit (UR = 8: one block whose rows 8-15 are zero).
+  constexpr int RB = UR >= 16 ? UR / 16 : 1;
+  constexpr bool HALF = UR < 16;
   float4 *red = reinterpret_cast<float4 *>(xh + (size_t)a.batch * a.xpitch * (XLO ? 2 : 1));
-  uint64_t *full = reinterpret_cast<uint64_t *>(red + (size_t)S * W * 32);
+  uint64_t *full = reinterpret_cast<uint64_t *>(red + (size_t)S * W * RB * 32);
   int *count = reinterpret_cast<int *>(full + S);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, q = lane & 3;
   if (blockDim.x != W * 32) return;  // the layout below assumes W warps
-  const long long v_lo = (long long)blockIdx.x * a.rpc;
-  const long long v_hi = min(a.total_rows, v_lo + a.rpc);
+  long long total = a.total_rows, rpc = a.rpc;
+  if (MOE) {
+    asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int live = min(max(*a.moe.count, 0), a.moe.cap);
+    total = (long long)live * a.moe.rpe;
+    rpc = ((total + gridDim.x - 1) / gridDim.x + 15) / 16 * 16;
+  }
+  const long long v_lo = (long long)blockIdx.x * rpc;
+  const long long v_hi = min(total, v_lo + rpc);
   if (v_lo >= v_hi) return;
   // The segment holding v_lo (segments are in virtual-row order).
   UnitIter it_c{0, 0, 0, v_lo};
-  while (it_c.seg + 1 < a.nseg && a.seg[it_c.seg + 1].vbeg <= v_lo) ++it_c.seg;
-  it_c.row = (int)(v_lo - a.seg[it_c.seg].vbeg);
-  it_c.seg_rows = a.seg[it_c.seg].rows;
+  if (MOE) {
+    it_c.seg = (int)(v_lo / a.moe.rpe);
+    it_c.row = (int)(v_lo % a.moe.rpe);
+    it_c.seg_rows = a.moe.rpe;
+  } else {
+    while (it_c.seg + 1 < a.nseg && a.seg[it_c.seg + 1].vbeg <= v_lo) ++it_c.seg;
+    it_c.row = (int)(v_lo - a.seg[it_c.seg].vbeg);
+    it_c.seg_rows = a.seg[it_c.seg].rows;
+  }
   UnitIter it_a = it_c;  // S units ahead of it_c once the ring is primed
 
   if (tid == 0) {
@@ -570,14 +636,17 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 2)
     sm100::fence_barrier_init();
   }
   __syncthreads();
-  // Weights are immutable while their handle exists: copy them before the wait.
+  // Weights are immutable while their handle exists: copy them before the
+  // wait (dense segments; device-indirect ones are known only after it).
   for (int s = 0; s < S; ++s) {
     Unit u;
-    if (!next_unit<UR>(a, it_a, v_hi, u)) break;
-    if (warp == 0) stream_issue<UR>(a, stages + (size_t)s * a.stage_bytes, &full[s], u, lane);
+    if (!next_unit<UR, MOE>(a, it_a, v_hi, u)) break;
+    if (warp == 0) stream_issue<UR, MOE>(a, stages + (size_t)s * a.stage_bytes, &full[s], u, lane);
   }
-  asm volatile("griddepcontrol.launch_dependents;");
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (!MOE) {
+    asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+  }
 
   const int chunks = a.K >> 7;
   const int cpw = (chunks + W - 1) / W;
@@ -595,34 +664,59 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 2)
 
   // ---- units -------------------------------------------------------------------
   Unit u;
-  for (int i = 0; next_unit<UR>(a, it_c, v_hi, u); ++i) {
+  for (int i = 0; next_unit<UR, MOE>(a, it_c, v_hi, u); ++i) {
     if (u.seg != cur_seg) {
       cur_seg = u.seg;
-      seg_x = a.seg[u.seg].x;
-      y_seg = a.seg[u.seg].y;
+      if (MOE) {
+        seg_x = static_cast<const char *>(a.seg[0].x) + (size_t)u.seg * a.moe.x_stride * (XLO ? 4 : 2);
+        y_seg = static_cast<char *>(a.seg[0].y) + (size_t)u.seg * a.moe.y_stride * (a.y_bf16 ? 2 : 4);
+      } else {
+        seg_x = a.seg[u.seg].x;
+        y_seg = a.seg[u.seg].y;
+      }
       y_rows = it_c.seg_rows;
     }
     if (seg_x != staged_x) {
       // ---- this warp's K slice of the segment's x, prescaled to f16 ----------
       staged_x = seg_x;
       float my_unscale = 1.0f;  // lane b: batch row b
-      for (int b = 0; b < a.batch; ++b) {
-        float v[2][8];
-        uint32_t m = 0;
+      // Rows in groups of G = 4, every load of a group
+      // issued before the first reduction: the rows' latencies overlap.
+      constexpr int G = 4, NV = XLO ? 2 : 1;
+      for (int b0 = 0; b0 < a.batch; b0 += G) {
+        uint4 raw[G][2][NV];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int p = lane + 32 * h;
-          const long long off = (long long)b * a.K + k_lo + p * 8;
-          if (p < pieces) {
+        for (int bb = 0; bb < G; ++bb)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int b = b0 + bb, p = lane + 32 * h;
+            const bool ok = b < a.batch && p < pieces;
+            const long long off = (long long)b * a.K + k_lo + p * 8;
+#pragma unroll
+            for (int j = 0; j < NV; ++j)
+              raw[bb][h][j] = !ok ? make_uint4(0, 0, 0, 0)
+                              : XLO ? *reinterpret_cast<const uint4 *>(reinterpret_cast<const float *>(seg_x) +
+                                                                       off + 4 * j)
+                                    : *reinterpret_cast<const uint4 *>(reinterpret_cast<const uint16_t *>(seg_x) +
+                                                                       off);
+          }
+#pragma unroll
+        for (int bb = 0; bb < G; ++bb) {
+          const int b = b0 + bb;
+          if (b >= a.batch) break;  // uniform over the warp
+          float v[2][8];
+          uint32_t m = 0;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
             if (XLO) {
-              const float4 f0 = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(seg_x) + off);
-              const float4 f1 =
-                  *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(seg_x) + off + 4);
-              v[h][0] = f0.x; v[h][1] = f0.y; v[h][2] = f0.z; v[h][3] = f0.w;
-              v[h][4] = f1.x; v[h][5] = f1.y; v[h][6] = f1.z; v[h][7] = f1.w;
+#pragma unroll
+              for (int j = 0; j < NV; ++j) {
+                const uint4 r = raw[bb][h][j];
+                v[h][4 * j + 0] = __uint_as_float(r.x); v[h][4 * j + 1] = __uint_as_float(r.y);
+                v[h][4 * j + 2] = __uint_as_float(r.z); v[h][4 * j + 3] = __uint_as_float(r.w);
+              }
             } else {
-              const uint4 r =
-                  *reinterpret_cast<const uint4 *>(reinterpret_cast<const uint16_t *>(seg_x) + off);
+              const uint4 r = raw[bb][h][0];
               const uint32_t wv[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
               for (int t = 0; t < 4; ++t) {
@@ -630,35 +724,32 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 2)
                 v[h][2 * t + 1] = __uint_as_float(wv[t] & 0xffff0000u);
               }
             }
-          } else {
 #pragma unroll
-            for (int t = 0; t < 8; ++t) v[h][t] = 0.0f;
+            for (int t = 0; t < 8; ++t) m = max(m, __float_as_uint(v[h][t]) & 0x7fffffffu);
           }
 #pragma unroll
-          for (int t = 0; t < 8; ++t) m = max(m, __float_as_uint(v[h][t]) & 0x7fffffffu);
-        }
+          for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+          const int F = prescale_exponent(m);
+          const float up = __uint_as_float((uint32_t)(127 + F) << 23);
+          if (lane == b) my_unscale = __uint_as_float((uint32_t)(127 - F) << 23);
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
-        const int F = prescale_exponent(m);
-        const float up = __uint_as_float((uint32_t)(127 + F) << 23);
-        if (lane == b) my_unscale = __uint_as_float((uint32_t)(127 - F) << 23);
+          for (int h = 0; h < 2; ++h) {
+            const int p = lane + 32 * h;
+            if (p >= pieces) continue;
+            uint32_t hv[4], lv[4];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int p = lane + 32 * h;
-          if (p >= pieces) continue;
-          uint32_t hv[4], lv[4];
-#pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            const float v0 = v[h][2 * t] * up, v1 = v[h][2 * t + 1] * up;
-            hv[t] = pack_half2(v0, v1);
-            if (XLO) {
-              const float2 f = __half22float2(*reinterpret_cast<__half2 *>(&hv[t]));
-              lv[t] = pack_half2(v0 - f.x, v1 - f.y);
+            for (int t = 0; t < 4; ++t) {
+              const float v0 = v[h][2 * t] * up, v1 = v[h][2 * t + 1] * up;
+              hv[t] = pack_half2(v0, v1);
+              if (XLO) {
+                const float2 f = __half22float2(*reinterpret_cast<__half2 *>(&hv[t]));
+                lv[t] = pack_half2(v0 - f.x, v1 - f.y);
+              }
             }
+            const size_t o = (size_t)b * a.xpitch + xswz(k_lo + p * 8);
+            *reinterpret_cast<uint4 *>(xh + o) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+            if (XLO) *reinterpret_cast<uint4 *>(xl + o) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
           }
-          const size_t o = (size_t)b * a.xpitch + k_lo + p * 8;
-          *reinterpret_cast<uint4 *>(xh + o) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-          if (XLO) *reinterpret_cast<uint4 *>(xl + o) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
         }
       }
       __syncwarp();
@@ -676,68 +767,88 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 2)
       if (lane == 0 && a.error) atomicCAS(a.error, 0, 201);
       return;
     }
-    float acc[4][4];
+    // RB row blocks, each with NCH independent accumulators (four chains for
+    // one block, two for several: the blocks are independent chains too).
+    constexpr int NCH = RB == 1 ? 4 : 2;
+    float acc[RB][NCH][4];
 #pragma unroll
-    for (int c4 = 0; c4 < 4; ++c4)
+    for (int rb = 0; rb < RB; ++rb)
 #pragma unroll
-      for (int t = 0; t < 4; ++t) acc[c4][t] = 0.0f;
+      for (int c4 = 0; c4 < NCH; ++c4)
+#pragma unroll
+        for (int t = 0; t < 4; ++t) acc[rb][c4][t] = 0.0f;
 
     const uint8_t *sc = st + UR * a.wpitch;
+    const int live_rb = min(RB, (u.nrows + 15) >> 4);  // blocks holding rows of this unit
     for (int c = c_lo; c < c_hi; ++c) {
-      const uint4 wa = lds128(st + g * a.wpitch + c * 64 + q * 16);
-      const uint4 wb = UR == 16 ? lds128(st + (g + 8) * a.wpitch + c * 64 + q * 16) : make_uint4(0, 0, 0, 0);
-      const uint16_t sa = lds16(sc + g * a.spitch + c * 8 + 2 * q);
-      const uint16_t sb = UR == 16 ? lds16(sc + (g + 8) * a.spitch + c * 8 + 2 * q) : (uint16_t)0;
-      uint32_t s_lo[2], s_hi[2];
-      {
-        const uint32_t fa = e4m3x2_to_f16x2(sa);
-        s_lo[0] = __byte_perm(fa, fa, 0x1010);
-        s_hi[0] = __byte_perm(fa, fa, 0x3232);
-        if (UR == 16) {
-          const uint32_t fb = e4m3x2_to_f16x2(sb);
-          s_lo[1] = __byte_perm(fb, fb, 0x1010);
-          s_hi[1] = __byte_perm(fb, fb, 0x3232);
+      uint4 wa[RB], wb[RB];
+      uint32_t s_lo[RB][2], s_hi[RB][2];
+#pragma unroll
+      for (int rb = 0; rb < RB; ++rb) {
+        const int r0 = rb * 16 + g;
+        wa[rb] = lds128(st + r0 * a.wpitch + c * 64 + q * 16);
+        wb[rb] = HALF ? make_uint4(0, 0, 0, 0) : lds128(st + (r0 + 8) * a.wpitch + c * 64 + q * 16);
+        const uint32_t fa = e4m3x2_to_f16x2(lds16(sc + r0 * a.spitch + c * 8 + 2 * q));
+        s_lo[rb][0] = __byte_perm(fa, fa, 0x1010);
+        s_hi[rb][0] = __byte_perm(fa, fa, 0x3232);
+        if (!HALF) {
+          const uint32_t fb = e4m3x2_to_f16x2(lds16(sc + (r0 + 8) * a.spitch + c * 8 + 2 * q));
+          s_lo[rb][1] = __byte_perm(fb, fb, 0x1010);
+          s_hi[rb][1] = __byte_perm(fb, fb, 0x3232);
         } else {
-          s_lo[1] = s_hi[1] = 0;
+          s_lo[rb][1] = s_hi[rb][1] = 0;
         }
       }
-      const uint32_t w0[4] = {wa.x, wa.y, wa.z, wa.w};
-      const uint32_t w1[4] = {wb.x, wb.y, wb.z, wb.w};
       const int k0 = c * 128 + q * 32;
 #pragma unroll
       for (int wi = 0; wi < 4; ++wi) {
         uint4 xv = make_uint4(0, 0, 0, 0), xlv = make_uint4(0, 0, 0, 0);
         if (n_ok) {
-          xv = lds128(xrow + k0 + 8 * wi);
-          if (XLO) xlv = lds128(xrow_lo + k0 + 8 * wi);
+          const int kx = xswz(k0 + 8 * wi);
+          xv = lds128(xrow + kx);
+          if (XLO) xlv = lds128(xrow_lo + kx);
         }
-        uint32_t f0[4], f1[4] = {0, 0, 0, 0};
-        e2m1x8_to_f16x8(w0[wi], f0);
-        if (UR == 16) e2m1x8_to_f16x8(w1[wi], f1);
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          f0[t] = hmul2(f0[t], wi < 2 ? s_lo[0] : s_hi[0]);
-          if (UR == 16) f1[t] = hmul2(f1[t], wi < 2 ? s_lo[1] : s_hi[1]);
-        }
-        // MMA 2wi + jj takes codes 4jj..4jj+3 of this word and x words 2jj, 2jj+1.
-        const int ch = (wi & 1) * 2;
-        mma_f16(acc[ch], f0[0], f1[0], f0[1], f1[1], xv.x, xv.y);
-        mma_f16(acc[ch + 1], f0[2], f1[2], f0[3], f1[3], xv.z, xv.w);
-        if (XLO) {
-          mma_f16(acc[ch], f0[0], f1[0], f0[1], f1[1], xlv.x, xlv.y);
-          mma_f16(acc[ch + 1], f0[2], f1[2], f0[3], f1[3], xlv.z, xlv.w);
+        for (int rb = 0; rb < RB; ++rb) {
+          if (rb >= live_rb) break;  // uniform over the warp
+          const uint32_t w0 = wi == 0 ? wa[rb].x : wi == 1 ? wa[rb].y : wi == 2 ? wa[rb].z : wa[rb].w;
+          const uint32_t w1 = wi == 0 ? wb[rb].x : wi == 1 ? wb[rb].y : wi == 2 ? wb[rb].z : wb[rb].w;
+          uint32_t f0[4], f1[4] = {0, 0, 0, 0};
+          e2m1x8_to_f16x8(w0, f0);
+          if (!HALF) e2m1x8_to_f16x8(w1, f1);
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            f0[t] = hmul2(f0[t], wi < 2 ? s_lo[rb][0] : s_hi[rb][0]);
+            if (!HALF) f1[t] = hmul2(f1[t], wi < 2 ? s_lo[rb][1] : s_hi[rb][1]);
+          }
+          // MMA 2wi + jj takes codes 4jj..4jj+3 of this word and x words 2jj, 2jj+1.
+          const int ch = NCH == 4 ? (wi & 1) * 2 : 0;
+          mma_f16(acc[rb][ch], f0[0], f1[0], f0[1], f1[1], xv.x, xv.y);
+          mma_f16(acc[rb][ch + 1], f0[2], f1[2], f0[3], f1[3], xv.z, xv.w);
+          if (XLO) {
+            mma_f16(acc[rb][ch], f0[0], f1[0], f0[1], f1[1], xlv.x, xlv.y);
+            mma_f16(acc[rb][ch + 1], f0[2], f1[2], f0[3], f1[3], xlv.z, xlv.w);
+          }
         }
       }
     }
-    float4 *slot = red + (size_t)s * W * 32;
-    slot[warp * 32 + lane] = make_float4((acc[0][0] + acc[1][0] + acc[2][0] + acc[3][0]) * us0,
-                                         (acc[0][1] + acc[1][1] + acc[2][1] + acc[3][1]) * us1,
-                                         (acc[0][2] + acc[1][2] + acc[2][2] + acc[3][2]) * us0,
-                                         (acc[0][3] + acc[1][3] + acc[2][3] + acc[3][3]) * us1);
+    float4 *slot = red + (size_t)s * W * RB * 32;
+#pragma unroll
+    for (int rb = 0; rb < RB; ++rb) {
+      float v4[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        float sum = acc[rb][0][t];
+#pragma unroll
+        for (int c4 = 1; c4 < NCH; ++c4) sum += acc[rb][c4][t];
+        v4[t] = sum * ((t & 1) ? us1 : us0);
+      }
+      slot[(warp * RB + rb) * 32 + lane] = make_float4(v4[0], v4[1], v4[2], v4[3]);
+    }
     // The unit S ahead, which the last warp to finish this one copies into
     // its stage (every warp advances its look-ahead iterator in step).
     Unit ahead;
-    const bool has_ahead = next_unit<UR>(a, it_a, v_hi, ahead);
+    const bool has_ahead = next_unit<UR, MOE>(a, it_a, v_hi, ahead);
     // The last of the W warps to finish this unit reduces it, stores y and
     // refills the stage (the counter only grows: last = W-th arrival).
     __syncwarp();
@@ -750,30 +861,34 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 2)
     last = __shfl_sync(0xffffffffu, last, 0);
     __syncwarp();
     if (!last) continue;
-    float4 sum = slot[lane];
-#pragma unroll
-    for (int w = 1; w < W; ++w) {
-      const float4 p = slot[w * 32 + lane];
-      sum.x += p.x; sum.y += p.y; sum.z += p.z; sum.w += p.w;
-    }
     const float *gl = reinterpret_cast<const float *>(sc + UR * a.spitch);
-    const float vals[4] = {sum.x, sum.y, sum.z, sum.w};
 #pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      const int rl = g + ((t >> 1) << 3), n = 2 * q + (t & 1);
-      if (rl < u.nrows && n < a.batch) {
-        const float v = vals[t] * gl[rl];
-        const size_t off = (size_t)n * y_rows + u.row0 + rl;
-        if (a.y_bf16)
-          reinterpret_cast<__nv_bfloat16 *>(y_seg)[off] = __float2bfloat16_rn(v);
-        else
-          reinterpret_cast<float *>(y_seg)[off] = v;
+    for (int rb = 0; rb < RB; ++rb) {
+      if (rb >= live_rb) break;
+      float4 sum = slot[rb * 32 + lane];
+#pragma unroll
+      for (int w = 1; w < W; ++w) {
+        const float4 p = slot[(w * RB + rb) * 32 + lane];
+        sum.x += p.x; sum.y += p.y; sum.z += p.z; sum.w += p.w;
+      }
+      const float vals[4] = {sum.x, sum.y, sum.z, sum.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const int rl = rb * 16 + g + ((t >> 1) << 3), n = 2 * q + (t & 1);
+        if (rl < u.nrows && n < a.batch) {
+          const float v = vals[t] * gl[rl];
+          const size_t off = (size_t)n * y_rows + u.row0 + rl;
+          if (a.y_bf16)
+            reinterpret_cast<__nv_bfloat16 *>(y_seg)[off] = __float2bfloat16_rn(v);
+          else
+            reinterpret_cast<float *>(y_seg)[off] = v;
+        }
       }
     }
     if (has_ahead) {
       __syncwarp();
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      stream_issue<UR>(a, st, &full[s], ahead, lane);
+      stream_issue<UR, MOE>(a, st, &full[s], ahead, lane);
     }
   }
 }
@@ -936,6 +1051,15 @@ static int run_gemv_slice(GemvArgs args, int slots, bool x_f32, cudaStream_t str
 // reservations) fit in the 228 KB of an SM.
 constexpr int kStreamSmemBudget = 110 * 1024;
 
+// A unit's codes, factors and row globals each arrive as one contiguous bulk
+// copy (rows are contiguous in HBM).  Copies of single rows would pad the
+// shared-memory row pitch against bank conflicts, but cost two copies per
+// row, and the copy issue rate, not the bytes, then bounded the kernel (a
+// 512-column expert GEMV ran 1.9x slower, 4096-column rows 1.15x).
+#ifndef FPB_STREAM_CONTIG
+#define FPB_STREAM_CONTIG 1
+#endif
+
 // Ring and staging geometry of the streaming kernel for (K, batch, x dtype,
 // unit rows); false when the streaming kernel cannot serve that shape.
 template <int NSEG>
@@ -945,13 +1069,15 @@ static bool stream_geometry(int K, int batch, bool x_f32, int unit_rows, long lo
   a->K = K;
   a->batch = batch;
   const int kb2 = K / 2, kb16 = K / 16;
-  a->wpitch = kb2 + ((kb2 % 128 == 0) ? 64 : 0);  // 64 mod 128
-  a->scale_rows = kb16 % 16 == 0;
+  a->contig = FPB_STREAM_CONTIG;
+  a->wpitch = a->contig ? kb2 : kb2 + ((kb2 % 128 == 0) ? 64 : 0);  // 64 mod 128 when per row
+  a->scale_rows = !a->contig && kb16 % 16 == 0;
   a->spitch = a->scale_rows ? kb16 + (16 - kb16 % 128 + 128) % 128 : kb16;  // 16 mod 128 when per row
-  a->stage_bytes = unit_rows * a->wpitch + unit_rows * a->spitch + 64;
-  a->xpitch = K + 32;
+  a->stage_bytes = unit_rows * a->wpitch + unit_rows * a->spitch + std::max(64, unit_rows * 4);  // + row globals
+  a->xpitch = K + 8;
   const size_t x_bytes = (size_t)batch * a->xpitch * 2 * (x_f32 ? 2 : 1);
-  const size_t per_stage = (size_t)a->stage_bytes + kStreamWarps * 32 * sizeof(float4) + 12;
+  const int row_blocks = unit_rows >= 16 ? unit_rows / 16 : 1;
+  const size_t per_stage = (size_t)a->stage_bytes + (size_t)kStreamWarps * row_blocks * 32 * sizeof(float4) + 12;
   if (x_bytes + per_stage + 16 > (size_t)kStreamSmemBudget) return false;
   long long S = (long long)((kStreamSmemBudget - x_bytes - 16) / per_stage);
   S = std::max(1LL, std::min({S, 8LL, max_units_per_cta}));
@@ -959,6 +1085,31 @@ static bool stream_geometry(int K, int batch, bool x_f32, int unit_rows, long lo
   *smem = (size_t)S * per_stage + x_bytes + 16;
   return true;
 }
+
+#ifndef FPB_STREAM_UNIT_ROWS_MAX
+#define FPB_STREAM_UNIT_ROWS_MAX 32  // 64-row units need more than 128 registers a thread (spills)
+#endif
+
+// Rows per unit for a launch whose CTAs own about `rows_per_cta` rows: a
+// unit's row blocks are independent MMA chains sharing each x fragment, and
+// the per-unit protocol (wait, partial sums, reduction, refill) is paid once
+// per unit, so the largest size up to FPB_STREAM_UNIT_ROWS_MAX that fits the
+// CTA's share and a ring of two stages, else 16.  0 when the kernel cannot
+// take the shape.
+template <int NSEG>
+static int stream_plan(int K, int batch, bool x_f32, long long rows_per_cta, long long extra_units,
+                       StreamArgs<NSEG> *a, size_t *smem) {
+  for (int ur = FPB_STREAM_UNIT_ROWS_MAX; ur > 16; ur /= 2) {
+    if (ur > rows_per_cta) continue;
+    if (stream_geometry(K, batch, x_f32, ur, (rows_per_cta + ur - 1) / ur + extra_units, a, smem) && a->stages >= 2)
+      return ur;
+  }
+  return stream_geometry(K, batch, x_f32, 16, (rows_per_cta + 15) / 16 + extra_units, a, smem) ? 16 : 0;
+}
+
+template <int NSEG, bool MOE = false>
+static int launch_stream_ur(int ur, const StreamArgs<NSEG> &a, int grid, size_t smem, bool x_f32,
+                            cudaStream_t stream);
 
 // A segment the streaming kernel can read with 16-byte bulk copies: rows and
 // the first row a multiple of 4 (so every unit's factor and global copies are
@@ -968,9 +1119,9 @@ static bool stream_segment_ok(const uint8_t *packed, const uint8_t *scales, cons
          reinterpret_cast<uintptr_t>(scales) % 16 == 0 && reinterpret_cast<uintptr_t>(globals) % 16 == 0;
 }
 
-template <int NSEG, int UR>
+template <int NSEG, int UR, bool MOE = false>
 static int launch_stream(const StreamArgs<NSEG> &a, int grid, size_t smem, bool x_f32, cudaStream_t stream) {
-  auto k = x_f32 ? gemv_nvfp4_stream_kernel<true, NSEG, UR> : gemv_nvfp4_stream_kernel<false, NSEG, UR>;
+  auto k = x_f32 ? gemv_nvfp4_stream_kernel<true, NSEG, UR, MOE> : gemv_nvfp4_stream_kernel<false, NSEG, UR, MOE>;
   {
     // Raised once per device and kernel to the budget, never lowered.
     static std::mutex mu;
@@ -1023,7 +1174,8 @@ static int try_stream_single(const uint8_t *packed, const uint8_t *scales, const
   int rpc = (rows + nsm - 1) / nsm;
   rpc = (rpc + 3) / 4 * 4;
   size_t smem = 0;
-  if (!stream_geometry(K, batch, x_f32, 16, (rpc + 15) / 16, &a, &smem)) return FPB_OK;
+  const int ur = stream_plan(K, batch, x_f32, rpc, 0, &a, &smem);
+  if (!ur) return FPB_OK;
   a.seg[0] = StreamSeg{packed, scales, globals, x, y, 0, rows, 0};
   a.nseg = 1;
   a.rpc = rpc;
@@ -1031,7 +1183,20 @@ static int try_stream_single(const uint8_t *packed, const uint8_t *scales, const
   a.error = device_error_ptr();
   a.y_bf16 = y_bf16;
   *served = true;
-  return launch_stream<1, 16>(a, (rows + rpc - 1) / rpc, smem, x_f32, stream);
+  return launch_stream_ur<1>(ur, a, (rows + rpc - 1) / rpc, smem, x_f32, stream);
+}
+
+template <int NSEG, bool MOE>
+static int launch_stream_ur(int ur, const StreamArgs<NSEG> &a, int grid, size_t smem, bool x_f32,
+                            cudaStream_t stream) {
+  switch (ur) {
+    case 16: return launch_stream<NSEG, 16, MOE>(a, grid, smem, x_f32, stream);
+    case 32: return launch_stream<NSEG, 32, MOE>(a, grid, smem, x_f32, stream);
+#if FPB_STREAM_UNIT_ROWS_MAX >= 64
+    case 64: return launch_stream<NSEG, 64, MOE>(a, grid, smem, x_f32, stream);
+#endif
+    default: return fail(FPB_ERR_UNSUPPORTED, "streaming GEMV: unit rows %d", ur);
+  }
 }
 
 }  // namespace fpb
@@ -1150,6 +1315,64 @@ extern "C" int fpb_nvfp4_expert_gemv_tokens(const fpb_nvfp4_matrix *w, const voi
   return run_gemv(a, tokens * slots_per_token, x_dtype == FPB_F32, as_stream(stream));
 }
 
+// The decode MoE GEMV over distinct experts (see fpb_nvfp4_moe_gemv in the
+// header): the streaming kernel with device-indirect segments when it can
+// take the shape, else the register kernel in expert mode over all `cap`
+// slots (ids past the count are -1 there and give zero rows).
+extern "C" int fpb_nvfp4_moe_gemv(const fpb_nvfp4_matrix *w, size_t rows_per_expert, const int32_t *experts,
+                                  const int32_t *count, int cap, const void *x, int x_dtype, size_t x_stride,
+                                  int tokens, void *y, int y_dtype, void *stream) {
+  if (!w || !experts || !count || !x || !y) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_moe_gemv: null pointer");
+  if (cap < 1 || cap > 65535) return fail(FPB_ERR_SHAPE, "fpb_nvfp4_moe_gemv: cap %d", cap);
+  if (tokens < 1 || tokens > 16) return fail(FPB_ERR_SHAPE, "fpb_nvfp4_moe_gemv: tokens %d not in [1, 16]", tokens);
+  if (rows_per_expert == 0 || w->rows % rows_per_expert != 0 || rows_per_expert > 0x7fffffff)
+    return fail(FPB_ERR_SHAPE, "fpb_nvfp4_moe_gemv: rows %zu not a multiple of rows_per_expert %zu", w->rows,
+                rows_per_expert);
+  if ((x_dtype != FPB_F32 && x_dtype != FPB_BF16) || (y_dtype != FPB_F32 && y_dtype != FPB_BF16))
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_moe_gemv: dtype");
+  const bool x_f32 = x_dtype == FPB_F32, y_bf16 = y_dtype == FPB_BF16;
+  const size_t xe = x_f32 ? 4 : 2;
+  if (reinterpret_cast<uintptr_t>(x) % 16 != 0 || (x_stride * xe) % 16 != 0)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_moe_gemv: x and x_stride must keep 16-byte alignment");
+  if (x_stride != 0 && x_stride < (size_t)tokens * w->cols)
+    return fail(FPB_ERR_SHAPE, "fpb_nvfp4_moe_gemv: x_stride %zu below tokens x cols", x_stride);
+  const int K = (int)w->cols, rpe = (int)rows_per_expert;
+  cudaStream_t s = as_stream(stream);
+  StreamArgs<1> a{};
+  size_t smem = 0;
+  const int grid = 2 * std::max(1, sm_count());
+  // rows per CTA when every slot holds a distinct expert (the most there can be)
+  const long long share = ((long long)cap * rpe + grid - 1) / grid;
+  int ur = 0;
+  if (tokens <= 8 && rpe % 4 == 0 && stream_segment_ok(w->packed, w->scales, w->row_globals, rpe) &&
+      (ur = stream_plan(K, tokens, x_f32, share, 2, &a, &smem)) != 0) {
+    a.seg[0] = StreamSeg{w->packed, w->scales, w->row_globals, x, y, 0, rpe, 0};
+    a.nseg = 1;
+    a.moe = StreamMoe{experts, count, cap, rpe, (int)(w->rows / rows_per_expert), (long long)x_stride,
+                      (long long)tokens * rpe};
+    a.error = device_error_ptr();
+    a.y_bf16 = y_bf16;
+    return launch_stream_ur<1, true>(ur, a, grid, smem, x_f32, s);
+  }
+  GemvArgs g{};
+  g.packed = w->packed;
+  g.scales = w->scales;
+  g.globals = w->row_globals;
+  g.x = x;
+  g.y = y;
+  g.expert_ids = experts;
+  g.n_experts = (int)(w->rows / rows_per_expert);
+  g.rows = rpe;
+  g.K = K;
+  g.batch = tokens;
+  g.y_bf16 = y_bf16;
+  g.y_batch_stride = rpe;
+  g.x_slot_stride = (long long)x_stride;
+  g.x_div = 1;
+  g.y_slot_stride = (long long)tokens * rpe;
+  return run_gemv(g, cap, x_f32, s);
+}
+
 // Several dense GEMVs in one launch (see fpb_nvfp4_gemv_batched in the
 // header).  Served by the streaming kernel over up to kStreamMaxSegs
 // segments, two CTAs per SM, each owning an equal share of the segments'
@@ -1204,22 +1427,21 @@ extern "C" int fpb_nvfp4_gemv_batched(const fpb_gemv_segment *segs, int count, i
   }
   bool streamed = false;
   if (nstream > 0) {
-    constexpr int unit_rows = 16;
     const int grid_target = 2 * std::max(1, sm_count());
     long long rpc = (total + grid_target - 1) / grid_target;
     rpc = (rpc + 3) / 4 * 4;
     size_t smem = 0;
     // A CTA's rows split into at most one more unit per segment they touch;
     // its ring never needs more stages than units.
-    if (rpc <= 0x7fffffff &&
-        stream_geometry((int)K, batch, x_f32, unit_rows, (rpc + unit_rows - 1) / unit_rows + nstream, &a, &smem)) {
+    int unit_rows = 0;
+    if (rpc <= 0x7fffffff && (unit_rows = stream_plan((int)K, batch, x_f32, rpc, nstream, &a, &smem)) != 0) {
       a.nseg = nstream;
       a.rpc = (int)rpc;
       a.total_rows = total;
       a.error = device_error_ptr();
       a.y_bf16 = y_dtype == FPB_BF16;
       const int grid = (int)((total + rpc - 1) / rpc);
-      int st = launch_stream<kStreamMaxSegs, unit_rows>(a, grid, smem, x_f32, s);
+      int st = launch_stream_ur<kStreamMaxSegs>(unit_rows, a, grid, smem, x_f32, s);
       if (st) return st;
       streamed = true;
     }

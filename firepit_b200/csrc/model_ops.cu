@@ -16,7 +16,10 @@
 //   argmax           firepit src/generation.rs:34-42 (greedy)
 // Every kernel starts with pdl_enter() (programmatic dependent launch: it waits
 // for the previous kernel before reading anything).
+#include <algorithm>
 #include <cmath>
+#include <mutex>
+#include <vector>
 
 #include "common.cuh"
 
@@ -66,18 +69,45 @@ __global__ void embedding_kernel(const __nv_bfloat16 *table, const int32_t *ids,
 }
 
 // ---- RMSNorm (norm.rs): out = x * rsqrt(mean(x^2) + eps) * gamma -------------------------------
-// One warp per row; with `delta`, x = residual + delta is also stored to `sum_out`.
+// Minimum over the CTA (every thread gets it); `red` holds 32 floats.
+__device__ __forceinline__ float block_min(float v, float *red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fminf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = red[0];
+  for (int i = 1; i < warps; ++i) t = fminf(t, red[i]);
+  return t;
+}
+
+// Sum over the CTA (every thread gets it); `red` holds 32 floats.
+__device__ __forceinline__ float block_sum(float v, float *red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();  // red may still be read by a previous call
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.0f;
+  for (int w = 0; w < warps; ++w) t += red[w];
+  return t;
+}
+
+// One CTA per row (a decode batch has a few rows, each a few thousand
+// columns: the row's loads spread over the CTA's threads); with `delta`,
+// x = residual + delta is also stored to `sum_out`.
 template <typename T>
 __global__ void rms_norm_kernel(const T *x, size_t x_pitch, const float *delta, float *sum_out, int rows,
                                 int width, const float *gamma, float inv_w, float eps, void *out, int out_bf16,
                                 size_t out_pitch) {
   pdl_enter();
-  const int warps = blockDim.x / 32, lane = threadIdx.x & 31;
-  const int r = blockIdx.x * warps + threadIdx.x / 32;
-  if (r >= rows) return;
+  __shared__ float red[32];
+  const int r = blockIdx.x;
   const T *xr = x + (size_t)r * x_pitch;
   float ss = 0.0f;
-  for (int c = lane; c < width; c += 32) {
+#pragma unroll 4
+  for (int c = threadIdx.x; c < width; c += blockDim.x) {
     float v = load_f(xr, c);
     if (delta) {
       v += delta[(size_t)r * width + c];
@@ -85,12 +115,76 @@ __global__ void rms_norm_kernel(const T *x, size_t x_pitch, const float *delta, 
     }
     ss = fmaf(v, v, ss);
   }
-  ss = warp_sum(ss);
-  const float scale = __frsqrt_rn(fmaf(ss, inv_w, eps));
-  for (int c = lane; c < width; c += 32) {
+  const float scale = __frsqrt_rn(fmaf(block_sum(ss, red), inv_w, eps));
+#pragma unroll 4
+  for (int c = threadIdx.x; c < width; c += blockDim.x) {
     const float v = delta ? sum_out[(size_t)r * width + c] : load_f(xr, c);
     store_f(out, out_bf16, (size_t)r * out_pitch + c, v * scale * gamma[c]);
   }
+}
+
+// Row norms over a thread-block cluster: a decode batch has a few rows of a
+// few thousand columns, so each row is spread over the `n` CTAs of one
+// cluster (CTA rank r owns columns [r * per, (r + 1) * per), each thread up
+// to kClusterVals of them, held in registers); the CTAs' sums of squares
+// meet through distributed shared memory, added in rank order on every CTA.
+constexpr int kClusterVals = 4, kClusterThreads = 256, kClusterMax = 8;
+
+// Sum over the cluster of one value per CTA (every thread gets it).  `slot`
+// is a shared float of this CTA that other CTAs read: the caller ends with
+// cluster_sync() so that no CTA leaves while its slot may still be read.
+__device__ __forceinline__ float cluster_total(float cta_value, float *slot) {
+  if (threadIdx.x == 0) *slot = cta_value;
+  cluster_sync();
+  const unsigned n = cluster_nctarank();
+  float t = 0.0f;
+  for (unsigned r = 0; r < n; ++r) t += dsmem_load(slot, r);
+  return t;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kClusterThreads) rms_norm_cluster_kernel(
+    const T *x, size_t x_pitch, const float *delta, float *sum_out, int width, const float *gamma, float inv_w,
+    float eps, void *out, int out_bf16, size_t out_pitch) {
+  pdl_enter();
+  __shared__ float red[32];
+  __shared__ float slot;
+  const int r = blockIdx.y;
+  const int n = (int)cluster_nctarank(), per = (width + n - 1) / n;
+  const int c0 = (int)cluster_ctarank() * per, c1 = min(width, c0 + per);
+  const T *xr = x + (size_t)r * x_pitch;
+  float v[kClusterVals];
+  float ss = 0.0f;
+#pragma unroll
+  for (int k = 0; k < kClusterVals; ++k) {
+    const int c = c0 + threadIdx.x + k * kClusterThreads;
+    float e = 0.0f;
+    if (c < c1) {
+      e = load_f(xr, c);
+      if (delta) {
+        e += delta[(size_t)r * width + c];
+        sum_out[(size_t)r * width + c] = e;
+      }
+    }
+    v[k] = e;
+    ss = fmaf(e, e, ss);
+  }
+  const float tot = cluster_total(block_sum(ss, red), &slot);
+  const float scale = __frsqrt_rn(fmaf(tot, inv_w, eps));
+#pragma unroll
+  for (int k = 0; k < kClusterVals; ++k) {
+    const int c = c0 + threadIdx.x + k * kClusterThreads;
+    if (c < c1) store_f(out, out_bf16, (size_t)r * out_pitch + c, v[k] * scale * gamma[c]);
+  }
+  cluster_sync();
+}
+
+// Cluster size for rows of `width` columns, or 0 when a row needs more than
+// kClusterMax CTAs' registers (the one-CTA-per-row kernels then run).
+int cluster_for(size_t width) {
+  const size_t n = (width + kClusterThreads - 1) / kClusterThreads;
+  const size_t c = std::min<size_t>(kClusterMax, std::max<size_t>(1, n));
+  return (width + c - 1) / c <= (size_t)kClusterVals * kClusterThreads ? (int)c : 0;
 }
 
 // ---- full attention: head norms, RoPE, cache append --------------------------------------------
@@ -217,6 +311,116 @@ __global__ void attn_decode_partial_kernel(const float *q, const float *k_cache,
   }
 }
 
+// The same partials from a shared-memory tile: block (b, kv head, chunk of
+// kAttnTile positions); the tile's K and V rows are loaded by all threads as
+// 16-byte pieces (each row 1 KB contiguous) into rows padded to 260 floats
+// (a warp's 16-byte reads of 32 rows fall on distinct banks), with the
+// group's q vectors.  Warp h scores query head h against the tile (lane t:
+// position t), takes the tile's max and sum of exponentials with warp
+// shuffles, and accumulates p . V with lanes over the head dimension.
+constexpr int kAttnTile = 32, kAttnPitch = kAttnMaxD + 4, kAttnTileThreads = 256;
+
+__global__ void __launch_bounds__(kAttnTileThreads) attn_decode_tile_kernel(
+    const float *q, const float *k_cache, const float *v_cache, const int32_t *positions, int q_heads, int kv_heads,
+    int D, int max_seq, int chunks, float scale, float *part) {
+  pdl_enter();
+  extern __shared__ float4 attn_sm[];
+  float *ks = reinterpret_cast<float *>(attn_sm);  // [kAttnTile][kAttnPitch]
+  float *vs = ks + kAttnTile * kAttnPitch;         // [kAttnTile][kAttnPitch]
+  float *qs = vs + kAttnTile * kAttnPitch;         // [group][D]
+  const int group = q_heads / kv_heads;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int bk = blockIdx.x, chunk = blockIdx.y;
+  const int b = bk / kv_heads, kvh = bk % kv_heads;
+  const int limit = min(positions[b], max_seq - 1) + 1;  // positions 0 .. pos
+  const int t0 = chunk * kAttnTile, n = min(limit - t0, kAttnTile);
+  if (n <= 0) return;  // past this row's position: not read by the merge
+  const int d4 = D / 4;
+  for (int i = tid; i < n * d4; i += kAttnTileThreads) {
+    const int r = i / d4, c = i % d4;
+    const size_t g = (((size_t)b * max_seq + t0 + r) * kv_heads + kvh) * D + 4 * c;
+    reinterpret_cast<float4 *>(ks + r * kAttnPitch)[c] = __ldg(reinterpret_cast<const float4 *>(k_cache + g));
+    reinterpret_cast<float4 *>(vs + r * kAttnPitch)[c] = __ldg(reinterpret_cast<const float4 *>(v_cache + g));
+  }
+  for (int i = tid; i < group * d4; i += kAttnTileThreads) {
+    const int h = i / d4, c = i % d4;
+    reinterpret_cast<float4 *>(qs + h * D)[c] =
+        __ldg(reinterpret_cast<const float4 *>(q + ((size_t)b * q_heads + kvh * group + h) * D) + c);
+  }
+  __syncthreads();
+  for (int h = w; h < group; h += kAttnTileThreads / 32) {
+    const int qh = kvh * group + h;
+    float sc = 0.0f;
+    if (lane < n) {
+      const float4 *kr = reinterpret_cast<const float4 *>(ks + lane * kAttnPitch);
+      const float4 *qr = reinterpret_cast<const float4 *>(qs + h * D);
+      for (int c = 0; c < d4; ++c) {
+        const float4 kv = kr[c], qv = qr[c];
+        sc = fmaf(qv.x, kv.x, sc);
+        sc = fmaf(qv.y, kv.y, sc);
+        sc = fmaf(qv.z, kv.z, sc);
+        sc = fmaf(qv.w, kv.w, sc);
+      }
+      sc *= scale;
+    }
+    float m = lane < n ? sc : -INFINITY;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float p = lane < n ? expf(sc - m) : 0.0f;
+    const float l = warp_sum(p);
+    constexpr int kPer = kAttnMaxD / 32;
+    float acc[kPer];
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) acc[i] = 0.0f;
+    for (int t = 0; t < n; ++t) {
+      const float pt = __shfl_sync(0xffffffffu, p, t);
+      const float *vr = vs + t * kAttnPitch;
+#pragma unroll
+      for (int i = 0; i < kPer; ++i)
+        if (lane + 32 * i < D) acc[i] = fmaf(pt, vr[lane + 32 * i], acc[i]);
+    }
+    float *out = part + (((size_t)b * q_heads + qh) * chunks + chunk) * (D + 2);
+#pragma unroll
+    for (int i = 0; i < kPer; ++i)
+      if (lane + 32 * i < D) out[lane + 32 * i] = acc[i];
+    if (lane == 0) {
+      out[D] = m;
+      out[D + 1] = l;
+    }
+  }
+}
+
+// Merge of the tile kernel's chunks with the output gate: one block per
+// (b, q head); the chunk weights exp(m_c - m) in shared memory, threads over
+// the head dimension.
+__global__ void attn_decode_merge_kernel(const float *part, const float *q_gate, long long qg_pitch,
+                                         const int32_t *positions, int q_heads, int D, int max_seq, int chunk_len,
+                                         int chunks, void *out, int out_bf16) {
+  pdl_enter();
+  extern __shared__ float wsm[];  // [chunks]
+  __shared__ float red[32];
+  const int item = blockIdx.x, b = item / q_heads, h = item % q_heads;
+  const int limit = min(positions[b], max_seq - 1) + 1;
+  const int used = (limit + chunk_len - 1) / chunk_len;
+  const float *pp = part + (size_t)item * chunks * (D + 2);
+  float m = -INFINITY;
+  for (int c = threadIdx.x; c < used; c += blockDim.x) m = fmaxf(m, pp[(size_t)c * (D + 2) + D]);
+  m = -block_min(-m, red);
+  float l = 0.0f;
+  for (int c = threadIdx.x; c < used; c += blockDim.x) {
+    const float wc = expf(pp[(size_t)c * (D + 2) + D] - m);
+    wsm[c] = wc;
+    l += pp[(size_t)c * (D + 2) + D + 1] * wc;
+  }
+  const float inv_l = 1.0f / block_sum(l, red);  // its barriers also publish wsm
+  const float *gate = q_gate + (size_t)b * qg_pitch + (size_t)h * 2 * D + D;
+  for (int j = threadIdx.x; j < D; j += blockDim.x) {
+    float num = 0.0f;
+    for (int c = 0; c < used; ++c) num = fmaf(pp[(size_t)c * (D + 2) + j], wsm[c], num);
+    store_f(out, out_bf16, (size_t)b * q_heads * D + (size_t)h * D + j, num * inv_l * sigmoidf_(gate[j]));
+  }
+}
+
 // Merges the chunks of each (b, q head) and applies the output gate
 // out = attn * sigmoid(gate) (attention.rs:170-190); one warp per (b, head).
 __global__ void attn_decode_combine_kernel(const float *part, const float *q_gate, long long qg_pitch,
@@ -265,16 +469,21 @@ __global__ void gdn_conv_kernel(const float *x, long long x_pitch, float *state,
   st[kernel - 2] = cur;
 }
 
-// The delta rule for one token (gdn.rs:206-263).  Block (b, value head),
-// thread j = value column: memory_j = decay * sum_i S[i][j] k_i, delta_j =
-// (v_j - memory_j) * beta, S[i][j] = S[i][j] * decay + k_i delta_j, out_j =
-// sum_i S[i][j] q_i, with q, k L2-normalised (q also by 1/sqrt(dk)).
+// The delta rule for one token (gdn.rs:206-263): memory_j = decay * sum_i
+// S[i][j] k_i, delta_j = (v_j - memory_j) * beta, S[i][j] = S[i][j] * decay +
+// k_i delta_j, out_j = sum_i S[i][j] q_i, with q, k L2-normalised (q also by
+// 1/sqrt(dk)).  Block (b * value_heads + h, column group).  With dk = 128
+// and 64-column groups (the config's heads), 256 threads each hold 32 rows of
+// one column in registers: the state is read once and written once, and the
+// four row groups' partial sums meet in shared memory (fixed order).  Other
+// shapes: one thread per column, two passes over the state.
+constexpr int kDeltaRows = 32, kDeltaRowGroups = 4, kDeltaCols = 64, kDeltaThreads = 256;
 __global__ void gdn_delta_kernel(const float *conv_out, int conv_dim, const float *a, const float *bgate,
                                  long long ab_pitch, const float *a_log, const float *dt_bias, float *state,
                                  int batch, int key_heads, int value_heads, int dk, int dv, float eps,
                                  float inv_sqrt_dk, float *out) {
   pdl_enter();
-  extern __shared__ float sh[];  // q[dk], k[dk], reduction scratch
+  extern __shared__ float sh[];  // q[dk], k[dk], reduction scratch [2 * warps], partial sums
   float *qs = sh, *ks = sh + dk, *red = sh + 2 * dk;
   const int b = blockIdx.x / value_heads, h = blockIdx.x % value_heads;
   const int kh = h / (value_heads / key_heads);
@@ -312,7 +521,44 @@ __global__ void gdn_delta_kernel(const float *conv_out, int conv_dim, const floa
   const float decay = expf(-(expf(a_log[h]) * softplus));
   float *S = state + ((size_t)b * value_heads + h) * dk * dv;
   const float *v = x + 2 * key_dim + (size_t)h * dv;
-  for (int j = tid; j < dv; j += blockDim.x) {
+  if (dk == kDeltaRowGroups * kDeltaRows && dv == kDeltaCols * (int)gridDim.y && blockDim.x == kDeltaThreads) {
+    // Thread (group, column): rows [group * 32, +32) of one state column,
+    // held in registers between the two products (one read, one write).
+    float *part = red + 2 * warps;  // [2][groups][cols]
+    const int col = tid % kDeltaCols, grp = tid / kDeltaCols;
+    const int j = blockIdx.y * kDeltaCols + col, i0 = grp * kDeltaRows;
+    float sv[kDeltaRows];
+#pragma unroll
+    for (int r = 0; r < kDeltaRows; ++r) sv[r] = S[(size_t)(i0 + r) * dv + j];
+    float mem = 0.0f;
+#pragma unroll
+    for (int r = 0; r < kDeltaRows; ++r) mem = fmaf(sv[r], ks[i0 + r] * k_scale, mem);
+    part[grp * kDeltaCols + col] = mem;
+    __syncthreads();
+    mem = 0.0f;
+#pragma unroll
+    for (int g2 = 0; g2 < kDeltaRowGroups; ++g2) mem += part[g2 * kDeltaCols + col];
+    mem *= decay;
+    const float delta = (v[j] - mem) * beta;
+    float o = 0.0f;
+#pragma unroll
+    for (int r = 0; r < kDeltaRows; ++r) {
+      const float nxt = fmaf(sv[r], decay, ks[i0 + r] * k_scale * delta);
+      S[(size_t)(i0 + r) * dv + j] = nxt;
+      o = fmaf(nxt, qs[i0 + r] * q_scale, o);
+    }
+    float *part2 = part + kDeltaRowGroups * kDeltaCols;
+    part2[grp * kDeltaCols + col] = o;
+    __syncthreads();
+    if (grp == 0) {
+      o = 0.0f;
+#pragma unroll
+      for (int g2 = 0; g2 < kDeltaRowGroups; ++g2) o += part2[g2 * kDeltaCols + col];
+      out[((size_t)b * value_heads + h) * dv + j] = o;
+    }
+    return;
+  }
+  for (int j = blockIdx.y * blockDim.x + tid; j < dv; j += blockDim.x * gridDim.y) {
     float mem = 0.0f;
     for (int i = 0; i < dk; ++i) mem = fmaf(S[(size_t)i * dv + j], ks[i] * k_scale, mem);
     mem *= decay;
@@ -351,32 +597,84 @@ __global__ void gdn_gated_norm_kernel(const float *x, const float *z, long long 
 }
 
 // ---- decode MoE combine + residual + RMSNorm ------------------------------------------------------
-// out[t] = residual[t] + sum_s w[t, s] * routed[t * slots + s] (slots in
-// order, moe.rs:111-147); normed = RMSNorm(out) * gamma in bf16.  One block
-// per token.
-__global__ void decode_combine_add_norm_kernel(const float *routed, const float *weights, int width, int slots,
-                                               const float *residual, const float *gamma, int hidden, float inv_h,
-                                               float eps, float *out, void *normed, int normed_bf16) {
+// out[t] = residual[t] + sum_s w[t, s] * routed[row(t, s)] (slots in order,
+// moe.rs:111-147); normed = RMSNorm(out) * gamma.  row(t, s) = t * slots + s,
+// or with `map` (the distinct-expert MoE GEMV's output [cap, tokens, hidden])
+// map[t * slots + s] * tokens + t.  One block per token; the slots' rows and
+// weights are read once into registers / shared memory per column group.
+constexpr int kCombineMaxSlots = 32;
+__global__ void decode_combine_add_norm_kernel(const float *routed, const int32_t *map, const float *weights,
+                                               int width, int slots, int tokens, const float *residual,
+                                               const float *gamma, int hidden, float inv_h, float eps, float *out,
+                                               void *normed, int normed_bf16) {
   pdl_enter();
   __shared__ float red[32];
+  __shared__ float w_s[kCombineMaxSlots];
+  __shared__ const float *row_s[kCombineMaxSlots];
   const int t = blockIdx.x;
+  if (threadIdx.x < slots) {
+    const int s = threadIdx.x;
+    w_s[s] = weights[(size_t)t * width + s];
+    const long long row = map ? (long long)max(map[(size_t)t * slots + s], 0) * tokens + t : (long long)t * slots + s;
+    row_s[s] = routed + row * hidden;
+  }
+  __syncthreads();
   float ss = 0.0f;
   for (int c = threadIdx.x; c < hidden; c += blockDim.x) {
     float acc = 0.0f;
-    for (int s = 0; s < slots; ++s)
-      acc = fmaf(weights[(size_t)t * width + s], routed[((size_t)t * slots + s) * hidden + c], acc);
+    for (int s = 0; s < slots; ++s) acc = fmaf(w_s[s], row_s[s][c], acc);
     const float v = residual[(size_t)t * hidden + c] + acc;
     out[(size_t)t * hidden + c] = v;
     ss = fmaf(v, v, ss);
   }
-  ss = warp_sum(ss);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x / 32] = ss;
-  __syncthreads();
-  float tot = 0.0f;
-  for (int w = 0; w < (int)(blockDim.x / 32); ++w) tot += red[w];
-  const float scale = __frsqrt_rn(fmaf(tot, inv_h, eps));
+  const float scale = __frsqrt_rn(fmaf(block_sum(ss, red), inv_h, eps));
   for (int c = threadIdx.x; c < hidden; c += blockDim.x)
     store_f(normed, normed_bf16, (size_t)t * hidden + c, out[(size_t)t * hidden + c] * scale * gamma[c]);
+}
+
+// The same over a cluster per token (see rms_norm_cluster_kernel).
+__global__ void __launch_bounds__(kClusterThreads) decode_combine_add_norm_cluster_kernel(
+    const float *routed, const int32_t *map, const float *weights, int width, int slots, int tokens,
+    const float *residual, const float *gamma, int hidden, float inv_h, float eps, float *out, void *normed,
+    int normed_bf16) {
+  pdl_enter();
+  __shared__ float red[32];
+  __shared__ float slot;
+  __shared__ float w_s[kCombineMaxSlots];
+  __shared__ const float *row_s[kCombineMaxSlots];
+  const int t = blockIdx.y;
+  if (threadIdx.x < slots) {
+    const int s = threadIdx.x;
+    w_s[s] = weights[(size_t)t * width + s];
+    const long long row = map ? (long long)max(map[(size_t)t * slots + s], 0) * tokens + t : (long long)t * slots + s;
+    row_s[s] = routed + row * hidden;
+  }
+  __syncthreads();
+  const int n = (int)cluster_nctarank(), per = (hidden + n - 1) / n;
+  const int c0 = (int)cluster_ctarank() * per, c1 = min(hidden, c0 + per);
+  float v[kClusterVals];
+  float ss = 0.0f;
+#pragma unroll
+  for (int k = 0; k < kClusterVals; ++k) {
+    const int c = c0 + threadIdx.x + k * kClusterThreads;
+    float e = 0.0f;
+    if (c < c1) {
+      float acc = 0.0f;
+      for (int s = 0; s < slots; ++s) acc = fmaf(w_s[s], row_s[s][c], acc);
+      e = residual[(size_t)t * hidden + c] + acc;
+      out[(size_t)t * hidden + c] = e;
+    }
+    v[k] = e;
+    ss = fmaf(e, e, ss);
+  }
+  const float tot = cluster_total(block_sum(ss, red), &slot);
+  const float scale = __frsqrt_rn(fmaf(tot, inv_h, eps));
+#pragma unroll
+  for (int k = 0; k < kClusterVals; ++k) {
+    const int c = c0 + threadIdx.x + k * kClusterThreads;
+    if (c < c1) store_f(normed, normed_bf16, (size_t)t * hidden + c, v[k] * scale * gamma[c]);
+  }
+  cluster_sync();
 }
 
 // ---- greedy sampling ----------------------------------------------------------------------------------
@@ -475,12 +773,25 @@ extern "C" int fpb_rms_norm(const void *x, int x_dtype, size_t x_pitch, const fl
     return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_rms_norm: dtype");
   const float inv_w = 1.0f / (float)width;
   cudaStream_t s = as_stream(stream);
+  if (const int cl = cluster_for(width); cl > 0 && rows <= 65535) {
+    const dim3 grid((unsigned)cl, (unsigned)rows);
+    cudaError_t e = x_dtype == FPB_F32
+        ? launch_pdl_cluster(rms_norm_cluster_kernel<float>, grid, kClusterThreads, 0, s, (unsigned)cl,
+                             static_cast<const float *>(x), x_pitch, residual_delta, sum_out, (int)width, gamma,
+                             inv_w, eps, out, out_dtype == FPB_BF16, out_pitch)
+        : launch_pdl_cluster(rms_norm_cluster_kernel<__nv_bfloat16>, grid, kClusterThreads, 0, s, (unsigned)cl,
+                             static_cast<const __nv_bfloat16 *>(x), x_pitch, residual_delta, sum_out, (int)width,
+                             gamma, inv_w, eps, out, out_dtype == FPB_BF16, out_pitch);
+    if (e != cudaSuccess) return cuda_fail(e, "rms_norm_cluster_kernel");
+    FPB_LAUNCH_CHECK("rms_norm_cluster_kernel");
+    return FPB_OK;
+  }
   if (x_dtype == FPB_F32)
-    FPB_LAUNCH(rms_norm_kernel<float>, blocks_for(rows, 8), 256, 0, s, static_cast<const float *>(x), x_pitch,
+    FPB_LAUNCH(rms_norm_kernel<float>, (unsigned)rows, 256, 0, s, static_cast<const float *>(x), x_pitch,
                residual_delta, sum_out, (int)rows, (int)width, gamma, inv_w, eps, out, out_dtype == FPB_BF16,
                out_pitch);
   else
-    FPB_LAUNCH(rms_norm_kernel<__nv_bfloat16>, blocks_for(rows, 8), 256, 0, s,
+    FPB_LAUNCH(rms_norm_kernel<__nv_bfloat16>, (unsigned)rows, 256, 0, s,
                static_cast<const __nv_bfloat16 *>(x), x_pitch, residual_delta, sum_out, (int)rows, (int)width,
                gamma, inv_w, eps, out, out_dtype == FPB_BF16, out_pitch);
   return FPB_OK;
@@ -550,6 +861,29 @@ extern "C" int fpb_attn_decode(const float *q, const float *k_cache, const float
   const int chunks = (int)((max_seq + chunk_len - 1) / chunk_len);
   cudaStream_t s = as_stream(stream);
   float *part = static_cast<float *>(workspace);
+  if (chunk_len == (size_t)kAttnTile && head_dim % 4 == 0 && chunks <= 8192) {
+    const size_t group = q_heads / kv_heads;
+    const size_t smem = (2 * kAttnTile * kAttnPitch + group * head_dim) * sizeof(float);
+    {
+      static std::mutex mu;
+      static std::vector<int> done;
+      int dev = 0;
+      cudaGetDevice(&dev);
+      std::lock_guard<std::mutex> lock(mu);
+      if (std::find(done.begin(), done.end(), dev) == done.end()) {
+        FPB_CUDA_TRY(cudaFuncSetAttribute(attn_decode_tile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)((2 * kAttnTile * kAttnPitch + 32 * kAttnMaxD) * sizeof(float))));
+        done.push_back(dev);
+      }
+    }
+    FPB_LAUNCH(attn_decode_tile_kernel, dim3((unsigned)(batch * kv_heads), (unsigned)chunks), kAttnTileThreads, smem,
+               s, q, k_cache, v_cache, positions, (int)q_heads, (int)kv_heads, (int)head_dim, (int)max_seq, chunks,
+               scale, part);
+    FPB_LAUNCH(attn_decode_merge_kernel, (unsigned)(batch * q_heads), 256, chunks * sizeof(float), s, part, q_gate,
+               (long long)qg_pitch, positions, (int)q_heads, (int)head_dim, (int)max_seq, (int)chunk_len, chunks, out,
+               out_dtype == FPB_BF16);
+    return FPB_OK;
+  }
   // Chunks past a row's position write nothing and are not read.
   FPB_LAUNCH(attn_decode_partial_kernel, dim3((unsigned)(batch * kv_heads), (unsigned)chunks),
              (unsigned)(32 * (q_heads / kv_heads)), 0, s, q, k_cache, v_cache, positions, (int)batch, (int)q_heads,
@@ -580,8 +914,11 @@ extern "C" int fpb_gdn_delta(const float *conv_out, const float *a, const float 
       batch * value_heads > 0x7fffffff)
     return fail(FPB_ERR_SHAPE, "fpb_gdn_delta: shape");
   const int conv_dim = (int)(2 * key_heads * dk + value_heads * dv);
-  FPB_LAUNCH(gdn_delta_kernel, (unsigned)(batch * value_heads), 128, (2 * dk + 16) * sizeof(float),
-             as_stream(stream), conv_out, conv_dim, a, b, (long long)ab_pitch, a_log, dt_bias, state, (int)batch,
+  const bool tiled = dk == (size_t)kDeltaRowGroups * kDeltaRows && dv % kDeltaCols == 0 && dv / kDeltaCols <= 65535;
+  const dim3 grid((unsigned)(batch * value_heads), tiled ? (unsigned)(dv / kDeltaCols) : 1u);
+  const int threads = tiled ? kDeltaThreads : 128;
+  const size_t smem = (2 * dk + 2 * (threads / 32) + (tiled ? 2 * kDeltaRowGroups * kDeltaCols : 0)) * sizeof(float);
+  FPB_LAUNCH(gdn_delta_kernel, grid, threads, smem, as_stream(stream), conv_out, conv_dim, a, b, (long long)ab_pitch, a_log, dt_bias, state, (int)batch,
              (int)key_heads, (int)value_heads, (int)dk, (int)dv, eps, 1.0f / sqrtf((float)dk), out);
   return FPB_OK;
 }
@@ -599,19 +936,44 @@ extern "C" int fpb_gdn_gated_norm(const float *x, const float *z, size_t z_pitch
   return FPB_OK;
 }
 
+static int combine_add_norm(const char *name, const float *routed, const int32_t *map, const float *weights,
+                            size_t width, size_t slots, const float *residual, const float *gamma, size_t tokens,
+                            size_t hidden, float eps, float *out, void *normed, int normed_dtype, void *stream) {
+  if (!routed || !weights || !residual || !gamma || !out || !normed)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "%s: null pointer", name);
+  if (tokens == 0 || tokens > 0x7fffffff || hidden == 0 || hidden > 0x7fffffff || slots == 0 || slots > width ||
+      slots > (size_t)kCombineMaxSlots)
+    return fail(FPB_ERR_SHAPE, "%s: shape (at most %d slots)", name, kCombineMaxSlots);
+  if (normed_dtype != FPB_F32 && normed_dtype != FPB_BF16) return fail(FPB_ERR_INVALID_ARGUMENT, "%s: dtype", name);
+  if (const int cl = cluster_for(hidden); cl > 0 && tokens <= 65535) {
+    cudaError_t e = launch_pdl_cluster(decode_combine_add_norm_cluster_kernel, dim3((unsigned)cl, (unsigned)tokens),
+                                       kClusterThreads, 0, as_stream(stream), (unsigned)cl, routed, map, weights,
+                                       (int)width, (int)slots, (int)tokens, residual, gamma, (int)hidden,
+                                       1.0f / (float)hidden, eps, out, normed, normed_dtype == FPB_BF16);
+    if (e != cudaSuccess) return cuda_fail(e, "decode_combine_add_norm_cluster_kernel");
+    FPB_LAUNCH_CHECK("decode_combine_add_norm_cluster_kernel");
+    return FPB_OK;
+  }
+  FPB_LAUNCH(decode_combine_add_norm_kernel, (unsigned)tokens, 256, 0, as_stream(stream), routed, map, weights,
+             (int)width, (int)slots, (int)tokens, residual, gamma, (int)hidden, 1.0f / (float)hidden, eps, out, normed,
+             normed_dtype == FPB_BF16);
+  return FPB_OK;
+}
+
 extern "C" int fpb_decode_combine_add_norm(const float *routed, const float *weights, size_t width, size_t slots,
                                            const float *residual, const float *gamma, size_t tokens, size_t hidden,
                                            float eps, float *out, void *normed, int normed_dtype, void *stream) {
-  if (!routed || !weights || !residual || !gamma || !out || !normed)
-    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_decode_combine_add_norm: null pointer");
-  if (tokens == 0 || tokens > 0x7fffffff || hidden == 0 || slots == 0 || slots > width)
-    return fail(FPB_ERR_SHAPE, "fpb_decode_combine_add_norm: shape");
-  if (normed_dtype != FPB_F32 && normed_dtype != FPB_BF16)
-    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_decode_combine_add_norm: dtype");
-  FPB_LAUNCH(decode_combine_add_norm_kernel, (unsigned)tokens, 256, 0, as_stream(stream), routed, weights, (int)width,
-             (int)slots, residual, gamma, (int)hidden, 1.0f / (float)hidden, eps, out, normed,
-             normed_dtype == FPB_BF16);
-  return FPB_OK;
+  return combine_add_norm("fpb_decode_combine_add_norm", routed, nullptr, weights, width, slots, residual, gamma,
+                          tokens, hidden, eps, out, normed, normed_dtype, stream);
+}
+
+extern "C" int fpb_moe_decode_combine_add_norm(const float *routed, const int32_t *map, const float *weights,
+                                               size_t width, size_t slots, const float *residual, const float *gamma,
+                                               size_t tokens, size_t hidden, float eps, float *out, void *normed,
+                                               int normed_dtype, void *stream) {
+  if (!map) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_moe_decode_combine_add_norm: null map");
+  return combine_add_norm("fpb_moe_decode_combine_add_norm", routed, map, weights, width, slots, residual, gamma,
+                          tokens, hidden, eps, out, normed, normed_dtype, stream);
 }
 
 extern "C" int fpb_argmax_advance(const float *logits, size_t rows, size_t vocab, int32_t *tokens,

@@ -671,6 +671,79 @@ static void launch_rows_encode(const Rows &src, size_t rows, const int32_t *vali
   launch_pdl(rows_encode_kernel<Rows>, row_grid(rows), 256, 0, s, src, rows, valid, skip, cols, amax, packed, sf_tiled, global_out);
 }
 
+// ---- decode: distinct experts of a batch's routes ------------------------------------------------
+// For a decode batch (a few tokens) the MoE GEMVs run over the distinct
+// experts the routes name, each expert's weights read once for every token:
+// experts[0, count) are those ids in ascending order (-1 up to cap) and
+// map[t * slots + s] is the index of ids[t, s] among them.  One CTA: a
+// shared-memory bitmap of the experts, popcount prefix sums over its words.
+// Device error 107 (and map -1) for an id outside [0, experts).
+constexpr int kPlanThreads = 256;
+__global__ void __launch_bounds__(kPlanThreads) moe_decode_plan_kernel(const int32_t *ids, int tokens, int width,
+                                                                       int slots, int n_experts, int cap,
+                                                                       int32_t *experts, int32_t *count,
+                                                                       int32_t *map, int *error) {
+  pdl_enter();
+  extern __shared__ uint32_t plan_sm[];
+  __shared__ int wsum[kPlanThreads / 32];
+  const int words = (n_experts + 31) / 32;
+  uint32_t *bits = plan_sm, *base = plan_sm + words;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int w = tid; w < words; w += kPlanThreads) bits[w] = 0;
+  __syncthreads();
+  const int n = tokens * slots;
+  for (int i = tid; i < n; i += kPlanThreads) {
+    const int e = ids[(size_t)(i / slots) * width + i % slots];
+    if (e >= 0 && e < n_experts)
+      atomicOr(&bits[e >> 5], 1u << (e & 31));
+    else if (error)
+      atomicCAS(error, 0, 107);
+  }
+  __syncthreads();
+  // exclusive prefix of the words' popcounts: contiguous words per thread
+  const int per = (words + kPlanThreads - 1) / kPlanThreads;
+  const int w0 = min(words, tid * per), w1 = min(words, w0 + per);
+  int local = 0;
+  for (int w = w0; w < w1; ++w) local += __popc(bits[w]);
+  int incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) wsum[warp] = incl;
+  __syncthreads();
+  int before = 0, total = 0;
+  for (int w = 0; w < kPlanThreads / 32; ++w) {
+    before += w < warp ? wsum[w] : 0;
+    total += wsum[w];
+  }
+  int run = before + incl - local;
+  for (int w = w0; w < w1; ++w) {
+    base[w] = run;
+    run += __popc(bits[w]);
+  }
+  __syncthreads();
+  for (int w = tid; w < words; w += kPlanThreads) {
+    uint32_t b = bits[w];
+    int idx = base[w];
+    while (b) {
+      const int bit = __ffs(b) - 1;
+      b &= b - 1;
+      if (idx < cap) experts[idx] = w * 32 + bit;
+      ++idx;
+    }
+  }
+  for (int i = total + tid; i < cap; i += kPlanThreads) experts[i] = -1;
+  if (tid == 0) *count = min(total, cap);
+  for (int i = tid; i < n; i += kPlanThreads) {
+    const int e = ids[(size_t)(i / slots) * width + i % slots];
+    int m = -1;
+    if (e >= 0 && e < n_experts) m = (int)base[e >> 5] + __popc(bits[e >> 5] & ((1u << (e & 31)) - 1u));
+    map[i] = m < cap ? m : -1;
+  }
+}
+
 }  // namespace fpb
 
 // ---- host side -------------------------------------------------------------------------
@@ -1049,4 +1122,20 @@ extern "C" int fpb_swiglu_amax(const void *gate_up, int dtype, size_t rows, cons
     FPB_LAUNCH_CHECK("rows_amax_kernel(swiglu)");
     return (int)FPB_OK;
   });
+}
+
+extern "C" int fpb_moe_decode_plan(const int32_t *ids, size_t tokens, size_t width, size_t slots, size_t experts,
+                                   int32_t *distinct, int32_t *count, size_t cap, int32_t *map, void *stream) {
+  if (!ids || !distinct || !count || !map) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_moe_decode_plan: null pointer");
+  if (tokens == 0 || slots == 0 || slots > width || experts == 0 || experts > 65536 || tokens * slots > 0x7fffffff ||
+      cap < tokens * slots || cap > 0x7fffffff)
+    return fail(FPB_ERR_SHAPE, "fpb_moe_decode_plan: tokens %zu slots %zu width %zu experts %zu cap %zu", tokens,
+                slots, width, experts, cap);
+  const size_t words = (experts + 31) / 32;
+  cudaError_t e = launch_pdl(moe_decode_plan_kernel, 1, kPlanThreads, 2 * words * sizeof(uint32_t), as_stream(stream),
+                             ids, (int)tokens, (int)width, (int)slots, (int)experts, (int)cap, distinct, count, map,
+                             device_error_ptr());
+  if (e != cudaSuccess) return cuda_fail(e, "moe_decode_plan_kernel");
+  FPB_LAUNCH_CHECK("moe_decode_plan_kernel");
+  return FPB_OK;
 }

@@ -206,15 +206,25 @@ class Decoder:
         self.vp = torch.zeros(B, c.kv_heads * c.head_dim, **f32)
         self.q_rot = torch.zeros(B, c.q_heads, c.head_dim, **f32)
         self.attn = torch.zeros(B, c.q_heads * c.head_dim, **bf)
-        self.attn_ws = torch.empty(int(N.lib.fpb_attn_decode_workspace_bytes(B, c.q_heads, c.head_dim, max_seq, 64)),
+        self.attn_ws = torch.empty(int(N.lib.fpb_attn_decode_workspace_bytes(B, c.q_heads, c.head_dim, max_seq, 32)),
                                    dtype=torch.uint8, device=dev)
         self.logits_r = torch.zeros(B, c.experts, **f32)
         self.gate = torch.zeros(B, **f32)
         self.ids = torch.zeros(B, c.slots, **i32)
         self.wts = torch.zeros(B, c.slots, **f32)
-        self.gu = torch.zeros(B * c.slots, 2 * c.moe_inter, **f32)
-        self.act = torch.zeros(B * c.slots, c.moe_inter, **bf)
-        self.routed = torch.zeros(B * c.slots, h, **f32)
+        # Up to 16 sessions the MoE runs over the step's distinct experts
+        # (each expert's weights read once for every session); [cap, B, ...]
+        # buffers, cap = B * slots.  Larger batches run per (session, slot).
+        self.distinct_moe = B <= 16
+        cap = B * c.slots
+        self.cap = cap
+        self.distinct = torch.zeros(cap, **i32)
+        self.n_distinct = torch.zeros(1, **i32)
+        self.route_map = torch.zeros(B * c.slots, **i32)
+        rows = cap * B if self.distinct_moe else B * c.slots
+        self.gu = torch.zeros(rows, 2 * c.moe_inter, **f32)
+        self.act = torch.zeros(rows, c.moe_inter, **bf)
+        self.routed = torch.zeros(rows, h, **f32)
         self.logits = torch.zeros(B, c.vocab, **f32)
         self.kv = {}
         self.gdn = {}
@@ -227,6 +237,7 @@ class Decoder:
                                torch.zeros(B, c.value_heads, c.key_head_dim, c.value_head_dim, **f32))
         self._batched = {}
         self.graph = None
+        self.route_log = None  # [layers, batch, slots] int32 when recording routes
 
     def _gemv(self, key, members, x, sh):
         """One batched NVFP4 GEMV launch of [(weight, y)] sharing input x."""
@@ -270,7 +281,7 @@ class Decoder:
                        self.positions.data_ptr(), B, c.q_heads, c.kv_heads, c.head_dim, c.rotary_dim, c.rope_theta, eps,
                        self.max_seq, self.q_rot.data_ptr(), kc.data_ptr(), vc.data_ptr(), sh)
                 N.call("fpb_attn_decode", self.q_rot.data_ptr(), kc.data_ptr(), vc.data_ptr(), self.positions.data_ptr(),
-                       self.qg.data_ptr(), self.qg.shape[1], B, c.q_heads, c.kv_heads, c.head_dim, self.max_seq, 64,
+                       self.qg.data_ptr(), self.qg.shape[1], B, c.q_heads, c.kv_heads, c.head_dim, self.max_seq, 32,
                        1.0 / math.sqrt(c.head_dim), self.attn_ws.data_ptr(), self.attn_ws.numel(),
                        self.attn.data_ptr(), BF, sh)
                 self._gemv(("attn_out", i), [(L["w_o"], self.delta)], self.attn, sh)
@@ -283,15 +294,31 @@ class Decoder:
                        sh)
             N.call("fpb_moe_topk", self.logits_r.data_ptr(), c.experts, self.gate.data_ptr(), B, c.experts, c.top_k,
                    c.slots, self.ids.data_ptr(), self.wts.data_ptr(), sh)
-            N.call("fpb_nvfp4_expert_gemv_tokens", L["w_gate_up"].handle, self.normed.data_ptr(), BF,
-                   self.ids.data_ptr(), B, c.slots, 2 * c.moe_inter, self.gu.data_ptr(), F32, sh)
-            N.call("fpb_swiglu", self.gu.data_ptr(), F32, B * c.slots, c.moe_inter, self.act.data_ptr(), BF, sh)
-            N.call("fpb_nvfp4_expert_gemv", L["w_down"].handle, self.act.data_ptr(), BF, self.ids.data_ptr(),
-                   B * c.slots, h, 1, self.routed.data_ptr(), F32, sh)
+            if self.route_log is not None:
+                self.route_log[i].copy_(self.ids)
             nxt = m.layers[i + 1]["input_norm"] if i + 1 < len(m.layers) else m.final_norm
-            N.call("fpb_decode_combine_add_norm", self.routed.data_ptr(), self.wts.data_ptr(), c.slots, c.slots,
-                   self.resid[cur].data_ptr(), nxt.data_ptr(), B, h, eps, self.resid[1 - cur].data_ptr(),
-                   self.normed.data_ptr(), BF, sh)
+            if self.distinct_moe:
+                cap = self.cap
+                N.call("fpb_moe_decode_plan", self.ids.data_ptr(), B, c.slots, c.slots, c.experts + 1,
+                       self.distinct.data_ptr(), self.n_distinct.data_ptr(), cap, self.route_map.data_ptr(), sh)
+                N.call("fpb_nvfp4_moe_gemv", L["w_gate_up"].handle, 2 * c.moe_inter, self.distinct.data_ptr(),
+                       self.n_distinct.data_ptr(), cap, self.normed.data_ptr(), BF, 0, B, self.gu.data_ptr(), F32, sh)
+                N.call("fpb_swiglu", self.gu.data_ptr(), F32, cap * B, c.moe_inter, self.act.data_ptr(), BF, sh)
+                N.call("fpb_nvfp4_moe_gemv", L["w_down"].handle, h, self.distinct.data_ptr(),
+                       self.n_distinct.data_ptr(), cap, self.act.data_ptr(), BF, B * c.moe_inter, B,
+                       self.routed.data_ptr(), F32, sh)
+                N.call("fpb_moe_decode_combine_add_norm", self.routed.data_ptr(), self.route_map.data_ptr(),
+                       self.wts.data_ptr(), c.slots, c.slots, self.resid[cur].data_ptr(), nxt.data_ptr(), B, h, eps,
+                       self.resid[1 - cur].data_ptr(), self.normed.data_ptr(), BF, sh)
+            else:
+                N.call("fpb_nvfp4_expert_gemv_tokens", L["w_gate_up"].handle, self.normed.data_ptr(), BF,
+                       self.ids.data_ptr(), B, c.slots, 2 * c.moe_inter, self.gu.data_ptr(), F32, sh)
+                N.call("fpb_swiglu", self.gu.data_ptr(), F32, B * c.slots, c.moe_inter, self.act.data_ptr(), BF, sh)
+                N.call("fpb_nvfp4_expert_gemv", L["w_down"].handle, self.act.data_ptr(), BF, self.ids.data_ptr(),
+                       B * c.slots, h, 1, self.routed.data_ptr(), F32, sh)
+                N.call("fpb_decode_combine_add_norm", self.routed.data_ptr(), self.wts.data_ptr(), c.slots, c.slots,
+                       self.resid[cur].data_ptr(), nxt.data_ptr(), B, h, eps, self.resid[1 - cur].data_ptr(),
+                       self.normed.data_ptr(), BF, sh)
             cur = 1 - cur
         self._gemv(("lm_head",), [(m.lm_head, self.logits)], self.normed, sh)
         N.call("fpb_argmax_advance", self.logits.data_ptr(), B, c.vocab, self.tokens.data_ptr(),

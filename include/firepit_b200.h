@@ -533,7 +533,7 @@ int fpb_gdn_gated_norm(const float *x, const float *z, size_t z_pitch, const flo
                        size_t dv, float eps, void *out, int out_dtype, void *stream);
 /* combine_add_norm_view (moe.rs:111-147) for decode: out[t] = residual[t] +
  * sum over slots s of weights[t, s] * routed[t * slots + s], normed =
- * RMSNorm(out) * gamma (f32 or bf16). */
+ * RMSNorm(out) * gamma (f32 or bf16); slots <= 32. */
 int fpb_decode_combine_add_norm(const float *routed, const float *weights, size_t width, size_t slots,
                                 const float *residual, const float *gamma, size_t tokens, size_t hidden, float eps,
                                 float *out, void *normed, int normed_dtype, void *stream);
@@ -551,6 +551,33 @@ int fpb_argmax_advance(const float *logits, size_t rows, size_t vocab, int32_t *
 int fpb_nvfp4_expert_gemv_tokens(const fpb_nvfp4_matrix *w, const void *x, int x_dtype, const int32_t *expert_ids,
                                  int tokens, int slots_per_token, size_t rows_per_expert, void *y, int y_dtype,
                                  void *stream);
+/* The decode MoE over distinct experts instead of (token, slot) pairs (no
+ * reference counterpart: the reference runs expert_gemv_weight_view per
+ * slot, gemv/mod.rs:137-206, reading a routed expert once per token).
+ * fpb_moe_decode_plan: distinct[0, *count) = the distinct ids of ids
+ * [tokens, width] (first `slots` of each row) in ascending order, -1 up to
+ * cap (cap >= tokens * slots); map[t * slots + s] = index of ids[t, s] in
+ * distinct.  Device error 107 (map -1) for an id outside [0, experts).
+ * fpb_nvfp4_moe_gemv: for u < *count (device), y[u] [tokens, rows_per_expert]
+ * (at y + u * tokens * rows_per_expert) = W[distinct[u]] x[u], x[u] =
+ * [tokens, cols] at x + u * x_stride elements (x_stride 0: one x for all);
+ * tokens <= 16.  K % 128 == 0, K <= 4096, tokens <= 8: one streaming launch
+ * whose CTAs share the live rows (device error 203 on an id outside the
+ * experts); other shapes: the register kernel over all cap slots (rows of
+ * slots past the count are zero).  Each token's result equals the per-slot
+ * expert GEMV's up to f32 summation order.
+ * fpb_moe_decode_combine_add_norm: fpb_decode_combine_add_norm reading the
+ * routed row of (t, s) at map[t * slots + s] * tokens + t of routed
+ * [cap, tokens, hidden] (the moe GEMV's output layout); slots <= 32. */
+int fpb_moe_decode_plan(const int32_t *ids, size_t tokens, size_t width, size_t slots, size_t experts,
+                        int32_t *distinct, int32_t *count, size_t cap, int32_t *map, void *stream);
+int fpb_nvfp4_moe_gemv(const fpb_nvfp4_matrix *w, size_t rows_per_expert, const int32_t *distinct,
+                       const int32_t *count, int cap, const void *x, int x_dtype, size_t x_stride, int tokens, void *y,
+                       int y_dtype, void *stream);
+int fpb_moe_decode_combine_add_norm(const float *routed, const int32_t *map, const float *weights, size_t width,
+                                    size_t slots, const float *residual, const float *gamma, size_t tokens,
+                                    size_t hidden, float eps, float *out, void *normed, int normed_dtype,
+                                    void *stream);
 
 /* ---- collectives (NCCL) ------------------------------------------------------
  * The reference runs on one GPU and has no collectives.  These are the

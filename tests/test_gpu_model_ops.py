@@ -59,9 +59,47 @@ def test_embedding_and_norms(F, torch):
     assert np.allclose(nb.float().cpu().numpy(), ref_b, rtol=8e-3, atol=1e-6)  # bf16 output
 
 
-def test_attention_prepare_and_decode(F, torch):
+@pytest.mark.parametrize("h", [2048, 5000, 10000])
+@pytest.mark.parametrize("rows", [1, 8])
+def test_norm_widths(F, torch, h, rows):
+    """Rows spread over a thread-block cluster (up to 8 CTAs, 2048 and 5000
+    columns) and the one-CTA-per-row kernels (10000 columns)."""
     N = F._native
-    B, hq, hkv, D, rot, max_seq, theta = 3, 16, 2, 256, 64, 300, 1e7
+    x = _rand(torch, rows, h, seed=h)
+    delta = _rand(torch, rows, h, seed=h + 1)
+    gamma = _rand(torch, h, seed=h + 2, scale=0.1) + 1.0
+    s = torch.empty(rows, h, device="cuda")
+    nf = torch.empty(rows, h, device="cuda")
+    N.call("fpb_rms_norm", x.data_ptr(), N.FPB_F32, h, delta.data_ptr(), s.data_ptr(), rows, h, gamma.data_ptr(),
+           1e-6, nf.data_ptr(), N.FPB_F32, h, None)
+    xb = x.to(torch.bfloat16)
+    nb = torch.empty(rows, h, device="cuda")
+    N.call("fpb_rms_norm", xb.data_ptr(), N.FPB_BF16, h, None, None, rows, h, gamma.data_ptr(), 1e-6, nb.data_ptr(),
+           N.FPB_F32, h, None)
+    slots = 11
+    routed = _rand(torch, rows * slots, h, seed=h + 3)
+    wts = torch.rand(rows, slots, device="cuda")
+    out = torch.empty(rows, h, device="cuda")
+    normed = torch.empty(rows, h, device="cuda")
+    N.call("fpb_decode_combine_add_norm", routed.data_ptr(), wts.data_ptr(), slots, slots, x.data_ptr(),
+           gamma.data_ptr(), rows, h, 1e-6, out.data_ptr(), normed.data_ptr(), N.FPB_F32, None)
+    torch.cuda.synchronize()
+    g = gamma.cpu().numpy()
+    xs = x.cpu().numpy() + delta.cpu().numpy()
+    assert np.array_equal(s.cpu().numpy(), xs)
+    assert np.allclose(nf.cpu().numpy(), R.rms_norm(xs, g, 1e-6), rtol=1e-5, atol=1e-6)
+    assert np.allclose(nb.cpu().numpy(), R.rms_norm(xb.float().cpu().numpy(), g, 1e-6), rtol=1e-5, atol=1e-6)
+    ref = x.cpu().numpy() + np.einsum("ts,tsh->th", wts.cpu().numpy(), routed.cpu().numpy().reshape(rows, slots, h))
+    assert np.allclose(out.cpu().numpy(), ref, rtol=1e-5, atol=1e-5)
+    assert np.allclose(normed.cpu().numpy(), R.rms_norm(out.cpu().numpy(), g, 1e-6), rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("chunk,hq,hkv,D", [(64, 16, 2, 256), (32, 16, 2, 256), (32, 8, 1, 128), (32, 32, 1, 64)])
+def test_attention_prepare_and_decode(F, torch, chunk, hq, hkv, D):
+    """chunk 32: shared-memory tiles and the per-head merge; 64: one warp per
+    query head streaming positions."""
+    N = F._native
+    B, rot, max_seq, theta = 3, 64, 300, 1e7
     positions = torch.tensor([0, 157, 299], dtype=torch.int32, device="cuda")
     kc = torch.zeros(B, max_seq, hkv, D, device="cuda")
     vc = torch.zeros(B, max_seq, hkv, D, device="cuda")
@@ -76,12 +114,12 @@ def test_attention_prepare_and_decode(F, torch):
     N.call("fpb_attn_prepare", qg.data_ptr(), qg.shape[1], k.data_ptr(), k.shape[1], v.data_ptr(), v.shape[1],
            qn.data_ptr(), kn.data_ptr(), positions.data_ptr(), B, hq, hkv, D, rot, theta, 1e-6, max_seq,
            q_rot.data_ptr(), kc.data_ptr(), vc.data_ptr(), None)
-    ws = torch.empty(int(N.lib.fpb_attn_decode_workspace_bytes(B, hq, D, max_seq, 64)), dtype=torch.uint8,
+    ws = torch.empty(int(N.lib.fpb_attn_decode_workspace_bytes(B, hq, D, max_seq, chunk)), dtype=torch.uint8,
                      device="cuda")
     out = torch.empty(B, hq * D, device="cuda")
     scale = 1.0 / math.sqrt(D)
     N.call("fpb_attn_decode", q_rot.data_ptr(), kc.data_ptr(), vc.data_ptr(), positions.data_ptr(), qg.data_ptr(),
-           qg.shape[1], B, hq, hkv, D, max_seq, 64, scale, ws.data_ptr(), ws.numel(), out.data_ptr(), N.FPB_F32,
+           qg.shape[1], B, hq, hkv, D, max_seq, chunk, scale, ws.data_ptr(), ws.numel(), out.data_ptr(), N.FPB_F32,
            None)
     torch.cuda.synchronize()
     assert F.device_error() == 0

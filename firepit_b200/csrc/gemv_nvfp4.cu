@@ -538,16 +538,21 @@ __device__ __forceinline__ bool next_unit(const StreamArgs<NSEG> &a, UnitIter &i
   return true;
 }
 
+// Expert ids of device-indirect segments held in shared memory (the refill
+// of a stage is on the warps' critical path; a global load there cost a
+// round trip per unit).
+constexpr int kMoeIdsShared = 1024;
+
 // Issues (one warp) the copies of one unit of `u.nrows` rows (a multiple of
 // 4, at most UR) into `stage`.
 template <int UR, bool MOE, int NSEG>
 __device__ __forceinline__ void stream_issue(const StreamArgs<NSEG> &a, uint8_t *stage, uint64_t *bar,
-                                             const Unit &u, int lane) {
+                                             const Unit &u, int lane, const int *ids_shared) {
   const uint32_t kb2 = (uint32_t)a.K >> 1, kb16 = (uint32_t)a.K >> 4;
   const uint8_t *packed, *scales;
   const float *globals;
   if (MOE) {
-    int e = a.moe.ids[u.seg];
+    int e = u.seg < kMoeIdsShared ? ids_shared[u.seg] : a.moe.ids[u.seg];
     if (e < 0 || e >= a.moe.n_experts) {  // a bad id reads expert 0 and is recorded
       if (lane == 0 && a.error) atomicCAS(a.error, 0, 203);
       e = 0;
@@ -605,12 +610,15 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 2)
   const int g = lane >> 2, q = lane & 3;
   if (blockDim.x != W * 32) return;  // the layout below assumes W warps
   long long total = a.total_rows, rpc = a.rpc;
+  __shared__ int ids_shared[MOE ? kMoeIdsShared : 1];
   if (MOE) {
     asm volatile("griddepcontrol.launch_dependents;");
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const int live = min(max(*a.moe.count, 0), a.moe.cap);
     total = (long long)live * a.moe.rpe;
     rpc = ((total + gridDim.x - 1) / gridDim.x + 15) / 16 * 16;
+    for (int i = tid; i < min(live, kMoeIdsShared); i += blockDim.x) ids_shared[i] = a.moe.ids[i];
+    __syncthreads();
   }
   const long long v_lo = (long long)blockIdx.x * rpc;
   const long long v_hi = min(total, v_lo + rpc);
@@ -641,7 +649,7 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 2)
   for (int s = 0; s < S; ++s) {
     Unit u;
     if (!next_unit<UR, MOE>(a, it_a, v_hi, u)) break;
-    if (warp == 0) stream_issue<UR, MOE>(a, stages + (size_t)s * a.stage_bytes, &full[s], u, lane);
+    if (warp == 0) stream_issue<UR, MOE>(a, stages + (size_t)s * a.stage_bytes, &full[s], u, lane, ids_shared);
   }
   if (!MOE) {
     asm volatile("griddepcontrol.launch_dependents;");
@@ -888,7 +896,7 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 2)
     if (has_ahead) {
       __syncwarp();
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      stream_issue<UR, MOE>(a, st, &full[s], ahead, lane);
+      stream_issue<UR, MOE>(a, st, &full[s], ahead, lane, ids_shared);
     }
   }
 }

@@ -538,6 +538,9 @@ __device__ __forceinline__ bool next_unit(const StreamArgs<NSEG> &a, UnitIter &i
   return true;
 }
 
+// Smallest piece a unit's contiguous code copy is split into.
+constexpr uint32_t kCopyPiece = 16384;
+
 // Expert ids of device-indirect segments held in shared memory (the refill
 // of a stage is on the warps' critical path; a global load there cost a
 // round trip per unit).
@@ -571,7 +574,16 @@ __device__ __forceinline__ void stream_issue(const StreamArgs<NSEG> &a, uint8_t 
   if (lane == 0) sm100::mbar_arrive_expect_tx(bar, (uint32_t)nrows * (kb2 + kb16 + 4));
   __syncwarp();
   if (a.contig) {
-    if (lane == 0) sm100::bulk_load(stage, packed + (size_t)row0 * kb2, (uint32_t)nrows * kb2, bar);
+    // a few row-aligned pieces of at least kCopyPiece bytes, issued by
+    // different lanes: few copies a row, but more than one in flight
+    const int pieces = max(1, min(8, (int)((uint32_t)nrows * kb2 / kCopyPiece)));
+    const int rpp = (nrows + pieces - 1) / pieces;
+    if (lane < pieces) {
+      const int r0 = lane * rpp, r1 = min(nrows, r0 + rpp);
+      if (r1 > r0)
+        sm100::bulk_load(stage + (size_t)r0 * kb2, packed + (size_t)(row0 + r0) * kb2, (uint32_t)(r1 - r0) * kb2,
+                         bar);
+    }
   } else {
     for (int r = lane; r < nrows; r += 32)
       sm100::bulk_load(stage + r * a.wpitch, packed + (size_t)(row0 + r) * kb2, kb2, bar);

@@ -163,6 +163,13 @@ SIGNATURES: dict[str, tuple] = {
     "fpb_argmax_advance": (i32, [vp, sz, sz, vp, vp, vp, sz, vp, vp]),
     "fpb_nvfp4_expert_gemv_tokens": (i32, [vp, vp, i32, vp, i32, i32, sz, vp, i32, vp]),
     "fpb_moe_decode_plan": (i32, [vp, sz, sz, sz, sz, vp, vp, sz, vp, vp]),
+    "fpb_nvfp4_gemv_planes_workspace_bytes": (sz, [sz, sz]),
+    "fpb_nvfp4_gemv_planes": (i32, [vp, sz, sz, vp, i32, i32, vp, i32, vp, sz, vp]),
+    "fpb_nvfp4_moe_gemv_planes": (i32, [vp, sz, vp, vp, i32, vp, i32, sz, i32, vp, i32, vp, sz, vp]),
+    "fpb_nvfp4_moe_gemv_planes_glu": (i32, [vp, sz, vp, vp, i32, vp, sz, i32, vp, i32, vp, sz, vp]),
+    "fpb_gdn_step": (i32, [vp, sz, vp, vp, sz, vp, vp, sz, vp, vp, vp, vp, sz, vp, sz, sz, sz, sz, sz, C.c_float, vp,
+                           i32, vp]),
+    "fpb_moe_decode_route": (i32, [vp, sz, C.c_longlong, sz, sz, sz, sz, vp, vp, vp, vp, sz, vp, vp]),
     "fpb_nvfp4_moe_gemv": (i32, [vp, sz, vp, vp, i32, vp, i32, sz, i32, vp, i32, vp]),
     "fpb_moe_decode_combine_add_norm": (i32, [vp, vp, vp, sz, sz, vp, vp, sz, sz, C.c_float, vp, vp, i32, vp]),
     "fpb_comm_available": (i32, []),

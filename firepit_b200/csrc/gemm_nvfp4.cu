@@ -116,6 +116,84 @@ __global__ void act_encode_kernel(const T *x, size_t rows, size_t cols, const ui
   }
 }
 
+// ---- x as NVFP4 digit planes (tensor-core GEMV) ----------------------------------------
+// Row t of x (K values) becomes kPlanes NVFP4 rows: plane 0 encodes x with
+// the config-0 rule (global g0 = amax / 2688, e4m3 factors per 16 values,
+// e2m1 codes), plane p encodes the residual x - (planes < p) with global
+// g0 / 4^p.  An e2m1 code is off by at most one unit (its factor times its
+// global), so a residual block never needs a factor above 4 / 6 of the
+// previous one: no factor saturates, and 8 planes reproduce x to about
+// 5e-9 of its norm.  With the globals fixed up front every 16-value group
+// runs its 8 planes independently (one thread, in registers).  Token slot j
+// of group g owns A rows g * 128 + j * kPlanes + p, their factors in the
+// tiled layout and their globals in ga[row].  GLU: x rows are f32
+// [gate (K) | up (K)] and the input is silu(gate) * up (swiglu.rs:16, in f32).
+constexpr int kPlanes = 8, kPlaneThreads = 256, kPlaneMaxK = 4096;
+template <typename T, bool GLU>
+__device__ __forceinline__ float plane_in(const T *xr, int K, int i) {
+  if (GLU) {
+    const float *f = reinterpret_cast<const float *>(xr);
+    return silu_mul(f[i], f[K + i]);
+  }
+  return act_load(xr, i);
+}
+
+template <typename T, bool GLU>
+__global__ void __launch_bounds__(kPlaneThreads) planes_encode_kernel(const T *x, long long x_group_stride,
+                                                                      int tokens, int K, const int32_t *live_groups,
+                                                                      uint8_t *packed, uint8_t *sf_tiled,
+                                                                      float *ga) {
+  pdl_enter();
+  __shared__ uint32_t red[32];
+  const int g = blockIdx.x / tokens, t = blockIdx.x % tokens;
+  if (live_groups && g >= *live_groups) return;  // a group nothing reads (uniform)
+  const T *xr = x + (long long)g * x_group_stride + (long long)t * K * (GLU ? 2 : 1);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int groups = K / kNvfp4Group;
+  uint32_t m = 0;
+  for (int i = tid; i < K; i += kPlaneThreads) m = max(m, __float_as_uint(plane_in<T, GLU>(xr, K, i)) & 0x7fffffffu);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  m = 0;
+  for (int w = 0; w < kPlaneThreads / 32; ++w) m = max(m, red[w]);
+  const float g0 = __fdiv_rn(__uint_as_float(m), 2688.0f);
+  const size_t row0 = (size_t)g * 128 + (size_t)t * kPlanes;
+  if (tid < kPlanes) ga[row0 + tid] = g0 * __uint_as_float((uint32_t)(127 - 2 * tid) << 23);  // g0 / 4^p
+  for (int q = tid; q < groups; q += kPlaneThreads) {
+    float r[kNvfp4Group];
+#pragma unroll
+    for (int i = 0; i < kNvfp4Group; ++i) r[i] = plane_in<T, GLU>(xr, K, q * kNvfp4Group + i);
+    float gp = g0;
+#pragma unroll 1
+    for (int p = 0; p < kPlanes; ++p, gp *= 0.25f) {
+      const size_t row = row0 + p;
+      uint8_t *cdst = packed + row * (K / 2) + q * (kNvfp4Group / 2);
+      uint8_t *sdst = sf_tiled + sf_tiled_row_offset(row, K) + sf_tiled_group_offset(q);
+      float bmax = 0.0f;
+#pragma unroll
+      for (int i = 0; i < kNvfp4Group; ++i) bmax = fmaxf(bmax, fabsf(r[i]));
+      const uint8_t sb = gp > 0.0f ? f32_to_e4m3(bmax * (1.0f / 6.0f) / gp) : (uint8_t)0;
+      const float unit = e4m3_to_f32(sb) * gp;
+      uint32_t lo = 0, hi = 0;
+      if (unit > 0.0f) {
+        const float inv = 1.0f / unit;
+        float qv[kNvfp4Group];
+#pragma unroll
+        for (int i = 0; i < kNvfp4Group; ++i) qv[i] = r[i] * inv;
+        lo = f32x8_to_e2m1x8(qv);
+        hi = f32x8_to_e2m1x8(qv + 8);
+#pragma unroll
+        for (int i = 0; i < kNvfp4Group; ++i)
+          r[i] -= e2m1_to_f32(((i < 8 ? lo : hi) >> (4 * (i & 7))) & 0xf) * unit;
+      }
+      *reinterpret_cast<uint2 *>(cdst) = make_uint2(lo, hi);
+      *sdst = sb;
+    }
+  }
+}
+
 }  // namespace fpb
 
 namespace fpb {
@@ -159,6 +237,25 @@ struct GemmParams {
   int f16;
   int passes;
   int a_sel[3], b_sel[3];
+  // Planes mode (the tensor-core GEMV): A row group g (128 rows) holds up to
+  // 16 tokens' 8 digit planes each (row j * 8 + p), with per-row globals
+  // a_globals[g * 128 + row]; the epilogue adds each token's 8 plane rows and
+  // stores y[g * y_group_stride + j * ldy + n] for j < tokens.  Items are
+  // (group, n tile): with moe_ids, group u < *moe_count uses expert
+  // moe_ids[u]'s rows (N = rows per expert) and A group u * a_group_step
+  // (0: one x for every expert); without, one group (a dense GEMV).
+  int planes;
+  int tokens;
+  const float *a_globals;
+  const int32_t *moe_ids;
+  const int32_t *moe_count;
+  int moe_cap;
+  int a_group_step;
+  long long y_group_stride;
+  // Rows of each A box tmap_a loads (planes: the tokens' 8 * tokens plane
+  // rows; the tile's other rows keep whatever the stage held and only feed
+  // accumulator rows nothing reads).  128 otherwise.
+  int a_box_rows;
 };
 
 constexpr int kTileBytes = kBM * kBKBytes;   // 16 KB per operand per stage
@@ -184,11 +281,33 @@ __device__ __forceinline__ void report(int *error, volatile int *abort, int code
 // Tile t of the launch: m-major over (m_tiles, n_tiles); false when it is a
 // grouped row tile past the layout's end (expert -1), which every role skips.
 // A malformed expert id records device error 106 and is skipped too.
+// Planes + MoE mode: the live count and the first kMoeIdsCached expert ids,
+// read once per CTA after the dependency wait (a global load per tile and
+// role put two dependent round trips in front of every tile's first copy).
+constexpr int kMoeIdsCached = 1024;
+struct MoeIdsCache {
+  int count;
+  int ids[kMoeIdsCached];
+};
+
 __device__ __forceinline__ bool gemm_tile(const GemmParams &p, int t, int n_tiles, int &m_tile, int &n_tile,
-                                          int &n_base) {
+                                          int &n_base, const MoeIdsCache *moe = nullptr) {
   m_tile = t / n_tiles;
   n_tile = t - m_tile * n_tiles;
   n_base = p.n_base;
+  if (p.planes && p.moe_ids) {
+    // m_tile is the group u: skipped past the live count; its expert's rows
+    const int u = m_tile;
+    if (u >= moe->count) return false;
+    const int e = u < kMoeIdsCached ? moe->ids[u] : p.moe_ids[u];
+    if (e < 0 || e >= p.n_experts) {
+      if (threadIdx.x == 0 && p.error) atomicCAS(p.error, 0, 106);
+      return false;
+    }
+    n_base = e * p.N;
+    m_tile = u * p.a_group_step;  // the A row group this item reads
+    return true;
+  }
   if (p.tile_experts) {
     const int e = p.tile_experts[m_tile];
     if (e == -1) return false;
@@ -225,7 +344,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   volatile int *abort_s = reinterpret_cast<volatile int *>(tmem_base_s + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_tiles = (p.N + kBN - 1) / kBN, m_tiles = (p.M + kBM - 1) / kBM;
+  const int n_tiles = (p.N + kBN - 1) / kBN;
+  const int m_tiles = p.planes ? (p.moe_ids ? p.moe_cap : 1) : (p.M + kBM - 1) / kBM;
   const int total = n_tiles * m_tiles;
   const int kb64_per_rb = p.kb_count * 4;
   // K blocks as the producer and the MMA issuer walk them (bf16 mode: each
@@ -260,6 +380,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // Programmatic dependent launch: the set-up above overlaps the previous
   // kernel in the stream; nothing it wrote is read before this wait.
   pdl_enter();
+  __shared__ MoeIdsCache moe_cache;
+  if (p.planes && p.moe_ids) {
+    const int live = min(max(*p.moe_count, 0), p.moe_cap);
+    for (int i = threadIdx.x; i < min(live, kMoeIdsCached); i += blockDim.x) moe_cache.ids[i] = p.moe_ids[i];
+    if (threadIdx.x == 0) moe_cache.count = live;
+    __syncthreads();
+  }
 
   if (warp == 0) {
     // ---- TMA producer ----------------------------------------------------------
@@ -268,7 +395,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       bool ok = true;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
         int m_tile, n_tile, n_base;
-        if (!gemm_tile(p, t, n_tiles, m_tile, n_tile, n_base)) continue;
+        if (!gemm_tile(p, t, n_tiles, m_tile, n_tile, n_base, &moe_cache)) continue;
         const int nb_global = n_base / 128 + n_tile;
         for (int vb = 0; vb < vblocks; ++vb, ++it) {
           const int s = it % kStages;
@@ -287,7 +414,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             continue;
           }
           const int kb = vb;
-          mbar_arrive_expect_tx(&full[s], 2 * kTileBytes + 2 * kSfStageBytes);
+          mbar_arrive_expect_tx(&full[s], (uint32_t)(p.a_box_rows * kBKBytes + kTileBytes + 2 * kSfStageBytes));
           tma_load_2d(sA + s * kTileBytes, &tmap_a, kb * kBKBytes, m_tile * kBM, &full[s]);
           if (p.glu) {
             const int row_gate = n_base + n_tile * 64;
@@ -316,7 +443,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       bool ok = true;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
         int m_tile, n_tile, n_base;
-        if (!gemm_tile(p, t, n_tiles, m_tile, n_tile, n_base)) continue;
+        if (!gemm_tile(p, t, n_tiles, m_tile, n_tile, n_base, &moe_cache)) continue;
         const uint32_t buf = lt & 1;
         if (lt >= 2 && !mbar_wait(&acc_empty[buf], ((lt >> 1) - 1) & 1, abort_s)) {
           report(p.error, abort_s, 107);
@@ -372,21 +499,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // columns ch*32 .. +31); each warp stages and stores its own boxes.
     const int qw = warp & 3, ch = (warp - 2) >> 2;
     const uint32_t lane_base = (uint32_t)(qw * 32) << 16;
-    const float ga = p.f16 ? 1.0f : __ldg(p.a_global);
+    const float ga = (p.f16 || p.planes) ? 1.0f : __ldg(p.a_global);
     uint8_t *stage = sOut + qw * kOutWarpBytes;
     uint8_t *row_s = stage + lane * 128;
     uint32_t lt = 0;
     uint32_t glu_max = 0;  // glu: this lane's max |h| bits over its live rows and tiles
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       int m_tile, n_tile, n_base;
-      if (!gemm_tile(p, t, n_tiles, m_tile, n_tile, n_base)) continue;
+      if (!gemm_tile(p, t, n_tiles, m_tile, n_tile, n_base, &moe_cache)) continue;
       const uint32_t buf = lt & 1;
       // What the tile's epilogue reads from memory besides the accumulator
       // (the rows' tokens, the weight rows' globals) is loaded before the
       // wait, so its latency hides behind the main loop.
       const int row0 = m_tile * kBM + qw * 32;
       const int n0 = n_tile * kBN;
-      const bool row_live = row0 + lane < p.M && (!p.row_tokens || p.row_tokens[row0 + lane] >= 0);
+      const bool row_live = p.planes ? qw * 32 + lane < p.tokens * 8
+                                     : row0 + lane < p.M && (!p.row_tokens || p.row_tokens[row0 + lane] >= 0);
+      const float ga_row = p.planes && row_live ? __ldg(p.a_globals + row0 + lane) : 0.0f;
       float gl[2];
       if (p.glu) {
         const int j0 = n_tile * 64;
@@ -422,6 +551,62 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
       ++lt;
+      if (p.planes) {
+        // Each token's 8 plane rows are 8 consecutive lanes.  Each value is
+        // scaled by its row's plane global, then the 8 lanes reduce-scatter
+        // (recursive halving over xor 4, 2, 1: 28 shuffles for 32 columns) so
+        // that lane p of the token holds the sums of columns p, p + 8,
+        // p + 16, p + 24, which it scales by their weight globals and stores.
+        if (qw * 32 >= p.tokens * 8) continue;  // no token in this quadrant (uniform)
+        const int token = (qw * 32 + lane) >> 3, pl = lane & 7;
+        const bool b2 = pl & 4, b1 = pl & 2, b0 = pl & 1;
+        const int item_group = t / n_tiles;  // the item's group: y block
+        const int nw = n0 + ch * 64;
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[c][j]) * ga_row;
+          // column j = 8 i + q; step 1 keeps q with bit 2 == b2
+          float w1[4][4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int ql = 0; ql < 4; ++ql) {
+              const float lo = v[8 * i + ql], hi = v[8 * i + 4 + ql];
+              w1[i][ql] = (b2 ? hi : lo) + __shfl_xor_sync(0xffffffffu, b2 ? lo : hi, 4);
+            }
+          float w2[4][2];
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int q0 = 0; q0 < 2; ++q0) {
+              const float lo = w1[i][q0], hi = w1[i][2 + q0];
+              w2[i][q0] = (b1 ? hi : lo) + __shfl_xor_sync(0xffffffffu, b1 ? lo : hi, 2);
+            }
+          float keep[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float lo = w2[i][0], hi = w2[i][1];
+            keep[i] = ((b0 ? hi : lo) + __shfl_xor_sync(0xffffffffu, b0 ? lo : hi, 1)) *
+                      __shfl_sync(0xffffffffu, gl[c], 8 * i + pl);
+          }
+          if (token < p.tokens) {
+            const long long ybase = (long long)item_group * p.y_group_stride + (long long)token * p.ldy;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int n = nw + c * 32 + i * 8 + pl;
+              if (n < p.N) {
+                if (p.y_bf16)
+                  reinterpret_cast<__nv_bfloat16 *>(p.y)[ybase + n] = __float2bfloat16_rn(keep[i]);
+                else
+                  reinterpret_cast<float *>(p.y)[ybase + n] = keep[i];
+              }
+            }
+          }
+        }
+        continue;
+      }
       if (row0 >= p.M) continue;  // the warp's rows are all past the end
       if (!__any_sync(0xffffffffu, row_live)) continue;  // nothing of these 32 rows is needed (both warps agree)
       if (p.glu) {
@@ -810,6 +995,7 @@ extern "C" int fpb_nvfp4_gemm_q(fpb_nvfp4_matrix *w, size_t row_begin, size_t ro
   int *err = nullptr;
   FPB_CUDA_TRY(cudaGetSymbolAddress(reinterpret_cast<void **>(&err), g_device_error));
   GemmParams p{};
+  p.a_box_rows = kBM;
   p.a_sf = a_sf_tiled;
   p.b_sf = w->extras->sf_tiled;
   p.a_global = a_global;
@@ -850,6 +1036,141 @@ extern "C" int fpb_nvfp4_gemm(fpb_nvfp4_matrix *w, size_t row_begin, size_t row_
   return fpb_nvfp4_gemm_q(w, row_begin, row_end, packed, sf, scalars, m, y, y_dtype, stream);
 }
 
+// ---- tensor-core GEMV: x as digit planes (fpb_nvfp4_gemv_planes, fpb_nvfp4_moe_gemv_planes)
+extern "C" size_t fpb_nvfp4_gemv_planes_workspace_bytes(size_t groups, size_t k) {
+  const size_t rows = groups * kBM;
+  return align256(rows * k / 2) + align256(sf_tiled_bytes(rows, k)) + align256(rows * sizeof(float)) + 256;
+}
+
+namespace fpb {
+// Encodes x's planes into the workspace and runs the GEMM kernel in planes
+// mode.  groups: A row groups (1, or cap with per-expert x); moe: device ids.
+static int run_planes(const char *fn, fpb_nvfp4_matrix *w, size_t n_base, size_t n_rows, const void *x, int x_dtype,
+                      bool glu, size_t x_group_stride, int tokens, size_t groups, const int32_t *moe_ids,
+                      const int32_t *moe_count, int moe_cap, int n_experts, void *y, int y_dtype,
+                      long long y_group_stride, long long ldy, void *workspace, size_t workspace_bytes,
+                      cudaStream_t s) {
+  const size_t K = w->cols;
+  if (tokens < 1 || tokens > 16) return fail(FPB_ERR_SHAPE, "%s: tokens %d not in [1, 16]", fn, tokens);
+  if (K % 256 || K > (size_t)kPlaneMaxK)
+    return fail(FPB_ERR_UNSUPPORTED, "%s: cols %zu must be a multiple of 256 and at most %d", fn, K, kPlaneMaxK);
+  if ((x_dtype != FPB_F32 && x_dtype != FPB_BF16) || (y_dtype != FPB_F32 && y_dtype != FPB_BF16))
+    return fail(FPB_ERR_INVALID_ARGUMENT, "%s: dtype", fn);
+  if (workspace_bytes < fpb_nvfp4_gemv_planes_workspace_bytes(groups, K))
+    return fail(FPB_ERR_WORKSPACE, "%s: workspace %zu < %zu bytes", fn, workspace_bytes,
+                fpb_nvfp4_gemv_planes_workspace_bytes(groups, K));
+  if (reinterpret_cast<uintptr_t>(workspace) & 255)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "%s: workspace must be 256-byte aligned", fn);
+  if (int st = require_prepared(w, fn)) return st;
+  if (int st = ensure_gemm_attr()) return st;
+  const size_t rows = groups * kBM;
+  uint8_t *ws = static_cast<uint8_t *>(workspace);
+  uint8_t *packed = ws;
+  uint8_t *sf = packed + align256(rows * K / 2);
+  float *ga = reinterpret_cast<float *>(sf + align256(sf_tiled_bytes(rows, K)));
+  const unsigned enc_grid = (unsigned)(groups * tokens);
+  const int32_t *live = moe_ids ? moe_count : nullptr;
+  cudaError_t e =
+      glu ? launch_pdl(planes_encode_kernel<float, true>, enc_grid, kPlaneThreads, 0, s, static_cast<const float *>(x),
+                       (long long)x_group_stride, tokens, (int)K, live, packed, sf, ga)
+      : x_dtype == FPB_F32
+          ? launch_pdl(planes_encode_kernel<float, false>, enc_grid, kPlaneThreads, 0, s,
+                       static_cast<const float *>(x), (long long)x_group_stride, tokens, (int)K, live, packed, sf, ga)
+          : launch_pdl(planes_encode_kernel<uint16_t, false>, enc_grid, kPlaneThreads, 0, s,
+                       static_cast<const uint16_t *>(x), (long long)x_group_stride, tokens, (int)K, live, packed, sf,
+                       ga);
+  if (e != cudaSuccess) return cuda_fail(e, "planes_encode_kernel");
+  FPB_LAUNCH_CHECK("planes_encode_kernel");
+  CUtensorMap tmap_a;
+  if (int st = encode_rows_u8(&tmap_a, packed, rows, K / 2, (uint32_t)(tokens * kPlanes))) return st;
+  int *err = nullptr;
+  FPB_CUDA_TRY(cudaGetSymbolAddress(reinterpret_cast<void **>(&err), g_device_error));
+  GemmParams p{};
+  p.a_box_rows = kBM;
+  p.a_sf = sf;
+  p.b_sf = w->extras->sf_tiled;
+  p.b_globals = w->row_globals;
+  p.y = y;
+  p.N = (int)n_rows;
+  p.ldy = ldy;
+  p.y_bf16 = y_dtype == FPB_BF16;
+  p.M = (int)rows;
+  p.n_base = (int)n_base;
+  p.kb_count = (int)(K / 256);
+  p.error = err;
+  p.planes = 1;
+  p.tokens = tokens;
+  p.a_box_rows = tokens * kPlanes;
+  p.a_globals = ga;
+  p.moe_ids = moe_ids;
+  p.moe_count = moe_count;
+  p.moe_cap = moe_cap;
+  p.n_experts = n_experts;
+  p.a_group_step = groups > 1 ? 1 : 0;
+  p.y_group_stride = y_group_stride;
+  const size_t items = (size_t)((n_rows + kBN - 1) / kBN) * (moe_ids ? (size_t)moe_cap : 1);
+  const unsigned grid = (unsigned)std::min<size_t>(items, (size_t)std::max(1, sm_count()));
+  const CUtensorMap &tb = *reinterpret_cast<const CUtensorMap *>(w->extras->tmap_b);
+  e = launch_pdl(nvfp4_gemm_kernel, grid, kGemmThreads, kGemmSmem, s, tmap_a, tb, tmap_a, tb, tmap_a, p);
+  if (e != cudaSuccess) return cuda_fail(e, "nvfp4_gemm_kernel (planes)");
+  FPB_LAUNCH_CHECK("nvfp4_gemm_kernel");
+  return FPB_OK;
+}
+}  // namespace fpb
+
+extern "C" int fpb_nvfp4_gemv_planes(fpb_nvfp4_matrix *w, size_t row_begin, size_t row_end, const void *x,
+                                     int x_dtype, int tokens, void *y, int y_dtype, void *workspace,
+                                     size_t workspace_bytes, void *stream) {
+  if (!w || !x || !y || !workspace) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_gemv_planes: null pointer");
+  if (row_end == 0) row_end = w->rows;
+  if (row_begin >= row_end || row_end > w->rows)
+    return fail(FPB_ERR_SHAPE, "fpb_nvfp4_gemv_planes: row range [%zu, %zu) outside %zu rows", row_begin, row_end,
+                w->rows);
+  if (row_begin % kBN)
+    return fail(FPB_ERR_UNSUPPORTED, "fpb_nvfp4_gemv_planes: row_begin %zu is not a multiple of %d", row_begin, kBN);
+  const size_t n = row_end - row_begin;
+  return run_planes("fpb_nvfp4_gemv_planes", w, row_begin, n, x, x_dtype, false, 0, tokens, 1, nullptr, nullptr, 0, 0, y,
+                    y_dtype, 0, (long long)n, workspace, workspace_bytes, as_stream(stream));
+}
+
+extern "C" int fpb_nvfp4_moe_gemv_planes(fpb_nvfp4_matrix *w, size_t rows_per_expert, const int32_t *distinct,
+                                         const int32_t *count, int cap, const void *x, int x_dtype, size_t x_stride,
+                                         int tokens, void *y, int y_dtype, void *workspace, size_t workspace_bytes,
+                                         void *stream) {
+  if (!w || !distinct || !count || !x || !y || !workspace)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_moe_gemv_planes: null pointer");
+  if (cap < 1 || cap > 65535) return fail(FPB_ERR_SHAPE, "fpb_nvfp4_moe_gemv_planes: cap %d", cap);
+  if (rows_per_expert == 0 || rows_per_expert % kBN || w->rows % rows_per_expert || rows_per_expert > 0x7fffffff)
+    return fail(FPB_ERR_SHAPE, "fpb_nvfp4_moe_gemv_planes: rows_per_expert %zu must be a multiple of %d dividing %zu",
+                rows_per_expert, kBN, w->rows);
+  if (x_stride != 0 && x_stride < (size_t)tokens * w->cols)
+    return fail(FPB_ERR_SHAPE, "fpb_nvfp4_moe_gemv_planes: x_stride %zu below tokens x cols", x_stride);
+  const size_t groups = x_stride ? (size_t)cap : 1;
+  return run_planes("fpb_nvfp4_moe_gemv_planes", w, 0, rows_per_expert, x, x_dtype, false, x_stride, tokens, groups,
+                    distinct, count, cap, (int)(w->rows / rows_per_expert), y, y_dtype,
+                    (long long)tokens * (long long)rows_per_expert, (long long)rows_per_expert, workspace,
+                    workspace_bytes, as_stream(stream));
+}
+
+extern "C" int fpb_nvfp4_moe_gemv_planes_glu(fpb_nvfp4_matrix *w, size_t rows_per_expert, const int32_t *distinct,
+                                             const int32_t *count, int cap, const float *gate_up,
+                                             size_t gate_up_stride, int tokens, void *y, int y_dtype,
+                                             void *workspace, size_t workspace_bytes, void *stream) {
+  if (!w || !distinct || !count || !gate_up || !y || !workspace)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_moe_gemv_planes_glu: null pointer");
+  if (cap < 1 || cap > 65535) return fail(FPB_ERR_SHAPE, "fpb_nvfp4_moe_gemv_planes_glu: cap %d", cap);
+  if (rows_per_expert == 0 || rows_per_expert % kBN || w->rows % rows_per_expert || rows_per_expert > 0x7fffffff)
+    return fail(FPB_ERR_SHAPE, "fpb_nvfp4_moe_gemv_planes_glu: rows_per_expert %zu must be a multiple of %d "
+                "dividing %zu", rows_per_expert, kBN, w->rows);
+  if (gate_up_stride < (size_t)tokens * 2 * w->cols)
+    return fail(FPB_ERR_SHAPE, "fpb_nvfp4_moe_gemv_planes_glu: gate_up_stride %zu below tokens x 2 x cols",
+                gate_up_stride);
+  return run_planes("fpb_nvfp4_moe_gemv_planes_glu", w, 0, rows_per_expert, gate_up, FPB_F32, true, gate_up_stride,
+                    tokens, (size_t)cap, distinct, count, cap, (int)(w->rows / rows_per_expert), y, y_dtype,
+                    (long long)tokens * (long long)rows_per_expert, (long long)rows_per_expert, workspace,
+                    workspace_bytes, as_stream(stream));
+}
+
 extern "C" int fpb_nvfp4_grouped_gemm_q(fpb_nvfp4_matrix *w, const uint8_t *a_packed, const uint8_t *a_sf_tiled,
                                         const float *a_global, size_t padded_rows, const int32_t *tile_experts,
                                         const int32_t *token_rows, size_t rows_per_expert, void *y, int y_dtype,
@@ -884,6 +1205,7 @@ extern "C" int fpb_nvfp4_grouped_gemm_q(fpb_nvfp4_matrix *w, const uint8_t *a_pa
   int *err = nullptr;
   FPB_CUDA_TRY(cudaGetSymbolAddress(reinterpret_cast<void **>(&err), g_device_error));
   GemmParams p{};
+  p.a_box_rows = kBM;
   p.a_sf = a_sf_tiled;
   p.b_sf = w->extras->sf_tiled;
   p.a_global = a_global;
@@ -973,6 +1295,7 @@ extern "C" int fpb_nvfp4_grouped_gemm_swiglu_q(fpb_nvfp4_matrix *w, const uint8_
   }
   FPB_CUDA_TRY(cudaMemsetAsync(amax_bits, 0, sizeof(uint32_t), s));
   GemmParams p{};
+  p.a_box_rows = kBM;
   p.a_sf = a_sf_tiled;
   p.b_sf = w->extras->sf_tiled_glu;
   p.a_global = a_global;
@@ -1074,6 +1397,7 @@ int run_f16_gemm(const F16Gemm &g, cudaStream_t s) {
   int *err = nullptr;
   FPB_CUDA_TRY(cudaGetSymbolAddress(reinterpret_cast<void **>(&err), g_device_error));
   GemmParams p{};
+  p.a_box_rows = kBM;
   p.b_globals = g.b_globals;
   p.y = g.y;
   p.N = (int)g.n;

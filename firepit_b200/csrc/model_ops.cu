@@ -573,6 +573,119 @@ __global__ void gdn_delta_kernel(const float *conv_out, int conv_dim, const floa
   }
 }
 
+// The whole GDN mixer step after the projections in one launch, for the
+// config's heads (dk = dv = 128, two value heads per key head, conv kernel
+// <= 8): block (b, key head) of 512 threads.
+//  1. conv1d_silu (gdn.rs:6-63) of the block's 512 channels (the key head's
+//     q and k channels, its two value heads' v channels), one per thread,
+//     state shifted in place;
+//  2. q, k L2 norms (block reductions);
+//  3. delta_step (gdn.rs:206-263) for both value heads: thread (row half,
+//     column) holds 64 state rows of one column in registers;
+//  4. gated RMSNorm times SiLU(z) (gdn.rs:266-278), out [B, value_dim].
+constexpr int kGdnThreads = 512, kGdnD = 128, kGdnRows = 64;
+__global__ void __launch_bounds__(kGdnThreads, 1) gdn_step_kernel(
+    const float *x, long long x_pitch, float *conv_state, const float *conv_w, int conv_kernel, const float *a,
+    const float *bgate, long long ab_pitch, const float *a_log, const float *dt_bias, float *state, const float *z,
+    long long z_pitch, const float *gamma, int key_heads, float eps, float inv_sqrt_dk, void *out, int out_bf16) {
+  pdl_enter();
+  __shared__ float qs[kGdnD], ks[kGdnD], vs[2 * kGdnD];
+  __shared__ float part[2][2 * kGdnD], part2[2][2 * kGdnD];
+  __shared__ float red[32];
+  const int b = blockIdx.x / key_heads, kh = blockIdx.x % key_heads;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int key_dim = key_heads * kGdnD, value_heads = 2 * key_heads;
+  const int conv_dim = 2 * key_dim + value_heads * kGdnD;
+  // 1. conv + SiLU
+  {
+    const int c = tid < kGdnD ? kh * kGdnD + tid
+                : tid < 2 * kGdnD ? key_dim + kh * kGdnD + (tid - kGdnD)
+                                  : 2 * key_dim + kh * 2 * kGdnD + (tid - 2 * kGdnD);
+    float *st = conv_state + ((size_t)b * conv_dim + c) * (conv_kernel - 1);
+    const float *wr = conv_w + (size_t)c * conv_kernel;
+    const float cur = x[(size_t)b * x_pitch + c];
+    float hist[8];
+    float sum = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 7; ++j)
+      if (j < conv_kernel - 1) {
+        hist[j] = st[j];
+        sum = fmaf(hist[j], wr[j], sum);
+      }
+    sum = fmaf(cur, wr[conv_kernel - 1], sum);
+    const float o = sum / (1.0f + expf(-sum));
+#pragma unroll
+    for (int j = 0; j < 6; ++j)
+      if (j + 1 < conv_kernel - 1) st[j] = hist[j + 1];
+    st[conv_kernel - 2] = cur;
+    if (tid < kGdnD)
+      qs[tid] = o;
+    else if (tid < 2 * kGdnD)
+      ks[tid - kGdnD] = o;
+    else
+      vs[tid - 2 * kGdnD] = o;
+  }
+  __syncthreads();
+  // 2. L2 norms: warps 0-3 hold q, warps 4-7 k
+  {
+    float v2 = 0.0f;
+    if (tid < kGdnD)
+      v2 = qs[tid] * qs[tid];
+    else if (tid < 2 * kGdnD)
+      v2 = ks[tid - kGdnD] * ks[tid - kGdnD];
+    v2 = warp_sum(v2);
+    if (lane == 0 && warp < 8) red[warp] = v2;
+  }
+  __syncthreads();
+  const float q_scale = __frsqrt_rn(red[0] + red[1] + red[2] + red[3] + eps) * inv_sqrt_dk;
+  const float k_scale = __frsqrt_rn(red[4] + red[5] + red[6] + red[7] + eps);
+  // 3. gates and the delta rule; thread (rg, col): head j = col / 128, column jc
+  const int col = tid & (2 * kGdnD - 1), rg = tid >> 8;
+  const int j = col >> 7, jc = col & (kGdnD - 1), h = 2 * kh + j;
+  const float bv = bgate[(size_t)b * ab_pitch + h], av = a[(size_t)b * ab_pitch + h];
+  const float beta = 1.0f / (1.0f + expf(-bv));
+  const float xs = av + dt_bias[h];
+  const float tiny = expf(fminf(xs, 0.0f));
+  const float series = tiny - tiny * tiny * 0.5f + tiny * tiny * tiny * 0.33333334f;
+  const float ordinary = fmaxf(xs, 0.0f) + logf(1.0f + expf(-fabsf(xs)));
+  const float softplus = xs < -8.0f ? series : ordinary;
+  const float decay = expf(-(expf(a_log[h]) * softplus));
+  float *S = state + ((size_t)b * value_heads + h) * kGdnD * kGdnD;
+  const int i0 = rg * kGdnRows;
+  float sv[kGdnRows];
+#pragma unroll
+  for (int r = 0; r < kGdnRows; ++r) sv[r] = S[(size_t)(i0 + r) * kGdnD + jc];
+  float mem = 0.0f;
+#pragma unroll
+  for (int r = 0; r < kGdnRows; ++r) mem = fmaf(sv[r], ks[i0 + r] * k_scale, mem);
+  part[rg][col] = mem;
+  __syncthreads();
+  mem = (part[0][col] + part[1][col]) * decay;
+  const float delta = (vs[col] - mem) * beta;
+  float o = 0.0f;
+#pragma unroll
+  for (int r = 0; r < kGdnRows; ++r) {
+    const float nxt = fmaf(sv[r], decay, ks[i0 + r] * k_scale * delta);
+    S[(size_t)(i0 + r) * kGdnD + jc] = nxt;
+    o = fmaf(nxt, qs[i0 + r] * q_scale, o);
+  }
+  part2[rg][col] = o;
+  __syncthreads();
+  // 4. gated norm: threads of row half 0 hold the 256 outputs (warps 0-3:
+  // head 0, warps 4-7: head 1)
+  o = part2[0][col] + part2[1][col];
+  float o2 = warp_sum(rg == 0 ? o * o : 0.0f);
+  if (lane == 0 && rg == 0) red[8 + warp] = o2;
+  __syncthreads();
+  if (rg == 0) {
+    const float ss = red[8 + 4 * j] + red[9 + 4 * j] + red[10 + 4 * j] + red[11 + 4 * j];
+    const float scale = __frsqrt_rn(fmaf(ss, 1.0f / kGdnD, eps));
+    const float zz = z[(size_t)b * z_pitch + (size_t)h * kGdnD + jc];
+    store_f(out, out_bf16, (size_t)b * value_heads * kGdnD + (size_t)h * kGdnD + jc,
+            o * scale * gamma[jc] * zz / (1.0f + expf(-zz)));
+  }
+}
+
 // RMSNorm of each value head's output (gated_norm gamma [dv]) times SiLU(z)
 // (gdn.rs:266-278); one warp per (b, head); out [B, value_heads * dv].
 __global__ void gdn_gated_norm_kernel(const float *x, const float *z, long long z_pitch, const float *gamma,
@@ -984,5 +1097,28 @@ extern "C" int fpb_argmax_advance(const float *logits, size_t rows, size_t vocab
     return fail(FPB_ERR_SHAPE, "fpb_argmax_advance: shape");
   FPB_LAUNCH(argmax_advance_kernel, (unsigned)rows, 1024, 0, as_stream(stream), logits, (int)vocab, tokens, positions,
              history, (int)history_len, step);
+  return FPB_OK;
+}
+
+extern "C" int fpb_gdn_step(const float *x, size_t x_pitch, float *conv_state, const float *conv_weight,
+                            size_t conv_kernel, const float *a, const float *b, size_t ab_pitch, const float *a_log,
+                            const float *dt_bias, float *state, const float *z, size_t z_pitch, const float *gamma,
+                            size_t batch, size_t key_heads, size_t value_heads, size_t dk, size_t dv, float eps,
+                            void *out, int out_dtype, void *stream) {
+  if (!x || !conv_state || !conv_weight || !a || !b || !a_log || !dt_bias || !state || !z || !gamma || !out)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_gdn_step: null pointer");
+  if (out_dtype != FPB_F32 && out_dtype != FPB_BF16) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_gdn_step: dtype");
+  if (batch == 0 || key_heads == 0 || batch * key_heads > 0x7fffffff)
+    return fail(FPB_ERR_SHAPE, "fpb_gdn_step: shape");
+  if (dk != (size_t)kGdnD || dv != (size_t)kGdnD || value_heads != 2 * key_heads || conv_kernel < 2 ||
+      conv_kernel > 8)
+    return fail(FPB_ERR_UNSUPPORTED, "fpb_gdn_step: dk = dv = 128, value_heads = 2 * key_heads and a conv kernel "
+                "of 2..8 only (other shapes: fpb_gdn_conv, fpb_gdn_delta, fpb_gdn_gated_norm)");
+  if (x_pitch < 2 * key_heads * dk + value_heads * dv || z_pitch < value_heads * dv)
+    return fail(FPB_ERR_SHAPE, "fpb_gdn_step: pitches");
+  FPB_LAUNCH(gdn_step_kernel, (unsigned)(batch * key_heads), kGdnThreads, 0, as_stream(stream), x,
+             (long long)x_pitch, conv_state, conv_weight, (int)conv_kernel, a, b, (long long)ab_pitch, a_log,
+             dt_bias, state, z, (long long)z_pitch, gamma, (int)key_heads, eps, 1.0f / sqrtf((float)dk), out,
+             out_dtype == FPB_BF16);
   return FPB_OK;
 }

@@ -41,13 +41,12 @@ __device__ __forceinline__ float order_key_value(uint32_t k) {
   return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
 }
 
+// Top-k of one token's logits `row` by one warp (lane l: logits l, l + 32,
+// ...); `gate`: the token's shared-expert gate logit or null.
 template <int PER_LANE>
-__global__ void moe_topk_kernel(const float *logits, long long ld, const float *shared_gate, int tokens,
-                                int experts, int k, int width, int32_t *ids, float *weights) {
-  pdl_enter();
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  if (warp >= tokens) return;
-  const float *row = logits + (long long)warp * ld;
+__device__ __forceinline__ void topk_warp(const float *row, const float *gate, int experts, int k, int width,
+                                          int32_t *ids_row, float *weights_row) {
+  const int lane = threadIdx.x & 31;
   float v[PER_LANE];
   float m = -INFINITY;
 #pragma unroll
@@ -97,14 +96,24 @@ __global__ void moe_topk_kernel(const float *logits, long long ld, const float *
     if (lane < k) {
       id = my_id;
       w = my_score / total;
-    } else if (lane == k && shared_gate) {
+    } else if (lane == k && gate) {
       id = experts;
-      const float g = shared_gate[warp];
+      const float g = *gate;
       w = 1.0f / (1.0f + expf(g * -1.0f));
     }
-    ids[(long long)warp * width + lane] = id;
-    weights[(long long)warp * width + lane] = w;
+    ids_row[lane] = id;
+    weights_row[lane] = w;
   }
+}
+
+template <int PER_LANE>
+__global__ void moe_topk_kernel(const float *logits, long long ld, const float *shared_gate, int tokens,
+                                int experts, int k, int width, int32_t *ids, float *weights) {
+  pdl_enter();
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (warp >= tokens) return;
+  topk_warp<PER_LANE>(logits + (long long)warp * ld, shared_gate ? shared_gate + warp : nullptr, experts, k, width,
+                      ids + (long long)warp * width, weights + (long long)warp * width);
 }
 
 // ---- layout: stable counting sort (moe.rs:452-516) -------------------------------------
@@ -679,20 +688,19 @@ static void launch_rows_encode(const Rows &src, size_t rows, const int32_t *vali
 // shared-memory bitmap of the experts, popcount prefix sums over its words.
 // Device error 107 (and map -1) for an id outside [0, experts).
 constexpr int kPlanThreads = 256;
-__global__ void __launch_bounds__(kPlanThreads) moe_decode_plan_kernel(const int32_t *ids, int tokens, int width,
-                                                                       int slots, int n_experts, int cap,
-                                                                       int32_t *experts, int32_t *count,
-                                                                       int32_t *map, int *error) {
-  pdl_enter();
-  extern __shared__ uint32_t plan_sm[];
-  __shared__ int wsum[kPlanThreads / 32];
+// The plan by one CTA (any multiple of 32 threads up to 1024); `plan_sm`:
+// 2 * ceil(n_experts / 32) words of shared memory.
+__device__ __forceinline__ void plan_block(const int32_t *ids, int tokens, int width, int slots, int n_experts,
+                                           int cap, int32_t *experts, int32_t *count, int32_t *map, int *error,
+                                           uint32_t *plan_sm) {
+  __shared__ int wsum[32];
   const int words = (n_experts + 31) / 32;
   uint32_t *bits = plan_sm, *base = plan_sm + words;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  for (int w = tid; w < words; w += kPlanThreads) bits[w] = 0;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthreads = blockDim.x, nwarps = nthreads >> 5;
+  for (int w = tid; w < words; w += nthreads) bits[w] = 0;
   __syncthreads();
   const int n = tokens * slots;
-  for (int i = tid; i < n; i += kPlanThreads) {
+  for (int i = tid; i < n; i += nthreads) {
     const int e = ids[(size_t)(i / slots) * width + i % slots];
     if (e >= 0 && e < n_experts)
       atomicOr(&bits[e >> 5], 1u << (e & 31));
@@ -701,7 +709,7 @@ __global__ void __launch_bounds__(kPlanThreads) moe_decode_plan_kernel(const int
   }
   __syncthreads();
   // exclusive prefix of the words' popcounts: contiguous words per thread
-  const int per = (words + kPlanThreads - 1) / kPlanThreads;
+  const int per = (words + nthreads - 1) / nthreads;
   const int w0 = min(words, tid * per), w1 = min(words, w0 + per);
   int local = 0;
   for (int w = w0; w < w1; ++w) local += __popc(bits[w]);
@@ -714,7 +722,7 @@ __global__ void __launch_bounds__(kPlanThreads) moe_decode_plan_kernel(const int
   if (lane == 31) wsum[warp] = incl;
   __syncthreads();
   int before = 0, total = 0;
-  for (int w = 0; w < kPlanThreads / 32; ++w) {
+  for (int w = 0; w < nwarps; ++w) {
     before += w < warp ? wsum[w] : 0;
     total += wsum[w];
   }
@@ -724,7 +732,7 @@ __global__ void __launch_bounds__(kPlanThreads) moe_decode_plan_kernel(const int
     run += __popc(bits[w]);
   }
   __syncthreads();
-  for (int w = tid; w < words; w += kPlanThreads) {
+  for (int w = tid; w < words; w += nthreads) {
     uint32_t b = bits[w];
     int idx = base[w];
     while (b) {
@@ -734,14 +742,46 @@ __global__ void __launch_bounds__(kPlanThreads) moe_decode_plan_kernel(const int
       ++idx;
     }
   }
-  for (int i = total + tid; i < cap; i += kPlanThreads) experts[i] = -1;
+  for (int i = total + tid; i < cap; i += nthreads) experts[i] = -1;
   if (tid == 0) *count = min(total, cap);
-  for (int i = tid; i < n; i += kPlanThreads) {
+  for (int i = tid; i < n; i += nthreads) {
     const int e = ids[(size_t)(i / slots) * width + i % slots];
     int m = -1;
     if (e >= 0 && e < n_experts) m = (int)base[e >> 5] + __popc(bits[e >> 5] & ((1u << (e & 31)) - 1u));
     map[i] = m < cap ? m : -1;
   }
+}
+
+__global__ void __launch_bounds__(kPlanThreads) moe_decode_plan_kernel(const int32_t *ids, int tokens, int width,
+                                                                       int slots, int n_experts, int cap,
+                                                                       int32_t *experts, int32_t *count,
+                                                                       int32_t *map, int *error) {
+  pdl_enter();
+  extern __shared__ uint32_t plan_sm[];
+  plan_block(ids, tokens, width, slots, n_experts, cap, experts, count, map, error, plan_sm);
+}
+
+// Router top-k and the plan in one launch for decode-size batches: warp t
+// takes token t's top-k (the shared-expert gate logit, when gate_col >= 0,
+// is column gate_col of the same logits row; the shared expert is id
+// `experts`), then the CTA builds the plan over the k (+1) slots.
+template <int PER_LANE>
+__global__ void __launch_bounds__(1024) moe_decode_route_kernel(const float *logits, long long ld, int gate_col,
+                                                                 int tokens, int experts, int k, int width,
+                                                                 int32_t *ids, float *weights, int cap,
+                                                                 int32_t *distinct, int32_t *count, int32_t *map,
+                                                                 int *error) {
+  pdl_enter();
+  extern __shared__ uint32_t plan_sm[];
+  const int warp = threadIdx.x >> 5;
+  if (warp < tokens) {
+    const float *row = logits + (long long)warp * ld;
+    topk_warp<PER_LANE>(row, gate_col >= 0 ? row + gate_col : nullptr, experts, k, width,
+                        ids + (long long)warp * width, weights + (long long)warp * width);
+  }
+  __syncthreads();  // the ids written above are read by the whole CTA below (same CTA: visible after the barrier)
+  const int slots = k + (gate_col >= 0 ? 1 : 0);
+  plan_block(ids, tokens, width, slots, experts + (gate_col >= 0 ? 1 : 0), cap, distinct, count, map, error, plan_sm);
 }
 
 }  // namespace fpb
@@ -1137,5 +1177,41 @@ extern "C" int fpb_moe_decode_plan(const int32_t *ids, size_t tokens, size_t wid
                              device_error_ptr());
   if (e != cudaSuccess) return cuda_fail(e, "moe_decode_plan_kernel");
   FPB_LAUNCH_CHECK("moe_decode_plan_kernel");
+  return FPB_OK;
+}
+
+extern "C" int fpb_moe_decode_route(const float *logits, size_t ld, long long gate_col, size_t tokens,
+                                    size_t experts, size_t top_k, size_t width, int32_t *ids, float *weights,
+                                    int32_t *distinct, int32_t *count, size_t cap, int32_t *map, void *stream) {
+  if (!logits || !ids || !weights || !distinct || !count || !map)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_moe_decode_route: null pointer");
+  const size_t slots = top_k + (gate_col >= 0 ? 1 : 0);
+  // up to 512 experts: a warp's logits stay in registers under the 1024-thread
+  // launch bound (64 registers a thread); larger routers use fpb_moe_topk +
+  // fpb_moe_decode_plan
+  if (tokens == 0 || tokens > 32 || experts == 0 || experts > 512 || top_k == 0 || top_k > experts ||
+      width < slots || width > 32 || ld < experts || (gate_col >= 0 && (size_t)gate_col >= ld) ||
+      cap < tokens * slots || cap > 0x7fffffff)
+    return fail(FPB_ERR_SHAPE, "fpb_moe_decode_route: tokens %zu (at most 32) experts %zu (at most 512) top_k %zu width %zu "
+                "ld %zu cap %zu", tokens, experts, top_k, width, ld, cap);
+  const size_t words = (experts + 1 + 31) / 32;
+  const int per = (int)((experts + 31) / 32);
+  const unsigned threads = (unsigned)std::max<size_t>(64, tokens * 32);
+  const size_t smem = 2 * words * sizeof(uint32_t);
+  cudaStream_t s = as_stream(stream);
+  auto go = [&](auto kernel) {
+    return launch_pdl(kernel, 1, threads, smem, s, logits, (long long)ld, (int)gate_col, (int)tokens,
+                      (int)experts, (int)top_k, (int)width, ids, weights, (int)cap, distinct, count, map,
+                      device_error_ptr());
+  };
+  cudaError_t e;
+  if (per <= 4)
+    e = go(moe_decode_route_kernel<4>);
+  else if (per <= 8)
+    e = go(moe_decode_route_kernel<8>);
+  else
+    e = go(moe_decode_route_kernel<16>);
+  if (e != cudaSuccess) return cuda_fail(e, "moe_decode_route_kernel");
+  FPB_LAUNCH_CHECK("moe_decode_route_kernel");
   return FPB_OK;
 }

@@ -65,6 +65,10 @@ class HybridConfig:
     def slots(self) -> int:
         return self.top_k + 1  # the shared expert runs as slot top_k
 
+    @property
+    def route_rows(self) -> int:
+        return (self.experts + 1 + 3) // 4 * 4  # router + gate rows, padded
+
 
 def _nvfp4(F, rows, cols, seed, stream_id, dev, rows_per_global=None, chunk_rows=None):
     """NVFP4 matrix from N(0, 0.02), generated and quantized on the device in
@@ -84,6 +88,27 @@ def _nvfp4(F, rows, cols, seed, stream_id, dev, rows_per_global=None, chunk_rows
     scales = torch.cat([p[1] for p in parts])
     globals_ = torch.cat([p[2] for p in parts])
     return F.Nvfp4Matrix.from_device(packed, scales, globals_, rows, cols)
+
+
+def _nvfp4_stacked(F, parts, cols, seed, dev, pad_rows=0):
+    """Matrices of N(0, 0.02) rows (parts: [(rows, stream_id)]), each
+    quantized with its own global and stacked (HostNvfp4Matrix::stack,
+    weights/nvfp4.rs:84-97), then `pad_rows` zero rows."""
+    import torch
+    packed, scales, globals_ = [], [], []
+    for rows, sid in parts:
+        w = torch.empty(rows, cols, device=dev)
+        F.synth_normal((rows, cols), seed=seed, stream_id=sid, std=0.02, out=w)
+        p, sc, g = F.quantize_nvfp4(w)
+        packed.append(p)
+        scales.append(sc)
+        globals_.append(g)
+    if pad_rows:
+        packed.append(torch.zeros(pad_rows, cols // 2, dtype=torch.uint8, device=dev))
+        scales.append(torch.zeros(pad_rows, cols // 16, dtype=torch.uint8, device=dev))
+        globals_.append(torch.zeros(pad_rows, dtype=torch.float32, device=dev))
+    rows = sum(r for r, _ in parts) + pad_rows
+    return F.Nvfp4Matrix.from_device(torch.cat(packed), torch.cat(scales), torch.cat(globals_), rows, cols)
 
 
 class HybridModel:
@@ -142,8 +167,11 @@ class HybridModel:
                 L["dt_bias"] = vec(c.value_heads, std=0.5)
                 L["gated_norm"] = norm(c.value_head_dim)
                 L["w_out"] = mat(h, c.value_dim)
-            L["w_router"] = mat(c.experts, h)
-            L["w_shared_gate"] = mat(1, h)
+            # router rows, the shared-expert gate row (each its own global) and
+            # zero rows up to a multiple of 4: one GEMV segment; the gate logit
+            # is column `experts` of the router output
+            L["w_route"] = _nvfp4_stacked(F, [(c.experts, next_id()), (1, next_id())], h, seed, dev,
+                                          c.route_rows - c.experts - 1)
             # routed experts 0 .. E-1 and the shared expert E, stacked, one global each
             L["w_gate_up"] = mat((c.experts + 1) * 2 * c.moe_inter, h, 2 * c.moe_inter)
             L["w_down"] = mat((c.experts + 1) * h, c.moe_inter, h)
@@ -167,7 +195,7 @@ class HybridModel:
                                                                                          c.q_heads * c.head_dim)
             else:
                 dense += nb(c.conv_dim + c.value_dim + 2 * c.value_heads, c.hidden) + nb(c.hidden, c.value_dim)
-            dense += nb(c.experts + 1, c.hidden)
+            dense += nb(c.route_rows, c.hidden)
         expert = nb(2 * c.moe_inter, c.hidden) + nb(c.hidden, c.moe_inter)
         return {"dense": dense, "expert": expert, "lm_head": nb(c.vocab, c.hidden)}
 
@@ -208,7 +236,7 @@ class Decoder:
         self.attn = torch.zeros(B, c.q_heads * c.head_dim, **bf)
         self.attn_ws = torch.empty(int(N.lib.fpb_attn_decode_workspace_bytes(B, c.q_heads, c.head_dim, max_seq, 32)),
                                    dtype=torch.uint8, device=dev)
-        self.logits_r = torch.zeros(B, c.experts, **f32)
+        self.logits_r = torch.zeros(B, c.route_rows, **f32)  # router logits, then the gate logit
         self.gate = torch.zeros(B, **f32)
         self.ids = torch.zeros(B, c.slots, **i32)
         self.wts = torch.zeros(B, c.slots, **f32)
@@ -235,6 +263,22 @@ class Decoder:
             else:
                 self.gdn[i] = (torch.zeros(B, c.conv_dim, c.conv_kernel - 1, **f32),
                                torch.zeros(B, c.value_heads, c.key_head_dim, c.value_head_dim, **f32))
+        # Tensor-core GEMVs (x as NVFP4 digit planes, tcgen05) where the shapes
+        # allow: the experts' gate/up and down (SwiGLU folded into the down
+        # projection's plane encoder) and the LM head.
+        def planes_ok(k, rows):
+            return k % 256 == 0 and k <= 4096 and rows % 128 == 0 and B <= 16
+
+        self.planes_gu = self.distinct_moe and planes_ok(h, 2 * c.moe_inter)
+        self.planes_down = self.planes_gu and planes_ok(c.moe_inter, h)
+        self.planes_lm = planes_ok(h, c.vocab)
+        ws = int(N.lib.fpb_nvfp4_gemv_planes_workspace_bytes(1, h))
+        self.ws_x = torch.empty(ws, dtype=torch.uint8, device=dev)  # one x: gate/up, LM head
+        ws = int(N.lib.fpb_nvfp4_gemv_planes_workspace_bytes(cap, c.moe_inter)) if self.planes_down else 256
+        self.ws_down = torch.empty(ws, dtype=torch.uint8, device=dev)
+        # conv + delta rule + gated norm in one launch for the config's heads
+        self.fused_gdn = (c.key_head_dim == 128 and c.value_head_dim == 128 and c.value_heads == 2 * c.key_heads
+                          and 2 <= c.conv_kernel <= 8)
         self._batched = {}
         self.graph = None
         self.route_log = None  # [layers, batch, slots] int32 when recording routes
@@ -263,14 +307,21 @@ class Decoder:
                 self._gemv(("gdn", i), [(L["w_qkv"], self.qkv), (L["w_z"], self.z), (L["w_b"], self.gb),
                                         (L["w_a"], self.ga)], self.normed, sh)
                 conv_state, rec = self.gdn[i]
-                N.call("fpb_gdn_conv", self.qkv.data_ptr(), c.conv_dim, conv_state.data_ptr(), L["conv"].data_ptr(),
-                       B, c.conv_dim, c.conv_kernel, self.conv_out.data_ptr(), sh)
-                N.call("fpb_gdn_delta", self.conv_out.data_ptr(), self.ga.data_ptr(), self.gb.data_ptr(), c.value_heads,
-                       L["a_log"].data_ptr(), L["dt_bias"].data_ptr(), rec.data_ptr(), B, c.key_heads, c.value_heads,
-                       c.key_head_dim, c.value_head_dim, eps, self.mix.data_ptr(), sh)
-                N.call("fpb_gdn_gated_norm", self.mix.data_ptr(), self.z.data_ptr(), c.value_dim,
-                       L["gated_norm"].data_ptr(), B, c.value_heads, c.value_head_dim, eps, self.gated.data_ptr(), BF,
-                       sh)
+                if self.fused_gdn:
+                    N.call("fpb_gdn_step", self.qkv.data_ptr(), c.conv_dim, conv_state.data_ptr(), L["conv"].data_ptr(),
+                           c.conv_kernel, self.ga.data_ptr(), self.gb.data_ptr(), c.value_heads, L["a_log"].data_ptr(),
+                           L["dt_bias"].data_ptr(), rec.data_ptr(), self.z.data_ptr(), c.value_dim,
+                           L["gated_norm"].data_ptr(), B, c.key_heads, c.value_heads, c.key_head_dim,
+                           c.value_head_dim, eps, self.gated.data_ptr(), BF, sh)
+                else:
+                    N.call("fpb_gdn_conv", self.qkv.data_ptr(), c.conv_dim, conv_state.data_ptr(),
+                           L["conv"].data_ptr(), B, c.conv_dim, c.conv_kernel, self.conv_out.data_ptr(), sh)
+                    N.call("fpb_gdn_delta", self.conv_out.data_ptr(), self.ga.data_ptr(), self.gb.data_ptr(),
+                           c.value_heads, L["a_log"].data_ptr(), L["dt_bias"].data_ptr(), rec.data_ptr(), B,
+                           c.key_heads, c.value_heads, c.key_head_dim, c.value_head_dim, eps, self.mix.data_ptr(), sh)
+                    N.call("fpb_gdn_gated_norm", self.mix.data_ptr(), self.z.data_ptr(), c.value_dim,
+                           L["gated_norm"].data_ptr(), B, c.value_heads, c.value_head_dim, eps,
+                           self.gated.data_ptr(), BF, sh)
                 self._gemv(("gdn_out", i), [(L["w_out"], self.delta)], self.gated, sh)
             else:
                 self._gemv(("attn", i), [(L["w_qg"], self.qg), (L["w_k"], self.kp), (L["w_v"], self.vp)],
@@ -290,23 +341,42 @@ class Decoder:
                    self.resid[1 - cur].data_ptr(), B, h, L["post_norm"].data_ptr(), eps, self.normed.data_ptr(), BF, h,
                    sh)
             cur = 1 - cur
-            self._gemv(("router", i), [(L["w_router"], self.logits_r), (L["w_shared_gate"], self.gate)], self.normed,
-                       sh)
-            N.call("fpb_moe_topk", self.logits_r.data_ptr(), c.experts, self.gate.data_ptr(), B, c.experts, c.top_k,
-                   c.slots, self.ids.data_ptr(), self.wts.data_ptr(), sh)
+            self._gemv(("router", i), [(L["w_route"], self.logits_r)], self.normed, sh)
+            nxt = m.layers[i + 1]["input_norm"] if i + 1 < len(m.layers) else m.final_norm
+            R = c.route_rows
+            if self.distinct_moe and B <= 32 and c.experts <= 512:
+                cap = self.cap
+                N.call("fpb_moe_decode_route", self.logits_r.data_ptr(), R, c.experts, B, c.experts, c.top_k, c.slots,
+                       self.ids.data_ptr(), self.wts.data_ptr(), self.distinct.data_ptr(),
+                       self.n_distinct.data_ptr(), cap, self.route_map.data_ptr(), sh)
+            else:  # batches beyond one CTA's warps: top-k with the gate column copied out
+                self.gate.copy_(self.logits_r[:, c.experts])
+                N.call("fpb_moe_topk", self.logits_r.data_ptr(), R, self.gate.data_ptr(), B, c.experts, c.top_k,
+                       c.slots, self.ids.data_ptr(), self.wts.data_ptr(), sh)
             if self.route_log is not None:
                 self.route_log[i].copy_(self.ids)
-            nxt = m.layers[i + 1]["input_norm"] if i + 1 < len(m.layers) else m.final_norm
             if self.distinct_moe:
                 cap = self.cap
-                N.call("fpb_moe_decode_plan", self.ids.data_ptr(), B, c.slots, c.slots, c.experts + 1,
-                       self.distinct.data_ptr(), self.n_distinct.data_ptr(), cap, self.route_map.data_ptr(), sh)
-                N.call("fpb_nvfp4_moe_gemv", L["w_gate_up"].handle, 2 * c.moe_inter, self.distinct.data_ptr(),
-                       self.n_distinct.data_ptr(), cap, self.normed.data_ptr(), BF, 0, B, self.gu.data_ptr(), F32, sh)
-                N.call("fpb_swiglu", self.gu.data_ptr(), F32, cap * B, c.moe_inter, self.act.data_ptr(), BF, sh)
-                N.call("fpb_nvfp4_moe_gemv", L["w_down"].handle, h, self.distinct.data_ptr(),
-                       self.n_distinct.data_ptr(), cap, self.act.data_ptr(), BF, B * c.moe_inter, B,
-                       self.routed.data_ptr(), F32, sh)
+                if not (B <= 32 and c.experts <= 512):
+                    N.call("fpb_moe_decode_plan", self.ids.data_ptr(), B, c.slots, c.slots, c.experts + 1,
+                           self.distinct.data_ptr(), self.n_distinct.data_ptr(), cap, self.route_map.data_ptr(), sh)
+                if self.planes_gu:
+                    N.call("fpb_nvfp4_moe_gemv_planes", L["w_gate_up"].handle, 2 * c.moe_inter,
+                           self.distinct.data_ptr(), self.n_distinct.data_ptr(), cap, self.normed.data_ptr(), BF, 0, B,
+                           self.gu.data_ptr(), F32, self.ws_x.data_ptr(), self.ws_x.numel(), sh)
+                else:
+                    N.call("fpb_nvfp4_moe_gemv", L["w_gate_up"].handle, 2 * c.moe_inter, self.distinct.data_ptr(),
+                           self.n_distinct.data_ptr(), cap, self.normed.data_ptr(), BF, 0, B, self.gu.data_ptr(), F32,
+                           sh)
+                if self.planes_down:  # SwiGLU in f32 inside the plane encoder
+                    N.call("fpb_nvfp4_moe_gemv_planes_glu", L["w_down"].handle, h, self.distinct.data_ptr(),
+                           self.n_distinct.data_ptr(), cap, self.gu.data_ptr(), B * 2 * c.moe_inter, B,
+                           self.routed.data_ptr(), F32, self.ws_down.data_ptr(), self.ws_down.numel(), sh)
+                else:
+                    N.call("fpb_swiglu", self.gu.data_ptr(), F32, cap * B, c.moe_inter, self.act.data_ptr(), BF, sh)
+                    N.call("fpb_nvfp4_moe_gemv", L["w_down"].handle, h, self.distinct.data_ptr(),
+                           self.n_distinct.data_ptr(), cap, self.act.data_ptr(), BF, B * c.moe_inter, B,
+                           self.routed.data_ptr(), F32, sh)
                 N.call("fpb_moe_decode_combine_add_norm", self.routed.data_ptr(), self.route_map.data_ptr(),
                        self.wts.data_ptr(), c.slots, c.slots, self.resid[cur].data_ptr(), nxt.data_ptr(), B, h, eps,
                        self.resid[1 - cur].data_ptr(), self.normed.data_ptr(), BF, sh)
@@ -320,7 +390,11 @@ class Decoder:
                        self.resid[cur].data_ptr(), nxt.data_ptr(), B, h, eps, self.resid[1 - cur].data_ptr(),
                        self.normed.data_ptr(), BF, sh)
             cur = 1 - cur
-        self._gemv(("lm_head",), [(m.lm_head, self.logits)], self.normed, sh)
+        if self.planes_lm:
+            N.call("fpb_nvfp4_gemv_planes", m.lm_head.handle, 0, 0, self.normed.data_ptr(), BF, B,
+                   self.logits.data_ptr(), F32, self.ws_x.data_ptr(), self.ws_x.numel(), sh)
+        else:
+            self._gemv(("lm_head",), [(m.lm_head, self.logits)], self.normed, sh)
         N.call("fpb_argmax_advance", self.logits.data_ptr(), B, c.vocab, self.tokens.data_ptr(),
                self.positions.data_ptr(), self.history.data_ptr() if self.history_len else None, self.history_len,
                self.step_ctr.data_ptr(), sh)

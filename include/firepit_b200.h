@@ -271,6 +271,34 @@ int fpb_nvfp4_gemm(fpb_nvfp4_matrix *w, size_t row_begin, size_t row_end, const 
 size_t fpb_nvfp4_gemm_hilo_workspace_bytes(size_t m, size_t rows, size_t k, int x_dtype);
 int fpb_nvfp4_gemm_hilo(fpb_nvfp4_matrix *w, size_t row_begin, size_t row_end, const void *x, int x_dtype,
                         size_t m, void *y, int y_dtype, void *workspace, size_t workspace_bytes, void *stream);
+/* The NVFP4 GEMV on the tensor cores (no reference counterpart for the
+ * method; same results as gemv() up to f32 rounding): each row of x
+ * (`tokens` of them, 1..16) becomes 8 NVFP4 digit planes (plane 0 = x with
+ * the config-0 quantize rule, plane p = the residual of the planes before
+ * it, each with its own global: x to about 2^-27 of its magnitude), the
+ * planes of up to 16 tokens are the 128-row A operand of tcgen05
+ * kind::mxf4nvf4 against the weight rows (the hardware decodes e2m1 / e4m3),
+ * and the epilogue adds each token's 8 plane rows times their globals.
+ * y [tokens, row_end - row_begin].  cols % 256 == 0, cols <= 4096,
+ * row_begin % 128 == 0; workspace 256-byte aligned,
+ * fpb_nvfp4_gemv_planes_workspace_bytes(1, cols) bytes.
+ * fpb_nvfp4_moe_gemv_planes: fpb_nvfp4_moe_gemv (distinct experts, device
+ * count) the same way; rows_per_expert % 128 == 0; x_stride 0 (one x for
+ * every expert: workspace for 1 group) or per distinct expert (cap groups). */
+size_t fpb_nvfp4_gemv_planes_workspace_bytes(size_t groups, size_t k);
+int fpb_nvfp4_gemv_planes(fpb_nvfp4_matrix *w, size_t row_begin, size_t row_end, const void *x, int x_dtype,
+                          int tokens, void *y, int y_dtype, void *workspace, size_t workspace_bytes, void *stream);
+int fpb_nvfp4_moe_gemv_planes(fpb_nvfp4_matrix *w, size_t rows_per_expert, const int32_t *distinct,
+                              const int32_t *count, int cap, const void *x, int x_dtype, size_t x_stride, int tokens,
+                              void *y, int y_dtype, void *workspace, size_t workspace_bytes, void *stream);
+/* The down projection after the gate/up one: gate_up [cap][tokens][2 * cols]
+ * f32 (distinct expert u's block at gate_up + u * gate_up_stride, gate
+ * columns first) and the GEMV input is silu(gate) * up (swiglu.rs:16) in f32,
+ * encoded straight into planes (no SwiGLU launch, no rounding of h). */
+int fpb_nvfp4_moe_gemv_planes_glu(fpb_nvfp4_matrix *w, size_t rows_per_expert, const int32_t *distinct,
+                                  const int32_t *count, int cap, const float *gate_up, size_t gate_up_stride,
+                                  int tokens, void *y, int y_dtype, void *workspace, size_t workspace_bytes,
+                                  void *stream);
 /* Grouped (MoE) GEMM on quantized activations; replaces
  * nvfp4_grouped_gemm_view (gemm/nvfp4.rs:209-264, kernel :56-107).  A holds
  * the prefill layout's padded_rows gathered rows (a multiple of 128: the
@@ -531,6 +559,17 @@ int fpb_gdn_delta(const float *conv_out, const float *a, const float *b, size_t 
  * out [batch, heads * dv]. */
 int fpb_gdn_gated_norm(const float *x, const float *z, size_t z_pitch, const float *gamma, size_t batch, size_t heads,
                        size_t dv, float eps, void *out, int out_dtype, void *stream);
+/* fpb_gdn_conv + fpb_gdn_delta + fpb_gdn_gated_norm in one launch (the GDN
+ * mixer after its projections): x [batch, x_pitch] the q/k/v projection,
+ * conv_state / conv_weight as fpb_gdn_conv, a / b / a_log / dt_bias / state
+ * as fpb_gdn_delta, z [batch, z_pitch] and gamma [dv] as fpb_gdn_gated_norm;
+ * out [batch, value_heads * dv].  dk = dv = 128, value_heads = 2 *
+ * key_heads and a conv kernel of 2..8 only (FPB_ERR_UNSUPPORTED otherwise:
+ * use the three calls).  Same results up to f32 summation order. */
+int fpb_gdn_step(const float *x, size_t x_pitch, float *conv_state, const float *conv_weight, size_t conv_kernel,
+                 const float *a, const float *b, size_t ab_pitch, const float *a_log, const float *dt_bias,
+                 float *state, const float *z, size_t z_pitch, const float *gamma, size_t batch, size_t key_heads,
+                 size_t value_heads, size_t dk, size_t dv, float eps, void *out, int out_dtype, void *stream);
 /* combine_add_norm_view (moe.rs:111-147) for decode: out[t] = residual[t] +
  * sum over slots s of weights[t, s] * routed[t * slots + s], normed =
  * RMSNorm(out) * gamma (f32 or bf16); slots <= 32. */
@@ -571,6 +610,14 @@ int fpb_nvfp4_expert_gemv_tokens(const fpb_nvfp4_matrix *w, const void *x, int x
  * [cap, tokens, hidden] (the moe GEMV's output layout); slots <= 32. */
 int fpb_moe_decode_plan(const int32_t *ids, size_t tokens, size_t width, size_t slots, size_t experts,
                         int32_t *distinct, int32_t *count, size_t cap, int32_t *map, void *stream);
+/* fpb_moe_topk followed by fpb_moe_decode_plan in one launch (decode-size
+ * batches: tokens <= 32, experts <= 512): the shared-expert gate logit, when
+ * gate_col >= 0, is column gate_col of each logits row (a router matrix with
+ * the gate row stacked under the experts' rows); the plan covers the top_k
+ * (+ 1 shared) slots with the shared expert as id `experts`. */
+int fpb_moe_decode_route(const float *logits, size_t ld, long long gate_col, size_t tokens, size_t experts,
+                         size_t top_k, size_t width, int32_t *ids, float *weights, int32_t *distinct,
+                         int32_t *count, size_t cap, int32_t *map, void *stream);
 int fpb_nvfp4_moe_gemv(const fpb_nvfp4_matrix *w, size_t rows_per_expert, const int32_t *distinct,
                        const int32_t *count, int cap, const void *x, int x_dtype, size_t x_stride, int tokens, void *y,
                        int y_dtype, void *stream);

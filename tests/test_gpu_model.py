@@ -20,12 +20,15 @@ def torch():
     return t
 
 
-@pytest.fixture(scope="module")
-def small(torch):
+@pytest.fixture(scope="module", params=[128, 256])
+def small(torch, request):
+    """moe_inter 128: the down projection on the streaming GEMV (K = 128),
+    SwiGLU output in bf16; 256: expert GEMVs on the tensor cores (digit
+    planes), SwiGLU in f32 inside the down projection's plane encoder."""
     from firepit_b200.model import HybridConfig, HybridModel
     cfg = HybridConfig(layers=4, hidden=256, vocab=512, full_attention_interval=2, q_heads=4, kv_heads=2,
                        head_dim=64, rotary_dim=16, key_heads=2, value_heads=4, key_head_dim=32, value_head_dim=32,
-                       experts=8, top_k=2, moe_inter=128)
+                       experts=8, top_k=2, moe_inter=request.param)
     return HybridModel(cfg, seed=3)
 
 
@@ -38,7 +41,7 @@ def _bf16(x):
     return O.bf16_to_f32(O.bf16_bits(np.asarray(x, np.float32))).astype(np.float64)
 
 
-def numpy_step(model, tokens, pos, state):
+def numpy_step(model, tokens, pos, state, round_act=True):
     """One decode step of every session, restated in numpy (f64 GEMVs on the
     dequantized NVFP4 weights, GEMV inputs rounded to bf16 as the device
     path feeds them)."""
@@ -87,8 +90,9 @@ def numpy_step(model, tokens, pos, state):
             delta = _bf16(out) @ _deq(L["w_o"]).T
         x = x + delta
         normed = _bf16(ln(x, L["post_norm"]))
-        logits = normed @ _deq(L["w_router"]).T
-        gate = normed @ _deq(L["w_shared_gate"]).T
+        route = _deq(L["w_route"])  # router rows, the gate row, zero rows
+        logits = normed @ route[:c.experts].T
+        gate = normed @ route[c.experts:c.experts + 1].T
         ids, w = O.moe_topk(logits.astype(np.float32), c.top_k, c.slots, gate.astype(np.float32))
         w1, w2 = _deq(L["w_gate_up"]), _deq(L["w_down"])
         moe = np.zeros_like(x)
@@ -96,7 +100,9 @@ def numpy_step(model, tokens, pos, state):
             for s in range(c.slots):
                 e = ids[b, s]
                 gu = normed[b] @ w1[e * 2 * c.moe_inter:(e + 1) * 2 * c.moe_inter].T
-                act = _bf16(gu[:c.moe_inter] * R.sigmoid(gu[:c.moe_inter]) * gu[c.moe_inter:])
+                act = gu[:c.moe_inter] * R.sigmoid(gu[:c.moe_inter]) * gu[c.moe_inter:]
+                if round_act:
+                    act = _bf16(act)
                 moe[b] += w[b, s] * (act @ w2[e * c.hidden:(e + 1) * c.hidden].T)
         x = x + moe
         nxt = model.layers[i + 1]["input_norm"] if i + 1 < len(model.layers) else model.final_norm
@@ -121,7 +127,7 @@ def test_decode_step_matches_numpy(torch, small):
         dec.tokens.copy_(torch.from_numpy(toks.astype(np.int32)))
         dec.step(torch.cuda.current_stream().cuda_stream)
         torch.cuda.synchronize()
-        want = numpy_step(small, toks, [t] * B, state)
+        want = numpy_step(small, toks, [t] * B, state, round_act=not dec.planes_down)
         got = dec.logits.cpu().numpy()
         assert O.rel_frobenius(got, want) <= 2e-3, f"step {t}"
         toks = (toks * 7 + 11) % c.vocab

@@ -187,6 +187,48 @@ def test_gdn_conv_delta_gated_norm(F, torch):
         assert np.allclose(g_out.cpu().numpy()[b], want.reshape(-1), rtol=1e-5, atol=1e-6)
 
 
+@pytest.mark.parametrize("B,hk,kern", [(2, 4, 4), (8, 16, 4), (3, 2, 2), (1, 1, 8)])
+def test_gdn_step_equals_conv_delta_gated_norm(F, torch, B, hk, kern):
+    """fpb_gdn_step (one launch) against the oracle's conv, delta rule and
+    gated norm chained in f64, and the three entries' state updates."""
+    N = F._native
+    hv, dk, dv = 2 * hk, 128, 128
+    conv_dim = 2 * hk * dk + hv * dv
+    x = _rand(torch, B, conv_dim, seed=31)
+    cst = _rand(torch, B, conv_dim, kern - 1, seed=32)
+    w = _rand(torch, conv_dim, kern, seed=33, scale=0.3)
+    a = _rand(torch, B, hv, seed=34)
+    bg = _rand(torch, B, hv, seed=35)
+    a[0, 0] = -20.0  # the series branch of the softplus
+    a_log = torch.log(1.0 + 15.0 * torch.rand(hv, device="cuda"))
+    dt = _rand(torch, hv, seed=36, scale=0.5)
+    S = _rand(torch, B, hv, dk, dv, seed=37, scale=0.1)
+    z = _rand(torch, B, hv * dv, seed=38)
+    gamma = _rand(torch, dv, seed=39, scale=0.1) + 1
+    c0, S0 = cst.cpu().numpy().copy(), S.cpu().numpy().copy()
+    out = torch.empty(B, hv * dv, device="cuda")
+    N.call("fpb_gdn_step", x.data_ptr(), conv_dim, cst.data_ptr(), w.data_ptr(), kern, a.data_ptr(), bg.data_ptr(),
+           hv, a_log.data_ptr(), dt.data_ptr(), S.data_ptr(), z.data_ptr(), hv * dv, gamma.data_ptr(), B, hk, hv, dk,
+           dv, 1e-6, out.data_ptr(), N.FPB_F32, None)
+    torch.cuda.synchronize()
+    assert F.device_error() == 0
+    for b in range(B):
+        co, ns = R.conv1d_silu(x.cpu().numpy()[b], c0[b], w.cpu().numpy())
+        assert np.array_equal(cst.cpu().numpy()[b], ns)
+        q = co[:hk * dk].reshape(hk, dk)
+        k = co[hk * dk:2 * hk * dk].reshape(hk, dk)
+        v = co[2 * hk * dk:].reshape(hv, dv)
+        o, nS = R.delta_step(q, k, v, bg.cpu().numpy()[b], a.cpu().numpy()[b], a_log.cpu().numpy(), dt.cpu().numpy(),
+                             S0[b], 1e-6, hk)
+        assert O.rel_frobenius(S.cpu().numpy()[b], nS) <= 1e-5
+        want = R.gated_norm(o.astype(np.float32), z.cpu().numpy()[b].reshape(hv, dv), gamma.cpu().numpy(), 1e-6)
+        assert O.rel_frobenius(out.cpu().numpy()[b], want.reshape(-1)) <= 1e-5
+    bad = N.lib.fpb_gdn_step(x.data_ptr(), conv_dim, cst.data_ptr(), w.data_ptr(), kern, a.data_ptr(), bg.data_ptr(),
+                             hv, a_log.data_ptr(), dt.data_ptr(), S.data_ptr(), z.data_ptr(), hv * dv, gamma.data_ptr(),
+                             B, hk, hk, dk, dv, 1e-6, out.data_ptr(), N.FPB_F32, None)
+    assert bad == N.FPB_ERR_UNSUPPORTED  # one value head per key head
+
+
 def test_combine_argmax_and_expert_tokens(F, torch):
     N = F._native
     T, slots, h, vocab = 4, 11, 256, 5000

@@ -233,3 +233,48 @@ def test_topk_plan_moe_gemv_in_one_graph(F, torch):
                                                np.array([want_ids[t, s_]], np.int32), rpe, 0, xf[t:t + 1])
                 assert O.rel_frobenius(yc[u, t:t + 1], want) <= REL_FROB_TOL
     assert F.device_error() == 0
+
+
+@pytest.mark.parametrize("T,experts,k,gate", [(8, 512, 10, True), (1, 512, 10, True), (32, 128, 4, False),
+                                              (5, 40, 8, True), (16, 512, 10, False)])
+def test_fused_route_equals_topk_then_plan(F, torch, T, experts, k, gate):
+    """fpb_moe_decode_route (gate logit as a column of the router output) ==
+    fpb_moe_topk (gate as its own array) followed by fpb_moe_decode_plan."""
+    N = F._native
+    ld = (experts + 1 + 3) // 4 * 4
+    rng = np.random.default_rng(T * 7 + experts)
+    lg = rng.standard_normal((T, ld)).astype(np.float32)
+    lg[0, 3] = lg[0, 5]  # a tie: the lower id first
+    logits = torch.from_numpy(lg).cuda()
+    slots = k + (1 if gate else 0)
+    width = slots
+    cap = T * slots
+    g = torch.from_numpy(np.ascontiguousarray(lg[:, experts])).cuda()
+    ids_a = torch.full((T, width), -7, dtype=torch.int32, device="cuda")
+    w_a = torch.zeros(T, width, device="cuda")
+    N.call("fpb_moe_topk", logits.data_ptr(), ld, g.data_ptr() if gate else None, T, experts, k, width,
+           ids_a.data_ptr(), w_a.data_ptr(), None)
+    d_a = torch.zeros(cap, dtype=torch.int32, device="cuda")
+    c_a = torch.zeros(1, dtype=torch.int32, device="cuda")
+    m_a = torch.zeros(cap, dtype=torch.int32, device="cuda")
+    N.call("fpb_moe_decode_plan", ids_a.data_ptr(), T, width, slots, experts + (1 if gate else 0), d_a.data_ptr(),
+           c_a.data_ptr(), cap, m_a.data_ptr(), None)
+    ids_b = torch.full((T, width), -7, dtype=torch.int32, device="cuda")
+    w_b = torch.zeros(T, width, device="cuda")
+    d_b = torch.full((cap,), 99, dtype=torch.int32, device="cuda")
+    c_b = torch.zeros(1, dtype=torch.int32, device="cuda")
+    m_b = torch.full((cap,), 99, dtype=torch.int32, device="cuda")
+    N.call("fpb_moe_decode_route", logits.data_ptr(), ld, experts if gate else -1, T, experts, k, width,
+           ids_b.data_ptr(), w_b.data_ptr(), d_b.data_ptr(), c_b.data_ptr(), cap, m_b.data_ptr(), None)
+    torch.cuda.synchronize()
+    assert torch.equal(ids_a, ids_b)
+    assert torch.equal(w_a, w_b)
+    assert int(c_a.item()) == int(c_b.item())
+    assert torch.equal(d_a, d_b) and torch.equal(m_a, m_b)
+    want_ids, want_w = O.moe_topk(lg[:, :experts], k, width, lg[:, experts] if gate else None)
+    assert np.array_equal(ids_b.cpu().numpy(), want_ids)
+    assert np.allclose(w_b.cpu().numpy(), want_w, rtol=2e-6, atol=1e-7)
+    assert F.device_error() == 0
+    bad = N.lib.fpb_moe_decode_route(logits.data_ptr(), ld, -1, 33, experts, k, k, ids_b.data_ptr(), w_b.data_ptr(),
+                                     d_b.data_ptr(), c_b.data_ptr(), 33 * k, m_b.data_ptr(), None)
+    assert bad == N.FPB_ERR_SHAPE

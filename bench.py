@@ -196,8 +196,9 @@ MAX_SEGS = 128  # fpb_nvfp4_gemv_batched's segments per launch
 def gemv_config(g: int) -> dict:
     return {"workload": "config0 NVFP4 GEMV 4096x4096 (x bf16 [1,4096] N(0,1), y bf16)",
             "matrices_per_step": MATS_PER_GPU * g, "rows_per_rank": ROWS // g,
-            "launch": f"each rank's slices of the {MATS_PER_GPU * g} matrices in batched launches of at most "
-                      f"{MAX_SEGS} (fpb_nvfp4_gemv_batched), every matrix with its own x row",
+            "launch": f"each rank's slices of the {MATS_PER_GPU * g} matrices in one prepared batch per "
+                      f"{MAX_SEGS} (fpb_nvfp4_gemv_batch_run: x as NVFP4 digit planes, tcgen05), every matrix "
+                      "with its own x row",
             "parallelism": f"N-split x{g} + NCCL all-gather after each launch" if g > 1 else "single GPU",
             "l2": "inputs larger than L2: 605 MB of distinct weights per rank per step",
             "timing": "CUDA graph replay per launch, CUDA events, max over ranks"}
@@ -318,13 +319,25 @@ def ours_arm(args):
     groups = [range(i, min(i + MAX_SEGS, mats)) for i in range(0, mats, MAX_SEGS)]
     y_all = [torch.empty(g, len(gr), rows_per_rank, dtype=torch.bfloat16, device=dev) for gr in groups]
 
-    def batched(xsrc):
-        return [F.gemv_batched([(slices[c], xsrc[c:c + 1], y_local[c:c + 1]) for c in gr]) for gr in groups]
+    def batched(xsrc, tensor_cores=True):
+        """The step's GEMVs, one batch per group of matrices: on the tensor
+        cores (x as NVFP4 digit planes, tcgen05) where the shapes allow, else
+        the streaming kernel."""
+        make = F.gemv_batch_planes if tensor_cores else F.gemv_batched
+        return [make([(slices[c], xsrc[c:c + 1], y_local[c:c + 1]) for c in gr]) for gr in groups]
 
-    launches_b = batched(x)
+    try:
+        launches_b = batched(x)
+        tensor_cores = True
+    except F.ShapeError:
+        launches_b = batched(x, tensor_cores=False)
+        tensor_cores = False
 
     def launch(i, sh):
-        N_.call("fpb_nvfp4_gemv_batched", launches_b[i]._segs, len(groups[i]), BF, BF, 1, sh)
+        if tensor_cores:
+            N_.call("fpb_nvfp4_gemv_batch_run", launches_b[i]._batch, sh)
+        else:
+            N_.call("fpb_nvfp4_gemv_batched", launches_b[i]._segs, len(groups[i]), BF, BF, 1, sh)
 
     s = torch.cuda.Stream(device=dev)
     with torch.cuda.stream(s):  # every code path initialised outside capture
@@ -396,6 +409,31 @@ def ours_arm(args):
     single_launch_ms = ts.item() / (single_steps * single_n)
     del gs
 
+    # ---- the same batch on the streaming CUDA-core kernel (fpb_nvfp4_gemv_batched) --
+    stream_b = batched(x, tensor_cores=False)
+
+    def streaming(sh):
+        for i in range(len(groups)):
+            N_.call("fpb_nvfp4_gemv_batched", stream_b[i]._segs, len(groups[i]), BF, BF, 1, sh)
+
+    with torch.cuda.stream(s):
+        streaming(s.cuda_stream)
+    torch.cuda.synchronize()
+    gsb = graph_of(torch, streaming, s)
+    for _ in range(3):
+        gsb.replay()
+    torch.cuda.synchronize()
+    s0.record()
+    for _ in range(single_steps):
+        gsb.replay()
+    s1.record()
+    torch.cuda.synchronize()
+    tsb = torch.tensor([s0.elapsed_time(s1)], device=dev, dtype=torch.float64)
+    if g > 1:
+        dist.all_reduce(tsb, op=dist.ReduceOp.MAX)
+    streaming_step_ms = tsb.item() / single_steps
+    del gsb
+
     # ---- end to end through the public API, host buffers ----------------------
     # The reference's Graph sink (sink.rs:94-105): one CUDA graph holds the
     # copy of x from pinned host memory, the batched GEMV submits and (one
@@ -404,7 +442,7 @@ def ours_arm(args):
     xh.copy_(x.cpu())
     yh = torch.empty(g, mats, rows_per_rank, dtype=torch.bfloat16, pin_memory=True)
     xd = torch.empty_like(x)
-    e2e_b = batched(xd)
+    e2e_b = batched(xd, tensor_cores)
     for b in e2e_b:  # eager once: every code path initialised outside capture
         b.submit(F.Async())
     torch.cuda.synchronize()
@@ -447,7 +485,8 @@ def ours_arm(args):
     single_achieved = slice_bytes / (single_launch_ms * 1e-3) / 1e9
     traffic = None
     if g == 1:
-        per_matrix = load_traffic("gemv_nvfp4_batched_config0_traffic.txt")
+        per_matrix = load_traffic("gemv_nvfp4_planes_config0_traffic.txt" if tensor_cores
+                                  else "gemv_nvfp4_batched_config0_traffic.txt")
         traffic = per_matrix * len(groups[0]) if per_matrix else None
     out = None
     if rank == 0:
@@ -462,11 +501,19 @@ def ours_arm(args):
                          "peak_kind": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)" if peak_kind == "measured"
                          else "fallback 6650 GB/s",
                          "per_launch_us": per_launch_ms * 1e3, "algorithmic_bytes_per_launch": launch_bytes,
-                         "note": "dominant kernel gemv_nvfp4_stream_kernel; one launch = the rank's slices of "
-                                 f"{len(groups[0])} matrices; traffic = ncu DRAM bytes per matrix x matrices"},
+                         "note": ("dominant kernel nvfp4_gemm_kernel in planes mode (x as 8 NVFP4 digit planes, "
+                                  "tcgen05 mxf4nvf4), after planes_encode_kernel" if tensor_cores else
+                                  "dominant kernel gemv_nvfp4_stream_kernel") +
+                                 f"; one launch = the rank's slices of {len(groups[0])} matrices; the time per "
+                                 "launch includes the plane encode; traffic = ncu DRAM bytes per matrix x matrices"},
             "single_gemv": {"per_launch_us": single_launch_ms * 1e3, "achieved_gbs": single_achieved,
                             "frac": single_achieved / peak,
                             "note": f"{single_n} fpb_nvfp4_gemv launches (one matrix slice each) in one CUDA graph"},
+            "streaming_batched": {"ms_per_step": streaming_step_ms,
+                                  "achieved_gbs": launch_bytes * len(groups) / (streaming_step_ms * 1e-3) / 1e9,
+                                  "frac": launch_bytes * len(groups) / (streaming_step_ms * 1e-3) / 1e9 / peak,
+                                  "note": "the same step on the CUDA-core streaming kernel (fpb_nvfp4_gemv_batched)"},
+            "gemv_path": "tensor cores (fpb_nvfp4_gemv_batch_run)" if tensor_cores else "streaming",
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": mats * COLS * 2,
                     "d2h_bytes_per_step": g * mats * rows_per_rank * 2,
                     "path": "firepit_b200.gemv_batched(...).submit(Graph sink): H2D x, the batched GEMVs and D2H y "

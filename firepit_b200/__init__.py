@@ -7,8 +7,8 @@ the library is missing: there is no CPU fallback.
 """
 from . import _native
 from ._native import FpbError, launch_count
-from .gemv import (DEFAULT_GEMV_TILE, BatchedGemv, ExpertGemvView, Gemv, GemvTile, ShapeError,
-                   expert_gemv_weight_view, fp8_tile, gemv, gemv_batched, row_scaled_tile)
+from .gemv import (DEFAULT_GEMV_TILE, BatchedGemv, ExpertGemvView, Gemv, GemvTile, PlanesGemvBatch, ShapeError,
+                   expert_gemv_weight_view, fp8_tile, gemv, gemv_batch_planes, gemv_batched, row_scaled_tile)
 from .moe import (ExpertSelection, ExpertSelectionError, MoeDimensionError, MoeDims, PrefillLayout, PrefillPlan,
                   layout_scratch,
                   combine, combine_add_norm_prefill, combine_add_norm_view, combine_prefill, gather_prefill_view,

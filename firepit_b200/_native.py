@@ -167,6 +167,9 @@ SIGNATURES: dict[str, tuple] = {
     "fpb_nvfp4_gemv_planes": (i32, [vp, sz, sz, vp, i32, i32, vp, i32, vp, sz, vp]),
     "fpb_nvfp4_moe_gemv_planes": (i32, [vp, sz, vp, vp, i32, vp, i32, sz, i32, vp, i32, vp, sz, vp]),
     "fpb_nvfp4_moe_gemv_planes_glu": (i32, [vp, sz, vp, vp, i32, vp, sz, i32, vp, i32, vp, sz, vp]),
+    "fpb_nvfp4_gemv_batch_create": (i32, [vp, i32, i32, i32, i32, vp, C.POINTER(vp)]),
+    "fpb_nvfp4_gemv_batch_run": (i32, [vp, vp]),
+    "fpb_nvfp4_gemv_batch_destroy": (i32, [vp]),
     "fpb_gdn_step": (i32, [vp, sz, vp, vp, sz, vp, vp, sz, vp, vp, vp, vp, sz, vp, sz, sz, sz, sz, sz, C.c_float, vp,
                            i32, vp]),
     "fpb_moe_decode_route": (i32, [vp, sz, C.c_longlong, sz, sz, sz, sz, vp, vp, vp, vp, sz, vp, vp]),

@@ -116,6 +116,21 @@ __global__ void act_encode_kernel(const T *x, size_t rows, size_t cols, const ui
   }
 }
 
+// One matrix of a prepared tensor-core GEMV batch (device table, built at
+// load time): weight rows [row_begin, row_begin + rows) of one handle times
+// its own x [batch, K], into y [batch, rows].  The tensor map lives in
+// global memory (64-byte aligned), which TMA reads like a parameter.
+struct alignas(64) PlaneSeg {
+  CUtensorMap tmap_b;       // the handle's codes (box 128 rows x 128 bytes)
+  const uint8_t *b_sf;      // the handle's tiled factors
+  const float *b_globals;   // the handle's row globals, row 0
+  const void *x;
+  void *y;
+  int row_begin, rows;
+  int item_begin;           // first item (128-row tile) of this segment
+  int pad_;
+};
+
 // ---- x as NVFP4 digit planes (tensor-core GEMV) ----------------------------------------
 // Row t of x (K values) becomes kPlanes NVFP4 rows: plane 0 encodes x with
 // the config-0 rule (global g0 = amax / 2688, e4m3 factors per 16 values,
@@ -142,12 +157,13 @@ template <typename T, bool GLU>
 __global__ void __launch_bounds__(kPlaneThreads) planes_encode_kernel(const T *x, long long x_group_stride,
                                                                       int tokens, int K, const int32_t *live_groups,
                                                                       uint8_t *packed, uint8_t *sf_tiled,
-                                                                      float *ga) {
+                                                                      float *ga, const PlaneSeg *segs) {
   pdl_enter();
   __shared__ uint32_t red[32];
   const int g = blockIdx.x / tokens, t = blockIdx.x % tokens;
   if (live_groups && g >= *live_groups) return;  // a group nothing reads (uniform)
-  const T *xr = x + (long long)g * x_group_stride + (long long)t * K * (GLU ? 2 : 1);
+  const T *xg = segs ? static_cast<const T *>(segs[g].x) : x + (long long)g * x_group_stride;
+  const T *xr = xg + (long long)t * K * (GLU ? 2 : 1);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int groups = K / kNvfp4Group;
   uint32_t m = 0;
@@ -252,6 +268,11 @@ struct GemmParams {
   int moe_cap;
   int a_group_step;
   long long y_group_stride;
+  // Planes mode over a prepared batch: items are the segments' 128-row tiles
+  // in order (segment s from segs[s].item_begin), A group s = segment s.
+  const PlaneSeg *segs;
+  int nseg;
+  int total_items;
   // Rows of each A box tmap_a loads (planes: the tokens' 8 * tokens plane
   // rows; the tile's other rows keep whatever the stage held and only feed
   // accumulator rows nothing reads).  128 otherwise.
@@ -291,7 +312,24 @@ struct MoeIdsCache {
 };
 
 __device__ __forceinline__ bool gemm_tile(const GemmParams &p, int t, int n_tiles, int &m_tile, int &n_tile,
-                                          int &n_base, const MoeIdsCache *moe = nullptr) {
+                                          int &n_base, const MoeIdsCache *moe = nullptr,
+                                          const PlaneSeg **seg = nullptr) {
+  if (p.segs) {
+    // the segment whose items hold t (item starts cached in moe->ids)
+    int lo = 0, hi = p.nseg - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (moe->ids[mid] <= t)
+        lo = mid;
+      else
+        hi = mid - 1;
+    }
+    if (seg) *seg = p.segs + lo;
+    m_tile = lo;
+    n_tile = t - moe->ids[lo];
+    n_base = p.segs[lo].row_begin;
+    return true;
+  }
   m_tile = t / n_tiles;
   n_tile = t - m_tile * n_tiles;
   n_base = p.n_base;
@@ -346,7 +384,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_tiles = (p.N + kBN - 1) / kBN;
   const int m_tiles = p.planes ? (p.moe_ids ? p.moe_cap : 1) : (p.M + kBM - 1) / kBM;
-  const int total = n_tiles * m_tiles;
+  const int total = p.segs ? p.total_items : n_tiles * m_tiles;
   const int kb64_per_rb = p.kb_count * 4;
   // K blocks as the producer and the MMA issuer walk them (bf16 mode: each
   // block once per (A, B) pass).
@@ -386,6 +424,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int i = threadIdx.x; i < min(live, kMoeIdsCached); i += blockDim.x) moe_cache.ids[i] = p.moe_ids[i];
     if (threadIdx.x == 0) moe_cache.count = live;
     __syncthreads();
+  } else if (p.segs) {  // the segments' first items (nseg <= kMoeIdsCached, checked by the host)
+    for (int i = threadIdx.x; i < p.nseg; i += blockDim.x) moe_cache.ids[i] = p.segs[i].item_begin;
+    __syncthreads();
   }
 
   if (warp == 0) {
@@ -395,8 +436,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       bool ok = true;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
         int m_tile, n_tile, n_base;
-        if (!gemm_tile(p, t, n_tiles, m_tile, n_tile, n_base, &moe_cache)) continue;
+        const PlaneSeg *sg = nullptr;
+        if (!gemm_tile(p, t, n_tiles, m_tile, n_tile, n_base, &moe_cache, &sg)) continue;
         const int nb_global = n_base / 128 + n_tile;
+        const CUtensorMap *tb = sg ? &sg->tmap_b : &tmap_b;
+        const uint8_t *bsf = sg ? sg->b_sf : p.b_sf;
         for (int vb = 0; vb < vblocks; ++vb, ++it) {
           const int s = it % kStages;
           if (it >= kStages && !mbar_wait(&empty[s], ((it / kStages) - 1) & 1, abort_s)) {
@@ -422,11 +466,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             tma_load_2d(sB + s * kTileBytes + kTileBytes / 2, &tmap_b64, kb * kBKBytes, row_gate + p.N / 2,
                         &full[s]);
           } else {
-            tma_load_2d(sB + s * kTileBytes, &tmap_b, kb * kBKBytes, n_base + n_tile * kBN, &full[s]);
+            tma_load_2d(sB + s * kTileBytes, tb, kb * kBKBytes, n_base + n_tile * kBN, &full[s]);
           }
           bulk_load(sSFA + s * kSfStageBytes, p.a_sf + ((size_t)m_tile * kb64_per_rb + kb * 4) * kSfChunk,
                     kSfStageBytes, &full[s]);
-          bulk_load(sSFB + s * kSfStageBytes, p.b_sf + ((size_t)nb_global * kb64_per_rb + kb * 4) * kSfChunk,
+          bulk_load(sSFB + s * kSfStageBytes, bsf + ((size_t)nb_global * kb64_per_rb + kb * 4) * kSfChunk,
                     kSfStageBytes, &full[s]);
         }
       }
@@ -506,8 +550,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint32_t glu_max = 0;  // glu: this lane's max |h| bits over its live rows and tiles
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       int m_tile, n_tile, n_base;
-      if (!gemm_tile(p, t, n_tiles, m_tile, n_tile, n_base, &moe_cache)) continue;
+      const PlaneSeg *sg = nullptr;
+      if (!gemm_tile(p, t, n_tiles, m_tile, n_tile, n_base, &moe_cache, &sg)) continue;
       const uint32_t buf = lt & 1;
+      const int n_lim = sg ? sg->rows : p.N;                        // rows of this item's view
+      const float *bglob = sg ? sg->b_globals : p.b_globals;
       // What the tile's epilogue reads from memory besides the accumulator
       // (the rows' tokens, the weight rows' globals) is loaded before the
       // wait, so its latency hides behind the main loop.
@@ -525,7 +572,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           const int n = n0 + ch * 64 + c * 32 + lane;
-          gl[c] = n < p.N ? (p.b_globals ? __ldg(p.b_globals + n_base + n) : 1.0f) : 0.0f;
+          gl[c] = n < n_lim ? (bglob ? __ldg(bglob + n_base + n) : 1.0f) : 0.0f;
         }
       }
       if (!mbar_wait(&acc_full[buf], (lt >> 1) & 1, abort_s)) {
@@ -592,15 +639,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                       __shfl_sync(0xffffffffu, gl[c], 8 * i + pl);
           }
           if (token < p.tokens) {
-            const long long ybase = (long long)item_group * p.y_group_stride + (long long)token * p.ldy;
+            void *ydst = sg ? sg->y : p.y;
+            const long long ybase = sg ? (long long)token * sg->rows
+                                       : (long long)item_group * p.y_group_stride + (long long)token * p.ldy;
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
               const int n = nw + c * 32 + i * 8 + pl;
-              if (n < p.N) {
+              if (n < n_lim) {
                 if (p.y_bf16)
-                  reinterpret_cast<__nv_bfloat16 *>(p.y)[ybase + n] = __float2bfloat16_rn(keep[i]);
+                  reinterpret_cast<__nv_bfloat16 *>(ydst)[ybase + n] = __float2bfloat16_rn(keep[i]);
                 else
-                  reinterpret_cast<float *>(p.y)[ybase + n] = keep[i];
+                  reinterpret_cast<float *>(ydst)[ybase + n] = keep[i];
               }
             }
           }
@@ -1072,13 +1121,13 @@ static int run_planes(const char *fn, fpb_nvfp4_matrix *w, size_t n_base, size_t
   const int32_t *live = moe_ids ? moe_count : nullptr;
   cudaError_t e =
       glu ? launch_pdl(planes_encode_kernel<float, true>, enc_grid, kPlaneThreads, 0, s, static_cast<const float *>(x),
-                       (long long)x_group_stride, tokens, (int)K, live, packed, sf, ga)
+                       (long long)x_group_stride, tokens, (int)K, live, packed, sf, ga, nullptr)
       : x_dtype == FPB_F32
           ? launch_pdl(planes_encode_kernel<float, false>, enc_grid, kPlaneThreads, 0, s,
-                       static_cast<const float *>(x), (long long)x_group_stride, tokens, (int)K, live, packed, sf, ga)
+                       static_cast<const float *>(x), (long long)x_group_stride, tokens, (int)K, live, packed, sf, ga, nullptr)
           : launch_pdl(planes_encode_kernel<uint16_t, false>, enc_grid, kPlaneThreads, 0, s,
                        static_cast<const uint16_t *>(x), (long long)x_group_stride, tokens, (int)K, live, packed, sf,
-                       ga);
+                       ga, nullptr);
   if (e != cudaSuccess) return cuda_fail(e, "planes_encode_kernel");
   FPB_LAUNCH_CHECK("planes_encode_kernel");
   CUtensorMap tmap_a;
@@ -1169,6 +1218,136 @@ extern "C" int fpb_nvfp4_moe_gemv_planes_glu(fpb_nvfp4_matrix *w, size_t rows_pe
                     tokens, (size_t)cap, distinct, count, cap, (int)(w->rows / rows_per_expert), y, y_dtype,
                     (long long)tokens * (long long)rows_per_expert, (long long)rows_per_expert, workspace,
                     workspace_bytes, as_stream(stream));
+}
+
+// ---- prepared tensor-core GEMV batch (fpb_nvfp4_gemv_batch_*) ------------------------
+struct fpb_gemv_batch {
+  fpb::PlaneSeg *segs = nullptr;  // device table
+  CUtensorMap tmap_a{};           // the planes' codes
+  CUtensorMap tmap_b0{};          // segment 0's weights (a valid map for the unused parameter)
+  void *ws = nullptr;             // planes workspace
+  int count = 0, batch = 0, K = 0, x_dtype = 0, y_dtype = 0, total_items = 0;
+};
+
+extern "C" int fpb_nvfp4_gemv_batch_create(const fpb_gemv_segment *segs, int count, int x_dtype, int y_dtype,
+                                           int batch, void *stream, fpb_gemv_batch **out) {
+  if (!segs || !out) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_gemv_batch_create: null pointer");
+  *out = nullptr;
+  if (count < 1 || count > kMoeIdsCached)
+    return fail(FPB_ERR_SHAPE, "fpb_nvfp4_gemv_batch_create: count %d not in [1, %d]", count, kMoeIdsCached);
+  if ((x_dtype != FPB_F32 && x_dtype != FPB_BF16) || (y_dtype != FPB_F32 && y_dtype != FPB_BF16))
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_gemv_batch_create: dtype");
+  if (batch < 1 || batch > 16) return fail(FPB_ERR_SHAPE, "fpb_nvfp4_gemv_batch_create: batch %d not in [1, 16]", batch);
+  if (!segs[0].w) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_gemv_batch_create: null matrix");
+  const size_t K = segs[0].w->cols;
+  if (K % 256 || K > (size_t)kPlaneMaxK)
+    return fail(FPB_ERR_UNSUPPORTED, "fpb_nvfp4_gemv_batch_create: cols %zu must be a multiple of 256 and at most %d",
+                K, kPlaneMaxK);
+  std::vector<PlaneSeg> host((size_t)count);
+  int items = 0;
+  for (int i = 0; i < count; ++i) {
+    const fpb_gemv_segment &sg = segs[i];
+    if (!sg.w || !sg.x || !sg.y)
+      return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_gemv_batch_create: null pointer in segment %d", i);
+    if (sg.w->cols != K)
+      return fail(FPB_ERR_SHAPE, "fpb_nvfp4_gemv_batch_create: segment %d has %zu columns, segment 0 has %zu", i,
+                  sg.w->cols, K);
+    const size_t end = sg.row_end ? sg.row_end : sg.w->rows;
+    if (sg.row_begin >= end || end > sg.w->rows || end - sg.row_begin > 0x7fffffff)
+      return fail(FPB_ERR_SHAPE, "fpb_nvfp4_gemv_batch_create: segment %d row range [%zu, %zu) outside %zu rows", i,
+                  sg.row_begin, end, sg.w->rows);
+    if (sg.row_begin % kBN)
+      return fail(FPB_ERR_UNSUPPORTED, "fpb_nvfp4_gemv_batch_create: segment %d row_begin %zu not a multiple of %d",
+                  i, sg.row_begin, kBN);
+    if (int st = require_prepared(sg.w, "fpb_nvfp4_gemv_batch_create")) return st;
+    PlaneSeg &d = host[(size_t)i];
+    std::memcpy(&d.tmap_b, sg.w->extras->tmap_b, sizeof(CUtensorMap));
+    d.b_sf = sg.w->extras->sf_tiled;
+    d.b_globals = sg.w->row_globals;
+    d.x = sg.x;
+    d.y = sg.y;
+    d.row_begin = (int)sg.row_begin;
+    d.rows = (int)(end - sg.row_begin);
+    d.item_begin = items;
+    items += (d.rows + kBN - 1) / kBN;
+  }
+  if (int st = ensure_gemm_attr()) return st;
+  fpb_gemv_batch *b = new fpb_gemv_batch();
+  b->count = count;
+  b->batch = batch;
+  b->K = (int)K;
+  b->x_dtype = x_dtype;
+  b->y_dtype = y_dtype;
+  b->total_items = items;
+  std::memcpy(&b->tmap_b0, segs[0].w->extras->tmap_b, sizeof(CUtensorMap));
+  cudaStream_t s = as_stream(stream);
+  const size_t ws_bytes = fpb_nvfp4_gemv_planes_workspace_bytes((size_t)count, K);
+  cudaError_t e = cudaMalloc(reinterpret_cast<void **>(&b->segs), sizeof(PlaneSeg) * (size_t)count);
+  if (e == cudaSuccess) e = cudaMalloc(&b->ws, ws_bytes);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(b->segs, host.data(), sizeof(PlaneSeg) * (size_t)count, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) {
+    cudaFree(b->segs);
+    cudaFree(b->ws);
+    delete b;
+    return cuda_fail(e, "fpb_nvfp4_gemv_batch_create");
+  }
+  if (int st = encode_rows_u8(&b->tmap_a, b->ws, (uint64_t)count * kBM, K / 2, (uint32_t)(batch * kPlanes))) {
+    cudaFree(b->segs);
+    cudaFree(b->ws);
+    delete b;
+    return st;
+  }
+  *out = b;
+  return FPB_OK;
+}
+
+extern "C" int fpb_nvfp4_gemv_batch_run(const fpb_gemv_batch *b, void *stream) {
+  if (!b) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_gemv_batch_run: null handle");
+  cudaStream_t s = as_stream(stream);
+  const size_t K = (size_t)b->K, rows = (size_t)b->count * kBM;
+  uint8_t *packed = static_cast<uint8_t *>(b->ws);
+  uint8_t *sf = packed + align256(rows * K / 2);
+  float *ga = reinterpret_cast<float *>(sf + align256(sf_tiled_bytes(rows, K)));
+  const unsigned enc_grid = (unsigned)(b->count * b->batch);
+  cudaError_t e = b->x_dtype == FPB_F32
+      ? launch_pdl(planes_encode_kernel<float, false>, enc_grid, kPlaneThreads, 0, s, static_cast<const float *>(nullptr),
+                   0LL, b->batch, b->K, static_cast<const int32_t *>(nullptr), packed, sf, ga,
+                   static_cast<const PlaneSeg *>(b->segs))
+      : launch_pdl(planes_encode_kernel<uint16_t, false>, enc_grid, kPlaneThreads, 0, s,
+                   static_cast<const uint16_t *>(nullptr), 0LL, b->batch, b->K, static_cast<const int32_t *>(nullptr),
+                   packed, sf, ga, static_cast<const PlaneSeg *>(b->segs));
+  if (e != cudaSuccess) return cuda_fail(e, "planes_encode_kernel");
+  FPB_LAUNCH_CHECK("planes_encode_kernel");
+  GemmParams p{};
+  p.a_box_rows = b->batch * kPlanes;
+  p.a_sf = sf;
+  p.y_bf16 = b->y_dtype == FPB_BF16;
+  p.M = (int)rows;
+  p.N = kBN;  // per segment in the kernel
+  p.kb_count = b->K / 256;
+  p.error = device_error_ptr();
+  p.planes = 1;
+  p.tokens = b->batch;
+  p.a_globals = ga;
+  p.segs = b->segs;
+  p.nseg = b->count;
+  p.total_items = b->total_items;
+  const unsigned grid = (unsigned)std::min<size_t>((size_t)b->total_items, (size_t)std::max(1, sm_count()));
+  e = launch_pdl(nvfp4_gemm_kernel, grid, kGemmThreads, kGemmSmem, s, b->tmap_a, b->tmap_b0, b->tmap_a, b->tmap_b0,
+                 b->tmap_a, p);
+  if (e != cudaSuccess) return cuda_fail(e, "nvfp4_gemm_kernel (batch)");
+  FPB_LAUNCH_CHECK("nvfp4_gemm_kernel");
+  return FPB_OK;
+}
+
+extern "C" int fpb_nvfp4_gemv_batch_destroy(fpb_gemv_batch *b) {
+  if (!b) return FPB_OK;
+  cudaFree(b->segs);
+  cudaFree(b->ws);
+  delete b;
+  return FPB_OK;
 }
 
 extern "C" int fpb_nvfp4_grouped_gemm_q(fpb_nvfp4_matrix *w, const uint8_t *a_packed, const uint8_t *a_sf_tiled,

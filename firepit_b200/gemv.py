@@ -8,6 +8,7 @@ tile argument is validated the way the reference asserts it
 """
 from __future__ import annotations
 
+import ctypes as C
 from dataclasses import dataclass
 
 from . import _native as N
@@ -159,6 +160,47 @@ class BatchedGemv:
 def gemv_batched(members, tile: GemvTile = DEFAULT_GEMV_TILE) -> BatchedGemv:
     """members: ``(weight, x, y)`` or ``(weight, x, y, rows)`` tuples."""
     return BatchedGemv(members, tile)
+
+
+class PlanesGemvBatch(BatchedGemv):
+    """The members of a ``BatchedGemv`` on the tensor cores
+    (fpb_nvfp4_gemv_batch_*): x as 8 NVFP4 digit planes against each
+    member's weight rows with tcgen05, every member in one launch.  The
+    member tensors are bound at construction (a device table is built and
+    the stream synchronised), so ``submit`` reads nothing on the host and can
+    be recorded by a Graph sink; results equal ``gemv`` up to f32 rounding.
+    Needs cols % 256 == 0, cols <= 4096 and rows starting at multiples of
+    128 (ShapeError otherwise: use ``gemv_batched``)."""
+
+    def __init__(self, members, tile: GemvTile = DEFAULT_GEMV_TILE):
+        super().__init__(members, tile)
+        first = self.gemvs[0]
+        h = C.c_void_p()
+        st = N.lib.fpb_nvfp4_gemv_batch_create(self._segs, len(self.gemvs), _dtype_code(first.x),
+                                                _dtype_code(first.y), first.x.shape[0],
+                                                current_stream_handle(first.x.device), C.byref(h))
+        if st == N.FPB_ERR_UNSUPPORTED or st == N.FPB_ERR_SHAPE:
+            raise ShapeError(N.last_error())
+        N.check(st, "fpb_nvfp4_gemv_batch_create")
+        self._batch = h
+
+    def submit(self, sink: Sink | None = None) -> None:
+        sink = sink or Eager()
+        sink.run("gemv_batch_planes", lambda stream: N.call("fpb_nvfp4_gemv_batch_run", self._batch, stream))
+
+    def __del__(self):
+        h = getattr(self, "_batch", None)
+        if h is not None and h.value:
+            try:
+                N.lib.fpb_nvfp4_gemv_batch_destroy(h)
+            except Exception:
+                pass
+            self._batch = None
+
+
+def gemv_batch_planes(members, tile: GemvTile = DEFAULT_GEMV_TILE) -> PlanesGemvBatch:
+    """members: ``(weight, x, y)`` or ``(weight, x, y, rows)`` tuples."""
+    return PlanesGemvBatch(members, tile)
 
 
 class ExpertGemvView:

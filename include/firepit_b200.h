@@ -291,6 +291,20 @@ int fpb_nvfp4_gemv_planes(fpb_nvfp4_matrix *w, size_t row_begin, size_t row_end,
 int fpb_nvfp4_moe_gemv_planes(fpb_nvfp4_matrix *w, size_t rows_per_expert, const int32_t *distinct,
                               const int32_t *count, int cap, const void *x, int x_dtype, size_t x_stride, int tokens,
                               void *y, int y_dtype, void *workspace, size_t workspace_bytes, void *stream);
+/* A prepared tensor-core GEMV batch: the segments of fpb_nvfp4_gemv_batched
+ * (each its own matrix rows, x [batch, cols] and y [batch, rows]) with every
+ * pointer fixed at creation, run as one plane encode + one tcgen05 launch
+ * (fpb_nvfp4_gemv_planes per segment, in one kernel).  create validates,
+ * allocates the segment table and the planes workspace and synchronises
+ * `stream` (load time); run allocates nothing and reads nothing on the host
+ * (graph-capturable).  cols % 256 == 0, cols <= 4096, every row_begin a
+ * multiple of 128, 1 <= batch <= 16, at most 1024 segments
+ * (FPB_ERR_UNSUPPORTED for other shapes: use fpb_nvfp4_gemv_batched). */
+typedef struct fpb_gemv_batch fpb_gemv_batch;
+int fpb_nvfp4_gemv_batch_create(const fpb_gemv_segment *segs, int count, int x_dtype, int y_dtype, int batch,
+                                void *stream, fpb_gemv_batch **out);
+int fpb_nvfp4_gemv_batch_run(const fpb_gemv_batch *b, void *stream);
+int fpb_nvfp4_gemv_batch_destroy(fpb_gemv_batch *b);
 /* The down projection after the gate/up one: gate_up [cap][tokens][2 * cols]
  * f32 (distinct expert u's block at gate_up + u * gate_up_stride, gate
  * columns first) and the GEMV input is silu(gate) * up (swiglu.rs:16) in f32,

@@ -158,3 +158,32 @@ def test_planes_moe_gemv_glu(F, torch):
         want = O.nvfp4_expert_gemv_f32(h.packed, h.scales, h.row_scales, inter, np.full(T, e, np.int32), rows, 1, act)
         assert O.rel_frobenius(yc[u], want) <= REL
     assert np.all(np.isnan(yc[4:]))
+
+
+@pytest.mark.parametrize("rows,cols,mats,batch", [(4096, 4096, 16, 1), (1024, 2048, 5, 8), (256, 512, 3, 16)])
+def test_planes_batch_matches_single(F, torch, rows, cols, mats, batch):
+    """A prepared batch (one launch over several matrices, each its own x)
+    equals the oracle per member, including a row range that starts past 0,
+    under a CUDA graph."""
+    weights = [F.Nvfp4Matrix.quantize(F.synth_normal((rows, cols), seed=40 + i, stream_id=1, std=0.02))
+               for i in range(mats)]
+    hosts = [w.to_host() for w in weights]
+    xs = [O.bf16_to_f32(O.bf16_bits(O.synth_normal(batch * cols, seed=i, stream=3))).reshape(batch, cols)
+          for i in range(mats)]
+    xt = [torch.from_numpy(x).cuda().to(torch.bfloat16) for x in xs]
+    ys = [torch.full((batch, rows if i else rows - 128), float("nan"), device="cuda") for i in range(mats)]
+    members = [(weights[i], xt[i], ys[i]) + ((range(128, rows),) if i == 0 else ()) for i in range(mats)]
+    b = F.gemv_batch_planes(members, F.GemvTile(1, 4))
+    g = F.Graph()
+    with g:
+        b.submit(g)
+    g.replay()
+    torch.cuda.synchronize()
+    assert F.device_error() == 0
+    for i in range(mats):
+        want = O.nvfp4_gemv_f32(hosts[i].packed, hosts[i].scales, hosts[i].row_scales, rows, cols, xs[i])
+        if i == 0:
+            want = want[:, 128:]
+        assert O.rel_frobenius(ys[i].cpu().numpy(), want) <= REL, i
+    with pytest.raises(F.ShapeError):  # row range not starting at a multiple of 128
+        F.gemv_batch_planes([(weights[0], xt[0], ys[0][:, :rows - 192], range(64, rows - 128))], F.GemvTile(1, 4))

@@ -5,22 +5,24 @@ Default workload ("gemv"): NVFP4 decode GEMV, W [4096 x
 rows from N(0, 1) seed 0, y bf16.  One step is one decode-style sweep over
 64*g distinct weight matrices (g = number of GPUs), each with its own x row:
 every matrix is split along N (rows) over the g ranks; each rank computes its
-row slices of all 64*g GEMVs with batched launches (fpb_nvfp4_gemv_batched, at
-most 128 matrices' slices per launch) and the slices of each launch group are
-all-gathered after it (NCCL).  Each rank streams 64 * 9.45 MB = 605 MB of
+row slices of all 64*g GEMVs as one prepared tensor-core batch
+(fpb_nvfp4_gemv_batch_run: each x row as 8 NVFP4 digit planes, the weights
+through tcgen05 mxf4nvf4, at most 128 matrices' slices per batch) and the
+slices of each batch are all-gathered after it (fpb_comm_all_gather).  Each rank streams 64 * 9.45 MB = 605 MB of
 weights per step at every g (inputs larger than L2); per-GPU work is fixed as
 g grows ("weak").
 
   value  device-resident GB/s (algorithmic bytes of all ranks / max step time),
          the launches replayed as CUDA graphs;
   e2e    the same metric through the public Python API
-         (firepit_b200.gemv_batched(...).submit(Graph sink)) with x copied from
+         (firepit_b200.gemv_batch_planes(...).submit(Graph sink)) with x copied from
          pinned host memory each step and y copied back.
 
 The default line also carries "sub_records" for the other BASELINE configs
 (config 1 FP8 GEMM; config 2 NVFP4 GEMM at M = 1, 16, 128, 2048; config 3 MoE
 layer at T = 64 and 4096 on one GPU, expert-parallel over the ranks when g >
-1), each with its own roofline, cpu_baseline (rank 0, one GPU), e2e and clocks;
+1; config 4 decode tokens/s of the hybrid MoE decoder, replicas over the
+ranks), each with its own roofline, cpu_baseline (rank 0, one GPU), e2e and clocks;
 --no-sub leaves them out, --config runs one of them as the main line.
 
 --impl reference times the reference's host path (the CPU restatement of
@@ -516,7 +518,8 @@ def ours_arm(args):
             "gemv_path": "tensor cores (fpb_nvfp4_gemv_batch_run)" if tensor_cores else "streaming",
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": mats * COLS * 2,
                     "d2h_bytes_per_step": g * mats * rows_per_rank * 2,
-                    "path": "firepit_b200.gemv_batched(...).submit(Graph sink): H2D x, the batched GEMVs and D2H y "
+                    "path": ("firepit_b200.gemv_batch_planes" if tensor_cores else "firepit_b200.gemv_batched") +
+                            "(...).submit(Graph sink): H2D x, the batched GEMVs and D2H y "
                             "in one CUDA graph" + (" + NCCL all-gathers" if g > 1 else "")},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks.summary(),
@@ -552,8 +555,8 @@ def gemv_batch_bytes(m, n, k):
 
 def gemm_config(m: int, g: int) -> dict:
     if m <= 16:
-        how = (f"x bf16 [{m},2048] through the decode GEMV entry (fpb_nvfp4_gemv_batched over the 16 matrices, "
-               f"batch {m}); weights NVFP4, x kept in bf16 (W4A16)")
+        how = (f"x bf16 [{m},2048] on the tensor-core GEMV (the decode-size path of nvfp4_gemm: x as NVFP4 digit "
+               f"planes, fpb_nvfp4_gemv_batch_run over the 16 matrices, {m} rows); weights NVFP4, x kept in bf16")
     else:
         how = "x bf16 quantized on the device to NVFP4 (W4A4), tcgen05 block-scaled GEMM"
     return {"workload": f"config2 NVFP4 GEMM M={m} K=2048 N=8192, {how}",
@@ -618,8 +621,9 @@ def gemm_reference_arm(args):
 
 def gemm_small_arm(args):
     """Config 2 at M = 1 and 16: x bf16 [M, 2048] N(0,1) times 16 distinct NVFP4
-    weights [8192, 2048] (N-split over the ranks) through the decode GEMV entry,
-    one batched launch per step (batch M); HBM-bound."""
+    weights [8192, 2048] (N-split over the ranks) on the tensor-core GEMV (x
+    as NVFP4 digit planes, the decode-size path of nvfp4_gemm), one prepared
+    batch launch per step; HBM-bound."""
     import torch
     import torch.distributed as dist
 
@@ -642,10 +646,12 @@ def gemm_small_arm(args):
     x = F.synth_normal((m, GEMM_K), seed=0, stream_id=0, dtype=torch.bfloat16, device=dev)
     ys = torch.empty(GEMM_MATS, m, n_rank, dtype=torch.bfloat16, device=dev)
     y_all = torch.empty(g, GEMM_MATS, m, n_rank, dtype=torch.bfloat16, device=dev)
-    bat = F.gemv_batched([(mats[c], x, ys[c]) for c in range(GEMM_MATS)])
+    # the 16 matrices as one prepared tensor-core batch (x as NVFP4 digit
+    # planes, tcgen05): the decode-size path of nvfp4_gemm
+    bat = F.gemv_batch_planes([(mats[c], x, ys[c]) for c in range(GEMM_MATS)])
 
     def launch(sh):
-        N_.call("fpb_nvfp4_gemv_batched", bat._segs, GEMM_MATS, BF, BF, m, sh)
+        N_.call("fpb_nvfp4_gemv_batch_run", bat._batch, sh)
 
     s = torch.cuda.Stream(device=dev)
     with torch.cuda.stream(s):
@@ -688,7 +694,7 @@ def gemm_small_arm(args):
     xh = x.cpu().pin_memory()
     yh = torch.empty(GEMM_MATS, m, n_rank, dtype=torch.bfloat16, pin_memory=True)
     xd = torch.empty_like(x)
-    e2e_b = F.gemv_batched([(mats[c], xd, ys[c]) for c in range(GEMM_MATS)])
+    e2e_b = F.gemv_batch_planes([(mats[c], xd, ys[c]) for c in range(GEMM_MATS)])
     e2e_b.submit(F.Async())
     torch.cuda.synchronize()
     gsink = F.Graph()
@@ -725,7 +731,7 @@ def gemm_small_arm(args):
                             "peak_kind": f"{kind} hbm_gbs"},
                "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": m * GEMM_K * 2,
                        "d2h_bytes_per_step": GEMM_MATS * m * n_rank * 2,
-                       "path": "firepit_b200.gemv_batched(...).submit(Graph sink): H2D x, GEMVs, D2H y in one "
+                       "path": "firepit_b200.gemv_batch_planes(...).submit(Graph sink): H2D x, GEMVs, D2H y in one "
                                "CUDA graph"},
                "gpu_launches": launches_per_step * args.steps, "clocks": clocks.summary()}
         if g == 1 and args.cpu_seconds > 0:

@@ -978,8 +978,12 @@ using namespace fpb;
 
 extern "C" size_t fpb_nvfp4_act_sf_bytes(size_t m, size_t k) { return sf_tiled_bytes(m, k); }
 
+extern "C" size_t fpb_nvfp4_gemv_planes_workspace_bytes(size_t groups, size_t k);
+
 extern "C" size_t fpb_nvfp4_gemm_workspace_bytes(size_t m, size_t k) {
-  return align256(m * k / 2) + align256(sf_tiled_bytes(m, k)) + 256;
+  const size_t quantized = align256(m * k / 2) + align256(sf_tiled_bytes(m, k)) + 256;
+  // m <= 16 runs as the tensor-core GEMV (x as digit planes): its workspace
+  return m <= 16 ? std::max(quantized, fpb_nvfp4_gemv_planes_workspace_bytes(1, k)) : quantized;
 }
 
 extern "C" int fpb_nvfp4_quantize_act(const void *x, int x_dtype, size_t m, size_t k, uint8_t *packed,
@@ -1067,6 +1071,14 @@ extern "C" int fpb_nvfp4_gemm_q(fpb_nvfp4_matrix *w, size_t row_begin, size_t ro
   return FPB_OK;
 }
 
+namespace fpb {
+static int run_planes(const char *fn, fpb_nvfp4_matrix *w, size_t n_base, size_t n_rows, const void *x, int x_dtype,
+                      bool glu, size_t x_group_stride, int tokens, size_t groups, const int32_t *moe_ids,
+                      const int32_t *moe_count, int moe_cap, int n_experts, void *y, int y_dtype,
+                      long long y_group_stride, long long ldy, void *workspace, size_t workspace_bytes,
+                      cudaStream_t s);
+}  // namespace fpb
+
 extern "C" int fpb_nvfp4_gemm(fpb_nvfp4_matrix *w, size_t row_begin, size_t row_end, const void *x, int x_dtype,
                               size_t m, void *y, int y_dtype, void *workspace, size_t workspace_bytes,
                               void *stream) {
@@ -1076,6 +1088,15 @@ extern "C" int fpb_nvfp4_gemm(fpb_nvfp4_matrix *w, size_t row_begin, size_t row_
                 fpb_nvfp4_gemm_workspace_bytes(m, w->cols));
   if (reinterpret_cast<uintptr_t>(workspace) & 255)
     return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_gemm: workspace must be 256-byte aligned");
+  if (row_end == 0) row_end = w->rows;
+  // Decode-size M (BASELINE config 2 keeps activations in bf16 below 128
+  // rows; the reference keeps them in f32): the tensor-core GEMV, x as 8
+  // NVFP4 digit planes, no activation quantization.
+  if (m <= 16 && w->cols % 256 == 0 && w->cols <= (size_t)kPlaneMaxK && row_begin % kBN == 0 &&
+      row_begin < row_end && row_end <= w->rows)
+    return run_planes("fpb_nvfp4_gemm", w, row_begin, row_end - row_begin, x, x_dtype, false, 0, (int)m, 1, nullptr,
+                      nullptr, 0, 0, y, y_dtype, 0, (long long)(row_end - row_begin), workspace, workspace_bytes,
+                      as_stream(stream));
   uint8_t *ws = static_cast<uint8_t *>(workspace);
   uint8_t *packed = ws;
   uint8_t *sf = packed + align256(m * w->cols / 2);

@@ -256,7 +256,10 @@ int fpb_nvfp4_gemm_q(fpb_nvfp4_matrix *w, size_t row_begin, size_t row_end, cons
                      const uint8_t *a_sf_tiled, const float *a_global, size_t m, void *y, int y_dtype,
                      void *stream);
 /* Quantize x into `workspace` (256-byte aligned, fpb_nvfp4_gemm_workspace_bytes)
- * and run the GEMM. */
+ * and run the GEMM (BASELINE config 2's rule for M >= 128).  m <= 16 with
+ * cols % 256 == 0, cols <= 4096 and row_begin % 128 == 0 runs as
+ * fpb_nvfp4_gemv_planes instead (x not quantized: config 2 keeps decode-size
+ * activations in bf16, the reference keeps them in f32). */
 int fpb_nvfp4_gemm(fpb_nvfp4_matrix *w, size_t row_begin, size_t row_end, const void *x, int x_dtype,
                    size_t m, void *y, int y_dtype, void *workspace, size_t workspace_bytes,
                    void *stream);

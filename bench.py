@@ -723,7 +723,7 @@ def gemm_small_arm(args):
     out = None
     if rank == 0:
         out = {"metric": "NVFP4 GEMM HBM GB/s", "value": value, "unit": "GB/s", "n_gpus": g, "steps": args.steps,
-               "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+               "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
                "vs_baseline": None, "dtype": "e2m1xe4m3 weights, bf16 x/y, f32 accumulate",
                "data": "synthetic (seeded Philox: W N(0,0.02), x N(0,1) seed 0)", "config": gemm_config(m, g),
                "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
@@ -882,7 +882,7 @@ def gemm_arm(args):
     out = None
     if rank == 0:
         out = ({"metric": "NVFP4 GEMM TFLOPS", "value": value, "unit": "TFLOP/s", "n_gpus": g, "steps": args.steps,
-              "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+              "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
               "vs_baseline": None, "dtype": "nvfp4 x nvfp4 (e2m1, ue4m3/16), f32 accumulate, bf16 out",
               "data": "synthetic (seeded Philox: W N(0,0.02), x N(0,1) seed 0)",
               "config": gemm_config(m, g),
@@ -1088,7 +1088,7 @@ def fp8_arm(args):
             "peak_kind": "2 x measured bf16 burst (nominal dense FP8:BF16 ratio; no FP8 measurement)"}
     if rank == 0:
         line = {"metric": "FP8 GEMM TFLOPS", "value": value, "unit": "TFLOP/s", "n_gpus": g, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+                "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "e4m3 x e4m3 (128x128 block / per-token f32 scales), f32 accumulate, "
                                               "bf16 out",
                 "data": "synthetic (seeded Philox: W N(0,0.02), A N(0,1) seed 0)",
@@ -1449,6 +1449,31 @@ def moe_ep_arm(args):
     ms = t.item() / args.steps
     flops = world * moe_flops(T)
     value = flops / (ms * 1e-3) / 1e12
+    # end to end through the public entry (firepit_b200.ep.ep_moe_forward): the
+    # rank's tokens copied in from pinned host memory and the output back
+    xh = x.cpu().pin_memory()
+    yh = torch.empty(T, MOE_H, dtype=torch.bfloat16, pin_memory=True)
+    xd = torch.empty_like(x)
+
+    def e2e_step():
+        xd.copy_(xh, non_blocking=True)
+        logits = torch.mm(xd, wr.t(), out_dtype=torch.float32)
+        yh.copy_(ep_moe_forward(ops, xd, logits, MOE_K, MOE_E, W1, W2, world=world, comm=comm()), non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    dist_sync()
+    e2e_steps = max(1, min(args.steps, 10))
+    start.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    end.record()
+    torch.cuda.synchronize()
+    te = torch.tensor([start.elapsed_time(end)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = flops / (te.item() / e2e_steps * 1e-3) / 1e12
     nbytes = world * moe_bytes(T, per)
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
     hbm = float(peaks.get("hbm_gbs", 6650.0))
@@ -1464,7 +1489,11 @@ def moe_ep_arm(args):
                "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                             "frac": achieved / hbm, "traffic": None, "peak_kind": "measured hbm_gbs",
                             "note": "per GPU: local experts' weights + router + x + y over the layer time"},
-               "e2e": None, "gpu_launches": launches, "clocks": clocks.summary()}
+               "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": world * T * MOE_H * 2,
+                       "d2h_bytes_per_step": world * T * MOE_H * 2,
+                       "path": "firepit_b200.ep.ep_moe_forward on x copied from pinned host memory, output copied "
+                               "back, every step"},
+               "gpu_launches": launches, "clocks": clocks.summary()}
     dist_sync()
     return out
 

@@ -128,7 +128,7 @@ struct alignas(64) PlaneSeg {
   void *y;
   int row_begin, rows;
   int item_begin;           // first item (128-row tile) of this segment
-  int pad_;
+  int a_group;              // A row group of its x: the first segment with the same x (encoded once)
 };
 
 // ---- x as NVFP4 digit planes (tensor-core GEMV) ----------------------------------------
@@ -162,6 +162,7 @@ __global__ void __launch_bounds__(kPlaneThreads) planes_encode_kernel(const T *x
   __shared__ uint32_t red[32];
   const int g = blockIdx.x / tokens, t = blockIdx.x % tokens;
   if (live_groups && g >= *live_groups) return;  // a group nothing reads (uniform)
+  if (segs && segs[g].a_group != g) return;      // its x is encoded by an earlier segment (uniform)
   const T *xg = segs ? static_cast<const T *>(segs[g].x) : x + (long long)g * x_group_stride;
   const T *xr = xg + (long long)t * K * (GLU ? 2 : 1);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -325,7 +326,7 @@ __device__ __forceinline__ bool gemm_tile(const GemmParams &p, int t, int n_tile
         hi = mid - 1;
     }
     if (seg) *seg = p.segs + lo;
-    m_tile = lo;
+    m_tile = p.segs[lo].a_group;
     n_tile = t - moe->ids[lo];
     n_base = p.segs[lo].row_begin;
     return true;
@@ -1291,6 +1292,12 @@ extern "C" int fpb_nvfp4_gemv_batch_create(const fpb_gemv_segment *segs, int cou
     d.rows = (int)(end - sg.row_begin);
     d.item_begin = items;
     items += (d.rows + kBN - 1) / kBN;
+    d.a_group = i;
+    for (int j = 0; j < i; ++j)
+      if (segs[j].x == sg.x) {
+        d.a_group = j;
+        break;
+      }
   }
   if (int st = ensure_gemm_attr()) return st;
   fpb_gemv_batch *b = new fpb_gemv_batch();

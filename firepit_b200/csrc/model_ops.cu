@@ -415,9 +415,19 @@ __global__ void attn_decode_merge_kernel(const float *part, const float *q_gate,
   const float inv_l = 1.0f / block_sum(l, red);  // its barriers also publish wsm
   const float *gate = q_gate + (size_t)b * qg_pitch + (size_t)h * 2 * D + D;
   for (int j = threadIdx.x; j < D; j += blockDim.x) {
-    float num = 0.0f;
-    for (int c = 0; c < used; ++c) num = fmaf(pp[(size_t)c * (D + 2) + j], wsm[c], num);
-    store_f(out, out_bf16, (size_t)b * q_heads * D + (size_t)h * D + j, num * inv_l * sigmoidf_(gate[j]));
+    // four independent partial sums, eight chunks' loads in flight
+    float num[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    int c = 0;
+    for (; c + 8 <= used; c += 8) {
+      float v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = pp[(size_t)(c + i) * (D + 2) + j];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) num[i & 3] = fmaf(v[i], wsm[c + i], num[i & 3]);
+    }
+    for (; c < used; ++c) num[c & 3] = fmaf(pp[(size_t)c * (D + 2) + j], wsm[c], num[c & 3]);
+    const float total = (num[0] + num[1]) + (num[2] + num[3]);
+    store_f(out, out_bf16, (size_t)b * q_heads * D + (size_t)h * D + j, total * inv_l * sigmoidf_(gate[j]));
   }
 }
 

@@ -283,14 +283,29 @@ class Decoder:
         self.graph = None
         self.route_log = None  # [layers, batch, slots] int32 when recording routes
 
-    def _gemv(self, key, members, x, sh):
-        """One batched NVFP4 GEMV launch of [(weight, y)] sharing input x."""
+    def _gemv(self, key, members, x, sh, tensor_cores=False):
+        """One batched NVFP4 GEMV launch of [(weight, y)] sharing input x: on
+        the tensor cores (a prepared batch, x encoded once as NVFP4 digit
+        planes) when asked and the shapes allow, else the streaming kernel.
+        The batch binds its buffers when first built (outside any capture:
+        the first step runs eagerly)."""
         import firepit_b200 as F
         b = self._batched.get(key)
         if b is None:
-            b = F.gemv_batched([(w, x, y.view(self.batch, -1)) for w, y in members], F.GemvTile(1, 4))
+            mem = [(w, x, y.view(self.batch, -1)) for w, y in members]
+            b = None
+            if tensor_cores and self.batch <= 16 and self.cfg.hidden % 256 == 0:
+                try:
+                    b = F.gemv_batch_planes(mem, F.GemvTile(1, 4))
+                except F.ShapeError:
+                    b = None
+            if b is None:
+                b = F.gemv_batched(mem, F.GemvTile(1, 4))
             self._batched[key] = b
-        N.call("fpb_nvfp4_gemv_batched", b._segs, len(members), N.FPB_BF16, N.FPB_F32, self.batch, sh)
+        if isinstance(b, F.PlanesGemvBatch):
+            N.call("fpb_nvfp4_gemv_batch_run", b._batch, sh)
+        else:
+            N.call("fpb_nvfp4_gemv_batched", b._segs, len(members), N.FPB_BF16, N.FPB_F32, self.batch, sh)
 
     def step(self, sh: int) -> None:
         """One decode step of every session on stream handle sh."""
@@ -305,7 +320,7 @@ class Decoder:
         for i, L in enumerate(m.layers):
             if L["kind"] == "gdn":
                 self._gemv(("gdn", i), [(L["w_qkv"], self.qkv), (L["w_z"], self.z), (L["w_b"], self.gb),
-                                        (L["w_a"], self.ga)], self.normed, sh)
+                                        (L["w_a"], self.ga)], self.normed, sh, tensor_cores=True)
                 conv_state, rec = self.gdn[i]
                 if self.fused_gdn:
                     N.call("fpb_gdn_step", self.qkv.data_ptr(), c.conv_dim, conv_state.data_ptr(), L["conv"].data_ptr(),
@@ -325,7 +340,7 @@ class Decoder:
                 self._gemv(("gdn_out", i), [(L["w_out"], self.delta)], self.gated, sh)
             else:
                 self._gemv(("attn", i), [(L["w_qg"], self.qg), (L["w_k"], self.kp), (L["w_v"], self.vp)],
-                           self.normed, sh)
+                           self.normed, sh, tensor_cores=True)
                 kc, vc = self.kv[i]
                 N.call("fpb_attn_prepare", self.qg.data_ptr(), self.qg.shape[1], self.kp.data_ptr(), self.kp.shape[1],
                        self.vp.data_ptr(), self.vp.shape[1], L["q_norm"].data_ptr(), L["k_norm"].data_ptr(),

@@ -320,7 +320,7 @@ class Decoder:
         for i, L in enumerate(m.layers):
             if L["kind"] == "gdn":
                 self._gemv(("gdn", i), [(L["w_qkv"], self.qkv), (L["w_z"], self.z), (L["w_b"], self.gb),
-                                        (L["w_a"], self.ga)], self.normed, sh, tensor_cores=True)
+                                        (L["w_a"], self.ga)], self.normed, sh)
                 conv_state, rec = self.gdn[i]
                 if self.fused_gdn:
                     N.call("fpb_gdn_step", self.qkv.data_ptr(), c.conv_dim, conv_state.data_ptr(), L["conv"].data_ptr(),
@@ -340,7 +340,7 @@ class Decoder:
                 self._gemv(("gdn_out", i), [(L["w_out"], self.delta)], self.gated, sh)
             else:
                 self._gemv(("attn", i), [(L["w_qg"], self.qg), (L["w_k"], self.kp), (L["w_v"], self.vp)],
-                           self.normed, sh, tensor_cores=True)
+                           self.normed, sh)
                 kc, vc = self.kv[i]
                 N.call("fpb_attn_prepare", self.qg.data_ptr(), self.qg.shape[1], self.kp.data_ptr(), self.kp.shape[1],
                        self.vp.data_ptr(), self.vp.shape[1], L["q_norm"].data_ptr(), L["k_norm"].data_ptr(),

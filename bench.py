@@ -1383,15 +1383,17 @@ def moe_arm(args):
 
 def moe_ep_arm(args):
     """Config 3 expert-parallel: E=512 experts split over the ranks (64 per GPU
-    at 8), T=4096 tokens per rank (weak scaling), NCCL all-to-all dispatch and
-    combine (firepit_b200.ep); activation globals all-reduced so every rank
-    encodes like the single-GPU layer.  Eager launches: the per-destination
-    counts are read by the host to size the all-to-all splits."""
+    at 8), T=4096 tokens per rank (weak scaling), firepit_b200.ep.EpMoeLayer:
+    one NVFP4 record per (token, destination rank) in fixed-size chunks, NCCL
+    all-to-all out and back (the library's fpb_comm_*), activation globals
+    all-reduced so every rank encodes like the single-GPU layer, partial sums
+    per record returned in f32; router GEMM + layer in one CUDA graph per
+    rank."""
     import torch
     import torch.distributed as dist
 
     import firepit_b200 as F
-    from firepit_b200.ep import DeviceOps, ep_moe_forward
+    from firepit_b200.ep import DeviceEpOps, EpMoeLayer
     rank, world, local, dev = dist_init()
     T = 4096
     per = MOE_E // world
@@ -1422,58 +1424,85 @@ def moe_ep_arm(args):
     del gp, gs, gg, dp, ds, dg
     wr = F.synth_normal((MOE_E, MOE_H), seed=0, stream_id=99, std=0.02, dtype=torch.bfloat16, device=dev)
     x = F.synth_normal((T, MOE_H), seed=rank, stream_id=0, dtype=torch.bfloat16, device=dev)
-    ops = DeviceOps(dev)
+    ops = DeviceEpOps(dev, T, MOE_H, MOE_I, MOE_E, MOE_K, world, W1, W2)
+    layer = EpMoeLayer(ops, comm=comm())
+    logits = torch.empty(T, MOE_E, device=dev)
 
-    def step():
-        logits = torch.mm(x, wr.t(), out_dtype=torch.float32)
-        return ep_moe_forward(ops, x, logits, MOE_K, MOE_E, W1, W2, world=world, comm=comm())
+    def step(xin, ev=None):
+        if ev is not None:
+            ev[0].record()
+        torch.mm(xin, wr.t(), out_dtype=torch.float32, out=logits)
+        if ev is not None:
+            ev[1].record()
+        return layer.forward(xin, logits, None if ev is None else (lambda i: ev[i + 2].record()))
 
-    for _ in range(max(args.warmup, 3)):
-        step()
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step(x)
     torch.cuda.synchronize()
     assert F.device_error() == 0
+    before = F.launch_count()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        step(x)
+    launches_per_step = F.launch_count() - before
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize()
     dist_sync()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    launches = F.launch_count()
     with ClockSampler(local) as clocks:
         start.record()
         for _ in range(args.steps):
-            step()
+            graph.replay()
         end.record()
         torch.cuda.synchronize()
-    launches = F.launch_count() - launches
     t = torch.tensor([start.elapsed_time(end)], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = t.item() / args.steps
     flops = world * moe_flops(T)
     value = flops / (ms * 1e-3) / 1e12
-    # end to end through the public entry (firepit_b200.ep.ep_moe_forward): the
-    # rank's tokens copied in from pinned host memory and the output back
+    # per-stage breakdown (eager launches with events on every rank, max over ranks)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(2 + len(EpMoeLayer.STAGES))]
+    dist_sync()
+    with torch.cuda.stream(s):
+        step(x, evs)
+    torch.cuda.synchronize()
+    names = ("router_gemm",) + EpMoeLayer.STAGES
+    bd = torch.tensor([evs[i].elapsed_time(evs[i + 1]) for i in range(len(names))], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(bd, op=dist.ReduceOp.MAX)
+    breakdown = dict(zip(names, bd.tolist()))
+    # end to end through the public entry (EpMoeLayer.forward): the rank's
+    # tokens copied in from pinned host memory and the output back, in the
+    # same CUDA graph as the layer
     xh = x.cpu().pin_memory()
     yh = torch.empty(T, MOE_H, dtype=torch.bfloat16, pin_memory=True)
     xd = torch.empty_like(x)
-
-    def e2e_step():
+    e2e_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(e2e_graph, stream=s):
         xd.copy_(xh, non_blocking=True)
-        logits = torch.mm(xd, wr.t(), out_dtype=torch.float32)
-        yh.copy_(ep_moe_forward(ops, xd, logits, MOE_K, MOE_E, W1, W2, world=world, comm=comm()), non_blocking=True)
-
+        yh.copy_(step(xd), non_blocking=True)
     for _ in range(2):
-        e2e_step()
+        e2e_graph.replay()
     torch.cuda.synchronize()
     dist_sync()
-    e2e_steps = max(1, min(args.steps, 10))
+    torch.cuda.synchronize()
+    e2e_steps = max(1, min(args.steps, 20))
     start.record()
     for _ in range(e2e_steps):
-        e2e_step()
+        e2e_graph.replay()
     end.record()
     torch.cuda.synchronize()
     te = torch.tensor([start.elapsed_time(end)], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_value = flops / (te.item() / e2e_steps * 1e-3) / 1e12
+    del graph, e2e_graph
+    assert F.device_error() == 0
     nbytes = world * moe_bytes(T, per)
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
     hbm = float(peaks.get("hbm_gbs", 6650.0))
@@ -1483,7 +1512,7 @@ def moe_ep_arm(args):
         out = {"metric": "NVFP4 MoE layer TFLOPS", "value": value, "unit": "TFLOP/s", "n_gpus": world,
                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
                "scaling": "weak", "vs_baseline": None,
-               "dtype": "nvfp4 x nvfp4 experts (f32 accumulate), bf16 router and dispatch",
+               "dtype": "nvfp4 x nvfp4 experts (f32 accumulate), bf16 router, nvfp4 dispatch, f32 partials back",
                "data": "synthetic (seeded Philox: W N(0,0.02) per expert, x N(0,1) per rank)",
                "config": moe_config(T, world, ep=True),
                "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
@@ -1491,9 +1520,10 @@ def moe_ep_arm(args):
                             "note": "per GPU: local experts' weights + router + x + y over the layer time"},
                "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": world * T * MOE_H * 2,
                        "d2h_bytes_per_step": world * T * MOE_H * 2,
-                       "path": "firepit_b200.ep.ep_moe_forward on x copied from pinned host memory, output copied "
-                               "back, every step"},
-               "gpu_launches": launches, "clocks": clocks.summary()}
+                       "path": "firepit_b200.ep.EpMoeLayer.forward on x copied from pinned host memory, output "
+                               "copied back, in one CUDA graph per rank"},
+               "gpu_launches": launches_per_step * args.steps, "clocks": clocks.summary(), "breakdown_ms": breakdown,
+               "exchange_bytes_per_rank": {"dispatch": world * T * ops.rec, "return": world * T * MOE_H * 4}}
     dist_sync()
     return out
 

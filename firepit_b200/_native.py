@@ -137,6 +137,11 @@ SIGNATURES: dict[str, tuple] = {
     "fpb_moe_topk": (i32, [vp, sz, vp, sz, sz, sz, sz, vp, vp, vp]),
     "fpb_moe_layout": (i32, [vp, sz, sz, sz, sz, sz, sz, vp, vp, vp, vp, vp, vp, sz, vp]),
     "fpb_moe_layout_scratch_bytes": (sz, [sz, sz, sz]),
+    "fpb_moe_layout_masked": (i32, [vp, sz, sz, sz, sz, sz, sz, vp, vp, vp, vp, vp, vp, sz, vp]),
+    "fpb_moe_gather_codes": (i32, [vp, sz, vp, sz, sz, sz, vp, sz, vp, i32, vp, vp, vp]),
+    "fpb_ep_record_bytes": (sz, [sz, sz]),
+    "fpb_ep_dispatch": (i32, [vp, i32, sz, sz, vp, vp, sz, sz, sz, sz, vp, vp, vp, vp, vp]),
+    "fpb_ep_unpack": (i32, [vp, sz, sz, sz, vp, vp, vp]),
     "fpb_moe_gather": (i32, [vp, i32, sz, sz, vp, sz, vp, i32, vp]),
     "fpb_moe_gather_quantize": (i32, [vp, i32, sz, sz, vp, sz, vp, vp, vp, vp, vp, i32, vp, sz, vp]),
     "fpb_moe_gather_quantize_workspace_bytes": (sz, [sz, sz]),

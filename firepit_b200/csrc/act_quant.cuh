@@ -103,9 +103,9 @@ __global__ void act_amax_kernel(const T *x, size_t n, uint32_t *amax_bits) {
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + expf(g * -1.0f)) * u; }
 
 // One 16-value group: s = RN_e4m3((bmax / 6) / global), codes =
-// RN_e2m1(v / (e4m3(s) * global)); writes 8 code bytes and the factor.
-__device__ __forceinline__ void encode_group16(const float v[16], float global, uint8_t *packed_dst,
-                                               uint8_t *sf_dst) {
+// RN_e2m1(v / (e4m3(s) * global)); returns the factor, the 8 code bytes in
+// `codes` (values 0-7 in .x, 8-15 in .y).
+__device__ __forceinline__ uint8_t encode_group16_regs(const float v[16], float global, uint2 &codes) {
   float bmax = 0.0f;
 #pragma unroll
   for (int i = 0; i < 16; ++i) bmax = fmaxf(bmax, fabsf(v[i]));
@@ -120,8 +120,16 @@ __device__ __forceinline__ void encode_group16(const float v[16], float global, 
     lo = f32x8_to_e2m1x8(q);
     hi = f32x8_to_e2m1x8(q + 8);
   }
-  *reinterpret_cast<uint2 *>(packed_dst) = make_uint2(lo, hi);
-  *sf_dst = s;
+  codes = make_uint2(lo, hi);
+  return s;
+}
+
+// The same group written out: 8 code bytes and the factor.
+__device__ __forceinline__ void encode_group16(const float v[16], float global, uint8_t *packed_dst,
+                                               uint8_t *sf_dst) {
+  uint2 codes;
+  *sf_dst = encode_group16_regs(v, global, codes);
+  *reinterpret_cast<uint2 *>(packed_dst) = codes;
 }
 
 }  // namespace fpb

@@ -125,26 +125,31 @@ __global__ void moe_topk_kernel(const float *logits, long long ld, const float *
 //  3. place: per CTA, ranks that keep the routes' order (per-warp counts over
 //     contiguous warp segments, __match_any_sync within a batch), so every
 //     expert's rows follow the (token, slot) order: the reference's stable sort.
-// The fills (token_rows = -1, tile_experts = -1, inverse = 0) are memsets.
+// The fills (token_rows = -1, tile_experts = -1, inverse = 0, or -1 in a
+// masked layout) are memsets.
 constexpr int kLayoutChunk = 1024;  // routes per CTA
 constexpr int kLayoutWarpsPerCta = 8;
 
-__device__ __forceinline__ int layout_id(const int32_t *ids, int e, int kk, int width, int experts) {
+// The route's expert, -1 for an id outside [0, experts) (a device error), or
+// -2 for the id -1 in a masked layout (a route that is not there: the
+// expert-parallel receiver marks the slots it does not own that way).
+__device__ __forceinline__ int layout_id(const int32_t *ids, int e, int kk, int width, int experts, bool masked) {
   const int id = ids[(long long)(e / kk) * width + e % kk];
-  return (id >= 0 && id < experts) ? id : -1;
+  if (id >= 0 && id < experts) return id;
+  return (masked && id == -1) ? -2 : -1;
 }
 
 __global__ void __launch_bounds__(256) moe_layout_count_kernel(const int32_t *ids, int n, int kk, int width,
-                                                               int experts, int *cnt, int *error) {
+                                                               int experts, int *cnt, int *error, bool masked) {
   extern __shared__ int hist[];
   for (int e = threadIdx.x; e < experts; e += blockDim.x) hist[e] = 0;
   __syncthreads();
   const int lo = blockIdx.x * kLayoutChunk, hi = min(n, lo + kLayoutChunk);
   for (int e = lo + threadIdx.x; e < hi; e += blockDim.x) {
-    const int id = layout_id(ids, e, kk, width, experts);
+    const int id = layout_id(ids, e, kk, width, experts, masked);
     if (id >= 0)
       atomicAdd(&hist[id], 1);
-    else if (error)
+    else if (id == -1 && error)
       atomicCAS(error, 0, 401);
   }
   __syncthreads();
@@ -210,7 +215,7 @@ __global__ void __launch_bounds__(1024) moe_layout_scan_kernel(int *cnt, int gro
 
 __global__ void __launch_bounds__(kLayoutWarpsPerCta * 32) moe_layout_place_kernel(
     const int32_t *ids, int n, int kk, int width, int experts, int cap, const int *cnt, const int64_t *ranges,
-    int32_t *token_rows, int32_t *inverse) {
+    int32_t *token_rows, int32_t *inverse, bool masked) {
   extern __shared__ int wcount[];  // [kLayoutWarpsPerCta][experts]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   for (int i = tid; i < kLayoutWarpsPerCta * experts; i += blockDim.x) wcount[i] = 0;
@@ -220,7 +225,7 @@ __global__ void __launch_bounds__(kLayoutWarpsPerCta * 32) moe_layout_place_kern
   const int w_lo = min(hi, lo + warp * kWarpSpan), w_hi = min(hi, w_lo + kWarpSpan);
   for (int b = w_lo; b < w_hi; b += 32) {
     const int e = b + lane;
-    const int id = e < w_hi ? layout_id(ids, e, kk, width, experts) : -1;
+    const int id = e < w_hi ? layout_id(ids, e, kk, width, experts, masked) : -1;
     const unsigned grp = __match_any_sync(0xffffffffu, id);
     if (id >= 0 && lane == __ffs(grp) - 1) wcount[warp * experts + id] += __popc(grp);
     __syncwarp();
@@ -238,7 +243,7 @@ __global__ void __launch_bounds__(kLayoutWarpsPerCta * 32) moe_layout_place_kern
   __syncthreads();
   for (int b = w_lo; b < w_hi; b += 32) {
     const int e = b + lane;
-    const int id = e < w_hi ? layout_id(ids, e, kk, width, experts) : -1;
+    const int id = e < w_hi ? layout_id(ids, e, kk, width, experts, masked) : -1;
     const unsigned grp = __match_any_sync(0xffffffffu, id);
     const int rank = __popc(grp & ((1u << lane) - 1));
     int pos = -1;
@@ -260,7 +265,8 @@ __global__ void __launch_bounds__(kLayoutWarpsPerCta * 32) moe_layout_place_kern
 constexpr int kLayoutSmallThreads = 1024;
 __global__ void __launch_bounds__(kLayoutSmallThreads) moe_layout_small_kernel(
     const int32_t *ids, int n, int kk, int width, int tokens, int experts, int tile_rows, int cap,
-    int32_t *token_rows, int32_t *tile_experts, int32_t *inverse, int64_t *ranges, int32_t *padded_out, int *error) {
+    int32_t *token_rows, int32_t *tile_experts, int32_t *inverse, int64_t *ranges, int32_t *padded_out, int *error,
+    bool masked) {
   pdl_enter();
   extern __shared__ int sm_small[];
   constexpr int kWarps = kLayoutSmallThreads / 32;
@@ -276,7 +282,8 @@ __global__ void __launch_bounds__(kLayoutSmallThreads) moe_layout_small_kernel(
     for (int i = tid; i < cap; i += blockDim.x) token_rows[i] = -1;
   }
   for (int i = tid; i < cap / tile_rows; i += blockDim.x) tile_experts[i] = -1;
-  for (int i = tid; i < tokens * width; i += blockDim.x) inverse[i] = 0;
+  const int inv_fill = masked ? -1 : 0;
+  for (int i = tid; i < tokens * width; i += blockDim.x) inverse[i] = inv_fill;
   for (int i = tid; i < kWarps * experts; i += blockDim.x) wcount[i] = 0;
   __syncthreads();
   // each warp counts a contiguous segment of the routes
@@ -284,8 +291,8 @@ __global__ void __launch_bounds__(kLayoutSmallThreads) moe_layout_small_kernel(
   const int w_lo = min(n, warp * span), w_hi = min(n, w_lo + span);
   for (int b = w_lo; b < w_hi; b += 32) {
     const int e = b + lane;
-    const int id = e < w_hi ? layout_id(ids, e, kk, width, experts) : -1;
-    if (e < w_hi && id < 0 && error) atomicCAS(error, 0, 401);
+    const int id = e < w_hi ? layout_id(ids, e, kk, width, experts, masked) : -1;
+    if (e < w_hi && id == -1 && error) atomicCAS(error, 0, 401);
     const unsigned grp = __match_any_sync(0xffffffffu, id);
     if (id >= 0 && lane == __ffs(grp) - 1) wcount[warp * experts + id] += __popc(grp);
     __syncwarp();
@@ -337,7 +344,7 @@ __global__ void __launch_bounds__(kLayoutSmallThreads) moe_layout_small_kernel(
   // stable placement: (token, slot) order within each expert
   for (int b = w_lo; b < w_hi; b += 32) {
     const int e = b + lane;
-    const int id = e < w_hi ? layout_id(ids, e, kk, width, experts) : -1;
+    const int id = e < w_hi ? layout_id(ids, e, kk, width, experts, masked) : -1;
     const unsigned grp = __match_any_sync(0xffffffffu, id);
     const int rank = __popc(grp & ((1u << lane) - 1));
     int pos = -1;
@@ -503,15 +510,17 @@ __global__ void rows_encode_kernel(Rows rows_src, size_t rows, const int32_t *va
   });
 }
 
-// Gathered NVFP4 rows from token rows quantized once (codes [tokens, cols/2],
-// row-major factors [tokens, cols/16], cols % 64 == 0): one warp per layout
-// row copies the token's codes (16-byte vectors) and its factors, four groups
-// (one 4-byte word) at a time, into the tiled layout; padding rows get zeros,
-// or nothing with `skip`.  NVFP4 encoding is row-local and every gathered row
-// shares the one global, so the copies equal encoding the gathered rows.
-__global__ void gather_codes_kernel(const uint8_t *tok_packed, const uint8_t *tok_sf, int tokens,
-                                    const int32_t *token_rows, size_t rows, const int32_t *valid,
-                                    const int32_t *skip, size_t cols, uint8_t *packed, uint8_t *sf_tiled) {
+// Gathered NVFP4 rows from token rows quantized once (token t's codes at
+// tok_packed + t * code_stride, its row-major factors at tok_sf + t *
+// sf_stride; cols % 64 == 0): one warp per layout row copies the token's
+// codes (16-byte vectors) and its factors, four groups (one 4-byte word) at a
+// time, into the tiled layout; padding rows get zeros, or nothing with
+// `skip`.  NVFP4 encoding is row-local and every gathered row shares the one
+// global, so the copies equal encoding the gathered rows.
+__global__ void gather_codes_kernel(const uint8_t *tok_packed, const uint8_t *tok_sf, size_t code_stride,
+                                    size_t sf_stride, int tokens, const int32_t *token_rows, size_t rows,
+                                    const int32_t *valid, const int32_t *skip, size_t cols, uint8_t *packed,
+                                    uint8_t *sf_tiled) {
   pdl_enter();
   const int lane = threadIdx.x & 31;
   const int code_vecs = (int)(cols / 32), sf_words = (int)(cols / 64);
@@ -519,10 +528,10 @@ __global__ void gather_codes_kernel(const uint8_t *tok_packed, const uint8_t *to
   for_live_rows(n, skip, [&](size_t r, int) {
     const int t = token_rows[r];
     const bool zero = t < 0 || t >= tokens;
-    const uint4 *csrc = reinterpret_cast<const uint4 *>(tok_packed + (size_t)max(t, 0) * (cols / 2));
+    const uint4 *csrc = reinterpret_cast<const uint4 *>(tok_packed + (size_t)max(t, 0) * code_stride);
     uint4 *cdst = reinterpret_cast<uint4 *>(packed + r * (cols / 2));
     for (int i = lane; i < code_vecs; i += 32) cdst[i] = zero ? make_uint4(0, 0, 0, 0) : csrc[i];
-    const uint32_t *ssrc = reinterpret_cast<const uint32_t *>(tok_sf + (size_t)max(t, 0) * (cols / 16));
+    const uint32_t *ssrc = reinterpret_cast<const uint32_t *>(tok_sf + (size_t)max(t, 0) * sf_stride);
     uint8_t *srow = sf_tiled + sf_tiled_row_offset(r, cols);
     for (int j = lane; j < sf_words; j += 32)
       *reinterpret_cast<uint32_t *>(srow + (size_t)j * kSfChunk) = zero ? 0u : ssrc[j];
@@ -658,6 +667,154 @@ __global__ void moe_route_dest_kernel(const int32_t *ids, int tokens, int width,
   const int n = tokens * width;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
     dest[i] = (i % width) < slots ? ids[i] / per_rank : 0;
+}
+
+// ---- expert parallel with fixed capacity ------------------------------------------------
+// A rank's tokens go to the ranks that own their experts as fixed-size
+// records, one per (token, destination) pair, never one per route: chunk d of
+// the send buffer holds `tokens` records for rank d, the first count_d of
+// them the tokens that route to rank d in token order, the rest marked empty.
+// Every chunk has the same size, so the all-to-all needs no host-read counts
+// and the whole layer is one CUDA graph.  A record is the token's NVFP4 row
+// (codes, then row-major factors, encoded with the global of the all-reduced
+// amax: the single-GPU encoding) and its routes as the receiver needs them:
+// receiver-local expert ids (-1 for a slot owned by another rank) and the
+// routing weights.
+struct EpRecord {
+  size_t sf, ids, weights, bytes;  // byte offsets in a record (codes at 0), record size
+};
+
+__host__ __device__ inline EpRecord ep_record(size_t cols, size_t width) {
+  auto a16 = [](size_t v) { return (v + 15) / 16 * 16; };
+  EpRecord r;
+  r.sf = a16(cols / 2);
+  r.ids = r.sf + a16(cols / 16);
+  r.weights = r.ids + 4 * width;
+  r.bytes = a16(r.weights + 4 * width);
+  return r;
+}
+
+// positions[t * nranks + d] = d * tokens + (t's index among the tokens that
+// route to rank d), or -1; positions[tokens * nranks + d] = count_d.  One CTA:
+// per 1024-token chunk, one ballot per destination gives each warp's counts,
+// one thread per destination scans the 32 warps, a second ballot places.
+constexpr int kEpPlanThreads = 1024;
+__global__ void __launch_bounds__(kEpPlanThreads) ep_plan_kernel(const int32_t *ids, int tokens, int width,
+                                                                 int slots, int experts, int per_rank, int nranks,
+                                                                 int32_t *positions, int *error) {
+  pdl_enter();
+  __shared__ int wtot[32][33];
+  __shared__ int carry[32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid < nranks) carry[tid] = 0;
+  __syncthreads();
+  for (int base = 0; base < tokens; base += kEpPlanThreads) {
+    const int t = base + tid;
+    uint32_t mask = 0;
+    if (t < tokens)
+      for (int s = 0; s < slots; ++s) {
+        const int id = ids[(size_t)t * width + s];
+        if (id >= 0 && id < experts)
+          mask |= 1u << (id / per_rank);
+        else if (error)
+          atomicCAS(error, 0, 403);
+      }
+    for (int d = 0; d < nranks; ++d) {
+      const unsigned b = __ballot_sync(0xffffffffu, (mask >> d) & 1u);
+      if (lane == 0) wtot[warp][d] = __popc(b);
+    }
+    __syncthreads();
+    if (tid < nranks) {
+      int run = carry[tid];
+      for (int w = 0; w < kEpPlanThreads / 32; ++w) {
+        const int c = wtot[w][tid];
+        wtot[w][tid] = run;
+        run += c;
+      }
+      carry[tid] = run;
+    }
+    __syncthreads();
+    for (int d = 0; d < nranks; ++d) {
+      const bool on = (mask >> d) & 1u;
+      const unsigned b = __ballot_sync(0xffffffffu, on);
+      if (t < tokens)
+        positions[(size_t)t * nranks + d] =
+            on ? d * tokens + wtot[warp][d] + __popc(b & ((1u << lane) - 1u)) : -1;
+    }
+    __syncthreads();
+  }
+  if (tid < nranks) positions[(size_t)tokens * nranks + tid] = carry[tid];
+}
+
+// One warp per token: the routes' metadata into each destination's record,
+// the empty marks of record t in every chunk past its count, and the NVFP4
+// row encoded once into the first destination's record and copied (16-byte
+// vectors, after __syncwarp) into the others.
+template <typename T>
+__global__ void ep_pack_kernel(const T *x, int tokens, int cols, const int32_t *ids, const float *weights, int width,
+                               int slots, int experts, int per_rank, int nranks, const int32_t *positions,
+                               const uint32_t *amax_bits, uint8_t *records, EpRecord rec, float *global_out) {
+  pdl_enter();
+  const float global = __fdiv_rn(__uint_as_float(*amax_bits), 2688.0f);
+  if (blockIdx.x == 0 && threadIdx.x == 0) *global_out = global;
+  const int lane = threadIdx.x & 31, gpr = cols / 16;
+  const int warps = gridDim.x * (blockDim.x / 32);
+  const int32_t *counts = positions + (size_t)tokens * nranks;
+  for (int t = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; t < tokens; t += warps) {
+    const int pos_l = lane < nranks ? positions[(size_t)t * nranks + lane] : -1;
+    const unsigned live = __ballot_sync(0xffffffffu, pos_l >= 0);
+    int id_l = -1;
+    float w_l = 0.0f;
+    if (lane < slots) {
+      id_l = ids[(size_t)t * width + lane];
+      w_l = weights[(size_t)t * width + lane];
+    }
+    for (int d = 0; d < nranks; ++d) {
+      const int p = __shfl_sync(0xffffffffu, pos_l, d);
+      if (p >= 0 && lane < width) {
+        uint8_t *r = records + (size_t)p * rec.bytes;
+        const bool mine = id_l >= 0 && id_l < experts && id_l / per_rank == d;
+        reinterpret_cast<int32_t *>(r + rec.ids)[lane] = mine ? id_l % per_rank : -1;
+        reinterpret_cast<float *>(r + rec.weights)[lane] = w_l;
+      }
+      if (t >= counts[d] && lane < width)
+        reinterpret_cast<int32_t *>(records + ((size_t)d * tokens + t) * rec.bytes + rec.ids)[lane] = -1;
+    }
+    if (!live) continue;
+    const int d0 = __ffs(live) - 1;
+    uint8_t *first = records + (size_t)__shfl_sync(0xffffffffu, pos_l, d0) * rec.bytes;
+    const T *src = x + (size_t)t * cols;
+    for (int g = lane; g < gpr; g += 32) {
+      float v[16];
+      load16_vec(src + (size_t)g * 16, v);
+      uint2 c;
+      first[rec.sf + g] = encode_group16_regs(v, global, c);
+      *reinterpret_cast<uint2 *>(first + (size_t)g * 8) = c;
+    }
+    __syncwarp();
+    const int vecs = (int)((rec.sf + (size_t)gpr + 15) / 16);
+    unsigned rest = live & (live - 1);
+    while (rest) {
+      const int d = __ffs(rest) - 1;
+      rest &= rest - 1;
+      uint8_t *r = records + (size_t)__shfl_sync(0xffffffffu, pos_l, d) * rec.bytes;
+      for (int i = lane; i < vecs; i += 32)
+        reinterpret_cast<uint4 *>(r)[i] = reinterpret_cast<const uint4 *>(first)[i];
+    }
+  }
+}
+
+// The received records' routes as dense tables: ids [rows, width] (-1 where
+// the slot is another rank's, or the record is empty) and weights.
+__global__ void ep_unpack_kernel(const uint8_t *records, int rows, EpRecord rec, int width, int32_t *ids_out,
+                                 float *w_out) {
+  pdl_enter();
+  const int n = rows * width;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const uint8_t *r = records + (size_t)(i / width) * rec.bytes;
+    ids_out[i] = reinterpret_cast<const int32_t *>(r + rec.ids)[i % width];
+    w_out[i] = reinterpret_cast<const float *>(r + rec.weights)[i % width];
+  }
 }
 
 static unsigned stride_grid(size_t n) {
@@ -832,10 +989,10 @@ extern "C" size_t fpb_moe_layout_scratch_bytes(size_t tokens, size_t slots, size
   return std::max<size_t>(1, groups) * experts * sizeof(int);
 }
 
-extern "C" int fpb_moe_layout(const int32_t *ids, size_t tokens, size_t width, size_t slots, size_t experts,
-                              size_t tile_rows, size_t cap, int32_t *token_rows, int32_t *tile_experts,
-                              int32_t *inverse, size_t *ranges, int32_t *padded_rows, void *scratch,
-                              size_t scratch_bytes, void *stream) {
+static int layout_impl(const int32_t *ids, size_t tokens, size_t width, size_t slots, size_t experts,
+                       size_t tile_rows, size_t cap, int32_t *token_rows, int32_t *tile_experts, int32_t *inverse,
+                       size_t *ranges, int32_t *padded_rows, void *scratch, size_t scratch_bytes, bool masked,
+                       void *stream) {
   if (!ids || !token_rows || !tile_experts || !inverse || !ranges || !padded_rows || !scratch)
     return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_moe_layout: null pointer");
   if (tokens == 0 || slots == 0 || slots > width || experts == 0 || tile_rows == 0 || (tile_rows & (tile_rows - 1)))
@@ -888,15 +1045,15 @@ extern "C" int fpb_moe_layout(const int32_t *ids, size_t tokens, size_t width, s
     }
     launch_pdl(moe_layout_small_kernel, 1, kLayoutSmallThreads, small_smem, s,
         ids, n, (int)slots, (int)width, (int)tokens, (int)experts, (int)tile_rows, (int)cap, token_rows,
-        tile_experts, inverse, reinterpret_cast<int64_t *>(ranges), padded_rows, err);
+        tile_experts, inverse, reinterpret_cast<int64_t *>(ranges), padded_rows, err, masked);
     FPB_LAUNCH_CHECK("moe_layout_small_kernel");
     return FPB_OK;
   }
   FPB_CUDA_TRY(cudaMemsetAsync(token_rows, 0xff, cap * sizeof(int32_t), s));
   FPB_CUDA_TRY(cudaMemsetAsync(tile_experts, 0xff, cap / tile_rows * sizeof(int32_t), s));
-  FPB_CUDA_TRY(cudaMemsetAsync(inverse, 0, tokens * width * sizeof(int32_t), s));
+  FPB_CUDA_TRY(cudaMemsetAsync(inverse, masked ? 0xff : 0, tokens * width * sizeof(int32_t), s));
   moe_layout_count_kernel<<<groups, 256, experts * sizeof(int), s>>>(ids, n, (int)slots, (int)width, (int)experts,
-                                                                     cnt, err);
+                                                                     cnt, err, masked);
   FPB_LAUNCH_CHECK("moe_layout_count_kernel");
   moe_layout_scan_kernel<<<1, 1024, experts * sizeof(int), s>>>(cnt, groups, (int)experts, (int)tile_rows, (int)cap,
                                                                 tile_experts, reinterpret_cast<int64_t *>(ranges),
@@ -904,9 +1061,25 @@ extern "C" int fpb_moe_layout(const int32_t *ids, size_t tokens, size_t width, s
   FPB_LAUNCH_CHECK("moe_layout_scan_kernel");
   moe_layout_place_kernel<<<groups, kLayoutWarpsPerCta * 32, wsmem, s>>>(
       ids, n, (int)slots, (int)width, (int)experts, (int)cap, cnt, reinterpret_cast<const int64_t *>(ranges),
-      token_rows, inverse);
+      token_rows, inverse, masked);
   FPB_LAUNCH_CHECK("moe_layout_place_kernel");
   return FPB_OK;
+}
+
+extern "C" int fpb_moe_layout(const int32_t *ids, size_t tokens, size_t width, size_t slots, size_t experts,
+                              size_t tile_rows, size_t cap, int32_t *token_rows, int32_t *tile_experts,
+                              int32_t *inverse, size_t *ranges, int32_t *padded_rows, void *scratch,
+                              size_t scratch_bytes, void *stream) {
+  return layout_impl(ids, tokens, width, slots, experts, tile_rows, cap, token_rows, tile_experts, inverse, ranges,
+                     padded_rows, scratch, scratch_bytes, false, stream);
+}
+
+extern "C" int fpb_moe_layout_masked(const int32_t *ids, size_t tokens, size_t width, size_t slots, size_t experts,
+                                     size_t tile_rows, size_t cap, int32_t *token_rows, int32_t *tile_experts,
+                                     int32_t *inverse, size_t *ranges, int32_t *padded_rows, void *scratch,
+                                     size_t scratch_bytes, void *stream) {
+  return layout_impl(ids, tokens, width, slots, experts, tile_rows, cap, token_rows, tile_experts, inverse, ranges,
+                     padded_rows, scratch, scratch_bytes, true, stream);
 }
 
 extern "C" int fpb_moe_gather(const void *x, int x_dtype, size_t tokens, size_t cols, const int32_t *token_rows,
@@ -978,8 +1151,8 @@ extern "C" int fpb_moe_gather_quantize(const void *x, int x_dtype, size_t tokens
     launch_pdl(rows_encode_kernel<PlainRows<T>, true>, row_grid(tokens), 256, 0, s, tok, tokens, nullptr, nullptr, cols, amax,
                                                                              tok_packed, tok_sf, global_out);
     FPB_LAUNCH_CHECK("rows_encode_kernel(tokens)");
-    launch_pdl(gather_codes_kernel, row_grid(rows), 256, 0, s, tok_packed, tok_sf, (int)tokens, token_rows, rows, valid_rows,
-                                                        skip, cols, packed, sf_tiled);
+    launch_pdl(gather_codes_kernel, row_grid(rows), 256, 0, s, tok_packed, tok_sf, cols / 2, cols / 16, (int)tokens,
+               token_rows, rows, valid_rows, skip, cols, packed, sf_tiled);
     FPB_LAUNCH_CHECK("gather_codes_kernel");
     return (int)FPB_OK;
   });
@@ -1128,6 +1301,70 @@ extern "C" int fpb_moe_route_dest(const int32_t *ids, size_t tokens, size_t widt
   moe_route_dest_kernel<<<stride_grid(tokens * width), 256, 0, as_stream(stream)>>>(
       ids, (int)tokens, (int)width, (int)slots, (int)experts_per_rank, dest);
   FPB_LAUNCH_CHECK("moe_route_dest_kernel");
+  return FPB_OK;
+}
+
+extern "C" size_t fpb_ep_record_bytes(size_t cols, size_t width) { return ep_record(cols, width).bytes; }
+
+extern "C" int fpb_ep_dispatch(const void *x, int x_dtype, size_t tokens, size_t cols, const int32_t *ids,
+                               const float *weights, size_t width, size_t slots, size_t experts, size_t nranks,
+                               const float *amax, void *records, int32_t *positions, float *global_out,
+                               void *stream) {
+  if (!x || !ids || !weights || !amax || !records || !positions || !global_out)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_ep_dispatch: null pointer");
+  if (tokens == 0 || cols == 0 || cols % 64 || slots == 0 || slots > width || width > 32 || nranks == 0 ||
+      nranks > 32 || experts == 0 || experts % nranks || tokens * nranks > 0x7fffffffu ||
+      tokens * width > 0x7fffffffu)
+    return fail(FPB_ERR_SHAPE, "fpb_ep_dispatch: tokens %zu cols %zu slots %zu width %zu experts %zu nranks %zu",
+                tokens, cols, slots, width, experts, nranks);
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(records) & 15))
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_ep_dispatch: x and records must be 16-byte aligned");
+  cudaStream_t s = as_stream(stream);
+  const int per_rank = (int)(experts / nranks);
+  launch_pdl(ep_plan_kernel, 1, kEpPlanThreads, 0, s, ids, (int)tokens, (int)width, (int)slots, (int)experts,
+             per_rank, (int)nranks, positions, device_error_ptr());
+  FPB_LAUNCH_CHECK("ep_plan_kernel");
+  const EpRecord rec = ep_record(cols, width);
+  return with_dtype(x_dtype, [&](auto tp) {
+    using T = std::remove_const_t<std::remove_pointer_t<decltype(tp)>>;
+    launch_pdl(ep_pack_kernel<T>, row_grid(tokens), 256, 0, s, static_cast<const T *>(x), (int)tokens, (int)cols,
+               ids, weights, (int)width, (int)slots, (int)experts, per_rank, (int)nranks,
+               (const int32_t *)positions, reinterpret_cast<const uint32_t *>(amax), static_cast<uint8_t *>(records),
+               rec, global_out);
+    FPB_LAUNCH_CHECK("ep_pack_kernel");
+    return (int)FPB_OK;
+  });
+}
+
+extern "C" int fpb_ep_unpack(const void *records, size_t rows, size_t cols, size_t width, int32_t *ids,
+                             float *weights, void *stream) {
+  if (!records || !ids || !weights) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_ep_unpack: null pointer");
+  if (rows == 0 || cols == 0 || cols % 64 || width == 0 || width > 32 || rows * width > 0x7fffffffu)
+    return fail(FPB_ERR_SHAPE, "fpb_ep_unpack: rows %zu cols %zu width %zu", rows, cols, width);
+  launch_pdl(ep_unpack_kernel, stride_grid(rows * width), 256, 0, as_stream(stream),
+             static_cast<const uint8_t *>(records), (int)rows, ep_record(cols, width), (int)width, ids, weights);
+  FPB_LAUNCH_CHECK("ep_unpack_kernel");
+  return FPB_OK;
+}
+
+extern "C" int fpb_moe_gather_codes(const uint8_t *codes, size_t code_stride, const uint8_t *sf, size_t sf_stride,
+                                    size_t tokens, size_t cols, const int32_t *token_rows, size_t rows,
+                                    const int32_t *valid_rows, int flags, uint8_t *packed, uint8_t *sf_tiled,
+                                    void *stream) {
+  if (!codes || !sf || !token_rows || !packed || !sf_tiled)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_moe_gather_codes: null pointer");
+  if (tokens == 0 || tokens > 0x7fffffffu || rows == 0 || cols == 0 || cols % 64 || code_stride < cols / 2 ||
+      sf_stride < cols / 16)
+    return fail(FPB_ERR_SHAPE, "fpb_moe_gather_codes: shape");
+  if ((reinterpret_cast<uintptr_t>(codes) & 15) || code_stride % 16 || (reinterpret_cast<uintptr_t>(sf) & 3) ||
+      sf_stride % 4 || (reinterpret_cast<uintptr_t>(packed) & 15) || (reinterpret_cast<uintptr_t>(sf_tiled) & 3))
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_moe_gather_codes: alignment (codes 16 B, factors 4 B)");
+  cudaStream_t s = as_stream(stream);
+  if (cols % 256) FPB_CUDA_TRY(cudaMemsetAsync(sf_tiled, 0, sf_tiled_bytes(rows, cols), s));
+  const int32_t *skip = (flags & FPB_QUANT_SKIP_PADDING) ? token_rows : nullptr;
+  launch_pdl(gather_codes_kernel, row_grid(rows), 256, 0, s, codes, sf, code_stride, sf_stride, (int)tokens,
+             token_rows, rows, valid_rows, skip, cols, packed, sf_tiled);
+  FPB_LAUNCH_CHECK("gather_codes_kernel");
   return FPB_OK;
 }
 

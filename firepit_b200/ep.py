@@ -158,6 +158,200 @@ class DeviceOps:
         return out
 
 
+class DeviceEpOps:
+    """The fixed-capacity expert-parallel layer's steps on the GPU (C ABI),
+    every buffer allocated here, so that ``EpMoeLayer.forward`` allocates
+    nothing and can be captured in one CUDA graph.
+
+    tokens = this rank's tokens per layer call; w1 / w2 = this rank's
+    experts ([per_rank * 2I, H] with the GLU factor copy prepared, and
+    [per_rank * H, I]); nranks = ranks the experts are split over."""
+
+    def __init__(self, device, tokens: int, hidden: int, inter: int, experts: int, top_k: int, nranks: int, w1,
+                 w2, x_dtype=None):
+        import torch
+        from .moe import MoeDims, PrefillLayout
+        t = torch
+        self.torch, self.device = torch, device
+        self.tokens, self.hidden, self.inter, self.experts, self.k, self.nranks = (tokens, hidden, inter, experts,
+                                                                                   top_k, nranks)
+        self.per_rank = experts // nranks
+        self.width = 1 << (top_k - 1).bit_length()
+        self.w1, self.w2 = w1, w2
+        self.rec = int(N.lib.fpb_ep_record_bytes(hidden, self.width))
+        rows = nranks * tokens
+        self.rows = rows
+        dims = MoeDims(hidden, inter, inter, self.per_rank, top_k)
+        cap = (PrefillLayout.max_padded_rows(rows, dims, 128) + 127) // 128 * 128
+        self.cap = cap
+        i32 = dict(dtype=t.int32, device=device)
+        u8 = dict(dtype=t.uint8, device=device)
+        self.ids = t.empty(tokens, self.width, **i32)
+        self.w = t.empty(tokens, self.width, dtype=t.float32, device=device)
+        self.scal = t.zeros(4, dtype=t.float32, device=device)
+        self.send = t.empty(rows * self.rec, **u8)
+        self.recv = t.empty(rows * self.rec, **u8) if nranks > 1 else self.send
+        self.pos = t.empty(tokens * nranks + nranks, **i32)
+        self.ids_r = t.empty(rows, self.width, **i32)
+        self.w_r = t.empty(rows, self.width, dtype=t.float32, device=device)
+        self.tr = t.empty(cap, **i32)
+        self.te = t.empty(cap // 128, **i32)
+        self.inv = t.empty(rows, self.width, **i32)
+        self.rg = t.empty(self.per_rank, 2, dtype=t.int64, device=device)
+        self.pad = t.empty(1, **i32)
+        self.lscr = t.empty(int(N.lib.fpb_moe_layout_scratch_bytes(rows, top_k, self.per_rank)), **u8)
+        self.a1 = t.empty(cap, hidden // 2, **u8)
+        self.sf1 = t.empty(int(N.lib.fpb_nvfp4_act_sf_bytes(cap, hidden)), **u8)
+        self.h = t.empty(cap, inter, dtype=t.bfloat16, device=device)
+        self.a2 = t.empty(cap, inter // 2, **u8)
+        self.sf2 = t.empty(int(N.lib.fpb_nvfp4_act_sf_bytes(cap, inter)), **u8)
+        self.y2 = t.empty(cap, hidden, dtype=t.bfloat16, device=device)
+        self.ret_send = t.empty(rows, hidden, dtype=t.float32, device=device)
+        self.ret_recv = t.empty(rows, hidden, dtype=t.float32, device=device) if nranks > 1 else self.ret_send
+        self.ones = t.ones(tokens, nranks, dtype=t.float32, device=device)
+        self.out = t.empty(tokens, hidden, dtype=x_dtype or t.bfloat16, device=device)
+
+    def _s(self):
+        return self.torch.cuda.current_stream(self.device).cuda_stream
+
+    def route(self, logits):
+        N.call("fpb_moe_topk", logits.data_ptr(), logits.shape[1], None, self.tokens, self.experts, self.k,
+               self.width, self.ids.data_ptr(), self.w.data_ptr(), self._s())
+        return self.ids, self.w
+
+    def amax(self, x):
+        N.call("fpb_act_amax", x.data_ptr(), _dt(x), x.numel(), self.scal[1:2].data_ptr(), 0, self._s())
+        return self.scal[1:2].view(self.torch.int32)
+
+    def dispatch(self, x, ids, w, amax):
+        N.call("fpb_ep_dispatch", x.data_ptr(), _dt(x), self.tokens, self.hidden, ids.data_ptr(), w.data_ptr(),
+               self.width, self.k, self.experts, self.nranks, amax.data_ptr(), self.send.data_ptr(),
+               self.pos.data_ptr(), self.scal[0:1].data_ptr(), self._s())
+        return self.send, self.pos
+
+    def experts_gate_up(self, recv):
+        """Unpack the received records' routes, lay them out by local expert,
+        gather their NVFP4 rows, gate/up GEMM + SwiGLU; returns the h amax
+        word (to be all-reduced before ``experts_down``)."""
+        s, BF, skip = self._s(), N.FPB_BF16, N.FPB_QUANT_SKIP_PADDING
+        rows, H = self.rows, self.hidden
+        N.call("fpb_ep_unpack", recv.data_ptr(), rows, H, self.width, self.ids_r.data_ptr(), self.w_r.data_ptr(), s)
+        N.call("fpb_moe_layout_masked", self.ids_r.data_ptr(), rows, self.width, self.k, self.per_rank, 128, self.cap,
+               self.tr.data_ptr(), self.te.data_ptr(), self.inv.data_ptr(), self.rg.data_ptr(), self.pad.data_ptr(),
+               self.lscr.data_ptr(), self.lscr.numel(), s)
+        N.call("fpb_moe_gather_codes", recv.data_ptr(), self.rec, recv.data_ptr() + H // 2, self.rec, rows, H,
+               self.tr.data_ptr(), self.cap, self.pad.data_ptr(), skip, self.a1.data_ptr(), self.sf1.data_ptr(), s)
+        N.call("fpb_nvfp4_grouped_gemm_swiglu_q", self.w1.handle, self.a1.data_ptr(), self.sf1.data_ptr(),
+               self.scal.data_ptr(), self.cap, self.te.data_ptr(), self.tr.data_ptr(), self.inter, self.h.data_ptr(),
+               BF, self.scal[3:].data_ptr(), s)
+        return self.scal[3:4].view(self.torch.int32)
+
+    def experts_down(self):
+        """h quantize (global from the reduced amax), down GEMM, and each
+        record's partial sum (f32, its local routes in slot order) into
+        ret_send."""
+        s, BF, skip = self._s(), N.FPB_BF16, N.FPB_QUANT_SKIP_PADDING
+        rows, H = self.rows, self.hidden
+        N.call("fpb_rows_quantize", self.h.data_ptr(), BF, self.cap, self.pad.data_ptr(), self.tr.data_ptr(),
+               self.inter, self.a2.data_ptr(), self.sf2.data_ptr(), self.scal[2:].data_ptr(), self.scal[3:].data_ptr(),
+               N.FPB_QUANT_AMAX_GIVEN | skip, s)
+        N.call("fpb_nvfp4_grouped_gemm_q", self.w2.handle, self.a2.data_ptr(), self.sf2.data_ptr(),
+               self.scal[2:].data_ptr(), self.cap, self.te.data_ptr(), self.tr.data_ptr(), H, self.y2.data_ptr(), BF,
+               s)
+        N.call("fpb_moe_combine", self.y2.data_ptr(), BF, self.cap, H, self.inv.data_ptr(), self.w_r.data_ptr(), rows,
+               self.width, self.k, self.ret_send.data_ptr(), N.FPB_F32, s)
+        return self.ret_send
+
+    def finish(self, ret, pos):
+        """out[t] = sum over ranks d (in rank order) of the partial that rank
+        d returned for token t."""
+        N.call("fpb_moe_combine", ret.data_ptr(), N.FPB_F32, self.rows, self.hidden, pos.data_ptr(),
+               self.ones.data_ptr(), self.tokens, self.nranks, self.nranks, self.out.data_ptr(), _dt(self.out),
+               self._s())
+        return self.out
+
+
+class EpMoeLayer:
+    """Expert-parallel MoE layer with fixed capacity: one record per (token,
+    destination rank) in equal chunks, so neither all-to-all needs counts read
+    by the host and ``forward`` can be captured in one CUDA graph per rank.
+
+    1. top-k of the rank's tokens; amax of x all-reduced (MAX) so the NVFP4
+       global is the single-GPU layer's;
+    2. ``dispatch``: each token encoded to NVFP4 once and written, with its
+       routes, into the chunk of every rank that owns one of its experts;
+    3. all-to-all of the chunks;
+    4. the receiver's experts over every record it got (masked layout, NVFP4
+       row gather, gate/up GEMM + SwiGLU with the h amax all-reduced, h
+       quantize, down GEMM) and one partial sum per record (its local routes,
+       slot order, f32);
+    5. all-to-all of the partials back; the source sums each token's
+       partials in rank order and rounds once to x's dtype.
+
+    Against the single-GPU layer over all ranks' tokens the encodings are the
+    same bit for bit; the output differs only by the grouping of the f32 sum
+    over a token's routes (rank by rank) before the one rounding.
+
+    ``comm`` is a firepit_b200.comm.Comm (NCCL through the C ABI) or None
+    with ``group`` a torch.distributed group (gloo on CPU); with one rank
+    there is no collective."""
+
+    def __init__(self, ops, comm=None, group=None):
+        self.ops, self.comm, self.group = ops, comm, group
+        if comm is not None:
+            self.nranks = comm.nranks
+        else:
+            import torch.distributed as dist
+            self.nranks = dist.get_world_size(group) if dist.is_initialized() else 1
+        if self.nranks != ops.nranks:
+            raise ValueError(f"ops built for {ops.nranks} ranks, communicator has {self.nranks}")
+
+    def _all_reduce_max(self, a):
+        if self.nranks == 1:
+            return a
+        if self.comm is not None:
+            self.comm.all_reduce_max_bits(a)
+        else:
+            import torch.distributed as dist
+            dist.all_reduce(a, op=dist.ReduceOp.MAX, group=self.group)
+        return a
+
+    def _exchange(self, send, recv):
+        """Equal chunks: chunk p of send to rank p, chunk p of recv from it."""
+        if self.nranks == 1:
+            return send
+        n = self.nranks
+        if self.comm is not None:
+            self.comm.all_to_all(send.view(n, -1), [1] * n, recv.view(n, -1), [1] * n)
+        else:
+            import torch.distributed as dist
+            dist.all_to_all_single(recv, send, group=self.group)
+        return recv
+
+    STAGES = ("route_dispatch", "all_to_all_out", "experts", "all_to_all_back", "combine")
+
+    def forward(self, x, logits, mark=None):
+        """x [tokens, H], router logits [tokens, experts] (f32) -> [tokens, H]
+        (the ops' output buffer).  ``mark(i)`` (optional) is called after
+        stage i of ``STAGES`` (e.g. to record CUDA events)."""
+        ops = self.ops
+        mark = mark or (lambda i: None)
+        ids, w = ops.route(logits)
+        amax = self._all_reduce_max(ops.amax(x))
+        send, pos = ops.dispatch(x, ids, w, amax)
+        mark(0)
+        recv = self._exchange(send, ops.recv)
+        mark(1)
+        self._all_reduce_max(ops.experts_gate_up(recv))
+        ret = ops.experts_down()
+        mark(2)
+        back = self._exchange(ret, ops.ret_recv)
+        mark(3)
+        out = ops.finish(back, pos)
+        mark(4)
+        return out
+
+
 def _dt(t) -> int:
     from .gemv import _dtype_code
     return _dtype_code(t)

@@ -437,6 +437,15 @@ int fpb_moe_layout(const int32_t *ids, size_t tokens, size_t width, size_t slots
                    size_t scratch_bytes, void *stream);
 /* Device scratch fpb_moe_layout needs (per-CTA expert counts). */
 size_t fpb_moe_layout_scratch_bytes(size_t tokens, size_t slots, size_t experts);
+/* fpb_moe_layout where an id of -1 is a route that is not there (the
+ * expert-parallel receiver's slots owned by other ranks): it takes no row, its
+ * inverse entry is -1 (every unused slot's is) and it is no error; other ids
+ * outside [0, experts) are device error 401 as above.  fpb_moe_combine skips
+ * slots whose inverse is negative. */
+int fpb_moe_layout_masked(const int32_t *ids, size_t tokens, size_t width, size_t slots, size_t experts,
+                          size_t tile_rows, size_t cap, int32_t *token_rows, int32_t *tile_experts,
+                          int32_t *inverse, size_t *ranges, int32_t *padded_rows, void *scratch,
+                          size_t scratch_bytes, void *stream);
 /* gather_prefill_view (moe.rs:71-89, 705-733): out [rows, cols] (f32/bf16),
  * row r = x[token_rows[r]] or zeros. */
 int fpb_moe_gather(const void *x, int x_dtype, size_t tokens, size_t cols, const int32_t *token_rows,
@@ -517,6 +526,49 @@ int fpb_moe_route_dest(const int32_t *ids, size_t tokens, size_t width, size_t s
                        int32_t *dest, void *stream);
 int fpb_moe_route_meta(const int32_t *ids, const int32_t *inverse, size_t tokens, size_t width, size_t slots,
                        size_t experts_per_rank, size_t rows, int32_t *send_expert, void *stream);
+
+/* Expert parallel with fixed capacity: one record per (token, destination
+ * rank), never one per route, in chunks of equal size, so the all-to-alls
+ * need no host-read counts and a layer is one CUDA graph.
+ * A record (fpb_ep_record_bytes(cols, width) bytes, a multiple of 16) holds
+ * the token's NVFP4 row - codes [cols/2] at offset 0, row-major e4m3 factors
+ * [cols/16] at offset cols/2 - then int32 ids [width] (receiver-local expert
+ * of each slot, -1 where another rank owns it or the record is empty) and f32
+ * routing weights [width], each region 16-byte aligned.
+ * fpb_ep_dispatch: ids / weights [tokens, width] (fpb_moe_topk's output, the
+ * first `slots` used), experts split evenly over nranks (<= 32) ranks, cols %
+ * 64 == 0, x [tokens, cols] (f32/bf16, 16-byte aligned), amax = the amax
+ * word all-reduced (MAX) over the ranks (fpb_act_amax + fpb_comm_all_reduce),
+ * so the global (amax / 2688, written to global_out) is the single-GPU
+ * layer's.  Writes records [nranks][tokens] (chunk d for rank d: the tokens
+ * that route to d in token order, then empty records) and positions
+ * [tokens * nranks + nranks] int32: positions[t * nranks + d] = d * tokens +
+ * the token's record index in chunk d, or -1; the last nranks entries are the
+ * chunk counts.  Two launches; device error 403 on an id outside [0, experts).
+ * The receiver turns the records it got (nranks chunks) into dense route
+ * tables with fpb_ep_unpack, lays them out with fpb_moe_layout_masked and
+ * gathers the NVFP4 rows with fpb_moe_gather_codes (code_stride = sf_stride =
+ * the record size, factors at records + cols/2); after the expert GEMMs,
+ * fpb_moe_combine with f32 output gives each record's partial sum (its
+ * routes in slot order), which goes back in the same fixed chunks; the source
+ * sums the partials in rank order with fpb_moe_combine over `positions`
+ * (width = slots = nranks, weights 1). */
+size_t fpb_ep_record_bytes(size_t cols, size_t width);
+int fpb_ep_dispatch(const void *x, int x_dtype, size_t tokens, size_t cols, const int32_t *ids,
+                    const float *weights, size_t width, size_t slots, size_t experts, size_t nranks,
+                    const float *amax, void *records, int32_t *positions, float *global_out, void *stream);
+/* ids / weights [rows, width] from `rows` records (rows = nranks * tokens). */
+int fpb_ep_unpack(const void *records, size_t rows, size_t cols, size_t width, int32_t *ids, float *weights,
+                  void *stream);
+/* The layout rows' NVFP4 codes from rows encoded once: row r of the layout
+ * copies token token_rows[r]'s codes (codes + t * code_stride, cols/2 bytes)
+ * and factors (sf + t * sf_stride, cols/16 bytes) into packed [rows, cols/2]
+ * and the tiled factor layout; token -1 rows are zeros (skipped with
+ * FPB_QUANT_SKIP_PADDING in flags).  cols % 64 == 0; codes and code_stride
+ * 16-byte aligned, sf and sf_stride 4-byte aligned. */
+int fpb_moe_gather_codes(const uint8_t *codes, size_t code_stride, const uint8_t *sf, size_t sf_stride,
+                         size_t tokens, size_t cols, const int32_t *token_rows, size_t rows,
+                         const int32_t *valid_rows, int flags, uint8_t *packed, uint8_t *sf_tiled, void *stream);
 
 /* ---- decode step of the hybrid MoE decoder -----------------
  * The operations around the quantized matmuls in firepit's decode step

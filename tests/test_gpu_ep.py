@@ -82,3 +82,86 @@ def test_expert_parallel_two_gpus_matches_single_gpu():
         assert err == 0
         assert np.all(np.isfinite(a)) and np.abs(b).max() > 0
         assert np.array_equal(a, b), f"rank {rank}: max diff {np.abs(a - b).max()}"
+
+
+def _rank_fixed(rank, world, port, q):
+    """EpMoeLayer over the library's NCCL communicator, eager and as one
+    CUDA graph per rank (replayed twice)."""
+    sys.path[:0] = [ROOT, HERE]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    import firepit_b200 as F
+    from firepit_b200.comm import Comm
+    from firepit_b200.ep import DeviceEpOps, DeviceOps, EpMoeLayer, ep_moe_forward
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    comm = None
+    graph = None
+    try:
+        comm = Comm.from_torch()
+        w1 = F.synth_normal((E * 2 * I, H), seed=1, stream_id=1, std=0.02, device=dev)
+        w2 = F.synth_normal((E * H, I), seed=2, stream_id=1, std=0.02, device=dev)
+        p1, s1, g1 = F.quantize_nvfp4(w1, 2 * I)
+        p2, s2, g2 = F.quantize_nvfp4(w2, H)
+        per = E // world
+        r1 = slice(rank * per * 2 * I, (rank + 1) * per * 2 * I)
+        r2 = slice(rank * per * H, (rank + 1) * per * H)
+        L1 = F.Nvfp4Matrix.from_device(p1[r1].contiguous(), s1[r1].contiguous(), g1[r1].contiguous(), per * 2 * I, H)
+        L2 = F.Nvfp4Matrix.from_device(p2[r2].contiguous(), s2[r2].contiguous(), g2[r2].contiguous(), per * H, I)
+        L1.prepare_glu(I)
+        A1 = F.Nvfp4Matrix.from_device(p1, s1, g1, E * 2 * I, H)
+        A2 = F.Nvfp4Matrix.from_device(p2, s2, g2, E * H, I)
+        x_all = F.synth_normal((world * T, H), seed=0, stream_id=0, dtype=torch.bfloat16, device=dev)
+        lg_all = F.synth_normal((world * T, E), seed=0, stream_id=7, device=dev)
+        rows = slice(rank * T, (rank + 1) * T)
+        x, lg = x_all[rows].contiguous(), lg_all[rows].contiguous()
+        layer = EpMoeLayer(DeviceEpOps(dev, T, H, I, E, K, world, L1, L2), comm=comm)
+        y_eager = layer.forward(x, lg).clone()
+        y_one = ep_moe_forward(DeviceOps(dev), x_all, lg_all, K, E, A1, A2, world=1)[rows]
+        torch.cuda.synchronize()
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            y_g = layer.forward(x, lg)
+        for _ in range(2):
+            graph.replay()
+        torch.cuda.synchronize()
+        q.put((rank, F.device_error(), y_eager.float().cpu().numpy().tobytes(), y_g.float().cpu().numpy().tobytes(),
+               y_one.float().cpu().numpy().tobytes()))
+    finally:
+        graph = None
+        if comm is not None:
+            comm.destroy()
+        dist.destroy_process_group()
+
+
+def test_fixed_capacity_two_gpus_match_single_gpu():
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_fixed, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, err, eager, graphed, one in results:
+        a = np.frombuffer(eager, np.float32)
+        g = np.frombuffer(graphed, np.float32)
+        b = np.frombuffer(one, np.float32)
+        assert err == 0
+        assert np.array_equal(a, g), f"rank {rank}: graph replay differs from the eager call"
+        assert np.all(np.isfinite(a)) and np.abs(b).max() > 0
+        diff = np.abs(a - b)
+        assert np.all(diff <= 2.0 ** -7 * np.abs(b) + 1e-4 * np.abs(b).max()), f"rank {rank}: {diff.max()}"
+        assert np.mean(diff == 0) > 0.9

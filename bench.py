@@ -1424,8 +1424,11 @@ def moe_ep_arm(args):
     del gp, gs, gg, dp, ds, dg
     wr = F.synth_normal((MOE_E, MOE_H), seed=0, stream_id=99, std=0.02, dtype=torch.bfloat16, device=dev)
     x = F.synth_normal((T, MOE_H), seed=rank, stream_id=0, dtype=torch.bfloat16, device=dev)
-    ops = DeviceEpOps(dev, T, MOE_H, MOE_I, MOE_E, MOE_K, world, W1, W2)
+    # peer mode on more than one GPU: dispatch and the partial combine store
+    # straight into the other GPUs' receive buffers (CUDA IPC over NVLink)
+    ops = DeviceEpOps(dev, T, MOE_H, MOE_I, MOE_E, MOE_K, world, W1, W2, ipc=world > 1)
     layer = EpMoeLayer(ops, comm=comm())
+    layer.connect_peers()
     logits = torch.empty(T, MOE_E, device=dev)
 
     def step(xin, ev=None):
@@ -1503,6 +1506,11 @@ def moe_ep_arm(args):
     e2e_value = flops / (te.item() / e2e_steps * 1e-3) / 1e12
     del graph, e2e_graph
     assert F.device_error() == 0
+    torch.cuda.synchronize()
+    dist_sync()
+    layer.close_peers()
+    dist_sync()  # no rank frees a buffer another still maps
+    ops.free()
     nbytes = world * moe_bytes(T, per)
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
     hbm = float(peaks.get("hbm_gbs", 6650.0))
@@ -1513,6 +1521,8 @@ def moe_ep_arm(args):
                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
                "scaling": "weak", "vs_baseline": None,
                "dtype": "nvfp4 x nvfp4 experts (f32 accumulate), bf16 router, nvfp4 dispatch, f32 partials back",
+               "exchange": "peer stores over NVLink (CUDA IPC) from the dispatch and partial-combine kernels, "
+                           "one-word all-reduce barriers" if world > 1 else "none",
                "data": "synthetic (seeded Philox: W N(0,0.02) per expert, x N(0,1) per rank)",
                "config": moe_config(T, world, ep=True),
                "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",

@@ -70,6 +70,7 @@ class GemvSegment(C.Structure):
 
 
 FPB_COMM_ID_BYTES = 128
+FPB_IPC_HANDLE_BYTES = 64
 sizep = C.POINTER(C.c_size_t)
 
 # name -> (restype, argtypes)
@@ -142,6 +143,13 @@ SIGNATURES: dict[str, tuple] = {
     "fpb_ep_record_bytes": (sz, [sz, sz]),
     "fpb_ep_dispatch": (i32, [vp, i32, sz, sz, vp, vp, sz, sz, sz, sz, vp, vp, vp, vp, vp]),
     "fpb_ep_unpack": (i32, [vp, sz, sz, sz, vp, vp, vp]),
+    "fpb_ep_dispatch_chunks": (i32, [vp, i32, sz, sz, vp, vp, sz, sz, sz, sz, vp, vp, i32, vp, vp, vp]),
+    "fpb_moe_combine_chunks": (i32, [vp, i32, sz, sz, vp, vp, sz, sz, sz, vp, sz, i32, vp]),
+    "fpb_ipc_alloc": (i32, [sz, C.POINTER(vp)]),
+    "fpb_ipc_free": (i32, [vp]),
+    "fpb_ipc_get_handle": (i32, [vp, vp]),
+    "fpb_ipc_open": (i32, [vp, C.POINTER(vp)]),
+    "fpb_ipc_close": (i32, [vp]),
     "fpb_moe_gather": (i32, [vp, i32, sz, sz, vp, sz, vp, i32, vp]),
     "fpb_moe_gather_quantize": (i32, [vp, i32, sz, sz, vp, sz, vp, vp, vp, vp, vp, i32, vp, sz, vp]),
     "fpb_moe_gather_quantize_workspace_bytes": (sz, [sz, sz]),

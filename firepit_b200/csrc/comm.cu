@@ -255,3 +255,44 @@ extern "C" int fpb_comm_all_to_all(fpb_comm *c, const void *send, const size_t *
     return FPB_OK;
   });
 }
+
+// ---- peer memory (CUDA IPC) ----------------------------------------------------------------
+// Buffers that other processes (one per GPU) map into their address space,
+// so that a kernel writes another GPU's buffer with plain stores over NVLink:
+// the expert-parallel layer's receive buffers.  An IPC handle names a whole
+// cudaMalloc allocation, so these buffers are allocated here, one allocation
+// each.
+extern "C" int fpb_ipc_alloc(size_t bytes, void **ptr) {
+  if (!ptr || bytes == 0) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_ipc_alloc: null pointer or zero size");
+  *ptr = nullptr;
+  FPB_CUDA_TRY(cudaMalloc(ptr, bytes));
+  return FPB_OK;
+}
+
+extern "C" int fpb_ipc_free(void *ptr) {
+  if (ptr) FPB_CUDA_TRY(cudaFree(ptr));
+  return FPB_OK;
+}
+
+extern "C" int fpb_ipc_get_handle(const void *ptr, uint8_t handle[FPB_IPC_HANDLE_BYTES]) {
+  static_assert(sizeof(cudaIpcMemHandle_t) == FPB_IPC_HANDLE_BYTES, "IPC handle size");
+  if (!ptr || !handle) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_ipc_get_handle: null pointer");
+  cudaIpcMemHandle_t h;
+  FPB_CUDA_TRY(cudaIpcGetMemHandle(&h, const_cast<void *>(ptr)));
+  std::memcpy(handle, &h, sizeof h);
+  return FPB_OK;
+}
+
+extern "C" int fpb_ipc_open(const uint8_t handle[FPB_IPC_HANDLE_BYTES], void **ptr) {
+  if (!handle || !ptr) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_ipc_open: null pointer");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof h);
+  *ptr = nullptr;
+  FPB_CUDA_TRY(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  return FPB_OK;
+}
+
+extern "C" int fpb_ipc_close(void *ptr) {
+  if (ptr) FPB_CUDA_TRY(cudaIpcCloseMemHandle(ptr));
+  return FPB_OK;
+}

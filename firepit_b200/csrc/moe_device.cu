@@ -575,10 +575,15 @@ __global__ void swiglu_kernel(const T *gu, size_t rows, size_t cols, O *out) {
 template <typename R, typename O>
 __global__ void combine_kernel(const R *routed, int routed_rows, size_t cols, const int32_t *inverse,
                                const float *weights, int width, int slots, const float *residual, const float *gamma,
-                               float inv_h, float eps, O *out, float *normed) {
+                               float inv_h, float eps, O *out, float *normed, void *const *out_chunks,
+                               int chunk_rows) {
   pdl_enter();
   extern __shared__ float red[];
   const int t = blockIdx.x;
+  // out_chunks (device table, nullable): token t's row is row t % chunk_rows
+  // of chunk t / chunk_rows, e.g. in another GPU's memory (plain peer stores)
+  O *orow = out_chunks ? static_cast<O *>(out_chunks[t / chunk_rows]) + (size_t)(t % chunk_rows) * cols
+                       : out + (size_t)t * cols;
   float ss = 0.0f;
   for (size_t c8 = threadIdx.x; c8 < cols / 8; c8 += blockDim.x) {
     const size_t c = c8 * 8;
@@ -614,16 +619,19 @@ __global__ void combine_kernel(const R *routed, int routed_rows, size_t cols, co
       }
     }
     if constexpr (sizeof(O) == 4) {
-      float4 *o = reinterpret_cast<float4 *>(out + (size_t)t * cols + c);
+      float4 *o = reinterpret_cast<float4 *>(orow + c);
       o[0] = make_float4(sum[0], sum[1], sum[2], sum[3]);
       o[1] = make_float4(sum[4], sum[5], sum[6], sum[7]);
     } else {
-      *reinterpret_cast<uint4 *>(out + (size_t)t * cols + c) =
+      *reinterpret_cast<uint4 *>(orow + c) =
           make_uint4(pack_bf16x2(sum[0], sum[1]), pack_bf16x2(sum[2], sum[3]), pack_bf16x2(sum[4], sum[5]),
                      pack_bf16x2(sum[6], sum[7]));
     }
   }
-  if (!residual) return;
+  if (!residual) {
+    if (out_chunks) __threadfence_system();  // the stores reach the peer before the host-ordered barrier
+    return;
+  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
@@ -639,9 +647,9 @@ __global__ void combine_kernel(const R *routed, int routed_rows, size_t cols, co
   for (size_t c = threadIdx.x; c < cols; c += blockDim.x) {
     float x;
     if constexpr (sizeof(O) == 4)
-      x = out[(size_t)t * cols + c];
+      x = orow[c];
     else
-      x = __bfloat162float(out[(size_t)t * cols + c]);
+      x = __bfloat162float(orow[c]);
     normed[(size_t)t * cols + c] = x * scale * gamma[c];
   }
 }
@@ -746,14 +754,24 @@ __global__ void __launch_bounds__(kEpPlanThreads) ep_plan_kernel(const int32_t *
   if (tid < nranks) positions[(size_t)tokens * nranks + tid] = carry[tid];
 }
 
+// Record p (= chunk p / tokens, index p % tokens): in `records`, or, with a
+// chunk table, at chunks[chunk] + index * record bytes (another GPU's
+// receive buffer: plain peer stores over NVLink).
+__device__ __forceinline__ uint8_t *ep_rec(uint8_t *records, void *const *chunks, int tokens, size_t p,
+                                           size_t bytes) {
+  return chunks ? static_cast<uint8_t *>(chunks[p / tokens]) + (p % tokens) * bytes : records + p * bytes;
+}
+
 // One warp per token: the routes' metadata into each destination's record,
 // the empty marks of record t in every chunk past its count, and the NVFP4
-// row encoded once into the first destination's record and copied (16-byte
-// vectors, after __syncwarp) into the others.
+// row encoded once into one destination's record (this rank's own when the
+// token routes here, so that the copies read local memory) and copied
+// (16-byte vectors, after __syncwarp) into the others.
 template <typename T>
 __global__ void ep_pack_kernel(const T *x, int tokens, int cols, const int32_t *ids, const float *weights, int width,
                                int slots, int experts, int per_rank, int nranks, const int32_t *positions,
-                               const uint32_t *amax_bits, uint8_t *records, EpRecord rec, float *global_out) {
+                               const uint32_t *amax_bits, uint8_t *records, void *const *chunks, int self,
+                               EpRecord rec, float *global_out) {
   pdl_enter();
   const float global = __fdiv_rn(__uint_as_float(*amax_bits), 2688.0f);
   if (blockIdx.x == 0 && threadIdx.x == 0) *global_out = global;
@@ -772,17 +790,18 @@ __global__ void ep_pack_kernel(const T *x, int tokens, int cols, const int32_t *
     for (int d = 0; d < nranks; ++d) {
       const int p = __shfl_sync(0xffffffffu, pos_l, d);
       if (p >= 0 && lane < width) {
-        uint8_t *r = records + (size_t)p * rec.bytes;
+        uint8_t *r = ep_rec(records, chunks, tokens, (size_t)p, rec.bytes);
         const bool mine = id_l >= 0 && id_l < experts && id_l / per_rank == d;
         reinterpret_cast<int32_t *>(r + rec.ids)[lane] = mine ? id_l % per_rank : -1;
         reinterpret_cast<float *>(r + rec.weights)[lane] = w_l;
       }
       if (t >= counts[d] && lane < width)
-        reinterpret_cast<int32_t *>(records + ((size_t)d * tokens + t) * rec.bytes + rec.ids)[lane] = -1;
+        reinterpret_cast<int32_t *>(ep_rec(records, chunks, tokens, (size_t)d * tokens + t, rec.bytes) +
+                                    rec.ids)[lane] = -1;
     }
     if (!live) continue;
-    const int d0 = __ffs(live) - 1;
-    uint8_t *first = records + (size_t)__shfl_sync(0xffffffffu, pos_l, d0) * rec.bytes;
+    const int d0 = (self >= 0 && ((live >> self) & 1u)) ? self : __ffs(live) - 1;
+    uint8_t *first = ep_rec(records, chunks, tokens, (size_t)__shfl_sync(0xffffffffu, pos_l, d0), rec.bytes);
     const T *src = x + (size_t)t * cols;
     for (int g = lane; g < gpr; g += 32) {
       float v[16];
@@ -793,15 +812,16 @@ __global__ void ep_pack_kernel(const T *x, int tokens, int cols, const int32_t *
     }
     __syncwarp();
     const int vecs = (int)((rec.sf + (size_t)gpr + 15) / 16);
-    unsigned rest = live & (live - 1);
+    unsigned rest = live & ~(1u << d0);
     while (rest) {
       const int d = __ffs(rest) - 1;
       rest &= rest - 1;
-      uint8_t *r = records + (size_t)__shfl_sync(0xffffffffu, pos_l, d) * rec.bytes;
+      uint8_t *r = ep_rec(records, chunks, tokens, (size_t)__shfl_sync(0xffffffffu, pos_l, d), rec.bytes);
       for (int i = lane; i < vecs; i += 32)
         reinterpret_cast<uint4 *>(r)[i] = reinterpret_cast<const uint4 *>(first)[i];
     }
   }
+  if (chunks) __threadfence_system();  // the peer stores land before the host-ordered barrier
 }
 
 // The received records' routes as dense tables: ids [rows, width] (-1 where
@@ -1237,8 +1257,12 @@ extern "C" int fpb_rows_quantize(const void *x, int dtype, size_t rows, const in
 
 static int combine_impl(const void *routed, int r_dtype, size_t routed_rows, size_t cols, const int32_t *inverse,
                         const float *weights, size_t tokens, size_t width, size_t slots, const float *residual,
-                        const float *gamma, float eps, void *out, int out_dtype, float *normed, cudaStream_t s) {
-  if (!routed || !inverse || !weights || !out) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_moe_combine: null pointer");
+                        const float *gamma, float eps, void *out, int out_dtype, float *normed, cudaStream_t s,
+                        void *const *out_chunks = nullptr, size_t chunk_rows = 0) {
+  if (!routed || !inverse || !weights || (!out && !out_chunks))
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_moe_combine: null pointer");
+  if (out_chunks && (chunk_rows == 0 || chunk_rows > 0x7fffffffu))
+    return fail(FPB_ERR_SHAPE, "fpb_moe_combine_chunks: chunk_rows %zu", chunk_rows);
   if (tokens == 0 || cols == 0 || cols % 32 || slots == 0 || slots > width || tokens > 0x7fffffffu ||
       routed_rows > 0x7fffffffu)
     return fail(FPB_ERR_SHAPE, "fpb_moe_combine: shape");
@@ -1252,11 +1276,11 @@ static int combine_impl(const void *routed, int r_dtype, size_t routed_rows, siz
     if (out_dtype == FPB_F32)
       launch_pdl(combine_kernel<R, float>, (unsigned)tokens, threads, 32 * sizeof(float), s,
           rs, (int)routed_rows, cols, inverse, weights, (int)width, (int)slots, residual, gamma, inv_h, eps,
-          static_cast<float *>(out), normed);
+          static_cast<float *>(out), normed, out_chunks, (int)chunk_rows);
     else if (out_dtype == FPB_BF16)
       launch_pdl(combine_kernel<R, __nv_bfloat16>, (unsigned)tokens, threads, 32 * sizeof(float), s,
           rs, (int)routed_rows, cols, inverse, weights, (int)width, (int)slots, residual, gamma, inv_h, eps,
-          static_cast<__nv_bfloat16 *>(out), normed);
+          static_cast<__nv_bfloat16 *>(out), normed, out_chunks, (int)chunk_rows);
     else
       return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_moe_combine: out dtype");
     FPB_LAUNCH_CHECK("combine_kernel");
@@ -1269,6 +1293,15 @@ extern "C" int fpb_moe_combine(const void *routed, int r_dtype, size_t routed_ro
                                size_t slots, void *out, int out_dtype, void *stream) {
   return combine_impl(routed, r_dtype, routed_rows, cols, inverse, weights, tokens, width, slots, nullptr, nullptr,
                       0.0f, out, out_dtype, nullptr, as_stream(stream));
+}
+
+extern "C" int fpb_moe_combine_chunks(const void *routed, int r_dtype, size_t routed_rows, size_t cols,
+                                      const int32_t *inverse, const float *weights, size_t tokens, size_t width,
+                                      size_t slots, void *const *out_chunks, size_t chunk_rows, int out_dtype,
+                                      void *stream) {
+  if (!out_chunks) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_moe_combine_chunks: null chunk table");
+  return combine_impl(routed, r_dtype, routed_rows, cols, inverse, weights, tokens, width, slots, nullptr, nullptr,
+                      0.0f, nullptr, out_dtype, nullptr, as_stream(stream), out_chunks, chunk_rows);
 }
 
 extern "C" int fpb_moe_combine_add_norm(const void *routed, int r_dtype, size_t routed_rows, size_t cols,
@@ -1306,11 +1339,11 @@ extern "C" int fpb_moe_route_dest(const int32_t *ids, size_t tokens, size_t widt
 
 extern "C" size_t fpb_ep_record_bytes(size_t cols, size_t width) { return ep_record(cols, width).bytes; }
 
-extern "C" int fpb_ep_dispatch(const void *x, int x_dtype, size_t tokens, size_t cols, const int32_t *ids,
-                               const float *weights, size_t width, size_t slots, size_t experts, size_t nranks,
-                               const float *amax, void *records, int32_t *positions, float *global_out,
-                               void *stream) {
-  if (!x || !ids || !weights || !amax || !records || !positions || !global_out)
+static int ep_dispatch_impl(const void *x, int x_dtype, size_t tokens, size_t cols, const int32_t *ids,
+                            const float *weights, size_t width, size_t slots, size_t experts, size_t nranks,
+                            const float *amax, void *records, void *const *chunks, int self, int32_t *positions,
+                            float *global_out, void *stream) {
+  if (!x || !ids || !weights || !amax || (!records && !chunks) || !positions || !global_out)
     return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_ep_dispatch: null pointer");
   if (tokens == 0 || cols == 0 || cols % 64 || slots == 0 || slots > width || width > 32 || nranks == 0 ||
       nranks > 32 || experts == 0 || experts % nranks || tokens * nranks > 0x7fffffffu ||
@@ -1319,6 +1352,7 @@ extern "C" int fpb_ep_dispatch(const void *x, int x_dtype, size_t tokens, size_t
                 tokens, cols, slots, width, experts, nranks);
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(records) & 15))
     return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_ep_dispatch: x and records must be 16-byte aligned");
+  if (self > 31) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_ep_dispatch: self rank");
   cudaStream_t s = as_stream(stream);
   const int per_rank = (int)(experts / nranks);
   launch_pdl(ep_plan_kernel, 1, kEpPlanThreads, 0, s, ids, (int)tokens, (int)width, (int)slots, (int)experts,
@@ -1330,10 +1364,29 @@ extern "C" int fpb_ep_dispatch(const void *x, int x_dtype, size_t tokens, size_t
     launch_pdl(ep_pack_kernel<T>, row_grid(tokens), 256, 0, s, static_cast<const T *>(x), (int)tokens, (int)cols,
                ids, weights, (int)width, (int)slots, (int)experts, per_rank, (int)nranks,
                (const int32_t *)positions, reinterpret_cast<const uint32_t *>(amax), static_cast<uint8_t *>(records),
-               rec, global_out);
+               chunks, self, rec, global_out);
     FPB_LAUNCH_CHECK("ep_pack_kernel");
     return (int)FPB_OK;
   });
+}
+
+extern "C" int fpb_ep_dispatch(const void *x, int x_dtype, size_t tokens, size_t cols, const int32_t *ids,
+                               const float *weights, size_t width, size_t slots, size_t experts, size_t nranks,
+                               const float *amax, void *records, int32_t *positions, float *global_out,
+                               void *stream) {
+  return ep_dispatch_impl(x, x_dtype, tokens, cols, ids, weights, width, slots, experts, nranks, amax, records,
+                          nullptr, -1, positions, global_out, stream);
+}
+
+extern "C" int fpb_ep_dispatch_chunks(const void *x, int x_dtype, size_t tokens, size_t cols, const int32_t *ids,
+                                      const float *weights, size_t width, size_t slots, size_t experts,
+                                      size_t nranks, const float *amax, void *const *chunks, int self_rank,
+                                      int32_t *positions, float *global_out, void *stream) {
+  if (!chunks) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_ep_dispatch_chunks: null chunk table");
+  if (self_rank < -1 || self_rank >= (int)std::min<size_t>(nranks, 32))
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_ep_dispatch_chunks: self_rank %d", self_rank);
+  return ep_dispatch_impl(x, x_dtype, tokens, cols, ids, weights, width, slots, experts, nranks, amax, nullptr,
+                          chunks, self_rank, positions, global_out, stream);
 }
 
 extern "C" int fpb_ep_unpack(const void *records, size_t rows, size_t cols, size_t width, int32_t *ids,

@@ -168,7 +168,7 @@ class DeviceEpOps:
     [per_rank * H, I]); nranks = ranks the experts are split over."""
 
     def __init__(self, device, tokens: int, hidden: int, inter: int, experts: int, top_k: int, nranks: int, w1,
-                 w2, x_dtype=None):
+                 w2, x_dtype=None, ipc: bool = False):
         import torch
         from .moe import MoeDims, PrefillLayout
         t = torch
@@ -189,8 +189,11 @@ class DeviceEpOps:
         self.ids = t.empty(tokens, self.width, **i32)
         self.w = t.empty(tokens, self.width, dtype=t.float32, device=device)
         self.scal = t.zeros(4, dtype=t.float32, device=device)
+        self._ipc = []
+        self.peer = False
         self.send = t.empty(rows * self.rec, **u8)
-        self.recv = t.empty(rows * self.rec, **u8) if nranks > 1 else self.send
+        self.recv = (self._ipc_buffer(rows * self.rec) if ipc else t.empty(rows * self.rec, **u8)) if nranks > 1 \
+            else self.send
         self.pos = t.empty(tokens * nranks + nranks, **i32)
         self.ids_r = t.empty(rows, self.width, **i32)
         self.w_r = t.empty(rows, self.width, dtype=t.float32, device=device)
@@ -207,9 +210,44 @@ class DeviceEpOps:
         self.sf2 = t.empty(int(N.lib.fpb_nvfp4_act_sf_bytes(cap, inter)), **u8)
         self.y2 = t.empty(cap, hidden, dtype=t.bfloat16, device=device)
         self.ret_send = t.empty(rows, hidden, dtype=t.float32, device=device)
-        self.ret_recv = t.empty(rows, hidden, dtype=t.float32, device=device) if nranks > 1 else self.ret_send
+        self.ret_recv = ((self._ipc_buffer(rows * hidden * 4).view(t.float32).view(rows, hidden) if ipc
+                          else t.empty(rows, hidden, dtype=t.float32, device=device)) if nranks > 1
+                         else self.ret_send)
+        self.barrier_word = t.zeros(1, dtype=t.int32, device=device)
         self.ones = t.ones(tokens, nranks, dtype=t.float32, device=device)
         self.out = t.empty(tokens, hidden, dtype=x_dtype or t.bfloat16, device=device)
+
+    def _ipc_buffer(self, nbytes: int):
+        """A uint8 tensor over a buffer of its own allocation (fpb_ipc_alloc),
+        which other processes can map (the receive buffers of peer mode)."""
+        import ctypes as C
+        p = C.c_void_p()
+        N.call("fpb_ipc_alloc", nbytes, C.byref(p))
+        self._ipc.append(p.value)
+
+        class _Buf:
+            __cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (p.value, False),
+                                        "version": 3, "strides": None}
+        return self.torch.as_tensor(_Buf(), device=self.device)
+
+    def connect(self, recv_chunks, ret_chunks, self_rank: int) -> None:
+        """Peer mode: recv_chunks[d] = where this rank's records for rank d go
+        (rank d's receive buffer, at this rank's chunk), ret_chunks[s] = where
+        this rank's partial sums for source s go; device pointers, e.g. of
+        buffers opened with fpb_ipc_open.  Dispatch and the partial combine
+        then store straight into them and no all-to-all runs."""
+        t = self.torch
+        if len(recv_chunks) != self.nranks or len(ret_chunks) != self.nranks:
+            raise ValueError("one chunk pointer per rank")
+        self.disp_tab = t.tensor([int(v) for v in recv_chunks], dtype=t.int64, device=self.device)
+        self.ret_tab = t.tensor([int(v) for v in ret_chunks], dtype=t.int64, device=self.device)
+        self.self_rank = int(self_rank)
+        self.peer = True
+
+    def free(self) -> None:
+        for p in self._ipc:
+            N.lib.fpb_ipc_free(p)
+        self._ipc = []
 
     def _s(self):
         return self.torch.cuda.current_stream(self.device).cuda_stream
@@ -224,6 +262,12 @@ class DeviceEpOps:
         return self.scal[1:2].view(self.torch.int32)
 
     def dispatch(self, x, ids, w, amax):
+        if self.peer:
+            N.call("fpb_ep_dispatch_chunks", x.data_ptr(), _dt(x), self.tokens, self.hidden, ids.data_ptr(),
+                   w.data_ptr(), self.width, self.k, self.experts, self.nranks, amax.data_ptr(),
+                   self.disp_tab.data_ptr(), self.self_rank, self.pos.data_ptr(), self.scal[0:1].data_ptr(),
+                   self._s())
+            return None, self.pos
         N.call("fpb_ep_dispatch", x.data_ptr(), _dt(x), self.tokens, self.hidden, ids.data_ptr(), w.data_ptr(),
                self.width, self.k, self.experts, self.nranks, amax.data_ptr(), self.send.data_ptr(),
                self.pos.data_ptr(), self.scal[0:1].data_ptr(), self._s())
@@ -258,6 +302,10 @@ class DeviceEpOps:
         N.call("fpb_nvfp4_grouped_gemm_q", self.w2.handle, self.a2.data_ptr(), self.sf2.data_ptr(),
                self.scal[2:].data_ptr(), self.cap, self.te.data_ptr(), self.tr.data_ptr(), H, self.y2.data_ptr(), BF,
                s)
+        if self.peer:
+            N.call("fpb_moe_combine_chunks", self.y2.data_ptr(), BF, self.cap, H, self.inv.data_ptr(),
+                   self.w_r.data_ptr(), rows, self.width, self.k, self.ret_tab.data_ptr(), self.tokens, N.FPB_F32, s)
+            return None
         N.call("fpb_moe_combine", self.y2.data_ptr(), BF, self.cap, H, self.inv.data_ptr(), self.w_r.data_ptr(), rows,
                self.width, self.k, self.ret_send.data_ptr(), N.FPB_F32, s)
         return self.ret_send
@@ -316,6 +364,56 @@ class EpMoeLayer:
             dist.all_reduce(a, op=dist.ReduceOp.MAX, group=self.group)
         return a
 
+    def _barrier(self):
+        """Orders every rank's earlier peer stores before this rank's next
+        reads: a one-word all-reduce on the stream."""
+        if self.nranks == 1:
+            return
+        self._all_reduce_max(self.ops.barrier_word)  # MAX of zeros: the word stays 0
+
+    def connect_peers(self) -> None:
+        """Peer mode over NVLink (ops built with ``ipc=True``): every rank
+        names its receive buffers with CUDA IPC handles, the handles go round
+        over torch.distributed (host), and each rank opens the others', so
+        dispatch and the partial combine store straight into the other GPUs'
+        buffers and a one-word all-reduce replaces each all-to-all."""
+        import ctypes as C
+        import torch.distributed as dist
+        ops, n = self.ops, self.nranks
+        if n == 1:
+            return
+        me = self.comm.rank if self.comm is not None else dist.get_rank(self.group)
+
+        def handle(ptr):
+            buf = (C.c_uint8 * N.FPB_IPC_HANDLE_BYTES)()
+            N.call("fpb_ipc_get_handle", ptr, buf)
+            return bytes(buf)
+
+        mine = (handle(ops.recv.data_ptr()), handle(ops.ret_recv.data_ptr()))
+        every = [None] * n
+        dist.all_gather_object(every, mine, group=self.group)
+        self._opened = []
+        bases = []
+        for r in range(n):
+            if r == me:
+                bases.append((ops.recv.data_ptr(), ops.ret_recv.data_ptr()))
+                continue
+            pair = []
+            for h in every[r]:
+                p = C.c_void_p()
+                N.call("fpb_ipc_open", (C.c_uint8 * N.FPB_IPC_HANDLE_BYTES).from_buffer_copy(h), C.byref(p))
+                self._opened.append(p.value)
+                pair.append(p.value)
+            bases.append(tuple(pair))
+        T = ops.tokens
+        ops.connect([bases[d][0] + me * T * ops.rec for d in range(n)],
+                    [bases[s][1] + me * T * ops.hidden * 4 for s in range(n)], me)
+
+    def close_peers(self) -> None:
+        for p in getattr(self, "_opened", []):
+            N.lib.fpb_ipc_close(p)
+        self._opened = []
+
     def _exchange(self, send, recv):
         """Equal chunks: chunk p of send to rank p, chunk p of recv from it."""
         if self.nranks == 1:
@@ -328,7 +426,7 @@ class EpMoeLayer:
             dist.all_to_all_single(recv, send, group=self.group)
         return recv
 
-    STAGES = ("route_dispatch", "all_to_all_out", "experts", "all_to_all_back", "combine")
+    STAGES = ("route_dispatch", "exchange_out", "experts", "exchange_back", "combine")
 
     def forward(self, x, logits, mark=None):
         """x [tokens, H], router logits [tokens, experts] (f32) -> [tokens, H]
@@ -340,12 +438,21 @@ class EpMoeLayer:
         amax = self._all_reduce_max(ops.amax(x))
         send, pos = ops.dispatch(x, ids, w, amax)
         mark(0)
-        recv = self._exchange(send, ops.recv)
+        peer = getattr(ops, "peer", False)
+        if peer:
+            self._barrier()
+            recv = ops.recv
+        else:
+            recv = self._exchange(send, ops.recv)
         mark(1)
         self._all_reduce_max(ops.experts_gate_up(recv))
         ret = ops.experts_down()
         mark(2)
-        back = self._exchange(ret, ops.ret_recv)
+        if peer:
+            self._barrier()
+            back = ops.ret_recv
+        else:
+            back = self._exchange(ret, ops.ret_recv)
         mark(3)
         out = ops.finish(back, pos)
         mark(4)

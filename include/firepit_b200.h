@@ -510,6 +510,13 @@ int fpb_moe_combine(const void *routed, int r_dtype, size_t routed_rows, size_t 
                     void *stream);
 /* combine_add_norm_{view,prefill} (moe.rs:111-147, 824-859): out = residual +
  * combine, normed = out * rsqrt(mean(out^2) + eps) * gamma (f32). */
+/* fpb_moe_combine with token t's output row at row t % chunk_rows of
+ * out_chunks[t / chunk_rows] (a device table of pointers, each 16-byte
+ * aligned; e.g. other GPUs' buffers, written with plain peer stores and a
+ * system-scope fence at the end, as fpb_ep_dispatch_chunks). */
+int fpb_moe_combine_chunks(const void *routed, int r_dtype, size_t routed_rows, size_t cols,
+                           const int32_t *inverse, const float *weights, size_t tokens, size_t width, size_t slots,
+                           void *const *out_chunks, size_t chunk_rows, int out_dtype, void *stream);
 int fpb_moe_combine_add_norm(const void *routed, int r_dtype, size_t routed_rows, size_t cols,
                              const int32_t *inverse, const float *weights, size_t tokens, size_t width,
                              size_t slots, const float *residual, const float *gamma, float eps, float *out,
@@ -557,6 +564,18 @@ size_t fpb_ep_record_bytes(size_t cols, size_t width);
 int fpb_ep_dispatch(const void *x, int x_dtype, size_t tokens, size_t cols, const int32_t *ids,
                     const float *weights, size_t width, size_t slots, size_t experts, size_t nranks,
                     const float *amax, void *records, int32_t *positions, float *global_out, void *stream);
+/* fpb_ep_dispatch writing through a device table of nranks chunk pointers
+ * (chunks[d] = where chunk d's `tokens` records go, each 16-byte aligned),
+ * e.g. straight into each destination GPU's receive buffer (its chunk for
+ * this rank, opened with fpb_ipc_open): plain peer stores over NVLink, no
+ * all-to-all.  The kernel ends with a system-scope fence; the caller orders
+ * the receivers' reads after it with a barrier on the stream (e.g. a
+ * one-word fpb_comm_all_reduce).  self_rank (-1 if none): the chunk in this
+ * GPU's memory, where each row is encoded before being copied to the others. */
+int fpb_ep_dispatch_chunks(const void *x, int x_dtype, size_t tokens, size_t cols, const int32_t *ids,
+                           const float *weights, size_t width, size_t slots, size_t experts, size_t nranks,
+                           const float *amax, void *const *chunks, int self_rank, int32_t *positions,
+                           float *global_out, void *stream);
 /* ids / weights [rows, width] from `rows` records (rows = nranks * tokens). */
 int fpb_ep_unpack(const void *records, size_t rows, size_t cols, size_t width, int32_t *ids, float *weights,
                   void *stream);
@@ -706,6 +725,17 @@ int fpb_moe_decode_combine_add_norm(const float *routed, const int32_t *map, con
  * collectives are enqueued on `stream` (asynchronous, capturable like any
  * NCCL call); every rank must make the same calls in the same order. */
 #define FPB_COMM_ID_BYTES 128
+/* Peer memory for kernels that store into another GPU's buffers (the
+ * expert-parallel chunks): fpb_ipc_alloc makes a device buffer of its own
+ * allocation, fpb_ipc_get_handle names it for other processes of the node,
+ * fpb_ipc_open maps a peer's buffer (peer access enabled lazily),
+ * fpb_ipc_close unmaps it, fpb_ipc_free frees an fpb_ipc_alloc buffer. */
+#define FPB_IPC_HANDLE_BYTES 64
+int fpb_ipc_alloc(size_t bytes, void **ptr);
+int fpb_ipc_free(void *ptr);
+int fpb_ipc_get_handle(const void *ptr, uint8_t handle[FPB_IPC_HANDLE_BYTES]);
+int fpb_ipc_open(const uint8_t handle[FPB_IPC_HANDLE_BYTES], void **ptr);
+int fpb_ipc_close(void *ptr);
 typedef struct fpb_comm fpb_comm;
 /* Extra element types of the collectives (besides FPB_F32, FPB_BF16). */
 enum { FPB_COMM_U32 = 2, FPB_COMM_I32 = 3, FPB_COMM_BYTES = 4 };

@@ -100,7 +100,7 @@ def _rank_fixed(rank, world, port, q):
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
     comm = None
-    graph = None
+    graph = graph_p = layer_p = None
     try:
         comm = Comm.from_torch()
         w1 = F.synth_normal((E * 2 * I, H), seed=1, stream_id=1, std=0.02, device=dev)
@@ -131,10 +131,29 @@ def _rank_fixed(rank, world, port, q):
         for _ in range(2):
             graph.replay()
         torch.cuda.synchronize()
+        # peer mode: the chunks stored straight into the other GPU's buffers (CUDA IPC), barriers instead of
+        # all-to-alls; the same sums, so the same bits as the all-to-all form
+        layer_p = EpMoeLayer(DeviceEpOps(dev, T, H, I, E, K, world, L1, L2, ipc=True), comm=comm)
+        layer_p.connect_peers()
+        y_peer = layer_p.forward(x, lg).clone()
+        torch.cuda.synchronize()
+        graph_p = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph_p, stream=s):
+            y_pg = layer_p.forward(x, lg)
+        for _ in range(3):
+            graph_p.replay()
+        torch.cuda.synchronize()
+        same = bool(torch.equal(y_peer, y_eager)) and bool(torch.equal(y_pg, y_eager))
         q.put((rank, F.device_error(), y_eager.float().cpu().numpy().tobytes(), y_g.float().cpu().numpy().tobytes(),
-               y_one.float().cpu().numpy().tobytes()))
+               y_one.float().cpu().numpy().tobytes(), same))
     finally:
-        graph = None
+        graph = graph_p = None
+        if layer_p is not None:
+            torch.cuda.synchronize()
+            dist.barrier()
+            layer_p.close_peers()
+            dist.barrier()  # no rank frees a buffer another still maps
+            layer_p.ops.free()
         if comm is not None:
             comm.destroy()
         dist.destroy_process_group()
@@ -155,7 +174,8 @@ def test_fixed_capacity_two_gpus_match_single_gpu():
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    for rank, err, eager, graphed, one in results:
+    for rank, err, eager, graphed, one, peer_same in results:
+        assert peer_same, f"rank {rank}: peer-store mode differs from the all-to-all form"
         a = np.frombuffer(eager, np.float32)
         g = np.frombuffer(graphed, np.float32)
         b = np.frombuffer(one, np.float32)

@@ -153,3 +153,47 @@ def test_dispatch_errors():
                                amax.data_ptr(), rec.data_ptr(), pos.data_ptr(), g.data_ptr(), s)
     assert st == N.FPB_ERR_SHAPE  # experts not divisible by ranks
     assert F.device_error() == 0
+
+
+def _emulated_peer(dev, halves, x, lg):
+    """Peer mode on one GPU: each rank's chunk tables point straight into the
+    other rank's receive buffers (what fpb_ipc_open gives across processes),
+    so dispatch and the partial combine store there and nothing is copied."""
+    import torch
+
+    from firepit_b200.ep import DeviceEpOps
+    ops = [DeviceEpOps(dev, T, H, I, E, K, 2, *halves[r]) for r in range(2)]
+    for r in range(2):
+        ops[r].connect([ops[d].recv.data_ptr() + r * T * ops[d].rec for d in range(2)],
+                       [ops[s].ret_recv.data_ptr() + r * T * H * 4 for s in range(2)], r)
+    xs = [x[r * T:(r + 1) * T].contiguous() for r in range(2)]
+    ls = [lg[r * T:(r + 1) * T].contiguous() for r in range(2)]
+    routes = [o.route(l) for o, l in zip(ops, ls)]
+    amax = [o.amax(xr) for o, xr in zip(ops, xs)]
+    m = torch.maximum(amax[0], amax[1])
+    for a in amax:
+        a.copy_(m)
+    pos = [o.dispatch(xr, ids, w, a)[1] for o, xr, (ids, w), a in zip(ops, xs, routes, amax)]
+    ah = [o.experts_gate_up(o.recv) for o in ops]
+    m = torch.maximum(ah[0], ah[1])
+    for a in ah:
+        a.copy_(m)
+    for o in ops:
+        o.experts_down()
+    return [o.finish(o.ret_recv, p).clone() for o, p in zip(ops, pos)]
+
+
+@pytest.mark.parametrize("skew", [False, True])
+def test_emulated_peer_stores_match_chunk_exchange(skew):
+    import torch
+
+    import firepit_b200 as F
+    dev, A1, A2, halves, x, lg = _setup(skew)
+    y_one = _single_gpu(dev, A1, A2, x, lg)
+    _, _, _, outs = _emulated(dev, halves, x, lg)
+    peer = _emulated_peer(dev, halves, x, lg)
+    torch.cuda.synchronize()
+    assert F.device_error() == 0
+    for r in range(2):
+        assert torch.equal(peer[r].float(), outs[r].float())  # the same sums, only the stores' addresses differ
+        _close(peer[r], y_one[r * T:(r + 1) * T])

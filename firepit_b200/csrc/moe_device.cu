@@ -706,27 +706,46 @@ __host__ __device__ inline EpRecord ep_record(size_t cols, size_t width) {
 // route to rank d), or -1; positions[tokens * nranks + d] = count_d.  One CTA:
 // per 1024-token chunk, one ballot per destination gives each warp's counts,
 // one thread per destination scans the 32 warps, a second ballot places.
+// With `staged` (tokens * 4 bytes of dynamic shared memory), every token's
+// destination mask is computed first, four tokens per thread in flight, so
+// the id loads of all chunks overlap instead of one chunk's at a time.
 constexpr int kEpPlanThreads = 1024;
+constexpr int kEpPlanStagedTokens = 10240;  // 40 KB of masks (+ 4.3 KB static: under the 48 KB default)
+
+__device__ __forceinline__ uint32_t ep_token_mask(const int32_t *ids, int t, int width, int slots, int experts,
+                                                  int per_rank, int *error) {
+  uint32_t mask = 0;
+  const int32_t *row = ids + (size_t)t * width;
+#pragma unroll 4
+  for (int s = 0; s < slots; ++s) {
+    const int id = row[s];
+    if (id >= 0 && id < experts)
+      mask |= 1u << (id / per_rank);
+    else if (error)
+      atomicCAS(error, 0, 403);
+  }
+  return mask;
+}
+
 __global__ void __launch_bounds__(kEpPlanThreads) ep_plan_kernel(const int32_t *ids, int tokens, int width,
                                                                  int slots, int experts, int per_rank, int nranks,
-                                                                 int32_t *positions, int *error) {
+                                                                 int32_t *positions, int *error, bool staged) {
   pdl_enter();
+  extern __shared__ uint32_t masks[];
   __shared__ int wtot[32][33];
   __shared__ int carry[32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (tid < nranks) carry[tid] = 0;
+  if (staged) {
+#pragma unroll 4
+    for (int t = tid; t < tokens; t += kEpPlanThreads)
+      masks[t] = ep_token_mask(ids, t, width, slots, experts, per_rank, error);
+  }
   __syncthreads();
   for (int base = 0; base < tokens; base += kEpPlanThreads) {
     const int t = base + tid;
     uint32_t mask = 0;
-    if (t < tokens)
-      for (int s = 0; s < slots; ++s) {
-        const int id = ids[(size_t)t * width + s];
-        if (id >= 0 && id < experts)
-          mask |= 1u << (id / per_rank);
-        else if (error)
-          atomicCAS(error, 0, 403);
-      }
+    if (t < tokens) mask = staged ? masks[t] : ep_token_mask(ids, t, width, slots, experts, per_rank, error);
     for (int d = 0; d < nranks; ++d) {
       const unsigned b = __ballot_sync(0xffffffffu, (mask >> d) & 1u);
       if (lane == 0) wtot[warp][d] = __popc(b);
@@ -1355,8 +1374,9 @@ static int ep_dispatch_impl(const void *x, int x_dtype, size_t tokens, size_t co
   if (self > 31) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_ep_dispatch: self rank");
   cudaStream_t s = as_stream(stream);
   const int per_rank = (int)(experts / nranks);
-  launch_pdl(ep_plan_kernel, 1, kEpPlanThreads, 0, s, ids, (int)tokens, (int)width, (int)slots, (int)experts,
-             per_rank, (int)nranks, positions, device_error_ptr());
+  const bool staged = tokens <= (size_t)kEpPlanStagedTokens;
+  launch_pdl(ep_plan_kernel, 1, kEpPlanThreads, staged ? tokens * sizeof(uint32_t) : 0, s, ids, (int)tokens,
+             (int)width, (int)slots, (int)experts, per_rank, (int)nranks, positions, device_error_ptr(), staged);
   FPB_LAUNCH_CHECK("ep_plan_kernel");
   const EpRecord rec = ep_record(cols, width);
   return with_dtype(x_dtype, [&](auto tp) {

@@ -197,3 +197,46 @@ def test_emulated_peer_stores_match_chunk_exchange(skew):
     for r in range(2):
         assert torch.equal(peer[r].float(), outs[r].float())  # the same sums, only the stores' addresses differ
         _close(peer[r], y_one[r * T:(r + 1) * T])
+
+
+@pytest.mark.parametrize("tokens", [1, 10240, 10300])
+def test_dispatch_plan_sizes(tokens):
+    """The plan with every mask staged in shared memory (<= 10240 tokens) and
+    computed chunk by chunk (more): positions and counts against numpy, and
+    the records' routes."""
+    import torch
+
+    import firepit_b200 as F
+    from firepit_b200 import _native as N
+    dev = torch.device("cuda", 0)
+    n, k, width, experts, cols = 4, 3, 4, 32, 64
+    g = torch.Generator().manual_seed(tokens)
+    ids = torch.stack([torch.randperm(experts, generator=g)[:width] for _ in range(tokens)]).to(torch.int32)
+    w = torch.rand(tokens, width, generator=g)
+    x = torch.randn(tokens, cols, generator=g).to(torch.bfloat16)
+    rec = int(N.lib.fpb_ep_record_bytes(cols, width))
+    records = torch.empty(n * tokens * rec, dtype=torch.uint8, device=dev)
+    pos = torch.empty(tokens * n + n, dtype=torch.int32, device=dev)
+    amax = torch.tensor([x.float().abs().max().item()], device=dev)
+    glob = torch.empty(1, device=dev)
+    idd, wd, xd = ids.to(dev), w.to(dev), x.to(dev)
+    N.call("fpb_ep_dispatch", xd.data_ptr(), N.FPB_BF16, tokens, cols, idd.data_ptr(), wd.data_ptr(), width, k,
+           experts, n, amax.data_ptr(), records.data_ptr(), pos.data_ptr(), glob.data_ptr(),
+           torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert F.device_error() == 0
+    p = pos.cpu().numpy()
+    owner = ids[:, :k].numpy() // (experts // n)
+    r = records.cpu().numpy().reshape(n * tokens, rec)
+    ids_at = (cols // 2 + 15) // 16 * 16 + (cols // 16 + 15) // 16 * 16  # codes, factors, then the ids
+    for d in range(n):
+        hit = np.any(owner == d, axis=1)
+        assert p[tokens * n + d] == hit.sum()
+        col = p[:tokens * n].reshape(tokens, n)[:, d]
+        assert np.array_equal(col[hit], d * tokens + np.arange(hit.sum()))
+        assert np.all(col[~hit] == -1)
+        got = np.ascontiguousarray(r[col[hit]][:, ids_at:ids_at + 4 * width]).view(np.int32)
+        want = np.where(owner[hit] == d, ids[hit][:, :k].numpy() % (experts // n), -1)
+        assert np.array_equal(got[:, :k], want) and np.all(got[:, k:] == -1)
+        empty = np.ascontiguousarray(r[d * tokens + hit.sum():(d + 1) * tokens][:, ids_at:ids_at + 4 * width]).view(np.int32)
+        assert np.all(empty == -1)

@@ -18,9 +18,10 @@ from .synth import synth_normal
 from .weights import (NVFP4_GROUP, Q8_BLOCK, FormatError, HostNvfp4Matrix, Nvfp4Matrix, current_stream_handle,
                       quantize_nvfp4)
 
-from .gemm import (DEFAULT_GEMM_TILE, DEFAULT_GROUPED_GEMM_TILE, GemmTile, Nvfp4Gemm, Nvfp4GroupedGemmView,
-                   device_error, nvfp4_gemm, nvfp4_gemm_view, nvfp4_grouped_gemm_q, nvfp4_grouped_gemm_swiglu_q,
-                   nvfp4_grouped_gemm_view, quantize_act, rows_quantize)
+from .gemm import (DEFAULT_GEMM_TILE, DEFAULT_GROUPED_GEMM_TILE, GemmTile, Nvfp4Gemm, Nvfp4GemmBatch,
+                   Nvfp4GroupedGemmView, device_error, nvfp4_gemm, nvfp4_gemm_batch, nvfp4_gemm_view,
+                   nvfp4_grouped_gemm_q, nvfp4_grouped_gemm_swiglu_q, nvfp4_grouped_gemm_view, quantize_act,
+                   rows_quantize)
 from .fp8 import (Fp8Gemm, Fp8GroupedGemmView, Fp8Matrix, Fp8Scaling, HostFp8Matrix, fp8_gemm, fp8_gemm_view,
                   fp8_grouped_gemm_q, fp8_grouped_gemm_view, quantize_fp8)
 from .checkpoint import (Checkpoint, CheckpointError, Fp8Config, HostBf16Weight, ModelOptConfig, Quantization,

@@ -141,6 +141,7 @@ SIGNATURES: dict[str, tuple] = {
     "fpb_moe_layout_masked": (i32, [vp, sz, sz, sz, sz, sz, sz, vp, vp, vp, vp, vp, vp, sz, vp]),
     "fpb_moe_gather_codes": (i32, [vp, sz, vp, sz, sz, sz, vp, sz, vp, i32, vp, vp, vp]),
     "fpb_ep_record_bytes": (sz, [sz, sz]),
+    "fpb_nvfp4_gemm_batch_create": (i32, [C.POINTER(GemvSegment), i32, i32, i32, i32, vp, C.POINTER(vp)]),
     "fpb_ep_dispatch": (i32, [vp, i32, sz, sz, vp, vp, sz, sz, sz, sz, vp, vp, vp, vp, vp]),
     "fpb_ep_unpack": (i32, [vp, sz, sz, sz, vp, vp, vp]),
     "fpb_ep_dispatch_chunks": (i32, [vp, i32, sz, sz, vp, vp, sz, sz, sz, sz, vp, vp, i32, vp, vp, vp]),

@@ -211,6 +211,52 @@ __global__ void __launch_bounds__(kPlaneThreads) planes_encode_kernel(const T *x
   }
 }
 
+// ---- W4A4 batch: each member's x [m, K] quantized to NVFP4 (config 2's rule) -----------
+// The prepared batch's W4A4 form (fpb_nvfp4_gemm_batch_create): every distinct
+// x gets the per-tensor quantization of fpb_nvfp4_quantize_act (global = amax
+// / 2688 over that x, e4m3 factors per 16 values, e2m1 codes), into A row
+// group a_group (rows a_group * 128 + r), each row's global in ga[row].
+// Pass 1: amax per group (blockIdx.y), atomicMax of each CTA's maximum
+// (amax zeroed by the caller).
+template <typename T>
+__global__ void batch_amax_kernel(const PlaneSeg *segs, int m, int K, uint32_t *amax) {
+  pdl_enter();
+  const int g = blockIdx.y;
+  if (segs[g].a_group != g) return;  // encoded with an earlier segment (uniform)
+  const T *x = static_cast<const T *>(segs[g].x);
+  const size_t n = (size_t)m * K;
+  uint32_t mx = 0;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    mx = max(mx, __float_as_uint(act_load(x, i)) & 0x7fffffffu);
+  block_amax_to(mx, &amax[g]);
+}
+
+// Pass 2: one warp per row of each group (the encode of act_encode_kernel).
+template <typename T>
+__global__ void batch_encode_kernel(const PlaneSeg *segs, int m, int K, const uint32_t *amax, uint8_t *packed,
+                                    uint8_t *sf_tiled, float *ga) {
+  pdl_enter();
+  const int g = blockIdx.y;
+  if (segs[g].a_group != g) return;
+  const float global = __fdiv_rn(__uint_as_float(amax[g]), 2688.0f);
+  const T *x = static_cast<const T *>(segs[g].x);
+  const int gpr = K / kNvfp4Group, lane = threadIdx.x & 31;
+  const int warps = gridDim.x * (blockDim.x / 32);
+  for (int r = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; r < m; r += warps) {
+    const size_t row = (size_t)g * 128 + r;
+    const T *xrow = x + (size_t)r * K;
+    uint8_t *prow = packed + row * (K / 2);
+    uint8_t *srow = sf_tiled + sf_tiled_row_offset(row, K);
+    if (lane == 0) ga[row] = global;
+    for (int q = lane; q < gpr; q += 32) {
+      float v[kNvfp4Group];
+#pragma unroll
+      for (int i = 0; i < kNvfp4Group; ++i) v[i] = act_load(xrow + q * kNvfp4Group, i);
+      encode_group16(v, global, prow + q * (kNvfp4Group / 2), srow + sf_tiled_group_offset(q));
+    }
+  }
+}
+
 }  // namespace fpb
 
 namespace fpb {
@@ -544,7 +590,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // columns ch*32 .. +31); each warp stages and stores its own boxes.
     const int qw = warp & 3, ch = (warp - 2) >> 2;
     const uint32_t lane_base = (uint32_t)(qw * 32) << 16;
-    const float ga = (p.f16 || p.planes) ? 1.0f : __ldg(p.a_global);
+    // W4A4 batch (segments without planes): each row's global from a_globals
+    const float ga = (p.f16 || p.planes || p.segs) ? 1.0f : __ldg(p.a_global);
     uint8_t *stage = sOut + qw * kOutWarpBytes;
     uint8_t *row_s = stage + lane * 128;
     uint32_t lt = 0;
@@ -562,8 +609,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int row0 = m_tile * kBM + qw * 32;
       const int n0 = n_tile * kBN;
       const bool row_live = p.planes ? qw * 32 + lane < p.tokens * 8
+                            : p.segs ? qw * 32 + lane < p.tokens
                                      : row0 + lane < p.M && (!p.row_tokens || p.row_tokens[row0 + lane] >= 0);
-      const float ga_row = p.planes && row_live ? __ldg(p.a_globals + row0 + lane) : 0.0f;
+      const float ga_row = (p.planes || p.segs) && row_live ? __ldg(p.a_globals + row0 + lane) : 0.0f;
       float gl[2];
       if (p.glu) {
         const int j0 = n_tile * 64;
@@ -714,11 +762,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // Lane l holds the weight global of column n0 + ch*64 + 32c + l; the
       // products are scaled in place by every lane (shuffles are warp-wide).
       const int nw = n0 + ch * 64;
+      const float gax = p.segs ? ga_row : ga;
 #pragma unroll
       for (int c = 0; c < 2; ++c)
 #pragma unroll
         for (int j = 0; j < 32; ++j)
-          r[c][j] = __float_as_uint((__uint_as_float(r[c][j]) * ga) * __shfl_sync(0xffffffffu, gl[c], j));
+          r[c][j] = __float_as_uint((__uint_as_float(r[c][j]) * gax) * __shfl_sync(0xffffffffu, gl[c], j));
       if (p.tma_store) {
         if (lane == 0) bulk_wait_read_all();  // this warp's previous stores have left its box
         __syncwarp();
@@ -763,19 +812,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         continue;
       }
-      // Direct stores (y not addressable by a tensor map).
-      const int row = row0 + lane;
+      // Direct stores (y not addressable by a tensor map; a W4A4 batch
+      // member's y [m, rows]).
+      const int row = sg ? qw * 32 + lane : row0 + lane;
       if (!row_live) continue;  // no warp-collective operation follows in this iteration
+      void *ydst = sg ? sg->y : p.y;
+      const long long ldy = sg ? (long long)sg->rows : p.ldy;
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         const int nc = nw + c * 32;
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[c][j]);
-        const long long off = (long long)row * p.ldy + nc;
-        const bool full_cols = nc + 32 <= p.N;
+        const long long off = (long long)row * ldy + nc;
+        const bool full_cols = nc + 32 <= n_lim;
         if (p.y_bf16) {
-          __nv_bfloat16 *yp = reinterpret_cast<__nv_bfloat16 *>(p.y) + off;
+          __nv_bfloat16 *yp = reinterpret_cast<__nv_bfloat16 *>(ydst) + off;
           if (full_cols && (reinterpret_cast<uintptr_t>(yp) & 15) == 0) {
 #pragma unroll
             for (int j = 0; j < 32; j += 8) {
@@ -789,10 +841,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           } else {
 #pragma unroll
             for (int j = 0; j < 32; ++j)
-              if (nc + j < p.N) yp[j] = __float2bfloat16_rn(v[j]);
+              if (nc + j < n_lim) yp[j] = __float2bfloat16_rn(v[j]);
           }
         } else {
-          float *yp = reinterpret_cast<float *>(p.y) + off;
+          float *yp = reinterpret_cast<float *>(ydst) + off;
           if (full_cols && (reinterpret_cast<uintptr_t>(yp) & 15) == 0) {
 #pragma unroll
             for (int j = 0; j < 32; j += 4)
@@ -800,7 +852,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           } else {
 #pragma unroll
             for (int j = 0; j < 32; ++j)
-              if (nc + j < p.N) yp[j] = v[j];
+              if (nc + j < n_lim) yp[j] = v[j];
           }
         }
       }
@@ -1247,24 +1299,28 @@ struct fpb_gemv_batch {
   fpb::PlaneSeg *segs = nullptr;  // device table
   CUtensorMap tmap_a{};           // the planes' codes
   CUtensorMap tmap_b0{};          // segment 0's weights (a valid map for the unused parameter)
-  void *ws = nullptr;             // planes workspace
+  void *ws = nullptr;             // planes (or W4A4 activations) workspace
   int count = 0, batch = 0, K = 0, x_dtype = 0, y_dtype = 0, total_items = 0;
+  int w4a4 = 0;                   // fpb_nvfp4_gemm_batch_create: x quantized to NVFP4, batch = m <= 128
 };
 
-extern "C" int fpb_nvfp4_gemv_batch_create(const fpb_gemv_segment *segs, int count, int x_dtype, int y_dtype,
-                                           int batch, void *stream, fpb_gemv_batch **out) {
+static int batch_create_impl(const fpb_gemv_segment *segs, int count, int x_dtype, int y_dtype, int batch,
+                             bool w4a4, void *stream, fpb_gemv_batch **out) {
   if (!segs || !out) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_gemv_batch_create: null pointer");
   *out = nullptr;
   if (count < 1 || count > kMoeIdsCached)
     return fail(FPB_ERR_SHAPE, "fpb_nvfp4_gemv_batch_create: count %d not in [1, %d]", count, kMoeIdsCached);
   if ((x_dtype != FPB_F32 && x_dtype != FPB_BF16) || (y_dtype != FPB_F32 && y_dtype != FPB_BF16))
     return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_gemv_batch_create: dtype");
-  if (batch < 1 || batch > 16) return fail(FPB_ERR_SHAPE, "fpb_nvfp4_gemv_batch_create: batch %d not in [1, 16]", batch);
+  const int max_batch = w4a4 ? kBM : 16;
+  if (batch < 1 || batch > max_batch)
+    return fail(FPB_ERR_SHAPE, "fpb_nvfp4_%s_batch_create: %s %d not in [1, %d]", w4a4 ? "gemm" : "gemv",
+                w4a4 ? "m" : "batch", batch, max_batch);
   if (!segs[0].w) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_gemv_batch_create: null matrix");
   const size_t K = segs[0].w->cols;
-  if (K % 256 || K > (size_t)kPlaneMaxK)
-    return fail(FPB_ERR_UNSUPPORTED, "fpb_nvfp4_gemv_batch_create: cols %zu must be a multiple of 256 and at most %d",
-                K, kPlaneMaxK);
+  if (K % 256 || (!w4a4 && K > (size_t)kPlaneMaxK))
+    return fail(FPB_ERR_UNSUPPORTED, "fpb_nvfp4_gemv_batch_create: cols %zu must be a multiple of 256%s", K,
+                w4a4 ? "" : " and at most 4096");
   std::vector<PlaneSeg> host((size_t)count);
   int items = 0;
   for (int i = 0; i < count; ++i) {
@@ -1307,11 +1363,16 @@ extern "C" int fpb_nvfp4_gemv_batch_create(const fpb_gemv_segment *segs, int cou
   b->x_dtype = x_dtype;
   b->y_dtype = y_dtype;
   b->total_items = items;
+  b->w4a4 = w4a4 ? 1 : 0;
   std::memcpy(&b->tmap_b0, segs[0].w->extras->tmap_b, sizeof(CUtensorMap));
   cudaStream_t s = as_stream(stream);
-  const size_t ws_bytes = fpb_nvfp4_gemv_planes_workspace_bytes((size_t)count, K);
+  // W4A4: the same layout (codes, tiled factors, row globals) plus one amax
+  // word per group; zeroed once, so rows past m stay zero codes and factors
+  const size_t ws_bytes =
+      fpb_nvfp4_gemv_planes_workspace_bytes((size_t)count, K) + (w4a4 ? 256 + (size_t)count * 4 : 0);
   cudaError_t e = cudaMalloc(reinterpret_cast<void **>(&b->segs), sizeof(PlaneSeg) * (size_t)count);
   if (e == cudaSuccess) e = cudaMalloc(&b->ws, ws_bytes);
+  if (e == cudaSuccess) e = cudaMemsetAsync(b->ws, 0, ws_bytes, s);
   if (e == cudaSuccess)
     e = cudaMemcpyAsync(b->segs, host.data(), sizeof(PlaneSeg) * (size_t)count, cudaMemcpyHostToDevice, s);
   if (e == cudaSuccess) e = cudaStreamSynchronize(s);
@@ -1321,7 +1382,8 @@ extern "C" int fpb_nvfp4_gemv_batch_create(const fpb_gemv_segment *segs, int cou
     delete b;
     return cuda_fail(e, "fpb_nvfp4_gemv_batch_create");
   }
-  if (int st = encode_rows_u8(&b->tmap_a, b->ws, (uint64_t)count * kBM, K / 2, (uint32_t)(batch * kPlanes))) {
+  const uint32_t a_box = w4a4 ? (uint32_t)((batch + 7) / 8 * 8) : (uint32_t)(batch * kPlanes);
+  if (int st = encode_rows_u8(&b->tmap_a, b->ws, (uint64_t)count * kBM, K / 2, a_box)) {
     cudaFree(b->segs);
     cudaFree(b->ws);
     delete b;
@@ -1331,9 +1393,68 @@ extern "C" int fpb_nvfp4_gemv_batch_create(const fpb_gemv_segment *segs, int cou
   return FPB_OK;
 }
 
+extern "C" int fpb_nvfp4_gemv_batch_create(const fpb_gemv_segment *segs, int count, int x_dtype, int y_dtype,
+                                           int batch, void *stream, fpb_gemv_batch **out) {
+  return batch_create_impl(segs, count, x_dtype, y_dtype, batch, false, stream, out);
+}
+
+extern "C" int fpb_nvfp4_gemm_batch_create(const fpb_gemv_segment *segs, int count, int x_dtype, int y_dtype, int m,
+                                           void *stream, fpb_gemv_batch **out) {
+  return batch_create_impl(segs, count, x_dtype, y_dtype, m, true, stream, out);
+}
+
+// The W4A4 form of a batch: every distinct x quantized (amax, then encode),
+// then the GEMM kernel over all members' tiles with per-row globals.
+static int run_w4a4_batch(const fpb_gemv_batch *b, cudaStream_t s) {
+  const size_t K = (size_t)b->K, rows = (size_t)b->count * kBM;
+  uint8_t *packed = static_cast<uint8_t *>(b->ws);
+  uint8_t *sf = packed + align256(rows * K / 2);
+  float *ga = reinterpret_cast<float *>(sf + align256(sf_tiled_bytes(rows, K)));
+  uint32_t *amax = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(b->ws) +
+                                                align256(fpb_nvfp4_gemv_planes_workspace_bytes((size_t)b->count, K)));
+  FPB_CUDA_TRY(cudaMemsetAsync(amax, 0, (size_t)b->count * sizeof(uint32_t), s));
+  const size_t n = (size_t)b->batch * K;
+  const dim3 agrid((unsigned)std::min<size_t>(64, (n + 2047) / 2048), (unsigned)b->count);
+  const dim3 egrid((unsigned)((b->batch + 7) / 8), (unsigned)b->count);
+  cudaError_t e;
+  if (b->x_dtype == FPB_F32) {
+    e = launch_pdl(batch_amax_kernel<float>, agrid, 256, 0, s, (const PlaneSeg *)b->segs, b->batch, b->K, amax);
+    if (e == cudaSuccess)
+      e = launch_pdl(batch_encode_kernel<float>, egrid, 256, 0, s, (const PlaneSeg *)b->segs, b->batch, b->K,
+                     (const uint32_t *)amax, packed, sf, ga);
+  } else {
+    e = launch_pdl(batch_amax_kernel<uint16_t>, agrid, 256, 0, s, (const PlaneSeg *)b->segs, b->batch, b->K, amax);
+    if (e == cudaSuccess)
+      e = launch_pdl(batch_encode_kernel<uint16_t>, egrid, 256, 0, s, (const PlaneSeg *)b->segs, b->batch, b->K,
+                     (const uint32_t *)amax, packed, sf, ga);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "batch_encode_kernel");
+  FPB_LAUNCH_CHECK("batch_encode_kernel");
+  GemmParams p{};
+  p.a_box_rows = (b->batch + 7) / 8 * 8;
+  p.a_sf = sf;
+  p.y_bf16 = b->y_dtype == FPB_BF16;
+  p.M = (int)rows;
+  p.N = kBN;  // per segment in the kernel
+  p.kb_count = b->K / 256;
+  p.error = device_error_ptr();
+  p.tokens = b->batch;
+  p.a_globals = ga;
+  p.segs = b->segs;
+  p.nseg = b->count;
+  p.total_items = b->total_items;
+  const unsigned grid = (unsigned)std::min<size_t>((size_t)b->total_items, (size_t)std::max(1, sm_count()));
+  e = launch_pdl(nvfp4_gemm_kernel, grid, kGemmThreads, kGemmSmem, s, b->tmap_a, b->tmap_b0, b->tmap_a, b->tmap_b0,
+                 b->tmap_a, p);
+  if (e != cudaSuccess) return cuda_fail(e, "nvfp4_gemm_kernel (W4A4 batch)");
+  FPB_LAUNCH_CHECK("nvfp4_gemm_kernel");
+  return FPB_OK;
+}
+
 extern "C" int fpb_nvfp4_gemv_batch_run(const fpb_gemv_batch *b, void *stream) {
   if (!b) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_gemv_batch_run: null handle");
   cudaStream_t s = as_stream(stream);
+  if (b->w4a4) return run_w4a4_batch(b, s);
   const size_t K = (size_t)b->K, rows = (size_t)b->count * kBM;
   uint8_t *packed = static_cast<uint8_t *>(b->ws);
   uint8_t *sf = packed + align256(rows * K / 2);

@@ -98,6 +98,69 @@ def nvfp4_gemm_view(weight: Nvfp4Matrix, rows: range, x, y, tile: GemmTile = DEF
     return Nvfp4Gemm(weight, x, y, tile, rows, workspace, act)
 
 
+class Nvfp4GemmBatch:
+    """Several NVFP4 GEMMs under BASELINE config 2's W4A4 rule in one launch
+    (fpb_nvfp4_gemm_batch_create / fpb_nvfp4_gemv_batch_run): each member
+    ``(weight, x, y[, rows])`` has its own weight rows and x [m, K] (f32 or
+    bf16, m <= 128), and y [m, len(rows)] (f32 or bf16) gets what
+    ``nvfp4_gemm_view(weight, rows, x, y)`` gives for m > 16: x quantized to
+    NVFP4 per tensor (the same codes as ``quantize_act``), the tcgen05 GEMM
+    over every member's 128-row weight tiles together, so that a few tokens
+    against many matrices (a layer's projections, the experts of a decode
+    batch) keep every SM busy.  Members sharing one x tensor quantize it
+    once.  The tensors are bound at construction (a device table is built
+    and the stream synchronised); ``submit`` can be recorded by a Graph sink.
+    Needs K % 256 == 0 and rows starting at multiples of 128 (ShapeError)."""
+
+    def __init__(self, members):
+        import ctypes as C
+
+        from .weights import current_stream_handle
+        if not members:
+            raise ShapeError("GEMM batch: no members")
+        arr = (N.GemvSegment * len(members))()
+        first_x, first_y = members[0][1], members[0][2]
+        m = first_x.shape[0]
+        for i, mem in enumerate(members):
+            w, x, y = mem[0], mem[1], mem[2]
+            rows = mem[3] if len(mem) > 3 and mem[3] is not None else range(0, w.rows)
+            if not isinstance(w, Nvfp4Matrix):
+                raise ShapeError("GEMM batch: NVFP4 weights only")
+            if x.dim() != 2 or x.shape != (m, w.cols) or y.shape != (m, len(rows)):
+                raise ShapeError(f"GEMM batch: member {i} shapes x {tuple(x.shape)} y {tuple(y.shape)}")
+            if x.dtype != first_x.dtype or y.dtype != first_y.dtype:
+                raise ShapeError("GEMM batch: members differ in dtypes")
+            if not (x.is_contiguous() and y.is_contiguous()):
+                raise ShapeError("GEMM batch: x and y must be contiguous")
+            arr[i] = N.GemvSegment(w.handle.value, rows.start, rows.stop, x.data_ptr(), y.data_ptr())
+        self._segs, self._members = arr, list(members)
+        h = C.c_void_p()
+        st = N.lib.fpb_nvfp4_gemm_batch_create(arr, len(members), _dtype_code(first_x), _dtype_code(first_y), m,
+                                               current_stream_handle(first_x.device), C.byref(h))
+        if st in (N.FPB_ERR_UNSUPPORTED, N.FPB_ERR_SHAPE):
+            raise ShapeError(N.last_error())
+        N.check(st, "fpb_nvfp4_gemm_batch_create")
+        self._batch = h
+
+    def submit(self, sink: Sink | None = None) -> None:
+        sink = sink or Eager()
+        sink.run("nvfp4_gemm_batch", lambda stream: N.call("fpb_nvfp4_gemv_batch_run", self._batch, stream))
+
+    def __del__(self):
+        h = getattr(self, "_batch", None)
+        if h is not None and h.value:
+            try:
+                N.lib.fpb_nvfp4_gemv_batch_destroy(h)
+            except Exception:
+                pass
+            self._batch = None
+
+
+def nvfp4_gemm_batch(members) -> Nvfp4GemmBatch:
+    """members: ``(weight, x, y)`` or ``(weight, x, y, rows)`` tuples."""
+    return Nvfp4GemmBatch(members)
+
+
 def quantize_act(x, stream=None):
     """NVFP4-quantizes activations [m, k]: (packed u8 [m, k/2], tiled factors,
     global f32 [1]) as device tensors."""

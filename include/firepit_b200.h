@@ -306,6 +306,16 @@ int fpb_nvfp4_moe_gemv_planes(fpb_nvfp4_matrix *w, size_t rows_per_expert, const
 typedef struct fpb_gemv_batch fpb_gemv_batch;
 int fpb_nvfp4_gemv_batch_create(const fpb_gemv_segment *segs, int count, int x_dtype, int y_dtype, int batch,
                                 void *stream, fpb_gemv_batch **out);
+/* The prepared batch under BASELINE config 2's W4A4 rule: members as above
+ * but each x is [m, K] (f32/bf16, m <= 128, K % 256 == 0) and y [m, rows];
+ * every distinct x is quantized to NVFP4 per tensor (global = amax / 2688,
+ * the codes of fpb_nvfp4_quantize_act) and y = fpb_nvfp4_gemm's W4A4 result
+ * (bit for bit).  One amax launch, one encode launch and one tcgen05 launch
+ * over all members' 128-row weight tiles per fpb_nvfp4_gemv_batch_run, so
+ * that a few tokens against many matrices keep every SM busy; the handle is
+ * run and destroyed with fpb_nvfp4_gemv_batch_run / _destroy. */
+int fpb_nvfp4_gemm_batch_create(const fpb_gemv_segment *segs, int count, int x_dtype, int y_dtype, int m,
+                                void *stream, fpb_gemv_batch **out);
 int fpb_nvfp4_gemv_batch_run(const fpb_gemv_batch *b, void *stream);
 int fpb_nvfp4_gemv_batch_destroy(fpb_gemv_batch *b);
 /* The down projection after the gate/up one: gate_up [cap][tokens][2 * cols]

@@ -122,6 +122,7 @@ __global__ void act_encode_kernel(const T *x, size_t rows, size_t cols, const ui
 // global memory (64-byte aligned), which TMA reads like a parameter.
 struct alignas(64) PlaneSeg {
   CUtensorMap tmap_b;       // the handle's codes (box 128 rows x 128 bytes)
+  CUtensorMap tmap_y;       // W4A4 batch: y [m, rows] for TMA stores (valid when the batch stores that way)
   const uint8_t *b_sf;      // the handle's tiled factors
   const float *b_globals;   // the handle's row globals, row 0
   const void *x;
@@ -450,7 +451,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     fence_barrier_init();
     prefetch_tensormap(&tmap_a);
     prefetch_tensormap(&tmap_b);
-    if (p.tma_store) prefetch_tensormap(&tmap_y);
+    if (p.tma_store && !p.segs) prefetch_tensormap(&tmap_y);
     if (p.glu || p.f16) prefetch_tensormap(&tmap_b64);
     if (p.f16) prefetch_tensormap(&tmap_a2);
   }
@@ -769,6 +770,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int j = 0; j < 32; ++j)
           r[c][j] = __float_as_uint((__uint_as_float(r[c][j]) * gax) * __shfl_sync(0xffffffffu, gl[c], j));
       if (p.tma_store) {
+        // a W4A4 batch member's own map: its y [m, rows], rows local to the member
+        const CUtensorMap *ymap = sg ? &sg->tmap_y : &tmap_y;
+        const int yrow = sg ? qw * 32 : row0;
         if (lane == 0) bulk_wait_read_all();  // this warp's previous stores have left its box
         __syncwarp();
         if (p.y_bf16) {
@@ -787,7 +791,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            if (nw < p.N) tma_store_2d(&tmap_y, stage + ch * kOutBoxBytes, nw, row0);
+            if (nw < n_lim) tma_store_2d(ymap, stage + ch * kOutBoxBytes, nw, yrow);
             bulk_commit_group();
           }
         } else {
@@ -805,7 +809,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-              if (nw + c * 32 < p.N) tma_store_2d(&tmap_y, stage + ch * kOutBoxBytes, nw + c * 32, row0);
+              if (nw + c * 32 < n_lim) tma_store_2d(ymap, stage + ch * kOutBoxBytes, nw + c * 32, yrow);
               bulk_commit_group();
             }
           }
@@ -1302,6 +1306,7 @@ struct fpb_gemv_batch {
   void *ws = nullptr;             // planes (or W4A4 activations) workspace
   int count = 0, batch = 0, K = 0, x_dtype = 0, y_dtype = 0, total_items = 0;
   int w4a4 = 0;                   // fpb_nvfp4_gemm_batch_create: x quantized to NVFP4, batch = m <= 128
+  int tma_store = 0;              // W4A4: every member's y takes TMA stores (16-byte aligned base and pitch)
 };
 
 static int batch_create_impl(const fpb_gemv_segment *segs, int count, int x_dtype, int y_dtype, int batch,
@@ -1323,6 +1328,7 @@ static int batch_create_impl(const fpb_gemv_segment *segs, int count, int x_dtyp
                 w4a4 ? "" : " and at most 4096");
   std::vector<PlaneSeg> host((size_t)count);
   int items = 0;
+  bool all_tma = w4a4;
   for (int i = 0; i < count; ++i) {
     const fpb_gemv_segment &sg = segs[i];
     if (!sg.w || !sg.x || !sg.y)
@@ -1348,6 +1354,9 @@ static int batch_create_impl(const fpb_gemv_segment *segs, int count, int x_dtyp
     d.rows = (int)(end - sg.row_begin);
     d.item_begin = items;
     items += (d.rows + kBN - 1) / kBN;
+    if (w4a4 && !encode_store_map(&d.tmap_y, sg.y, y_dtype == FPB_BF16, (uint64_t)batch, (uint64_t)d.rows,
+                                  (uint64_t)d.rows, 32, 0))
+      all_tma = false;
     d.a_group = i;
     for (int j = 0; j < i; ++j)
       if (segs[j].x == sg.x) {
@@ -1364,6 +1373,7 @@ static int batch_create_impl(const fpb_gemv_segment *segs, int count, int x_dtyp
   b->y_dtype = y_dtype;
   b->total_items = items;
   b->w4a4 = w4a4 ? 1 : 0;
+  b->tma_store = all_tma ? 1 : 0;
   std::memcpy(&b->tmap_b0, segs[0].w->extras->tmap_b, sizeof(CUtensorMap));
   cudaStream_t s = as_stream(stream);
   // W4A4: the same layout (codes, tiled factors, row globals) plus one amax
@@ -1443,7 +1453,9 @@ static int run_w4a4_batch(const fpb_gemv_batch *b, cudaStream_t s) {
   p.segs = b->segs;
   p.nseg = b->count;
   p.total_items = b->total_items;
+  p.tma_store = b->tma_store;
   const unsigned grid = (unsigned)std::min<size_t>((size_t)b->total_items, (size_t)std::max(1, sm_count()));
+  // tmap_y (unused with segments: each member's map is in the table) gets a valid map
   e = launch_pdl(nvfp4_gemm_kernel, grid, kGemmThreads, kGemmSmem, s, b->tmap_a, b->tmap_b0, b->tmap_a, b->tmap_b0,
                  b->tmap_a, p);
   if (e != cudaSuccess) return cuda_fail(e, "nvfp4_gemm_kernel (W4A4 batch)");

@@ -83,3 +83,25 @@ def test_batch_errors():
         F.nvfp4_gemm_batch([(w2, x2, torch.empty(8, 256, dtype=torch.bfloat16, device="cuda"))])  # K % 256
     with pytest.raises(F.ShapeError):
         F.nvfp4_gemm_batch([(w, x[:8], torch.empty(8, 128, dtype=torch.bfloat16, device="cuda"), range(64, 192))])
+
+
+@pytest.mark.parametrize("ydt", ["bf16", "f32"])
+def test_ragged_view_takes_direct_stores(ydt):
+    """A member whose y pitch is not 16-byte aligned (a 300-row view) makes
+    the batch store every member directly; results are the same."""
+    import torch
+
+    import firepit_b200 as F
+    yd = {"bf16": torch.bfloat16, "f32": torch.float32}[ydt]
+    m = 40
+    ws = [_weight(F, 384, K, 60 + i) for i in range(2)]
+    x = F.synth_normal((m, K), seed=61, stream_id=0, dtype=torch.bfloat16)
+    members = [(ws[0], x, torch.empty(m, 300, dtype=yd, device="cuda"), range(0, 300)),
+               (ws[1], x, torch.empty(m, 384, dtype=yd, device="cuda"), None)]
+    F.nvfp4_gemm_batch(members).submit(F.Eager())
+    for w, xx, y, r in members:
+        ref = torch.empty_like(y)
+        F.nvfp4_gemm_view(w, r or range(0, w.rows), xx, ref, F.GemmTile(1, 1, 32)).submit(F.Eager())
+        torch.cuda.synchronize()
+        assert torch.equal(y, ref)
+    assert F.device_error() == 0

@@ -226,13 +226,33 @@ __global__ void batch_amax_kernel(const PlaneSeg *segs, int m, int K, uint32_t *
   if (segs[g].a_group != g) return;  // encoded with an earlier segment (uniform)
   const T *x = static_cast<const T *>(segs[g].x);
   const size_t n = (size_t)m * K;
+  const size_t tid = (size_t)blockIdx.x * blockDim.x + threadIdx.x, stride = (size_t)gridDim.x * blockDim.x;
+  constexpr size_t kVec = 16 / sizeof(T);
   uint32_t mx = 0;
-  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
-    mx = max(mx, __float_as_uint(act_load(x, i)) & 0x7fffffffu);
+  size_t head = 0;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) == 0) {  // 16-byte loads, four in flight
+    const uint4 *xv = reinterpret_cast<const uint4 *>(x);
+    const size_t nv = n / kVec;
+#pragma unroll 4
+    for (size_t i = tid; i < nv; i += stride) {
+      const uint4 u = xv[i];
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        if constexpr (sizeof(T) == 4)
+          mx = max(mx, w[k] & 0x7fffffffu);
+        else
+          mx = max(mx, max((w[k] << 16) & 0x7fffffffu, w[k] & 0x7fff0000u));
+      }
+    }
+    head = nv * kVec;
+  }
+  for (size_t i = head + tid; i < n; i += stride) mx = max(mx, __float_as_uint(act_load(x, i)) & 0x7fffffffu);
   block_amax_to(mx, &amax[g]);
 }
 
-// Pass 2: one warp per row of each group (the encode of act_encode_kernel).
+// Pass 2: one warp per (row, 32 groups) of each group: lane l encodes group
+// 32 c + l of the row (the encode of act_encode_kernel).
 template <typename T>
 __global__ void batch_encode_kernel(const PlaneSeg *segs, int m, int K, const uint32_t *amax, uint8_t *packed,
                                     uint8_t *sf_tiled, float *ga) {
@@ -242,19 +262,19 @@ __global__ void batch_encode_kernel(const PlaneSeg *segs, int m, int K, const ui
   const float global = __fdiv_rn(__uint_as_float(amax[g]), 2688.0f);
   const T *x = static_cast<const T *>(segs[g].x);
   const int gpr = K / kNvfp4Group, lane = threadIdx.x & 31;
+  const int chunks = (gpr + 31) / 32;
   const int warps = gridDim.x * (blockDim.x / 32);
-  for (int r = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; r < m; r += warps) {
+  for (int w = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; w < m * chunks; w += warps) {
+    const int r = w / chunks, q = (w % chunks) * 32 + lane;
     const size_t row = (size_t)g * 128 + r;
-    const T *xrow = x + (size_t)r * K;
-    uint8_t *prow = packed + row * (K / 2);
-    uint8_t *srow = sf_tiled + sf_tiled_row_offset(row, K);
-    if (lane == 0) ga[row] = global;
-    for (int q = lane; q < gpr; q += 32) {
-      float v[kNvfp4Group];
+    if (lane == 0 && w % chunks == 0) ga[row] = global;
+    if (q >= gpr) continue;
+    float v[kNvfp4Group];
+    const T *src = x + (size_t)r * K + q * kNvfp4Group;
 #pragma unroll
-      for (int i = 0; i < kNvfp4Group; ++i) v[i] = act_load(xrow + q * kNvfp4Group, i);
-      encode_group16(v, global, prow + q * (kNvfp4Group / 2), srow + sf_tiled_group_offset(q));
-    }
+    for (int i = 0; i < kNvfp4Group; ++i) v[i] = act_load(src, i);
+    encode_group16(v, global, packed + row * (K / 2) + q * (kNvfp4Group / 2),
+                   sf_tiled + sf_tiled_row_offset(row, K) + sf_tiled_group_offset(q));
   }
 }
 
@@ -1424,8 +1444,9 @@ static int run_w4a4_batch(const fpb_gemv_batch *b, cudaStream_t s) {
                                                 align256(fpb_nvfp4_gemv_planes_workspace_bytes((size_t)b->count, K)));
   FPB_CUDA_TRY(cudaMemsetAsync(amax, 0, (size_t)b->count * sizeof(uint32_t), s));
   const size_t n = (size_t)b->batch * K;
-  const dim3 agrid((unsigned)std::min<size_t>(64, (n + 2047) / 2048), (unsigned)b->count);
-  const dim3 egrid((unsigned)((b->batch + 7) / 8), (unsigned)b->count);
+  const dim3 agrid((unsigned)std::min<size_t>(128, (n + 8191) / 8192), (unsigned)b->count);
+  const size_t warp_items = (size_t)b->batch * ((K / kNvfp4Group + 31) / 32);
+  const dim3 egrid((unsigned)std::min<size_t>(256, (warp_items + 7) / 8), (unsigned)b->count);
   cudaError_t e;
   if (b->x_dtype == FPB_F32) {
     e = launch_pdl(batch_amax_kernel<float>, agrid, 256, 0, s, (const PlaneSeg *)b->segs, b->batch, b->K, amax);

@@ -707,8 +707,9 @@ __host__ __device__ inline EpRecord ep_record(size_t cols, size_t width) {
 // per 1024-token chunk, one ballot per destination gives each warp's counts,
 // one thread per destination scans the 32 warps, a second ballot places.
 // With `staged` (tokens * 4 bytes of dynamic shared memory), every token's
-// destination mask is computed first from coalesced id loads, instead of one
-// token's row per thread chunk by chunk.
+// destination mask comes from ep_mask_kernel (many CTAs, one warp per token)
+// through positions[0, tokens); otherwise each thread reads its token's ids
+// chunk by chunk (one CTA's loads in flight: slower).
 constexpr int kEpPlanThreads = 1024;
 constexpr int kEpPlanStagedTokens = 10240;  // 40 KB of masks (+ 4.3 KB static: under the 48 KB default)
 
@@ -727,6 +728,27 @@ __device__ __forceinline__ uint32_t ep_token_mask(const int32_t *ids, int t, int
   return mask;
 }
 
+// Destination mask of every token (bit d: a route to rank d), one warp per
+// token, into masks[t].
+__global__ void ep_mask_kernel(const int32_t *ids, int tokens, int width, int slots, int experts, int per_rank,
+                               uint32_t *masks, int *error) {
+  pdl_enter();
+  const int lane = threadIdx.x & 31;
+  const int warps = gridDim.x * (blockDim.x / 32);
+  for (int t = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; t < tokens; t += warps) {
+    uint32_t bit = 0;
+    if (lane < slots) {
+      const int id = ids[(size_t)t * width + lane];
+      if (id >= 0 && id < experts)
+        bit = 1u << (id / per_rank);
+      else if (error)
+        atomicCAS(error, 0, 403);
+    }
+    const uint32_t mask = __reduce_or_sync(0xffffffffu, bit);
+    if (lane == 0) masks[t] = mask;
+  }
+}
+
 __global__ void __launch_bounds__(kEpPlanThreads) ep_plan_kernel(const int32_t *ids, int tokens, int width,
                                                                  int slots, int experts, int per_rank, int nranks,
                                                                  int32_t *positions, int *error, bool staged) {
@@ -736,24 +758,9 @@ __global__ void __launch_bounds__(kEpPlanThreads) ep_plan_kernel(const int32_t *
   __shared__ int carry[32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (tid < nranks) carry[tid] = 0;
-  if (staged) {
-    // coalesced: thread e reads ids element e (token e / width, slot e %
-    // width); the width lanes of a token (width a power of two <= 32, so a
-    // token never straddles warps) OR their destination bits together
-    const int total = tokens * width, padded = (total + 31) / 32 * 32;
-    for (int e = tid; e < padded; e += kEpPlanThreads) {
-      const int slot = e & (width - 1);
-      uint32_t bit = 0;
-      if (e < total && slot < slots) {
-        const int id = ids[e];
-        if (id >= 0 && id < experts)
-          bit = 1u << (id / per_rank);
-        else if (error)
-          atomicCAS(error, 0, 403);
-      }
-      for (int o = width >> 1; o > 0; o >>= 1) bit |= __shfl_xor_sync(0xffffffffu, bit, o);
-      if (e < total && slot == 0) masks[e / width] = bit;
-    }
+  if (staged) {  // the masks ep_mask_kernel left in positions[0, tokens), read before any write
+    const uint32_t *src = reinterpret_cast<const uint32_t *>(positions);
+    for (int t = tid; t < tokens; t += kEpPlanThreads) masks[t] = src[t];
   }
   __syncthreads();
   for (int base = 0; base < tokens; base += kEpPlanThreads) {
@@ -1388,7 +1395,12 @@ static int ep_dispatch_impl(const void *x, int x_dtype, size_t tokens, size_t co
   if (self > 31) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_ep_dispatch: self rank");
   cudaStream_t s = as_stream(stream);
   const int per_rank = (int)(experts / nranks);
-  const bool staged = tokens <= (size_t)kEpPlanStagedTokens && (width & (width - 1)) == 0;
+  const bool staged = tokens <= (size_t)kEpPlanStagedTokens;
+  if (staged) {
+    launch_pdl(ep_mask_kernel, row_grid(tokens), 256, 0, s, ids, (int)tokens, (int)width, (int)slots, (int)experts,
+               per_rank, reinterpret_cast<uint32_t *>(positions), device_error_ptr());
+    FPB_LAUNCH_CHECK("ep_mask_kernel");
+  }
   launch_pdl(ep_plan_kernel, 1, kEpPlanThreads, staged ? tokens * sizeof(uint32_t) : 0, s, ids, (int)tokens,
              (int)width, (int)slots, (int)experts, per_rank, (int)nranks, positions, device_error_ptr(), staged);
   FPB_LAUNCH_CHECK("ep_plan_kernel");

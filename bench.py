@@ -933,8 +933,12 @@ def gemm_arm(args):
     else:
         hbm = float(peaks.get("hbm_gbs", 6650.0))
         achieved = gemm_bytes(m, n_rank, GEMM_K) / (per_launch_ms * 1e-3) / 1e9
+        traffic = None
+        if batched and (m, g) == (128, 1):  # DRAM bytes of one batch launch, scaled to one GEMM like `achieved`
+            t_launch = load_traffic("nvfp4_gemm_batch_config2_m128_traffic.txt")
+            traffic = t_launch / GEMM_MATS if t_launch else None
         roof = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                "traffic": None, "peak_kind": "measured hbm_gbs"}
+                "traffic": traffic, "algorithmic_bytes": gemm_bytes(m, n_rank, GEMM_K), "peak_kind": "measured hbm_gbs"}
     roof["per_launch_us"] = per_launch_ms * 1e3
     if batched:
         roof["per_launch_us"] = gemm_ms / args.steps * 1e3

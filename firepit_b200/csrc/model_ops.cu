@@ -390,6 +390,127 @@ __global__ void __launch_bounds__(kAttnTileThreads) attn_decode_tile_kernel(
   }
 }
 
+// The same partials with K and V rows read straight from global memory (no
+// shared-memory tile): block (b, kv head, chunk of kAttnTile positions), 8
+// warps, D = 32 * DPL.  Lane l holds columns [l * DPL, (l + 1) * DPL) of
+// every query head of the group in registers (group * DPL <= 64).
+//  1. scores: warp w takes positions w, w + 8, ...; it reads each K row once
+//     (a coalesced row per warp) and reduces each head's dot product over
+//     the lanes;
+//  2. softmax: warp w takes heads w, w + 8, ... (lane t: position t), the
+//     tile's max and sum of exponentials;
+//  3. p . V: warp w owns 32 columns (slice w % DPL) of the heads w / DPL,
+//     + 8 / DPL, ...; it reads each V row's slice once.
+// Each K and V element crosses the SM once.  The tile kernel above staged
+// the rows in shared memory and had each of the group's warps read all of
+// them: shared-memory bound at 3 CTAs per SM.
+template <int DPL>
+__global__ void __launch_bounds__(256) attn_decode_rows_kernel(const float *q, const float *k_cache,
+                                                               const float *v_cache, const int32_t *positions,
+                                                               int q_heads, int kv_heads, int max_seq, int chunks,
+                                                               float scale, float *part) {
+  pdl_enter();
+  constexpr int D = 32 * DPL, kMaxHeads = 64 / DPL, kSlicesPerHead = DPL, kHeadStride = 8 / DPL;
+  constexpr int kAccHeads = kMaxHeads / kHeadStride;  // heads a warp accumulates in step 3
+  __shared__ float sc[32][kAttnTile + 1];             // [head][position]: scores, then probabilities
+  const int group = q_heads / kv_heads;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int bk = blockIdx.x, chunk = blockIdx.y;
+  const int b = bk / kv_heads, kvh = bk % kv_heads;
+  const int limit = min(positions[b], max_seq - 1) + 1;
+  const int t0 = chunk * kAttnTile, n = min(limit - t0, kAttnTile);
+  if (n <= 0) return;  // past this row's position: not read by the merge
+  auto load_slice = [&](const float *src, float (&dst)[DPL]) {
+    if constexpr (DPL % 4 == 0) {
+#pragma unroll
+      for (int j = 0; j < DPL / 4; ++j) {
+        const float4 v = __ldg(reinterpret_cast<const float4 *>(src) + j);
+        dst[4 * j] = v.x; dst[4 * j + 1] = v.y; dst[4 * j + 2] = v.z; dst[4 * j + 3] = v.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < DPL / 2; ++j) {
+        const float2 v = __ldg(reinterpret_cast<const float2 *>(src) + j);
+        dst[2 * j] = v.x; dst[2 * j + 1] = v.y;
+      }
+    }
+  };
+  float qv[kMaxHeads][DPL];
+#pragma unroll
+  for (int h = 0; h < kMaxHeads; ++h) {
+    if (h < group) {
+      load_slice(q + ((size_t)b * q_heads + kvh * group + h) * D + lane * DPL, qv[h]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < DPL; ++j) qv[h][j] = 0.0f;
+    }
+  }
+  // 1. scores: the warp's (up to) four K rows requested together
+  constexpr int kRowsPerWarp = kAttnTile / 8;
+  float kx[kRowsPerWarp][DPL];
+#pragma unroll
+  for (int i = 0; i < kRowsPerWarp; ++i) {
+    const int t = w + 8 * i;
+    if (t < n) load_slice(k_cache + (((size_t)b * max_seq + t0 + t) * kv_heads + kvh) * D + lane * DPL, kx[i]);
+  }
+#pragma unroll
+  for (int i = 0; i < kRowsPerWarp; ++i) {
+    const int t = w + 8 * i;
+    if (t >= n) break;  // warp-uniform
+#pragma unroll
+    for (int h = 0; h < kMaxHeads; ++h) {
+      if (h < group) {
+        float sdot = 0.0f;
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) sdot = fmaf(qv[h][j], kx[i][j], sdot);
+        sdot = warp_sum(sdot);
+        if (lane == 0) sc[h][t] = sdot * scale;
+      }
+    }
+  }
+  __syncthreads();
+  // 2. softmax of each head over the tile
+  for (int h = w; h < group; h += 8) {
+    const float sv = lane < n ? sc[h][lane] : -INFINITY;
+    float m = sv;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float p = lane < n ? expf(sv - m) : 0.0f;
+    const float l = warp_sum(p);
+    sc[h][lane] = p;
+    if (lane == 0) {
+      float *out = part + (((size_t)b * q_heads + kvh * group + h) * chunks + chunk) * (D + 2);
+      out[D] = m;
+      out[D + 1] = l;
+    }
+  }
+  __syncthreads();
+  // 3. p . V: column d = slice * 32 + lane of heads h0, h0 + kHeadStride, ...
+  const int slice = w % kSlicesPerHead, h0 = w / kSlicesPerHead;
+  const int d = slice * 32 + lane;
+  float acc[kAccHeads];
+#pragma unroll
+  for (int i = 0; i < kAccHeads; ++i) acc[i] = 0.0f;
+  const float *vcol = v_cache + ((size_t)b * max_seq + t0) * kv_heads * D + (size_t)kvh * D + d;
+  const size_t vstride = (size_t)kv_heads * D;
+  float vv[kAttnTile];  // the column's tile, all requested before use
+#pragma unroll
+  for (int t = 0; t < kAttnTile; ++t) vv[t] = t < n ? __ldg(vcol + (size_t)t * vstride) : 0.0f;
+#pragma unroll
+  for (int t = 0; t < kAttnTile; ++t) {
+#pragma unroll
+    for (int i = 0; i < kAccHeads; ++i) {
+      const int h = h0 + i * kHeadStride;
+      if (h < group && t < n) acc[i] = fmaf(sc[h][t], vv[t], acc[i]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kAccHeads; ++i) {
+    const int h = h0 + i * kHeadStride;
+    if (h < group) part[(((size_t)b * q_heads + kvh * group + h) * chunks + chunk) * (D + 2) + d] = acc[i];
+  }
+}
+
 // Merge of the tile kernel's chunks with the output gate: one block per
 // (b, q head); the chunk weights exp(m_c - m) in shared memory, threads over
 // the head dimension.
@@ -984,8 +1105,25 @@ extern "C" int fpb_attn_decode(const float *q, const float *k_cache, const float
   const int chunks = (int)((max_seq + chunk_len - 1) / chunk_len);
   cudaStream_t s = as_stream(stream);
   float *part = static_cast<float *>(workspace);
+  const size_t group = q_heads / kv_heads;
+  if (chunk_len == (size_t)kAttnTile && chunks <= 65535 && (head_dim == 64 || head_dim == 128 || head_dim == 256) &&
+      group * (head_dim / 32) <= 64) {
+    const dim3 grid((unsigned)(batch * kv_heads), (unsigned)chunks);
+    auto go = [&](auto kernel) {
+      FPB_LAUNCH(kernel, grid, 256, 0, s, q, k_cache, v_cache, positions, (int)q_heads, (int)kv_heads, (int)max_seq,
+                 chunks, scale, part);
+      return (int)FPB_OK;
+    };
+    const int st = head_dim == 64    ? go(attn_decode_rows_kernel<2>)
+                   : head_dim == 128 ? go(attn_decode_rows_kernel<4>)
+                                     : go(attn_decode_rows_kernel<8>);
+    if (st) return st;
+    FPB_LAUNCH(attn_decode_merge_kernel, (unsigned)(batch * q_heads), 256, chunks * sizeof(float), s, part, q_gate,
+               (long long)qg_pitch, positions, (int)q_heads, (int)head_dim, (int)max_seq, (int)chunk_len, chunks, out,
+               out_dtype == FPB_BF16);
+    return FPB_OK;
+  }
   if (chunk_len == (size_t)kAttnTile && head_dim % 4 == 0 && chunks <= 8192) {
-    const size_t group = q_heads / kv_heads;
     const size_t smem = (2 * kAttnTile * kAttnPitch + group * head_dim) * sizeof(float);
     {
       static std::mutex mu;

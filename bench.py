@@ -944,6 +944,7 @@ def gemm_arm(args):
         roof["per_launch_us"] = gemm_ms / args.steps * 1e3
         roof["note"] = (f"one W4A4 batch launch per step (x quantize + {GEMM_MATS} GEMMs); achieved = the "
                         f"{GEMM_MATS} GEMMs' algorithmic bytes / that launch")
+    out = None
     if rank == 0:
         out = ({"metric": "NVFP4 GEMM TFLOPS", "value": value, "unit": "TFLOP/s", "n_gpus": g, "steps": args.steps,
               "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",

@@ -202,7 +202,8 @@ def gemv_config(g: int) -> dict:
             "launch": f"each rank's slices of the {MATS_PER_GPU * g} matrices in one prepared batch per "
                       f"{MAX_SEGS} (fpb_nvfp4_gemv_batch_run: x as NVFP4 digit planes, tcgen05), every matrix "
                       "with its own x row",
-            "parallelism": f"N-split x{g} + NCCL all-gather after each launch" if g > 1 else "single GPU",
+            "parallelism": f"N-split x{g}; the GEMV launch stores each rank's slices into every rank's gathered "
+                           "output (NVLink peer stores), one peer-memory barrier per step" if g > 1 else "single GPU",
             "l2": "inputs larger than L2: 605 MB of distinct weights per rank per step",
             "timing": "CUDA graph replay per launch, CUDA events, max over ranks"}
 
@@ -320,21 +321,39 @@ def ours_arm(args):
     x = F.synth_normal((mats, COLS), seed=0, stream_id=0, dtype=torch.bfloat16, device=dev)
     y_local = torch.empty(mats, rows_per_rank, dtype=torch.bfloat16, device=dev)
     groups = [range(i, min(i + MAX_SEGS, mats)) for i in range(0, mats, MAX_SEGS)]
-    y_all = [torch.empty(g, len(gr), rows_per_rank, dtype=torch.bfloat16, device=dev) for gr in groups]
+    # On more than one GPU the gathered outputs are buffers every rank maps
+    # (CUDA IPC): the GEMV's epilogue stores this rank's slices into all of
+    # them over NVLink, so the all-gather is part of the GEMV launch.
+    peer_bufs, barrier = [], None
+    if g > 1:
+        from firepit_b200.comm import PeerBarrier, PeerBuffer
+        peer_bufs = [PeerBuffer(g * len(gr) * rows_per_rank * 2) for gr in groups]
+        barrier = PeerBarrier()
+        y_all = [pb.local.view(torch.bfloat16).view(g, len(gr), rows_per_rank) for pb, gr in zip(peer_bufs, groups)]
+    else:
+        y_all = [torch.empty(g, len(gr), rows_per_rank, dtype=torch.bfloat16, device=dev) for gr in groups]
 
-    def batched(xsrc, tensor_cores=True):
+    def peers_of(i):
+        gr = groups[i]
+        return [[peer_bufs[i].ptrs[p] + (rank * len(gr) + j) * rows_per_rank * 2 for p in range(g)]
+                for j in range(len(gr))]
+
+    def batched(xsrc, tensor_cores=True, peers=False):
         """The step's GEMVs, one batch per group of matrices: on the tensor
         cores (x as NVFP4 digit planes, tcgen05) where the shapes allow, else
-        the streaming kernel."""
-        make = F.gemv_batch_planes if tensor_cores else F.gemv_batched
-        return [make([(slices[c], xsrc[c:c + 1], y_local[c:c + 1]) for c in gr]) for gr in groups]
+        the streaming kernel; with `peers` the batch also does the all-gather."""
+        if tensor_cores:
+            return [F.gemv_batch_planes([(slices[c], xsrc[c:c + 1], y_local[c:c + 1]) for c in gr],
+                                        y_peers=peers_of(i) if peers else None) for i, gr in enumerate(groups)]
+        return [F.gemv_batched([(slices[c], xsrc[c:c + 1], y_local[c:c + 1]) for c in gr]) for gr in groups]
 
     try:
-        launches_b = batched(x)
+        launches_b = batched(x, peers=g > 1)
         tensor_cores = True
     except F.ShapeError:
         launches_b = batched(x, tensor_cores=False)
         tensor_cores = False
+    fused = g > 1 and tensor_cores
 
     def launch(i, sh):
         if tensor_cores:
@@ -353,19 +372,24 @@ def ours_arm(args):
     ng = len(groups)
     overlap = g > 1
     if overlap:
-        # One graph per step: the groups' GEMVs on the capture stream, and each
-        # group's all-gather on a second stream as soon as its GEMV is done, so
-        # that it overlaps the next group's GEMV; the streams join at the end.
+        # One graph per step: the groups' GEMVs, which store every rank's
+        # gathered output themselves (peer stores), then a one-word all-reduce
+        # as the barrier; on the streaming fallback each group's NCCL
+        # all-gather runs on a second stream, overlapping the next group's GEMV.
         cs = torch.cuda.Stream(device=dev)
 
         def whole(sh):
             cur = torch.cuda.current_stream()
             for i in range(ng):
                 launch(i, sh)
-                cs.wait_stream(cur)
-                with torch.cuda.stream(cs):
-                    comm().all_gather_into(y_all[i], y_local[groups[i].start:groups[i].stop])
-            cur.wait_stream(cs)
+                if not fused:
+                    cs.wait_stream(cur)
+                    with torch.cuda.stream(cs):
+                        comm().all_gather_into(y_all[i], y_local[groups[i].start:groups[i].stop])
+            if fused:
+                barrier()  # every rank's peer stores have landed (fpb_peer_barrier)
+            else:
+                cur.wait_stream(cs)
 
         with torch.cuda.stream(s):  # eager once: the collectives set up outside capture
             whole(s.cuda_stream)
@@ -482,7 +506,7 @@ def ours_arm(args):
     xh.copy_(x.cpu())
     yh = torch.empty(g, mats, rows_per_rank, dtype=torch.bfloat16, pin_memory=True)
     xd = torch.empty_like(x)
-    e2e_b = batched(xd, tensor_cores)
+    e2e_b = batched(xd, tensor_cores, peers=fused)
     for b in e2e_b:  # eager once: every code path initialised outside capture
         b.submit(F.Async())
     torch.cuda.synchronize()
@@ -493,10 +517,14 @@ def ours_arm(args):
             b.submit(gsink)
         if g == 1:
             yh[0].copy_(y_local, non_blocking=True)
+        elif fused:
+            barrier()
+            for i, gr in enumerate(groups):
+                yh[:, gr.start:gr.stop].copy_(y_all[i], non_blocking=True)
 
     def e2e_step():
         gsink.replay()
-        if g > 1:
+        if g > 1 and not fused:
             for i, gr in enumerate(groups):
                 comm().all_gather_into(y_all[i], y_local[gr.start:gr.stop])
                 yh[:, gr.start:gr.stop].copy_(y_all[i], non_blocking=True)
@@ -563,14 +591,22 @@ def ours_arm(args):
             "clocks": clocks.summary(),
             "breakdown_ms": {"gemv": gemv_ms / args.steps,
                              "all_gather": (total_ms - gemv_ms) / args.steps if g > 1 else 0.0,
-                             "note": "all_gather = the step's time beyond its GEMVs (each group's all-gather "
-                                     "overlaps the next group's GEMV)" if g > 1 else "one GPU: no exchange"},
+                             "note": ("all_gather = the step's time beyond the GEMV launches, which store the "
+                                      "gathered output on every rank themselves (NVLink peer stores): the barrier"
+                                      if fused else "all_gather = the step's time beyond its GEMVs (each group's "
+                                      "NCCL all-gather overlaps the next group's GEMV)") if g > 1
+                                     else "one GPU: no exchange"},
         }
         if g == 1 and args.cpu_seconds > 0:
             out["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
     del graphs, gsink
     if overlap:
         del step_graph
+    del launches_b, e2e_b
+    if barrier is not None:
+        barrier.close()
+    for pb in peer_bufs:
+        pb.close()
     dist_sync()
     return out
 

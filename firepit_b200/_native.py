@@ -142,6 +142,8 @@ SIGNATURES: dict[str, tuple] = {
     "fpb_moe_gather_codes": (i32, [vp, sz, vp, sz, sz, sz, vp, sz, vp, i32, vp, vp, vp]),
     "fpb_ep_record_bytes": (sz, [sz, sz]),
     "fpb_nvfp4_gemm_batch_create": (i32, [C.POINTER(GemvSegment), i32, i32, i32, i32, vp, C.POINTER(vp)]),
+    "fpb_nvfp4_gemv_batch_create_peers": (i32, [C.POINTER(GemvSegment), i32, i32, i32, i32, C.POINTER(vp), i32, vp,
+                                                C.POINTER(vp)]),
     "fpb_ep_dispatch": (i32, [vp, i32, sz, sz, vp, vp, sz, sz, sz, sz, vp, vp, vp, vp, vp]),
     "fpb_ep_unpack": (i32, [vp, sz, sz, sz, vp, vp, vp]),
     "fpb_ep_dispatch_chunks": (i32, [vp, i32, sz, sz, vp, vp, sz, sz, sz, sz, vp, vp, i32, vp, vp, vp]),
@@ -151,6 +153,7 @@ SIGNATURES: dict[str, tuple] = {
     "fpb_ipc_get_handle": (i32, [vp, vp]),
     "fpb_ipc_open": (i32, [vp, C.POINTER(vp)]),
     "fpb_ipc_close": (i32, [vp]),
+    "fpb_peer_barrier": (i32, [vp, vp, vp, i32, i32, i32, vp]),
     "fpb_moe_gather": (i32, [vp, i32, sz, sz, vp, sz, vp, i32, vp]),
     "fpb_moe_gather_quantize": (i32, [vp, i32, sz, sz, vp, sz, vp, vp, vp, vp, vp, i32, vp, sz, vp]),
     "fpb_moe_gather_quantize_workspace_bytes": (sz, [sz, sz]),

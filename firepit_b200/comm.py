@@ -114,3 +114,90 @@ class Comm:
             self.destroy()
         except Exception:
             pass
+
+
+class PeerBuffer:
+    """A device buffer that every rank of a torch.distributed group maps
+    (CUDA IPC over NVLink): ``local`` is this rank's uint8 tensor, ``ptrs[r]``
+    the device address of rank r's buffer as this process sees it, so that a
+    kernel stores straight into another GPU's buffer.  Collective: every rank
+    constructs it with the same size, in the same order.  ``close()`` unmaps
+    the peers' buffers and frees this one after a barrier (no rank frees a
+    buffer another still maps)."""
+
+    def __init__(self, nbytes: int, group=None):
+        import torch
+        import torch.distributed as dist
+        self.group = group
+        p = C.c_void_p()
+        N.call("fpb_ipc_alloc", nbytes, C.byref(p))
+        self._own = p.value
+        dev = torch.cuda.current_device()
+
+        class _Buf:
+            __cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (p.value, False),
+                                        "version": 3, "strides": None}
+        self.local = torch.as_tensor(_Buf(), device=torch.device("cuda", dev))
+        h = (C.c_uint8 * N.FPB_IPC_HANDLE_BYTES)()
+        N.call("fpb_ipc_get_handle", p.value, h)
+        world = dist.get_world_size(group)
+        rank = dist.get_rank(group)
+        every = [None] * world
+        dist.all_gather_object(every, bytes(h), group=group)
+        self._opened = []
+        self.ptrs = []
+        for r in range(world):
+            if r == rank:
+                self.ptrs.append(self._own)
+                continue
+            q = C.c_void_p()
+            N.call("fpb_ipc_open", (C.c_uint8 * N.FPB_IPC_HANDLE_BYTES).from_buffer_copy(every[r]), C.byref(q))
+            self._opened.append(q.value)
+            self.ptrs.append(q.value)
+
+    def close(self) -> None:
+        import torch
+        import torch.distributed as dist
+        if self._own is None:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        for q in self._opened:
+            N.lib.fpb_ipc_close(q)
+        self._opened = []
+        dist.barrier(group=self.group)
+        self.local = None
+        N.lib.fpb_ipc_free(self._own)
+        self._own = None
+
+
+class PeerBarrier:
+    """``fpb_peer_barrier`` over a group of ranks (one GPU each): the flag
+    words live in a ``PeerBuffer``, the epoch counter on this GPU.  Calling it
+    enqueues the barrier on the current stream (graph-capturable); every rank
+    must call it the same number of times.  A rank that does not arrive
+    within ``timeout_ms`` makes the others record device error 601 and go
+    on."""
+
+    def __init__(self, group=None, timeout_ms: int = 2000):
+        import torch
+        import torch.distributed as dist
+        self.nranks = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.timeout_ms = int(timeout_ms)
+        self.buf = PeerBuffer(256, group)
+        self.buf.local.zero_()
+        dev = self.buf.local.device
+        self.counter = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.table = torch.tensor(self.buf.ptrs, dtype=torch.int64, device=dev)
+        torch.cuda.synchronize()
+        dist.barrier(group=group)  # every flag word is zero before any rank announces
+
+    def __call__(self, stream=None) -> None:
+        import torch
+        s = torch.cuda.current_stream().cuda_stream if stream is None else stream
+        N.call("fpb_peer_barrier", self.counter.data_ptr(), self.buf.local.data_ptr(), self.table.data_ptr(),
+               self.nranks, self.rank, self.timeout_ms, s)
+
+    def close(self) -> None:
+        self.buf.close()

@@ -296,3 +296,65 @@ extern "C" int fpb_ipc_close(void *ptr) {
   if (ptr) FPB_CUDA_TRY(cudaIpcCloseMemHandle(ptr));
   return FPB_OK;
 }
+
+// ---- barrier over peer memory ----------------------------------------------------------------
+// One warp: lane r < nranks stores this barrier's epoch into rank r's flag
+// word for this rank (a system-scope release store over NVLink), then waits
+// until rank r's epoch has arrived in this rank's own flag word r (acquire
+// loads).  The release orders every store this rank made before the barrier
+// (the peer stores of the kernels before it, which end with a system-scope
+// fence) before the flag, so a rank that has seen every flag sees every
+// rank's stores.  A flag already past the epoch counts: a faster rank may
+// announce the next barrier first.  The epoch is a device counter, so a CUDA
+// graph replays the barrier with new epochs.  Every wait ends after
+// `timeout_ns` of global time with device error 601 (fpb_device_error) and
+// the kernel returns: a rank that never arrives cannot hang the others.
+namespace fpb {
+namespace {
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__global__ void peer_barrier_kernel(uint32_t *counter, const uint32_t *flags, uint32_t *const *peer_flags, int nranks,
+                                    int rank, unsigned long long timeout_ns, int *error) {
+  pdl_enter();
+  const int t = threadIdx.x;
+  const uint32_t epoch = *counter + 1;
+  if (t < nranks) {
+    uint32_t *dst = peer_flags[t] + rank;
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(dst), "r"(epoch) : "memory");
+    const uint64_t start = global_ns();
+    bool arrived = false;
+    while (true) {
+      uint32_t v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + t) : "memory");
+      if ((int)(v - epoch) >= 0) {
+        arrived = true;
+        break;
+      }
+      if (global_ns() - start > timeout_ns) break;
+    }
+    if (!arrived && error) atomicCAS(error, 0, 601);
+  }
+  __syncwarp();
+  if (t == 0) *counter = epoch;
+}
+
+}  // namespace
+}  // namespace fpb
+
+extern "C" int fpb_peer_barrier(uint32_t *counter, const uint32_t *flags, uint32_t *const *peer_flags, int nranks,
+                                int rank, int timeout_ms, void *stream) {
+  if (!counter || !flags || !peer_flags) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_peer_barrier: null pointer");
+  if (nranks < 1 || nranks > 32 || rank < 0 || rank >= nranks || timeout_ms < 1)
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_peer_barrier: nranks %d rank %d timeout %d ms", nranks, rank,
+                timeout_ms);
+  cudaError_t e = launch_pdl(fpb::peer_barrier_kernel, 1, 32, 0, fpb::as_stream(stream), counter, flags, peer_flags,
+                              nranks, rank, (unsigned long long)timeout_ms * 1000000ull, fpb::device_error_ptr());
+  if (e != cudaSuccess) return cuda_fail(e, "peer_barrier_kernel");
+  FPB_LAUNCH_CHECK("peer_barrier_kernel");
+  return FPB_OK;
+}

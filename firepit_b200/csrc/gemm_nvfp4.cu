@@ -120,6 +120,7 @@ __global__ void act_encode_kernel(const T *x, size_t rows, size_t cols, const ui
 // load time): weight rows [row_begin, row_begin + rows) of one handle times
 // its own x [batch, K], into y [batch, rows].  The tensor map lives in
 // global memory (64-byte aligned), which TMA reads like a parameter.
+constexpr int kMaxPeerCopies = 8;
 struct alignas(64) PlaneSeg {
   CUtensorMap tmap_b;       // the handle's codes (box 128 rows x 128 bytes)
   CUtensorMap tmap_y;       // W4A4 batch: y [m, rows] for TMA stores (valid when the batch stores that way)
@@ -130,6 +131,11 @@ struct alignas(64) PlaneSeg {
   int row_begin, rows;
   int item_begin;           // first item (128-row tile) of this segment
   int a_group;              // A row group of its x: the first segment with the same x (encoded once)
+  // Planes batch with peer copies: y goes to these n_peer rows instead (e.g.
+  // this rank's slice in every rank's gathered buffer: plain stores over
+  // NVLink, the all-gather of an N-split GEMV done by the epilogue).
+  int n_peer;
+  void *y_peer[kMaxPeerCopies];
 };
 
 // ---- x as NVFP4 digit planes (tensor-core GEMV) ----------------------------------------
@@ -341,6 +347,7 @@ struct GemmParams {
   const PlaneSeg *segs;
   int nseg;
   int total_items;
+  int peer_stores;  // some segment stores to peer copies: a system-scope fence ends the epilogue
   // Rows of each A box tmap_a loads (planes: the tokens' 8 * tokens plane
   // rows; the tile's other rows keep whatever the stage held and only feed
   // accumulator rows nothing reads).  128 otherwise.
@@ -712,14 +719,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             void *ydst = sg ? sg->y : p.y;
             const long long ybase = sg ? (long long)token * sg->rows
                                        : (long long)item_group * p.y_group_stride + (long long)token * p.ldy;
+            const int copies = sg && sg->n_peer ? sg->n_peer : 1;
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
               const int n = nw + c * 32 + i * 8 + pl;
               if (n < n_lim) {
-                if (p.y_bf16)
-                  reinterpret_cast<__nv_bfloat16 *>(ydst)[ybase + n] = __float2bfloat16_rn(keep[i]);
-                else
-                  reinterpret_cast<float *>(ydst)[ybase + n] = keep[i];
+                for (int k = 0; k < copies; ++k) {
+                  void *dst = sg && sg->n_peer ? sg->y_peer[k] : ydst;
+                  if (p.y_bf16)
+                    reinterpret_cast<__nv_bfloat16 *>(dst)[ybase + n] = __float2bfloat16_rn(keep[i]);
+                  else
+                    reinterpret_cast<float *>(dst)[ybase + n] = keep[i];
+                }
               }
             }
           }
@@ -888,6 +899,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     // Stores in flight read this CTA's shared memory: complete them before exit.
     if (lane == 0 && p.tma_store) bulk_wait_all();
+    if (p.peer_stores) __threadfence_system();  // peer copies land before the caller's barrier
   }
   tc_fence_before();
   __syncthreads();
@@ -1327,16 +1339,21 @@ struct fpb_gemv_batch {
   int count = 0, batch = 0, K = 0, x_dtype = 0, y_dtype = 0, total_items = 0;
   int w4a4 = 0;                   // fpb_nvfp4_gemm_batch_create: x quantized to NVFP4, batch = m <= 128
   int tma_store = 0;              // W4A4: every member's y takes TMA stores (16-byte aligned base and pitch)
+  int n_peer = 0;                 // peer copies of every member's y
 };
 
 static int batch_create_impl(const fpb_gemv_segment *segs, int count, int x_dtype, int y_dtype, int batch,
-                             bool w4a4, void *stream, fpb_gemv_batch **out) {
+                             bool w4a4, void *stream, fpb_gemv_batch **out, const void *const *y_peers = nullptr,
+                             int n_peer = 0) {
   if (!segs || !out) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_gemv_batch_create: null pointer");
   *out = nullptr;
   if (count < 1 || count > kMoeIdsCached)
     return fail(FPB_ERR_SHAPE, "fpb_nvfp4_gemv_batch_create: count %d not in [1, %d]", count, kMoeIdsCached);
   if ((x_dtype != FPB_F32 && x_dtype != FPB_BF16) || (y_dtype != FPB_F32 && y_dtype != FPB_BF16))
     return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_gemv_batch_create: dtype");
+  if (n_peer < 0 || n_peer > kMaxPeerCopies || (n_peer && (!y_peers || w4a4)))
+    return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_gemv_batch_create_peers: %d peer copies (at most %d)", n_peer,
+                kMaxPeerCopies);
   const int max_batch = w4a4 ? kBM : 16;
   if (batch < 1 || batch > max_batch)
     return fail(FPB_ERR_SHAPE, "fpb_nvfp4_%s_batch_create: %s %d not in [1, %d]", w4a4 ? "gemm" : "gemv",
@@ -1377,6 +1394,14 @@ static int batch_create_impl(const fpb_gemv_segment *segs, int count, int x_dtyp
     if (w4a4 && !encode_store_map(&d.tmap_y, sg.y, y_dtype == FPB_BF16, (uint64_t)batch, (uint64_t)d.rows,
                                   (uint64_t)d.rows, 32, 0))
       all_tma = false;
+    d.n_peer = n_peer;
+    for (int k = 0; k < n_peer; ++k) {
+      const void *yp = y_peers[(size_t)i * n_peer + k];
+      if (!yp || (reinterpret_cast<uintptr_t>(yp) & (y_dtype == FPB_BF16 ? 1 : 3)))
+        return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_nvfp4_gemv_batch_create_peers: segment %d copy %d null or unaligned",
+                    i, k);
+      d.y_peer[k] = const_cast<void *>(yp);
+    }
     d.a_group = i;
     for (int j = 0; j < i; ++j)
       if (segs[j].x == sg.x) {
@@ -1393,6 +1418,7 @@ static int batch_create_impl(const fpb_gemv_segment *segs, int count, int x_dtyp
   b->y_dtype = y_dtype;
   b->total_items = items;
   b->w4a4 = w4a4 ? 1 : 0;
+  b->n_peer = n_peer;
   b->tma_store = all_tma ? 1 : 0;
   std::memcpy(&b->tmap_b0, segs[0].w->extras->tmap_b, sizeof(CUtensorMap));
   cudaStream_t s = as_stream(stream);
@@ -1426,6 +1452,12 @@ static int batch_create_impl(const fpb_gemv_segment *segs, int count, int x_dtyp
 extern "C" int fpb_nvfp4_gemv_batch_create(const fpb_gemv_segment *segs, int count, int x_dtype, int y_dtype,
                                            int batch, void *stream, fpb_gemv_batch **out) {
   return batch_create_impl(segs, count, x_dtype, y_dtype, batch, false, stream, out);
+}
+
+extern "C" int fpb_nvfp4_gemv_batch_create_peers(const fpb_gemv_segment *segs, int count, int x_dtype, int y_dtype,
+                                                 int batch, const void *const *y_peers, int n_peer, void *stream,
+                                                 fpb_gemv_batch **out) {
+  return batch_create_impl(segs, count, x_dtype, y_dtype, batch, false, stream, out, y_peers, n_peer);
 }
 
 extern "C" int fpb_nvfp4_gemm_batch_create(const fpb_gemv_segment *segs, int count, int x_dtype, int y_dtype, int m,
@@ -1516,6 +1548,7 @@ extern "C" int fpb_nvfp4_gemv_batch_run(const fpb_gemv_batch *b, void *stream) {
   p.segs = b->segs;
   p.nseg = b->count;
   p.total_items = b->total_items;
+  p.peer_stores = b->n_peer > 0;
   const unsigned grid = (unsigned)std::min<size_t>((size_t)b->total_items, (size_t)std::max(1, sm_count()));
   e = launch_pdl(nvfp4_gemm_kernel, grid, kGemmThreads, kGemmSmem, s, b->tmap_a, b->tmap_b0, b->tmap_a, b->tmap_b0,
                  b->tmap_a, p);

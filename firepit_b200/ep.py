@@ -369,6 +369,9 @@ class EpMoeLayer:
         reads: a one-word all-reduce on the stream."""
         if self.nranks == 1:
             return
+        if getattr(self, "_peer_barrier", None) is not None:
+            self._peer_barrier()  # fpb_peer_barrier: flags over NVLink
+            return
         self._all_reduce_max(self.ops.barrier_word)  # MAX of zeros: the word stays 0
 
     def connect_peers(self) -> None:
@@ -408,8 +411,13 @@ class EpMoeLayer:
         T = ops.tokens
         ops.connect([bases[d][0] + me * T * ops.rec for d in range(n)],
                     [bases[s][1] + me * T * ops.hidden * 4 for s in range(n)], me)
+        from .comm import PeerBarrier
+        self._peer_barrier = PeerBarrier(self.group)
 
     def close_peers(self) -> None:
+        if getattr(self, "_peer_barrier", None) is not None:
+            self._peer_barrier.close()
+            self._peer_barrier = None
         for p in getattr(self, "_opened", []):
             N.lib.fpb_ipc_close(p)
         self._opened = []

@@ -172,13 +172,26 @@ class PlanesGemvBatch(BatchedGemv):
     Needs cols % 256 == 0, cols <= 4096 and rows starting at multiples of
     128 (ShapeError otherwise: use ``gemv_batched``)."""
 
-    def __init__(self, members, tile: GemvTile = DEFAULT_GEMV_TILE):
+    def __init__(self, members, tile: GemvTile = DEFAULT_GEMV_TILE, y_peers=None):
+        """y_peers (optional): per member, the device pointers of the copies
+        its result goes to instead of its y (fpb_nvfp4_gemv_batch_create_peers:
+        e.g. this rank's slice in every rank's gathered output)."""
         super().__init__(members, tile)
         first = self.gemvs[0]
         h = C.c_void_p()
-        st = N.lib.fpb_nvfp4_gemv_batch_create(self._segs, len(self.gemvs), _dtype_code(first.x),
-                                                _dtype_code(first.y), first.x.shape[0],
-                                                current_stream_handle(first.x.device), C.byref(h))
+        stream = current_stream_handle(first.x.device)
+        if y_peers is None:
+            st = N.lib.fpb_nvfp4_gemv_batch_create(self._segs, len(self.gemvs), _dtype_code(first.x),
+                                                    _dtype_code(first.y), first.x.shape[0], stream, C.byref(h))
+        else:
+            n_peer = len(y_peers[0])
+            if len(y_peers) != len(self.gemvs) or any(len(p) != n_peer for p in y_peers):
+                raise ShapeError("batched GEMV: one list of peer copies per member, all of one length")
+            arr = (C.c_void_p * (len(self.gemvs) * n_peer))(*[int(v) for p in y_peers for v in p])
+            self._peers = arr
+            st = N.lib.fpb_nvfp4_gemv_batch_create_peers(self._segs, len(self.gemvs), _dtype_code(first.x),
+                                                          _dtype_code(first.y), first.x.shape[0], arr, n_peer,
+                                                          stream, C.byref(h))
         if st == N.FPB_ERR_UNSUPPORTED or st == N.FPB_ERR_SHAPE:
             raise ShapeError(N.last_error())
         N.check(st, "fpb_nvfp4_gemv_batch_create")
@@ -198,9 +211,10 @@ class PlanesGemvBatch(BatchedGemv):
             self._batch = None
 
 
-def gemv_batch_planes(members, tile: GemvTile = DEFAULT_GEMV_TILE) -> PlanesGemvBatch:
-    """members: ``(weight, x, y)`` or ``(weight, x, y, rows)`` tuples."""
-    return PlanesGemvBatch(members, tile)
+def gemv_batch_planes(members, tile: GemvTile = DEFAULT_GEMV_TILE, y_peers=None) -> PlanesGemvBatch:
+    """members: ``(weight, x, y)`` or ``(weight, x, y, rows)`` tuples; y_peers
+    as in ``PlanesGemvBatch``."""
+    return PlanesGemvBatch(members, tile, y_peers)
 
 
 class ExpertGemvView:

@@ -316,6 +316,18 @@ int fpb_nvfp4_gemv_batch_create(const fpb_gemv_segment *segs, int count, int x_d
  * run and destroyed with fpb_nvfp4_gemv_batch_run / _destroy. */
 int fpb_nvfp4_gemm_batch_create(const fpb_gemv_segment *segs, int count, int x_dtype, int y_dtype, int m,
                                 void *stream, fpb_gemv_batch **out);
+/* fpb_nvfp4_gemv_batch_create whose members' results go, instead of to y, to
+ * n_peer copies each: y_peers [count * n_peer] host array of device
+ * pointers (member i's copies at y_peers[i * n_peer .. + n_peer), each laid
+ * out like its y, 2-byte (bf16) or 4-byte (f32) aligned, n_peer <= 8).  For
+ * an N-split GEMV the copies are this rank's slice in every rank's gathered
+ * output (buffers of the other GPUs opened with fpb_ipc_open): the epilogue
+ * does the all-gather with plain stores over NVLink and ends with a
+ * system-scope fence; the caller orders the readers after it with a barrier
+ * on the stream (e.g. a one-word fpb_comm_all_reduce), and the next run's
+ * stores after the readers. */
+int fpb_nvfp4_gemv_batch_create_peers(const fpb_gemv_segment *segs, int count, int x_dtype, int y_dtype, int batch,
+                                      const void *const *y_peers, int n_peer, void *stream, fpb_gemv_batch **out);
 int fpb_nvfp4_gemv_batch_run(const fpb_gemv_batch *b, void *stream);
 int fpb_nvfp4_gemv_batch_destroy(fpb_gemv_batch *b);
 /* The down projection after the gate/up one: gate_up [cap][tokens][2 * cols]
@@ -746,6 +758,20 @@ int fpb_ipc_free(void *ptr);
 int fpb_ipc_get_handle(const void *ptr, uint8_t handle[FPB_IPC_HANDLE_BYTES]);
 int fpb_ipc_open(const uint8_t handle[FPB_IPC_HANDLE_BYTES], void **ptr);
 int fpb_ipc_close(void *ptr);
+/* Barrier of nranks GPUs over peer memory, one 32-thread launch on the
+ * stream: flags = this rank's nranks uint32 words in a buffer every rank
+ * maps (zeroed before first use), peer_flags = device table of every rank's
+ * flags as this process maps them (fpb_ipc_open), counter = this rank's
+ * device uint32 epoch counter (zeroed; the same number of barriers on every
+ * rank).  Each rank stores the new epoch into every rank's flag word for it
+ * (system-scope release) and waits for every rank's (acquire), so the stores
+ * each rank made before its barrier - e.g. peer copies of
+ * fpb_nvfp4_gemv_batch_create_peers or fpb_ep_dispatch_chunks - are visible
+ * to all ranks after theirs.  A wait gives up after timeout_ms of global time
+ * with device error 601 (fpb_device_error) and the kernel returns.  Cheaper
+ * than a one-word NCCL all-reduce; graph-capturable. */
+int fpb_peer_barrier(uint32_t *counter, const uint32_t *flags, uint32_t *const *peer_flags, int nranks, int rank,
+                     int timeout_ms, void *stream);
 typedef struct fpb_comm fpb_comm;
 /* Extra element types of the collectives (besides FPB_F32, FPB_BF16). */
 enum { FPB_COMM_U32 = 2, FPB_COMM_I32 = 3, FPB_COMM_BYTES = 4 };

@@ -187,3 +187,35 @@ def test_planes_batch_matches_single(F, torch, rows, cols, mats, batch):
         assert O.rel_frobenius(ys[i].cpu().numpy(), want) <= REL, i
     with pytest.raises(F.ShapeError):  # row range not starting at a multiple of 128
         F.gemv_batch_planes([(weights[0], xt[0], ys[0][:, :rows - 192], range(64, rows - 128))], F.GemvTile(1, 4))
+
+
+@pytest.mark.parametrize("out_bf16", [True, False])
+def test_planes_batch_peer_copies(F, torch, out_bf16):
+    """fpb_nvfp4_gemv_batch_create_peers: each member's result goes to its
+    copies (here three places in one local buffer, standing for this rank's
+    slice in three ranks' gathered outputs), equal to the plain batch's y bit
+    for bit, and the member's own y is left alone."""
+    rows, cols, mats, batch = 512, 1024, 3, 2
+    yd = torch.bfloat16 if out_bf16 else torch.float32
+    weights = []
+    for c in range(mats):
+        w = F.synth_normal((rows, cols), seed=70 + c, stream_id=1, std=0.02)
+        packed, scales, g = F.quantize_nvfp4(w)
+        weights.append(F.Nvfp4Matrix.from_device(packed, scales, g, rows, cols))
+    xs = [F.synth_normal((batch, cols), seed=80 + c, stream_id=0, dtype=torch.bfloat16) for c in range(mats)]
+    ys = [torch.empty(batch, rows, dtype=yd, device="cuda") for _ in range(mats)]
+    F.gemv_batch_planes([(weights[c], xs[c], ys[c]) for c in range(mats)], F.GemvTile(1, 4)).submit(F.Eager())
+    ranks = 3
+    gathered = torch.full((ranks, mats, batch, rows), -7.0, dtype=yd, device="cuda")
+    own = [torch.full((batch, rows), -3.0, dtype=yd, device="cuda") for _ in range(mats)]
+    peers = [[gathered[r, c].data_ptr() for r in range(ranks)] for c in range(mats)]
+    F.gemv_batch_planes([(weights[c], xs[c], own[c]) for c in range(mats)], F.GemvTile(1, 4),
+                        y_peers=peers).submit(F.Eager())
+    torch.cuda.synchronize()
+    for c in range(mats):
+        for r in range(ranks):
+            assert torch.equal(gathered[r, c], ys[c])
+        assert bool((own[c] == -3.0).all())
+    assert F.device_error() == 0
+    with pytest.raises(Exception):
+        F.gemv_batch_planes([(weights[0], xs[0], own[0])], F.GemvTile(1, 4), y_peers=[[gathered[0, 0].data_ptr()] * 9])

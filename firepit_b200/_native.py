@@ -154,6 +154,7 @@ SIGNATURES: dict[str, tuple] = {
     "fpb_ipc_open": (i32, [vp, C.POINTER(vp)]),
     "fpb_ipc_close": (i32, [vp]),
     "fpb_peer_barrier": (i32, [vp, vp, vp, i32, i32, i32, vp]),
+    "fpb_peer_all_reduce_max": (i32, [vp, vp, vp, i32, i32, vp, i32, vp]),
     "fpb_moe_gather": (i32, [vp, i32, sz, sz, vp, sz, vp, i32, vp]),
     "fpb_moe_gather_quantize": (i32, [vp, i32, sz, sz, vp, sz, vp, vp, vp, vp, vp, i32, vp, sz, vp]),
     "fpb_moe_gather_quantize_workspace_bytes": (sz, [sz, sz]),

@@ -185,7 +185,7 @@ class PeerBarrier:
         self.nranks = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.timeout_ms = int(timeout_ms)
-        self.buf = PeerBuffer(256, group)
+        self.buf = PeerBuffer(512, group)  # 32 flag words, then two banks of 32 value slots
         self.buf.local.zero_()
         dev = self.buf.local.device
         self.counter = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -198,6 +198,14 @@ class PeerBarrier:
         s = torch.cuda.current_stream().cuda_stream if stream is None else stream
         N.call("fpb_peer_barrier", self.counter.data_ptr(), self.buf.local.data_ptr(), self.table.data_ptr(),
                self.nranks, self.rank, self.timeout_ms, s)
+
+    def all_reduce_max(self, t, stream=None) -> None:
+        """In place MAX over the ranks of the uint32 word t (e.g. amax float
+        bits), with the barrier (fpb_peer_all_reduce_max)."""
+        import torch
+        s = torch.cuda.current_stream().cuda_stream if stream is None else stream
+        N.call("fpb_peer_all_reduce_max", self.counter.data_ptr(), self.buf.local.data_ptr(), self.table.data_ptr(),
+               self.nranks, self.rank, t.data_ptr(), self.timeout_ms, s)
 
     def close(self) -> None:
         self.buf.close()

@@ -318,13 +318,22 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 
+// With `value` (all-reduce MAX of one uint32 word): before its flag, lane r
+// also stores *value into rank r's slot for this rank; the slots alternate
+// between two banks by epoch parity (a rank that is already one barrier
+// ahead writes the other bank), and after the waits the lanes take the
+// maximum of this rank's slots.
+constexpr int kBarrierSlots = 32;  // words [32, 96) of the flag buffer: two banks of 32
+
 __global__ void peer_barrier_kernel(uint32_t *counter, const uint32_t *flags, uint32_t *const *peer_flags, int nranks,
-                                    int rank, unsigned long long timeout_ns, int *error) {
+                                    int rank, unsigned long long timeout_ns, int *error, uint32_t *value) {
   pdl_enter();
   const int t = threadIdx.x;
   const uint32_t epoch = *counter + 1;
+  const int bank = kBarrierSlots + (int)(epoch & 1u) * kBarrierSlots;
   if (t < nranks) {
     uint32_t *dst = peer_flags[t] + rank;
+    if (value) peer_flags[t][bank + rank] = *value;
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(dst), "r"(epoch) : "memory");
     const uint64_t start = global_ns();
     bool arrived = false;
@@ -340,21 +349,40 @@ __global__ void peer_barrier_kernel(uint32_t *counter, const uint32_t *flags, ui
     if (!arrived && error) atomicCAS(error, 0, 601);
   }
   __syncwarp();
+  if (value) {
+    uint32_t m = t < nranks ? *reinterpret_cast<const volatile uint32_t *>(flags + bank + t) : 0u;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+    __syncwarp();
+    if (t == 0) *value = m;
+  }
   if (t == 0) *counter = epoch;
 }
 
 }  // namespace
 }  // namespace fpb
 
-extern "C" int fpb_peer_barrier(uint32_t *counter, const uint32_t *flags, uint32_t *const *peer_flags, int nranks,
-                                int rank, int timeout_ms, void *stream) {
+static int peer_barrier_impl(uint32_t *counter, const uint32_t *flags, uint32_t *const *peer_flags, int nranks,
+                             int rank, int timeout_ms, uint32_t *value, void *stream) {
   if (!counter || !flags || !peer_flags) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_peer_barrier: null pointer");
   if (nranks < 1 || nranks > 32 || rank < 0 || rank >= nranks || timeout_ms < 1)
     return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_peer_barrier: nranks %d rank %d timeout %d ms", nranks, rank,
                 timeout_ms);
   cudaError_t e = launch_pdl(fpb::peer_barrier_kernel, 1, 32, 0, fpb::as_stream(stream), counter, flags, peer_flags,
-                              nranks, rank, (unsigned long long)timeout_ms * 1000000ull, fpb::device_error_ptr());
+                              nranks, rank, (unsigned long long)timeout_ms * 1000000ull, fpb::device_error_ptr(),
+                              value);
   if (e != cudaSuccess) return cuda_fail(e, "peer_barrier_kernel");
   FPB_LAUNCH_CHECK("peer_barrier_kernel");
   return FPB_OK;
+}
+
+extern "C" int fpb_peer_barrier(uint32_t *counter, const uint32_t *flags, uint32_t *const *peer_flags, int nranks,
+                                int rank, int timeout_ms, void *stream) {
+  return peer_barrier_impl(counter, flags, peer_flags, nranks, rank, timeout_ms, nullptr, stream);
+}
+
+extern "C" int fpb_peer_all_reduce_max(uint32_t *counter, const uint32_t *flags, uint32_t *const *peer_flags,
+                                       int nranks, int rank, uint32_t *value, int timeout_ms, void *stream) {
+  if (!value) return fail(FPB_ERR_INVALID_ARGUMENT, "fpb_peer_all_reduce_max: null value");
+  return peer_barrier_impl(counter, flags, peer_flags, nranks, rank, timeout_ms, value, stream);
 }

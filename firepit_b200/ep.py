@@ -1,32 +1,25 @@
-"""Expert-parallel MoE over NCCL all-to-all (no reference counterpart: the
-reference runs one GPU).
+"""Expert-parallel MoE (no reference counterpart: the reference runs one GPU).
 
 Experts are sharded ``experts / world`` per rank; every rank routes its own
-tokens.  One layer:
+tokens.  Two forms:
 
-1. router top-k on the rank's tokens (``fpb_moe_topk``);
-2. dispatch order: the routes' destination ranks (``fpb_moe_route_dest``) laid
-   out with ``fpb_moe_layout`` (ranks as experts, one-row tiles) — a stable
-   counting sort, so each destination receives its routes in (token, slot)
-   order; the send buffer is the gather of those token rows and
-   ``fpb_moe_route_meta`` tags each row with its receiver-local expert;
-3. per-destination counts are exchanged (one small all-to-all; the host reads
-   them to size the variable splits), then rows and tags (all-to-all);
-4. the receiver runs its local experts on the rows it got (the single-GPU MoE
-   path: layout by local expert, gather + NVFP4 quantize, grouped gate/up
-   GEMM with SwiGLU in its epilogue, h quantize, grouped down GEMM,
-   un-permute);
-5. results go back the reverse way (all-to-all) and the source rank combines
-   them with its routing weights (``fpb_moe_combine`` over the dispatch
-   layout's ``inverse``).
+* ``EpMoeLayer`` + ``DeviceEpOps`` (what the bench runs): fixed capacity, one
+  NVFP4 record per (token, destination rank) in equal chunks
+  (``fpb_ep_dispatch``), so nothing is read by the host and the layer is one
+  CUDA graph per rank.  The receiver lays out the records by local expert
+  (``fpb_moe_layout_masked``), gathers their codes (``fpb_moe_gather_codes``),
+  runs the grouped GEMMs and returns one f32 partial sum per record; the
+  source adds the partials in rank order.  With ``connect_peers`` (CUDA IPC)
+  dispatch and the partial combine store straight into the other GPUs'
+  buffers and ``fpb_peer_barrier`` / ``fpb_peer_all_reduce_max`` replace the
+  collectives; otherwise NCCL all-to-alls carry the chunks.
+* ``ep_moe_forward``: variable splits, one bf16 row per route, the counts
+  read by the host; with ``HostOps`` (the oracle, test infrastructure) it is
+  the CPU restatement the gloo tests run.
 
 The activation quantizers take their global from an amax reduced over all
-ranks (all-reduce MAX), so every row is encoded exactly as the single-GPU path
-would encode it and the expert-parallel output equals the single-GPU output.
-
-``DeviceOps`` runs the CUDA library; ``HostOps`` runs the CPU oracle (test
-infrastructure, used only by tests) with the same interface, so the dispatch
-logic is testable with gloo ranks on CPU.
+ranks (MAX), so every row is encoded exactly as the single-GPU layer would
+encode it.  ``HostEpOps`` (tests) is the CPU stand-in of ``DeviceEpOps``.
 """
 from __future__ import annotations
 
@@ -356,6 +349,9 @@ class EpMoeLayer:
 
     def _all_reduce_max(self, a):
         if self.nranks == 1:
+            return a
+        if getattr(self, "_peer_barrier", None) is not None:
+            self._peer_barrier.all_reduce_max(a)  # over NVLink flags, no NCCL launch
             return a
         if self.comm is not None:
             self.comm.all_reduce_max_bits(a)

@@ -772,6 +772,12 @@ int fpb_ipc_close(void *ptr);
  * than a one-word NCCL all-reduce; graph-capturable. */
 int fpb_peer_barrier(uint32_t *counter, const uint32_t *flags, uint32_t *const *peer_flags, int nranks, int rank,
                      int timeout_ms, void *stream);
+/* The same barrier carrying one uint32 word: *value (device, in/out) becomes
+ * the maximum of every rank's *value (e.g. activation amax float bits, as
+ * fpb_comm_all_reduce MAX).  The flag buffer then needs 96 words (the flags
+ * and two banks of slots, by epoch parity). */
+int fpb_peer_all_reduce_max(uint32_t *counter, const uint32_t *flags, uint32_t *const *peer_flags, int nranks,
+                            int rank, uint32_t *value, int timeout_ms, void *stream);
 typedef struct fpb_comm fpb_comm;
 /* Extra element types of the collectives (besides FPB_F32, FPB_BF16). */
 enum { FPB_COMM_U32 = 2, FPB_COMM_I32 = 3, FPB_COMM_BYTES = 4 };

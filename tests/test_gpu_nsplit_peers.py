@@ -74,7 +74,12 @@ def _rank(rank, world, port, q):
         for _ in range(3):
             graph.replay()
         torch.cuda.synchronize()
-        q.put((rank, F.device_error(), eager_ok, bool(torch.equal(gathered, ref))))
+        graph_ok = bool(torch.equal(gathered, ref))
+        # the barrier's all-reduce MAX: ranks hold 1 and 2, both end with 2
+        v = torch.tensor([rank + 1], dtype=torch.int32, device=dev)
+        barrier.all_reduce_max(v)
+        torch.cuda.synchronize()
+        q.put((rank, F.device_error(), eager_ok, graph_ok and v.item() == world))
     finally:
         graph = None
         if barrier is not None:

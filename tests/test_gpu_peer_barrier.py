@@ -1,5 +1,5 @@
 """fpb_peer_barrier on one GPU: a barrier of one rank passes at once and
-counts its epochs; a barrier whose other rank never announces gives up after
+counts its epochs (and its all-reduce MAX keeps the value); a barrier whose other rank never announces gives up after
 its time limit with device error 601, and the context stays usable.  (The
 two-rank barrier that passes runs on two GPUs in test_gpu_nsplit_peers.py;
 two waiting ranks never share one GPU.)"""
@@ -47,3 +47,21 @@ def test_missing_rank_times_out_with_error():
     assert float(x.sum()) == 8.0
     with pytest.raises(Exception):
         _call(N, torch, counter, flags, table, 2, 2, 50)  # rank outside [0, nranks)
+
+
+def test_single_rank_all_reduce_max_keeps_value():
+    import torch
+
+    import firepit_b200 as F
+    N = F._native
+    F.device_error()
+    flags = torch.zeros(128, dtype=torch.int32, device="cuda")
+    counter = torch.zeros(1, dtype=torch.int32, device="cuda")
+    table = torch.tensor([flags.data_ptr()], dtype=torch.int64, device="cuda")
+    v = torch.tensor([12345], dtype=torch.int32, device="cuda")
+    for _ in range(2):
+        N.call("fpb_peer_all_reduce_max", counter.data_ptr(), flags.data_ptr(), table.data_ptr(), 1, 0, v.data_ptr(),
+               1000, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert F.device_error() == 0
+    assert v.item() == 12345 and counter.item() == 2

@@ -719,17 +719,33 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             void *ydst = sg ? sg->y : p.y;
             const long long ybase = sg ? (long long)token * sg->rows
                                        : (long long)item_group * p.y_group_stride + (long long)token * p.ldy;
-            const int copies = sg && sg->n_peer ? sg->n_peer : 1;
+            // peer copies: the count read once per tile, the addresses through
+            // the read-only path (the stores cannot alias the segment table)
+            const int n_peer = sg ? __ldg(&sg->n_peer) : 0;
+            if (n_peer == 0) {
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const int n = nw + c * 32 + i * 8 + pl;
-              if (n < n_lim) {
-                for (int k = 0; k < copies; ++k) {
-                  void *dst = sg && sg->n_peer ? sg->y_peer[k] : ydst;
+              for (int i = 0; i < 4; ++i) {
+                const int n = nw + c * 32 + i * 8 + pl;
+                if (n < n_lim) {
                   if (p.y_bf16)
-                    reinterpret_cast<__nv_bfloat16 *>(dst)[ybase + n] = __float2bfloat16_rn(keep[i]);
+                    reinterpret_cast<__nv_bfloat16 *>(ydst)[ybase + n] = __float2bfloat16_rn(keep[i]);
                   else
-                    reinterpret_cast<float *>(dst)[ybase + n] = keep[i];
+                    reinterpret_cast<float *>(ydst)[ybase + n] = keep[i];
+                }
+              }
+            } else {
+              for (int k = 0; k < n_peer; ++k) {
+                void *dst = reinterpret_cast<void *>(
+                    __ldg(reinterpret_cast<const unsigned long long *>(&sg->y_peer[k])));
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  const int n = nw + c * 32 + i * 8 + pl;
+                  if (n < n_lim) {
+                    if (p.y_bf16)
+                      reinterpret_cast<__nv_bfloat16 *>(dst)[ybase + n] = __float2bfloat16_rn(keep[i]);
+                    else
+                      reinterpret_cast<float *>(dst)[ybase + n] = keep[i];
+                  }
                 }
               }
             }

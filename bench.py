@@ -505,6 +505,9 @@ def ours_arm(args):
     xh = torch.empty(mats, COLS, dtype=torch.bfloat16, pin_memory=True)
     xh.copy_(x.cpu())
     yh = torch.empty(g, mats, rows_per_rank, dtype=torch.bfloat16, pin_memory=True)
+    # per group, the gathered [g, group, rows] block in one contiguous pinned buffer
+    # (a strided slice of yh is no pinned copy target inside a graph)
+    yh_g = [torch.empty(g, len(gr), rows_per_rank, dtype=torch.bfloat16, pin_memory=True) for gr in groups]
     xd = torch.empty_like(x)
     e2e_b = batched(xd, tensor_cores, peers=fused)
     for b in e2e_b:  # eager once: every code path initialised outside capture
@@ -519,15 +522,15 @@ def ours_arm(args):
             yh[0].copy_(y_local, non_blocking=True)
         elif fused:
             barrier()
-            for i, gr in enumerate(groups):
-                yh[:, gr.start:gr.stop].copy_(y_all[i], non_blocking=True)
+            for i in range(len(groups)):
+                yh_g[i].copy_(y_all[i], non_blocking=True)
 
     def e2e_step():
         gsink.replay()
         if g > 1 and not fused:
             for i, gr in enumerate(groups):
                 comm().all_gather_into(y_all[i], y_local[gr.start:gr.stop])
-                yh[:, gr.start:gr.stop].copy_(y_all[i], non_blocking=True)
+                yh_g[i].copy_(y_all[i], non_blocking=True)
 
     e2e_steps = max(1, min(args.steps, 50))
     for _ in range(3):

@@ -66,6 +66,9 @@ def parse_args():
                         "decode: config 4, the hybrid MoE decoder's decode tokens/s")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="budget of the cpu_baseline sample")
     p.add_argument("--no-sub", action="store_true", help="default line without the other configs' sub-records")
+    p.add_argument("--all-gather", choices=["peer", "nccl"], default="peer",
+                   help="config 0 at N > 1: the GEMV epilogue's NVLink peer stores + peer barrier (peer), or "
+                        "NCCL all-gathers overlapping the next batch (nccl)")
     p.add_argument("--sub-steps", type=int, default=20, help="timed steps of each sub-record")
     p.add_argument("--sub-cpu-seconds", type=float, default=3.0, help="cpu_baseline budget of each sub-record")
     p.add_argument("--dec-prompt", type=int, default=2048, help="config 4 prompt tokens per session (2048)")
@@ -347,13 +350,14 @@ def ours_arm(args):
                                         y_peers=peers_of(i) if peers else None) for i, gr in enumerate(groups)]
         return [F.gemv_batched([(slices[c], xsrc[c:c + 1], y_local[c:c + 1]) for c in gr]) for gr in groups]
 
+    use_peers = g > 1 and getattr(args, "all_gather", "peer") == "peer"
     try:
-        launches_b = batched(x, peers=g > 1)
+        launches_b = batched(x, peers=use_peers)
         tensor_cores = True
     except F.ShapeError:
         launches_b = batched(x, tensor_cores=False)
         tensor_cores = False
-    fused = g > 1 and tensor_cores
+    fused = use_peers and tensor_cores
 
     def launch(i, sh):
         if tensor_cores:

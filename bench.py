@@ -197,13 +197,14 @@ class ClockSampler:
 
 # ---- config 0 -----------------------------------------------------------------------------
 MAX_SEGS = 128  # fpb_nvfp4_gemv_batched's segments per launch
+MAX_PLANES_SEGS = 512  # members of one tensor-core batch here (the library takes up to 1024)
 
 
 def gemv_config(g: int) -> dict:
     return {"workload": "config0 NVFP4 GEMV 4096x4096 (x bf16 [1,4096] N(0,1), y bf16)",
             "matrices_per_step": MATS_PER_GPU * g, "rows_per_rank": ROWS // g,
             "launch": f"each rank's slices of the {MATS_PER_GPU * g} matrices in one prepared batch per "
-                      f"{MAX_SEGS} (fpb_nvfp4_gemv_batch_run: x as NVFP4 digit planes, tcgen05), every matrix "
+                      f"{MAX_PLANES_SEGS} (fpb_nvfp4_gemv_batch_run: x as NVFP4 digit planes, tcgen05), every matrix "
                       "with its own x row",
             "parallelism": f"N-split x{g}; the GEMV launch stores each rank's slices into every rank's gathered "
                            "output (NVLink peer stores), one peer-memory barrier per step" if g > 1 else "single GPU",
@@ -323,7 +324,11 @@ def ours_arm(args):
     # x row c (of one seed-0 N(0,1) stream) is matrix c's input; row 0 is config 0's x.
     x = F.synth_normal((mats, COLS), seed=0, stream_id=0, dtype=torch.bfloat16, device=dev)
     y_local = torch.empty(mats, rows_per_rank, dtype=torch.bfloat16, device=dev)
-    groups = [range(i, min(i + MAX_SEGS, mats)) for i in range(0, mats, MAX_SEGS)]
+    # the tensor-core batch (cols % 256 == 0, <= 4096: config 0) takes every
+    # rank's slices at N <= 8 in one launch, so the tiles of all matrices share
+    # one tail; the streaming kernel takes at most MAX_SEGS per launch
+    gsize = MAX_PLANES_SEGS if COLS % 256 == 0 and COLS <= 4096 else MAX_SEGS
+    groups = [range(i, min(i + gsize, mats)) for i in range(0, mats, gsize)]
     # On more than one GPU the gathered outputs are buffers every rank maps
     # (CUDA IPC): the GEMV's epilogue stores this rank's slices into all of
     # them over NVLink, so the all-gather is part of the GEMV launch.
@@ -348,7 +353,9 @@ def ours_arm(args):
         if tensor_cores:
             return [F.gemv_batch_planes([(slices[c], xsrc[c:c + 1], y_local[c:c + 1]) for c in gr],
                                         y_peers=peers_of(i) if peers else None) for i, gr in enumerate(groups)]
-        return [F.gemv_batched([(slices[c], xsrc[c:c + 1], y_local[c:c + 1]) for c in gr]) for gr in groups]
+        # streaming: each group in launches of at most MAX_SEGS matrices
+        return [[F.gemv_batched([(slices[c], xsrc[c:c + 1], y_local[c:c + 1]) for c in gr[j:j + MAX_SEGS]])
+                 for j in range(0, len(gr), MAX_SEGS)] for gr in groups]
 
     use_peers = g > 1 and getattr(args, "all_gather", "peer") == "peer"
     try:
@@ -363,7 +370,8 @@ def ours_arm(args):
         if tensor_cores:
             N_.call("fpb_nvfp4_gemv_batch_run", launches_b[i]._batch, sh)
         else:
-            N_.call("fpb_nvfp4_gemv_batched", launches_b[i]._segs, len(groups[i]), BF, BF, 1, sh)
+            for sub in launches_b[i]:
+                N_.call("fpb_nvfp4_gemv_batched", sub._segs, len(sub.gemvs), BF, BF, 1, sh)
 
     s = torch.cuda.Stream(device=dev)
     with torch.cuda.stream(s):  # every code path initialised outside capture
@@ -481,8 +489,9 @@ def ours_arm(args):
     stream_b = batched(x, tensor_cores=False)
 
     def streaming(sh):
-        for i in range(len(groups)):
-            N_.call("fpb_nvfp4_gemv_batched", stream_b[i]._segs, len(groups[i]), BF, BF, 1, sh)
+        for subs in stream_b:
+            for sub in subs:
+                N_.call("fpb_nvfp4_gemv_batched", sub._segs, len(sub.gemvs), BF, BF, 1, sh)
 
     with torch.cuda.stream(s):
         streaming(s.cuda_stream)
@@ -514,6 +523,8 @@ def ours_arm(args):
     yh_g = [torch.empty(g, len(gr), rows_per_rank, dtype=torch.bfloat16, pin_memory=True) for gr in groups]
     xd = torch.empty_like(x)
     e2e_b = batched(xd, tensor_cores, peers=fused)
+    if not tensor_cores:
+        e2e_b = [sub for subs in e2e_b for sub in subs]
     for b in e2e_b:  # eager once: every code path initialised outside capture
         b.submit(F.Async())
     torch.cuda.synchronize()

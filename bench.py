@@ -7,11 +7,13 @@ rows from N(0, 1) seed 0, y bf16.  One step is one decode-style sweep over
 every matrix is split along N (rows) over the g ranks; each rank computes its
 row slices of all 64*g GEMVs as one prepared tensor-core batch
 (fpb_nvfp4_gemv_batch_run: each x row as 8 NVFP4 digit planes, the weights
-through tcgen05 mxf4nvf4, at most 128 matrices' slices per batch) and the
-slices of each batch are all-gathered after it (fpb_comm_all_gather, on a
-second stream, overlapping the next batch; the step is one CUDA graph).  Each
-rank streams 64 * 9.45 MB = 605 MB of weights per step at every g (inputs
-larger than L2); per-GPU work is fixed as g grows ("weak").
+through tcgen05 mxf4nvf4, up to 512 matrices' slices per batch).  At g > 1
+the batch's epilogue also stores each slice into every rank's gathered
+output (NVLink peer stores into buffers mapped with CUDA IPC) and a
+peer-memory barrier (fpb_peer_barrier) ends the step, which is one CUDA
+graph; `--all-gather nccl` uses fpb_comm_all_gather instead.  Each rank
+streams 64 * 9.45 MB = 605 MB of weights per step at every g (inputs larger
+than L2); per-GPU work is fixed as g grows ("weak").
 
   value  device-resident GB/s (algorithmic bytes of all ranks / max step time),
          the launches replayed as CUDA graphs;

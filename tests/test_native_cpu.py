@@ -164,3 +164,40 @@ def test_comm_host_side():
     assert N.lib.fpb_comm_init(uid, 2, 2, 0, C.byref(h)) == N.FPB_ERR_INVALID_ARGUMENT
     assert N.lib.fpb_comm_init(uid, 0, 0, 0, C.byref(h)) == N.FPB_ERR_INVALID_ARGUMENT
     assert N.lib.fpb_status_string(N.FPB_ERR_COMM) == b"communication error"
+
+
+def test_multi_gpu_and_batch_entry_points_check_arguments_first():
+    """The expert-parallel, peer-memory and gather entry points reject bad
+    shapes and pointers on the host, before any CUDA call (no GPU needed)."""
+    fake = 1 << 20  # a 16-byte-aligned address that is never dereferenced
+    # fpb_ep_dispatch: cols % 64, experts not divisible by ranks, too many ranks
+    args = [fake, N.FPB_BF16, 4, 96, fake, fake, 4, 4, 16, 2, fake, fake, fake, fake, None]
+    assert N.lib.fpb_ep_dispatch(*args) == N.FPB_ERR_SHAPE
+    args[3], args[8] = 64, 15
+    assert N.lib.fpb_ep_dispatch(*args) == N.FPB_ERR_SHAPE
+    args[8], args[9] = 64, 33
+    assert N.lib.fpb_ep_dispatch(*args) == N.FPB_ERR_SHAPE
+    args[9], args[0] = 2, fake + 8  # x not 16-byte aligned
+    assert N.lib.fpb_ep_dispatch(*args) == N.FPB_ERR_INVALID_ARGUMENT
+    assert N.lib.fpb_ep_dispatch_chunks(fake, N.FPB_BF16, 4, 64, fake, fake, 4, 4, 16, 2, fake, None, 0, fake,
+                                        fake, None) == N.FPB_ERR_INVALID_ARGUMENT  # no chunk table
+    assert N.lib.fpb_ep_unpack(fake, 0, 64, 4, fake, fake, None) == N.FPB_ERR_SHAPE
+    assert N.lib.fpb_ep_record_bytes(2048, 16) == 1280
+    # fpb_moe_gather_codes: cols % 64, then the factor stride's alignment
+    assert N.lib.fpb_moe_gather_codes(fake, 16, fake, 4, 8, 96, fake, 128, None, 0, fake, fake,
+                                      None) == N.FPB_ERR_SHAPE
+    assert N.lib.fpb_moe_gather_codes(fake, 1280, fake + 1024, 1282, 8, 2048, fake, 128, None, 0, fake, fake,
+                                      None) == N.FPB_ERR_INVALID_ARGUMENT
+    # masked layout: the same selection checks as fpb_moe_layout
+    assert N.lib.fpb_moe_layout_masked(fake, 0, 4, 4, 16, 128, 128, fake, fake, fake, fake, fake, fake, 1 << 20,
+                                       None) == N.FPB_ERR_SELECTION
+    assert N.lib.fpb_moe_combine_chunks(fake, N.FPB_BF16, 128, 64, fake, fake, 8, 4, 4, None, 8, N.FPB_F32,
+                                        None) == N.FPB_ERR_INVALID_ARGUMENT
+    # peer memory and the barrier
+    p = C.c_void_p()
+    assert N.lib.fpb_ipc_alloc(0, C.byref(p)) == N.FPB_ERR_INVALID_ARGUMENT
+    assert N.lib.fpb_ipc_get_handle(None, None) == N.FPB_ERR_INVALID_ARGUMENT
+    assert N.lib.fpb_peer_barrier(fake, fake, fake, 0, 0, 100, None) == N.FPB_ERR_INVALID_ARGUMENT
+    assert N.lib.fpb_peer_barrier(fake, fake, fake, 2, 2, 100, None) == N.FPB_ERR_INVALID_ARGUMENT
+    assert N.lib.fpb_peer_barrier(fake, fake, fake, 2, 0, 0, None) == N.FPB_ERR_INVALID_ARGUMENT
+    assert N.lib.fpb_peer_all_reduce_max(fake, fake, fake, 2, 0, None, 100, None) == N.FPB_ERR_INVALID_ARGUMENT

@@ -573,7 +573,8 @@ int fpb_moe_route_meta(const int32_t *ids, const int32_t *inverse, size_t tokens
  * that route to d in token order, then empty records) and positions
  * [tokens * nranks + nranks] int32: positions[t * nranks + d] = d * tokens +
  * the token's record index in chunk d, or -1; the last nranks entries are the
- * chunk counts.  Two launches; device error 403 on an id outside [0, experts).
+ * chunk counts.  Three launches (two above 10240 tokens); device error 403 on
+ * an id outside [0, experts).
  * The receiver turns the records it got (nranks chunks) into dense route
  * tables with fpb_ep_unpack, lays them out with fpb_moe_layout_masked and
  * gathers the NVFP4 rows with fpb_moe_gather_codes (code_stride = sf_stride =
